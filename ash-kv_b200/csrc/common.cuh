@@ -1,0 +1,117 @@
+// Shared device/host helpers for libashkv_cuda (sm_100a).
+#pragma once
+
+#include <cstdint>
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include "ashkv.h"
+
+namespace ashkv {
+
+// ---------------------------------------------------------------- host side
+// Records the last CUDA error (thread-local) and maps it to a status code.
+ashkv_status_t check_launch(const char* what);
+void set_error(const char* what, cudaError_t err);
+
+inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+
+inline bool aligned(const void* p, uintptr_t a) {
+  return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0;
+}
+
+int sm_count();
+
+// ---------------------------------------------------------------- bf16/fp16
+__device__ __forceinline__ float bf16lo(uint32_t w) { return __uint_as_float(w << 16); }
+__device__ __forceinline__ float bf16hi(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
+__device__ __forceinline__ float bf16_to_f32(uint16_t h) { return __uint_as_float(uint32_t(h) << 16); }
+
+// fp32 -> bf16, round to nearest even; NaN becomes 0x7FFF.
+__device__ __forceinline__ uint16_t f32_to_bf16(float f) {
+  return __bfloat16_as_ushort(__float2bfloat16_rn(f));
+}
+// Two fp32 -> packed bf16x2 (lo in bits 0..15), round to nearest even.
+__device__ __forceinline__ uint32_t f32x2_to_bf16x2(float lo, float hi) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+__device__ __forceinline__ uint16_t f32_to_f16(float f) {
+  return __half_as_ushort(__float2half_rn(f));
+}
+__device__ __forceinline__ float f16_to_f32(uint16_t h) {
+  return __half2float(__ushort_as_half(h));
+}
+
+// Streaming 16-byte load through the non-coherent path (data read once).
+__device__ __forceinline__ uint4 ld_nc_v4(const void* p) {
+  uint4 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(p));
+  return r;
+}
+__device__ __forceinline__ float4 ld_nc_f4(const void* p) {
+  float4 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.f32 {%0,%1,%2,%3}, [%4];"
+               : "=f"(r.x), "=f"(r.y), "=f"(r.z), "=f"(r.w)
+               : "l"(p));
+  return r;
+}
+// Streaming 16-byte store (evict-first: written once, not re-read soon).
+__device__ __forceinline__ void st_cs_v4(void* p, uint4 v) {
+  asm volatile("st.global.cs.v4.u32 [%0], {%1,%2,%3,%4};"
+               :: "l"(p), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w) : "memory");
+}
+
+// NaN-propagating |a| max (PTX max.NaN): returns NaN if either input is NaN.
+__device__ __forceinline__ float max_nan(float a, float b) {
+  float r;
+  asm("max.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+  return r;
+}
+
+// Round-half-even of a value already clamped to [0, 2^22) via the 1.5*2^23
+// magic constant; returns the integer in the low mantissa bits.
+__device__ __forceinline__ uint32_t rint_small(float v) {
+  return __float_as_uint(__fadd_rn(v, 12582912.0f)) & 0x3FFFFFu;
+}
+
+// ---------------------------------------------------------------- Philox
+// Philox4x32-10 (Salmon, Moraes, Dror, Shaw, "Parallel random numbers: as easy
+// as 1, 2, 3", SC'11): 10 rounds of two 32x32->64 multiplies with the round
+// key bumped by the Weyl constants between rounds.
+struct Philox4 { uint32_t v[4]; };
+
+__device__ __host__ __forceinline__ void mulhilo32(uint32_t a, uint32_t b, uint32_t& hi, uint32_t& lo) {
+  uint64_t p = uint64_t(a) * uint64_t(b);
+  hi = uint32_t(p >> 32);
+  lo = uint32_t(p);
+}
+
+__device__ __host__ __forceinline__ Philox4 philox4x32_10(uint32_t c0, uint32_t c1, uint32_t c2, uint32_t c3,
+                                                          uint32_t k0, uint32_t k1) {
+  constexpr uint32_t M0 = 0xD2511F53u, M1 = 0xCD9E8D57u;
+  constexpr uint32_t W0 = 0x9E3779B9u, W1 = 0xBB67AE85u;
+#pragma unroll
+  for (int r = 0; r < 10; ++r) {
+    uint32_t hi0, lo0, hi1, lo1;
+    mulhilo32(M0, c0, hi0, lo0);
+    mulhilo32(M1, c2, hi1, lo1);
+    uint32_t n0 = hi1 ^ c1 ^ k0;
+    uint32_t n2 = hi0 ^ c3 ^ k1;
+    c0 = n0; c1 = lo1; c2 = n2; c3 = lo0;
+    k0 += W0; k1 += W1;
+  }
+  Philox4 out;
+  out.v[0] = c0; out.v[1] = c1; out.v[2] = c2; out.v[3] = c3;
+  return out;
+}
+
+// 16-bit field -> dither value h * 2^-16 - 0.5 in [-0.5, 0.5), exact.
+__device__ __forceinline__ float dither16(uint32_t h16) {
+  return __fadd_rn(__uint_as_float(0x3F800000u | (h16 << 7)), -1.5f);
+}
+
+}  // namespace ashkv

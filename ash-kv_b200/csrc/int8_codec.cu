@@ -1,0 +1,331 @@
+// INT8 per-row absmax codec (sm_100a).
+//
+// Restates the arithmetic of the reference's Triton kernels
+// (ashkv/codecs/int8.py:50-81 encode, :98-116 decode) as a single-pass CUDA
+// kernel: a "team" of threads owns one row, keeps the row in registers
+// between the absmax reduction and the quantisation, and issues 16-byte
+// loads/stores.  The team size is min(32, row_len / 8) so short rows
+// (INT8Codec, 128 elements) pack several rows per warp and long rows (the
+// SGLang hooks, head_num * head_dim elements) spread over a full warp.
+#include "common.cuh"
+
+namespace ashkv {
+namespace {
+
+struct Int8EncParams {
+  const uint16_t* src;      // bf16 or fp16 bits
+  int64_t n_rows;
+  int32_t row_len;
+  int64_t src_stride;       // elements
+  const int64_t* row_index; // optional gather
+  uint8_t* codes;
+  int64_t codes_stride;     // bytes
+  uint8_t* scales;          // byte-addressed
+  int32_t scales_per_slot;
+  int64_t scale_slot_stride;
+  int32_t scale_fp16;
+  int32_t fp32_product;
+};
+
+struct Int8DecParams {
+  const uint8_t* codes;
+  int64_t codes_stride;
+  const uint8_t* scales;
+  int32_t scales_per_slot;
+  int64_t scale_slot_stride;
+  int32_t scale_fp16;
+  int64_t n_rows;
+  int32_t row_len;
+  uint16_t* dst;
+  int32_t dst_fp16;
+  int64_t dst_stride;
+  const int64_t* row_index;
+};
+
+template <bool FP16>
+__device__ __forceinline__ float in_lo(uint32_t w) {
+  if constexpr (FP16) return __half2float(__ushort_as_half(uint16_t(w & 0xFFFFu)));
+  else return bf16lo(w);
+}
+template <bool FP16>
+__device__ __forceinline__ float in_hi(uint32_t w) {
+  if constexpr (FP16) return __half2float(__ushort_as_half(uint16_t(w >> 16)));
+  else return bf16hi(w);
+}
+
+// s = x * 127 rounded to the input dtype (Triton >= 3 keeps the bf16/fp16
+// product of a tensor and a weakly-typed Python float in the tensor's dtype).
+template <bool FP16>
+__device__ __forceinline__ float scaled127(float x, bool fp32_product) {
+  float p = __fmul_rn(x, 127.0f);  // exact for bf16 inputs (8+7 bits); fp16 needs <= 18 bits
+  if (fp32_product) return p;
+  if constexpr (FP16) return __half2float(__float2half_rn(p));
+  else return __bfloat162float(__float2bfloat16_rn(p));
+}
+
+__device__ __forceinline__ int32_t quant_code(float s, float am) {
+  float q = __fdiv_rn(s, am);
+  float r = __fadd_rn(q, q > 0.0f ? 0.5f : -0.5f);
+  int32_t c;
+  asm("cvt.rzi.sat.s8.f32 %0, %1;" : "=r"(c) : "f"(r));  // NaN -> 0
+  return c;
+}
+
+__device__ __forceinline__ uint8_t* scale_addr(uint8_t* base, int64_t r, int32_t sps, int64_t slot_stride) {
+  return base + (r / sps) * slot_stride + (r % sps) * 2;
+}
+
+// Each thread owns NCH chunks of 8 consecutive elements of its row.
+template <bool FP16, int NCH, int TEAM>
+__global__ void __launch_bounds__(256) int8_encode_kernel(const Int8EncParams p) {
+  constexpr int ROWS_PER_CTA = 256 / TEAM;
+  const int lane_in_team = threadIdx.x % TEAM;
+  const int64_t r = int64_t(blockIdx.x) * ROWS_PER_CTA + threadIdx.x / TEAM;
+  const bool active = r < p.n_rows;
+
+  uint4 chunk[NCH];
+  float am = 0.0f;
+  const uint16_t* row = nullptr;
+  if (active) {
+    const int64_t src_row = p.row_index ? p.row_index[r] : r;
+    row = p.src + src_row * p.src_stride;
+#pragma unroll
+    for (int c = 0; c < NCH; ++c) {
+      chunk[c] = ld_nc_v4(row + (int64_t(c) * TEAM + lane_in_team) * 8);
+      const uint32_t w[4] = {chunk[c].x, chunk[c].y, chunk[c].z, chunk[c].w};
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        am = fmaxf(am, fabsf(in_lo<FP16>(w[k])));  // fmaxf ignores NaN, like tl.maximum
+        am = fmaxf(am, fabsf(in_hi<FP16>(w[k])));
+      }
+    }
+  }
+#pragma unroll
+  for (int off = TEAM / 2; off > 0; off >>= 1)
+    am = fmaxf(am, __shfl_xor_sync(0xFFFFFFFFu, am, off, TEAM));
+  if (!active) return;
+  am = fmaxf(am, 1e-8f);
+
+  if (lane_in_team == 0) {
+    uint8_t* sp = scale_addr(p.scales, r, p.scales_per_slot, p.scale_slot_stride);
+    uint16_t sv = p.scale_fp16 ? f32_to_f16(am) : f32_to_bf16(am);
+    *reinterpret_cast<uint16_t*>(sp) = sv;
+  }
+
+  uint8_t* out = p.codes + r * p.codes_stride;
+  const bool f32p = p.fp32_product != 0;
+#pragma unroll
+  for (int c = 0; c < NCH; ++c) {
+    const uint32_t w[4] = {chunk[c].x, chunk[c].y, chunk[c].z, chunk[c].w};
+    uint32_t packed[2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      uint32_t b = 0;
+#pragma unroll
+      for (int k = 0; k < 2; ++k) {
+        const uint32_t word = w[h * 2 + k];
+        const int32_t c0 = quant_code(scaled127<FP16>(in_lo<FP16>(word), f32p), am);
+        const int32_t c1 = quant_code(scaled127<FP16>(in_hi<FP16>(word), f32p), am);
+        b |= (uint32_t(c0) & 0xFFu) << (16 * k);
+        b |= (uint32_t(c1) & 0xFFu) << (16 * k + 8);
+      }
+      packed[h] = b;
+    }
+    *reinterpret_cast<uint2*>(out + (int64_t(c) * TEAM + lane_in_team) * 8) = make_uint2(packed[0], packed[1]);
+  }
+}
+
+// Generic path: any row length / alignment, one element per thread step.
+template <bool FP16>
+__global__ void __launch_bounds__(256) int8_encode_generic_kernel(const Int8EncParams p) {
+  const int64_t r = int64_t(blockIdx.x) * 8 + threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  if (r >= p.n_rows) return;
+  const int64_t src_row = p.row_index ? p.row_index[r] : r;
+  const uint16_t* row = p.src + src_row * p.src_stride;
+  float am = 0.0f;
+  for (int i = lane; i < p.row_len; i += 32) {
+    const uint32_t w = row[i];
+    am = fmaxf(am, fabsf(in_lo<FP16>(w)));
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) am = fmaxf(am, __shfl_xor_sync(0xFFFFFFFFu, am, off));
+  am = fmaxf(am, 1e-8f);
+  if (lane == 0) {
+    uint8_t* sp = scale_addr(p.scales, r, p.scales_per_slot, p.scale_slot_stride);
+    *reinterpret_cast<uint16_t*>(sp) = p.scale_fp16 ? f32_to_f16(am) : f32_to_bf16(am);
+  }
+  uint8_t* out = p.codes + r * p.codes_stride;
+  for (int i = lane; i < p.row_len; i += 32) {
+    const uint32_t w = row[i];
+    out[i] = uint8_t(quant_code(scaled127<FP16>(in_lo<FP16>(w), p.fp32_product != 0), am) & 0xFF);
+  }
+}
+
+__device__ __forceinline__ float dequant(int32_t c, float scale) {
+  // c * scale is exact in fp32 (8-bit code times an 8/11-bit significand).
+  return __fdiv_rn(__fmul_rn(float(c), scale), 127.0f);
+}
+
+__device__ __forceinline__ uint16_t out_bits(float v, bool fp16) {
+  // Triton casts to bf16 first, then the store converts to the pointer's type.
+  const float b = __bfloat162float(__float2bfloat16_rn(v));
+  return fp16 ? f32_to_f16(b) : f32_to_bf16(v);
+}
+
+template <int NCH, int TEAM>
+__global__ void __launch_bounds__(256) int8_decode_kernel(const Int8DecParams p) {
+  constexpr int ROWS_PER_CTA = 256 / TEAM;
+  const int lane_in_team = threadIdx.x % TEAM;
+  const int64_t r = int64_t(blockIdx.x) * ROWS_PER_CTA + threadIdx.x / TEAM;
+  if (r >= p.n_rows) return;
+  const uint16_t sbits = *reinterpret_cast<const uint16_t*>(
+      p.scales + (r / p.scales_per_slot) * p.scale_slot_stride + (r % p.scales_per_slot) * 2);
+  const float scale = p.scale_fp16 ? f16_to_f32(sbits) : bf16_to_f32(sbits);
+  const uint8_t* in = p.codes + r * p.codes_stride;
+  const int64_t dst_row = p.row_index ? p.row_index[r] : r;
+  uint16_t* out = p.dst + dst_row * p.dst_stride;
+  const bool f16 = p.dst_fp16 != 0;
+#pragma unroll
+  for (int c = 0; c < NCH; ++c) {
+    const int64_t e0 = (int64_t(c) * TEAM + lane_in_team) * 8;
+    const uint2 w = *reinterpret_cast<const uint2*>(in + e0);
+    const uint32_t ww[2] = {w.x, w.y};
+    uint32_t o[4];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+#pragma unroll
+      for (int k = 0; k < 2; ++k) {
+        const int32_t c0 = int32_t(int8_t((ww[h] >> (16 * k)) & 0xFF));
+        const int32_t c1 = int32_t(int8_t((ww[h] >> (16 * k + 8)) & 0xFF));
+        o[h * 2 + k] = uint32_t(out_bits(dequant(c0, scale), f16)) |
+                       (uint32_t(out_bits(dequant(c1, scale), f16)) << 16);
+      }
+    }
+    *reinterpret_cast<uint4*>(out + e0) = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+}
+
+__global__ void __launch_bounds__(256) int8_decode_generic_kernel(const Int8DecParams p) {
+  const int64_t r = int64_t(blockIdx.x) * 8 + threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  if (r >= p.n_rows) return;
+  const uint16_t sbits = *reinterpret_cast<const uint16_t*>(
+      p.scales + (r / p.scales_per_slot) * p.scale_slot_stride + (r % p.scales_per_slot) * 2);
+  const float scale = p.scale_fp16 ? f16_to_f32(sbits) : bf16_to_f32(sbits);
+  const uint8_t* in = p.codes + r * p.codes_stride;
+  const int64_t dst_row = p.row_index ? p.row_index[r] : r;
+  uint16_t* out = p.dst + dst_row * p.dst_stride;
+  for (int i = lane; i < p.row_len; i += 32)
+    out[i] = out_bits(dequant(int32_t(int8_t(in[i])), scale), p.dst_fp16 != 0);
+}
+
+template <typename P, typename KFast>
+bool pick_team(int32_t row_len, int& team, int& nch) {
+  if (row_len % 8 != 0) return false;
+  const int chunks = row_len / 8;
+  team = chunks >= 32 ? 32 : chunks;
+  if (team & (team - 1)) return false;  // team must be a power of two
+  if (chunks % team) return false;
+  nch = chunks / team;
+  return nch == 1 || nch == 2 || nch == 4 || nch == 8 || nch == 16;
+}
+
+}  // namespace
+
+#define ASHKV_ENC_CASE(FP, NC, TM)                                                        \
+  if (nch == NC && team == TM) {                                                          \
+    int8_encode_kernel<FP, NC, TM><<<unsigned((p.n_rows + 256 / TM - 1) / (256 / TM)), 256, 0, st>>>(p); \
+    return check_launch("int8_encode");                                                  \
+  }
+
+template <bool FP16>
+static ashkv_status_t launch_encode(const Int8EncParams& p, int team, int nch, bool fast, cudaStream_t st) {
+  if (fast) {
+    ASHKV_ENC_CASE(FP16, 1, 1) ASHKV_ENC_CASE(FP16, 1, 2) ASHKV_ENC_CASE(FP16, 1, 4)
+    ASHKV_ENC_CASE(FP16, 1, 8) ASHKV_ENC_CASE(FP16, 1, 16) ASHKV_ENC_CASE(FP16, 1, 32)
+    ASHKV_ENC_CASE(FP16, 2, 32) ASHKV_ENC_CASE(FP16, 4, 32) ASHKV_ENC_CASE(FP16, 8, 32)
+    ASHKV_ENC_CASE(FP16, 16, 32)
+  }
+  int8_encode_generic_kernel<FP16><<<unsigned((p.n_rows + 7) / 8), 256, 0, st>>>(p);
+  return check_launch("int8_encode_generic");
+}
+#undef ASHKV_ENC_CASE
+
+}  // namespace ashkv
+
+using namespace ashkv;
+
+extern "C" ashkv_status_t ashkv_int8_encode_rows(
+    const void* d_src, int32_t src_dtype, int64_t n_rows, int32_t row_len,
+    int64_t src_row_stride, const int64_t* d_row_index,
+    void* d_codes, int64_t codes_row_stride,
+    void* d_scales, int32_t scale_dtype, int32_t scales_per_slot, int64_t scale_slot_stride,
+    uint32_t flags, void* stream) {
+  if (n_rows < 0 || row_len <= 0 || scales_per_slot <= 0) return ASHKV_BAD_ARGUMENT;
+  if (src_dtype != ASHKV_DTYPE_BF16 && src_dtype != ASHKV_DTYPE_FP16) return ASHKV_BAD_ARGUMENT;
+  if (scale_dtype != ASHKV_DTYPE_BF16 && scale_dtype != ASHKV_DTYPE_FP16) return ASHKV_BAD_ARGUMENT;
+  if (n_rows == 0) return ASHKV_OK;
+  if (!d_src || !d_codes || !d_scales) return ASHKV_BAD_ARGUMENT;
+  if (n_rows > (int64_t(1) << 40)) return ASHKV_BAD_ARGUMENT;
+  if (!aligned(d_scales, 2) || (scale_slot_stride % 2)) return ASHKV_BAD_ARGUMENT;
+
+  Int8EncParams p;
+  p.src = static_cast<const uint16_t*>(d_src);
+  p.n_rows = n_rows; p.row_len = row_len; p.src_stride = src_row_stride; p.row_index = d_row_index;
+  p.codes = static_cast<uint8_t*>(d_codes); p.codes_stride = codes_row_stride;
+  p.scales = static_cast<uint8_t*>(d_scales); p.scales_per_slot = scales_per_slot;
+  p.scale_slot_stride = scale_slot_stride; p.scale_fp16 = scale_dtype == ASHKV_DTYPE_FP16;
+  p.fp32_product = (flags & ASHKV_INT8_FP32_PRODUCT) ? 1 : 0;
+
+  int team = 0, nch = 0;
+  bool fast = pick_team<void, void>(row_len, team, nch);
+  // 16-byte loads need 16-byte aligned rows; 8-byte stores need 8-byte aligned code rows.
+  fast = fast && aligned(d_src, 16) && ((src_row_stride * 2) % 16 == 0) &&
+         aligned(d_codes, 8) && (codes_row_stride % 8 == 0);
+  cudaStream_t st = as_stream(stream);
+  return src_dtype == ASHKV_DTYPE_FP16 ? launch_encode<true>(p, team, nch, fast, st)
+                                       : launch_encode<false>(p, team, nch, fast, st);
+}
+
+#define ASHKV_DEC_CASE(NC, TM)                                                             \
+  if (nch == NC && team == TM) {                                                           \
+    int8_decode_kernel<NC, TM><<<unsigned((p.n_rows + 256 / TM - 1) / (256 / TM)), 256, 0, st>>>(p); \
+    return check_launch("int8_decode");                                                   \
+  }
+
+extern "C" ashkv_status_t ashkv_int8_decode_rows(
+    const void* d_codes, int64_t codes_row_stride,
+    const void* d_scales, int32_t scale_dtype, int32_t scales_per_slot, int64_t scale_slot_stride,
+    int64_t n_rows, int32_t row_len,
+    void* d_dst, int32_t dst_dtype, int64_t dst_row_stride, const int64_t* d_row_index,
+    void* stream) {
+  if (n_rows < 0 || row_len <= 0 || scales_per_slot <= 0) return ASHKV_BAD_ARGUMENT;
+  if (scale_dtype != ASHKV_DTYPE_BF16 && scale_dtype != ASHKV_DTYPE_FP16) return ASHKV_BAD_ARGUMENT;
+  if (dst_dtype != ASHKV_DTYPE_BF16 && dst_dtype != ASHKV_DTYPE_FP16) return ASHKV_BAD_ARGUMENT;
+  if (n_rows == 0) return ASHKV_OK;
+  if (!d_codes || !d_scales || !d_dst) return ASHKV_BAD_ARGUMENT;
+  if (!aligned(d_scales, 2) || (scale_slot_stride % 2)) return ASHKV_BAD_ARGUMENT;
+
+  Int8DecParams p;
+  p.codes = static_cast<const uint8_t*>(d_codes); p.codes_stride = codes_row_stride;
+  p.scales = static_cast<const uint8_t*>(d_scales); p.scales_per_slot = scales_per_slot;
+  p.scale_slot_stride = scale_slot_stride; p.scale_fp16 = scale_dtype == ASHKV_DTYPE_FP16;
+  p.n_rows = n_rows; p.row_len = row_len;
+  p.dst = static_cast<uint16_t*>(d_dst); p.dst_fp16 = dst_dtype == ASHKV_DTYPE_FP16;
+  p.dst_stride = dst_row_stride; p.row_index = d_row_index;
+
+  int team = 0, nch = 0;
+  bool fast = pick_team<void, void>(row_len, team, nch);
+  fast = fast && aligned(d_codes, 8) && (codes_row_stride % 8 == 0) &&
+         aligned(d_dst, 16) && ((dst_row_stride * 2) % 16 == 0);
+  cudaStream_t st = as_stream(stream);
+  if (fast) {
+    ASHKV_DEC_CASE(1, 1) ASHKV_DEC_CASE(1, 2) ASHKV_DEC_CASE(1, 4) ASHKV_DEC_CASE(1, 8)
+    ASHKV_DEC_CASE(1, 16) ASHKV_DEC_CASE(1, 32) ASHKV_DEC_CASE(2, 32) ASHKV_DEC_CASE(4, 32)
+    ASHKV_DEC_CASE(8, 32) ASHKV_DEC_CASE(16, 32)
+  }
+  int8_decode_generic_kernel<<<unsigned((n_rows + 7) / 8), 256, 0, st>>>(p);
+  return check_launch("int8_decode_generic");
+}
+#undef ASHKV_DEC_CASE

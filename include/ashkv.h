@@ -1,0 +1,176 @@
+/*
+ * ashkv.h — C ABI of libashkv_cuda.so, the sm_100a kernels behind ASH-KV's
+ * KV-page codec and demote/promote hot path.
+ *
+ * Conventions shared by every entry point:
+ *   - Plain pointers and sizes only.  Pointers named d_* are device pointers;
+ *     `stream` is a cudaStream_t passed as void* (NULL = legacy default stream).
+ *   - Every call is asynchronous on `stream`, performs no host synchronisation
+ *     and allocates nothing; all buffers are owned by the caller.
+ *   - The return value is an ashkv_status_t.  Conditions that only the device
+ *     can see (outlier-list overflow, out-of-range indices) are OR-ed as
+ *     ASHKV_FLAG_* bits into the caller's device status word `d_status`, which
+ *     the caller reads back whenever it chooses.
+ *   - No C++ exception crosses this boundary.
+ *
+ * Each declaration cites the reference interface it replaces (paths are
+ * relative to the ASH-KV source tree).
+ */
+#ifndef ASHKV_H_
+#define ASHKV_H_
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define ASHKV_API __attribute__((visibility("default")))
+#else
+#define ASHKV_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes (host return values) --------------------------------- */
+typedef int32_t ashkv_status_t;
+#define ASHKV_OK               0
+#define ASHKV_BAD_ARGUMENT     1
+#define ASHKV_OUTLIER_OVERFLOW 2
+#define ASHKV_LAUNCH_ERROR     3
+#define ASHKV_TIMEOUT          4
+
+/* ---- device status-word flags (OR-ed into *d_status) ------------------- */
+#define ASHKV_FLAG_OUTLIER_OVERFLOW 0x1u  /* a bucket had more outliers than its capacity */
+#define ASHKV_FLAG_INDEX_RANGE      0x2u  /* an index pointed outside its buffer; that element was skipped */
+
+/* ---- element-type tags -------------------------------------------------- */
+#define ASHKV_DTYPE_BF16 0
+#define ASHKV_DTYPE_FP16 1
+
+/* ---- N-bit codec constants ---------------------------------------------- */
+#define ASHKV_NBIT_GROUP          32    /* elements per quantisation group */
+#define ASHKV_NBIT_BUCKET_GROUPS  256   /* groups per outlier bucket */
+#define ASHKV_NBIT_BUCKET_ELEMS   8192  /* elements per outlier bucket */
+#define ASHKV_DITHER_TENSOR 0           /* dither read from a caller fp32 tensor (U - 0.5) */
+#define ASHKV_DITHER_PHILOX 1           /* dither generated in-kernel: Philox4x32-10(seed) */
+
+/* ---- flags for the INT8 codec ------------------------------------------- */
+#define ASHKV_INT8_FP32_PRODUCT 0x1u  /* v*127 in fp32 (Triton 2.x typing) instead of the input dtype */
+
+/* Library version (major*10000 + minor*100 + patch). */
+ASHKV_API int32_t ashkv_version(void);
+
+/* Human-readable text for a status code; static storage, never NULL. */
+ASHKV_API const char* ashkv_status_string(ashkv_status_t status);
+
+/* Text of the last CUDA error seen by this thread inside the library. */
+ASHKV_API const char* ashkv_last_error(void);
+
+/* Number of streaming multiprocessors of the current device (0 on error). */
+ASHKV_API int32_t ashkv_device_sm_count(void);
+
+/* ========================================================================
+ * INT8 per-row absmax codec.
+ * Replaces the Triton `_int8_encode_kernel` / `_int8_decode_kernel`
+ * (ashkv/codecs/int8.py:50-81 and :98-116) as used by INT8Codec
+ * (ashkv/codecs/int8.py:149-221) and the SGLang hooks
+ * (ashkv/adapters/sglang/hooks.py:104-128, :220-236).
+ *
+ * encode, per row r of `row_len` elements:
+ *   am      = max(max_i |x_i|, 1e-8)              (fp32, NaN ignored)
+ *   s_i     = round_to_input_dtype(x_i * 127)      (fp32 product if ASHKV_INT8_FP32_PRODUCT)
+ *   q       = s_i / am                              (fp32, correctly rounded)
+ *   code_i  = sat_int8(trunc(q + (q > 0 ? 0.5 : -0.5)))   (NaN -> 0)
+ *   scale_r = am rounded to scale_dtype
+ * Row r is read from d_src + (d_row_index ? d_row_index[r] : r) * src_row_stride
+ * (elements), written to d_codes + r * codes_row_stride (bytes).  Its scale
+ * goes to byte offset (r / scales_per_slot) * scale_slot_stride
+ * + (r % scales_per_slot) * 2 of d_scales; scales_per_slot == 1 with
+ * scale_slot_stride == 2 is a plain contiguous scale array.
+ * ======================================================================== */
+ASHKV_API ashkv_status_t ashkv_int8_encode_rows(
+    const void* d_src, int32_t src_dtype, int64_t n_rows, int32_t row_len,
+    int64_t src_row_stride, const int64_t* d_row_index,
+    void* d_codes, int64_t codes_row_stride,
+    void* d_scales, int32_t scale_dtype, int32_t scales_per_slot, int64_t scale_slot_stride,
+    uint32_t flags, void* stream);
+
+/* decode, per element: out = round_to_out_dtype(bf16((float)code * (float)scale / 127)).
+ * Row r is written to d_dst + (d_row_index ? d_row_index[r] : r) * dst_row_stride.
+ * Scale addressing mirrors ashkv_int8_encode_rows. */
+ASHKV_API ashkv_status_t ashkv_int8_decode_rows(
+    const void* d_codes, int64_t codes_row_stride,
+    const void* d_scales, int32_t scale_dtype, int32_t scales_per_slot, int64_t scale_slot_stride,
+    int64_t n_rows, int32_t row_len,
+    void* d_dst, int32_t dst_dtype, int64_t dst_row_stride, const int64_t* d_row_index,
+    void* stream);
+
+/* ========================================================================
+ * Dithered N-bit codec with 3-sigma outlier isolation (bits = 2, 4 or 8).
+ * Replaces DitheredNBitCodec.encode/decode (ashkv/codecs/nbit_dithered.py:43-167)
+ * and DitheredINT2Codec.encode/decode (ashkv/codecs/int2_dithered.py:36-147).
+ *
+ * Input: n_groups groups of 32 bf16 elements, contiguous.  Per group:
+ *   mu      = fp32 mean (8 strided fp32 partial sums, then summed in order)
+ *   sd      = fp32(sqrt(M2 / 31)), M2 accumulated in fp64
+ *   outlier = |x - mu| > sigma * (sd + 1e-8)
+ *   x'      = outlier ? mu : x
+ *   delta   = max(max|x'|, 1e-8) / ((2^bits - 1) / 2)
+ *   code    = clamp(rint((x' + dither * delta) / delta + half), 0, 2^bits - 1)
+ * Outputs: d_scales (bf16 delta per group), d_codes (MSB-first packing,
+ * 32*bits/8 bytes per group), and the outlier list in buckets of 256 groups:
+ * d_bucket_counts[b] is the number of outliers of bucket b (even when it
+ * exceeds bucket_cap), d_bucket_entries[b*bucket_cap + j] =
+ * (element index within the bucket << 16) | bf16 bits, ascending.
+ * dither_mode ASHKV_DITHER_TENSOR reads d_dither[e] (= U - 0.5, fp32, one per
+ * element); ASHKV_DITHER_PHILOX derives it from Philox4x32-10 keyed by `seed`
+ * at counter (dither_elem_offset + e) / 8.
+ * ======================================================================== */
+ASHKV_API ashkv_status_t ashkv_nbit_encode(
+    const void* d_src, int64_t n_groups, int32_t bits, float sigma,
+    int32_t dither_mode, const float* d_dither, uint64_t seed, uint64_t dither_elem_offset,
+    void* d_scales, void* d_codes,
+    uint32_t* d_bucket_counts, uint32_t* d_bucket_entries, int32_t bucket_cap,
+    uint32_t* d_status, void* stream);
+
+/* Decode groups, then overwrite the bucketed outliers:
+ *   out = bf16(((float)code - half) * (float)bf16_delta); out[idx] = val. */
+ASHKV_API ashkv_status_t ashkv_nbit_decode(
+    const void* d_scales, const void* d_codes, int64_t n_groups, int32_t bits,
+    const uint32_t* d_bucket_counts, const uint32_t* d_bucket_entries, int32_t bucket_cap,
+    void* d_dst, uint32_t* d_status, void* stream);
+
+/* Exclusive scan of min(count, cap) over the buckets, then gather the bucketed
+ * outliers into the reference blob's flat form: d_out_index[k] (int32 element
+ * index within the call, ascending) and d_out_value[k] (bf16 bits).
+ * d_total receives the number of outliers written.  d_offsets holds
+ * n_buckets + 1 uint32 of caller scratch. */
+ASHKV_API ashkv_status_t ashkv_nbit_outliers_flatten(
+    const uint32_t* d_bucket_counts, const uint32_t* d_bucket_entries, int32_t bucket_cap,
+    int64_t n_buckets, uint32_t* d_offsets,
+    int32_t* d_out_index, uint16_t* d_out_value, uint32_t* d_total, void* stream);
+
+/* Decode from the blob form: dense dequantisation followed by a scatter of a
+ * flat outlier list (any order; indices outside [0, n_groups*32) are skipped
+ * and flagged with ASHKV_FLAG_INDEX_RANGE). */
+ASHKV_API ashkv_status_t ashkv_nbit_decode_flat(
+    const void* d_scales, const void* d_codes, int64_t n_groups, int32_t bits,
+    const int32_t* d_out_index, const uint16_t* d_out_value, int64_t n_outliers,
+    void* d_dst, uint32_t* d_status, void* stream);
+
+/* ========================================================================
+ * XXH64 of many equal-sized items (pages), one 64-bit digest per item.
+ * Replaces checksum() (ashkv/codecs/checksum.py:26-37, xxhash.xxh64(...).intdigest())
+ * as applied per page by migrate's verify step (ashkv/runtime/migrate.py:151-176)
+ * and PageTable's bf16/current checksums (ashkv/contracts/page.py:43-44).
+ * Item i occupies item_bytes bytes at d_data + i * item_stride.
+ * ======================================================================== */
+ASHKV_API ashkv_status_t ashkv_xxh64_items(
+    const void* d_data, int64_t n_items, int64_t item_bytes, int64_t item_stride,
+    uint64_t seed, uint64_t* d_out, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* ASHKV_H_ */

@@ -1,0 +1,246 @@
+"""CPU oracle for the ASH-KV codec and policy path — TEST INFRASTRUCTURE ONLY.
+
+This package restates, on the CPU, the arithmetic of the reference ASH-KV
+implementation for the paths the CUDA kernels replace.  It is the checker:
+only ``tests/``, ``__graft_entry__.smoke()`` and ``bench.py``'s
+``cpu_baseline`` / ``--impl reference`` legs import it.  The product
+(``ashkv``) never imports, links or calls it.
+
+Parity status: pinned.  ``tests/golden/`` holds fixtures produced by running
+the reference's own Python code (N-bit/INT2 codecs with an injected dither,
+score/controller, checksum) and its Triton INT8 kernel under the Triton
+interpreter; ``tests/test_oracle_golden.py`` checks this oracle against them.
+
+Restated reference functions (paths relative to the ASH-KV source tree):
+
+* ``int8_encode`` / ``int8_decode``   — ``ashkv/codecs/int8.py:50-81, 98-116``
+* ``nbit_encode`` / ``nbit_decode``   — ``ashkv/codecs/nbit_dithered.py:43-167``,
+  ``ashkv/codecs/int2_dithered.py:36-147``
+* ``nbit_blob`` / ``nbit_parse_blob`` — blob layout, ``nbit_dithered.py:106-110``
+* ``int8_blob``                       — ``ashkv/codecs/int8.py:179-182``
+* ``xxh64``                           — ``ashkv/codecs/checksum.py:26-37``
+* ``score``                           — ``ashkv/runtime/score.py:15-52``
+* ``desired_tiers``                   — ``ashkv/runtime/controller.py:32-106``
+* ``controller_tables``               — ``ashkv/compiler/runtime_builder.py:91-109``
+"""
+from __future__ import annotations
+
+import ctypes
+import struct
+
+import numpy as np
+
+from . import build as _build
+
+_LIB = None
+
+
+def lib() -> ctypes.CDLL:
+    """Load (building first if needed) the oracle's C library."""
+    global _LIB
+    if _LIB is None:
+        path = _build.build()
+        L = ctypes.CDLL(str(path))
+        P = ctypes.c_void_p
+        i64, i32, f32, u64 = ctypes.c_int64, ctypes.c_int32, ctypes.c_float, ctypes.c_uint64
+        L.oracle_int8_encode.argtypes = [P, i32, i64, i32, i32, P, P, i32]
+        L.oracle_int8_decode.argtypes = [P, P, i32, i64, i32, P, i32]
+        L.oracle_nbit_encode.argtypes = [P, i64, i32, f32, P, P, P, P]
+        L.oracle_nbit_decode.argtypes = [P, P, i64, i32, P, P, i64, P]
+        L.oracle_xxh64.argtypes = [P, i64, u64]
+        L.oracle_xxh64.restype = u64
+        L.oracle_xxh64_items.argtypes = [P, i64, i64, i64, u64, P]
+        L.oracle_philox4x32_10.argtypes = [P, P, P]
+        L.oracle_philox_dither.argtypes = [i64, u64, u64, P]
+        L.oracle_f32_to_bf16.argtypes = [f32]
+        L.oracle_f32_to_bf16.restype = ctypes.c_uint16
+        _LIB = L
+    return _LIB
+
+
+def _p(a: np.ndarray):
+    return a.ctypes.data_as(ctypes.c_void_p)
+
+
+# --------------------------------------------------------------------- INT8
+def int8_encode(x_bits: np.ndarray, row_len: int, src_fp16: bool = False, scale_fp16: bool = False,
+                fp32_product: bool = False) -> tuple[np.ndarray, np.ndarray]:
+    """Rows of ``row_len`` bf16/fp16 values (uint16 bits) -> (int8 codes, uint16 scale bits)."""
+    x = np.ascontiguousarray(x_bits, dtype=np.uint16).reshape(-1)
+    n_rows = x.size // row_len
+    codes = np.empty(n_rows * row_len, dtype=np.int8)
+    scales = np.empty(n_rows, dtype=np.uint16)
+    if n_rows:
+        lib().oracle_int8_encode(_p(x), int(src_fp16), n_rows, row_len, int(fp32_product), _p(codes),
+                                 _p(scales), int(scale_fp16))
+    return codes.reshape(n_rows, row_len), scales
+
+
+def int8_decode(codes: np.ndarray, scales: np.ndarray, scale_fp16: bool = False,
+                dst_fp16: bool = False) -> np.ndarray:
+    c = np.ascontiguousarray(codes, dtype=np.int8)
+    n_rows, row_len = c.shape
+    s = np.ascontiguousarray(scales, dtype=np.uint16)
+    out = np.empty(n_rows * row_len, dtype=np.uint16)
+    if n_rows:
+        lib().oracle_int8_decode(_p(c), _p(s), int(scale_fp16), n_rows, row_len, _p(out), int(dst_fp16))
+    return out.reshape(n_rows, row_len)
+
+
+def int8_blob(codes: np.ndarray, scales: np.ndarray) -> bytes:
+    """INT8Codec blob: <I num_tokens> + bf16 scales + int8 codes."""
+    return struct.pack("<I", codes.shape[0]) + scales.astype(np.uint16).tobytes() + codes.astype(np.int8).tobytes()
+
+
+# --------------------------------------------------------------------- N-bit
+def half_states(bits: int) -> float:
+    return ((1 << bits) - 1) / 2.0
+
+
+def nbit_encode(x_bits: np.ndarray, bits: int, dither: np.ndarray, sigma: float = 3.0):
+    """Encode groups of 32 bf16 values.
+
+    ``dither`` is ``U - 0.5`` in fp32, one per element.  Returns
+    ``(scales uint16[n_groups], codes uint8[n_groups*32*bits/8],
+    outlier_index int32[n], outlier_value uint16[n])`` with indices ascending.
+    """
+    x = np.ascontiguousarray(x_bits, dtype=np.uint16).reshape(-1)
+    assert x.size % 32 == 0
+    n_groups = x.size // 32
+    d = np.ascontiguousarray(dither, dtype=np.float32).reshape(-1)
+    assert d.size == x.size
+    scales = np.empty(n_groups, dtype=np.uint16)
+    codes = np.empty(n_groups * 32 * bits // 8, dtype=np.uint8)
+    masks = np.empty(n_groups, dtype=np.uint32)
+    if n_groups:
+        lib().oracle_nbit_encode(_p(x), n_groups, bits, float(sigma), _p(d), _p(scales), _p(codes), _p(masks))
+    bitpos = ((masks[:, None] >> np.arange(32, dtype=np.uint32)[None, :]) & 1).astype(bool).reshape(-1)
+    idx = np.nonzero(bitpos)[0].astype(np.int32)
+    vals = x[idx]
+    return scales, codes, idx, vals
+
+
+def nbit_decode(scales: np.ndarray, codes: np.ndarray, bits: int, idx: np.ndarray, vals: np.ndarray) -> np.ndarray:
+    s = np.ascontiguousarray(scales, dtype=np.uint16)
+    c = np.ascontiguousarray(codes, dtype=np.uint8)
+    i = np.ascontiguousarray(idx, dtype=np.int32)
+    v = np.ascontiguousarray(vals, dtype=np.uint16)
+    n_groups = s.size
+    out = np.empty(n_groups * 32, dtype=np.uint16)
+    if n_groups:
+        lib().oracle_nbit_decode(_p(s), _p(c), n_groups, bits, _p(i), _p(v), i.size, _p(out))
+    return out
+
+
+def nbit_blob(num_tokens: int, scales, codes, idx, vals) -> bytes:
+    """Reference blob: <II tokens, n_out> + bf16 delta + int32 idx + bf16 vals + packed codes."""
+    return (struct.pack("<II", num_tokens, len(idx)) + np.asarray(scales, np.uint16).tobytes()
+            + np.asarray(idx, np.int32).tobytes() + np.asarray(vals, np.uint16).tobytes()
+            + np.asarray(codes, np.uint8).tobytes())
+
+
+def nbit_parse_blob(blob: bytes, hidden_dim: int = 128, group_size: int = 32):
+    """Inverse of nbit_blob -> (num_tokens, scales, idx, vals, codes)."""
+    num_tokens, n_out = struct.unpack("<II", blob[:8])
+    n_scales = num_tokens * (hidden_dim // group_size)
+    off = 8
+    scales = np.frombuffer(blob, np.uint16, n_scales, off); off += 2 * n_scales
+    idx = np.frombuffer(blob, np.int32, n_out, off); off += 4 * n_out
+    vals = np.frombuffer(blob, np.uint16, n_out, off); off += 2 * n_out
+    codes = np.frombuffer(blob, np.uint8, len(blob) - off, off)
+    return num_tokens, scales, idx, vals, codes
+
+
+def max_outliers_per_group(sigma: float, group: int = 32) -> int:
+    """Upper bound on elements with |x-mu| > sigma*std in one group.
+
+    m * sigma^2 < (group - 1) for the unbiased std, so m <= ceil((g-1)/sigma^2) - 1;
+    one extra slot of margin covers rounding in the threshold.
+    """
+    if sigma <= 0:
+        return group
+    return int(min(group, np.floor((group - 1) / (sigma * sigma)) + 1))
+
+
+# --------------------------------------------------------------------- hashes / RNG
+def xxh64(data: bytes, seed: int = 0) -> int:
+    buf = np.frombuffer(data, dtype=np.uint8) if len(data) else np.zeros(1, np.uint8)
+    return int(lib().oracle_xxh64(_p(buf), len(data), seed))
+
+
+def xxh64_items(data: np.ndarray, item_bytes: int, stride: int, n_items: int, seed: int = 0) -> np.ndarray:
+    buf = np.ascontiguousarray(data).view(np.uint8).reshape(-1)
+    out = np.empty(n_items, dtype=np.uint64)
+    if n_items:
+        lib().oracle_xxh64_items(_p(buf), n_items, item_bytes, stride, seed, _p(out))
+    return out
+
+
+def philox4x32_10(ctr, key) -> np.ndarray:
+    c = np.asarray(ctr, dtype=np.uint32)
+    k = np.asarray(key, dtype=np.uint32)
+    out = np.empty(4, dtype=np.uint32)
+    lib().oracle_philox4x32_10(_p(c), _p(k), _p(out))
+    return out
+
+
+def philox_dither(n: int, seed: int, offset: int = 0) -> np.ndarray:
+    out = np.empty(n, dtype=np.float32)
+    if n:
+        lib().oracle_philox_dither(n, seed, offset, _p(out))
+    return out
+
+
+# --------------------------------------------------------------------- policy
+NUM_TIERS = 6  # BF16, FP8, INT4, ARCHIVE, CPU, DISK
+TIER_BF16, TIER_FP8, TIER_INT4 = 0, 1, 2
+
+
+def score(T, S, N, P, w_T, w_S, w_N, w_P) -> np.ndarray:
+    """R = clip(((wT*T + wS*S) + wN*N) + wP*P, 0, 1), each op one fp32 rounding."""
+    n = len(T)
+    if not (len(S) == len(N) == len(P) == n) or n == 0:
+        return np.zeros(0, dtype=np.float32)
+    R = np.float32(w_T) * T + np.float32(w_S) * S + np.float32(w_N) * N + np.float32(w_P) * P
+    return np.clip(R, np.float32(0.0), np.float32(1.0))
+
+
+def thresholds(pressure: float, theta_high: float, theta_low: float, delta: float,
+               p_emergency: float) -> tuple[float, float]:
+    """(promote_threshold, demote_threshold) in Python doubles."""
+    boost = 0.0
+    if pressure >= p_emergency:
+        boost = min((pressure - p_emergency) * 2.0, 0.15)
+    return theta_high + delta, (theta_low + boost) - delta
+
+
+def desired_tiers(R, cur, pressure, theta_high, theta_low, delta, p_emergency, next_colder, next_hotter):
+    n = len(R)
+    if n == 0 or len(cur) != n:
+        return np.asarray(cur).copy()
+    up, down = thresholds(pressure, theta_high, theta_low, delta, p_emergency)
+    tgt = np.array(cur, copy=True)
+    pm = (R >= np.float32(up)) & (cur > TIER_BF16)
+    tgt[pm] = next_hotter[cur[pm]]
+    dm = (R <= np.float32(down)) & (cur < TIER_INT4)
+    tgt[dm] = next_colder[cur[dm]]
+    return tgt
+
+
+def controller_tables(codec_keys) -> tuple[np.ndarray, np.ndarray]:
+    """next_colder / next_hotter lookup tables from the codec table's (from, to) keys."""
+    nc = np.arange(NUM_TIERS, dtype=np.int8)
+    nh = np.arange(NUM_TIERS, dtype=np.int8)
+    for i in range(NUM_TIERS - 1):
+        nc[i] = i + 1
+    for i in range(1, NUM_TIERS):
+        nh[i] = i - 1
+    keys = list(codec_keys)
+    for src in range(NUM_TIERS):
+        colder = [t for (s, t) in keys if s == src and t > src]
+        if colder:
+            nc[src] = min(colder)
+        hotter = [t for (s, t) in keys if s == src and t < src]
+        if hotter:
+            nh[src] = max(hotter)
+    return nc, nh
