@@ -1,0 +1,230 @@
+"""Dithered N-bit (2/4/8) group codec with sigma-rule outlier isolation on sm_100a.
+
+Drop-in for ``DitheredNBitCodec`` (ashkv/codecs/nbit_dithered.py:14-167 of
+the reference): same constructor, same blob layout
+``<II num_tokens, num_outliers> + bf16 delta[num_tokens*hidden_dim/32]
++ int32 outlier_index[] + bf16 outlier_value[] + packed codes`` (MSB-first),
+same empty-input behaviour and the same SHA-256-based ``checksum``.
+
+Dither.  The reference draws ``U = torch.rand(...)`` from a CUDA generator
+seeded ``42 + encode_calls``.  Here ``encode`` generates the dither in-kernel
+from Philox4x32-10 keyed by that same seed (a different random stream, same
+distribution and seeding policy).  Passing ``uniform=`` (the U tensor the
+reference would draw) reproduces the reference's output bit for bit.
+
+Device-resident entry points (no host copies): :func:`encode_groups`,
+:func:`decode_groups` and :class:`NBitEncoded`.
+"""
+from __future__ import annotations
+
+import hashlib
+import math
+import struct
+from dataclasses import dataclass
+from typing import Optional
+
+import numpy as np
+import torch
+
+from .. import _native, _staging
+
+
+def max_outliers_per_group(sigma: float, group: int = 32) -> int:
+    """Bound on how many of ``group`` values can satisfy |x - mean| > sigma * std.
+
+    With the unbiased std, m * sigma^2 < group - 1; one extra slot of margin
+    absorbs rounding in the threshold.
+    """
+    if not sigma > 0:
+        return group
+    return int(min(group, math.floor((group - 1) / (sigma * sigma)) + 1))
+
+
+@dataclass
+class NBitEncoded:
+    """Device-resident encoding of ``n_groups`` groups of 32 elements."""
+    bits: int
+    n_groups: int
+    scales: torch.Tensor          # bf16 [n_groups]
+    codes: torch.Tensor           # uint8 [n_groups * 32 * bits / 8]
+    bucket_counts: torch.Tensor   # int32 [n_buckets] (true counts)
+    bucket_entries: torch.Tensor  # int32 [n_buckets * bucket_cap]: (local_idx << 16) | bf16 bits
+    bucket_cap: int
+    status: torch.Tensor          # int32 [1], ASHKV_FLAG_* bits
+
+    @property
+    def n_buckets(self) -> int:
+        return _native.nbit_bucket_count(self.n_groups)
+
+    @staticmethod
+    def allocate(n_groups: int, bits: int, bucket_cap: int, device: torch.device) -> "NBitEncoded":
+        nb = _native.nbit_bucket_count(n_groups)
+        return NBitEncoded(
+            bits=bits, n_groups=n_groups,
+            scales=torch.empty(n_groups, dtype=torch.bfloat16, device=device),
+            codes=torch.empty(max(n_groups * 32 * bits // 8, 16), dtype=torch.uint8, device=device),
+            bucket_counts=torch.empty(max(nb, 1), dtype=torch.int32, device=device),
+            bucket_entries=torch.empty(max(nb * bucket_cap, 1), dtype=torch.int32, device=device),
+            bucket_cap=bucket_cap,
+            status=torch.zeros(1, dtype=torch.int32, device=device))
+
+
+def encode_groups(src: torch.Tensor, bits: int, sigma: float = 3.0, *, uniform: Optional[torch.Tensor] = None,
+                  seed: int = 42, dither_offset: int = 0, bucket_cap: Optional[int] = None,
+                  out: Optional[NBitEncoded] = None) -> NBitEncoded:
+    """Encode a contiguous bf16 CUDA tensor (numel a multiple of 32).
+
+    ``bucket_cap`` defaults to the worst case for ``sigma`` (never overflows).
+    ``out`` lets callers reuse preallocated buffers; its status word is
+    cleared here.
+    """
+    n_groups = src.numel() // 32
+    if out is None:
+        if bucket_cap is None:
+            bucket_cap = _native.NBIT_BUCKET_GROUPS * max_outliers_per_group(sigma)
+        out = NBitEncoded.allocate(n_groups, bits, bucket_cap, src.device)
+    else:
+        out.status.zero_()
+    _native.nbit_encode(src.reshape(-1), bits, sigma, out.scales, out.codes, out.bucket_counts,
+                        out.bucket_entries, out.bucket_cap, out.status,
+                        dither=None if uniform is None else uniform.reshape(-1), seed=seed,
+                        dither_offset=dither_offset)
+    return out
+
+
+def decode_groups(enc: NBitEncoded, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Decode an :class:`NBitEncoded` back to bf16 (outliers restored)."""
+    if out is None:
+        out = torch.empty(enc.n_groups * 32, dtype=torch.bfloat16, device=enc.scales.device)
+    _native.nbit_decode(enc.scales, enc.codes, enc.n_groups, enc.bits, out, enc.status,
+                        enc.bucket_counts, enc.bucket_entries, enc.bucket_cap)
+    return out
+
+
+def flatten_outliers(enc: NBitEncoded) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """Bucketed outliers -> (int32 flat index, bf16-bit values, total) on the device."""
+    dev = enc.scales.device
+    nb = enc.n_buckets
+    cap_total = max(nb * enc.bucket_cap, 1)
+    offsets = torch.empty(nb + 1, dtype=torch.int32, device=dev)
+    idx = torch.empty(cap_total, dtype=torch.int32, device=dev)
+    val = torch.empty(cap_total, dtype=torch.int16, device=dev)
+    total = torch.empty(1, dtype=torch.int32, device=dev)
+    _native.nbit_outliers_flatten(enc.bucket_counts, enc.bucket_entries, enc.bucket_cap, nb, offsets, idx, val,
+                                  total)
+    return idx, val, total
+
+
+def _sha8(raw: bytes) -> int:
+    return int.from_bytes(hashlib.sha256(raw).digest()[:8], "little", signed=False)
+
+
+class DitheredNBitCodec:
+    """N-bit codec: group quantisation, sigma-rule outliers, stochastic dither."""
+
+    __slots__ = ("_encode_calls", "_decode_calls", "_hidden_dim", "_group_size", "_sigma", "_bits",
+                 "_num_states", "_half_states")
+
+    def __init__(self, hidden_dim: int = 128, group_size: int = 32, sigma: float = 3.0, bits: int = 4) -> None:
+        if bits not in (2, 4, 8):
+            raise ValueError(f"DitheredNBitCodec only supports 2, 4, or 8 bits. Got: {bits}")
+        if group_size != 32:
+            raise ValueError(f"group_size must be 32 for the sm_100a kernel, got {group_size}")
+        self._encode_calls = 0
+        self._decode_calls = 0
+        self._hidden_dim = hidden_dim
+        self._group_size = group_size
+        self._sigma = sigma
+        self._bits = bits
+        self._num_states = 2 ** bits
+        self._half_states = (self._num_states - 1) / 2.0
+
+    # The dither seed for this call (the reference seeds its generator the same way).
+    def _seed(self) -> int:
+        return 42 + self._encode_calls
+
+    def checksum(self, raw_bytes: bytes) -> int:
+        return _sha8(raw_bytes)
+
+    def encode(self, source_bytes: bytes, *, uniform=None) -> bytes:
+        """Encode bf16 bytes.  ``uniform`` (optional, fp32, one value per encoded
+        element, CPU or CUDA) replaces the in-kernel dither with the given U."""
+        self._encode_calls += 1
+        if not source_bytes:
+            return struct.pack("<II", 0, 0)
+        _staging.check_even(source_bytes)
+        L = self._hidden_dim
+        num_tokens = (len(source_bytes) // 2) // L
+        if num_tokens == 0:
+            return struct.pack("<II", 0, 0)
+        if L % self._group_size:
+            raise RuntimeError(f"shape '[{num_tokens}, {L // self._group_size}, {self._group_size}]' is invalid "
+                               f"for input of size {num_tokens * L}")
+        dev = _staging.device()
+        n_elems = num_tokens * L
+        h_in = _staging.pinned(2 * n_elems, "in")
+        h_in.numpy()[:] = np.frombuffer(source_bytes, dtype=np.uint8, count=2 * n_elems)
+        d_src = torch.empty(2 * n_elems, dtype=torch.uint8, device=dev)
+        d_src.copy_(h_in, non_blocking=True)
+        u = None
+        if uniform is not None:
+            u = torch.as_tensor(uniform, dtype=torch.float32).reshape(-1)
+            if u.numel() != n_elems:
+                raise ValueError(f"uniform has {u.numel()} values, expected {n_elems}")
+            u = u.to(dev, non_blocking=True).contiguous()
+        enc = encode_groups(d_src.view(torch.bfloat16), self._bits, self._sigma, uniform=u, seed=self._seed())
+        idx, val, total = flatten_outliers(enc)
+        n_out = int(total.item())  # one sync: the blob layout depends on the outlier count
+        n_groups = enc.n_groups
+        n_codes = n_groups * 32 * self._bits // 8
+        size = 8 + 2 * n_groups + 6 * n_out + n_codes
+        h_out = _staging.pinned(size, "out")
+        h_out.numpy()[:8] = np.frombuffer(struct.pack("<II", num_tokens, n_out), dtype=np.uint8)
+        o = 8
+        h_out[o:o + 2 * n_groups].copy_(enc.scales.view(torch.uint8), non_blocking=True); o += 2 * n_groups
+        if n_out:
+            h_out[o:o + 4 * n_out].copy_(idx[:n_out].view(torch.uint8), non_blocking=True); o += 4 * n_out
+            h_out[o:o + 2 * n_out].copy_(val[:n_out].view(torch.uint8), non_blocking=True); o += 2 * n_out
+        h_out[o:o + n_codes].copy_(enc.codes[:n_codes], non_blocking=True)
+        torch.cuda.current_stream(dev).synchronize()
+        return h_out.numpy().tobytes()
+
+    def decode(self, target_bytes: bytes) -> bytes:
+        self._decode_calls += 1
+        if len(target_bytes) < 8:
+            return b""
+        num_tokens, n_out = struct.unpack("<II", target_bytes[:8])
+        if num_tokens == 0:
+            return b""
+        groups_per_row = self._hidden_dim // self._group_size
+        n_groups = num_tokens * groups_per_row
+        n_codes = n_groups * 32 * self._bits // 8
+        need = 8 + 2 * n_groups + 6 * n_out + n_codes
+        if len(target_bytes) < need:
+            raise RuntimeError(f"N-bit blob too short: {len(target_bytes)} bytes, layout needs {need}")
+        dev = _staging.device()
+        body = len(target_bytes) - 8
+        h_in = _staging.pinned(body, "in")
+        h_in.numpy()[:] = np.frombuffer(target_bytes, dtype=np.uint8, offset=8)
+        d_sc = torch.empty(2 * n_groups, dtype=torch.uint8, device=dev)
+        d_idx = torch.empty(max(4 * n_out, 4), dtype=torch.uint8, device=dev)
+        d_val = torch.empty(max(2 * n_out, 2), dtype=torch.uint8, device=dev)
+        d_codes = torch.empty(max(n_codes, 16), dtype=torch.uint8, device=dev)
+        o = 0
+        d_sc.copy_(h_in[o:o + 2 * n_groups], non_blocking=True); o += 2 * n_groups
+        if n_out:
+            d_idx[:4 * n_out].copy_(h_in[o:o + 4 * n_out], non_blocking=True); o += 4 * n_out
+            d_val[:2 * n_out].copy_(h_in[o:o + 2 * n_out], non_blocking=True); o += 2 * n_out
+        d_codes[:n_codes].copy_(h_in[o:o + n_codes], non_blocking=True)
+        out = torch.empty(n_groups * 32, dtype=torch.bfloat16, device=dev)
+        status = torch.zeros(1, dtype=torch.int32, device=dev)
+        _native.nbit_decode_flat(d_sc.view(torch.bfloat16), d_codes, n_groups, self._bits,
+                                 d_idx.view(torch.int32) if n_out else None,
+                                 d_val.view(torch.int16) if n_out else None, n_out, out, status)
+        h_out = _staging.pinned(2 * n_groups * 32, "out")
+        h_out.copy_(out.view(torch.uint8), non_blocking=True)
+        st = status.to("cpu", non_blocking=True)
+        torch.cuda.current_stream(dev).synchronize()
+        if int(st.item()) & _native.FLAG_INDEX_RANGE:
+            raise IndexError(f"outlier index out of range for a decoded size of {n_groups * 32} elements")
+        return h_out.numpy().tobytes()

@@ -147,7 +147,9 @@ __global__ void __launch_bounds__(kThreads) nbit_encode_kernel(const NbitEncPara
 #pragma unroll
       for (int k = 0; k < 8; ++k) {
         const float4 v = ld_nc_f4(dp + 4 * k);
-        dz[4 * k + 0] = v.x; dz[4 * k + 1] = v.y; dz[4 * k + 2] = v.z; dz[4 * k + 3] = v.w;
+        // U - 0.5 is exact for U in [0, 1)
+        dz[4 * k + 0] = __fadd_rn(v.x, -0.5f); dz[4 * k + 1] = __fadd_rn(v.y, -0.5f);
+        dz[4 * k + 2] = __fadd_rn(v.z, -0.5f); dz[4 * k + 3] = __fadd_rn(v.w, -0.5f);
       }
     } else {
 #pragma unroll

@@ -1,0 +1,335 @@
+#!/usr/bin/env python
+"""Benchmark: ASH-KV dithered INT4 codec round trip (encode + decode) on B200.
+
+Workload (one step): the INT4 dithered codec with 3-sigma outlier isolation
+over K and V, each bf16 [4096 pages, 16 tokens, 8 KV heads, 128 head_dim],
+values N(0,1) with 0.1% of entries (seeded positions) scaled x50, dither from
+in-kernel Philox4x32-10 (seed per step).  A step encodes K and V and decodes
+both back to bf16.
+
+``value``  — bf16 bytes of K+V pushed through encode AND decode per second,
+             inputs resident in HBM (device-timed with CUDA events), summed
+             over ranks (weak scaling: every rank owns its own K/V shard).
+``e2e``    — the same metric through the public bytes API
+             (``DitheredNBitCodec.encode(bytes)`` / ``.decode(bytes)``) with
+             host buffers, host<->device copies inside the timed region.
+``roofline`` — the encode kernel (the dominant one): algorithmic bytes per
+             launch / its average CUDA-event duration vs the measured HBM copy
+             peak.
+``cpu_baseline`` — the oracle's scalar C port of the reference codec on one
+             host core, on a bounded sample of the same data.
+
+``--impl reference`` times that CPU port with all host threads instead (the
+reference arm; no GPU work).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import re
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO / "ash-kv_b200"))
+sys.path.insert(0, str(REPO))
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+
+PAGES, TOKENS, HEADS, HEAD_DIM = 4096, 16, 8, 128
+ELEMS = PAGES * TOKENS * HEADS * HEAD_DIM          # per tensor (K or V)
+BITS, SIGMA = 4, 3.0
+METRIC = "codec encode+decode GB/s (bf16 bytes) per GPU & % HBM peak; demote pages/s at 1/2/4/8"
+WORKLOAD = ("INT4 dithered codec round trip (3-sigma outliers, group 32, Philox dither): K and V bf16 "
+            "[4096 pages, 16 tokens, 8 KV heads, 128 head_dim] each, N(0,1) with 0.1% x50 outliers")
+
+
+def measured_hbm_peak() -> tuple[float, str]:
+    p = REPO / "MEASURED_PEAKS.json"
+    try:
+        return float(json.loads(p.read_text())["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def profile_traffic() -> float | None:
+    """DRAM bytes per encode launch from the committed ncu summary, if present."""
+    p = REPO / "profiles" / "nbit_encode_int4_config2.md"
+    if not p.exists():
+        return None
+    m = re.search(r"dram_bytes_per_launch:\s*([0-9.eE+]+)", p.read_text())
+    return float(m.group(1)) if m else None
+
+
+def make_kv(seed: int, device) -> torch.Tensor:
+    g = torch.Generator(device=device).manual_seed(seed)
+    x = torch.randn(ELEMS, generator=g, device=device)
+    pos = torch.randperm(ELEMS, generator=g, device=device)[: ELEMS // 1000]
+    x[pos] *= 50.0
+    return x.to(torch.bfloat16)
+
+
+class ClockSampler:
+    """nvidia-smi samples of SM clock and throttle reasons during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines: list[str] = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+        return False
+
+    def summary(self) -> dict:
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx.append(float(parts[2]))
+            except ValueError:
+                continue
+            for name, flag in zip(names, parts[5:9]):
+                if flag.lower() == "active":
+                    reasons.add(name)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ------------------------------------------------------------------ CPU legs
+def cpu_port_rate(threads: int, budget_s: float) -> tuple[float, dict]:
+    """bf16 GB/s of the oracle's C port (encode + decode) over config-2 sample chunks."""
+    import oracle
+    from concurrent.futures import ThreadPoolExecutor
+
+    chunk = 64 * TOKENS * HEADS * HEAD_DIM  # 64 pages
+    g = torch.Generator().manual_seed(0)
+    x = torch.randn(chunk * 4, generator=g)
+    pos = torch.randperm(x.numel(), generator=g)[: x.numel() // 1000]
+    x[pos] *= 50.0
+    xb = x.to(torch.bfloat16).view(torch.int16).numpy().view(np.uint16)
+    chunks = [xb[i * chunk:(i + 1) * chunk] for i in range(4)]
+    oracle.lib()  # build/load before timing
+
+    def one(i: int) -> int:
+        c = chunks[i % 4]
+        u = oracle.philox_dither(c.size, 42, 0)
+        sc, codes, idx, vals = oracle.nbit_encode(c, BITS, u, SIGMA)
+        oracle.nbit_decode(sc, codes, BITS, idx, vals)
+        return c.size
+
+    done = 0
+    t0 = time.perf_counter()
+    with ThreadPoolExecutor(max_workers=threads) as ex:
+        i = 0
+        while time.perf_counter() - t0 < budget_s:
+            done += sum(ex.map(one, range(i, i + threads)))
+            i += threads
+    dt = time.perf_counter() - t0
+    rate = done * 2 / dt / 1e9
+    return rate, {"elements": done, "seconds": round(dt, 3),
+                  "sample": f"{done // chunk} chunks of 64 pages x [16,8,128] bf16 (config-2 data), "
+                            f"encode+decode, Philox dither"}
+
+
+def run_reference(args) -> None:
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    steps = []
+    for _ in range(args.warmup):
+        cpu_port_rate(threads, 1.0)
+    for _ in range(args.steps):
+        r, info = cpu_port_rate(threads, args.ref_seconds)
+        steps.append((r, info))
+    vals = [r for r, _ in steps]
+    value = statistics.median(vals)
+    info = steps[-1][1]
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(value, 4), "unit": "GB/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(args.ref_seconds * 1000, 1), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": WORKLOAD, "sample": info["sample"]},
+        "cpu_baseline": {"value": round(value, 4), "unit": "GB/s", "cores": threads, "kind": "port",
+                         "sample": info["sample"]},
+        "e2e": {"value": round(value, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------ GPU leg
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ashkv", choices=["ashkv", "reference"])
+    ap.add_argument("--e2e-steps", type=int, default=3)
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--ref-seconds", type=float, default=5.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+        return
+
+    from ashkv import _build
+    if _build.needs_build():
+        _build.build_library()
+    from ashkv.codecs import DitheredNBitCodec
+    from ashkv.codecs import nbit_dithered as nb
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+
+    K = make_kv(1000 + 2 * rank, dev)
+    V = make_kv(1001 + 2 * rank, dev)
+    cap = 256 * nb.max_outliers_per_group(SIGMA)
+    encK = nb.NBitEncoded.allocate(ELEMS // 32, BITS, cap, dev)
+    encV = nb.NBitEncoded.allocate(ELEMS // 32, BITS, cap, dev)
+    outK = torch.empty_like(K)
+    outV = torch.empty_like(V)
+    stream = torch.cuda.current_stream(dev)
+
+    def step(i: int, ev=None):
+        if ev is not None:
+            ev[0].record(stream)
+        nb.encode_groups(K, BITS, SIGMA, seed=2 * i, out=encK)
+        if ev is not None:
+            ev[1].record(stream)
+        nb.encode_groups(V, BITS, SIGMA, seed=2 * i + 1, out=encV, dither_offset=0)
+        if ev is not None:
+            ev[2].record(stream)
+        nb.decode_groups(encK, out=outK)
+        nb.decode_groups(encV, out=outV)
+
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        torch.cuda.synchronize()
+        start.record(stream)
+        for i in range(args.steps):
+            step(args.warmup + i, evs[i])
+        stop.record(stream)
+        torch.cuda.synchronize()
+    elapsed_ms = start.elapsed_time(stop)
+    enc_ms = statistics.mean([e[0].elapsed_time(e[1]) for e in evs] + [e[1].elapsed_time(e[2]) for e in evs])
+    n_out = int(encK.bucket_counts.sum().item())
+
+    # end-to-end through the bytes API (host buffers)
+    codec = DitheredNBitCodec(hidden_dim=HEAD_DIM, group_size=32, sigma=SIGMA, bits=BITS)
+    hostK = K.cpu().view(torch.int16).numpy().tobytes()
+    hostV = V.cpu().view(torch.int16).numpy().tobytes()
+    blob = codec.encode(hostK)
+    codec.decode(blob)  # warm
+    h2d = d2h = 0
+    t_e2e = 0.0
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    for _ in range(args.e2e_steps):
+        t0 = time.perf_counter()
+        bk = codec.encode(hostK)
+        bv = codec.encode(hostV)
+        dk = codec.decode(bk)
+        dv = codec.decode(bv)
+        t_e2e += time.perf_counter() - t0
+        h2d = len(hostK) + len(hostV) + (len(bk) - 8) + (len(bv) - 8)
+        d2h = (len(bk) - 8) + (len(bv) - 8) + len(dk) + len(dv)
+
+    # max over ranks
+    t = torch.tensor([elapsed_ms, t_e2e], dtype=torch.float64, device=dev)
+    if dist:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    elapsed_ms, t_e2e = float(t[0]), float(t[1])
+
+    bytes_per_step = 2 * ELEMS * 2  # bf16 K + V through encode and decode
+    value = world * bytes_per_step * args.steps / (elapsed_ms / 1e3) / 1e9
+    e2e_value = world * bytes_per_step * args.e2e_steps / t_e2e / 1e9
+    enc_alg_bytes = ELEMS * 2 + ELEMS * BITS // 8 + (ELEMS // 32) * 2 + 4 * n_out + 4 * nb._native.nbit_bucket_count(ELEMS // 32)
+    achieved = enc_alg_bytes / (enc_ms / 1e3) / 1e9
+    peak, peak_kind = measured_hbm_peak()
+    traffic = profile_traffic()
+
+    if rank == 0:
+        cpu = None
+        if not args.no_cpu_baseline:
+            r, info = cpu_port_rate(1, args.cpu_seconds)
+            cpu = {"value": round(r, 5), "unit": "GB/s", "cores": 1, "kind": "port", "sample": info["sample"]}
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(elapsed_ms / args.steps, 4), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": WORKLOAD, "pages_per_rank": PAGES, "bits": BITS, "sigma": SIGMA,
+                       "bytes_per_step_per_rank": bytes_per_step, "l2": "inputs larger than L2 (256 MiB per rank)",
+                       "parallelism": f"replicas x{world} (pages sharded, no collective)"},
+            "encode_gbs_bf16": round(world * ELEMS * 2 / (enc_ms / 1e3) / 1e9, 2),
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "traffic": traffic, "peak_kind": peak_kind,
+                         "kernel": "nbit_encode_kernel<4,PHILOX>",
+                         "alg_bytes_per_launch": enc_alg_bytes, "avg_launch_ms": round(enc_ms, 4)},
+            "e2e": {"value": round(e2e_value, 3), "unit": "GB/s", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h},
+            "gpu_launches": 4 * args.steps,
+            "clocks": clocks.summary(),
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -51,7 +51,7 @@ typedef int32_t ashkv_status_t;
 #define ASHKV_NBIT_GROUP          32    /* elements per quantisation group */
 #define ASHKV_NBIT_BUCKET_GROUPS  256   /* groups per outlier bucket */
 #define ASHKV_NBIT_BUCKET_ELEMS   8192  /* elements per outlier bucket */
-#define ASHKV_DITHER_TENSOR 0           /* dither read from a caller fp32 tensor (U - 0.5) */
+#define ASHKV_DITHER_TENSOR 0           /* uniform U in [0,1) read from a caller fp32 tensor */
 #define ASHKV_DITHER_PHILOX 1           /* dither generated in-kernel: Philox4x32-10(seed) */
 
 /* ---- flags for the INT8 codec ------------------------------------------- */
@@ -116,15 +116,16 @@ ASHKV_API ashkv_status_t ashkv_int8_decode_rows(
  *   outlier = |x - mu| > sigma * (sd + 1e-8)
  *   x'      = outlier ? mu : x
  *   delta   = max(max|x'|, 1e-8) / ((2^bits - 1) / 2)
- *   code    = clamp(rint((x' + dither * delta) / delta + half), 0, 2^bits - 1)
+ *   code    = clamp(rint((x' + (U - 0.5) * delta) / delta + half), 0, 2^bits - 1)
  * Outputs: d_scales (bf16 delta per group), d_codes (MSB-first packing,
  * 32*bits/8 bytes per group), and the outlier list in buckets of 256 groups:
  * d_bucket_counts[b] is the number of outliers of bucket b (even when it
  * exceeds bucket_cap), d_bucket_entries[b*bucket_cap + j] =
  * (element index within the bucket << 16) | bf16 bits, ascending.
- * dither_mode ASHKV_DITHER_TENSOR reads d_dither[e] (= U - 0.5, fp32, one per
- * element); ASHKV_DITHER_PHILOX derives it from Philox4x32-10 keyed by `seed`
- * at counter (dither_elem_offset + e) / 8.
+ * dither_mode ASHKV_DITHER_TENSOR reads U = d_dither[e] (fp32 in [0, 1), one
+ * per element, what torch.rand returns in the reference); ASHKV_DITHER_PHILOX
+ * derives U - 0.5 = h * 2^-16 - 0.5 from the (e & 7)-th 16-bit field of
+ * Philox4x32-10(key = seed, counter = (dither_elem_offset + e) / 8).
  * ======================================================================== */
 ASHKV_API ashkv_status_t ashkv_nbit_encode(
     const void* d_src, int64_t n_groups, int32_t bits, float sigma,
@@ -168,6 +169,42 @@ ASHKV_API ashkv_status_t ashkv_nbit_decode_flat(
 ASHKV_API ashkv_status_t ashkv_xxh64_items(
     const void* d_data, int64_t n_items, int64_t item_bytes, int64_t item_stride,
     uint64_t seed, uint64_t* d_out, void* stream);
+
+/* ========================================================================
+ * Page-table policy.
+ * ashkv_score replaces score_vectorized (ashkv/runtime/score.py:15-52):
+ *   R = clip(((w_T*T + w_S*S) + w_N*N) + w_P*P, 0, 1), one fp32 rounding per
+ *   operation, NaN kept.
+ * ashkv_desired_tiers replaces desired_tiers (ashkv/runtime/controller.py:32-106):
+ *   boost = min((pressure - p_emergency) * 2, 0.15) if pressure >= p_emergency else 0
+ *   up = theta_high + delta; down = theta_low + boost - delta   (double, then fp32)
+ *   target = cur; if R >= up and cur > BF16: target = next_hotter[cur];
+ *   if R <= down and cur < INT4: target = next_colder[cur]   (demotion wins).
+ *   next_colder / next_hotter are HOST arrays of 6 int8 (one per Tier), as
+ *   compiled by compile_controller (ashkv/compiler/runtime_builder.py:80-122).
+ *   Tiers outside [0, 6) are left unchanged.
+ * ashkv_policy_step fuses both and emits the ascending page-row lists of
+ * demotions (target > cur) and promotions (target < cur); d_counts[0..1] get
+ * their lengths.  d_scratch holds ashkv_policy_scratch_ints(n) int32.
+ * d_R may be NULL in ashkv_policy_step.
+ * ======================================================================== */
+ASHKV_API ashkv_status_t ashkv_score(const float* d_T, const float* d_S, const float* d_N, const float* d_P,
+                                     int64_t n, float w_T, float w_S, float w_N, float w_P, float* d_R,
+                                     void* stream);
+
+ASHKV_API ashkv_status_t ashkv_desired_tiers(const float* d_R, const int8_t* d_cur, int64_t n, double pressure,
+                                             double theta_high, double theta_low, double delta,
+                                             double p_emergency, const int8_t* next_colder,
+                                             const int8_t* next_hotter, int8_t* d_target, void* stream);
+
+ASHKV_API int64_t ashkv_policy_scratch_ints(int64_t n);
+
+ASHKV_API ashkv_status_t ashkv_policy_step(
+    const float* d_T, const float* d_S, const float* d_N, const float* d_P, const int8_t* d_cur, int64_t n,
+    float w_T, float w_S, float w_N, float w_P, double pressure, double theta_high, double theta_low,
+    double delta, double p_emergency, const int8_t* next_colder, const int8_t* next_hotter,
+    float* d_R, int8_t* d_target, int32_t* d_demote_list, int32_t* d_promote_list, int32_t* d_counts,
+    int32_t* d_scratch, void* stream);
 
 #ifdef __cplusplus
 }

@@ -100,7 +100,7 @@ def half_states(bits: int) -> float:
 def nbit_encode(x_bits: np.ndarray, bits: int, dither: np.ndarray, sigma: float = 3.0):
     """Encode groups of 32 bf16 values.
 
-    ``dither`` is ``U - 0.5`` in fp32, one per element.  Returns
+    ``dither`` is the uniform ``U`` in [0, 1) (fp32, one per element).  Returns
     ``(scales uint16[n_groups], codes uint8[n_groups*32*bits/8],
     outlier_index int32[n], outlier_value uint16[n])`` with indices ascending.
     """

@@ -125,7 +125,8 @@ static float max_nan(float a, float b) {
   return a > b ? a : b;
 }
 
-/* One group of 32 elements; see the header comment of ashkv_nbit_encode. */
+/* Groups of 32 elements; `dither` holds U in [0, 1) per element (the
+ * reference's torch.rand draw), noise = (U - 0.5) * delta. */
 void oracle_nbit_encode(const uint16_t* src, int64_t n_groups, int bits, float sigma,
                         const float* dither, uint16_t* scales, uint8_t* codes, uint32_t* omask_out) {
   const float half = (float)((1 << bits) - 1) / 2.0f;
@@ -166,7 +167,7 @@ void oracle_nbit_encode(const uint16_t* src, int64_t n_groups, int bits, float s
     if (omask_out) omask_out[g] = om;
     uint32_t code[32];
     for (int i = 0; i < 32; ++i) {
-      const float noise = dither[g * 32 + i] * delta;
+      const float noise = (dither[g * 32 + i] - 0.5f) * delta;
       const float a = x[i] + noise;
       const float v = a / delta + half;
       float vc = isnan(v) ? 0.0f : v;
@@ -263,9 +264,9 @@ void oracle_philox4x32_10(const uint32_t ctr[4], const uint32_t key[2], uint32_t
   out[0] = c0; out[1] = c1; out[2] = c2; out[3] = c3;
 }
 
-/* Dither values the PHILOX mode of the kernel uses for elements
- * [offset, offset + n): d = h16 * 2^-16 - 0.5 with h16 the (e & 7)-th 16-bit
- * field (little-endian order) of Philox4x32-10(counter = e >> 3, key = seed). */
+/* Uniforms U = h16 * 2^-16 that the PHILOX mode of the kernel uses for
+ * elements [offset, offset + n), h16 being the (e & 7)-th 16-bit field
+ * (little-endian order) of Philox4x32-10(counter = e >> 3, key = seed). */
 void oracle_philox_dither(int64_t n, uint64_t seed, uint64_t offset, float* out) {
   const uint32_t key[2] = {(uint32_t)seed, (uint32_t)(seed >> 32)};
   uint64_t cached = ~0ull;
@@ -280,6 +281,6 @@ void oracle_philox_dither(int64_t n, uint64_t seed, uint64_t offset, float* out)
     }
     const int f = (int)(e & 7u);
     const uint32_t h = (r[f >> 1] >> (16 * (f & 1))) & 0xFFFFu;
-    out[i] = (float)h * (1.0f / 65536.0f) - 0.5f;
+    out[i] = (float)h * (1.0f / 65536.0f);
   }
 }

@@ -1,0 +1,250 @@
+"""GPU parity: the sm_100a codec kernels (through the C ABI) against the oracle.
+
+Integer/byte outputs (codes, scales, outlier lists, packed blobs, decoded
+bf16 bits) must be bit-exact.  The oracle itself is pinned to the
+reference's outputs by tests/test_oracle_golden.py.
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from conftest import GOLDEN
+
+from ashkv import _native
+from ashkv.codecs import DitheredINT2Codec, DitheredNBitCodec, INT8Codec
+from ashkv.codecs import int8 as int8_mod
+from ashkv.codecs import nbit_dithered as nb
+
+pytestmark = pytest.mark.gpu
+
+NBIT = np.load(GOLDEN / "nbit.npz")
+INT8 = np.load(GOLDEN / "int8.npz")
+
+
+def bits_of(t: torch.Tensor) -> np.ndarray:
+    return t.detach().cpu().contiguous().view(torch.int16).numpy().view(np.uint16).reshape(-1)
+
+
+def rand_bf16(n: int, seed: int, kind: str = "normal") -> torch.Tensor:
+    g = torch.Generator().manual_seed(seed)
+    x = torch.randn(n, generator=g)
+    if kind == "wide":
+        x = x * torch.exp(torch.randn(n, generator=g) * 3.0)
+    elif kind == "outliers":
+        pos = torch.randperm(n, generator=g)[: max(1, n // 1000)]
+        x[pos] *= 50.0
+    return x.to(torch.bfloat16)
+
+
+# ------------------------------------------------------------------- INT8
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("row_len", [128, 1024, 4096, 8, 24, 136])
+@pytest.mark.parametrize("fp32_product", [False, True])
+def test_int8_rows_bitexact(cuda, dtype, row_len, fp32_product):
+    n_rows = 300
+    x = (rand_bf16(n_rows * row_len, row_len, "wide").float() * 0.25).to(dtype).view(n_rows, row_len)
+    codes = torch.empty(n_rows, row_len, dtype=torch.int8, device=cuda)
+    scales = torch.empty(n_rows, dtype=dtype, device=cuda)
+    _native.int8_encode_rows(x.to(cuda), codes, scales, fp32_product=fp32_product)
+    oc, osc = oracle.int8_encode(bits_of(x), row_len, src_fp16=dtype == torch.float16,
+                                 scale_fp16=dtype == torch.float16, fp32_product=fp32_product)
+    assert np.array_equal(codes.cpu().numpy(), oc)
+    assert np.array_equal(bits_of(scales), osc)
+    for out_dtype in (torch.bfloat16, torch.float16):
+        dec = torch.empty(n_rows, row_len, dtype=out_dtype, device=cuda)
+        _native.int8_decode_rows(codes, scales, dec)
+        want = oracle.int8_decode(oc, osc, scale_fp16=dtype == torch.float16, dst_fp16=out_dtype == torch.float16)
+        assert np.array_equal(bits_of(dec), want.reshape(-1))
+
+
+@pytest.mark.parametrize("ci", range(int(INT8["int8_n_cases"])))
+def test_int8_kernel_matches_reference_golden(cuda, ci):
+    pre = f"int8_{ci}_"
+    rows, L, _ = (int(v) for v in INT8[pre + "meta"])
+    src = torch.from_numpy(INT8[pre + "src"].view(np.int16).copy()).view(torch.float16).view(rows, L)
+    codes = torch.empty(rows, L, dtype=torch.int8, device=cuda)
+    scales = torch.empty(rows, dtype=torch.float16, device=cuda)
+    _native.int8_encode_rows(src.to(cuda), codes, scales)
+    got = codes.cpu().numpy()
+    x = src.float().numpy()
+    overflow = np.abs(x) * 127.0 > 65504.0  # fp16 product is inf: the reference cast is undefined there
+    assert np.array_equal(got[~overflow], INT8[pre + "codes"][~overflow])
+    assert np.array_equal(bits_of(scales), INT8[pre + "scales"])
+
+
+def test_int8_gather_and_flat_scale_slots(cuda):
+    """Hook layout: rows gathered by index, codes into slot rows, fp16 scales at the
+    reference's flat positions (token t -> slot t // H, offset 2 * (t % H))."""
+    H, D, n, cap = 8, 128, 37, 100
+    L = H * D
+    pool = rand_bf16(cap * L, 3).view(cap, L).to(cuda)
+    idx = torch.randperm(cap, generator=torch.Generator().manual_seed(4))[:n].to(cuda)
+    slot = 2 * H * D
+    staging = torch.zeros(n, slot, dtype=torch.uint8, device=cuda)
+    codes_view = staging[:, 2 * H:2 * H + L].view(torch.int8)
+    scales_base = staging.view(-1)[:].view(torch.float16)  # scale t at byte (t//H)*slot + 2*(t%H)
+    _native.int8_encode_rows(pool, codes_view, scales_base, row_index=idx, scales_per_slot=H,
+                             scale_slot_stride=slot)
+    oc, osc = oracle.int8_encode(bits_of(pool[idx.cpu()]), L, scale_fp16=True)
+    st = staging.cpu().numpy()
+    assert np.array_equal(st[:, 2 * H:2 * H + L].view(np.int8), oc)
+    flat = st[:, :2 * H].copy().view(np.uint16).reshape(-1)  # concatenated per-slot scale regions
+    assert np.array_equal(flat[:n], osc)
+    # decode straight back into a scattered destination
+    out = torch.zeros(cap, L, dtype=torch.bfloat16, device=cuda)
+    _native.int8_decode_rows(codes_view, scales_base, out, row_index=idx, scales_per_slot=H, scale_slot_stride=slot)
+    want = oracle.int8_decode(oc, osc, scale_fp16=True)
+    assert np.array_equal(bits_of(out[idx]).reshape(n, L), want)
+
+
+def test_int8_codec_bytes_api_matches_oracle(cuda):
+    x = rand_bf16(123 * 128 + 5, 9)  # ragged tail: trailing values are dropped
+    codec = INT8Codec()
+    blob = codec.encode(bits_of(x).tobytes())
+    oc, osc = oracle.int8_encode(bits_of(x)[:123 * 128], 128)
+    assert blob == oracle.int8_blob(oc, osc)
+    dec = codec.decode(blob)
+    assert dec == oracle.int8_decode(oc, osc).tobytes()
+    assert codec.encode(b"") == b"\x00\x00\x00\x00"
+    assert codec.encode(b"\x00\x01" * 10) == b"\x00\x00\x00\x00"
+    assert codec.decode(b"\x00\x00\x00\x00") == b"" and codec.decode(b"\x01") == b""
+    with pytest.raises(ValueError):
+        codec.encode(b"\x00\x01\x02")
+
+
+def test_int8_reference_fidelity_budget(cuda):
+    """The reference GPU test's bounds: cos > 0.99, MSE < 0.05 on fp16 [1024, 32, 128]."""
+    g = torch.Generator(device="cpu").manual_seed(0)
+    x = (torch.randn(1024, 32, 128, generator=g) * 0.5 + 0.1).half().to(cuda)
+    codes, scales = int8_mod.encode_rows(x.view(1024, -1), scale_dtype=torch.float16)
+    y = int8_mod.decode_rows(codes, scales, out_dtype=torch.float16)
+    a, b = x.float().view(-1), y.float().view(-1)
+    assert torch.nn.functional.cosine_similarity(a[None], b[None]).item() > 0.99
+    assert torch.nn.functional.mse_loss(a, b).item() < 0.05
+
+
+def test_int8_nan_inf_do_not_crash(cuda):
+    x = torch.zeros(2, 1, 128, dtype=torch.float16, device=cuda)
+    x[0, 0, 0], x[0, 0, 1], x[1, 0, 0] = float("inf"), float("nan"), 65504.0
+    codes, scales = int8_mod.encode_rows(x.view(2, -1), scale_dtype=torch.float16)
+    torch.cuda.synchronize()
+    assert codes.shape == (2, 128)
+    c = codes.cpu()
+    assert c[0, 1].item() == 0  # NaN -> 0
+
+
+# ------------------------------------------------------------------- N-bit
+@pytest.mark.parametrize("ci", range(int(NBIT["nbit_n_cases"])))
+def test_nbit_bytes_api_reproduces_reference_blob(cuda, ci):
+    pre = f"nbit_{ci}_"
+    bits, hidden, is_int2, n, _trail = (int(v) for v in NBIT[pre + "meta"])
+    sigma = float(NBIT[pre + "sigma"])
+    codec = DitheredINT2Codec(hidden) if is_int2 else DitheredNBitCodec(hidden, 32, sigma, bits)
+    src = NBIT[pre + "src"].tobytes()
+    blob = codec.encode(src, uniform=NBIT[pre + "u"] if n else None)
+    assert blob == NBIT[pre + "blob"].tobytes()
+    assert codec.decode(blob) == NBIT[pre + "decoded"].tobytes()
+
+
+@pytest.mark.parametrize("bits", [2, 4, 8])
+@pytest.mark.parametrize("kind", ["normal", "wide", "outliers"])
+def test_nbit_kernel_vs_oracle_tensor_dither(cuda, bits, kind):
+    n = 300 * 8192 + 96  # ragged last bucket
+    x = rand_bf16(n, 17 + bits, kind)
+    u = torch.rand(n, generator=torch.Generator().manual_seed(5))
+    enc = nb.encode_groups(x.to(cuda), bits, 3.0, uniform=u.to(cuda))
+    osc, ocodes, oidx, ovals = oracle.nbit_encode(bits_of(x), bits, u.numpy(), 3.0)
+    assert np.array_equal(bits_of(enc.scales), osc)
+    assert np.array_equal(enc.codes[: ocodes.size].cpu().numpy(), ocodes)
+    idx, val, total = nb.flatten_outliers(enc)
+    t = int(total.item())
+    assert t == oidx.size
+    assert np.array_equal(idx[:t].cpu().numpy(), oidx)
+    assert np.array_equal(val[:t].cpu().numpy().view(np.uint16), ovals)
+    assert int(enc.status.item()) == 0
+    dec = nb.decode_groups(enc)
+    want = oracle.nbit_decode(osc, ocodes, bits, oidx, ovals)
+    assert np.array_equal(bits_of(dec), want)
+
+
+@pytest.mark.parametrize("bits", [2, 4])
+def test_nbit_philox_dither_matches_oracle(cuda, bits):
+    n = 64 * 8192
+    x = rand_bf16(n, 23, "outliers")
+    seed, offset = 0x1234_5678_9ABC, 4096
+    enc = nb.encode_groups(x.to(cuda), bits, 3.0, seed=seed, dither_offset=offset)
+    u = oracle.philox_dither(n, seed, offset)
+    osc, ocodes, oidx, ovals = oracle.nbit_encode(bits_of(x), bits, u, 3.0)
+    assert np.array_equal(bits_of(enc.scales), osc)
+    assert np.array_equal(enc.codes[: ocodes.size].cpu().numpy(), ocodes)
+
+
+def test_nbit_bucket_overflow_is_flagged(cuda):
+    n = 4 * 8192
+    x = rand_bf16(n, 31, "outliers")
+    enc = nb.encode_groups(x.to(cuda), 4, 3.0, uniform=torch.rand(n).to(cuda), bucket_cap=2)
+    torch.cuda.synchronize()
+    assert int(enc.status.item()) & _native.FLAG_OUTLIER_OVERFLOW
+    counts = enc.bucket_counts.cpu().numpy()
+    assert counts.max() > 2  # true counts are reported even past the capacity
+
+
+def test_nbit_decode_paths_agree(cuda):
+    n = 40 * 8192
+    x = rand_bf16(n, 41, "outliers").to(cuda)
+    enc = nb.encode_groups(x, 4, 3.0)
+    a = nb.decode_groups(enc)
+    idx, val, total = nb.flatten_outliers(enc)
+    t = int(total.item())
+    b = torch.empty_like(a)
+    _native.nbit_decode_flat(enc.scales, enc.codes, enc.n_groups, 4, idx[:t], val[:t], t, b, enc.status)
+    assert torch.equal(a.view(torch.int16), b.view(torch.int16))
+    # outliers come back exactly
+    xi = x.view(-1)[idx[:t].long()]
+    assert torch.equal(xi.view(torch.int16), a[idx[:t].long()].view(torch.int16))
+
+
+def test_nbit_config2_full_size_properties(cuda):
+    """BASELINE config 2 (INT4, K: [4096, 16, 8, 128], 0.1% x50 outliers) at full size:
+    outliers restored bit-exactly, inlier error bounded by one quantisation step,
+    and a 1/64 sample of buckets bit-exact against the oracle."""
+    n = 4096 * 16 * 8 * 128
+    g = torch.Generator(device=cuda).manual_seed(0)
+    x = torch.randn(n, generator=g, device=cuda)
+    pos = torch.randperm(n, generator=g, device=cuda)[: n // 1000]
+    x[pos] *= 50.0
+    x = x.to(torch.bfloat16)
+    enc = nb.encode_groups(x, 4, 3.0, seed=42)
+    dec = nb.decode_groups(enc)
+    idx, val, total = nb.flatten_outliers(enc)
+    t = int(total.item())
+    assert t >= n // 1000  # every injected x50 outlier is beyond 3 sigma of its group
+    ii = idx[:t].long()
+    assert torch.equal(dec[ii].view(torch.int16), x[ii].view(torch.int16))
+    delta = enc.scales.float().repeat_interleave(32)
+    err = (dec.float() - x.float()).abs()
+    mask = torch.ones(n, dtype=torch.bool, device=cuda)
+    mask[ii] = False
+    assert bool((err[mask] <= delta[mask] * 1.05).all())
+    # sampled bit-exactness against the oracle (same Philox dither)
+    xs = bits_of(x)
+    sc, codes = bits_of(enc.scales), enc.codes.cpu().numpy()
+    for b in range(0, n // 8192, 64):
+        lo = b * 8192
+        u = oracle.philox_dither(8192, 42, lo)
+        osc, ocodes, _, _ = oracle.nbit_encode(xs[lo:lo + 8192], 4, u, 3.0)
+        assert np.array_equal(sc[lo // 32:(lo + 8192) // 32], osc)
+        assert np.array_equal(codes[lo // 2:(lo + 8192) // 2], ocodes)
+
+
+def test_nbit_codec_seeding_policy(cuda):
+    x = bits_of(rand_bf16(4 * 128, 51)).tobytes()
+    c = DitheredNBitCodec()
+    a, b = c.encode(x), c.encode(x)
+    assert a != b  # seed 42 + call count: the dither differs between calls
+    c2 = DitheredINT2Codec()
+    assert c2.encode(x) == c2.encode(x)  # fixed seed 42
+    assert DitheredNBitCodec().encode(b"") == b"\x00" * 8

@@ -1,0 +1,130 @@
+"""The CPU oracle against golden vectors produced by the reference itself.
+
+tests/golden/make_golden.py ran the reference's own codec/policy/checksum
+code (N-bit and INT2 codecs on the CPU with an injected dither; the Triton
+INT8 kernel under Triton's interpreter) and stored inputs and outputs.
+These tests pin the oracle that the GPU parity tests compare against.
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+import oracle
+from conftest import GOLDEN
+
+NBIT = np.load(GOLDEN / "nbit.npz")
+INT8 = np.load(GOLDEN / "int8.npz")
+POLICY = np.load(GOLDEN / "policy.npz")
+XXH = np.load(GOLDEN / "xxh64.npz")
+
+
+@pytest.mark.parametrize("ci", range(int(NBIT["nbit_n_cases"])))
+def test_nbit_oracle_matches_reference_blob(ci):
+    pre = f"nbit_{ci}_"
+    bits, hidden, _is_int2, n, _trail = (int(v) for v in NBIT[pre + "meta"])
+    sigma = float(NBIT[pre + "sigma"])
+    blob = NBIT[pre + "blob"].tobytes()
+    x = NBIT[pre + "src"][:n]
+    sc, codes, idx, vals = oracle.nbit_encode(x, bits, NBIT[pre + "u"], sigma)
+    num_tokens = n // hidden
+    assert oracle.nbit_blob(num_tokens, sc, codes, idx, vals) == blob  # every byte, incl. outlier list
+    dec = oracle.nbit_decode(sc, codes, bits, idx, vals)
+    assert dec.tobytes() == NBIT[pre + "decoded"].tobytes()
+
+
+def test_nbit_golden_covers_outliers_and_all_widths():
+    widths, outliers = set(), 0
+    for ci in range(int(NBIT["nbit_n_cases"])):
+        pre = f"nbit_{ci}_"
+        widths.add(int(NBIT[pre + "meta"][0]))
+        outliers += oracle.nbit_parse_blob(NBIT[pre + "blob"].tobytes(), int(NBIT[pre + "meta"][1]))[2].size
+    assert widths == {2, 4, 8} and outliers > 1000
+
+
+@pytest.mark.parametrize("ci", range(int(INT8["int8_n_cases"])))
+def test_int8_oracle_matches_reference_kernel(ci):
+    pre = f"int8_{ci}_"
+    rows, L, _ = (int(v) for v in INT8[pre + "meta"])
+    src = INT8[pre + "src"].reshape(rows, L)
+    codes, scales = oracle.int8_encode(src, L, src_fp16=True, scale_fp16=True)
+    assert np.array_equal(scales, INT8[pre + "scales"])
+    # Where v*127 overflows fp16 (|v| > 65504/127) the product is inf; the
+    # interpreter's numpy cast of that is undefined (it yields 0), while the
+    # oracle and the CUDA kernel saturate like PTX cvt.rzi.sat.  Everywhere
+    # else the codes must be identical.
+    x = src.view(np.float16).astype(np.float32)
+    overflow = np.abs(x) * 127.0 > 65504.0
+    assert np.array_equal(codes[~overflow], INT8[pre + "codes"][~overflow])
+    assert np.all(np.abs(codes[overflow].astype(np.int16)) >= 127)
+
+
+def test_int8_decode_formula():
+    rng = np.random.default_rng(0)
+    codes = rng.integers(-128, 128, size=(16, 128)).astype(np.int8)
+    scales = (rng.random(16).astype(np.float32) * 4).astype(np.float32)
+    sbits = np.array([oracle.lib().oracle_f32_to_bf16(float(s)) for s in scales], dtype=np.uint16)
+    out = oracle.int8_decode(codes, sbits)
+    s32 = (sbits.astype(np.uint32) << 16).view(np.float32)
+    want = (codes.astype(np.float32) * s32[:, None]) / np.float32(127.0)
+    got = (out.astype(np.uint32) << 16).view(np.float32)
+    assert np.all(np.abs(got - want) <= np.abs(want) * 2.0 ** -8)
+
+
+def test_policy_oracle_matches_reference():
+    z = POLICY
+    R = oracle.score(z["policy_T"], z["policy_S"], z["policy_N"], z["policy_P"], 0.7, 0.1, 0.1, 0.1)
+    assert np.array_equal(R, z["policy_R"], equal_nan=True)
+    nc, nh = oracle.controller_tables([tuple(k) for k in z["policy_codec_keys"]])
+    assert np.array_equal(nc, z["policy_next_colder"]) and np.array_equal(nh, z["policy_next_hotter"])
+    for i, p in enumerate(z["policy_pressures"]):
+        t = oracle.desired_tiers(R, z["policy_cur"], float(p), 0.72, 0.33, 0.04, 0.95, nc, nh)
+        assert np.array_equal(t, z[f"policy_target_{i}"]), p
+    R2 = oracle.score(z["policy_T"], z["policy_S"], z["policy_N"], z["policy_P"], 0.55, 0.15, 0.2, 0.1)
+    assert np.array_equal(R2, z["policy_R2"], equal_nan=True)
+    t2 = oracle.desired_tiers(R2, z["policy_cur"], 0.963, 0.61, 0.29, 0.03, 0.9, nc, nh)
+    assert np.array_equal(t2, z["policy_target_alt"])
+
+
+def test_xxh64_oracle_matches_reference_checksum():
+    off = 0
+    for L, digest in zip(XXH["xxh64_lengths"], XXH["xxh64_digest"]):
+        L = int(L)
+        assert oracle.xxh64(XXH["xxh64_data"][off:off + L].tobytes()) == int(digest), L
+        off += L
+
+
+def test_xxh64_known_answers():
+    # Published XXH64 test values (seed 0).
+    assert oracle.xxh64(b"") == 0xEF46DB3751D8E999
+    assert oracle.xxh64(b"abc") == 0x44BC2CF5AD770999
+
+
+def test_philox_known_answers():
+    # Random123 known-answer vectors for philox4x32-10.
+    assert list(oracle.philox4x32_10([0, 0, 0, 0], [0, 0])) == [0x6627E8D5, 0xE169C58D, 0xBC57AC4C, 0x9B00DBD8]
+    assert list(oracle.philox4x32_10([0xFFFFFFFF] * 4, [0xFFFFFFFF] * 2)) == [
+        0x408F276D, 0x41C83B0E, 0xA20BC7C6, 0x6D5451FD]
+    assert list(oracle.philox4x32_10([0x243F6A88, 0x85A308D3, 0x13198A2E, 0x03707344],
+                                     [0xA4093822, 0x299F31D0])) == [0xD16CFE09, 0x94FDCCEB, 0x5001E420, 0x24126EA1]
+
+
+def test_philox_dither_range_and_offset():
+    u = oracle.philox_dither(4096, seed=7)
+    assert u.min() >= 0.0 and u.max() < 1.0
+    assert np.array_equal(oracle.philox_dither(64, seed=7, offset=1024), u[1024:1088])
+    assert abs(float(u.mean()) - 0.5) < 0.02
+
+
+def test_outlier_bound_holds_on_adversarial_groups():
+    rng = np.random.default_rng(5)
+    worst = 0
+    for _ in range(200):
+        x = rng.standard_normal((256, 32)).astype(np.float32)
+        k = rng.integers(1, 6)
+        x[:, :k] *= 1e3
+        xb = ((x.view(np.uint32) + 0x7FFF + ((x.view(np.uint32) >> 16) & 1)) >> 16).astype(np.uint16)
+        _, _, idx, _ = oracle.nbit_encode(xb, 4, np.full(xb.size, 0.5, np.float32), 3.0)
+        if idx.size:
+            worst = max(worst, np.bincount(idx // 32).max())
+    assert worst <= oracle.max_outliers_per_group(3.0)
