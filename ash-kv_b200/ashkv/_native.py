@@ -45,6 +45,13 @@ SIGNATURES: dict[str, tuple] = {
     "ashkv_score": (_I32, [_P, _P, _P, _P, _I64, _F32, _F32, _F32, _F32, _P, _P]),
     "ashkv_desired_tiers": (_I32, [_P, _P, _I64, _F64, _F64, _F64, _F64, _F64, _P, _P, _P, _P]),
     "ashkv_policy_scratch_ints": (_I64, [_I64]),
+    "ashkv_memcpy2d": (_I32, [_P, _I64, _P, _I64, _I64, _I64, _P]),
+    "ashkv_int8_page_slot_bytes": (_I64, [_I32, _I32]),
+    "ashkv_int8_encode_pages": (_I32, [_P, _P, _I32, _P, _P, _P, _P, _I32, _I32, _I32, _I64, _P, _I64, _I64, _P, _P,
+                                       _P, _P, _P]),
+    "ashkv_slots_commit": (_I32, [_P, _I32, _P, _P]),
+    "ashkv_int8_decode_pages": (_I32, [_P, _P, _I32, _P, _P, _P, _P, _I32, _I32, _I32, _I64, _P, _I64, _I64, _P,
+                                       _I32, _P, _P, _P, _P]),
     "ashkv_policy_step": (_I32, [_P, _P, _P, _P, _P, _I64, _F32, _F32, _F32, _F32, _F64, _F64, _F64, _F64,
                                  _F64, _P, _P, _P, _P, _P, _P, _P, _P, _P]),
 }
@@ -286,3 +293,11 @@ def policy_step(T, S, N, P, cur, weights, pressure: float, theta_high: float, th
         pressure, theta_high, theta_low, delta, p_emergency, _addr(nc), _addr(nh),
         _ptr(R), target.data_ptr(), demote_list.data_ptr(), promote_list.data_ptr(), counts.data_ptr(),
         scratch.data_ptr(), stream_handle(T.device)), "policy_step")
+
+
+# --------------------------------------------------------------------------- copies
+def memcpy2d(dst_ptr: int, dst_pitch: int, src_ptr: int, src_pitch: int, width: int, height: int,
+             device: Optional[torch.device] = None) -> None:
+    """Pitched async copy on the current stream (host pointers should be pinned for async)."""
+    check(lib().ashkv_memcpy2d(dst_ptr, dst_pitch, src_ptr, src_pitch, width, height, stream_handle(device)),
+          "memcpy2d")

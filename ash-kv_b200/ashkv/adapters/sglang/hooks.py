@@ -1,0 +1,204 @@
+"""SGLang HiCache IO interception on sm_100a.
+
+Drop-in for ``SGLangHooks`` (ashkv/adapters/sglang/hooks.py:20-245 of the
+reference).  Same constructor, ``stats`` keys, debounced JSON stats file,
+``compressible_layers`` semantics, return values (``False`` declines and
+lets SGLang run its native copy) and host-slot byte format:
+
+    slot(token t, layer l) = 2 * head_num * head_dim bytes:
+      [0, 2H)            fp16 scales of tokens t*H .. t*H+H-1 (see below)
+      [2H, 2H + H*D)     int8 codes of token t (one absmax scale per token
+                         over all local heads)
+      [2H + H*D, 2*H*D)  zero
+
+The reference writes token t's scale at flat index t of a [num_tokens, H]
+buffer and then copies that buffer to the slots H entries at a time, so slot
+t carries the scales of tokens t*H .. t*H+H-1; promote reads them back the
+same way.  This module keeps that placement byte for byte (entries past the
+last token, which the reference leaves uninitialised, are zero here).
+
+Differences in how the work is done:
+  * demote: one gather+encode launch per layer and K/V writes the packed
+    slots straight into a device staging buffer [tokens, layers, slot]; a
+    single device->host copy moves all layers (the reference runs two
+    synchronous .cpu() copies and a host scatter per layer);
+  * promote: a pitched host->device copy moves only the used 2H + H*D bytes
+    of each slot, and the decode kernel scatters rows straight into the
+    device pool at ``device_indices``;
+  * layers outside ``compressible_layers`` are copied as bf16 in both
+    directions (the reference's ``tensor[index].copy_()`` there writes into
+    a temporary produced by advanced indexing, so those copies never land).
+"""
+from __future__ import annotations
+
+import json
+import logging
+import os
+import time
+from typing import Any
+
+import torch
+
+from ... import _native
+from ...safety.circuit_breaker import CircuitBreakerRegistry
+
+logger = logging.getLogger("ashkv.adapters.sglang.hooks")
+
+
+def _contiguous_range(idx: torch.Tensor) -> int | None:
+    """First index if ``idx`` is an ascending run of consecutive integers, else None."""
+    n = idx.numel()
+    if n == 0:
+        return None
+    i = idx.detach().to("cpu", torch.int64)
+    first = int(i[0])
+    if n == 1 or (int(i[-1]) - first == n - 1 and bool((i[1:] - i[:-1] == 1).all())):
+        return first
+    return None
+
+
+class SGLangHooks:
+    """Demote (GPU -> CPU, compress) and promote (CPU -> GPU, decompress) hooks."""
+
+    def __init__(self, codec_name: str = "int8_default"):
+        self.codec_name = codec_name
+        self.circuit_breaker = CircuitBreakerRegistry()
+        self.compressible_layers = None
+        self.stats = {"tokens_compressed": 0, "tokens_decompressed": 0, "bytes_saved": 0,
+                      "blocks_intercepted": 0, "last_flush_time": 0}
+        os.makedirs("stats", exist_ok=True)
+        self.stats_file = "stats/ashkv_stats.json"
+        self._flush_stats()
+
+    # ------------------------------------------------------------------ stats
+    def _flush_stats(self) -> None:
+        try:
+            with open(self.stats_file, "w") as f:
+                json.dump(self.stats, f)
+        except Exception as e:  # never let telemetry break the IO path
+            logger.warning("[ASH-KV] Failed to flush stats: %s", e)
+
+    def _maybe_flush(self) -> None:
+        if time.time() - self.stats["last_flush_time"] > 1.0:
+            self._flush_stats()
+            self.stats["last_flush_time"] = time.time()
+
+    # ------------------------------------------------------------------ demote
+    def demote_hook(self, device_pool: Any, host_pool: Any, host_indices: torch.Tensor,
+                    device_indices: torch.Tensor, pool_type: str, io_backend: Any = None) -> bool:
+        if pool_type != "MHA":
+            return False
+        n = len(device_indices)
+        if n == 0:
+            return False
+        H, D, L = device_pool.head_num, device_pool.head_dim, device_pool.layer_num
+        if self.compressible_layers is None:
+            self.compressible_layers = list(range(L))
+        compress = set(self.compressible_layers)
+        row = H * D
+        slot = 2 * row
+        dev = device_pool.k_buffer[0].device
+        if dev.type == "cuda":
+            with torch.cuda.device(dev):
+                self._demote_cuda(device_pool, host_pool, host_indices, device_indices, n, H, D, L, compress)
+        else:
+            raise RuntimeError("SGLangHooks needs the device KV pool on a CUDA device")
+
+        nc = len(self.compressible_layers)
+        self.stats["blocks_intercepted"] += 1
+        self.stats["tokens_compressed"] += n * nc
+        bf16_bytes = n * nc * row * 2 * 2
+        int8_bytes = n * nc * (row + 2 * H) * 2
+        self.stats["bytes_saved"] += bf16_bytes - int8_bytes
+        self._maybe_flush()
+        return True
+
+    def _demote_cuda(self, device_pool, host_pool, host_indices, device_indices, n, H, D, L, compress) -> None:
+        row, slot = H * D, 2 * H * D
+        dev = device_pool.k_buffer[0].device
+        didx = device_indices.to(device=dev, dtype=torch.int64)
+        for name in ("k_buffer", "v_buffer"):
+            dbuf = getattr(device_pool, name)
+            staging = torch.zeros((n, L, slot), dtype=torch.uint8, device=dev)
+            flat = staging.view(-1)
+            for layer in range(L):
+                src = dbuf[layer].view(-1, row)
+                if layer in compress:
+                    codes = staging[:, layer, 2 * H:2 * H + row].view(torch.int8)
+                    # scale of token t -> staging[t // H, layer, 2 * (t % H)]
+                    scales = flat[layer * slot:].view(torch.float16)
+                    _native.int8_encode_rows(src, codes, scales, row_index=didx, scales_per_slot=H,
+                                             scale_slot_stride=L * slot)
+                else:
+                    staging[:, layer, :].view(torch.bfloat16).copy_(src[didx].view(n, row))
+            self._write_host_rows(getattr(host_pool, name), host_indices, staging, n, L, slot)
+
+    @staticmethod
+    def _write_host_rows(host_buf: torch.Tensor, host_indices, staging: torch.Tensor, n: int, L: int,
+                         slot: int) -> None:
+        """Copy staging [n, L, slot] into host rows host_buf[host_indices] (each row [L, H, D] bf16)."""
+        hview = host_buf.view(host_buf.shape[0], -1).view(torch.uint8)
+        first = _contiguous_range(host_indices) if host_buf.is_contiguous() else None
+        if first is not None:
+            hview[first:first + n].copy_(staging.view(n, L * slot), non_blocking=host_buf.is_pinned())
+            if host_buf.is_pinned():
+                torch.cuda.current_stream(staging.device).synchronize()
+        else:
+            bounce = staging.view(n, L * slot).to("cpu")
+            hidx = host_indices.detach().to("cpu", torch.int64)
+            hview[hidx] = bounce
+
+    # ------------------------------------------------------------------ promote
+    def promote_hook(self, device_pool: Any, host_pool: Any, host_indices: torch.Tensor,
+                     device_indices: torch.Tensor, layer_id: int, pool_type: str, io_backend: Any = None) -> bool:
+        if pool_type != "MHA":
+            return False
+        n = len(device_indices)
+        if n == 0:
+            return False
+        H, D = device_pool.head_num, device_pool.head_dim
+        dev = device_pool.k_buffer[0].device
+        if dev.type != "cuda":
+            raise RuntimeError("SGLangHooks needs the device KV pool on a CUDA device")
+        native_layer = self.compressible_layers is not None and layer_id not in self.compressible_layers
+        with torch.cuda.device(dev):
+            self._promote_cuda(device_pool, host_pool, host_indices, device_indices, layer_id, H, D, native_layer)
+        if not native_layer:
+            self.stats["tokens_decompressed"] += n
+            self._maybe_flush()
+        return True
+
+    def _promote_cuda(self, device_pool, host_pool, host_indices, device_indices, layer_id, H, D,
+                      native_layer: bool) -> None:
+        row, slot = H * D, 2 * H * D
+        n = len(device_indices)
+        dev = device_pool.k_buffer[0].device
+        didx = device_indices.to(device=dev, dtype=torch.int64)
+        used = slot if native_layer else 2 * H + row
+        for name in ("k_buffer", "v_buffer"):
+            hbuf = getattr(host_pool, name)
+            L = hbuf.shape[1]
+            staged = torch.empty((n, used), dtype=torch.uint8, device=dev)
+            self._read_host_slots(hbuf, host_indices, layer_id, staged, n, L, slot, used)
+            dst = getattr(device_pool, name)[layer_id].view(-1, row)
+            if native_layer:
+                dst[didx] = staged.view(torch.bfloat16).view(n, row)
+                continue
+            codes = staged[:, 2 * H:].view(torch.int8)
+            scales = staged.view(-1).view(torch.float16)
+            _native.int8_decode_rows(codes, scales, dst, row_index=didx, scales_per_slot=H,
+                                     scale_slot_stride=used)
+
+    @staticmethod
+    def _read_host_slots(hbuf: torch.Tensor, host_indices, layer_id: int, staged: torch.Tensor, n: int, L: int,
+                         slot: int, used: int) -> None:
+        first = _contiguous_range(host_indices) if hbuf.is_contiguous() else None
+        if first is not None:
+            base = hbuf.data_ptr() + (first * L + layer_id) * slot
+            _native.memcpy2d(staged.data_ptr(), used, base, L * slot, used, n, staged.device)
+            if not hbuf.is_pinned():
+                torch.cuda.current_stream(staged.device).synchronize()
+        else:
+            hidx = host_indices.detach().to("cpu", torch.int64)
+            rows = hbuf[hidx, layer_id].contiguous().view(n, -1).view(torch.uint8)[:, :used].contiguous()
+            staged.copy_(rows)

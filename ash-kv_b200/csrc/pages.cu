@@ -1,0 +1,299 @@
+// Batched page migration kernels: gather + INT8 encode into shadow-arena
+// slots (demotion) and INT8 decode + scatter back into the KV pool
+// (promotion), driven by device-resident transition lists.
+//
+// Replaces the per-page loop around migrate() (ashkv/runtime/migrate.py:35-191)
+// for the BF16 <-> INT8 transition with the hooks' INT8 layout
+// (ashkv/adapters/sglang/hooks.py:83-137): one fp16 absmax scale per token over
+// all local heads.  A page is `tokens_per_page` consecutive token rows of one
+// layer; page-table row p names it by (layer_id[p], token_start[p]).  The K
+// and V rows of a page are found at layer_k[l] + (token_start + j) * row_stride
+// (and layer_v likewise).
+//
+// Slot layout in the arena (slot_bytes per slot, 16-byte aligned):
+//   [0, 2T)                  fp16 scales of the K rows
+//   [2T, 4T)                 fp16 scales of the V rows
+//   [S0, S0 + T*row)         int8 K codes,  S0 = round_up(4T, 16)
+//   [S0 + T*row, S0 + 2T*row) int8 V codes
+//
+// Slots come from a device free stack (free_stack[0 .. *free_top)).  List
+// entry i takes free_stack[*free_top - 1 - i], so assignment is deterministic
+// and needs no atomics; ashkv_slots_commit then lowers *free_top.  The list
+// length is read on the device (d_count), so no host synchronisation sits
+// between the policy kernel and these kernels.
+#include <algorithm>
+
+#include "common.cuh"
+
+namespace ashkv {
+namespace {
+
+constexpr int kThreads = 256;
+constexpr int kTeam = 32;  // one warp per row
+
+struct PagesParams {
+  const uint64_t* layer_k;
+  const uint64_t* layer_v;
+  int32_t n_layers;
+  const int32_t* layer_id;
+  const int32_t* token_start;
+  const int32_t* list;
+  const int32_t* count;
+  int32_t max_entries;
+  int32_t tokens_per_page;
+  int32_t row_len;
+  int64_t row_stride;
+  uint8_t* arena;
+  int64_t slot_bytes;
+  int64_t n_slots;
+  int32_t* free_stack;
+  const int32_t* free_top;
+  int32_t* page_slot;
+  int32_t* entry_status;  // per list entry: 0 ok, 1 no slot, 2 bad page / slot
+  int32_t free_slots;     // decode: push the slot back onto the free stack
+  int32_t* free_top_rw;
+};
+
+__host__ __device__ __forceinline__ int64_t codes_offset(int T) { return (4 * int64_t(T) + 15) / 16 * 16; }
+
+// Encode one row of `row_len` bf16 (NCH chunks of 8 per lane) into int8 codes + fp16 scale.
+// HALF: 128-element rows, only lanes 0..15 hold data.
+template <int NCH, bool HALF>
+__device__ __forceinline__ void encode_row(const uint16_t* src, int8_t* codes, uint16_t* scale, int lane) {
+  const bool on = !HALF || lane < 16;
+  uint4 ch[NCH];
+  float am = 0.0f;
+#pragma unroll
+  for (int c = 0; c < NCH; ++c) {
+    ch[c] = on ? ld_nc_v4(src + (c * kTeam + lane) * 8) : make_uint4(0, 0, 0, 0);
+    const uint32_t w[4] = {ch[c].x, ch[c].y, ch[c].z, ch[c].w};
+#pragma unroll
+    for (int k = 0; k < 4; ++k) am = fmaxf(am, fmaxf(fabsf(bf16lo(w[k])), fabsf(bf16hi(w[k]))));
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) am = fmaxf(am, __shfl_xor_sync(0xFFFFFFFFu, am, off));
+  am = fmaxf(am, 1e-8f);
+  if (lane == 0) *scale = f32_to_f16(am);
+  if (!on) return;
+#pragma unroll
+  for (int c = 0; c < NCH; ++c) {
+    const uint32_t w[4] = {ch[c].x, ch[c].y, ch[c].z, ch[c].w};
+    uint32_t pk[2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      uint32_t b = 0;
+#pragma unroll
+      for (int k = 0; k < 2; ++k) {
+        const uint32_t word = w[2 * h + k];
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const float x = e ? bf16hi(word) : bf16lo(word);
+          const float s = __bfloat162float(__float2bfloat16_rn(__fmul_rn(x, 127.0f)));
+          const float q = __fdiv_rn(s, am);
+          const float r = __fadd_rn(q, q > 0.0f ? 0.5f : -0.5f);
+          int32_t cv;
+          asm("cvt.rzi.sat.s8.f32 %0, %1;" : "=r"(cv) : "f"(r));
+          b |= (uint32_t(cv) & 0xFFu) << (16 * k + 8 * e);
+        }
+      }
+      pk[h] = b;
+    }
+    *reinterpret_cast<uint2*>(codes + (c * kTeam + lane) * 8) = make_uint2(pk[0], pk[1]);
+  }
+}
+
+template <int NCH, bool HALF>
+__device__ __forceinline__ void decode_row(const int8_t* codes, float scale, uint16_t* dst, int lane) {
+  if (HALF && lane >= 16) return;
+#pragma unroll
+  for (int c = 0; c < NCH; ++c) {
+    const int e0 = (c * kTeam + lane) * 8;
+    const uint2 w = *reinterpret_cast<const uint2*>(codes + e0);
+    const uint32_t ww[2] = {w.x, w.y};
+    uint32_t o[4];
+#pragma unroll
+    for (int h = 0; h < 2; ++h)
+#pragma unroll
+      for (int k = 0; k < 2; ++k) {
+        const float a = __fdiv_rn(__fmul_rn(float(int8_t((ww[h] >> (16 * k)) & 0xFF)), scale), 127.0f);
+        const float b = __fdiv_rn(__fmul_rn(float(int8_t((ww[h] >> (16 * k + 8)) & 0xFF)), scale), 127.0f);
+        o[2 * h + k] = f32x2_to_bf16x2(a, b);
+      }
+    *reinterpret_cast<uint4*>(dst + e0) = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+}
+
+template <int NCH, bool HALF>
+__global__ void __launch_bounds__(kThreads) encode_pages_kernel(const PagesParams p) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int32_t count = min(*p.count, p.max_entries);
+  const int32_t top = *p.free_top;
+  const int T = p.tokens_per_page;
+  const int64_t c0 = codes_offset(T);
+  for (int32_t i = blockIdx.x; i < count; i += gridDim.x) {
+    const int32_t page = p.list[i];
+    const bool have_slot = i < top;
+    const int32_t l = p.layer_id[page];
+    if (!have_slot || l < 0 || l >= p.n_layers) {
+      if (threadIdx.x == 0) p.entry_status[i] = have_slot ? 2 : 1;
+      continue;
+    }
+    const int32_t slot = p.free_stack[top - 1 - i];
+    if (slot < 0 || slot >= p.n_slots) {
+      if (threadIdx.x == 0) p.entry_status[i] = 2;
+      continue;
+    }
+    uint8_t* base = p.arena + int64_t(slot) * p.slot_bytes;
+    const int64_t ts = p.token_start[page];
+    for (int r = warp; r < 2 * T; r += kThreads / 32) {
+      const bool is_v = r >= T;
+      const int j = is_v ? r - T : r;
+      const uint16_t* src = reinterpret_cast<const uint16_t*>(is_v ? p.layer_v[l] : p.layer_k[l]) +
+                            (ts + j) * p.row_stride;
+      int8_t* codes = reinterpret_cast<int8_t*>(base + c0 + int64_t(r) * p.row_len);
+      uint16_t* scale = reinterpret_cast<uint16_t*>(base) + r;
+      encode_row<NCH, HALF>(src, codes, scale, lane);
+    }
+    if (threadIdx.x == 0) {
+      p.page_slot[page] = slot;
+      p.entry_status[i] = 0;
+    }
+  }
+}
+
+template <int NCH, bool HALF>
+__global__ void __launch_bounds__(kThreads) decode_pages_kernel(const PagesParams p) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int32_t count = min(*p.count, p.max_entries);
+  const int T = p.tokens_per_page;
+  const int64_t c0 = codes_offset(T);
+  for (int32_t i = blockIdx.x; i < count; i += gridDim.x) {
+    const int32_t page = p.list[i];
+    const int32_t l = p.layer_id[page];
+    const int32_t slot = p.page_slot[page];
+    if (l < 0 || l >= p.n_layers || slot < 0 || slot >= p.n_slots) {
+      if (threadIdx.x == 0) p.entry_status[i] = 2;
+      continue;
+    }
+    const uint8_t* base = p.arena + int64_t(slot) * p.slot_bytes;
+    const int64_t ts = p.token_start[page];
+    for (int r = warp; r < 2 * T; r += kThreads / 32) {
+      const bool is_v = r >= T;
+      const int j = is_v ? r - T : r;
+      uint16_t* dst = reinterpret_cast<uint16_t*>(is_v ? p.layer_v[l] : p.layer_k[l]) + (ts + j) * p.row_stride;
+      const float scale = f16_to_f32(reinterpret_cast<const uint16_t*>(base)[r]);
+      decode_row<NCH, HALF>(reinterpret_cast<const int8_t*>(base + c0 + int64_t(r) * p.row_len), scale, dst, lane);
+    }
+    __syncthreads();  // every warp is done reading the slot before it is released
+    if (threadIdx.x == 0) {
+      p.entry_status[i] = 0;
+      if (p.free_slots) {
+        p.page_slot[page] = -1;
+        const int32_t pos = atomicAdd(p.free_top_rw, 1);
+        if (pos < p.n_slots) p.free_stack[pos] = slot;
+      }
+    }
+  }
+}
+
+__global__ void slots_commit_kernel(const int32_t* count, int32_t max_entries, int32_t* free_top) {
+  const int32_t c = min(*count, max_entries);
+  const int32_t t = *free_top;
+  *free_top = t - min(c, t);
+}
+
+// Row lengths head_num_local * 128 for 1..16 local heads (powers of two).
+bool pick_nch(int32_t row_len, int& nch) {
+  if (row_len == 128) { nch = 0; return true; }  // half-warp rows
+  if (row_len % 256) return false;
+  nch = row_len / 256;
+  return nch == 1 || nch == 2 || nch == 4 || nch == 8;
+}
+
+ashkv_status_t validate(const PagesParams& p) {
+  if (p.n_layers <= 0 || p.tokens_per_page <= 0 || p.max_entries < 0 || p.n_slots < 0) return ASHKV_BAD_ARGUMENT;
+  if (!p.layer_k || !p.layer_v || !p.layer_id || !p.token_start || !p.list || !p.count || !p.arena ||
+      !p.page_slot || !p.entry_status)
+    return ASHKV_BAD_ARGUMENT;
+  const int64_t need = codes_offset(p.tokens_per_page) + 2 * int64_t(p.tokens_per_page) * p.row_len;
+  if (p.slot_bytes < need || (p.slot_bytes % 16) || !aligned(p.arena, 16)) return ASHKV_BAD_ARGUMENT;
+  if ((p.row_stride * 2) % 16) return ASHKV_BAD_ARGUMENT;
+  return ASHKV_OK;
+}
+
+unsigned grid_for(int32_t max_entries) {
+  const int sms = sm_count() > 0 ? sm_count() : 148;
+  const int64_t g = std::min<int64_t>(max_entries, int64_t(sms) * 8);
+  return unsigned(g > 0 ? g : 1);
+}
+
+}  // namespace
+}  // namespace ashkv
+
+using namespace ashkv;
+
+#define ASHKV_PAGES_DISPATCH(KERNEL, NAME)                                                  \
+  switch (nch) {                                                                           \
+    case 0: KERNEL<1, true><<<grid_for(p.max_entries), kThreads, 0, st>>>(p); break;       \
+    case 1: KERNEL<1, false><<<grid_for(p.max_entries), kThreads, 0, st>>>(p); break;      \
+    case 2: KERNEL<2, false><<<grid_for(p.max_entries), kThreads, 0, st>>>(p); break;      \
+    case 4: KERNEL<4, false><<<grid_for(p.max_entries), kThreads, 0, st>>>(p); break;      \
+    default: KERNEL<8, false><<<grid_for(p.max_entries), kThreads, 0, st>>>(p); break;     \
+  }                                                                                        \
+  return check_launch(NAME);
+
+extern "C" int64_t ashkv_int8_page_slot_bytes(int32_t tokens_per_page, int32_t row_len) {
+  const int64_t need = codes_offset(tokens_per_page) + 2 * int64_t(tokens_per_page) * row_len;
+  return (need + 255) / 256 * 256;
+}
+
+extern "C" ashkv_status_t ashkv_int8_encode_pages(
+    const uint64_t* d_layer_k, const uint64_t* d_layer_v, int32_t n_layers, const int32_t* d_layer_id,
+    const int32_t* d_token_start, const int32_t* d_list, const int32_t* d_count, int32_t max_entries,
+    int32_t tokens_per_page, int32_t row_len, int64_t row_stride, void* d_arena, int64_t slot_bytes,
+    int64_t n_slots, int32_t* d_free_stack, int32_t* d_free_top, int32_t* d_page_slot, int32_t* d_entry_status,
+    void* stream) {
+  PagesParams p{};
+  p.layer_k = d_layer_k; p.layer_v = d_layer_v; p.n_layers = n_layers; p.layer_id = d_layer_id;
+  p.token_start = d_token_start; p.list = d_list; p.count = d_count; p.max_entries = max_entries;
+  p.tokens_per_page = tokens_per_page; p.row_len = row_len; p.row_stride = row_stride;
+  p.arena = static_cast<uint8_t*>(d_arena); p.slot_bytes = slot_bytes; p.n_slots = n_slots;
+  p.free_stack = d_free_stack; p.free_top = d_free_top; p.page_slot = d_page_slot; p.entry_status = d_entry_status;
+  if (max_entries == 0) return ASHKV_OK;
+  int nch = 0;
+  if (!pick_nch(row_len, nch) || !d_free_stack || !d_free_top) return ASHKV_BAD_ARGUMENT;
+  const ashkv_status_t v = validate(p);
+  if (v != ASHKV_OK) return v;
+  cudaStream_t st = as_stream(stream);
+  ASHKV_PAGES_DISPATCH(encode_pages_kernel, "int8_encode_pages")
+}
+
+extern "C" ashkv_status_t ashkv_slots_commit(const int32_t* d_count, int32_t max_entries, int32_t* d_free_top,
+                                             void* stream) {
+  if (!d_count || !d_free_top || max_entries < 0) return ASHKV_BAD_ARGUMENT;
+  slots_commit_kernel<<<1, 1, 0, as_stream(stream)>>>(d_count, max_entries, d_free_top);
+  return check_launch("slots_commit");
+}
+
+extern "C" ashkv_status_t ashkv_int8_decode_pages(
+    const uint64_t* d_layer_k, const uint64_t* d_layer_v, int32_t n_layers, const int32_t* d_layer_id,
+    const int32_t* d_token_start, const int32_t* d_list, const int32_t* d_count, int32_t max_entries,
+    int32_t tokens_per_page, int32_t row_len, int64_t row_stride, const void* d_arena, int64_t slot_bytes,
+    int64_t n_slots, int32_t* d_page_slot, int32_t free_slots, int32_t* d_free_stack, int32_t* d_free_top,
+    int32_t* d_entry_status, void* stream) {
+  PagesParams p{};
+  p.layer_k = d_layer_k; p.layer_v = d_layer_v; p.n_layers = n_layers; p.layer_id = d_layer_id;
+  p.token_start = d_token_start; p.list = d_list; p.count = d_count; p.max_entries = max_entries;
+  p.tokens_per_page = tokens_per_page; p.row_len = row_len; p.row_stride = row_stride;
+  p.arena = static_cast<uint8_t*>(const_cast<void*>(d_arena)); p.slot_bytes = slot_bytes; p.n_slots = n_slots;
+  p.page_slot = d_page_slot; p.entry_status = d_entry_status; p.free_slots = free_slots;
+  p.free_stack = d_free_stack; p.free_top_rw = d_free_top;
+  if (max_entries == 0) return ASHKV_OK;
+  int nch = 0;
+  if (!pick_nch(row_len, nch)) return ASHKV_BAD_ARGUMENT;
+  if (free_slots && (!d_free_stack || !d_free_top)) return ASHKV_BAD_ARGUMENT;
+  const ashkv_status_t v = validate(p);
+  if (v != ASHKV_OK) return v;
+  cudaStream_t st = as_stream(stream);
+  ASHKV_PAGES_DISPATCH(decode_pages_kernel, "int8_decode_pages")
+}

@@ -206,6 +206,54 @@ ASHKV_API ashkv_status_t ashkv_policy_step(
     float* d_R, int8_t* d_target, int32_t* d_demote_list, int32_t* d_promote_list, int32_t* d_counts,
     int32_t* d_scratch, void* stream);
 
+/* ========================================================================
+ * Pitched copy (cudaMemcpy2DAsync, direction inferred from the pointers):
+ * `height` rows of `width` bytes from src (row pitch src_pitch) to dst (row
+ * pitch dst_pitch).  Used by the SGLang promote path to move only the used
+ * bytes of each compressed host slot (ashkv/adapters/sglang/hooks.py:198-216
+ * moves whole slots through a host-side gather instead).
+ * ======================================================================== */
+ASHKV_API ashkv_status_t ashkv_memcpy2d(void* dst, int64_t dst_pitch, const void* src, int64_t src_pitch,
+                                        int64_t width, int64_t height, void* stream);
+
+/* ========================================================================
+ * Batched BF16 <-> INT8 page migration over device-resident lists.
+ * Replaces the per-page migrate() loop (ashkv/runtime/migrate.py:35-191) for
+ * the BF16 -> FP8/INT8-slot transition and its promotion, with the SGLang
+ * hooks' INT8 layout (one fp16 scale per token over the local heads,
+ * ashkv/adapters/sglang/hooks.py:83-137).
+ *   page p = tokens_per_page rows of row_len bf16 starting at token
+ *   d_token_start[p] of layer d_layer_id[p]; K rows at d_layer_k[l] +
+ *   token * row_stride (elements), V rows likewise.  row_len must be 128 or a
+ *   power-of-two multiple of 256 up to 2048.
+ *   Entry i < min(*d_count, max_entries) of d_list is encoded into arena slot
+ *   d_free_stack[*d_free_top - 1 - i] (slot_bytes each, see
+ *   ashkv_int8_page_slot_bytes); d_page_slot[p] records it; d_entry_status[i]
+ *   = 0 ok, 1 no free slot, 2 bad page/slot.  ashkv_slots_commit then pops
+ *   the used slots off the stack.
+ * ashkv_int8_decode_pages decodes the slot of each listed page back into the
+ * K/V rows; with free_slots != 0 it pushes the slot back on the stack and
+ * sets d_page_slot[p] = -1.
+ * ======================================================================== */
+ASHKV_API int64_t ashkv_int8_page_slot_bytes(int32_t tokens_per_page, int32_t row_len);
+
+ASHKV_API ashkv_status_t ashkv_int8_encode_pages(
+    const uint64_t* d_layer_k, const uint64_t* d_layer_v, int32_t n_layers, const int32_t* d_layer_id,
+    const int32_t* d_token_start, const int32_t* d_list, const int32_t* d_count, int32_t max_entries,
+    int32_t tokens_per_page, int32_t row_len, int64_t row_stride, void* d_arena, int64_t slot_bytes,
+    int64_t n_slots, int32_t* d_free_stack, int32_t* d_free_top, int32_t* d_page_slot, int32_t* d_entry_status,
+    void* stream);
+
+ASHKV_API ashkv_status_t ashkv_slots_commit(const int32_t* d_count, int32_t max_entries, int32_t* d_free_top,
+                                            void* stream);
+
+ASHKV_API ashkv_status_t ashkv_int8_decode_pages(
+    const uint64_t* d_layer_k, const uint64_t* d_layer_v, int32_t n_layers, const int32_t* d_layer_id,
+    const int32_t* d_token_start, const int32_t* d_list, const int32_t* d_count, int32_t max_entries,
+    int32_t tokens_per_page, int32_t row_len, int64_t row_stride, const void* d_arena, int64_t slot_bytes,
+    int64_t n_slots, int32_t* d_page_slot, int32_t free_slots, int32_t* d_free_stack, int32_t* d_free_top,
+    int32_t* d_entry_status, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
