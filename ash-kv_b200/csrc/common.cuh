@@ -114,4 +114,86 @@ __device__ __forceinline__ float dither16(uint32_t h16) {
   return __fadd_rn(__uint_as_float(0x3F800000u | (h16 << 7)), -1.5f);
 }
 
+
+// ---------------------------------------------------------------- sm_100 vector ops
+// 256-bit streaming load / store (one full 32-byte sector per thread).
+struct U8 { uint32_t v[8]; };
+__device__ __forceinline__ U8 ld_nc_v8(const void* p) {
+  U8 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v8.u32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(r.v[0]), "=r"(r.v[1]), "=r"(r.v[2]), "=r"(r.v[3]), "=r"(r.v[4]), "=r"(r.v[5]),
+                 "=r"(r.v[6]), "=r"(r.v[7])
+               : "l"(p));
+  return r;
+}
+__device__ __forceinline__ void st_cs_v8(void* p, const U8& r) {
+  asm volatile("st.global.cs.v8.u32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};"
+               :: "l"(p), "r"(r.v[0]), "r"(r.v[1]), "r"(r.v[2]), "r"(r.v[3]), "r"(r.v[4]), "r"(r.v[5]),
+                  "r"(r.v[6]), "r"(r.v[7]) : "memory");
+}
+
+// Packed fp32 pairs (lo, hi) in a 64-bit register; f32x2 arithmetic rounds
+// each lane exactly like the scalar .rn instruction.
+typedef unsigned long long f2;
+__device__ __forceinline__ f2 pk2(float lo, float hi) {
+  f2 r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void upk2(f2 v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ f2 add2(f2 a, f2 b) {
+  f2 r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ f2 mul2(f2 a, f2 b) {
+  f2 r;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ f2 fma2(f2 a, f2 b, f2 c) {
+  f2 r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+// max(|a|, |b|, |c|), NaN if any input is NaN.
+__device__ __forceinline__ float max3_abs_nan(float a, float b, float c) {
+  float r;
+  asm("max.NaN.abs.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
+// Correctly rounded division by a divisor shared by many dividends.
+// Per divisor b: y_hi = RN(1/b), y_lo = RN((1 - b*y_hi) * y_hi), so that
+// y_hi + y_lo approximates 1/b to ~2^-47.  Per dividend a:
+//   q0 = RN(a*y_hi + RN(a*y_lo))   -- within one ulp of a/b
+//   r  = a - q0*b                  -- exact (fused multiply-add)
+//   q1 = RN(q0 + r*y_hi)           -- = RN(a/b)
+// The last step is Markstein's correction (P. Markstein, IBM J. Res. Dev.
+// 34(1), 1990): with y within half an ulp of 1/b and q0 within one ulp of
+// a/b it yields the correctly rounded quotient, barring overflow/underflow,
+// which recip_ok() excludes by keeping b inside [2^-100, 2^100].
+struct Recip { float hi, lo; };
+__device__ __forceinline__ Recip make_recip(float b) {
+  Recip r;
+  r.hi = __frcp_rn(b);
+  const float e = __fmaf_rn(-b, r.hi, 1.0f);
+  r.lo = __fmul_rn(e, r.hi);
+  return r;
+}
+__device__ __forceinline__ bool recip_ok(float b) { return fabsf(b) >= 0x1p-100f && fabsf(b) <= 0x1p+100f; }
+__device__ __forceinline__ float div_rn(float a, float b, Recip y) {
+  const float q0 = __fmaf_rn(a, y.hi, __fmul_rn(a, y.lo));
+  const float r = __fmaf_rn(-q0, b, a);
+  return __fmaf_rn(r, y.hi, q0);
+}
+// The same on fp32 pairs: Y_HI/Y_LO/NB = (y.hi, y.hi), (y.lo, y.lo), (-b, -b).
+__device__ __forceinline__ f2 div2_rn(f2 a, f2 yhi, f2 ylo, f2 nb) {
+  const f2 q0 = fma2(a, yhi, mul2(a, ylo));
+  const f2 r = fma2(q0, nb, a);
+  return fma2(r, yhi, q0);
+}
+
 }  // namespace ashkv

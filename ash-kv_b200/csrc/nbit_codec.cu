@@ -74,150 +74,239 @@ __device__ __forceinline__ uint32_t cta_exclusive_scan(uint32_t v, uint32_t* sme
   return warp_base + inc - v;
 }
 
+// Exact reference threshold sigma * (sd + 1e-8), sd = fp32(sqrt(M2 / 31)) with
+// M2 accumulated in fp64 (two-pass).  Used only when the fast bound below
+// cannot decide every element of a group.
+__device__ __forceinline__ float exact_threshold(const f2 (&X)[16], float sigma) {
+  double s64 = 0.0;
+#pragma unroll
+  for (int k = 0; k < 16; ++k) {
+    float x0, x1;
+    upk2(X[k], x0, x1);
+    s64 = __dadd_rn(__dadd_rn(s64, double(x0)), double(x1));
+  }
+  const double mu64 = __dmul_rn(s64, 0.03125);
+  double m2 = 0.0;
+#pragma unroll
+  for (int k = 0; k < 16; ++k) {
+    float x0, x1;
+    upk2(X[k], x0, x1);
+    const double d0 = __dadd_rn(double(x0), -mu64);
+    m2 = __dadd_rn(m2, __dmul_rn(d0, d0));
+    const double d1 = __dadd_rn(double(x1), -mu64);
+    m2 = __dadd_rn(m2, __dmul_rn(d1, d1));
+  }
+  const float sd = __double2float_rn(__dsqrt_rn(__ddiv_rn(m2, 31.0)));
+  return __fmul_rn(sigma, __fadd_rn(sd, 1e-8f));
+}
+
+// One thread per 32-element group, one CTA (256 groups) per outlier bucket.
+//
+// Outlier decisions are made against the reference threshold without
+// computing its fp64 variance in the common case: an fp32 variance with a
+// rigorous error bound gives thr_lo <= thr <= thr_hi.  If every |x - mu| of
+// the group is <= thr_lo the group has no outliers (the usual case).
+// Otherwise per-element masks against thr_lo and thr_hi are built; if they
+// agree, that is the exact mask, and only if some |x - mu| falls between the
+// two bounds is the exact fp64 threshold computed.
 template <int BITS, int DMODE>
-__global__ void __launch_bounds__(kThreads) nbit_encode_kernel(const NbitEncParams p) {
+__global__ void __launch_bounds__(kThreads, 2) nbit_encode_kernel(const NbitEncParams p) {
   constexpr uint32_t kMaxCode = (1u << BITS) - 1u;
   __shared__ uint32_t s_warp[kThreads / 32];
 
   const int64_t g = int64_t(blockIdx.x) * kThreads + threadIdx.x;
   const bool active = g < p.n_groups;
 
-  float x[32];
-  if (active) {
-    const uint16_t* src = p.src + g * 32;
+  // ---- load 32 bf16 as two full 32-byte sectors
+  f2 X[16];
+  {
+    U8 a, b;
+    if (active) {
+      a = ld_nc_v8(p.src + g * 32);
+      b = ld_nc_v8(p.src + g * 32 + 16);
+    } else {
 #pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      const uint4 v = ld_nc_v4(src + 8 * k);
-      x[8 * k + 0] = bf16lo(v.x); x[8 * k + 1] = bf16hi(v.x);
-      x[8 * k + 2] = bf16lo(v.y); x[8 * k + 3] = bf16hi(v.y);
-      x[8 * k + 4] = bf16lo(v.z); x[8 * k + 5] = bf16hi(v.z);
-      x[8 * k + 6] = bf16lo(v.w); x[8 * k + 7] = bf16hi(v.w);
+      for (int k = 0; k < 8; ++k) a.v[k] = b.v[k] = 0u;
     }
-  } else {
 #pragma unroll
-    for (int i = 0; i < 32; ++i) x[i] = 0.0f;
+    for (int k = 0; k < 8; ++k) {
+      X[k] = pk2(bf16lo(a.v[k]), bf16hi(a.v[k]));
+      X[8 + k] = pk2(bf16lo(b.v[k]), bf16hi(b.v[k]));
+    }
   }
 
-  // ---- mean: 8 lane accumulators over the 4 rows of 8, then lanes in order.
-  float acc[8];
-#pragma unroll
-  for (int i = 0; i < 8; ++i) acc[i] = x[i];
+  // ---- mean: lane accumulators acc[i] = ((x_i + x_{8+i}) + x_{16+i}) + x_{24+i},
+  //      then acc[0] + acc[1] + ... + acc[7] in order (PyTorch's CPU order).
+  f2 A[4] = {X[0], X[1], X[2], X[3]};
 #pragma unroll
   for (int j = 1; j < 4; ++j)
 #pragma unroll
-    for (int i = 0; i < 8; ++i) acc[i] = __fadd_rn(acc[i], x[8 * j + i]);
+    for (int i = 0; i < 4; ++i) A[i] = add2(A[i], X[4 * j + i]);
+  float acc[8];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) upk2(A[i], acc[2 * i], acc[2 * i + 1]);
   float s = acc[0];
 #pragma unroll
   for (int i = 1; i < 8; ++i) s = __fadd_rn(s, acc[i]);
-  const float mu = __fmul_rn(s, 0.03125f);  // exact: division by 32
+  const float mu = __fmul_rn(s, 0.03125f);
 
-  // ---- unbiased standard deviation, fp64 two-pass, rounded once to fp32.
-  double s64 = 0.0;
+  // ---- fp32 variance estimate, max|x - mu|, max|x| (NaN-propagating)
+  const f2 NMU = pk2(-mu, -mu);
+  f2 M2 = pk2(0.0f, 0.0f);
+  float dmax = 0.0f, xmax = 0.0f;
 #pragma unroll
-  for (int i = 0; i < 32; ++i) s64 = __dadd_rn(s64, double(x[i]));
-  const double mu64 = __dmul_rn(s64, 0.03125);
-  double m2 = 0.0;
-#pragma unroll
-  for (int i = 0; i < 32; ++i) {
-    const double d = __dadd_rn(double(x[i]), -mu64);
-    m2 = __dadd_rn(m2, __dmul_rn(d, d));
+  for (int k = 0; k < 16; ++k) {
+    const f2 D = add2(X[k], NMU);
+    M2 = fma2(D, D, M2);
+    float d0, d1, x0, x1;
+    upk2(D, d0, d1);
+    upk2(X[k], x0, x1);
+    dmax = max3_abs_nan(dmax, d0, d1);
+    xmax = max3_abs_nan(xmax, x0, x1);
   }
-  const float sd = __double2float_rn(__dsqrt_rn(__ddiv_rn(m2, 31.0)));
-  const float thr = __fmul_rn(p.sigma, __fadd_rn(sd, 1e-8f));
+  float m2a, m2b;
+  upk2(M2, m2a, m2b);
+  const float m2 = __fadd_rn(m2a, m2b);
 
-  // ---- outlier mask, inlier substitution, inlier absmax (NaN-propagating).
+  // Bounds on the reference threshold.  m2 has relative error < 2^-19 w.r.t.
+  // sum (x - mu32)^2, which exceeds the exact M2 by 32 (mu - mu32)^2 with
+  // |mu - mu32| <= 31 * 2^-24 * max|x|.  Margins of 2^-16 / 2^-14 cover the
+  // remaining roundings (fp32 bound arithmetic, the fp32 rounding of sd,
+  // + 1e-8 and * sigma in the reference).
+  const float sigma = p.sigma;
+  const bool bounds_ok = sigma > 0.0f && isfinite(m2) && isfinite(xmax);
+  float thr_lo = 0.0f, thr_hi = 0.0f;
+  if (bounds_ok) {
+    const float emu = 31.0001f * 0x1p-24f * xmax;
+    const float m2_hi = m2 * (1.0f + 0x1p-16f);
+    const float m2_lo = fmaxf(m2 * (1.0f - 0x1p-16f) - 32.0f * emu * emu * (1.0f + 0x1p-16f), 0.0f);
+    thr_hi = sigma * (sqrtf(m2_hi / 31.0f) + 1e-8f) * (1.0f + 0x1p-14f);
+    thr_lo = sigma * (sqrtf(m2_lo / 31.0f) + 1e-8f) * (1.0f - 0x1p-14f);
+  }
   uint32_t omask = 0;
-  float am = 0.0f;
+  float am = xmax;
+  if (!(bounds_ok && dmax <= thr_lo)) {
+    uint32_t mlo = 0, mhi = 0;
 #pragma unroll
-  for (int i = 0; i < 32; ++i) {
-    const bool o = fabsf(__fadd_rn(x[i], -mu)) > thr;
-    omask |= uint32_t(o) << i;
-    const float xi = o ? mu : x[i];
-    am = max_nan(am, fabsf(xi));
-    x[i] = xi;
+    for (int k = 0; k < 16; ++k) {
+      float x0, x1;
+      upk2(X[k], x0, x1);
+      const float d0 = fabsf(__fadd_rn(x0, -mu)), d1 = fabsf(__fadd_rn(x1, -mu));
+      mlo |= (uint32_t(d0 > thr_lo) << (2 * k)) | (uint32_t(d1 > thr_lo) << (2 * k + 1));
+      mhi |= (uint32_t(d0 > thr_hi) << (2 * k)) | (uint32_t(d1 > thr_hi) << (2 * k + 1));
+    }
+    omask = mhi;
+    if (!bounds_ok || mlo != mhi) {
+      const float thr = exact_threshold(X, sigma);
+      omask = 0;
+#pragma unroll
+      for (int k = 0; k < 16; ++k) {
+        float x0, x1;
+        upk2(X[k], x0, x1);
+        omask |= (uint32_t(fabsf(__fadd_rn(x0, -mu)) > thr) << (2 * k)) |
+                 (uint32_t(fabsf(__fadd_rn(x1, -mu)) > thr) << (2 * k + 1));
+      }
+    }
+    if (omask) {
+      am = 0.0f;
+#pragma unroll
+      for (int k = 0; k < 16; ++k) {
+        float x0, x1;
+        upk2(X[k], x0, x1);
+        x0 = (omask >> (2 * k)) & 1u ? mu : x0;
+        x1 = (omask >> (2 * k + 1)) & 1u ? mu : x1;
+        X[k] = pk2(x0, x1);
+        am = max3_abs_nan(am, x0, x1);
+      }
+    }
   }
+  if (!active) omask = 0;
   if (!(am >= 1e-8f) && am == am) am = 1e-8f;  // clamp(min=1e-8); NaN propagates
   const float delta = __fdiv_rn(am, p.half_states);
 
-  // ---- dither, quantise, pack.
-  float dz[32];
-  if constexpr (DMODE == ASHKV_DITHER_TENSOR) {
-    if (active) {
-      const float* dp = p.dither + g * 32;
+  // ---- dither, quantise (x' + (U-0.5)*delta) / delta + half, pack
+  const Recip y = make_recip(delta);
+  const bool fast_div = recip_ok(delta);
+  const f2 DELTA = pk2(delta, delta), YHI = pk2(y.hi, y.hi), YLO = pk2(y.lo, y.lo), NDELTA = pk2(-delta, -delta);
+  const f2 HALF = pk2(p.half_states, p.half_states);
+  const f2 MAGIC = pk2(12582912.0f, 12582912.0f);
+  const f2 C128 = pk2(128.0f, 128.0f), CM = pk2(-128.5f, -128.5f), NHALF = pk2(-0.5f, -0.5f);
+  // packed codes: 32 * BITS / 32 words (MSB-first within each byte)
+  uint32_t o[BITS];
 #pragma unroll
-      for (int k = 0; k < 8; ++k) {
-        const float4 v = ld_nc_f4(dp + 4 * k);
-        // U - 0.5 is exact for U in [0, 1)
-        dz[4 * k + 0] = __fadd_rn(v.x, -0.5f); dz[4 * k + 1] = __fadd_rn(v.y, -0.5f);
-        dz[4 * k + 2] = __fadd_rn(v.z, -0.5f); dz[4 * k + 3] = __fadd_rn(v.w, -0.5f);
+  for (int k = 0; k < BITS; ++k) o[k] = 0u;
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {  // 8 elements per Philox draw
+    f2 DZ[4];
+    if constexpr (DMODE == ASHKV_DITHER_TENSOR) {
+      U8 u;
+      if (active) u = ld_nc_v8(p.dither + g * 32 + 8 * c);
+      else {
+#pragma unroll
+        for (int k = 0; k < 8; ++k) u.v[k] = 0x3F000000u;  // 0.5 -> zero dither
       }
+#pragma unroll
+      for (int h = 0; h < 4; ++h)
+        DZ[h] = add2(pk2(__uint_as_float(u.v[2 * h]), __uint_as_float(u.v[2 * h + 1])), NHALF);
     } else {
-#pragma unroll
-      for (int i = 0; i < 32; ++i) dz[i] = 0.0f;
-    }
-  } else {
-    const uint64_t e0 = p.dither_offset + uint64_t(g) * 32;  // multiple of 8 when the offset is
-    const uint32_t k0 = uint32_t(p.seed), k1 = uint32_t(p.seed >> 32);
-#pragma unroll
-    for (int c = 0; c < 4; ++c) {
-      const uint64_t ctr = (e0 >> 3) + c;
-      const Philox4 r = philox4x32_10(uint32_t(ctr), uint32_t(ctr >> 32), 0u, 0u, k0, k1);
+      const uint64_t ctr = ((p.dither_offset + uint64_t(g) * 32) >> 3) + c;
+      const Philox4 r = philox4x32_10(uint32_t(ctr), uint32_t(ctr >> 32), 0u, 0u, uint32_t(p.seed),
+                                      uint32_t(p.seed >> 32));
 #pragma unroll
       for (int h = 0; h < 4; ++h) {
-        dz[8 * c + 2 * h + 0] = dither16(r.v[h] & 0xFFFFu);
-        dz[8 * c + 2 * h + 1] = dither16(r.v[h] >> 16);
+        // f = 1 + h16 * 2^-23; U - 0.5 = 128 f - 128.5 exactly
+        const float flo = __uint_as_float(__byte_perm(r.v[h], 0x3F800000u, 0x7610));
+        const float fhi = __uint_as_float(__byte_perm(r.v[h], 0x3F800000u, 0x7632));
+        DZ[h] = fma2(pk2(flo, fhi), C128, CM);
       }
     }
-  }
-
-  uint32_t code[32];
 #pragma unroll
-  for (int i = 0; i < 32; ++i) {
-    const float noise = __fmul_rn(dz[i], delta);
-    const float a = __fadd_rn(x[i], noise);
-    const float v = __fadd_rn(__fdiv_rn(a, delta), p.half_states);
-    const float vc = fminf(fmaxf(v, 0.0f), float(kMaxCode));  // NaN -> 0
-    code[i] = rint_small(vc);
+    for (int h = 0; h < 4; ++h) {
+      const int k = 4 * c + h;
+      const f2 A2 = add2(X[k], mul2(DZ[h], DELTA));
+      f2 Q;
+      if (fast_div) {
+        Q = div2_rn(A2, YHI, YLO, NDELTA);
+      } else {
+        float a0, a1;
+        upk2(A2, a0, a1);
+        Q = pk2(__fdiv_rn(a0, delta), __fdiv_rn(a1, delta));
+      }
+      float v0, v1;
+      upk2(add2(Q, HALF), v0, v1);
+      v0 = fminf(fmaxf(v0, 0.0f), float(kMaxCode));  // NaN -> 0
+      v1 = fminf(fmaxf(v1, 0.0f), float(kMaxCode));
+      float t0, t1;
+      upk2(add2(pk2(v0, v1), MAGIC), t0, t1);
+      const uint32_t c0 = __float_as_uint(t0) & kMaxCode, c1 = __float_as_uint(t1) & kMaxCode;
+      // element e = 2k (+1) sits in byte e*BITS/8, MSB first within the byte
+      if constexpr (BITS == 4) {
+        o[k >> 2] |= ((c0 << 4) | c1) << (8 * (k & 3));
+      } else if constexpr (BITS == 2) {
+        const int e = 2 * k;  // even: the pair shares a byte
+        o[e >> 4] |= ((c0 << (6 - 2 * (e & 3))) | (c1 << (4 - 2 * (e & 3)))) << (8 * ((e >> 2) & 3));
+      } else {
+        o[k >> 1] |= (c0 | (c1 << 8)) << (16 * (k & 1));
+      }
+    }
   }
 
   if (active) {
     p.scales[g] = f32_to_bf16(delta);
     if constexpr (BITS == 4) {
-      uint32_t w[4];
-#pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        uint32_t b = 0;
-#pragma unroll
-        for (int j = 0; j < 4; ++j)
-          b |= ((code[8 * k + 2 * j] << 4) | code[8 * k + 2 * j + 1]) << (8 * j);
-        w[k] = b;
-      }
-      st_cs_v4(p.codes + g * 16, make_uint4(w[0], w[1], w[2], w[3]));
+      st_cs_v4(p.codes + g * 16, make_uint4(o[0], o[1], o[2], o[3]));
     } else if constexpr (BITS == 2) {
-      uint32_t w[2];
-#pragma unroll
-      for (int k = 0; k < 2; ++k) {
-        uint32_t b = 0;
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const int i = 16 * k + 4 * j;
-          b |= ((code[i] << 6) | (code[i + 1] << 4) | (code[i + 2] << 2) | code[i + 3]) << (8 * j);
-        }
-        w[k] = b;
-      }
-      *reinterpret_cast<uint2*>(p.codes + g * 8) = make_uint2(w[0], w[1]);
+      *reinterpret_cast<uint2*>(p.codes + g * 8) = make_uint2(o[0], o[1]);
     } else {
-      uint32_t w[8];
+      U8 ov;
 #pragma unroll
-      for (int k = 0; k < 8; ++k)
-        w[k] = code[4 * k] | (code[4 * k + 1] << 8) | (code[4 * k + 2] << 16) | (code[4 * k + 3] << 24);
-      st_cs_v4(p.codes + g * 32, make_uint4(w[0], w[1], w[2], w[3]));
-      st_cs_v4(p.codes + g * 32 + 16, make_uint4(w[4], w[5], w[6], w[7]));
+      for (int k = 0; k < 8; ++k) ov.v[k] = o[k];
+      st_cs_v8(p.codes + g * 32, ov);
     }
   }
 
   // ---- outlier list of this bucket, ascending element order.
-  const uint32_t cnt = active ? uint32_t(__popc(omask)) : 0u;
+  const uint32_t cnt = uint32_t(__popc(omask));
   uint32_t total = 0;
   uint32_t pos = cta_exclusive_scan(cnt, s_warp, total);
   if (threadIdx.x == 0) {
@@ -226,14 +315,13 @@ __global__ void __launch_bounds__(kThreads) nbit_encode_kernel(const NbitEncPara
   }
   if (cnt) {
     uint32_t* out = p.bucket_entries + int64_t(blockIdx.x) * p.bucket_cap;
-    const uint16_t* src = p.src + g * 32;
     uint32_t m = omask;
     while (m) {
       const int i = __ffs(m) - 1;
       m &= m - 1;
       if (pos < uint32_t(p.bucket_cap)) {
         const uint32_t local = uint32_t(threadIdx.x) * 32u + uint32_t(i);
-        out[pos] = (local << 16) | uint32_t(src[i]);
+        out[pos] = (local << 16) | uint32_t(p.src[g * 32 + i]);  // original bits (rare path)
       }
       ++pos;
     }
@@ -401,9 +489,10 @@ extern "C" ashkv_status_t ashkv_nbit_encode(
   if (dither_mode == ASHKV_DITHER_TENSOR && !d_dither) return ASHKV_BAD_ARGUMENT;
   if (dither_mode == ASHKV_DITHER_PHILOX && (dither_elem_offset % 8)) return ASHKV_BAD_ARGUMENT;
   // 16-byte vector accesses; the 2-bit codes use 8-byte stores.
-  if (!aligned(d_src, 16) || !aligned(d_scales, 2) || !aligned(d_codes, bits == 2 ? 8 : 16))
+  // 32-byte vector loads of the source and dither; 8/16/32-byte code stores.
+  if (!aligned(d_src, 32) || !aligned(d_scales, 2) || !aligned(d_codes, bits == 2 ? 8 : bits == 4 ? 16 : 32))
     return ASHKV_BAD_ARGUMENT;
-  if (dither_mode == ASHKV_DITHER_TENSOR && !aligned(d_dither, 16)) return ASHKV_BAD_ARGUMENT;
+  if (dither_mode == ASHKV_DITHER_TENSOR && !aligned(d_dither, 32)) return ASHKV_BAD_ARGUMENT;
   const int64_t n_buckets = (n_groups + kThreads - 1) / kThreads;
   if (n_buckets > 0x7FFFFFFF) return ASHKV_BAD_ARGUMENT;
 
