@@ -16,6 +16,11 @@
 // the group mean uses PyTorch's 8-lane partial-sum order, the standard
 // deviation is PyTorch's fp64 computation rounded once to fp32, divisions
 // are true divisions and rounding is half-to-even.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
 #include "common.cuh"
 
 namespace ashkv {
@@ -74,32 +79,6 @@ __device__ __forceinline__ uint32_t cta_exclusive_scan(uint32_t v, uint32_t* sme
   return warp_base + inc - v;
 }
 
-// Exact reference threshold sigma * (sd + 1e-8), sd = fp32(sqrt(M2 / 31)) with
-// M2 accumulated in fp64 (two-pass).  Used only when the fast bound below
-// cannot decide every element of a group.
-__device__ __forceinline__ float exact_threshold(const f2 (&X)[16], float sigma) {
-  double s64 = 0.0;
-#pragma unroll
-  for (int k = 0; k < 16; ++k) {
-    float x0, x1;
-    upk2(X[k], x0, x1);
-    s64 = __dadd_rn(__dadd_rn(s64, double(x0)), double(x1));
-  }
-  const double mu64 = __dmul_rn(s64, 0.03125);
-  double m2 = 0.0;
-#pragma unroll
-  for (int k = 0; k < 16; ++k) {
-    float x0, x1;
-    upk2(X[k], x0, x1);
-    const double d0 = __dadd_rn(double(x0), -mu64);
-    m2 = __dadd_rn(m2, __dmul_rn(d0, d0));
-    const double d1 = __dadd_rn(double(x1), -mu64);
-    m2 = __dadd_rn(m2, __dmul_rn(d1, d1));
-  }
-  const float sd = __double2float_rn(__dsqrt_rn(__ddiv_rn(m2, 31.0)));
-  return __fmul_rn(sigma, __fadd_rn(sd, 1e-8f));
-}
-
 // One thread per 32-element group, one CTA (256 groups) per outlier bucket.
 //
 // Outlier decisions are made against the reference threshold without
@@ -109,39 +88,42 @@ __device__ __forceinline__ float exact_threshold(const f2 (&X)[16], float sigma)
 // Otherwise per-element masks against thr_lo and thr_hi are built; if they
 // agree, that is the exact mask, and only if some |x - mu| falls between the
 // two bounds is the exact fp64 threshold computed.
-template <int BITS, int DMODE>
-__global__ void __launch_bounds__(kThreads, 2) nbit_encode_kernel(const NbitEncParams p) {
+// A group's 32 bf16 values as 4 chunks of 8 (16 bytes each).
+struct RegGroup {  // held in registers
+  const uint32_t* w;
+  __device__ __forceinline__ uint4 chunk(int c) const { return make_uint4(w[4 * c], w[4 * c + 1], w[4 * c + 2], w[4 * c + 3]); }
+};
+struct SmemGroup {  // one 64-byte row of a 64-byte-swizzled shared-memory tile
+  uint32_t row, sw;
+  __device__ __forceinline__ uint4 chunk(int c) const { return lds128(row + 16u * (uint32_t(c) ^ sw)); }
+};
+
+template <typename Src>
+__device__ __forceinline__ void chunk_pairs(const Src& src, int c, f2 (&P)[4]) {
+  const uint4 q = src.chunk(c);
+  P[0] = pk2(bf16lo(q.x), bf16hi(q.x));
+  P[1] = pk2(bf16lo(q.y), bf16hi(q.y));
+  P[2] = pk2(bf16lo(q.z), bf16hi(q.z));
+  P[3] = pk2(bf16lo(q.w), bf16hi(q.w));
+}
+
+// Encodes one group (writes its packed codes and bf16 delta) and returns the
+// outlier bit mask.  The group is re-read from `src` for each pass so only
+// one 8-element chunk is live in registers at a time.
+template <int BITS, int DMODE, typename Src>
+__device__ __forceinline__ uint32_t encode_group(const Src& src, const NbitEncParams& p, int64_t g, bool active) {
   constexpr uint32_t kMaxCode = (1u << BITS) - 1u;
-  __shared__ uint32_t s_warp[kThreads / 32];
-
-  const int64_t g = int64_t(blockIdx.x) * kThreads + threadIdx.x;
-  const bool active = g < p.n_groups;
-
-  // ---- load 32 bf16 as two full 32-byte sectors
-  f2 X[16];
-  {
-    U8 a, b;
-    if (active) {
-      a = ld_nc_v8(p.src + g * 32);
-      b = ld_nc_v8(p.src + g * 32 + 16);
-    } else {
+  // ---- mean: acc[i] = ((x_i + x_{8+i}) + x_{16+i}) + x_{24+i}, then acc[0] + ... + acc[7]
+  //      in order (PyTorch's CPU reduction order for a 32-wide inner dimension).
+  f2 A[4];
+  chunk_pairs(src, 0, A);
 #pragma unroll
-      for (int k = 0; k < 8; ++k) a.v[k] = b.v[k] = 0u;
-    }
+  for (int c = 1; c < 4; ++c) {
+    f2 P[4];
+    chunk_pairs(src, c, P);
 #pragma unroll
-    for (int k = 0; k < 8; ++k) {
-      X[k] = pk2(bf16lo(a.v[k]), bf16hi(a.v[k]));
-      X[8 + k] = pk2(bf16lo(b.v[k]), bf16hi(b.v[k]));
-    }
+    for (int i = 0; i < 4; ++i) A[i] = add2(A[i], P[i]);
   }
-
-  // ---- mean: lane accumulators acc[i] = ((x_i + x_{8+i}) + x_{16+i}) + x_{24+i},
-  //      then acc[0] + acc[1] + ... + acc[7] in order (PyTorch's CPU order).
-  f2 A[4] = {X[0], X[1], X[2], X[3]};
-#pragma unroll
-  for (int j = 1; j < 4; ++j)
-#pragma unroll
-    for (int i = 0; i < 4; ++i) A[i] = add2(A[i], X[4 * j + i]);
   float acc[8];
 #pragma unroll
   for (int i = 0; i < 4; ++i) upk2(A[i], acc[2 * i], acc[2 * i + 1]);
@@ -155,14 +137,19 @@ __global__ void __launch_bounds__(kThreads, 2) nbit_encode_kernel(const NbitEncP
   f2 M2 = pk2(0.0f, 0.0f);
   float dmax = 0.0f, xmax = 0.0f;
 #pragma unroll
-  for (int k = 0; k < 16; ++k) {
-    const f2 D = add2(X[k], NMU);
-    M2 = fma2(D, D, M2);
-    float d0, d1, x0, x1;
-    upk2(D, d0, d1);
-    upk2(X[k], x0, x1);
-    dmax = max3_abs_nan(dmax, d0, d1);
-    xmax = max3_abs_nan(xmax, x0, x1);
+  for (int c = 0; c < 4; ++c) {
+    f2 P[4];
+    chunk_pairs(src, c, P);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const f2 D = add2(P[i], NMU);
+      M2 = fma2(D, D, M2);
+      float d0, d1, x0, x1;
+      upk2(D, d0, d1);
+      upk2(P[i], x0, x1);
+      dmax = max3_abs_nan(dmax, d0, d1);
+      xmax = max3_abs_nan(xmax, x0, x1);
+    }
   }
   float m2a, m2b;
   upk2(M2, m2a, m2b);
@@ -188,35 +175,78 @@ __global__ void __launch_bounds__(kThreads, 2) nbit_encode_kernel(const NbitEncP
   if (!(bounds_ok && dmax <= thr_lo)) {
     uint32_t mlo = 0, mhi = 0;
 #pragma unroll
-    for (int k = 0; k < 16; ++k) {
-      float x0, x1;
-      upk2(X[k], x0, x1);
-      const float d0 = fabsf(__fadd_rn(x0, -mu)), d1 = fabsf(__fadd_rn(x1, -mu));
-      mlo |= (uint32_t(d0 > thr_lo) << (2 * k)) | (uint32_t(d1 > thr_lo) << (2 * k + 1));
-      mhi |= (uint32_t(d0 > thr_hi) << (2 * k)) | (uint32_t(d1 > thr_hi) << (2 * k + 1));
+    for (int c = 0; c < 4; ++c) {
+      f2 P[4];
+      chunk_pairs(src, c, P);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        float x0, x1;
+        upk2(P[i], x0, x1);
+        const int e = 8 * c + 2 * i;
+        const float d0 = fabsf(__fadd_rn(x0, -mu)), d1 = fabsf(__fadd_rn(x1, -mu));
+        mlo |= (uint32_t(d0 > thr_lo) << e) | (uint32_t(d1 > thr_lo) << (e + 1));
+        mhi |= (uint32_t(d0 > thr_hi) << e) | (uint32_t(d1 > thr_hi) << (e + 1));
+      }
     }
     omask = mhi;
     if (!bounds_ok || mlo != mhi) {
-      const float thr = exact_threshold(X, sigma);
+      // Exact reference threshold: fp64 two-pass M2, sd rounded once to fp32.
+      double s64 = 0.0;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        f2 P[4];
+        chunk_pairs(src, c, P);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          float x0, x1;
+          upk2(P[i], x0, x1);
+          s64 = __dadd_rn(__dadd_rn(s64, double(x0)), double(x1));
+        }
+      }
+      const double mu64 = __dmul_rn(s64, 0.03125);
+      double m2e = 0.0;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        f2 P[4];
+        chunk_pairs(src, c, P);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          float x0, x1;
+          upk2(P[i], x0, x1);
+          const double e0 = __dadd_rn(double(x0), -mu64), e1 = __dadd_rn(double(x1), -mu64);
+          m2e = __dadd_rn(__dadd_rn(m2e, __dmul_rn(e0, e0)), __dmul_rn(e1, e1));
+        }
+      }
+      const float sd = __double2float_rn(__dsqrt_rn(__ddiv_rn(m2e, 31.0)));
+      const float thr = __fmul_rn(sigma, __fadd_rn(sd, 1e-8f));
       omask = 0;
 #pragma unroll
-      for (int k = 0; k < 16; ++k) {
-        float x0, x1;
-        upk2(X[k], x0, x1);
-        omask |= (uint32_t(fabsf(__fadd_rn(x0, -mu)) > thr) << (2 * k)) |
-                 (uint32_t(fabsf(__fadd_rn(x1, -mu)) > thr) << (2 * k + 1));
+      for (int c = 0; c < 4; ++c) {
+        f2 P[4];
+        chunk_pairs(src, c, P);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          float x0, x1;
+          upk2(P[i], x0, x1);
+          const int e = 8 * c + 2 * i;
+          omask |= (uint32_t(fabsf(__fadd_rn(x0, -mu)) > thr) << e) |
+                   (uint32_t(fabsf(__fadd_rn(x1, -mu)) > thr) << (e + 1));
+        }
       }
     }
     if (omask) {
       am = 0.0f;
 #pragma unroll
-      for (int k = 0; k < 16; ++k) {
-        float x0, x1;
-        upk2(X[k], x0, x1);
-        x0 = (omask >> (2 * k)) & 1u ? mu : x0;
-        x1 = (omask >> (2 * k + 1)) & 1u ? mu : x1;
-        X[k] = pk2(x0, x1);
-        am = max3_abs_nan(am, x0, x1);
+      for (int c = 0; c < 4; ++c) {
+        f2 P[4];
+        chunk_pairs(src, c, P);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          float x0, x1;
+          upk2(P[i], x0, x1);
+          const int e = 8 * c + 2 * i;
+          am = max3_abs_nan(am, (omask >> e) & 1u ? mu : x0, (omask >> (e + 1)) & 1u ? mu : x1);
+        }
       }
     }
   }
@@ -228,15 +258,23 @@ __global__ void __launch_bounds__(kThreads, 2) nbit_encode_kernel(const NbitEncP
   const Recip y = make_recip(delta);
   const bool fast_div = recip_ok(delta);
   const f2 DELTA = pk2(delta, delta), YHI = pk2(y.hi, y.hi), YLO = pk2(y.lo, y.lo), NDELTA = pk2(-delta, -delta);
-  const f2 HALF = pk2(p.half_states, p.half_states);
-  const f2 MAGIC = pk2(12582912.0f, 12582912.0f);
-  const f2 C128 = pk2(128.0f, 128.0f), CM = pk2(-128.5f, -128.5f), NHALF = pk2(-0.5f, -0.5f);
-  // packed codes: 32 * BITS / 32 words (MSB-first within each byte)
-  uint32_t o[BITS];
+  const float half = p.half_states;
+  uint32_t o[BITS];  // packed codes: 32 * BITS bits, MSB-first within each byte
 #pragma unroll
   for (int k = 0; k < BITS; ++k) o[k] = 0u;
 #pragma unroll
-  for (int c = 0; c < 4; ++c) {  // 8 elements per Philox draw
+  for (int c = 0; c < 4; ++c) {  // 8 elements per chunk / Philox draw
+    f2 P[4];
+    chunk_pairs(src, c, P);
+    if (omask & (0xFFu << (8 * c))) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        float x0, x1;
+        upk2(P[i], x0, x1);
+        const int e = 8 * c + 2 * i;
+        P[i] = pk2((omask >> e) & 1u ? mu : x0, (omask >> (e + 1)) & 1u ? mu : x1);
+      }
+    }
     f2 DZ[4];
     if constexpr (DMODE == ASHKV_DITHER_TENSOR) {
       U8 u;
@@ -247,43 +285,47 @@ __global__ void __launch_bounds__(kThreads, 2) nbit_encode_kernel(const NbitEncP
       }
 #pragma unroll
       for (int h = 0; h < 4; ++h)
-        DZ[h] = add2(pk2(__uint_as_float(u.v[2 * h]), __uint_as_float(u.v[2 * h + 1])), NHALF);
+        DZ[h] = add2(pk2(__uint_as_float(u.v[2 * h]), __uint_as_float(u.v[2 * h + 1])), pk2(-0.5f, -0.5f));
     } else {
       const uint64_t ctr = ((p.dither_offset + uint64_t(g) * 32) >> 3) + c;
       const Philox4 r = philox4x32_10(uint32_t(ctr), uint32_t(ctr >> 32), 0u, 0u, uint32_t(p.seed),
                                       uint32_t(p.seed >> 32));
 #pragma unroll
       for (int h = 0; h < 4; ++h) {
-        // f = 1 + h16 * 2^-23; U - 0.5 = 128 f - 128.5 exactly
+        // f = 1 + h16 * 2^-23, so U - 0.5 = 128 f - 128.5 exactly
         const float flo = __uint_as_float(__byte_perm(r.v[h], 0x3F800000u, 0x7610));
         const float fhi = __uint_as_float(__byte_perm(r.v[h], 0x3F800000u, 0x7632));
-        DZ[h] = fma2(pk2(flo, fhi), C128, CM);
+        DZ[h] = fma2(pk2(flo, fhi), pk2(128.0f, 128.0f), pk2(-128.5f, -128.5f));
+      }
+    }
+    f2 Q[4];
+#pragma unroll
+    for (int h = 0; h < 4; ++h) Q[h] = add2(P[h], mul2(DZ[h], DELTA));  // a = x' + noise
+    if (fast_div) {
+#pragma unroll
+      for (int h = 0; h < 4; ++h) Q[h] = div2_rn(Q[h], YHI, YLO, NDELTA);
+    } else {
+#pragma unroll
+      for (int h = 0; h < 4; ++h) {
+        float a0, a1;
+        upk2(Q[h], a0, a1);
+        Q[h] = pk2(__fdiv_rn(a0, delta), __fdiv_rn(a1, delta));
       }
     }
 #pragma unroll
     for (int h = 0; h < 4; ++h) {
-      const int k = 4 * c + h;
-      const f2 A2 = add2(X[k], mul2(DZ[h], DELTA));
-      f2 Q;
-      if (fast_div) {
-        Q = div2_rn(A2, YHI, YLO, NDELTA);
-      } else {
-        float a0, a1;
-        upk2(A2, a0, a1);
-        Q = pk2(__fdiv_rn(a0, delta), __fdiv_rn(a1, delta));
-      }
+      const int k = 4 * c + h;  // pair index: elements 2k, 2k+1
       float v0, v1;
-      upk2(add2(Q, HALF), v0, v1);
-      v0 = fminf(fmaxf(v0, 0.0f), float(kMaxCode));  // NaN -> 0
-      v1 = fminf(fmaxf(v1, 0.0f), float(kMaxCode));
+      upk2(Q[h], v0, v1);
+      v0 = fminf(fmaxf(__fadd_rn(v0, half), 0.0f), float(kMaxCode));  // NaN -> 0
+      v1 = fminf(fmaxf(__fadd_rn(v1, half), 0.0f), float(kMaxCode));
       float t0, t1;
-      upk2(add2(pk2(v0, v1), MAGIC), t0, t1);
+      upk2(add2(pk2(v0, v1), pk2(12582912.0f, 12582912.0f)), t0, t1);
       const uint32_t c0 = __float_as_uint(t0) & kMaxCode, c1 = __float_as_uint(t1) & kMaxCode;
-      // element e = 2k (+1) sits in byte e*BITS/8, MSB first within the byte
       if constexpr (BITS == 4) {
         o[k >> 2] |= ((c0 << 4) | c1) << (8 * (k & 3));
       } else if constexpr (BITS == 2) {
-        const int e = 2 * k;  // even: the pair shares a byte
+        const int e = 2 * k;
         o[e >> 4] |= ((c0 << (6 - 2 * (e & 3))) | (c1 << (4 - 2 * (e & 3)))) << (8 * ((e >> 2) & 3));
       } else {
         o[k >> 1] |= (c0 | (c1 << 8)) << (16 * (k & 1));
@@ -304,17 +346,22 @@ __global__ void __launch_bounds__(kThreads, 2) nbit_encode_kernel(const NbitEncP
       st_cs_v8(p.codes + g * 32, ov);
     }
   }
+  return omask;
+}
 
-  // ---- outlier list of this bucket, ascending element order.
+// Append this thread's outliers (bits of omask) to the bucket's list; the
+// ranks come from a CTA-wide scan, so the list is in ascending element order.
+__device__ __forceinline__ void write_outliers(const NbitEncParams& p, int64_t bucket, int64_t g, uint32_t omask,
+                                               uint32_t* s_warp) {
   const uint32_t cnt = uint32_t(__popc(omask));
   uint32_t total = 0;
   uint32_t pos = cta_exclusive_scan(cnt, s_warp, total);
   if (threadIdx.x == 0) {
-    p.bucket_counts[blockIdx.x] = total;
+    p.bucket_counts[bucket] = total;
     if (total > uint32_t(p.bucket_cap)) atomicOr(p.status, ASHKV_FLAG_OUTLIER_OVERFLOW);
   }
   if (cnt) {
-    uint32_t* out = p.bucket_entries + int64_t(blockIdx.x) * p.bucket_cap;
+    uint32_t* out = p.bucket_entries + bucket * p.bucket_cap;
     uint32_t m = omask;
     while (m) {
       const int i = __ffs(m) - 1;
@@ -324,6 +371,97 @@ __global__ void __launch_bounds__(kThreads, 2) nbit_encode_kernel(const NbitEncP
         out[pos] = (local << 16) | uint32_t(p.src[g * 32 + i]);  // original bits (rare path)
       }
       ++pos;
+    }
+  }
+}
+
+// Direct-load variant: one CTA per bucket, each thread loads its 64-byte
+// group with two 256-bit loads.  Used when a tensor map cannot be built.
+template <int BITS, int DMODE>
+__global__ void __launch_bounds__(kThreads, 2) nbit_encode_kernel(const NbitEncParams p) {
+  __shared__ uint32_t s_warp[kThreads / 32];
+  const int64_t g = int64_t(blockIdx.x) * kThreads + threadIdx.x;
+  const bool active = g < p.n_groups;
+  uint32_t w[16];
+  if (active) {
+    const U8 a = ld_nc_v8(p.src + g * 32);
+    const U8 b = ld_nc_v8(p.src + g * 32 + 16);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) { w[k] = a.v[k]; w[8 + k] = b.v[k]; }
+  } else {
+#pragma unroll
+    for (int k = 0; k < 16; ++k) w[k] = 0u;
+  }
+  const uint32_t omask = encode_group<BITS, DMODE>(RegGroup{w}, p, g, active);
+  write_outliers(p, blockIdx.x, g, omask, s_warp);
+}
+
+constexpr int kTileBytes = kThreads * 64;      // one bucket of bf16 = 16 KiB
+constexpr uint32_t kMaxPolls = 1u << 24;       // bounded mbarrier waits
+
+// Persistent TMA variant: each CTA walks buckets b = blockIdx.x + i*gridDim.x.
+// A 2-D tensor map views the source as [n_groups, 32] bf16; one TMA copy
+// brings a whole bucket (256 rows of 64 bytes) into a shared-memory stage
+// with the 64-byte swizzle (16-byte chunk k of row r stored at chunk
+// k ^ ((r >> 1) & 3)), so the 8 threads of each shared-memory phase hit 8
+// distinct bank groups when they read their own row.  STAGES buckets are in
+// flight per CTA; a stage is refilled as soon as every thread has copied its
+// row into registers.
+template <int BITS, int DMODE, int STAGES>
+__global__ void __launch_bounds__(kThreads, 3) nbit_encode_tma_kernel(const __grid_constant__ CUtensorMap tmap,
+                                                                       const NbitEncParams p, int64_t n_buckets) {
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ uint64_t full[STAGES];
+  __shared__ uint32_t s_warp[kThreads / 32];
+  uint8_t* tiles = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int tid = threadIdx.x;
+  if (tid == 0) {
+#pragma unroll
+    for (int s = 0; s < STAGES; ++s) mbar_init(&full[s], 1);
+    mbar_init_fence();
+  }
+  __syncthreads();
+  if (tid == 0) {
+#pragma unroll
+    for (int s = 0; s < STAGES; ++s) {
+      const int64_t b = blockIdx.x + int64_t(s) * gridDim.x;
+      if (b < n_buckets) {
+        mbar_arrive_expect_tx(&full[s], kTileBytes);
+        tma_load_2d(tiles + s * kTileBytes, &tmap, &full[s], 0, int32_t(b * kThreads));
+      }
+    }
+  }
+  const uint32_t sw = uint32_t(tid >> 1) & 3u;
+  for (int64_t it = 0;; ++it) {
+    const int64_t b = blockIdx.x + it * gridDim.x;
+    if (b >= n_buckets) break;
+    const int s = int(it % STAGES);
+    const uint32_t parity = uint32_t(it / STAGES) & 1u;
+    const bool ok = mbar_wait_bounded(&full[s], parity, kMaxPolls);
+    if (__syncthreads_or(!ok)) {
+      // Give up: flag it, let the copies already issued land, and leave.
+      if (tid == 0) {
+        atomicOr(p.status, ASHKV_FLAG_TIMEOUT);
+        for (int k = 0; k < STAGES; ++k) {
+          const int64_t i2 = it + k;
+          if (blockIdx.x + i2 * gridDim.x < n_buckets)
+            mbar_wait_bounded(&full[i2 % STAGES], uint32_t(i2 / STAGES) & 1u, kMaxPolls);
+        }
+      }
+      return;
+    }
+    const int64_t g = b * kThreads + tid;
+    const bool active = g < p.n_groups;
+    const SmemGroup src{smem_u32(tiles + s * kTileBytes) + uint32_t(tid) * 64u, sw};
+    const uint32_t omask = encode_group<BITS, DMODE>(src, p, g, active);
+    write_outliers(p, b, g, omask, s_warp);  // ends with a CTA barrier: stage s is free
+    if (tid == 0) {
+      const int64_t nb = b + int64_t(STAGES) * gridDim.x;
+      if (nb < n_buckets) {
+        fence_proxy_async_smem();
+        mbar_arrive_expect_tx(&full[s], kTileBytes);
+        tma_load_2d(tiles + s * kTileBytes, &tmap, &full[s], 0, int32_t(nb * kThreads));
+      }
     }
   }
 }
@@ -469,6 +607,54 @@ __global__ void __launch_bounds__(256) bucket_flatten_kernel(const uint32_t* cou
 
 float half_states_for(int bits) { return float((1 << bits) - 1) / 2.0f; }
 
+constexpr int kStages = 4;  // 64 KiB of tiles per CTA, three CTAs per SM
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no -lcuda).
+PFN_cuTensorMapEncodeTiled_v12000 tmap_encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &ptr, 12000, cudaEnableDefault, &q) ==
+            cudaSuccess && q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+    else
+      cudaGetLastError();
+  });
+  return fn;
+}
+
+// [n_groups, 32] bf16 rows of 64 bytes, box = one bucket (256 rows), 64-byte swizzle.
+bool make_group_tmap(CUtensorMap* map, const void* src, int64_t n_groups) {
+  auto fn = tmap_encode_fn();
+  if (!fn || n_groups <= 0 || n_groups > 0x7FFFFF00LL || !aligned(src, 16)) return false;
+  cuuint64_t dims[2] = {32, cuuint64_t(n_groups)};
+  cuuint64_t strides[1] = {64};
+  cuuint32_t box[2] = {32, uint32_t(kThreads)};
+  cuuint32_t estr[2] = {1, 1};
+  const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<void*>(src), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+template <int BITS, int DMODE>
+ashkv_status_t launch_tma(const CUtensorMap& tmap, const NbitEncParams& p, int64_t n_buckets, unsigned grid,
+                          cudaStream_t st) {
+  constexpr int smem = kStages * kTileBytes + 1024;
+  auto kern = nbit_encode_tma_kernel<BITS, DMODE, kStages>;
+  static std::once_flag once;
+  static cudaError_t attr_err = cudaSuccess;
+  std::call_once(once, [&] { attr_err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem); });
+  if (attr_err != cudaSuccess) {
+    set_error("nbit_encode_tma smem attribute", attr_err);
+    return ASHKV_LAUNCH_ERROR;
+  }
+  kern<<<grid, kThreads, smem, st>>>(tmap, p, n_buckets);
+  return check_launch("nbit_encode_tma");
+}
+
 }  // namespace
 }  // namespace ashkv
 
@@ -505,6 +691,21 @@ extern "C" ashkv_status_t ashkv_nbit_encode(
   p.status = d_status;
 
   cudaStream_t st = as_stream(stream);
+  CUtensorMap tmap;
+  if (make_group_tmap(&tmap, d_src, n_groups)) {
+    const int sms = sm_count() > 0 ? sm_count() : 148;
+    const int64_t want = int64_t(sms) * 3;
+    const unsigned grid = unsigned(n_buckets < want ? n_buckets : want);
+    const bool tensor = dither_mode == ASHKV_DITHER_TENSOR;
+    ashkv_status_t s = ASHKV_OK;
+    if (bits == 2) s = tensor ? launch_tma<2, ASHKV_DITHER_TENSOR>(tmap, p, n_buckets, grid, st)
+                              : launch_tma<2, ASHKV_DITHER_PHILOX>(tmap, p, n_buckets, grid, st);
+    else if (bits == 4) s = tensor ? launch_tma<4, ASHKV_DITHER_TENSOR>(tmap, p, n_buckets, grid, st)
+                                   : launch_tma<4, ASHKV_DITHER_PHILOX>(tmap, p, n_buckets, grid, st);
+    else s = tensor ? launch_tma<8, ASHKV_DITHER_TENSOR>(tmap, p, n_buckets, grid, st)
+                    : launch_tma<8, ASHKV_DITHER_PHILOX>(tmap, p, n_buckets, grid, st);
+    return s;
+  }
   const dim3 grid{unsigned(n_buckets)}, block{unsigned(kThreads)};
   if (dither_mode == ASHKV_DITHER_TENSOR) {
     if (bits == 2) nbit_encode_kernel<2, ASHKV_DITHER_TENSOR><<<grid, block, 0, st>>>(p);

@@ -42,6 +42,7 @@ typedef int32_t ashkv_status_t;
 /* ---- device status-word flags (OR-ed into *d_status) ------------------- */
 #define ASHKV_FLAG_OUTLIER_OVERFLOW 0x1u  /* a bucket had more outliers than its capacity */
 #define ASHKV_FLAG_INDEX_RANGE      0x2u  /* an index pointed outside its buffer; that element was skipped */
+#define ASHKV_FLAG_TIMEOUT          0x4u  /* a bounded wait inside a kernel gave up; its outputs are incomplete */
 
 /* ---- element-type tags -------------------------------------------------- */
 #define ASHKV_DTYPE_BF16 0
