@@ -1,0 +1,203 @@
+"""Batched, device-resident page migration (the per-step hot path).
+
+The reference applies ``score_vectorized`` -> ``desired_tiers`` to a host
+snapshot of the page table and would call ``migrate`` once per page
+(ashkv/runtime/migrate.py:35-191), moving bytes through the host for every
+page.  Here one decode step is four kernel launches with no host round trip:
+
+1. ``ashkv_policy_step``      score -> desired tier -> stable demote / promote lists
+2. ``ashkv_int8_encode_pages`` gather each listed BF16 page (K and V rows of one
+                               layer) and INT8-encode it into a shadow-arena slot
+3. ``ashkv_slots_commit``      pop the used slots off the device free stack
+4. ``ashkv_int8_decode_pages`` decode listed pages back into the KV pool and
+                               push their slots back on the free stack
+
+List lengths stay on the device; every kernel reads them there.
+
+Tier commits are explicit (``commit_transitions``): with a lossy codec the
+reference's verify step (checksum of decode(encode(x)) against the BF16
+checksum) always reports CORRUPT, so the batched path leaves the choice of
+when a page changes tier to the caller instead of re-running that check.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import Optional, Sequence
+
+import numpy as np
+import torch
+
+from .. import _native
+from ..compiler.runtime_builder import controller_tables
+from ..contracts.config import ASHKVConfig
+from ..contracts.page import PageTable
+from ..contracts.tiers import Tier
+
+
+@dataclass
+class DevicePageTable:
+    """GPU mirror (struct of arrays) of the PageTable columns the hot path reads."""
+    T: torch.Tensor
+    S: torch.Tensor
+    N: torch.Tensor
+    P: torch.Tensor
+    tier: torch.Tensor         # int8
+    pin: torch.Tensor          # int32
+    layer: torch.Tensor        # int32
+    token_start: torch.Tensor  # int32
+    slot: torch.Tensor         # int32, arena slot of the encoded copy or -1
+
+    @property
+    def n(self) -> int:
+        return self.T.numel()
+
+    @staticmethod
+    def empty(n: int, device: torch.device) -> "DevicePageTable":
+        f = lambda dt: torch.zeros(n, dtype=dt, device=device)  # noqa: E731
+        t = DevicePageTable(f(torch.float32), f(torch.float32), f(torch.float32), f(torch.float32),
+                            f(torch.int8), f(torch.int32), f(torch.int32), f(torch.int32), f(torch.int32))
+        t.slot.fill_(-1)
+        return t
+
+    @staticmethod
+    def from_host(table: PageTable, device: torch.device) -> "DevicePageTable":
+        cols = table.columns()
+        up = lambda name, dt: torch.from_numpy(np.ascontiguousarray(cols[name]).astype(dt)).to(device)  # noqa: E731
+        slot = torch.full((len(cols),), -1, dtype=torch.int32, device=device)
+        return DevicePageTable(up("T", np.float32), up("S", np.float32), up("N", np.float32), up("P", np.float32),
+                               up("tier", np.int8), up("pin_count", np.int32), up("layer_id", np.int32),
+                               up("token_start", np.int32), slot)
+
+    def update_scores(self, table: PageTable) -> None:
+        cols = table.columns()
+        for name in ("T", "S", "N", "P"):
+            getattr(self, name).copy_(torch.from_numpy(np.ascontiguousarray(cols[name])), non_blocking=False)
+
+
+class SlotArena:
+    """Fixed-size slots in one device buffer with a device-side free stack."""
+
+    def __init__(self, n_slots: int, slot_bytes: int, device: torch.device):
+        self.n_slots, self.slot_bytes = n_slots, slot_bytes
+        self.data = torch.empty(n_slots * slot_bytes, dtype=torch.uint8, device=device)
+        # slot 0 on top of the stack first
+        self.free_stack = torch.arange(n_slots - 1, -1, -1, dtype=torch.int32, device=device)
+        self.free_top = torch.full((1,), n_slots, dtype=torch.int32, device=device)
+
+    def free_count(self) -> int:
+        return int(self.free_top.item())
+
+    def pressure(self) -> float:
+        return 1.0 - self.free_count() / max(self.n_slots, 1)
+
+
+class KVLayers:
+    """Per-layer K/V token pools ([tokens, heads, head_dim] bf16 each), addressed by pointer tables."""
+
+    def __init__(self, k: Sequence[torch.Tensor], v: Sequence[torch.Tensor]):
+        if len(k) != len(v) or not k:
+            raise ValueError("need the same number (>0) of K and V layer tensors")
+        self.k, self.v = list(k), list(v)
+        t0 = self.k[0]
+        for t in self.k + self.v:
+            if t.dtype != torch.bfloat16 or not t.is_contiguous() or t.shape != t0.shape or not t.is_cuda:
+                raise ValueError("K/V layers must be contiguous CUDA bf16 tensors of one shape")
+            if t.data_ptr() % 16:
+                raise ValueError("K/V layer tensors must be 16-byte aligned")
+        self.row_len = int(np.prod(t0.shape[1:]))
+        dev = t0.device
+        self.k_ptrs = torch.tensor([t.data_ptr() for t in self.k], dtype=torch.int64, device=dev)
+        self.v_ptrs = torch.tensor([t.data_ptr() for t in self.v], dtype=torch.int64, device=dev)
+
+    @property
+    def n_layers(self) -> int:
+        return len(self.k)
+
+
+@dataclass
+class StepLists:
+    demote: torch.Tensor   # int32 page rows, first counts[0] valid
+    promote: torch.Tensor  # int32 page rows, first counts[1] valid
+    counts: torch.Tensor   # int32 [2] on the device
+    target: torch.Tensor   # int8 desired tier per page
+    R: Optional[torch.Tensor]
+
+
+class BatchMigrator:
+    """Policy + BF16<->INT8 page migration over a DevicePageTable (see module docstring).
+
+    ``status_encode[i]`` / ``status_decode[i]`` report list entry i of the last
+    encode / decode: 0 ok, 1 no free slot, 2 bad page or slot.
+    """
+
+    def __init__(self, table: DevicePageTable, kv: KVLayers, arena: SlotArena, config: ASHKVConfig,
+                 codec_keys: Sequence[tuple[int, int]], tokens_per_page: int = 16, keep_scores: bool = False):
+        self.table, self.kv, self.arena, self.cfg = table, kv, arena, config
+        self.tokens_per_page = tokens_per_page
+        self.next_colder, self.next_hotter = controller_tables(codec_keys)
+        need = int(_native.lib().ashkv_int8_page_slot_bytes(tokens_per_page, kv.row_len))
+        if arena.slot_bytes < need:
+            raise ValueError(f"arena slots of {arena.slot_bytes} bytes cannot hold a page ({need} bytes)")
+        n, dev = table.n, table.T.device
+        self.lists = StepLists(torch.empty(n, dtype=torch.int32, device=dev), torch.empty(n, dtype=torch.int32, device=dev),
+                               torch.zeros(2, dtype=torch.int32, device=dev), torch.empty(n, dtype=torch.int8, device=dev),
+                               torch.empty(n, dtype=torch.float32, device=dev) if keep_scores else None)
+        self._scratch = torch.empty(_native.policy_scratch_ints(n), dtype=torch.int32, device=dev)
+        self.status_encode = torch.zeros(n, dtype=torch.int32, device=dev)
+        self.status_decode = torch.zeros(n, dtype=torch.int32, device=dev)
+
+    def plan(self, pressure: float) -> StepLists:
+        """Score every page, pick desired tiers and build the transition lists (device-resident)."""
+        t, c, L = self.table, self.cfg, self.lists
+        _native.policy_step(t.T, t.S, t.N, t.P, t.tier, (c.w_T, c.w_S, c.w_N, c.w_P), float(pressure), c.theta_high,
+                            c.theta_low, c.delta, c.p_emergency, self.next_colder, self.next_hotter, L.R, L.target,
+                            L.demote, L.promote, L.counts, self._scratch)
+        return L
+
+    def _pages_args(self, lst: torch.Tensor, count: torch.Tensor):
+        t, kv, a = self.table, self.kv, self.arena
+        return (kv.k_ptrs.data_ptr(), kv.v_ptrs.data_ptr(), kv.n_layers, t.layer.data_ptr(), t.token_start.data_ptr(),
+                lst.data_ptr(), count.data_ptr(), lst.numel(), self.tokens_per_page, kv.row_len,
+                kv.row_len, a.data.data_ptr(), a.slot_bytes, a.n_slots)
+
+    def encode(self, lst: torch.Tensor, count: torch.Tensor) -> None:
+        """INT8-encode the first *count pages of ``lst`` into fresh arena slots."""
+        a = self.arena
+        st = _native.stream_handle(lst.device)
+        _native.check(_native.lib().ashkv_int8_encode_pages(
+            *self._pages_args(lst, count), a.free_stack.data_ptr(), a.free_top.data_ptr(),
+            self.table.slot.data_ptr(), self.status_encode.data_ptr(), st), "int8_encode_pages")
+        _native.check(_native.lib().ashkv_slots_commit(count.data_ptr(), lst.numel(), a.free_top.data_ptr(), st),
+                      "slots_commit")
+
+    def decode(self, lst: torch.Tensor, count: torch.Tensor, free_slots: bool = True) -> None:
+        """Decode the slots of the first *count pages of ``lst`` back into the KV pool."""
+        a = self.arena
+        _native.check(_native.lib().ashkv_int8_decode_pages(
+            *self._pages_args(lst, count), self.table.slot.data_ptr(), int(free_slots), a.free_stack.data_ptr(),
+            a.free_top.data_ptr(), self.status_decode.data_ptr(), _native.stream_handle(lst.device)),
+            "int8_decode_pages")
+
+    def demote(self) -> None:
+        self.encode(self.lists.demote, self.lists.counts[0:1])
+
+    def promote(self) -> None:
+        self.decode(self.lists.promote, self.lists.counts[1:2])
+
+    def commit_transitions(self) -> None:
+        """Make the planned target tiers current for pages whose transition succeeded."""
+        t, L = self.table, self.lists
+        n_d, n_p = (int(v) for v in L.counts.tolist())
+        for lst, cnt, status in ((L.demote, n_d, self.status_encode), (L.promote, n_p, self.status_decode)):
+            if cnt:
+                rows = lst[:cnt].long()
+                ok = status[:cnt] == 0
+                ok &= t.pin[rows] <= 0
+                t.tier[rows[ok]] = L.target[rows[ok]]
+
+
+def int8_page_slot_bytes(tokens_per_page: int, row_len: int) -> int:
+    return int(_native.lib().ashkv_int8_page_slot_bytes(tokens_per_page, row_len))
+
+
+__all__ = ["DevicePageTable", "SlotArena", "KVLayers", "BatchMigrator", "StepLists", "int8_page_slot_bytes", "Tier"]

@@ -1,0 +1,231 @@
+"""GPU tests: SGLang hooks, shadow allocator and batched page migration.
+
+Byte formats are compared with the oracle: the host slot of (token t, layer
+l) must hold [fp16 scales of tokens t*H..t*H+H-1 | int8 codes of token t |
+zeros], as the reference's hooks write it.
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+
+from ashkv.adapters.sglang.allocator import SGLangShadowAllocator
+from ashkv.adapters.sglang.hooks import SGLangHooks
+from ashkv.contracts import ASHKVConfig, Tier
+from ashkv.runtime.batch import BatchMigrator, DevicePageTable, KVLayers, SlotArena, int8_page_slot_bytes
+
+pytestmark = pytest.mark.gpu
+
+
+def u16(t: torch.Tensor) -> np.ndarray:
+    return t.detach().cpu().contiguous().view(torch.int16).numpy().view(np.uint16)
+
+
+class DevicePool:
+    def __init__(self, layer_num, capacity, head_num, head_dim, device, seed=0):
+        self.layer_num, self.capacity, self.head_num, self.head_dim = layer_num, capacity, head_num, head_dim
+        g = torch.Generator(device=device).manual_seed(seed)
+        self.k_buffer = [torch.randn(capacity, head_num, head_dim, generator=g, device=device).to(torch.bfloat16)
+                         for _ in range(layer_num)]
+        self.v_buffer = [torch.randn(capacity, head_num, head_dim, generator=g, device=device).to(torch.bfloat16)
+                         for _ in range(layer_num)]
+
+
+class HostPool:
+    def __init__(self, layer_num, capacity, head_num, head_dim, pin=False):
+        shape = (capacity, layer_num, head_num, head_dim)
+        self.k_buffer = torch.full(shape, 7.0, dtype=torch.bfloat16).pin_memory() if pin else \
+            torch.full(shape, 7.0, dtype=torch.bfloat16)
+        self.v_buffer = torch.full(shape, 7.0, dtype=torch.bfloat16).pin_memory() if pin else \
+            torch.full(shape, 7.0, dtype=torch.bfloat16)
+        self.layer_num, self.head_num, self.head_dim = layer_num, head_num, head_dim
+
+
+def expected_slots(k_layer: torch.Tensor, didx: torch.Tensor, H: int, D: int) -> np.ndarray:
+    """Oracle bytes of the host slots [n, 2*H*D] for one layer of K (or V)."""
+    n, row = didx.numel(), H * D
+    rows = u16(k_layer.view(-1, row)[didx.long()]).reshape(n, row)
+    codes, scales = oracle.int8_encode(rows, row, scale_fp16=True)
+    out = np.zeros((n, 2 * row), dtype=np.uint8)
+    out[:, 2 * H:2 * H + row] = codes.view(np.uint8)
+    flat = np.zeros(n * H, dtype=np.uint16)  # slot t carries scales of tokens t*H .. t*H+H-1
+    flat[:n] = scales
+    out[:, :2 * H] = flat.view(np.uint8).reshape(n, 2 * H)
+    return out
+
+
+@pytest.mark.parametrize("contiguous,pin", [(True, True), (True, False), (False, False)])
+def test_demote_writes_reference_slot_bytes(cuda, tmp_path, monkeypatch, contiguous, pin):
+    monkeypatch.chdir(tmp_path)
+    L, cap, H, D, n = 3, 300, 8, 128, 77
+    dev = DevicePool(L, cap, H, D, cuda, seed=1)
+    host = HostPool(L, cap, H, D, pin=pin)
+    didx = torch.randperm(cap, generator=torch.Generator().manual_seed(2))[:n].to(cuda)
+    hidx = torch.arange(10, 10 + n) if contiguous else torch.randperm(cap, generator=torch.Generator().manual_seed(3))[:n]
+    hooks = SGLangHooks()
+    assert hooks.demote_hook(dev, host, hidx, didx, "MHA") is True
+    for name in ("k_buffer", "v_buffer"):
+        hb = getattr(host, name).view(cap, L, -1).view(torch.uint8)
+        for layer in range(L):
+            got = hb[hidx.long(), layer].numpy()
+            want = expected_slots(getattr(dev, name)[layer], didx, H, D)
+            assert np.array_equal(got, want), (name, layer)
+    # untouched host rows keep their contents
+    others = np.setdiff1d(np.arange(cap), hidx.numpy())
+    assert bool((host.k_buffer[torch.from_numpy(others)] == 7.0).all())
+    # stats: the reference's byte math
+    assert hooks.stats["tokens_compressed"] == n * L
+    assert hooks.stats["bytes_saved"] == n * L * H * D * 4 - n * L * (H * D + 2 * H) * 2
+
+
+def test_demote_promote_roundtrip_matches_oracle(cuda, tmp_path, monkeypatch):
+    monkeypatch.chdir(tmp_path)
+    L, cap, H, D, n = 2, 1000, 32, 128, 500  # the reference GPU test's shapes
+    dev = DevicePool(L, cap, H, D, cuda, seed=4)
+    host = HostPool(L, cap, H, D)
+    didx = torch.arange(n, device=cuda)
+    hidx = torch.arange(n)
+    orig = [t.clone() for t in dev.k_buffer]
+    hooks = SGLangHooks()
+    hooks.compressible_layers = [0, 1]
+    hooks.demote_hook(dev, host, hidx, didx, "MHA")
+    dev.k_buffer[0].zero_()
+    assert hooks.promote_hook(dev, host, hidx, didx, 0, "MHA") is True
+    restored = dev.k_buffer[0][didx]
+    cos = torch.nn.functional.cosine_similarity(orig[0][:n].float().view(1, -1), restored.float().view(1, -1)).item()
+    assert cos > 0.99
+    rows = u16(orig[0].view(-1, H * D)[:n]).reshape(n, H * D)
+    codes, scales = oracle.int8_encode(rows, H * D, scale_fp16=True)
+    want = oracle.int8_decode(codes, scales, scale_fp16=True)
+    assert np.array_equal(u16(restored).reshape(n, H * D), want)
+    assert hooks.stats["tokens_decompressed"] == n
+
+
+def test_promote_subset_in_reference_order(cuda, tmp_path, monkeypatch):
+    """Promote into different device rows with a non-contiguous host index list."""
+    monkeypatch.chdir(tmp_path)
+    L, cap, H, D, n = 2, 200, 8, 128, 40
+    dev = DevicePool(L, cap, H, D, cuda, seed=5)
+    host = HostPool(L, cap, H, D)
+    didx = torch.arange(n, device=cuda)
+    hidx = torch.randperm(cap, generator=torch.Generator().manual_seed(6))[:n]
+    hooks = SGLangHooks()
+    src = dev.v_buffer[1][:n].clone()
+    hooks.demote_hook(dev, host, hidx, didx, "MHA")
+    tgt = torch.arange(100, 100 + n, device=cuda)
+    hooks.promote_hook(dev, host, hidx, tgt, 1, "MHA")
+    rows = u16(src).reshape(n, H * D)
+    codes, scales = oracle.int8_encode(rows, H * D, scale_fp16=True)
+    assert np.array_equal(u16(dev.v_buffer[1][100:100 + n]).reshape(n, H * D),
+                          oracle.int8_decode(codes, scales, scale_fp16=True))
+
+
+def test_hooks_decline_and_native_layers(cuda, tmp_path, monkeypatch):
+    monkeypatch.chdir(tmp_path)
+    L, cap, H, D, n = 2, 64, 4, 128, 16
+    dev = DevicePool(L, cap, H, D, cuda, seed=7)
+    host = HostPool(L, cap, H, D)
+    idx = torch.arange(n)
+    hooks = SGLangHooks()
+    assert hooks.demote_hook(dev, host, idx, idx.to(cuda), "MLA") is False
+    assert hooks.demote_hook(dev, host, idx[:0], idx[:0].to(cuda), "MHA") is False
+    assert hooks.promote_hook(dev, host, idx, idx.to(cuda), 0, "MLA") is False
+    hooks.compressible_layers = [0]  # layer 1 travels as plain bf16
+    hooks.demote_hook(dev, host, idx, idx.to(cuda), "MHA")
+    assert torch.equal(host.k_buffer[:n, 1].view(torch.int16), dev.k_buffer[1][:n].cpu().view(torch.int16))
+    saved = dev.k_buffer[1][:n].clone()
+    dev.k_buffer[1].zero_()
+    hooks.promote_hook(dev, host, idx, idx.to(cuda), 1, "MHA")
+    assert torch.equal(dev.k_buffer[1][:n].view(torch.int16), saved.view(torch.int16))
+
+
+def test_shadow_allocator_arena(cuda):
+    a = SGLangShadowAllocator(max_bytes=1 << 20, device=cuda)
+    h1 = a.alloc(Tier.FP8, 1000)
+    h2 = a.alloc(Tier.FP8, 5000)
+    assert h1 > 0 and h2 > 0 and a.pressure() == pytest.approx(6000 / (1 << 20))
+    a.write(h1, b"hello world")
+    assert a.read(h1)[:11] == b"hello world"
+    t = a.get_tensor(h2)
+    assert t.is_cuda and t.numel() == 5000 and t.dtype == torch.uint8
+    t.fill_(3)
+    assert a.read(h2) == b"\x03" * 5000
+    offs = a.offsets([h1, h2]).cpu().numpy()
+    assert offs[0] % 256 == 0 and offs[1] % 256 == 0 and offs[0] != offs[1]
+    assert a.alloc(Tier.FP8, 1 << 20) == -1  # past the budget
+    a.free(h1)
+    h3 = a.alloc(Tier.FP8, 1000)  # exact-size reuse
+    assert a.offsets([h3]).item() == offs[0]
+    assert a.read(12345) == b"" and a.get_tensor(12345) is None
+    a.free(12345)
+
+
+@pytest.mark.parametrize("heads", [8, 1])
+def test_batch_policy_demote_promote_pages(cuda, heads):
+    """Config-4 style: score -> tier -> gather+INT8 encode of demoted pages into arena
+    slots, then decode+scatter back; bytes compared with the oracle per token row."""
+    layers, tokens, T = 4, 4096, 16
+    pages_per_layer = tokens // T
+    g = torch.Generator(device=cuda).manual_seed(11)
+    k = [torch.randn(tokens, heads, 128, generator=g, device=cuda).to(torch.bfloat16) for _ in range(layers)]
+    v = [torch.randn(tokens, heads, 128, generator=g, device=cuda).to(torch.bfloat16) for _ in range(layers)]
+    kv = KVLayers(k, v)
+    n = layers * pages_per_layer
+    tab = DevicePageTable.empty(n, cuda)
+    for name in ("T", "S", "N", "P"):
+        getattr(tab, name).copy_(torch.rand(n, generator=g, device=cuda))
+    tab.layer.copy_(torch.arange(n, device=cuda) // pages_per_layer)
+    tab.token_start.copy_((torch.arange(n, device=cuda) % pages_per_layer) * T)
+    slot = int8_page_slot_bytes(T, kv.row_len)
+    arena = SlotArena(n, slot, cuda)
+    keys = [(0, 1), (1, 0), (1, 2), (2, 1)]
+    mig = BatchMigrator(tab, kv, arena, ASHKVConfig(), keys, keep_scores=True)
+    L = mig.plan(0.9)
+    nd, npro = L.counts.tolist()
+    assert npro == 0 and nd > n // 10
+    orig_k = [t.clone() for t in k]
+    mig.demote()
+    torch.cuda.synchronize()
+    assert arena.free_count() == n - nd
+    assert int(mig.status_encode[:nd].abs().sum()) == 0
+    rows = L.demote[:nd].long()
+    assert bool((tab.slot[rows] >= 0).all())
+    # wipe the demoted pages' K/V, then decode them back from their slots
+    for li in range(layers):
+        k[li].zero_(); v[li].zero_()
+    mig.decode(L.demote, L.counts[0:1], free_slots=True)
+    torch.cuda.synchronize()
+    assert arena.free_count() == n
+    sample = rows[:: max(1, nd // 50)].cpu().numpy()
+    for p in sample:
+        li, ts = int(p) // pages_per_layer, (int(p) % pages_per_layer) * T
+        src = u16(orig_k[li][ts:ts + T]).reshape(T, -1)
+        codes, scales = oracle.int8_encode(src, kv.row_len, scale_fp16=True)
+        assert np.array_equal(u16(k[li][ts:ts + T]).reshape(T, -1), oracle.int8_decode(codes, scales, scale_fp16=True))
+    # pages that were not demoted stay wiped (decode touched only listed pages)
+    keep = np.setdiff1d(np.arange(n), rows.cpu().numpy())[:5]
+    for p in keep:
+        li, ts = int(p) // pages_per_layer, (int(p) % pages_per_layer) * T
+        assert bool((k[li][ts:ts + T] == 0).all())
+    mig.commit_transitions()
+    assert bool((tab.tier[rows] == 1).all())
+
+
+def test_batch_encode_runs_out_of_slots(cuda):
+    layers, tokens, T = 1, 1024, 16
+    kv = KVLayers([torch.randn(tokens, 8, 128, device=cuda).to(torch.bfloat16)],
+                  [torch.randn(tokens, 8, 128, device=cuda).to(torch.bfloat16)])
+    n = tokens // T
+    tab = DevicePageTable.empty(n, cuda)
+    tab.token_start.copy_(torch.arange(n, device=cuda, dtype=torch.int32) * T)
+    arena = SlotArena(10, int8_page_slot_bytes(T, kv.row_len), cuda)
+    mig = BatchMigrator(tab, kv, arena, ASHKVConfig(), [(0, 1), (1, 0)])
+    lst = torch.arange(n, dtype=torch.int32, device=cuda)
+    cnt = torch.tensor([n], dtype=torch.int32, device=cuda)
+    mig.encode(lst, cnt)
+    st = mig.status_encode[:n].cpu().numpy()
+    assert (st[:10] == 0).all() and (st[10:] == 1).all()
+    assert arena.free_count() == 0
