@@ -109,6 +109,33 @@ __device__ __host__ __forceinline__ Philox4 philox4x32_10(uint32_t c0, uint32_t 
   return out;
 }
 
+// The same generator with the ten round keys precomputed by
+// philox_round_keys(): rk[2r], rk[2r+1] = key + r * (W0, W1).
+__device__ __forceinline__ Philox4 philox4x32_10_rk(uint32_t c0, uint32_t c1, uint32_t c2, uint32_t c3,
+                                                    const uint32_t (&rk)[20]) {
+  constexpr uint32_t M0 = 0xD2511F53u, M1 = 0xCD9E8D57u;
+#pragma unroll
+  for (int r = 0; r < 10; ++r) {
+    uint32_t hi0, lo0, hi1, lo1;
+    mulhilo32(M0, c0, hi0, lo0);
+    mulhilo32(M1, c2, hi1, lo1);
+    const uint32_t n0 = hi1 ^ c1 ^ rk[2 * r];
+    const uint32_t n2 = hi0 ^ c3 ^ rk[2 * r + 1];
+    c0 = n0; c1 = lo1; c2 = n2; c3 = lo0;
+  }
+  Philox4 out;
+  out.v[0] = c0; out.v[1] = c1; out.v[2] = c2; out.v[3] = c3;
+  return out;
+}
+
+inline void philox_round_keys(uint64_t seed, uint32_t (&rk)[20]) {
+  uint32_t k0 = uint32_t(seed), k1 = uint32_t(seed >> 32);
+  for (int r = 0; r < 10; ++r) {
+    rk[2 * r] = k0; rk[2 * r + 1] = k1;
+    k0 += 0x9E3779B9u; k1 += 0xBB67AE85u;
+  }
+}
+
 // 16-bit field -> dither value h * 2^-16 - 0.5 in [-0.5, 0.5), exact.
 __device__ __forceinline__ float dither16(uint32_t h16) {
   return __fadd_rn(__uint_as_float(0x3F800000u | (h16 << 7)), -1.5f);

@@ -32,6 +32,7 @@ struct NbitEncParams {
   const uint16_t* src;
   int64_t n_groups;
   const float* dither;
+  uint32_t round_keys[20];  // Philox key schedule: (k0 + r*W0, k1 + r*W1) for r = 0..9
   uint64_t seed;
   uint64_t dither_offset;
   float sigma;
@@ -88,15 +89,38 @@ __device__ __forceinline__ uint32_t cta_exclusive_scan(uint32_t v, uint32_t* sme
 // Otherwise per-element masks against thr_lo and thr_hi are built; if they
 // agree, that is the exact mask, and only if some |x - mu| falls between the
 // two bounds is the exact fp64 threshold computed.
-// A group's 32 bf16 values as 4 chunks of 8 (16 bytes each).
-struct RegGroup {  // held in registers
+// A group's 32 bf16 values as 4 chunks of 8 (16 bytes each), plus access to
+// element e of the group owned by another thread of the CTA.
+struct RegGroup {  // held in registers; other groups read back from global memory
   const uint32_t* w;
+  const uint16_t* src;  // the kernel's source (group g at src + 32 g)
+  int64_t g0;           // group of thread 0 of the CTA
   __device__ __forceinline__ uint4 chunk(int c) const { return make_uint4(w[4 * c], w[4 * c + 1], w[4 * c + 2], w[4 * c + 3]); }
+  __device__ __forceinline__ uint32_t elem(int owner_tid, int e) const { return src[(g0 + owner_tid) * 32 + e]; }
 };
-struct SmemGroup {  // one 64-byte row of a 64-byte-swizzled shared-memory tile
-  uint32_t row, sw;
+struct SmemGroup {  // rows of a 64-byte-swizzled shared-memory tile, one per thread
+  uint32_t tile, row, sw;
   __device__ __forceinline__ uint4 chunk(int c) const { return lds128(row + 16u * (uint32_t(c) ^ sw)); }
+  __device__ __forceinline__ uint32_t elem(int owner_tid, int e) const {
+    const uint32_t osw = uint32_t(owner_tid >> 1) & 3u;
+    const uint32_t a = tile + uint32_t(owner_tid) * 64u + 16u * ((uint32_t(e) >> 3) ^ osw) + 2u * (uint32_t(e) & 7u);
+    uint16_t v;
+    asm volatile("ld.shared.u16 %0, [%1];" : "=h"(v) : "r"(a));
+    return v;
+  }
 };
+
+__device__ __forceinline__ double warp_sum_f64(double v) {  // pairwise (butterfly) order, same in every lane
+#pragma unroll
+  for (int off = 1; off < 32; off <<= 1) v = __dadd_rn(v, __shfl_xor_sync(0xFFFFFFFFu, v, off));
+  return v;
+}
+__device__ __forceinline__ float warp_max_abs_nan(float v) {
+  v = fabsf(v);
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) v = max_nan(v, __shfl_xor_sync(0xFFFFFFFFu, v, off));
+  return v;
+}
 
 template <typename Src>
 __device__ __forceinline__ void chunk_pairs(const Src& src, int c, f2 (&P)[4]) {
@@ -170,84 +194,37 @@ __device__ __forceinline__ uint32_t encode_group(const Src& src, const NbitEncPa
     thr_hi = sigma * (sqrtf(m2_hi / 31.0f) + 1e-8f) * (1.0f + 0x1p-14f);
     thr_lo = sigma * (sqrtf(m2_lo / 31.0f) + 1e-8f) * (1.0f - 0x1p-14f);
   }
+  // Groups whose max |x - mu| exceeds thr_lo are resolved by the whole warp,
+  // one group at a time: lane e takes element e, masks come from ballots, and
+  // if an |x - mu| lies between the bounds the exact threshold is computed
+  // (fp64, pairwise order over the 32 elements).
   uint32_t omask = 0;
   float am = xmax;
-  if (!(bounds_ok && dmax <= thr_lo)) {
-    uint32_t mlo = 0, mhi = 0;
-#pragma unroll
-    for (int c = 0; c < 4; ++c) {
-      f2 P[4];
-      chunk_pairs(src, c, P);
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        float x0, x1;
-        upk2(P[i], x0, x1);
-        const int e = 8 * c + 2 * i;
-        const float d0 = fabsf(__fadd_rn(x0, -mu)), d1 = fabsf(__fadd_rn(x1, -mu));
-        mlo |= (uint32_t(d0 > thr_lo) << e) | (uint32_t(d1 > thr_lo) << (e + 1));
-        mhi |= (uint32_t(d0 > thr_hi) << e) | (uint32_t(d1 > thr_hi) << (e + 1));
-      }
-    }
-    omask = mhi;
-    if (!bounds_ok || mlo != mhi) {
-      // Exact reference threshold: fp64 two-pass M2, sd rounded once to fp32.
-      double s64 = 0.0;
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        f2 P[4];
-        chunk_pairs(src, c, P);
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          float x0, x1;
-          upk2(P[i], x0, x1);
-          s64 = __dadd_rn(__dadd_rn(s64, double(x0)), double(x1));
-        }
-      }
-      const double mu64 = __dmul_rn(s64, 0.03125);
-      double m2e = 0.0;
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        f2 P[4];
-        chunk_pairs(src, c, P);
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          float x0, x1;
-          upk2(P[i], x0, x1);
-          const double e0 = __dadd_rn(double(x0), -mu64), e1 = __dadd_rn(double(x1), -mu64);
-          m2e = __dadd_rn(__dadd_rn(m2e, __dmul_rn(e0, e0)), __dmul_rn(e1, e1));
-        }
-      }
+  const int lane = threadIdx.x & 31;
+  uint32_t todo = __ballot_sync(0xFFFFFFFFu, active && !(bounds_ok && dmax <= thr_lo));
+  while (todo) {
+    const int owner = __ffs(todo) - 1;
+    todo &= todo - 1;
+    const float mu_o = __shfl_sync(0xFFFFFFFFu, mu, owner);
+    const float lo_o = __shfl_sync(0xFFFFFFFFu, thr_lo, owner);
+    const float hi_o = __shfl_sync(0xFFFFFFFFu, thr_hi, owner);
+    const bool ok_o = __shfl_sync(0xFFFFFFFFu, int(bounds_ok), owner) != 0;
+    const float x = bf16_to_f32(uint16_t(src.elem((threadIdx.x & ~31) + owner, lane)));
+    const float d = fabsf(__fadd_rn(x, -mu_o));
+    const uint32_t mlo = __ballot_sync(0xFFFFFFFFu, d > lo_o);
+    uint32_t m = __ballot_sync(0xFFFFFFFFu, d > hi_o);
+    if (!ok_o || mlo != m) {
+      const double s64 = warp_sum_f64(double(x));
+      const double e = __dadd_rn(double(x), -__dmul_rn(s64, 0.03125));
+      const double m2e = warp_sum_f64(__dmul_rn(e, e));
       const float sd = __double2float_rn(__dsqrt_rn(__ddiv_rn(m2e, 31.0)));
       const float thr = __fmul_rn(sigma, __fadd_rn(sd, 1e-8f));
-      omask = 0;
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        f2 P[4];
-        chunk_pairs(src, c, P);
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          float x0, x1;
-          upk2(P[i], x0, x1);
-          const int e = 8 * c + 2 * i;
-          omask |= (uint32_t(fabsf(__fadd_rn(x0, -mu)) > thr) << e) |
-                   (uint32_t(fabsf(__fadd_rn(x1, -mu)) > thr) << (e + 1));
-        }
-      }
+      m = __ballot_sync(0xFFFFFFFFu, d > thr);
     }
-    if (omask) {
-      am = 0.0f;
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        f2 P[4];
-        chunk_pairs(src, c, P);
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          float x0, x1;
-          upk2(P[i], x0, x1);
-          const int e = 8 * c + 2 * i;
-          am = max3_abs_nan(am, (omask >> e) & 1u ? mu : x0, (omask >> (e + 1)) & 1u ? mu : x1);
-        }
-      }
+    const float amv = warp_max_abs_nan((m >> lane) & 1u ? mu_o : x);
+    if (lane == owner) {
+      omask = m;
+      am = amv;
     }
   }
   if (!active) omask = 0;
@@ -288,8 +265,7 @@ __device__ __forceinline__ uint32_t encode_group(const Src& src, const NbitEncPa
         DZ[h] = add2(pk2(__uint_as_float(u.v[2 * h]), __uint_as_float(u.v[2 * h + 1])), pk2(-0.5f, -0.5f));
     } else {
       const uint64_t ctr = ((p.dither_offset + uint64_t(g) * 32) >> 3) + c;
-      const Philox4 r = philox4x32_10(uint32_t(ctr), uint32_t(ctr >> 32), 0u, 0u, uint32_t(p.seed),
-                                      uint32_t(p.seed >> 32));
+      const Philox4 r = philox4x32_10_rk(uint32_t(ctr), uint32_t(ctr >> 32), 0u, 0u, p.round_keys);
 #pragma unroll
       for (int h = 0; h < 4; ++h) {
         // f = 1 + h16 * 2^-23, so U - 0.5 = 128 f - 128.5 exactly
@@ -392,7 +368,8 @@ __global__ void __launch_bounds__(kThreads, 2) nbit_encode_kernel(const NbitEncP
 #pragma unroll
     for (int k = 0; k < 16; ++k) w[k] = 0u;
   }
-  const uint32_t omask = encode_group<BITS, DMODE>(RegGroup{w}, p, g, active);
+  const uint32_t omask =
+      encode_group<BITS, DMODE>(RegGroup{w, p.src, int64_t(blockIdx.x) * kThreads}, p, g, active);
   write_outliers(p, blockIdx.x, g, omask, s_warp);
 }
 
@@ -452,7 +429,8 @@ __global__ void __launch_bounds__(kThreads, 3) nbit_encode_tma_kernel(const __gr
     }
     const int64_t g = b * kThreads + tid;
     const bool active = g < p.n_groups;
-    const SmemGroup src{smem_u32(tiles + s * kTileBytes) + uint32_t(tid) * 64u, sw};
+    const uint32_t tile = smem_u32(tiles + s * kTileBytes);
+    const SmemGroup src{tile, tile + uint32_t(tid) * 64u, sw};
     const uint32_t omask = encode_group<BITS, DMODE>(src, p, g, active);
     write_outliers(p, b, g, omask, s_warp);  // ends with a CTA barrier: stage s is free
     if (tid == 0) {
@@ -685,6 +663,7 @@ extern "C" ashkv_status_t ashkv_nbit_encode(
   NbitEncParams p;
   p.src = static_cast<const uint16_t*>(d_src); p.n_groups = n_groups;
   p.dither = d_dither; p.seed = seed; p.dither_offset = dither_elem_offset;
+  philox_round_keys(seed, p.round_keys);
   p.sigma = sigma; p.half_states = half_states_for(bits);
   p.scales = static_cast<uint16_t*>(d_scales); p.codes = static_cast<uint8_t*>(d_codes);
   p.bucket_counts = d_bucket_counts; p.bucket_entries = d_bucket_entries; p.bucket_cap = bucket_cap;

@@ -125,6 +125,15 @@ static float max_nan(float a, float b) {
   return a > b ? a : b;
 }
 
+/* Pairwise sum of 32 doubles: level k adds elements i and i ^ 2^k. */
+static double pairwise_sum32(const double* v) {
+  double a[32];
+  for (int i = 0; i < 32; ++i) a[i] = v[i];
+  for (int w = 1; w < 32; w <<= 1)
+    for (int i = 0; i < 32; i += 2 * w) a[i] = a[i] + a[i + w];
+  return a[0];
+}
+
 /* Groups of 32 elements; `dither` holds U in [0, 1) per element (the
  * reference's torch.rand draw), noise = (U - 0.5) * delta. */
 void oracle_nbit_encode(const uint16_t* src, int64_t n_groups, int bits, float sigma,
@@ -142,15 +151,17 @@ void oracle_nbit_encode(const uint16_t* src, int64_t n_groups, int bits, float s
     float s = acc[0];
     for (int i = 1; i < 8; ++i) s = s + acc[i];
     const float mu = s / 32.0f;
-    /* unbiased std in fp64, two-pass, rounded once to fp32. */
-    double s64 = 0.0;
-    for (int i = 0; i < 32; ++i) s64 = s64 + (double)x[i];
-    const double mu64 = s64 * 0.03125;
-    double m2 = 0.0;
+    /* unbiased std in fp64 (two-pass, pairwise sums), rounded once to fp32;
+     * PyTorch computes the same quantity in fp64 (Welford), the fp32 result
+     * agrees except when it sits within ~1e-16 of a rounding boundary. */
+    double t[32];
+    for (int i = 0; i < 32; ++i) t[i] = (double)x[i];
+    const double mu64 = pairwise_sum32(t) * 0.03125;
     for (int i = 0; i < 32; ++i) {
-      double d = (double)x[i] - mu64;
-      m2 = m2 + d * d;
+      const double d = (double)x[i] - mu64;
+      t[i] = d * d;
     }
+    const double m2 = pairwise_sum32(t);
     const float sd = (float)sqrt(m2 / 31.0);
     const float thr = sigma * (sd + 1e-8f);
     uint32_t om = 0;
