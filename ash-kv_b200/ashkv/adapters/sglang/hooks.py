@@ -94,16 +94,9 @@ class SGLangHooks:
         H, D, L = device_pool.head_num, device_pool.head_dim, device_pool.layer_num
         if self.compressible_layers is None:
             self.compressible_layers = list(range(L))
-        compress = set(self.compressible_layers)
+        self._demote(device_pool, host_pool, host_indices, device_indices, n, H, D, L,
+                     set(self.compressible_layers))
         row = H * D
-        slot = 2 * row
-        dev = device_pool.k_buffer[0].device
-        if dev.type == "cuda":
-            with torch.cuda.device(dev):
-                self._demote_cuda(device_pool, host_pool, host_indices, device_indices, n, H, D, L, compress)
-        else:
-            raise RuntimeError("SGLangHooks needs the device KV pool on a CUDA device")
-
         nc = len(self.compressible_layers)
         self.stats["blocks_intercepted"] += 1
         self.stats["tokens_compressed"] += n * nc
@@ -112,6 +105,13 @@ class SGLangHooks:
         self.stats["bytes_saved"] += bf16_bytes - int8_bytes
         self._maybe_flush()
         return True
+
+    def _demote(self, device_pool, host_pool, host_indices, device_indices, n, H, D, L, compress) -> None:
+        dev = device_pool.k_buffer[0].device
+        if dev.type != "cuda":
+            raise RuntimeError("SGLangHooks needs the device KV pool on a CUDA device")
+        with torch.cuda.device(dev):
+            self._demote_cuda(device_pool, host_pool, host_indices, device_indices, n, H, D, L, compress)
 
     def _demote_cuda(self, device_pool, host_pool, host_indices, device_indices, n, H, D, L, compress) -> None:
         row, slot = H * D, 2 * H * D

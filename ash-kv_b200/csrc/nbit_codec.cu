@@ -493,9 +493,11 @@ __device__ __forceinline__ void dequant_group(const uint16_t* scales, const uint
     o[i] = f32x2_to_bf16x2(a, b);
   }
   uint16_t* out = dst + g * 32;
+  U8 lo, hi;
 #pragma unroll
-  for (int k = 0; k < 4; ++k)
-    st_cs_v4(out + 8 * k, make_uint4(o[4 * k], o[4 * k + 1], o[4 * k + 2], o[4 * k + 3]));
+  for (int k = 0; k < 8; ++k) { lo.v[k] = o[k]; hi.v[k] = o[8 + k]; }
+  st_cs_v8(out, lo);
+  st_cs_v8(out + 16, hi);
 }
 
 template <int BITS>
@@ -707,7 +709,7 @@ extern "C" ashkv_status_t ashkv_nbit_decode(
   if (n_groups == 0) return ASHKV_OK;
   if (!d_scales || !d_codes || !d_dst) return ASHKV_BAD_ARGUMENT;
   if (d_bucket_counts && (!d_status || (bucket_cap > 0 && !d_bucket_entries))) return ASHKV_BAD_ARGUMENT;
-  if (!aligned(d_dst, 16) || !aligned(d_scales, 2) || !aligned(d_codes, bits == 2 ? 8 : 16))
+  if (!aligned(d_dst, 32) || !aligned(d_scales, 2) || !aligned(d_codes, bits == 2 ? 8 : 16))
     return ASHKV_BAD_ARGUMENT;
   const int64_t n_buckets = (n_groups + kThreads - 1) / kThreads;
   if (n_buckets > 0x7FFFFFFF) return ASHKV_BAD_ARGUMENT;
@@ -758,7 +760,7 @@ extern "C" ashkv_status_t ashkv_nbit_decode_flat(
   if (n_groups == 0) return ASHKV_OK;
   if (!d_scales || !d_codes || !d_dst) return ASHKV_BAD_ARGUMENT;
   if (n_outliers > 0 && (!d_out_index || !d_out_value || !d_status)) return ASHKV_BAD_ARGUMENT;
-  if (!aligned(d_dst, 16) || !aligned(d_scales, 2) || !aligned(d_codes, bits == 2 ? 8 : 16))
+  if (!aligned(d_dst, 32) || !aligned(d_scales, 2) || !aligned(d_codes, bits == 2 ? 8 : 16))
     return ASHKV_BAD_ARGUMENT;
   const int64_t n_blocks = (n_groups + kThreads - 1) / kThreads;
   if (n_blocks > 0x7FFFFFFF) return ASHKV_BAD_ARGUMENT;

@@ -191,6 +191,93 @@ def run_reference(args) -> None:
     print(json.dumps(line), flush=True)
 
 
+
+# ------------------------------------------------------------------ demote leg (config 4)
+DEMOTE_LAYERS, DEMOTE_HEADS, DEMOTE_TOKENS, DEMOTE_T = 64, 8, 32 * 8192, 16
+
+
+def run_demote(dev, world: int, rank: int, dist, steps: int, warmup: int) -> dict:
+    """64-layer model, 8 KV heads x 128, 32 seq x 8192 tokens in 16-token
+    pages, features U[0,1], default policy, pressure 0.9.  KV heads are sharded over the
+    ranks (TP); the page table is replicated; the only collective is the MAX all-reduce of
+    the allocator pressure before each plan.  One step = policy kernel (score -> tier ->
+    lists) + gather/INT8-encode of every page on the demotion list into arena slots
+    (demote) + decode of those pages back into the KV pool (promote)."""
+    from ashkv.contracts import ASHKVConfig
+    from ashkv.runtime.batch import BatchMigrator, DevicePageTable, KVLayers, SlotArena, int8_page_slot_bytes
+
+    heads = DEMOTE_HEADS // world
+    pages_per_layer = DEMOTE_TOKENS // DEMOTE_T
+    n = DEMOTE_LAYERS * pages_per_layer
+    g = torch.Generator(device=dev).manual_seed(4000 + rank)
+    k, v = [], []
+    for _ in range(DEMOTE_LAYERS):
+        k.append(torch.randn(DEMOTE_TOKENS, heads, 128, generator=g, device=dev).to(torch.bfloat16))
+        v.append(torch.randn(DEMOTE_TOKENS, heads, 128, generator=g, device=dev).to(torch.bfloat16))
+    kv = KVLayers(k, v)
+    tab = DevicePageTable.empty(n, dev)
+    gf = torch.Generator(device=dev).manual_seed(4242)  # same features on every rank (replicated table)
+    for name in ("T", "S", "N", "P"):
+        getattr(tab, name).copy_(torch.rand(n, generator=gf, device=dev))
+    idx = torch.arange(n, device=dev, dtype=torch.int64)
+    tab.layer.copy_(idx // pages_per_layer)
+    tab.token_start.copy_((idx % pages_per_layer) * DEMOTE_T)
+    keys = [(0, 1), (1, 0), (1, 2), (2, 1), (0, 2), (2, 0), (2, 3), (3, 2)]
+    slot = int8_page_slot_bytes(DEMOTE_T, kv.row_len)
+    mig0 = BatchMigrator(tab, kv, SlotArena(1, slot, dev), ASHKVConfig(), keys)
+    n_demote = int(mig0.plan(0.9).counts[0].item())
+    arena = SlotArena(n_demote + 1024, slot, dev)
+    mig = BatchMigrator(tab, kv, arena, ASHKVConfig(), keys)
+    del mig0
+    local_p = torch.tensor([0.9], dtype=torch.float32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def step(ev=None):
+        pr = local_p.clone()
+        if dist:
+            dist.all_reduce(pr, op=dist.ReduceOp.MAX)
+        L = mig.plan(float(pr.item()))
+        if ev is not None:
+            ev[0].record(stream)
+        mig.demote()
+        if ev is not None:
+            ev[1].record(stream)
+        mig.decode(L.demote, L.counts[0:1], free_slots=True)
+
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(steps)]
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for i in range(steps):
+        step(evs[i])
+    stop.record(stream)
+    torch.cuda.synchronize()
+    ms = start.elapsed_time(stop) / steps
+    enc_ms = statistics.mean(e[0].elapsed_time(e[1]) for e in evs)
+    t = torch.tensor([ms, enc_ms], dtype=torch.float64, device=dev)
+    if dist:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms, enc_ms = float(t[0]), float(t[1])
+    page_bytes = DEMOTE_T * kv.row_len * 2 * 2  # K + V bf16 of one page on this rank
+    enc_alg = n_demote * (page_bytes + page_bytes // 2 + 4 * DEMOTE_T)
+    ok = int(mig.status_encode[:n_demote].ne(0).sum().item()) == 0
+    del k, v, kv, arena, mig
+    torch.cuda.empty_cache()
+    return {"workload": "64 layers x K,V [262144 tokens, 8 KV heads, 128] bf16 sharded over KV heads; "
+                        "1,048,576 (layer, 16-token page) entries; U[0,1] features; pressure 0.9",
+            "pages": n, "demoted_pages": n_demote, "heads_per_rank": heads,
+            "demote_pages_per_s": round(n_demote / (enc_ms / 1e3), 1),
+            "step_pages_per_s": round(n_demote / (ms / 1e3), 1),
+            "ms_per_step": round(ms, 4), "encode_ms": round(enc_ms, 4),
+            "encode_hbm_gbs": round(enc_alg / (enc_ms / 1e3) / 1e9, 1),
+            "scaling": "strong (fixed model, heads split over ranks)", "all_slots_ok": ok,
+            "step": "pressure all-reduce (N>1) + policy kernel + gather/INT8 encode of demoted pages + decode back",
+            "gpu_launches_per_step": 5}
+
 # ------------------------------------------------------------------ GPU leg
 def main() -> None:
     ap = argparse.ArgumentParser()
@@ -202,6 +289,8 @@ def main() -> None:
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--ref-seconds", type=float, default=5.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-demote", action="store_true")
+    ap.add_argument("--demote-steps", type=int, default=10)
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)
@@ -243,6 +332,8 @@ def main() -> None:
         if ev is not None:
             ev[2].record(stream)
         nb.decode_groups(encK, out=outK)
+        if ev is not None:
+            ev[3].record(stream)
         nb.decode_groups(encV, out=outV)
 
     for i in range(args.warmup):
@@ -250,7 +341,7 @@ def main() -> None:
     torch.cuda.synchronize()
     if dist:
         dist.barrier()
-    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(args.steps)]
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clocks:
         torch.cuda.synchronize()
@@ -261,6 +352,7 @@ def main() -> None:
         torch.cuda.synchronize()
     elapsed_ms = start.elapsed_time(stop)
     enc_ms = statistics.mean([e[0].elapsed_time(e[1]) for e in evs] + [e[1].elapsed_time(e[2]) for e in evs])
+    dec_ms = statistics.mean(e[2].elapsed_time(e[3]) for e in evs)
     n_out = int(encK.bucket_counts.sum().item())
 
     # end-to-end through the bytes API (host buffers)
@@ -295,8 +387,14 @@ def main() -> None:
     e2e_value = world * bytes_per_step * args.e2e_steps / t_e2e / 1e9
     enc_alg_bytes = ELEMS * 2 + ELEMS * BITS // 8 + (ELEMS // 32) * 2 + 4 * n_out + 4 * nb._native.nbit_bucket_count(ELEMS // 32)
     achieved = enc_alg_bytes / (enc_ms / 1e3) / 1e9
+    dec_alg_bytes = ELEMS * BITS // 8 + (ELEMS // 32) * 2 + 4 * nb._native.nbit_bucket_count(ELEMS // 32) + 4 * n_out + ELEMS * 2
+    dec_achieved = dec_alg_bytes / (dec_ms / 1e3) / 1e9
     peak, peak_kind = measured_hbm_peak()
     traffic = profile_traffic()
+
+    demote = None
+    if not args.no_demote:
+        demote = run_demote(dev, world, rank, dist, args.demote_steps, 3)
 
     if rank == 0:
         cpu = None
@@ -313,13 +411,16 @@ def main() -> None:
             "encode_gbs_bf16": round(world * ELEMS * 2 / (enc_ms / 1e3) / 1e9, 2),
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "traffic": traffic, "peak_kind": peak_kind,
-                         "kernel": "nbit_encode_kernel<4,PHILOX>",
+                         "kernel": "nbit_encode_tma_kernel<4,PHILOX,4>",
                          "alg_bytes_per_launch": enc_alg_bytes, "avg_launch_ms": round(enc_ms, 4)},
+            "decode": {"kernel": "nbit_decode_kernel<4>", "avg_launch_ms": round(dec_ms, 4),
+                       "achieved_gbs": round(dec_achieved, 1), "frac": round(dec_achieved / peak, 4)},
             "e2e": {"value": round(e2e_value, 3), "unit": "GB/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h},
             "gpu_launches": 4 * args.steps,
             "clocks": clocks.summary(),
             "cpu_baseline": cpu,
+            "demote": demote,
         }
         print(json.dumps(line), flush=True)
     if dist:
