@@ -196,7 +196,7 @@ def run_reference(args) -> None:
 DEMOTE_LAYERS, DEMOTE_HEADS, DEMOTE_TOKENS, DEMOTE_T = 64, 8, 32 * 8192, 16
 
 
-def run_demote(dev, world: int, rank: int, dist, steps: int, warmup: int) -> dict:
+def run_demote(dev, world: int, rank: int, dist, steps: int, warmup: int, layers: int = DEMOTE_LAYERS) -> dict:
     """64-layer model, 8 KV heads x 128, 32 seq x 8192 tokens in 16-token
     pages, features U[0,1], default policy, pressure 0.9.  KV heads are sharded over the
     ranks (TP); the page table is replicated; the only collective is the MAX all-reduce of
@@ -208,10 +208,10 @@ def run_demote(dev, world: int, rank: int, dist, steps: int, warmup: int) -> dic
 
     heads = DEMOTE_HEADS // world
     pages_per_layer = DEMOTE_TOKENS // DEMOTE_T
-    n = DEMOTE_LAYERS * pages_per_layer
+    n = layers * pages_per_layer
     g = torch.Generator(device=dev).manual_seed(4000 + rank)
     k, v = [], []
-    for _ in range(DEMOTE_LAYERS):
+    for _ in range(layers):
         k.append(torch.randn(DEMOTE_TOKENS, heads, 128, generator=g, device=dev).to(torch.bfloat16))
         v.append(torch.randn(DEMOTE_TOKENS, heads, 128, generator=g, device=dev).to(torch.bfloat16))
     kv = KVLayers(k, v)
@@ -267,8 +267,8 @@ def run_demote(dev, world: int, rank: int, dist, steps: int, warmup: int) -> dic
     ok = int(mig.status_encode[:n_demote].ne(0).sum().item()) == 0
     del k, v, kv, arena, mig
     torch.cuda.empty_cache()
-    return {"workload": "64 layers x K,V [262144 tokens, 8 KV heads, 128] bf16 sharded over KV heads; "
-                        "1,048,576 (layer, 16-token page) entries; U[0,1] features; pressure 0.9",
+    return {"workload": f"{layers} layers x K,V [262144 tokens, 8 KV heads, 128] bf16 sharded over KV heads; "
+                        f"{n} (layer, 16-token page) entries; U[0,1] features; pressure 0.9",
             "pages": n, "demoted_pages": n_demote, "heads_per_rank": heads,
             "demote_pages_per_s": round(n_demote / (enc_ms / 1e3), 1),
             "step_pages_per_s": round(n_demote / (ms / 1e3), 1),
@@ -291,6 +291,8 @@ def main() -> None:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-demote", action="store_true")
     ap.add_argument("--demote-steps", type=int, default=10)
+    ap.add_argument("--demote-layers", type=int, default=DEMOTE_LAYERS,
+                    help="layers of the config-4 model (64; fewer only for small profiling cases)")
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)
@@ -394,7 +396,7 @@ def main() -> None:
 
     demote = None
     if not args.no_demote:
-        demote = run_demote(dev, world, rank, dist, args.demote_steps, 3)
+        demote = run_demote(dev, world, rank, dist, args.demote_steps, 3, args.demote_layers)
 
     if rank == 0:
         cpu = None
