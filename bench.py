@@ -62,7 +62,7 @@ def profile_traffic() -> float | None:
     p = REPO / "profiles" / "nbit_encode_int4_config2.md"
     if not p.exists():
         return None
-    m = re.search(r"dram_bytes_per_launch:\s*([0-9.eE+]+)", p.read_text())
+    m = re.search(r"dram_bytes_per_launch:\s*([0-9]+)", p.read_text())
     return float(m.group(1)) if m else None
 
 
