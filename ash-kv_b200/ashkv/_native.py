@@ -46,6 +46,8 @@ SIGNATURES: dict[str, tuple] = {
     "ashkv_desired_tiers": (_I32, [_P, _P, _I64, _F64, _F64, _F64, _F64, _F64, _P, _P, _P, _P]),
     "ashkv_policy_scratch_ints": (_I64, [_I64]),
     "ashkv_memcpy2d": (_I32, [_P, _I64, _P, _I64, _I64, _I64, _P]),
+    "ashkv_policy_step_noalloc": (_I32, [_P, _P, _P, _P, _P, _I64, _F32, _F32, _F32, _F32, _F64, _F64, _F64, _F64,
+                                         _F64, _P, _P, _P, _P, _P, _P, _P, _P]),
     "ashkv_int8_page_slot_bytes": (_I64, [_I32, _I32]),
     "ashkv_int8_encode_pages": (_I32, [_P, _P, _I32, _P, _P, _P, _P, _I32, _I32, _I32, _I64, _P, _I64, _I64, _P, _P,
                                        _P, _P, _P]),
@@ -301,3 +303,26 @@ def memcpy2d(dst_ptr: int, dst_pitch: int, src_ptr: int, src_pitch: int, width: 
     """Pitched async copy on the current stream (host pointers should be pinned for async)."""
     check(lib().ashkv_memcpy2d(dst_ptr, dst_pitch, src_ptr, src_pitch, width, height, stream_handle(device)),
           "memcpy2d")
+
+
+POLICY_NOALLOC_MAX_PAGES = 4194304
+
+
+def policy_step_noalloc(T, S, N, P, cur, weights, pressure: float, theta_high: float, theta_low: float,
+                        delta: float, p_emergency: float, next_colder, next_hotter, R: Optional[torch.Tensor],
+                        target: torch.Tensor, demote_list: torch.Tensor, promote_list: torch.Tensor,
+                        counts: torch.Tensor) -> None:
+    """``policy_step`` without a scratch buffer: for callers that cannot allocate device
+    memory during a step.  The library keeps the per-block counts in a static device array
+    (page tables up to POLICY_NOALLOC_MAX_PAGES entries); calls that overlap on the GPU race."""
+    _require_cuda(T, S, N, P, cur, R, target, demote_list, promote_list, counts)
+    n = T.numel()
+    if demote_list.numel() < n or promote_list.numel() < n:
+        raise ValueError("policy_step_noalloc: list buffers too small")
+    w_T, w_S, w_N, w_P = (float(w) for w in weights)
+    nc, nh = _table(next_colder), _table(next_hotter)
+    check(lib().ashkv_policy_step_noalloc(
+        T.data_ptr(), S.data_ptr(), N.data_ptr(), P.data_ptr(), cur.data_ptr(), n, w_T, w_S, w_N, w_P,
+        pressure, theta_high, theta_low, delta, p_emergency, _addr(nc), _addr(nh), _ptr(R), target.data_ptr(),
+        demote_list.data_ptr(), promote_list.data_ptr(), counts.data_ptr(), stream_handle(T.device)),
+        "policy_step_noalloc")

@@ -12,6 +12,8 @@ void set_error(const char* what, cudaError_t err) {
   std::snprintf(g_last_error, sizeof(g_last_error), "%s: %s (%d)", what, cudaGetErrorString(err), int(err));
 }
 
+void set_message(const char* text) { std::snprintf(g_last_error, sizeof(g_last_error), "%s", text); }
+
 ashkv_status_t check_launch(const char* what) {
   const cudaError_t err = cudaGetLastError();
   if (err == cudaSuccess) return ASHKV_OK;

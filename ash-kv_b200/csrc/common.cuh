@@ -14,6 +14,7 @@ namespace ashkv {
 // Records the last CUDA error (thread-local) and maps it to a status code.
 ashkv_status_t check_launch(const char* what);
 void set_error(const char* what, cudaError_t err);
+void set_message(const char* text);
 
 inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
 

@@ -240,3 +240,80 @@ extern "C" ashkv_status_t ashkv_policy_step(
                                                         d_promote_list, d_counts);
   return check_launch("policy_compact");
 }
+
+// ---------------------------------------------------------------------------
+// Allocation-free policy step.
+//
+// Some callers cannot allocate device memory when they plan a step: a serving
+// engine that reserves almost all of HBM for its KV pool at start-up leaves
+// nothing for a per-step cudaMalloc (it can fail, or fragment the pool), and
+// plain C/FFI callers have no caching allocator to borrow a scratch buffer
+// from.  ashkv_policy_step_noalloc needs no scratch argument: the per-block
+// transition counts live in the static device array below, so the caller
+// passes only inputs and outputs.
+//
+// The array is a file-scope __device__ object: every GPU that loads the
+// library holds it (32 KiB) until the process exits.  It bounds the page
+// table at ASHKV_POLICY_NOALLOC_MAX_PAGES entries.  All calls share it, so
+// two calls whose kernels overlap on the GPU (e.g. on different streams)
+// race; calls on one stream are ordered and safe.  Nothing in it needs to
+// start at zero: the first kernel writes every count the second one reads.
+// ---------------------------------------------------------------------------
+#include <mutex>
+
+namespace ashkv {
+namespace {
+
+constexpr int64_t kNoallocMaxBlocks = (ASHKV_POLICY_NOALLOC_MAX_PAGES + kPagesPerBlock - 1) / kPagesPerBlock;
+static __device__ __align__(256) int32_t g_policy_scratch[2 * kNoallocMaxBlocks + 2];
+
+constexpr int kMaxDevices = 64;
+int32_t* g_scratch_ptr[kMaxDevices] = {};
+std::mutex g_scratch_mu;
+
+// Device address of g_policy_scratch on the current device (looked up once per
+// device: in host code the symbol name is only a host-side stand-in).
+ashkv_status_t scratch_for_current_device(int32_t** out) {
+  int dev = -1;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) {
+    set_error("policy_step_noalloc: cudaGetDevice", e);
+    return ASHKV_LAUNCH_ERROR;
+  }
+  if (dev < 0 || dev >= kMaxDevices) return ASHKV_BAD_ARGUMENT;
+  std::lock_guard<std::mutex> lock(g_scratch_mu);
+  if (!g_scratch_ptr[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_policy_scratch);
+    if (e != cudaSuccess || !p) {
+      set_error("policy_step_noalloc: cudaGetSymbolAddress", e);
+      cudaGetLastError();
+      return ASHKV_LAUNCH_ERROR;
+    }
+    g_scratch_ptr[dev] = static_cast<int32_t*>(p);
+  }
+  *out = g_scratch_ptr[dev];
+  return ASHKV_OK;
+}
+
+}  // namespace
+}  // namespace ashkv
+
+extern "C" ashkv_status_t ashkv_policy_step_noalloc(
+    const float* d_T, const float* d_S, const float* d_N, const float* d_P, const int8_t* d_cur, int64_t n,
+    float w_T, float w_S, float w_N, float w_P, double pressure, double theta_high, double theta_low,
+    double delta, double p_emergency, const int8_t* next_colder, const int8_t* next_hotter,
+    float* d_R, int8_t* d_target, int32_t* d_demote_list, int32_t* d_promote_list, int32_t* d_counts,
+    void* stream) {
+  if (n > ASHKV_POLICY_NOALLOC_MAX_PAGES) {
+    set_message("policy_step_noalloc: the page table has more entries than the static scratch holds "
+                "(ASHKV_POLICY_NOALLOC_MAX_PAGES = 4194304); use ashkv_policy_step with caller scratch");
+    return ASHKV_BAD_ARGUMENT;
+  }
+  int32_t* scratch = nullptr;
+  const ashkv_status_t s = scratch_for_current_device(&scratch);
+  if (s != ASHKV_OK) return s;
+  return ashkv_policy_step(d_T, d_S, d_N, d_P, d_cur, n, w_T, w_S, w_N, w_P, pressure, theta_high, theta_low,
+                           delta, p_emergency, next_colder, next_hotter, d_R, d_target, d_demote_list,
+                           d_promote_list, d_counts, scratch, stream);
+}

@@ -255,6 +255,28 @@ ASHKV_API ashkv_status_t ashkv_int8_decode_pages(
     int64_t n_slots, int32_t* d_page_slot, int32_t free_slots, int32_t* d_free_stack, int32_t* d_free_top,
     int32_t* d_entry_status, void* stream);
 
+/* ========================================================================
+ * ashkv_policy_step without a scratch argument.  No counterpart in the
+ * reference: it exists for callers that cannot allocate device memory while
+ * they plan a step (an engine that has reserved nearly all HBM for its KV
+ * pool, or a plain C/FFI caller without a caching allocator).  The per-block
+ * counts live in a static 32 KiB device array inside the library, held by
+ * every GPU that loads it until the process exits, which limits the page
+ * table to ASHKV_POLICY_NOALLOC_MAX_PAGES entries (larger n returns
+ * ASHKV_BAD_ARGUMENT with a message in ashkv_last_error()).  The first call
+ * on each device looks up the array's device address (cudaGetSymbolAddress)
+ * with that device current; make that first call before any stream capture.
+ * All calls share the array: calls whose kernels overlap on the GPU race.
+ * The function allocates nothing.
+ * ======================================================================== */
+#define ASHKV_POLICY_NOALLOC_MAX_PAGES 4194304
+ASHKV_API ashkv_status_t ashkv_policy_step_noalloc(
+    const float* d_T, const float* d_S, const float* d_N, const float* d_P, const int8_t* d_cur, int64_t n,
+    float w_T, float w_S, float w_N, float w_P, double pressure, double theta_high, double theta_low,
+    double delta, double p_emergency, const int8_t* next_colder, const int8_t* next_hotter,
+    float* d_R, int8_t* d_target, int32_t* d_demote_list, int32_t* d_promote_list, int32_t* d_counts,
+    void* stream);
+
 #ifdef __cplusplus
 }
 #endif
