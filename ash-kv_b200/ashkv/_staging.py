@@ -8,7 +8,10 @@ buffer is never reused while a transfer that reads or writes it is in flight.
 """
 from __future__ import annotations
 
+import ctypes
+import os
 import threading
+from concurrent.futures import ThreadPoolExecutor
 
 import numpy as np
 import torch
@@ -43,3 +46,62 @@ def check_even(source_bytes: bytes) -> None:
     if len(source_bytes) % 2:
         raise ValueError(f"buffer length ({len(source_bytes)} bytes) after offset (0 bytes) "
                          f"must be a multiple of element size (2)")
+
+
+# ---------------------------------------------------------------- parallel host copies
+_CHUNK = 8 << 20          # split copies above this size across threads
+_POOL: ThreadPoolExecutor | None = None
+_POOL_LOCK = threading.Lock()
+
+_new_bytes = ctypes.pythonapi.PyBytes_FromStringAndSize
+_new_bytes.restype = ctypes.py_object
+_new_bytes.argtypes = [ctypes.c_void_p, ctypes.c_ssize_t]
+_bytes_ptr = ctypes.pythonapi.PyBytes_AsString
+_bytes_ptr.restype = ctypes.c_void_p
+_bytes_ptr.argtypes = [ctypes.py_object]
+
+
+def _pool() -> ThreadPoolExecutor:
+    global _POOL
+    if _POOL is None:
+        with _POOL_LOCK:
+            if _POOL is None:
+                _POOL = ThreadPoolExecutor(max_workers=min(16, os.cpu_count() or 1),
+                                           thread_name_prefix="ashkv-memcpy")
+    return _POOL
+
+
+def memcpy(dst: int, src: int, n: int) -> None:
+    """Host memcpy of n bytes; large copies are split over a thread pool
+    (ctypes.memmove releases the GIL)."""
+    if n <= _CHUNK:
+        ctypes.memmove(dst, src, n)
+        return
+    parts = min((n + _CHUNK - 1) // _CHUNK, 4 * (os.cpu_count() or 1))
+    step = (n + parts - 1) // parts
+    futs = [_pool().submit(ctypes.memmove, dst + o, src + o, min(step, n - o)) for o in range(0, n, step)]
+    for f in futs:
+        f.result()
+
+
+def bytes_address(b: bytes) -> int:
+    return _bytes_ptr(b)
+
+
+def fill_from(dst: torch.Tensor, src: bytes, offset: int = 0) -> None:
+    """Copy len(dst) bytes of ``src`` starting at ``offset`` into a CPU uint8 tensor."""
+    n = dst.numel()
+    if offset + n > len(src):
+        raise ValueError("source too short")
+    memcpy(dst.data_ptr(), bytes_address(src) + offset, n)
+
+
+def to_bytes(src: torch.Tensor, header: bytes = b"") -> bytes:
+    """A new ``bytes`` = header + the contents of a CPU uint8 tensor (one parallel copy)."""
+    n = src.numel()
+    out = _new_bytes(None, len(header) + n)  # uninitialised, not yet shared
+    base = bytes_address(out)
+    if header:
+        ctypes.memmove(base, header, len(header))
+    memcpy(base + len(header), src.data_ptr(), n)
+    return out

@@ -66,18 +66,16 @@ class INT8Codec:
         dev = _staging.device()
         n_in = num_tokens * L * 2
         h_in = _staging.pinned(n_in, "in")
-        h_in.numpy()[:] = np.frombuffer(source_bytes, dtype=np.uint8, count=n_in)
+        _staging.fill_from(h_in, source_bytes)
         d_in = torch.empty(n_in, dtype=torch.uint8, device=dev)
         d_in.copy_(h_in, non_blocking=True)
         codes, scales = encode_rows(d_in.view(torch.bfloat16).view(num_tokens, L))
         n_sc = 2 * num_tokens
-        total = 4 + n_sc + num_tokens * L
-        h_out = _staging.pinned(total, "out")
-        h_out.numpy()[:4] = np.frombuffer(struct.pack("<I", num_tokens), dtype=np.uint8)
-        h_out[4:4 + n_sc].copy_(scales.view(torch.uint8), non_blocking=True)
-        h_out[4 + n_sc:].copy_(codes.view(torch.uint8).view(-1), non_blocking=True)
+        h_out = _staging.pinned(n_sc + num_tokens * L, "out")
+        h_out[:n_sc].copy_(scales.view(torch.uint8), non_blocking=True)
+        h_out[n_sc:].copy_(codes.view(torch.uint8).view(-1), non_blocking=True)
         torch.cuda.current_stream(dev).synchronize()
-        return h_out.numpy().tobytes()
+        return _staging.to_bytes(h_out, struct.pack("<I", num_tokens))
 
     def decode(self, target_bytes: bytes) -> bytes:
         self._decode_calls += 1
@@ -93,7 +91,7 @@ class INT8Codec:
                                f"{L} elements")
         dev = _staging.device()
         h_in = _staging.pinned(n_sc + n_codes, "in")
-        h_in.numpy()[:] = np.frombuffer(target_bytes, dtype=np.uint8, count=n_sc + n_codes, offset=4)
+        _staging.fill_from(h_in, target_bytes, 4)
         d_sc = torch.empty(n_sc, dtype=torch.uint8, device=dev)
         d_codes = torch.empty(n_codes, dtype=torch.uint8, device=dev)
         d_sc.copy_(h_in[:n_sc], non_blocking=True)
@@ -102,7 +100,7 @@ class INT8Codec:
         h_out = _staging.pinned(n_codes * 2, "out")
         h_out.copy_(out.view(torch.uint8).view(-1), non_blocking=True)
         torch.cuda.current_stream(dev).synchronize()
-        return h_out.numpy().tobytes()
+        return _staging.to_bytes(h_out)
 
     def checksum(self, raw_bytes: bytes) -> int:
         return checksum(raw_bytes)

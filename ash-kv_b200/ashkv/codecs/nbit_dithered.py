@@ -163,7 +163,7 @@ class DitheredNBitCodec:
         dev = _staging.device()
         n_elems = num_tokens * L
         h_in = _staging.pinned(2 * n_elems, "in")
-        h_in.numpy()[:] = np.frombuffer(source_bytes, dtype=np.uint8, count=2 * n_elems)
+        _staging.fill_from(h_in, source_bytes)
         d_src = torch.empty(2 * n_elems, dtype=torch.uint8, device=dev)
         d_src.copy_(h_in, non_blocking=True)
         u = None
@@ -177,17 +177,16 @@ class DitheredNBitCodec:
         n_out = int(total.item())  # one sync: the blob layout depends on the outlier count
         n_groups = enc.n_groups
         n_codes = n_groups * 32 * self._bits // 8
-        size = 8 + 2 * n_groups + 6 * n_out + n_codes
+        size = 2 * n_groups + 6 * n_out + n_codes
         h_out = _staging.pinned(size, "out")
-        h_out.numpy()[:8] = np.frombuffer(struct.pack("<II", num_tokens, n_out), dtype=np.uint8)
-        o = 8
+        o = 0
         h_out[o:o + 2 * n_groups].copy_(enc.scales.view(torch.uint8), non_blocking=True); o += 2 * n_groups
         if n_out:
             h_out[o:o + 4 * n_out].copy_(idx[:n_out].view(torch.uint8), non_blocking=True); o += 4 * n_out
             h_out[o:o + 2 * n_out].copy_(val[:n_out].view(torch.uint8), non_blocking=True); o += 2 * n_out
         h_out[o:o + n_codes].copy_(enc.codes[:n_codes], non_blocking=True)
         torch.cuda.current_stream(dev).synchronize()
-        return h_out.numpy().tobytes()
+        return _staging.to_bytes(h_out, struct.pack("<II", num_tokens, n_out))
 
     def decode(self, target_bytes: bytes) -> bytes:
         self._decode_calls += 1
@@ -205,7 +204,7 @@ class DitheredNBitCodec:
         dev = _staging.device()
         body = len(target_bytes) - 8
         h_in = _staging.pinned(body, "in")
-        h_in.numpy()[:] = np.frombuffer(target_bytes, dtype=np.uint8, offset=8)
+        _staging.fill_from(h_in, target_bytes, 8)
         d_sc = torch.empty(2 * n_groups, dtype=torch.uint8, device=dev)
         d_idx = torch.empty(max(4 * n_out, 4), dtype=torch.uint8, device=dev)
         d_val = torch.empty(max(2 * n_out, 2), dtype=torch.uint8, device=dev)
@@ -227,4 +226,4 @@ class DitheredNBitCodec:
         torch.cuda.current_stream(dev).synchronize()
         if int(st.item()) & _native.FLAG_INDEX_RANGE:
             raise IndexError(f"outlier index out of range for a decoded size of {n_groups * 32} elements")
-        return h_out.numpy().tobytes()
+        return _staging.to_bytes(h_out)
