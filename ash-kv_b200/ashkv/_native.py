@@ -56,6 +56,11 @@ SIGNATURES: dict[str, tuple] = {
                                        _I32, _P, _P, _P, _P]),
     "ashkv_policy_step": (_I32, [_P, _P, _P, _P, _P, _I64, _F32, _F32, _F32, _F32, _F64, _F64, _F64, _F64,
                                  _F64, _P, _P, _P, _P, _P, _P, _P, _P, _P]),
+    "ashkv_fp8_encode": (_I32, [_P, _I64, _P, _P]),
+    "ashkv_fp8_decode": (_I32, [_P, _I64, _P, _P]),
+    "ashkv_int4_group_count": (_I64, [_I64, _I32]),
+    "ashkv_int4_encode": (_I32, [_P, _I64, _I32, _P, _P, _P]),
+    "ashkv_int4_decode": (_I32, [_P, _P, _I64, _I32, _P, _P]),
 }
 
 
@@ -239,6 +244,66 @@ def xxh64_items(data: torch.Tensor, n_items: int, item_bytes: int, item_stride: 
         raise ValueError("xxh64_items: out must hold n_items 64-bit values")
     check(lib().ashkv_xxh64_items(data.data_ptr(), n_items, item_bytes, item_stride, seed & ((1 << 64) - 1),
                                   out.data_ptr(), stream_handle(data.device)), "xxh64_items")
+
+
+# --------------------------------------------------------------------------- FP8 / INT4
+def _byte_view(t: torch.Tensor) -> torch.Tensor:
+    if not t.is_contiguous():
+        raise ValueError("ashkv codec buffers must be contiguous")
+    return t
+
+
+def fp8_encode(src: torch.Tensor, dst: torch.Tensor) -> None:
+    """bf16 elements of ``src`` -> float8_e4m3fn bytes in ``dst`` (uint8 or float8_e4m3fn)."""
+    _require_cuda(src, dst)
+    _byte_view(src), _byte_view(dst)
+    if src.dtype != torch.bfloat16:
+        raise TypeError("fp8_encode takes bfloat16 input")
+    n = src.numel()
+    if dst.numel() * dst.element_size() < n:
+        raise ValueError("fp8_encode: dst too small")
+    check(lib().ashkv_fp8_encode(src.data_ptr(), n, dst.data_ptr(), stream_handle(src.device)), "fp8_encode")
+
+
+def fp8_decode(src: torch.Tensor, dst: torch.Tensor) -> None:
+    """float8_e4m3fn bytes of ``src`` -> bf16 elements of ``dst``."""
+    _require_cuda(src, dst)
+    _byte_view(src), _byte_view(dst)
+    n = src.numel() * src.element_size()
+    if dst.dtype != torch.bfloat16 or dst.numel() < n:
+        raise ValueError("fp8_decode: dst must be bfloat16 with one element per code")
+    check(lib().ashkv_fp8_decode(src.data_ptr(), n, dst.data_ptr(), stream_handle(src.device)), "fp8_decode")
+
+
+def int4_group_count(n: int, group_size: int) -> int:
+    return int(lib().ashkv_int4_group_count(n, group_size))
+
+
+def int4_encode(src: torch.Tensor, group_size: int, scales: torch.Tensor, packed: torch.Tensor) -> None:
+    """bf16 ``src`` (n elements, zero-padded to whole groups) -> bf16 ``scales`` + packed nibbles."""
+    _require_cuda(src, scales, packed)
+    _byte_view(src), _byte_view(scales), _byte_view(packed)
+    if src.dtype != torch.bfloat16:
+        raise TypeError("int4_encode takes bfloat16 input")
+    n = src.numel()
+    n_groups = -(-n // group_size) if group_size > 0 else 0
+    if scales.numel() * scales.element_size() < 2 * n_groups or \
+            packed.numel() * packed.element_size() < n_groups * group_size // 2:
+        raise ValueError("int4_encode: output buffers too small")
+    check(lib().ashkv_int4_encode(src.data_ptr(), n, group_size, scales.data_ptr(), packed.data_ptr(),
+                                  stream_handle(src.device)), "int4_encode")
+
+
+def int4_decode(scales: torch.Tensor, packed: torch.Tensor, n_groups: int, group_size: int,
+                dst: torch.Tensor) -> None:
+    _require_cuda(scales, packed, dst)
+    _byte_view(scales), _byte_view(packed), _byte_view(dst)
+    total = n_groups * group_size
+    if dst.dtype != torch.bfloat16 or dst.numel() < total or \
+            packed.numel() * packed.element_size() < total // 2 or scales.numel() * scales.element_size() < 2 * n_groups:
+        raise ValueError("int4_decode: buffer sizes do not match n_groups * group_size")
+    check(lib().ashkv_int4_decode(scales.data_ptr(), packed.data_ptr(), n_groups, group_size, dst.data_ptr(),
+                                  stream_handle(dst.device)), "int4_decode")
 
 
 # --------------------------------------------------------------------------- policy

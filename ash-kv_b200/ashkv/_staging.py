@@ -105,3 +105,29 @@ def to_bytes(src: torch.Tensor, header: bytes = b"") -> bytes:
         ctypes.memmove(base, header, len(header))
     memcpy(base + len(header), src.data_ptr(), n)
     return out
+
+
+def upload(src: bytes, offset: int, nbytes: int, dev: torch.device, slot: str = "in") -> torch.Tensor:
+    """``src[offset:offset+nbytes]`` as a new uint8 CUDA tensor (through the pinned buffer)."""
+    h = pinned(nbytes, slot)
+    fill_from(h, src, offset)
+    d = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=dev)[:nbytes]
+    d.copy_(h, non_blocking=True)
+    return d
+
+
+def download(parts, header: bytes = b"", slot: str = "out") -> bytes:
+    """header + the bytes of the given CUDA tensors, in order, as one ``bytes``.
+
+    Synchronises the current stream (the pinned buffer is reused by the next call)."""
+    parts = [p.reshape(-1).view(torch.uint8) for p in parts]
+    total = sum(p.numel() for p in parts)
+    h = pinned(total, slot)
+    o = 0
+    for p in parts:
+        if p.numel():
+            h[o:o + p.numel()].copy_(p, non_blocking=True)
+            o += p.numel()
+    dev = parts[0].device if parts else device()
+    torch.cuda.current_stream(dev).synchronize()
+    return to_bytes(h, header)

@@ -9,14 +9,18 @@ from __future__ import annotations
 from ..compiler.registry import codec_registry
 from .bf16 import BF16Codec
 from .checksum import checksum, checksum_pages, checksum_pair
+from .fp8 import FP8Codec
 from .int2_dithered import DitheredINT2Codec
+from .int4 import INT4Codec
 from .int8 import INT8Codec
 from .nbit_dithered import DitheredNBitCodec
 
 codec_registry.register("bf16", BF16Codec())
 codec_registry.register("int8_default", INT8Codec())
+codec_registry.register("int4_default", INT4Codec())
 codec_registry.register("int2_dithered", DitheredINT2Codec())
 codec_registry.register("nbit_dithered", DitheredNBitCodec())
+codec_registry.register("fp8_default", FP8Codec())
 
-__all__ = ["BF16Codec", "INT8Codec", "DitheredINT2Codec", "DitheredNBitCodec", "checksum", "checksum_pair",
-           "checksum_pages"]
+__all__ = ["BF16Codec", "FP8Codec", "INT8Codec", "INT4Codec", "DitheredINT2Codec", "DitheredNBitCodec",
+           "checksum", "checksum_pair", "checksum_pages"]

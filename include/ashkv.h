@@ -277,6 +277,37 @@ ASHKV_API ashkv_status_t ashkv_policy_step_noalloc(
     float* d_R, int8_t* d_target, int32_t* d_demote_list, int32_t* d_promote_list, int32_t* d_counts,
     void* stream);
 
+/* ========================================================================
+ * FP8 codec: bf16 <-> float8_e4m3fn, one byte per element.
+ * Replaces FP8Codec (ashkv/codecs/fp8.py:32-79), i.e. torch's casts
+ * tensor.to(torch.float8_e4m3fn) and view(float8_e4m3fn).to(bfloat16):
+ *   encode: round to nearest even, no saturation -- |x| > 464, inf and NaN
+ *           give 0x7F | sign (E4M3FN's NaN);
+ *   decode: exact; NaN codes give bf16 0x7FFF (torch's CUDA cast).
+ * n elements; any alignment (16/32-byte aligned buffers take the vector path).
+ * ======================================================================== */
+ASHKV_API ashkv_status_t ashkv_fp8_encode(const void* d_src_bf16, int64_t n, void* d_dst_fp8, void* stream);
+ASHKV_API ashkv_status_t ashkv_fp8_decode(const void* d_src_fp8, int64_t n, void* d_dst_bf16, void* stream);
+
+/* ========================================================================
+ * INT4 group codec.  Replaces INT4Codec (ashkv/codecs/int4.py:38-112),
+ * which the reference runs in numpy on the host.  The n bf16 inputs are
+ * zero-padded to n_groups = ceil(n / group_size) groups; per group
+ *   am = maximum(max|x|, 1e-8) (NaN propagates), scale = bf16(am),
+ *   q  = clip(int8(round_half_even(x*7/am)), -8, 7)  (numpy's x86 int8 cast:
+ *        NaN / inf give 0), stored as q + 8, even element in the high nibble;
+ * decode: bf16(float(q) * float(scale) / 7).  Every NaN written as bf16 is
+ * 0xFFFF (torch's CPU cast, where the reference computes).
+ * d_scales: n_groups bf16; d_packed: n_groups * group_size / 2 bytes (the
+ * padded count must be even, else ASHKV_BAD_ARGUMENT); d_dst: n_groups *
+ * group_size bf16.  ashkv_int4_group_count(n, group_size) = n_groups.
+ * ======================================================================== */
+ASHKV_API int64_t ashkv_int4_group_count(int64_t n, int32_t group_size);
+ASHKV_API ashkv_status_t ashkv_int4_encode(const void* d_src_bf16, int64_t n, int32_t group_size,
+                                           void* d_scales_bf16, void* d_packed, void* stream);
+ASHKV_API ashkv_status_t ashkv_int4_decode(const void* d_scales_bf16, const void* d_packed, int64_t n_groups,
+                                           int32_t group_size, void* d_dst_bf16, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

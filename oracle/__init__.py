@@ -22,6 +22,8 @@ Restated reference functions (paths relative to the ASH-KV source tree):
 * ``score``                           — ``ashkv/runtime/score.py:15-52``
 * ``desired_tiers``                   — ``ashkv/runtime/controller.py:32-106``
 * ``controller_tables``               — ``ashkv/compiler/runtime_builder.py:91-109``
+* ``fp8_encode`` / ``fp8_decode``     — ``ashkv/codecs/fp8.py:32-79``
+* ``int4_encode`` / ``int4_decode`` / ``int4_blob`` — ``ashkv/codecs/int4.py:38-112``
 """
 from __future__ import annotations
 
@@ -54,6 +56,11 @@ def lib() -> ctypes.CDLL:
         L.oracle_philox_dither.argtypes = [i64, u64, u64, P]
         L.oracle_f32_to_bf16.argtypes = [f32]
         L.oracle_f32_to_bf16.restype = ctypes.c_uint16
+        u16 = ctypes.c_uint16
+        L.oracle_fp8_encode.argtypes = [P, i64, P]
+        L.oracle_fp8_decode.argtypes = [P, i64, u16, P]
+        L.oracle_int4_encode.argtypes = [P, i64, i32, i64, u16, P, P]
+        L.oracle_int4_decode.argtypes = [P, P, i64, i32, u16, P]
         _LIB = L
     return _LIB
 
@@ -244,3 +251,57 @@ def controller_tables(codec_keys) -> tuple[np.ndarray, np.ndarray]:
         if hotter:
             nh[src] = max(hotter)
     return nc, nh
+
+
+# --------------------------------------------------------------------- FP8
+FP8_NAN_BF16_CUDA = 0x7FFF   # torch's CUDA float8 -> bf16 cast writes NaN as 0x7FFF
+INT4_NAN_BF16_CPU = 0xFFFF   # torch's vectorised CPU float32 -> bf16 cast writes NaN as 0xFFFF
+
+
+def fp8_encode(x_bits: np.ndarray) -> np.ndarray:
+    """bf16 bits -> float8_e4m3fn bytes (torch's non-saturating cast)."""
+    x = np.ascontiguousarray(x_bits, dtype=np.uint16).reshape(-1)
+    out = np.empty(x.size, dtype=np.uint8)
+    if x.size:
+        lib().oracle_fp8_encode(_p(x), x.size, _p(out))
+    return out
+
+
+def fp8_decode(codes: np.ndarray, nan_bits: int = FP8_NAN_BF16_CUDA) -> np.ndarray:
+    """float8_e4m3fn bytes -> bf16 bits."""
+    c = np.ascontiguousarray(codes, dtype=np.uint8).reshape(-1)
+    out = np.empty(c.size, dtype=np.uint16)
+    if c.size:
+        lib().oracle_fp8_decode(_p(c), c.size, nan_bits, _p(out))
+    return out
+
+
+# --------------------------------------------------------------------- INT4
+def int4_encode(x_bits: np.ndarray, group_size: int = 64,
+                nan_bits: int = INT4_NAN_BF16_CPU) -> tuple[np.ndarray, np.ndarray, int]:
+    """bf16 bits -> (bf16 scale bits [n_groups], packed nibbles, num_values)."""
+    x = np.ascontiguousarray(x_bits, dtype=np.uint16).reshape(-1)
+    n_groups = -(-x.size // group_size)
+    total = n_groups * group_size
+    if total % 2:
+        raise ValueError("padded value count must be even")
+    scales = np.empty(n_groups, dtype=np.uint16)
+    packed = np.empty(total // 2, dtype=np.uint8)
+    if n_groups:
+        lib().oracle_int4_encode(_p(x), x.size, group_size, n_groups, nan_bits, _p(scales), _p(packed))
+    return scales, packed, total
+
+
+def int4_decode(scales: np.ndarray, packed: np.ndarray, group_size: int = 64,
+                nan_bits: int = INT4_NAN_BF16_CPU) -> np.ndarray:
+    s = np.ascontiguousarray(scales, dtype=np.uint16).reshape(-1)
+    p = np.ascontiguousarray(packed, dtype=np.uint8).reshape(-1)
+    out = np.empty(s.size * group_size, dtype=np.uint16)
+    if out.size:
+        lib().oracle_int4_decode(_p(s), _p(p), s.size, group_size, nan_bits, _p(out))
+    return out
+
+
+def int4_blob(scales: np.ndarray, packed: np.ndarray, num_values: int) -> bytes:
+    """INT4Codec blob (int4.py:74-75): <II num_groups, num_values> + bf16 scales + packed."""
+    return struct.pack("<II", scales.size, num_values) + scales.astype(np.uint16).tobytes() + packed.tobytes()

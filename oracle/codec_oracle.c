@@ -17,6 +17,8 @@
  *   oracle_xxh64                   ashkv/codecs/checksum.py:26-37 (xxhash.xxh64,
  *                                  public XXH64 specification)
  *   oracle_philox4x32_10           Salmon et al., SC'11 (the production dither source)
+ *   oracle_fp8_encode / _decode    ashkv/codecs/fp8.py:32-79 (torch float8_e4m3fn casts)
+ *   oracle_int4_encode / _decode   ashkv/codecs/int4.py:38-112
  */
 #include <math.h>
 #include <stdint.h>
@@ -293,5 +295,106 @@ void oracle_philox_dither(int64_t n, uint64_t seed, uint64_t offset, float* out)
     const int f = (int)(e & 7u);
     const uint32_t h = (r[f >> 1] >> (16 * (f & 1))) & 0xFFFFu;
     out[i] = (float)h * (1.0f / 65536.0f);
+  }
+}
+
+/* ------------------------------------------------------------ FP8 (E4M3FN) codec */
+/* bf16 -> float8_e4m3fn as torch's cast computes it (ashkv/codecs/fp8.py:51-60
+ * calls tensor.to(torch.float8_e4m3fn)): round to nearest even over the
+ * E4M3FN grid (bias 7, subnormal step 2^-9, largest finite 448), with NO
+ * saturation: a magnitude that rounds past 448 (> 464), an infinity or a NaN
+ * becomes the NaN code 0x7F with the input's sign. */
+static uint8_t fp8_from_f32(float f) {
+  const uint8_t sign = (f32_to_bits(f) >> 24) & 0x80u;
+  const float a = fabsf(f);
+  if (!(a <= 464.0f)) return (uint8_t)(sign | 0x7Fu);
+  if (a < 0x1p-6f) /* subnormal range: multiples of 2^-9 (8 rounds up to the smallest normal) */
+    return (uint8_t)(sign | (uint8_t)nearbyintf(a * 512.0f));
+  int e;
+  frexpf(a, &e);                                  /* a = m * 2^e, m in [0.5, 1) */
+  e -= 1;                                         /* a = 1.f * 2^e, e in [-6, 8] */
+  const int steps = (int)nearbyintf(ldexpf(a, 3 - e)); /* 8..16 eighths of 2^e */
+  return (uint8_t)(sign | (((e + 7) << 3) + steps - 8)); /* 16 carries into the exponent */
+}
+
+void oracle_fp8_encode(const uint16_t* src, int64_t n, uint8_t* dst) {
+  for (int64_t i = 0; i < n; ++i) dst[i] = fp8_from_f32(bf16_to_f32(src[i]));
+}
+
+/* float8_e4m3fn -> bf16 (fp8.py:71-79: view(float8_e4m3fn).to(bfloat16)).
+ * Every finite E4M3FN value is exact in bf16; NaN codes (0x7F, 0xFF) become
+ * `nan_bits` (0x7FFF from torch's CUDA cast, which the reference uses
+ * whenever a GPU is present). */
+void oracle_fp8_decode(const uint8_t* src, int64_t n, uint16_t nan_bits, uint16_t* dst) {
+  for (int64_t i = 0; i < n; ++i) {
+    const uint8_t c = src[i];
+    const int e = (c >> 3) & 15, m = c & 7;
+    if (e == 15 && m == 7) { dst[i] = nan_bits; continue; }
+    const float mag = e == 0 ? ldexpf((float)m, -9) : ldexpf((float)(8 + m), e - 10);
+    dst[i] = oracle_f32_to_bf16((c & 0x80) ? -mag : mag);
+  }
+}
+
+/* ------------------------------------------------------------ INT4 group codec */
+/* numpy's float32 -> int8 cast on x86 (the cast ashkv/codecs/int4.py:61
+ * applies after np.round): truncate to int32 (NaN, infinities and values
+ * outside int32 give INT32_MIN) and keep the low byte. */
+static int8_t np_f32_to_i8(float r) {
+  int32_t v = INT32_MIN;
+  if (r > -2147483648.0f && r < 2147483648.0f) v = (int32_t)r;
+  return (int8_t)(uint8_t)(uint32_t)v;
+}
+
+/* torch CPU float32 -> bf16 (int4.py:72, :112): round to nearest even, every
+ * NaN written as `nan_bits` (0xFFFF from torch's vectorised CPU cast). */
+static uint16_t bf16_cpu(float f, uint16_t nan_bits) {
+  return isnan(f) ? nan_bits : oracle_f32_to_bf16(f);
+}
+
+/* INT4Codec.encode (int4.py:38-75) over n bf16 values zero-padded to
+ * n_groups * group_size: am = maximum(max|x|, 1e-8) with NaN propagating
+ * (np.max / np.maximum), q = clip(int8(round_half_even(x*7/am)), -8, 7),
+ * nibble = q + 8, high nibble = even element; scale = bf16(am).
+ * packed holds n_groups*group_size/2 bytes (the caller checks evenness). */
+void oracle_int4_encode(const uint16_t* src, int64_t n, int32_t group_size, int64_t n_groups,
+                        uint16_t nan_bits, uint16_t* scales, uint8_t* packed) {
+  const int64_t total = n_groups * group_size;
+  for (int64_t i = 0; i < total / 2; ++i) packed[i] = 0;
+  for (int64_t g = 0; g < n_groups; ++g) {
+    float am = 0.0f;
+    int nan_seen = 0;
+    for (int32_t k = 0; k < group_size; ++k) {
+      const int64_t i = g * group_size + k;
+      const float x = i < n ? bf16_to_f32(src[i]) : 0.0f;
+      if (isnan(x)) nan_seen = 1;
+      else if (fabsf(x) > am) am = fabsf(x);
+    }
+    if (nan_seen) am = NAN;
+    else if (am < 1e-8f) am = 1e-8f;
+    scales[g] = bf16_cpu(am, nan_bits);
+    for (int32_t k = 0; k < group_size; ++k) {
+      const int64_t i = g * group_size + k;
+      const float x = i < n ? bf16_to_f32(src[i]) : 0.0f;
+      const float prod = x * 7.0f;
+      const float v = prod / am;
+      int q = np_f32_to_i8(nearbyintf(v));
+      if (q < -8) q = -8;
+      if (q > 7) q = 7;
+      const uint8_t nib = (uint8_t)(q + 8) & 15u;
+      if ((i & 1) == 0) packed[i >> 1] |= (uint8_t)(nib << 4);
+      else packed[i >> 1] |= nib;
+    }
+  }
+}
+
+/* INT4Codec.decode (int4.py:77-112): out = bf16(float(nibble - 8) * float(scale) / 7). */
+void oracle_int4_decode(const uint16_t* scales, const uint8_t* packed, int64_t n_groups, int32_t group_size,
+                        uint16_t nan_bits, uint16_t* dst) {
+  const int64_t total = n_groups * group_size;
+  for (int64_t i = 0; i < total; ++i) {
+    const uint8_t b = packed[i >> 1];
+    const int q = ((i & 1) == 0 ? (b >> 4) : (b & 15)) - 8;
+    const float p = (float)q * bf16_to_f32(scales[i / group_size]);
+    dst[i] = bf16_cpu(p / 7.0f, nan_bits);
   }
 }

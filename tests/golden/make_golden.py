@@ -21,6 +21,11 @@ script must not import this repository's own ``ashkv``.  It produces:
   compiled by ``compile_controller``.
 * ``xxh64.npz``  — ``ashkv.codecs.checksum.checksum`` (xxhash 3.x XXH64,
   seed 0) over seeded byte strings of many lengths.
+* ``fp8_int4.npz`` — ``FP8Codec`` over all 65,536 bf16 bit patterns and all
+  256 codes (torch's CPU casts; the same conversion function torch runs on
+  CUDA, except that CUDA writes a NaN bf16 as 0x7FFF), and ``INT4Codec``
+  encode/decode blobs for seeded inputs, group sizes 7..128, special values,
+  and decode of random blobs.
 
 Inputs are seeded synthetic data; the script is deterministic.
 """
@@ -245,6 +250,72 @@ def make_xxh64(out: dict) -> None:
     out["xxh64_digest"] = np.array(digests, dtype=np.uint64)
 
 
+def make_fp8_int4(out: dict) -> None:
+    import torch
+    from ashkv.codecs.fp8 import FP8Codec
+    from ashkv.codecs.int4 import INT4Codec
+
+    assert not torch.cuda.is_available()
+    allb = np.arange(65536, dtype=np.uint16)
+    fp8 = FP8Codec()
+    out["fp8_encode_all"] = np.frombuffer(fp8.encode(allb.tobytes()), np.uint8).copy()
+    out["fp8_decode_all"] = np.frombuffer(fp8.decode(np.arange(256, dtype=np.uint8).tobytes()), np.uint16).copy()
+
+    rng = np.random.default_rng(404)
+    g = torch.Generator().manual_seed(404)
+    cases = []
+    cases.append((64, np.random.RandomState(42).randn(64 * 10).astype(np.float16).view(np.uint16)))
+    cases.append((64, _bf16_bits(torch.randn(1000, generator=g) * 10)))
+    cases.append((32, _bf16_bits(torch.randn(4096, generator=g))))
+    x = torch.randn(8192, generator=g)
+    x[torch.randint(0, 8192, (40,), generator=g)] *= 50
+    cases.append((128, _bf16_bits(x)))
+    cases.append((8, _bf16_bits(torch.randn(1024, generator=g) * 0.01)))
+    cases.append((24, _bf16_bits(torch.randn(500, generator=g))))
+    cases.append((7, _bf16_bits(torch.randn(70, generator=g))))
+    cases.append((16, _bf16_bits(torch.randn(3, generator=g))))
+    special = torch.zeros(16 * 10)
+    special[0:16] = torch.randn(16, generator=g); special[3] = float("nan")
+    special[16:32] = torch.randn(16, generator=g); special[20] = float("inf")
+    special[32:48] = torch.randn(16, generator=g); special[40] = float("-inf")
+    special[48:64] = torch.randn(16, generator=g) * 1e37; special[50] = 3.0e38; special[51] = -2.0e38
+    special[64:80] = torch.randn(16, generator=g) * 1e-9
+    special[80:96] = torch.tensor([7.0, 0.5, 1.5, 2.5, -0.5, -1.5, -2.5, 3.5, -3.5, 4.5, 5.5, -6.5, 6.5, 0.0,
+                                   -0.0, -7.0])
+    special[96:112] = torch.randn(16, generator=g) * 1e-39
+    special[112:128] = -torch.rand(16, generator=g)
+    special[128:144] = torch.full((16,), 1e-8)
+    special[144:160] = torch.randn(16, generator=g) * 1e30
+    cases.append((16, _bf16_bits(special)))
+    raw = rng.integers(0, 65536, 4096, dtype=np.uint16)
+    raw[(raw & 0x7F80) == 0x7F80] &= 0xBFFF   # keep most groups finite; a few NaN/inf remain below
+    raw[[5, 700, 2100]] = [0x7FC1, 0x7F80, 0xFF80]
+    cases.append((64, raw))
+    blobs, inputs, gsz, decoded = [], [], [], []
+    for gs, bits in cases:
+        codec = INT4Codec(group_size=gs)
+        blob = codec.encode(bits.astype(np.uint16).tobytes())
+        inputs.append(bits.astype(np.uint16))
+        blobs.append(np.frombuffer(blob, np.uint8).copy())
+        decoded.append(np.frombuffer(codec.decode(blob), np.uint16).copy())
+        gsz.append(gs)
+    for i in range(len(cases)):
+        out[f"int4_in_{i}"] = inputs[i]
+        out[f"int4_blob_{i}"] = blobs[i]
+        out[f"int4_dec_{i}"] = decoded[i]
+    out["int4_group_size"] = np.array(gsz, dtype=np.int64)
+    # decode of random blobs: scales over the whole bf16 range, random nibbles
+    n_groups, gs = 256, 64
+    sc = rng.integers(0, 65536, n_groups, dtype=np.uint16)
+    sc[:4] = [0x7F80, 0xFF80, 0x7FC0, 0x0001]
+    packed = rng.integers(0, 256, n_groups * gs // 2, dtype=np.uint8)
+    import struct
+    blob = struct.pack("<II", n_groups, n_groups * gs) + sc.tobytes() + packed.tobytes()
+    out["int4_rand_blob"] = np.frombuffer(blob, np.uint8).copy()
+    out["int4_rand_dec"] = np.frombuffer(INT4Codec(group_size=gs).decode(blob), np.uint16).copy()
+    out["int4_empty_blob"] = np.frombuffer(INT4Codec().encode(b""), np.uint8).copy()
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default="/root/reference")
@@ -256,7 +327,8 @@ def main() -> None:
     assert Path(ashkv.__file__).resolve().is_relative_to(Path(args.reference).resolve()), ashkv.__file__
 
     outdir = Path(args.out)
-    for name, fn in (("nbit", make_nbit), ("int8", make_int8), ("policy", make_policy), ("xxh64", make_xxh64)):
+    for name, fn in (("nbit", make_nbit), ("int8", make_int8), ("policy", make_policy), ("xxh64", make_xxh64),
+                     ("fp8_int4", make_fp8_int4)):
         d: dict = {}
         fn(d)
         np.savez_compressed(outdir / f"{name}.npz", **d)

@@ -240,6 +240,21 @@ def test_registry_freeze_and_duplicates():
     assert r.get("a") is not None and r.get("zzz") is None and r.names == ("a",) and r.frozen
 
 
+def test_default_registry_has_the_reference_codec_names():
+    """ashkv/codecs/__init__.py:26-32 of the reference registers these six names."""
+    from ashkv.codecs import (BF16Codec, DitheredINT2Codec, DitheredNBitCodec, FP8Codec, INT4Codec,
+                              INT8Codec)
+    from ashkv.compiler.registry import codec_registry
+    expect = {"bf16": BF16Codec, "int8_default": INT8Codec, "int4_default": INT4Codec,
+              "int2_dithered": DitheredINT2Codec, "nbit_dithered": DitheredNBitCodec, "fp8_default": FP8Codec}
+    for name, cls in expect.items():
+        assert isinstance(codec_registry.get(name), cls), name
+    # empty inputs never touch the device
+    assert FP8Codec().encode(b"") == b"" and FP8Codec().decode(b"") == b""
+    assert INT4Codec().encode(b"") == b"\0\0\0\0" and INT4Codec().decode(b"\0\0\0\0") == b""
+    assert INT4Codec().decode(bytes(8)) == b""
+
+
 def test_circuit_breaker_trip_and_cooldown():
     b = CircuitBreaker(threshold=3, window_seconds=60, cooldown_seconds=0.05)
     for _ in range(2):

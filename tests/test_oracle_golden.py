@@ -17,6 +17,7 @@ NBIT = np.load(GOLDEN / "nbit.npz")
 INT8 = np.load(GOLDEN / "int8.npz")
 POLICY = np.load(GOLDEN / "policy.npz")
 XXH = np.load(GOLDEN / "xxh64.npz")
+F84 = np.load(GOLDEN / "fp8_int4.npz")
 
 
 @pytest.mark.parametrize("ci", range(int(NBIT["nbit_n_cases"])))
@@ -128,3 +129,46 @@ def test_outlier_bound_holds_on_adversarial_groups():
         if idx.size:
             worst = max(worst, np.bincount(idx // 32).max())
     assert worst <= oracle.max_outliers_per_group(3.0)
+
+
+def test_fp8_oracle_matches_reference_on_every_bf16_pattern():
+    allb = np.arange(65536, dtype=np.uint16)
+    np.testing.assert_array_equal(oracle.fp8_encode(allb), F84["fp8_encode_all"])
+
+
+def test_fp8_decode_oracle_matches_reference_on_every_code():
+    dec = oracle.fp8_decode(np.arange(256, dtype=np.uint8))
+    ref = F84["fp8_decode_all"]
+    nan = np.array([0x7F, 0xFF])
+    finite = np.setdiff1d(np.arange(256), nan)
+    np.testing.assert_array_equal(dec[finite], ref[finite])
+    # The fixture comes from torch's CPU cast (NaN -> 0x7FC0); the reference runs
+    # the cast on CUDA when a GPU is present, which writes 0x7FFF.
+    assert set(ref[nan].tolist()) == {0x7FC0}
+    assert set(dec[nan].tolist()) == {oracle.FP8_NAN_BF16_CUDA}
+    assert set(oracle.fp8_decode(nan.astype(np.uint8), nan_bits=0x7FC0).tolist()) == {0x7FC0}
+
+
+@pytest.mark.parametrize("ci", range(len(F84["int4_group_size"])))
+def test_int4_oracle_matches_reference_blob(ci):
+    gs = int(F84["int4_group_size"][ci])
+    x = F84[f"int4_in_{ci}"]
+    scales, packed, total = oracle.int4_encode(x, gs)
+    blob = oracle.int4_blob(scales, packed, total)
+    assert blob == F84[f"int4_blob_{ci}"].tobytes()
+    np.testing.assert_array_equal(oracle.int4_decode(scales, packed, gs), F84[f"int4_dec_{ci}"])
+
+
+def test_int4_oracle_decodes_random_reference_blobs():
+    blob = F84["int4_rand_blob"].tobytes()
+    n_groups, n_values = np.frombuffer(blob[:8], np.uint32)
+    sc = np.frombuffer(blob[8:8 + 2 * n_groups], np.uint16)
+    packed = np.frombuffer(blob[8 + 2 * n_groups:], np.uint8)
+    np.testing.assert_array_equal(oracle.int4_decode(sc, packed, int(n_values // n_groups)), F84["int4_rand_dec"])
+
+
+def test_int4_golden_covers_special_values():
+    specials = [ci for ci in range(len(F84["int4_group_size"]))
+                if np.any((F84[f"int4_in_{ci}"] & 0x7F80) == 0x7F80)]
+    assert specials, "no NaN/inf case in the INT4 fixture"
+    assert F84["int4_empty_blob"].tobytes() == b"\0\0\0\0"
