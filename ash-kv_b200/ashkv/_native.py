@@ -24,8 +24,8 @@ DTYPE_BF16, DTYPE_FP16 = 0, 1
 DITHER_TENSOR, DITHER_PHILOX = 0, 1
 INT8_FP32_PRODUCT = 0x1
 NBIT_GROUP = 32
-NBIT_BUCKET_GROUPS = 256
-NBIT_BUCKET_ELEMS = 8192
+NBIT_BUCKET_GROUPS = 32
+NBIT_BUCKET_ELEMS = 1024
 
 # name -> (restype, argtypes)
 _P, _I32, _I64, _U32, _U64, _F32, _F64 = (ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64, ctypes.c_uint32,
@@ -59,6 +59,7 @@ SIGNATURES: dict[str, tuple] = {
     "ashkv_fp8_encode": (_I32, [_P, _I64, _P, _P]),
     "ashkv_fp8_decode": (_I32, [_P, _I64, _P, _P]),
     "ashkv_int4_group_count": (_I64, [_I64, _I32]),
+    "ashkv_nbit_flatten_scratch_ints": (_I64, [_I64]),
     "ashkv_int4_encode": (_I32, [_P, _I64, _I32, _P, _P, _P]),
     "ashkv_int4_decode": (_I32, [_P, _P, _I64, _I32, _P, _P]),
 }
@@ -212,12 +213,16 @@ def nbit_decode(scales: torch.Tensor, codes: torch.Tensor, n_groups: int, bits: 
         bucket_cap, dst.data_ptr(), status.data_ptr(), stream_handle(dst.device)), "nbit_decode")
 
 
+def nbit_flatten_scratch_ints(n_buckets: int) -> int:
+    return int(lib().ashkv_nbit_flatten_scratch_ints(n_buckets))
+
+
 def nbit_outliers_flatten(bucket_counts: torch.Tensor, bucket_entries: torch.Tensor, bucket_cap: int,
                           n_buckets: int, offsets: torch.Tensor, out_index: torch.Tensor,
                           out_value: torch.Tensor, total: torch.Tensor) -> None:
     _require_cuda(bucket_counts, bucket_entries, offsets, out_index, out_value, total)
-    if offsets.numel() < n_buckets + 1:
-        raise ValueError("nbit_outliers_flatten: offsets needs n_buckets + 1 entries")
+    if offsets.numel() < nbit_flatten_scratch_ints(n_buckets):
+        raise ValueError("nbit_outliers_flatten: offsets needs nbit_flatten_scratch_ints(n_buckets) entries")
     check(lib().ashkv_nbit_outliers_flatten(
         bucket_counts.data_ptr(), bucket_entries.data_ptr(), bucket_cap, n_buckets, offsets.data_ptr(),
         out_index.data_ptr(), out_value.data_ptr(), total.data_ptr(), stream_handle(total.device)),

@@ -106,7 +106,7 @@ def flatten_outliers(enc: NBitEncoded) -> tuple[torch.Tensor, torch.Tensor, torc
     dev = enc.scales.device
     nb = enc.n_buckets
     cap_total = max(nb * enc.bucket_cap, 1)
-    offsets = torch.empty(nb + 1, dtype=torch.int32, device=dev)
+    offsets = torch.empty(_native.nbit_flatten_scratch_ints(nb), dtype=torch.int32, device=dev)
     idx = torch.empty(cap_total, dtype=torch.int32, device=dev)
     val = torch.empty(cap_total, dtype=torch.int16, device=dev)
     total = torch.empty(1, dtype=torch.int32, device=dev)

@@ -66,7 +66,7 @@ __device__ __forceinline__ void st_cs_v4(void* p, uint4 v) {
                :: "l"(p), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w) : "memory");
 }
 
-// NaN-propagating |a| max (PTX max.NaN): returns NaN if either input is NaN.
+// NaN-propagating max (PTX max.NaN): NaN if either input is NaN.
 __device__ __forceinline__ float max_nan(float a, float b) {
   float r;
   asm("max.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));

@@ -7,9 +7,9 @@
 //   load (16-byte streaming loads) -> mean -> fp64 variance -> outlier mask
 //   -> inlier absmax -> delta -> dithered quantise -> MSB-first pack ->
 //   one vector store of the codes + one bf16 delta store.
-// Outliers are ranked with a CTA-wide scan of per-group popcounts, so each
-// CTA (256 groups = one "bucket" of 8192 elements) writes its ascending
-// outlier list with no global synchronisation.
+// Outliers are ranked with a warp scan of per-group popcounts: each warp's
+// 32 groups form one "bucket" of 1024 elements whose ascending outlier list
+// the warp writes with no CTA or global synchronisation.
 //
 // Arithmetic follows the reference exactly as PyTorch evaluates it on the
 // host: every fp32 operation is a separate IEEE operation (no contraction),
@@ -26,7 +26,9 @@
 namespace ashkv {
 namespace {
 
-constexpr int kThreads = ASHKV_NBIT_BUCKET_GROUPS;  // one group per thread, one bucket per CTA
+constexpr int kThreads = 256;                     // 8 warps per CTA
+constexpr int kWarps = kThreads / 32;
+static_assert(ASHKV_NBIT_BUCKET_GROUPS == 32, "one bucket per warp, one group per lane");
 
 struct NbitEncParams {
   const uint16_t* src;
@@ -57,30 +59,7 @@ struct NbitDecParams {
   uint32_t* status;
 };
 
-// Inclusive scan across the CTA of one uint32 per thread; returns the
-// exclusive prefix and writes the CTA total to *total.
-__device__ __forceinline__ uint32_t cta_exclusive_scan(uint32_t v, uint32_t* smem_warp, uint32_t& total) {
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  uint32_t inc = v;
-#pragma unroll
-  for (int off = 1; off < 32; off <<= 1) {
-    const uint32_t n = __shfl_up_sync(0xFFFFFFFFu, inc, off);
-    if (lane >= off) inc += n;
-  }
-  if (lane == 31) smem_warp[warp] = inc;
-  __syncthreads();
-  uint32_t warp_base = 0, tot = 0;
-#pragma unroll
-  for (int w = 0; w < kThreads / 32; ++w) {
-    const uint32_t t = smem_warp[w];
-    if (w < warp) warp_base += t;
-    tot += t;
-  }
-  total = tot;
-  return warp_base + inc - v;
-}
-
-// One thread per 32-element group, one CTA (256 groups) per outlier bucket.
+// One thread per 32-element group, one warp (32 groups) per outlier bucket.
 //
 // Outlier decisions are made against the reference threshold without
 // computing its fp64 variance in the common case: an fp32 variance with a
@@ -90,25 +69,32 @@ __device__ __forceinline__ uint32_t cta_exclusive_scan(uint32_t v, uint32_t* sme
 // agree, that is the exact mask, and only if some |x - mu| falls between the
 // two bounds is the exact fp64 threshold computed.
 // A group's 32 bf16 values as 4 chunks of 8 (16 bytes each), plus access to
-// element e of the group owned by another thread of the CTA.
+// element e of the group owned by another lane of the warp.
 struct RegGroup {  // held in registers; other groups read back from global memory
   const uint32_t* w;
   const uint16_t* src;  // the kernel's source (group g at src + 32 g)
-  int64_t g0;           // group of thread 0 of the CTA
+  int64_t g0;           // group of lane 0 of the warp
   __device__ __forceinline__ uint4 chunk(int c) const { return make_uint4(w[4 * c], w[4 * c + 1], w[4 * c + 2], w[4 * c + 3]); }
-  __device__ __forceinline__ uint32_t elem(int owner_tid, int e) const { return src[(g0 + owner_tid) * 32 + e]; }
+  __device__ __forceinline__ uint32_t elem(int owner_lane, int e) const { return src[(g0 + owner_lane) * 32 + e]; }
 };
-struct SmemGroup {  // rows of a 64-byte-swizzled shared-memory tile, one per thread
+struct SmemGroup {  // rows of a 64-byte-swizzled shared-memory tile (the warp's bucket), one per lane
   uint32_t tile, row, sw;
   __device__ __forceinline__ uint4 chunk(int c) const { return lds128(row + 16u * (uint32_t(c) ^ sw)); }
-  __device__ __forceinline__ uint32_t elem(int owner_tid, int e) const {
-    const uint32_t osw = uint32_t(owner_tid >> 1) & 3u;
-    const uint32_t a = tile + uint32_t(owner_tid) * 64u + 16u * ((uint32_t(e) >> 3) ^ osw) + 2u * (uint32_t(e) & 7u);
+  __device__ __forceinline__ uint32_t elem(int owner_lane, int e) const {
+    const uint32_t osw = uint32_t(owner_lane >> 1) & 3u;
+    const uint32_t a = tile + uint32_t(owner_lane) * 64u + 16u * ((uint32_t(e) >> 3) ^ osw) + 2u * (uint32_t(e) & 7u);
     uint16_t v;
     asm volatile("ld.shared.u16 %0, [%1];" : "=h"(v) : "r"(a));
     return v;
   }
 };
+
+// Two signed 16-bit integers clamped to [0, hi]: max(min(v, hi), 0) per half.
+__device__ __forceinline__ uint32_t clamp_codes_s16x2(uint32_t v, uint32_t hi) {
+  uint32_t r;
+  asm("min.relu.s16x2 %0, %1, %2;" : "=r"(r) : "r"(v), "r"(hi | (hi << 16)));
+  return r;
+}
 
 __device__ __forceinline__ double warp_sum_f64(double v) {  // pairwise (butterfly) order, same in every lane
 #pragma unroll
@@ -209,7 +195,7 @@ __device__ __forceinline__ uint32_t encode_group(const Src& src, const NbitEncPa
     const float lo_o = __shfl_sync(0xFFFFFFFFu, thr_lo, owner);
     const float hi_o = __shfl_sync(0xFFFFFFFFu, thr_hi, owner);
     const bool ok_o = __shfl_sync(0xFFFFFFFFu, int(bounds_ok), owner) != 0;
-    const float x = bf16_to_f32(uint16_t(src.elem((threadIdx.x & ~31) + owner, lane)));
+    const float x = bf16_to_f32(uint16_t(src.elem(owner, lane)));
     const float d = fabsf(__fadd_rn(x, -mu_o));
     const uint32_t mlo = __ballot_sync(0xFFFFFFFFu, d > lo_o);
     uint32_t m = __ballot_sync(0xFFFFFFFFu, d > hi_o);
@@ -236,6 +222,7 @@ __device__ __forceinline__ uint32_t encode_group(const Src& src, const NbitEncPa
   const bool fast_div = recip_ok(delta);
   const f2 DELTA = pk2(delta, delta), YHI = pk2(y.hi, y.hi), YLO = pk2(y.lo, y.lo), NDELTA = pk2(-delta, -delta);
   const float half = p.half_states;
+  const f2 HALF = pk2(half, half), MAGIC = pk2(12582912.0f, 12582912.0f);
   uint32_t o[BITS];  // packed codes: 32 * BITS bits, MSB-first within each byte
 #pragma unroll
   for (int k = 0; k < BITS; ++k) o[k] = 0u;
@@ -274,38 +261,46 @@ __device__ __forceinline__ uint32_t encode_group(const Src& src, const NbitEncPa
         DZ[h] = fma2(pk2(flo, fhi), pk2(128.0f, 128.0f), pk2(-128.5f, -128.5f));
       }
     }
+    // v = RN(RN(a / delta) + half), a = x' + noise; code = clamp(rint(v), 0, 2^bits - 1).
+    // rint: RN(v + 1.5 * 2^23) leaves rint(v) in the low mantissa bits (|v| < 2^22).
+    // With delta in Markstein's range every a is finite and |a / delta| <= half + 1,
+    // so the clamp runs on the integers (two codes per s16x2 word); otherwise the
+    // float clamp comes first (NaN -> 0), as in the reference.
     f2 Q[4];
 #pragma unroll
     for (int h = 0; h < 4; ++h) Q[h] = add2(P[h], mul2(DZ[h], DELTA));  // a = x' + noise
     if (fast_div) {
 #pragma unroll
-      for (int h = 0; h < 4; ++h) Q[h] = div2_rn(Q[h], YHI, YLO, NDELTA);
+      for (int h = 0; h < 4; ++h) Q[h] = add2(add2(div2_rn(Q[h], YHI, YLO, NDELTA), HALF), MAGIC);
     } else {
 #pragma unroll
       for (int h = 0; h < 4; ++h) {
         float a0, a1;
         upk2(Q[h], a0, a1);
-        Q[h] = pk2(__fdiv_rn(a0, delta), __fdiv_rn(a1, delta));
+        const float v0 = fminf(fmaxf(__fadd_rn(__fdiv_rn(a0, delta), half), 0.0f), float(kMaxCode));
+        const float v1 = fminf(fmaxf(__fadd_rn(__fdiv_rn(a1, delta), half), 0.0f), float(kMaxCode));
+        Q[h] = add2(pk2(v0, v1), MAGIC);
       }
     }
+    uint32_t W[4];  // codes of elements 2h (low half) and 2h + 1 (high half)
 #pragma unroll
     for (int h = 0; h < 4; ++h) {
-      const int k = 4 * c + h;  // pair index: elements 2k, 2k+1
-      float v0, v1;
-      upk2(Q[h], v0, v1);
-      v0 = fminf(fmaxf(__fadd_rn(v0, half), 0.0f), float(kMaxCode));  // NaN -> 0
-      v1 = fminf(fmaxf(__fadd_rn(v1, half), 0.0f), float(kMaxCode));
       float t0, t1;
-      upk2(add2(pk2(v0, v1), pk2(12582912.0f, 12582912.0f)), t0, t1);
-      const uint32_t c0 = __float_as_uint(t0) & kMaxCode, c1 = __float_as_uint(t1) & kMaxCode;
-      if constexpr (BITS == 4) {
-        o[k >> 2] |= ((c0 << 4) | c1) << (8 * (k & 3));
-      } else if constexpr (BITS == 2) {
-        const int e = 2 * k;
-        o[e >> 4] |= ((c0 << (6 - 2 * (e & 3))) | (c1 << (4 - 2 * (e & 3)))) << (8 * ((e >> 2) & 3));
-      } else {
-        o[k >> 1] |= (c0 | (c1 << 8)) << (16 * (k & 1));
-      }
+      upk2(Q[h], t0, t1);
+      W[h] = clamp_codes_s16x2(__byte_perm(__float_as_uint(t0), __float_as_uint(t1), 0x5410), kMaxCode);
+    }
+    // bytes c0..c3 of elements 8c..8c+3, and c4..c7
+    const uint32_t X = __byte_perm(W[0], W[1], 0x6420), Y = __byte_perm(W[2], W[3], 0x6420);
+    if constexpr (BITS == 8) {
+      o[2 * c] = X;
+      o[2 * c + 1] = Y;
+    } else if constexpr (BITS == 4) {
+      // byte j of X*16 + (X >> 8) is (c_j << 4) + c_{j+1}: keep bytes 0 and 2 of each half.
+      o[c] = __byte_perm(X * 16u + (X >> 8), Y * 16u + (Y >> 8), 0x6420);
+    } else {
+      const uint32_t tx = X * 4u + (X >> 8), ty = Y * 4u + (Y >> 8);   // bytes 0, 2: c0c1, c2c3
+      const uint32_t ux = tx * 16u + (tx >> 16), uy = ty * 16u + (ty >> 16);  // byte 0: c0c1c2c3
+      o[c >> 1] |= (__byte_perm(ux, uy, 0x0040) & 0xFFFFu) << (16 * (c & 1));
     }
   }
 
@@ -325,14 +320,25 @@ __device__ __forceinline__ uint32_t encode_group(const Src& src, const NbitEncPa
   return omask;
 }
 
-// Append this thread's outliers (bits of omask) to the bucket's list; the
-// ranks come from a CTA-wide scan, so the list is in ascending element order.
-__device__ __forceinline__ void write_outliers(const NbitEncParams& p, int64_t bucket, int64_t g, uint32_t omask,
-                                               uint32_t* s_warp) {
+// Append this lane's outliers (bits of omask) to the warp's bucket; the
+// ranks come from a warp scan, so the list is in ascending element order.
+// Called by all 32 lanes; inactive lanes pass omask = 0.
+__device__ __forceinline__ void write_outliers(const NbitEncParams& p, int64_t bucket, int64_t g, uint32_t omask) {
+  const int lane = threadIdx.x & 31;
+  if (!__any_sync(0xFFFFFFFFu, omask != 0)) {  // the common case: no outliers in the bucket
+    if (lane == 0) p.bucket_counts[bucket] = 0;
+    return;
+  }
   const uint32_t cnt = uint32_t(__popc(omask));
-  uint32_t total = 0;
-  uint32_t pos = cta_exclusive_scan(cnt, s_warp, total);
-  if (threadIdx.x == 0) {
+  uint32_t inc = cnt;
+#pragma unroll
+  for (int off = 1; off < 32; off <<= 1) {
+    const uint32_t t = __shfl_up_sync(0xFFFFFFFFu, inc, off);
+    if (lane >= off) inc += t;
+  }
+  const uint32_t total = __shfl_sync(0xFFFFFFFFu, inc, 31);
+  uint32_t pos = inc - cnt;
+  if (lane == 0) {
     p.bucket_counts[bucket] = total;
     if (total > uint32_t(p.bucket_cap)) atomicOr(p.status, ASHKV_FLAG_OUTLIER_OVERFLOW);
   }
@@ -343,7 +349,7 @@ __device__ __forceinline__ void write_outliers(const NbitEncParams& p, int64_t b
       const int i = __ffs(m) - 1;
       m &= m - 1;
       if (pos < uint32_t(p.bucket_cap)) {
-        const uint32_t local = uint32_t(threadIdx.x) * 32u + uint32_t(i);
+        const uint32_t local = uint32_t(lane) * 32u + uint32_t(i);
         out[pos] = (local << 16) | uint32_t(p.src[g * 32 + i]);  // original bits (rare path)
       }
       ++pos;
@@ -351,11 +357,10 @@ __device__ __forceinline__ void write_outliers(const NbitEncParams& p, int64_t b
   }
 }
 
-// Direct-load variant: one CTA per bucket, each thread loads its 64-byte
-// group with two 256-bit loads.  Used when a tensor map cannot be built.
+// Direct-load variant: each warp encodes one bucket, each lane loads its
+// 64-byte group with two 256-bit loads.  Used when a tensor map cannot be built.
 template <int BITS, int DMODE>
 __global__ void __launch_bounds__(kThreads, 2) nbit_encode_kernel(const NbitEncParams p) {
-  __shared__ uint32_t s_warp[kThreads / 32];
   const int64_t g = int64_t(blockIdx.x) * kThreads + threadIdx.x;
   const bool active = g < p.n_groups;
   uint32_t w[16];
@@ -368,77 +373,79 @@ __global__ void __launch_bounds__(kThreads, 2) nbit_encode_kernel(const NbitEncP
 #pragma unroll
     for (int k = 0; k < 16; ++k) w[k] = 0u;
   }
-  const uint32_t omask =
-      encode_group<BITS, DMODE>(RegGroup{w, p.src, int64_t(blockIdx.x) * kThreads}, p, g, active);
-  write_outliers(p, blockIdx.x, g, omask, s_warp);
+  const int64_t g0 = g - (threadIdx.x & 31);
+  if (g0 >= p.n_groups) return;  // whole warp past the end
+  const uint32_t omask = encode_group<BITS, DMODE>(RegGroup{w, p.src, g0}, p, g, active);
+  write_outliers(p, g0 / 32, g, omask);
 }
 
-constexpr int kTileBytes = kThreads * 64;      // one bucket of bf16 = 16 KiB
+constexpr int kTileBytes = 32 * 64;            // one bucket of bf16 = 2 KiB
 constexpr uint32_t kMaxPolls = 1u << 24;       // bounded mbarrier waits
 
-// Persistent TMA variant: each CTA walks buckets b = blockIdx.x + i*gridDim.x.
-// A 2-D tensor map views the source as [n_groups, 32] bf16; one TMA copy
-// brings a whole bucket (256 rows of 64 bytes) into a shared-memory stage
+// Persistent TMA variant with one pipeline per warp: warp w of CTA c walks
+// buckets b = (c * kWarps + w) + i * (gridDim.x * kWarps).  A 2-D tensor map
+// views the source as [n_groups, 32] bf16; one TMA copy brings a bucket
+// (32 rows of 64 bytes) into one of the warp's STAGES shared-memory stages
 // with the 64-byte swizzle (16-byte chunk k of row r stored at chunk
-// k ^ ((r >> 1) & 3)), so the 8 threads of each shared-memory phase hit 8
-// distinct bank groups when they read their own row.  STAGES buckets are in
-// flight per CTA; a stage is refilled as soon as every thread has copied its
-// row into registers.
+// k ^ ((r >> 1) & 3)), so the 8 lanes of each shared-memory phase hit 8
+// distinct bank groups when they read their own row.  Lane 0 refills a stage
+// once the warp has encoded its bucket; warps never wait for one another.
 template <int BITS, int DMODE, int STAGES>
-__global__ void __launch_bounds__(kThreads, 3) nbit_encode_tma_kernel(const __grid_constant__ CUtensorMap tmap,
+__global__ void __launch_bounds__(kThreads, 4) nbit_encode_tma_kernel(const __grid_constant__ CUtensorMap tmap,
                                                                        const NbitEncParams p, int64_t n_buckets) {
   extern __shared__ uint8_t smem_raw[];
-  __shared__ uint64_t full[STAGES];
-  __shared__ uint32_t s_warp[kThreads / 32];
+  __shared__ uint64_t full[kWarps][STAGES];
   uint8_t* tiles = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  const int tid = threadIdx.x;
-  if (tid == 0) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  uint8_t* my_tiles = tiles + warp * (STAGES * kTileBytes);
+  uint64_t* bar = full[warp];
+  const int64_t first = int64_t(blockIdx.x) * kWarps + warp, step = int64_t(gridDim.x) * kWarps;
+  if (lane == 0) {
 #pragma unroll
-    for (int s = 0; s < STAGES; ++s) mbar_init(&full[s], 1);
+    for (int s = 0; s < STAGES; ++s) mbar_init(&bar[s], 1);
     mbar_init_fence();
-  }
-  __syncthreads();
-  if (tid == 0) {
 #pragma unroll
     for (int s = 0; s < STAGES; ++s) {
-      const int64_t b = blockIdx.x + int64_t(s) * gridDim.x;
+      const int64_t b = first + int64_t(s) * step;
       if (b < n_buckets) {
-        mbar_arrive_expect_tx(&full[s], kTileBytes);
-        tma_load_2d(tiles + s * kTileBytes, &tmap, &full[s], 0, int32_t(b * kThreads));
+        mbar_arrive_expect_tx(&bar[s], kTileBytes);
+        tma_load_2d(my_tiles + s * kTileBytes, &tmap, &bar[s], 0, int32_t(b * 32));
       }
     }
   }
-  const uint32_t sw = uint32_t(tid >> 1) & 3u;
+  __syncwarp();
+  const uint32_t sw = uint32_t(lane >> 1) & 3u;
   for (int64_t it = 0;; ++it) {
-    const int64_t b = blockIdx.x + it * gridDim.x;
+    const int64_t b = first + it * step;
     if (b >= n_buckets) break;
     const int s = int(it % STAGES);
     const uint32_t parity = uint32_t(it / STAGES) & 1u;
-    const bool ok = mbar_wait_bounded(&full[s], parity, kMaxPolls);
-    if (__syncthreads_or(!ok)) {
-      // Give up: flag it, let the copies already issued land, and leave.
-      if (tid == 0) {
+    const bool ok = mbar_wait_bounded(&bar[s], parity, kMaxPolls);
+    if (!__all_sync(0xFFFFFFFFu, ok)) {
+      // Give up: flag it, let this warp's copies already issued land, and leave.
+      if (lane == 0) {
         atomicOr(p.status, ASHKV_FLAG_TIMEOUT);
         for (int k = 0; k < STAGES; ++k) {
           const int64_t i2 = it + k;
-          if (blockIdx.x + i2 * gridDim.x < n_buckets)
-            mbar_wait_bounded(&full[i2 % STAGES], uint32_t(i2 / STAGES) & 1u, kMaxPolls);
+          if (first + i2 * step < n_buckets)
+            mbar_wait_bounded(&bar[i2 % STAGES], uint32_t(i2 / STAGES) & 1u, kMaxPolls);
         }
       }
       return;
     }
-    const int64_t g = b * kThreads + tid;
+    const int64_t g = b * 32 + lane;
     const bool active = g < p.n_groups;
-    const uint32_t tile = smem_u32(tiles + s * kTileBytes);
-    const SmemGroup src{tile, tile + uint32_t(tid) * 64u, sw};
+    const uint32_t tile = smem_u32(my_tiles + s * kTileBytes);
+    const SmemGroup src{tile, tile + uint32_t(lane) * 64u, sw};
     const uint32_t omask = encode_group<BITS, DMODE>(src, p, g, active);
-    write_outliers(p, b, g, omask, s_warp);  // ends with a CTA barrier: stage s is free
-    if (tid == 0) {
-      const int64_t nb = b + int64_t(STAGES) * gridDim.x;
+    write_outliers(p, b, g, omask);
+    __syncwarp();  // every lane is done with stage s
+    if (lane == 0) {
+      const int64_t nb = b + int64_t(STAGES) * step;
       if (nb < n_buckets) {
         fence_proxy_async_smem();
-        mbar_arrive_expect_tx(&full[s], kTileBytes);
-        tma_load_2d(tiles + s * kTileBytes, &tmap, &full[s], 0, int32_t(nb * kThreads));
+        mbar_arrive_expect_tx(&bar[s], kTileBytes);
+        tma_load_2d(my_tiles + s * kTileBytes, &tmap, &bar[s], 0, int32_t(nb * 32));
       }
     }
   }
@@ -500,17 +507,22 @@ __device__ __forceinline__ void dequant_group(const uint16_t* scales, const uint
   st_cs_v8(out + 16, hi);
 }
 
+// One lane per group; each warp then overwrites its bucket's outliers.
 template <int BITS>
 __global__ void __launch_bounds__(kThreads) nbit_decode_kernel(const NbitDecParams p) {
   const int64_t g = int64_t(blockIdx.x) * kThreads + threadIdx.x;
+  const int64_t g0 = g - (threadIdx.x & 31);
+  const int64_t bucket = g0 / 32;
+  // the bucket's count is fetched first so its latency overlaps the dequantisation
+  const uint32_t count = (p.bucket_counts && g0 < p.n_groups) ? p.bucket_counts[bucket] : 0u;
   if (g < p.n_groups) dequant_group<BITS>(p.scales, p.codes, g, p.half_states, p.dst);
-  if (!p.bucket_counts) return;
-  __syncthreads();  // the bucket's dense values are stored before its outliers overwrite them
-  const uint32_t n = min(p.bucket_counts[blockIdx.x], uint32_t(p.bucket_cap));
-  const uint32_t* ent = p.bucket_entries + int64_t(blockIdx.x) * p.bucket_cap;
-  const int64_t base = int64_t(blockIdx.x) * ASHKV_NBIT_BUCKET_ELEMS;
+  if (!p.bucket_counts || g0 >= p.n_groups) return;  // whole warp past the end
+  __syncwarp();  // the bucket's dense values are stored before its outliers overwrite them
+  const uint32_t n = min(count, uint32_t(p.bucket_cap));
+  const uint32_t* ent = p.bucket_entries + bucket * p.bucket_cap;
+  const int64_t base = bucket * ASHKV_NBIT_BUCKET_ELEMS;
   const int64_t n_elems = p.n_groups * 32;
-  for (uint32_t j = threadIdx.x; j < n; j += kThreads) {
+  for (uint32_t j = threadIdx.x & 31; j < n; j += 32) {
     const uint32_t e = ent[j];
     const int64_t idx = base + (e >> 16);
     if (idx < n_elems) p.dst[idx] = uint16_t(e & 0xFFFFu);
@@ -534,51 +546,91 @@ __global__ void __launch_bounds__(256) scatter_outliers_kernel(const int32_t* id
   }
 }
 
-// Single-CTA exclusive scan over bucket counts (clamped to the capacity).
-__global__ void __launch_bounds__(1024) bucket_scan_kernel(const uint32_t* counts, int32_t cap, int64_t n,
-                                                           uint32_t* offsets, uint32_t* total) {
-  __shared__ uint32_t s_warp[32];
-  __shared__ uint32_t s_carry;
-  if (threadIdx.x == 0) s_carry = 0;
-  __syncthreads();
+// Outlier-list scan in three phases: each CTA scans a tile of kScanTile
+// bucket counts (clamped to the capacity) into tile-relative offsets and a
+// tile total; one CTA scans the tile totals; the flatten kernel adds the
+// tile's base.  Tile totals live after the n_buckets + 1 offsets.
+constexpr int kScanTile = 4096;  // 1024 threads x 4 buckets
+
+__device__ __forceinline__ uint32_t block_exclusive_scan_1024(uint32_t v, uint32_t* s_warp, uint32_t& total) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  for (int64_t base = 0; base < n; base += 1024) {
-    const int64_t i = base + threadIdx.x;
-    const uint32_t v = i < n ? min(counts[i], uint32_t(cap)) : 0u;
-    uint32_t inc = v;
+  uint32_t inc = v;
+#pragma unroll
+  for (int off = 1; off < 32; off <<= 1) {
+    const uint32_t t = __shfl_up_sync(0xFFFFFFFFu, inc, off);
+    if (lane >= off) inc += t;
+  }
+  if (lane == 31) s_warp[warp] = inc;
+  __syncthreads();
+  if (warp == 0) {
+    const uint32_t w = s_warp[lane];
+    uint32_t wi = w;
 #pragma unroll
     for (int off = 1; off < 32; off <<= 1) {
-      const uint32_t t = __shfl_up_sync(0xFFFFFFFFu, inc, off);
-      if (lane >= off) inc += t;
+      const uint32_t t = __shfl_up_sync(0xFFFFFFFFu, wi, off);
+      if (lane >= off) wi += t;
     }
-    if (lane == 31) s_warp[warp] = inc;
-    __syncthreads();
-    uint32_t wbase = 0, tile = 0;
-    for (int w = 0; w < 32; ++w) {
-      const uint32_t t = s_warp[w];
-      if (w < warp) wbase += t;
-      tile += t;
-    }
-    const uint32_t carry = s_carry;
-    if (i < n) offsets[i] = carry + wbase + inc - v;
-    __syncthreads();
-    if (threadIdx.x == 0) s_carry = carry + tile;
-    __syncthreads();
+    s_warp[lane] = wi - w;  // exclusive prefix of warp totals
+    if (lane == 31) s_warp[32] = wi;
+  }
+  __syncthreads();
+  total = s_warp[32];
+  return s_warp[warp] + inc - v;
+}
+
+__global__ void __launch_bounds__(1024) bucket_scan_tiles_kernel(const uint32_t* counts, int32_t cap, int64_t n,
+                                                                 uint32_t* offsets, uint32_t* tile_totals) {
+  __shared__ uint32_t s_warp[33];
+  const int64_t base = int64_t(blockIdx.x) * kScanTile + int64_t(threadIdx.x) * 4;
+  uint32_t v[4], local = 0;
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    v[k] = base + k < n ? min(counts[base + k], uint32_t(cap)) : 0u;
+    local += v[k];
+  }
+  uint32_t total;
+  uint32_t run = block_exclusive_scan_1024(local, s_warp, total);
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    if (base + k < n) offsets[base + k] = run;
+    run += v[k];
+  }
+  if (threadIdx.x == 0) tile_totals[blockIdx.x] = total;
+}
+
+// Exclusive scan of the tile totals in place (one CTA); writes the grand total.
+__global__ void __launch_bounds__(1024) tile_scan_kernel(uint32_t* tile_totals, int64_t n_tiles, uint32_t* end,
+                                                         uint32_t* total_out) {
+  __shared__ uint32_t s_warp[33];
+  uint32_t carry = 0;
+  for (int64_t b0 = 0; b0 < n_tiles; b0 += 1024) {
+    const int64_t i = b0 + threadIdx.x;
+    const uint32_t v = i < n_tiles ? tile_totals[i] : 0u;
+    uint32_t chunk;
+    const uint32_t ex = block_exclusive_scan_1024(v, s_warp, chunk);
+    if (i < n_tiles) tile_totals[i] = carry + ex;
+    carry += chunk;
+    __syncthreads();  // s_warp is reused by the next chunk
   }
   if (threadIdx.x == 0) {
-    offsets[n] = s_carry;
-    *total = s_carry;
+    *end = carry;
+    *total_out = carry;
   }
 }
 
+// One warp per bucket; turns offsets[b] into the bucket's absolute position.
 __global__ void __launch_bounds__(256) bucket_flatten_kernel(const uint32_t* counts, const uint32_t* entries,
-                                                             int32_t cap, const uint32_t* offsets,
-                                                             int32_t* out_idx, uint16_t* out_val) {
-  const int64_t b = blockIdx.x;
+                                                             int32_t cap, int64_t n_buckets, uint32_t* offsets,
+                                                             const uint32_t* tile_base, int32_t* out_idx,
+                                                             uint16_t* out_val) {
+  const int64_t b = int64_t(blockIdx.x) * (blockDim.x / 32) + (threadIdx.x >> 5);
+  if (b >= n_buckets) return;
   const uint32_t n = min(counts[b], uint32_t(cap));
-  const uint32_t off = offsets[b];
+  const uint32_t off = offsets[b] + tile_base[b / kScanTile];
+  __syncwarp();
+  if ((threadIdx.x & 31) == 0) offsets[b] = off;
   const uint32_t* ent = entries + b * cap;
-  for (uint32_t j = threadIdx.x; j < n; j += blockDim.x) {
+  for (uint32_t j = threadIdx.x & 31; j < n; j += 32) {
     const uint32_t e = ent[j];
     out_idx[off + j] = int32_t(b * ASHKV_NBIT_BUCKET_ELEMS + (e >> 16));
     out_val[off + j] = uint16_t(e & 0xFFFFu);
@@ -587,7 +639,8 @@ __global__ void __launch_bounds__(256) bucket_flatten_kernel(const uint32_t* cou
 
 float half_states_for(int bits) { return float((1 << bits) - 1) / 2.0f; }
 
-constexpr int kStages = 4;  // 64 KiB of tiles per CTA, three CTAs per SM
+constexpr int kStages = 3;      // 3 buckets in flight per warp: 48 KiB of tiles per CTA
+constexpr int kCtasPerSm = 4;   // 32 warps per SM
 
 // cuTensorMapEncodeTiled through the runtime's driver entry point (no -lcuda).
 PFN_cuTensorMapEncodeTiled_v12000 tmap_encode_fn() {
@@ -605,13 +658,13 @@ PFN_cuTensorMapEncodeTiled_v12000 tmap_encode_fn() {
   return fn;
 }
 
-// [n_groups, 32] bf16 rows of 64 bytes, box = one bucket (256 rows), 64-byte swizzle.
+// [n_groups, 32] bf16 rows of 64 bytes, box = one bucket (32 rows), 64-byte swizzle.
 bool make_group_tmap(CUtensorMap* map, const void* src, int64_t n_groups) {
   auto fn = tmap_encode_fn();
   if (!fn || n_groups <= 0 || n_groups > 0x7FFFFF00LL || !aligned(src, 16)) return false;
   cuuint64_t dims[2] = {32, cuuint64_t(n_groups)};
   cuuint64_t strides[1] = {64};
-  cuuint32_t box[2] = {32, uint32_t(kThreads)};
+  cuuint32_t box[2] = {32, 32};
   cuuint32_t estr[2] = {1, 1};
   const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<void*>(src), dims, strides, box, estr,
                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -622,7 +675,7 @@ bool make_group_tmap(CUtensorMap* map, const void* src, int64_t n_groups) {
 template <int BITS, int DMODE>
 ashkv_status_t launch_tma(const CUtensorMap& tmap, const NbitEncParams& p, int64_t n_buckets, unsigned grid,
                           cudaStream_t st) {
-  constexpr int smem = kStages * kTileBytes + 1024;
+  constexpr int smem = kWarps * kStages * kTileBytes + 1024;
   auto kern = nbit_encode_tma_kernel<BITS, DMODE, kStages>;
   static std::once_flag once;
   static cudaError_t attr_err = cudaSuccess;
@@ -659,8 +712,8 @@ extern "C" ashkv_status_t ashkv_nbit_encode(
   if (!aligned(d_src, 32) || !aligned(d_scales, 2) || !aligned(d_codes, bits == 2 ? 8 : bits == 4 ? 16 : 32))
     return ASHKV_BAD_ARGUMENT;
   if (dither_mode == ASHKV_DITHER_TENSOR && !aligned(d_dither, 32)) return ASHKV_BAD_ARGUMENT;
-  const int64_t n_buckets = (n_groups + kThreads - 1) / kThreads;
-  if (n_buckets > 0x7FFFFFFF) return ASHKV_BAD_ARGUMENT;
+  const int64_t n_buckets = (n_groups + 31) / 32;
+  if (n_groups > 0x7FFFFF00LL) return ASHKV_BAD_ARGUMENT;
 
   NbitEncParams p;
   p.src = static_cast<const uint16_t*>(d_src); p.n_groups = n_groups;
@@ -675,8 +728,8 @@ extern "C" ashkv_status_t ashkv_nbit_encode(
   CUtensorMap tmap;
   if (make_group_tmap(&tmap, d_src, n_groups)) {
     const int sms = sm_count() > 0 ? sm_count() : 148;
-    const int64_t want = int64_t(sms) * 3;
-    const unsigned grid = unsigned(n_buckets < want ? n_buckets : want);
+    const int64_t want = int64_t(sms) * kCtasPerSm, need = (n_buckets + kWarps - 1) / kWarps;
+    const unsigned grid = unsigned(need < want ? need : want);
     const bool tensor = dither_mode == ASHKV_DITHER_TENSOR;
     ashkv_status_t s = ASHKV_OK;
     if (bits == 2) s = tensor ? launch_tma<2, ASHKV_DITHER_TENSOR>(tmap, p, n_buckets, grid, st)
@@ -687,7 +740,7 @@ extern "C" ashkv_status_t ashkv_nbit_encode(
                     : launch_tma<8, ASHKV_DITHER_PHILOX>(tmap, p, n_buckets, grid, st);
     return s;
   }
-  const dim3 grid{unsigned(n_buckets)}, block{unsigned(kThreads)};
+  const dim3 grid{unsigned((n_groups + kThreads - 1) / kThreads)}, block{unsigned(kThreads)};
   if (dither_mode == ASHKV_DITHER_TENSOR) {
     if (bits == 2) nbit_encode_kernel<2, ASHKV_DITHER_TENSOR><<<grid, block, 0, st>>>(p);
     else if (bits == 4) nbit_encode_kernel<4, ASHKV_DITHER_TENSOR><<<grid, block, 0, st>>>(p);
@@ -711,8 +764,8 @@ extern "C" ashkv_status_t ashkv_nbit_decode(
   if (d_bucket_counts && (!d_status || (bucket_cap > 0 && !d_bucket_entries))) return ASHKV_BAD_ARGUMENT;
   if (!aligned(d_dst, 32) || !aligned(d_scales, 2) || !aligned(d_codes, bits == 2 ? 8 : 16))
     return ASHKV_BAD_ARGUMENT;
-  const int64_t n_buckets = (n_groups + kThreads - 1) / kThreads;
-  if (n_buckets > 0x7FFFFFFF) return ASHKV_BAD_ARGUMENT;
+  const int64_t n_ctas = (n_groups + kThreads - 1) / kThreads;  // 8 buckets per CTA
+  if (n_ctas > 0x7FFFFFFF) return ASHKV_BAD_ARGUMENT;
 
   NbitDecParams p;
   p.scales = static_cast<const uint16_t*>(d_scales); p.codes = static_cast<const uint8_t*>(d_codes);
@@ -720,11 +773,16 @@ extern "C" ashkv_status_t ashkv_nbit_decode(
   p.bucket_counts = d_bucket_counts; p.bucket_entries = d_bucket_entries; p.bucket_cap = bucket_cap;
   p.dst = static_cast<uint16_t*>(d_dst); p.status = d_status;
   cudaStream_t st = as_stream(stream);
-  const dim3 grid{unsigned(n_buckets)}, block{unsigned(kThreads)};
+  const dim3 grid{unsigned(n_ctas)}, block{unsigned(kThreads)};
   if (bits == 2) nbit_decode_kernel<2><<<grid, block, 0, st>>>(p);
   else if (bits == 4) nbit_decode_kernel<4><<<grid, block, 0, st>>>(p);
   else nbit_decode_kernel<8><<<grid, block, 0, st>>>(p);
   return check_launch("nbit_decode");
+}
+
+extern "C" int64_t ashkv_nbit_flatten_scratch_ints(int64_t n_buckets) {
+  if (n_buckets < 0) return -1;
+  return n_buckets + 1 + (n_buckets + kScanTile - 1) / kScanTile;
 }
 
 extern "C" ashkv_status_t ashkv_nbit_outliers_flatten(
@@ -743,11 +801,16 @@ extern "C" ashkv_status_t ashkv_nbit_outliers_flatten(
   }
   if (!d_bucket_counts || (bucket_cap > 0 && (!d_bucket_entries || !d_out_index || !d_out_value)))
     return ASHKV_BAD_ARGUMENT;
-  bucket_scan_kernel<<<1, 1024, 0, st>>>(d_bucket_counts, bucket_cap, n_buckets, d_offsets, d_total);
+  const int64_t n_tiles = (n_buckets + kScanTile - 1) / kScanTile;
+  uint32_t* tile_totals = d_offsets + n_buckets + 1;
+  bucket_scan_tiles_kernel<<<unsigned(n_tiles), 1024, 0, st>>>(d_bucket_counts, bucket_cap, n_buckets, d_offsets,
+                                                               tile_totals);
+  tile_scan_kernel<<<1, 1024, 0, st>>>(tile_totals, n_tiles, d_offsets + n_buckets, d_total);
   ashkv_status_t s = check_launch("nbit_bucket_scan");
-  if (s != ASHKV_OK || bucket_cap == 0) return s;
-  bucket_flatten_kernel<<<unsigned(n_buckets), 256, 0, st>>>(d_bucket_counts, d_bucket_entries, bucket_cap,
-                                                             d_offsets, d_out_index, d_out_value);
+  if (s != ASHKV_OK) return s;
+  bucket_flatten_kernel<<<unsigned((n_buckets + 7) / 8), 256, 0, st>>>(d_bucket_counts, d_bucket_entries,
+                                                                       bucket_cap, n_buckets, d_offsets, tile_totals,
+                                                                       d_out_index, d_out_value);
   return check_launch("nbit_bucket_flatten");
 }
 

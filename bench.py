@@ -413,7 +413,7 @@ def main() -> None:
             "encode_gbs_bf16": round(world * ELEMS * 2 / (enc_ms / 1e3) / 1e9, 2),
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "traffic": traffic, "peak_kind": peak_kind,
-                         "kernel": "nbit_encode_tma_kernel<4,PHILOX,4>",
+                         "kernel": "nbit_encode_tma_kernel<4,PHILOX,3>",
                          "alg_bytes_per_launch": enc_alg_bytes, "avg_launch_ms": round(enc_ms, 4)},
             "decode": {"kernel": "nbit_decode_kernel<4>", "avg_launch_ms": round(dec_ms, 4),
                        "achieved_gbs": round(dec_achieved, 1), "frac": round(dec_achieved / peak, 4)},

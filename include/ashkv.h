@@ -50,8 +50,8 @@ typedef int32_t ashkv_status_t;
 
 /* ---- N-bit codec constants ---------------------------------------------- */
 #define ASHKV_NBIT_GROUP          32    /* elements per quantisation group */
-#define ASHKV_NBIT_BUCKET_GROUPS  256   /* groups per outlier bucket */
-#define ASHKV_NBIT_BUCKET_ELEMS   8192  /* elements per outlier bucket */
+#define ASHKV_NBIT_BUCKET_GROUPS  32    /* groups per outlier bucket (one warp's groups) */
+#define ASHKV_NBIT_BUCKET_ELEMS   1024  /* elements per outlier bucket */
 #define ASHKV_DITHER_TENSOR 0           /* uniform U in [0,1) read from a caller fp32 tensor */
 #define ASHKV_DITHER_PHILOX 1           /* dither generated in-kernel: Philox4x32-10(seed) */
 
@@ -119,7 +119,7 @@ ASHKV_API ashkv_status_t ashkv_int8_decode_rows(
  *   delta   = max(max|x'|, 1e-8) / ((2^bits - 1) / 2)
  *   code    = clamp(rint((x' + (U - 0.5) * delta) / delta + half), 0, 2^bits - 1)
  * Outputs: d_scales (bf16 delta per group), d_codes (MSB-first packing,
- * 32*bits/8 bytes per group), and the outlier list in buckets of 256 groups:
+ * 32*bits/8 bytes per group), and the outlier list in buckets of 32 groups:
  * d_bucket_counts[b] is the number of outliers of bucket b (even when it
  * exceeds bucket_cap), d_bucket_entries[b*bucket_cap + j] =
  * (element index within the bucket << 16) | bf16 bits, ascending.
@@ -146,7 +146,10 @@ ASHKV_API ashkv_status_t ashkv_nbit_decode(
  * outliers into the reference blob's flat form: d_out_index[k] (int32 element
  * index within the call, ascending) and d_out_value[k] (bf16 bits).
  * d_total receives the number of outliers written.  d_offsets holds
- * n_buckets + 1 uint32 of caller scratch. */
+ * ashkv_nbit_flatten_scratch_ints(n_buckets) uint32 of caller scratch; on
+ * return d_offsets[b] is bucket b's first position in the flat list and
+ * d_offsets[n_buckets] the total. */
+ASHKV_API int64_t ashkv_nbit_flatten_scratch_ints(int64_t n_buckets);
 ASHKV_API ashkv_status_t ashkv_nbit_outliers_flatten(
     const uint32_t* d_bucket_counts, const uint32_t* d_bucket_entries, int32_t bucket_cap,
     int64_t n_buckets, uint32_t* d_offsets,

@@ -170,6 +170,40 @@ def test_nbit_kernel_vs_oracle_tensor_dither(cuda, bits, kind):
     assert np.array_equal(bits_of(dec), want)
 
 
+def _offset_and_threshold_groups(n_groups: int, seed: int) -> np.ndarray:
+    """Groups whose mean dwarfs their spread (offsets up to 1e5 sd, both signs),
+    groups of bf16-quantised offsets (many equal values), and groups with one
+    element moved to about 3 sd from the rest, to sit near the outlier threshold."""
+    g = torch.Generator().manual_seed(seed)
+    z = torch.randn(n_groups, 32, generator=g)
+    offs = torch.tensor([0.0, 3.0, 30.0, 300.0, 3e3, 3e4, 1e5, -1e5, -7.0])
+    k = torch.randint(0, offs.numel(), (n_groups, 1), generator=g)
+    sd = torch.exp(torch.empty(n_groups, 1).uniform_(-8.0, 8.0, generator=g))
+    x = (offs[k] + z) * sd
+    near = torch.rand(n_groups, generator=g) < 0.25
+    mult = torch.empty(n_groups).uniform_(2.9, 3.3, generator=g)
+    x[near, 0] = (offs[k[near, 0]] + mult[near] * 1.0) * sd[near, 0]
+    return x.reshape(-1).to(torch.bfloat16).view(torch.int16).numpy().view(np.uint16).copy()
+
+
+@pytest.mark.parametrize("bits", [4, 2])
+def test_nbit_offset_and_near_threshold_groups_vs_oracle(cuda, bits):
+    n_groups = 1 << 16
+    xb = _offset_and_threshold_groups(n_groups, 99 + bits)
+    n = xb.size
+    u = torch.rand(n, generator=torch.Generator().manual_seed(6))
+    x = torch.from_numpy(xb.view(np.int16)).view(torch.bfloat16)
+    enc = nb.encode_groups(x.to(cuda), bits, 3.0, uniform=u.to(cuda))
+    osc, ocodes, oidx, ovals = oracle.nbit_encode(xb, bits, u.numpy(), 3.0)
+    assert oidx.size > n_groups // 50  # the near-threshold elements produce outliers
+    assert np.array_equal(bits_of(enc.scales), osc)
+    assert np.array_equal(enc.codes[: ocodes.size].cpu().numpy(), ocodes)
+    idx, val, total = nb.flatten_outliers(enc)
+    t = int(total.item())
+    assert t == oidx.size and np.array_equal(idx[:t].cpu().numpy(), oidx)
+    assert np.array_equal(val[:t].cpu().numpy().view(np.uint16), ovals)
+
+
 @pytest.mark.parametrize("bits", [2, 4])
 def test_nbit_philox_dither_matches_oracle(cuda, bits):
     n = 64 * 8192
@@ -180,6 +214,30 @@ def test_nbit_philox_dither_matches_oracle(cuda, bits):
     osc, ocodes, oidx, ovals = oracle.nbit_encode(bits_of(x), bits, u, 3.0)
     assert np.array_equal(bits_of(enc.scales), osc)
     assert np.array_equal(enc.codes[: ocodes.size].cpu().numpy(), ocodes)
+
+
+def test_nbit_flatten_spans_scan_tiles(cuda):
+    """More buckets than one scan tile (4096): flat list and offsets against the oracle."""
+    n = 5 * 4096 * 1024 + 32 * 77
+    x = rand_bf16(n, 61, "outliers")
+    u = torch.rand(n, generator=torch.Generator().manual_seed(8))
+    enc = nb.encode_groups(x.to(cuda), 4, 3.0, uniform=u.to(cuda))
+    _, _, oidx, ovals = oracle.nbit_encode(bits_of(x), 4, u.numpy(), 3.0)
+    nbk = enc.n_buckets
+    assert nbk > 4 * 4096
+    offsets = torch.empty(_native.nbit_flatten_scratch_ints(nbk), dtype=torch.int32, device=cuda)
+    idx = torch.empty(nbk * enc.bucket_cap, dtype=torch.int32, device=cuda)
+    val = torch.empty(nbk * enc.bucket_cap, dtype=torch.int16, device=cuda)
+    total = torch.empty(1, dtype=torch.int32, device=cuda)
+    _native.nbit_outliers_flatten(enc.bucket_counts, enc.bucket_entries, enc.bucket_cap, nbk, offsets, idx, val,
+                                  total)
+    t = int(total.item())
+    assert t == oidx.size
+    assert np.array_equal(idx[:t].cpu().numpy(), oidx)
+    assert np.array_equal(val[:t].cpu().numpy().view(np.uint16), ovals)
+    counts = enc.bucket_counts[:nbk].cpu().numpy().astype(np.int64)
+    want = np.concatenate([[0], np.cumsum(counts)])
+    assert np.array_equal(offsets[: nbk + 1].cpu().numpy(), want)
 
 
 def test_nbit_bucket_overflow_is_flagged(cuda):
