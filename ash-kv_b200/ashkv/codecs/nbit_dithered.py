@@ -13,7 +13,10 @@ distribution and seeding policy).  Passing ``uniform=`` (the U tensor the
 reference would draw) reproduces the reference's output bit for bit.
 
 Device-resident entry points (no host copies): :func:`encode_groups`,
-:func:`decode_groups` and :class:`NBitEncoded`.
+:func:`decode_groups` and :class:`NBitEncoded`.  Host-buffer entry points:
+``encode_pinned`` / ``decode_pinned`` take and fill host tensors (pinned for
+asynchronous DMA) holding the same blob as ``encode``/``decode``, with no
+copy on the host.
 """
 from __future__ import annotations
 
@@ -115,6 +118,33 @@ def flatten_outliers(enc: NBitEncoded) -> tuple[torch.Tensor, torch.Tensor, torc
     return idx, val, total
 
 
+def _host_flat(t: torch.Tensor, dtype: torch.dtype) -> torch.Tensor:
+    """A contiguous host tensor viewed as a flat tensor of ``dtype`` (same bytes)."""
+    if t.is_cuda:
+        raise ValueError("expected a host tensor")
+    if not t.is_contiguous():
+        raise ValueError("host buffers must be contiguous")
+    flat = t.reshape(-1)
+    if flat.dtype != dtype:
+        flat = flat.view(torch.uint8).view(dtype)
+    return flat
+
+
+def _host_out(out: Optional[torch.Tensor], n: int, dtype: torch.dtype) -> torch.Tensor:
+    if out is None:
+        return torch.empty(max(n, 1), dtype=dtype, pin_memory=torch.cuda.is_available())
+    flat = _host_flat(out, dtype)
+    if flat.numel() < n:
+        raise ValueError(f"output buffer holds {flat.numel()} elements, {n} needed")
+    return flat
+
+
+def _host_bytes(data: bytes, out: Optional[torch.Tensor]) -> torch.Tensor:
+    o = _host_out(out, len(data), torch.uint8)
+    o[:len(data)].numpy()[:] = np.frombuffer(data, dtype=np.uint8)
+    return o[:len(data)]
+
+
 def _sha8(raw: bytes) -> int:
     return int.from_bytes(hashlib.sha256(raw).digest()[:8], "little", signed=False)
 
@@ -187,6 +217,92 @@ class DitheredNBitCodec:
         h_out[o:o + n_codes].copy_(enc.codes[:n_codes], non_blocking=True)
         torch.cuda.current_stream(dev).synchronize()
         return _staging.to_bytes(h_out, struct.pack("<II", num_tokens, n_out))
+
+    # ---------------------------------------------------------------- host tensors
+    def encode_pinned(self, src: torch.Tensor, out: Optional[torch.Tensor] = None, *, uniform=None) -> torch.Tensor:
+        """Encode a contiguous host tensor of bf16 values into the blob ``encode``
+        returns for the same bytes, written into the host uint8 tensor ``out``
+        (allocated pinned when None); returns ``out[:blob_size]``.
+
+        With pinned buffers the host<->device transfers are DMA copies straight
+        from ``src`` and into ``out``; the call returns once ``out`` is complete."""
+        self._encode_calls += 1
+        flat = _host_flat(src, torch.bfloat16)
+        L = self._hidden_dim
+        num_tokens = flat.numel() // L
+        header = struct.pack("<II", num_tokens, 0)
+        if num_tokens == 0:
+            return _host_bytes(header, out)
+        if L % self._group_size:
+            raise RuntimeError(f"shape '[{num_tokens}, {L // self._group_size}, {self._group_size}]' is invalid "
+                               f"for input of size {num_tokens * L}")
+        dev = _staging.device()
+        n_elems = num_tokens * L
+        d_src = torch.empty(n_elems, dtype=torch.bfloat16, device=dev)
+        d_src.copy_(flat[:n_elems], non_blocking=True)
+        u = None
+        if uniform is not None:
+            u = torch.as_tensor(uniform, dtype=torch.float32).reshape(-1)
+            if u.numel() != n_elems:
+                raise ValueError(f"uniform has {u.numel()} values, expected {n_elems}")
+            u = u.to(dev, non_blocking=True).contiguous()
+        enc = encode_groups(d_src, self._bits, self._sigma, uniform=u, seed=self._seed())
+        idx, val, total = flatten_outliers(enc)
+        n_out = int(total.item())
+        n_groups = enc.n_groups
+        n_codes = n_groups * 32 * self._bits // 8
+        size = 8 + 2 * n_groups + 6 * n_out + n_codes
+        out = _host_out(out, size, torch.uint8)
+        out[:8].numpy()[:] = np.frombuffer(struct.pack("<II", num_tokens, n_out), dtype=np.uint8)
+        o = 8
+        out[o:o + 2 * n_groups].copy_(enc.scales.view(torch.uint8), non_blocking=True); o += 2 * n_groups
+        if n_out:
+            out[o:o + 4 * n_out].copy_(idx[:n_out].view(torch.uint8), non_blocking=True); o += 4 * n_out
+            out[o:o + 2 * n_out].copy_(val[:n_out].view(torch.uint8), non_blocking=True); o += 2 * n_out
+        out[o:o + n_codes].copy_(enc.codes[:n_codes], non_blocking=True)
+        torch.cuda.current_stream(dev).synchronize()
+        return out[:size]
+
+    def decode_pinned(self, blob: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """Decode a blob held in a host uint8 tensor into the host bf16 tensor
+        ``out`` (allocated pinned when None); returns ``out[:n]``, the values
+        ``decode`` returns for the same bytes."""
+        self._decode_calls += 1
+        b = _host_flat(blob, torch.uint8)
+        if b.numel() < 8:
+            return _host_out(out, 0, torch.bfloat16)[:0]
+        num_tokens, n_out = struct.unpack("<II", b[:8].numpy().tobytes())
+        if num_tokens == 0:
+            return _host_out(out, 0, torch.bfloat16)[:0]
+        n_groups = num_tokens * (self._hidden_dim // self._group_size)
+        n_codes = n_groups * 32 * self._bits // 8
+        need = 8 + 2 * n_groups + 6 * n_out + n_codes
+        if b.numel() < need:
+            raise RuntimeError(f"N-bit blob too short: {b.numel()} bytes, layout needs {need}")
+        dev = _staging.device()
+        # one DMA per blob section, each into its own (aligned) device buffer
+        o = 8
+        d_sc = torch.empty(2 * n_groups, dtype=torch.uint8, device=dev)
+        d_sc.copy_(b[o:o + 2 * n_groups], non_blocking=True); o += 2 * n_groups
+        d_idx = torch.empty(max(4 * n_out, 4), dtype=torch.uint8, device=dev)
+        d_val = torch.empty(max(2 * n_out, 2), dtype=torch.uint8, device=dev)
+        if n_out:
+            d_idx[:4 * n_out].copy_(b[o:o + 4 * n_out], non_blocking=True); o += 4 * n_out
+            d_val[:2 * n_out].copy_(b[o:o + 2 * n_out], non_blocking=True); o += 2 * n_out
+        codes = torch.empty(max(n_codes, 16), dtype=torch.uint8, device=dev)
+        codes[:n_codes].copy_(b[o:o + n_codes], non_blocking=True)
+        dv = torch.empty(n_groups * 32, dtype=torch.bfloat16, device=dev)
+        status = torch.zeros(1, dtype=torch.int32, device=dev)
+        _native.nbit_decode_flat(d_sc.view(torch.bfloat16), codes, n_groups, self._bits,
+                                 d_idx.view(torch.int32) if n_out else None,
+                                 d_val.view(torch.int16) if n_out else None, n_out, dv, status)
+        out = _host_out(out, n_groups * 32, torch.bfloat16)
+        out[:n_groups * 32].copy_(dv, non_blocking=True)
+        st = status.to("cpu", non_blocking=True)
+        torch.cuda.current_stream(dev).synchronize()
+        if int(st.item()) & _native.FLAG_INDEX_RANGE:
+            raise IndexError(f"outlier index out of range for a decoded size of {n_groups * 32} elements")
+        return out[:n_groups * 32]
 
     def decode(self, target_bytes: bytes) -> bytes:
         self._decode_calls += 1

@@ -10,9 +10,15 @@ both back to bf16.
 ``value``  — bf16 bytes of K+V pushed through encode AND decode per second,
              inputs resident in HBM (device-timed with CUDA events), summed
              over ranks (weak scaling: every rank owns its own K/V shard).
-``e2e``    — the same metric through the public bytes API
-             (``DitheredNBitCodec.encode(bytes)`` / ``.decode(bytes)``) with
-             host buffers, host<->device copies inside the timed region.
+``e2e``    — the same metric through the codec's host-buffer API
+             (``DitheredNBitCodec.encode_pinned`` / ``.decode_pinned``): K and V
+             start in pinned host memory, every step copies them to the device,
+             encodes, writes the reference blob into pinned host memory, copies
+             the blobs back, decodes, and reads the bf16 result back to the
+             host -- all inside the timed region.
+``e2e_bytes_api`` — the same through ``encode(bytes)`` / ``decode(bytes)``
+             (Python ``bytes`` in and out: adds host copies into pinned staging
+             and into freshly allocated result objects).
 ``roofline`` — the encode kernel (the dominant one): algorithmic bytes per
              launch / its average CUDA-event duration vs the measured HBM copy
              peak.
@@ -285,7 +291,8 @@ def main() -> None:
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ashkv", choices=["ashkv", "reference"])
-    ap.add_argument("--e2e-steps", type=int, default=3)
+    ap.add_argument("--e2e-steps", type=int, default=10)
+    ap.add_argument("--e2e-bytes-steps", type=int, default=2)
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--ref-seconds", type=float, default=5.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -357,12 +364,17 @@ def main() -> None:
     dec_ms = statistics.mean(e[2].elapsed_time(e[3]) for e in evs)
     n_out = int(encK.bucket_counts.sum().item())
 
-    # end-to-end through the bytes API (host buffers)
+    # end-to-end through the host-buffer API (pinned host memory in and out)
     codec = DitheredNBitCodec(hidden_dim=HEAD_DIM, group_size=32, sigma=SIGMA, bits=BITS)
-    hostK = K.cpu().view(torch.int16).numpy().tobytes()
-    hostV = V.cpu().view(torch.int16).numpy().tobytes()
-    blob = codec.encode(hostK)
-    codec.decode(blob)  # warm
+    pinK = K.cpu().pin_memory()
+    pinV = V.cpu().pin_memory()
+    n_groups = ELEMS // 32
+    blob_cap = 8 + 2 * n_groups + 6 * n_groups * nb.max_outliers_per_group(SIGMA) + n_groups * 32 * BITS // 8
+    blobK = torch.empty(blob_cap, dtype=torch.uint8, pin_memory=True)
+    blobV = torch.empty(blob_cap, dtype=torch.uint8, pin_memory=True)
+    decK = torch.empty(ELEMS, dtype=torch.bfloat16, pin_memory=True)
+    decV = torch.empty(ELEMS, dtype=torch.bfloat16, pin_memory=True)
+    codec.decode_pinned(codec.encode_pinned(pinK, blobK), decK)  # warm
     h2d = d2h = 0
     t_e2e = 0.0
     torch.cuda.synchronize()
@@ -370,23 +382,38 @@ def main() -> None:
         dist.barrier()
     for _ in range(args.e2e_steps):
         t0 = time.perf_counter()
-        bk = codec.encode(hostK)
-        bv = codec.encode(hostV)
-        dk = codec.decode(bk)
-        dv = codec.decode(bv)
+        bk = codec.encode_pinned(pinK, blobK)
+        bv = codec.encode_pinned(pinV, blobV)
+        dk = codec.decode_pinned(bk, decK)
+        dv = codec.decode_pinned(bv, decV)
         t_e2e += time.perf_counter() - t0
-        h2d = len(hostK) + len(hostV) + (len(bk) - 8) + (len(bv) - 8)
-        d2h = (len(bk) - 8) + (len(bv) - 8) + len(dk) + len(dv)
+        h2d = 2 * ELEMS * 2 + (bk.numel() - 8) + (bv.numel() - 8)
+        d2h = bk.numel() + bv.numel() + 2 * (dk.numel() + dv.numel())
+
+    # the same through the bytes API
+    hostK = pinK.view(torch.int16).numpy().tobytes()
+    hostV = pinV.view(torch.int16).numpy().tobytes()
+    codec.decode(codec.encode(hostK))  # warm
+    t_bytes = 0.0
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    for _ in range(args.e2e_bytes_steps):
+        t0 = time.perf_counter()
+        codec.decode(codec.encode(hostK))
+        codec.decode(codec.encode(hostV))
+        t_bytes += time.perf_counter() - t0
 
     # max over ranks
-    t = torch.tensor([elapsed_ms, t_e2e], dtype=torch.float64, device=dev)
+    t = torch.tensor([elapsed_ms, t_e2e, t_bytes], dtype=torch.float64, device=dev)
     if dist:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    elapsed_ms, t_e2e = float(t[0]), float(t[1])
+    elapsed_ms, t_e2e, t_bytes = float(t[0]), float(t[1]), float(t[2])
 
     bytes_per_step = 2 * ELEMS * 2  # bf16 K + V through encode and decode
     value = world * bytes_per_step * args.steps / (elapsed_ms / 1e3) / 1e9
     e2e_value = world * bytes_per_step * args.e2e_steps / t_e2e / 1e9
+    e2e_bytes_value = world * bytes_per_step * args.e2e_bytes_steps / t_bytes / 1e9 if t_bytes > 0 else None
     enc_alg_bytes = ELEMS * 2 + ELEMS * BITS // 8 + (ELEMS // 32) * 2 + 4 * n_out + 4 * nb._native.nbit_bucket_count(ELEMS // 32)
     achieved = enc_alg_bytes / (enc_ms / 1e3) / 1e9
     dec_alg_bytes = ELEMS * BITS // 8 + (ELEMS // 32) * 2 + 4 * nb._native.nbit_bucket_count(ELEMS // 32) + 4 * n_out + ELEMS * 2
@@ -418,7 +445,11 @@ def main() -> None:
             "decode": {"kernel": "nbit_decode_kernel<4>", "avg_launch_ms": round(dec_ms, 4),
                        "achieved_gbs": round(dec_achieved, 1), "frac": round(dec_achieved / peak, 4)},
             "e2e": {"value": round(e2e_value, 3), "unit": "GB/s", "h2d_bytes_per_step": h2d,
-                    "d2h_bytes_per_step": d2h},
+                    "d2h_bytes_per_step": d2h, "api": "DitheredNBitCodec.encode_pinned/decode_pinned",
+                    "steps": args.e2e_steps},
+            "e2e_bytes_api": None if e2e_bytes_value is None else
+            {"value": round(e2e_bytes_value, 3), "unit": "GB/s", "api": "DitheredNBitCodec.encode/decode(bytes)",
+             "steps": args.e2e_bytes_steps},
             "gpu_launches": 4 * args.steps,
             "clocks": clocks.summary(),
             "cpu_baseline": cpu,

@@ -298,6 +298,24 @@ def test_nbit_config2_full_size_properties(cuda):
         assert np.array_equal(codes[lo // 2:(lo + 8192) // 2], ocodes)
 
 
+@pytest.mark.parametrize("bits,hidden", [(4, 128), (2, 128), (8, 64), (4, 32)])
+def test_nbit_pinned_api_matches_bytes_api(cuda, bits, hidden):
+    x = rand_bf16(257 * hidden, 71, "outliers")
+    data = bits_of(x).tobytes()
+    a, b = DitheredNBitCodec(hidden_dim=hidden, bits=bits), DitheredNBitCodec(hidden_dim=hidden, bits=bits)
+    for _ in range(2):  # the second call checks the per-call seed stays in step
+        blob = a.encode(data)
+        pblob = b.encode_pinned(x.view(torch.int16).pin_memory())
+        assert pblob.numpy().tobytes() == blob
+        out = torch.empty(x.numel() + 8, dtype=torch.bfloat16, pin_memory=True)
+        dec = b.decode_pinned(pblob, out)
+        assert dec.view(torch.int16).numpy().tobytes() == a.decode(blob)
+    c = DitheredINT2Codec()
+    u = torch.rand(x.numel() // 128 * 128)
+    assert c.encode_pinned(x, uniform=u).numpy().tobytes() == c.encode(data, uniform=u)
+    assert DitheredNBitCodec().encode_pinned(torch.empty(0, dtype=torch.bfloat16)).numpy().tobytes() == bytes(8)
+
+
 def test_nbit_codec_seeding_policy(cuda):
     x = bits_of(rand_bf16(4 * 128, 51)).tobytes()
     c = DitheredNBitCodec()
