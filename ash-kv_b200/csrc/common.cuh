@@ -193,6 +193,13 @@ __device__ __forceinline__ float max3_abs_nan(float a, float b, float c) {
   return r;
 }
 
+// fp32 pair -> packed bf16x2, round to nearest even (NaN -> 0x7FFF).
+__device__ __forceinline__ uint32_t f32x2_to_bf16x2_pk(f2 v) {
+  float lo, hi;
+  upk2(v, lo, hi);
+  return f32x2_to_bf16x2(lo, hi);
+}
+
 // Correctly rounded division by a divisor shared by many dividends.
 // Per divisor b: y_hi = RN(1/b), y_lo = RN((1 - b*y_hi) * y_hi), so that
 // y_hi + y_lo approximates 1/b to ~2^-47.  Per dividend a:
@@ -224,6 +231,78 @@ __device__ __forceinline__ f2 div2_rn(f2 a, f2 yhi, f2 ylo, f2 nb) {
   return fma2(r, yhi, q0);
 }
 
+
+// ---------------------------------------------------------------- INT8 codec arithmetic
+// Shared by the row kernels (int8_codec.cu) and the page kernels (pages.cu);
+// restates ashkv/codecs/int8.py:70-80 (encode) and :110-115 (decode).
+//   code = sat_int8(trunc(q + copysign(0.5, q))),  q = RN(s / am)   (NaN -> 0)
+// (the reference adds +0.5 when q > 0 and -0.5 otherwise; the two differ only
+// at q = +0, where both truncate to 0).  s / am uses the per-row reciprocal
+// pair and Markstein's correction when `fast` (am within [2^-100, 2^100] and
+// s finite for every element of the row), __fdiv_rn otherwise.
+struct Int8Div {
+  float am;
+  Recip y;
+  bool fast;
+};
+__device__ __forceinline__ Int8Div int8_div(float am, bool s_finite) {
+  Int8Div d;
+  d.am = am;
+  d.y = make_recip(am);
+  d.fast = s_finite && recip_ok(am);
+  return d;
+}
+__device__ __forceinline__ int32_t int8_round_sat(float q) {
+  const float r = __fadd_rn(q, copysignf(0.5f, q));
+  int32_t c;
+  asm("cvt.rzi.sat.s8.f32 %0, %1;" : "=r"(c) : "f"(r));  // NaN -> 0
+  return c;
+}
+__device__ __forceinline__ int32_t int8_code(float s, const Int8Div& d) {
+  return int8_round_sat(d.fast ? div_rn(s, d.am, d.y) : __fdiv_rn(s, d.am));
+}
+// Four bf16 inputs (two words, element 0 in the low half of w0) -> four
+// codes packed little-endian: s = bf16(x * 127) (exact product, one rounding).
+__device__ __forceinline__ uint32_t int8_codes4_bf16(uint32_t w0, uint32_t w1, const Int8Div& d) {
+  const f2 k127 = pk2(127.0f, 127.0f);
+  const uint32_t s01 = f32x2_to_bf16x2_pk(mul2(pk2(bf16lo(w0), bf16hi(w0)), k127));
+  const uint32_t s23 = f32x2_to_bf16x2_pk(mul2(pk2(bf16lo(w1), bf16hi(w1)), k127));
+  const f2 Q0 = pk2(bf16lo(s01), bf16hi(s01)), Q1 = pk2(bf16lo(s23), bf16hi(s23));
+  float q[4];
+  if (d.fast) {
+    const f2 yhi = pk2(d.y.hi, d.y.hi), ylo = pk2(d.y.lo, d.y.lo), nb = pk2(-d.am, -d.am);
+    upk2(div2_rn(Q0, yhi, ylo, nb), q[0], q[1]);
+    upk2(div2_rn(Q1, yhi, ylo, nb), q[2], q[3]);
+  } else {
+    upk2(Q0, q[0], q[1]);
+    upk2(Q1, q[2], q[3]);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) q[k] = __fdiv_rn(q[k], d.am);
+  }
+  uint32_t out = 0;
+#pragma unroll
+  for (int k = 0; k < 4; ++k) out |= (uint32_t(int8_round_sat(q[k])) & 0xFFu) << (8 * k);
+  return out;
+}
+// Decode: v = RN(RN(float(code) * scale) / 127).  `fast` when the scale is
+// finite and in [2^-90, 2^90] (products are 0 or inside Markstein's range;
+// scale > 0 keeps the sign of zero products).
+__device__ __forceinline__ bool int8_dec_fast(float scale) { return scale >= 0x1p-90f && scale <= 0x1p+90f; }
+__device__ __forceinline__ float int8_dequant(int32_t c, float scale, bool fast) {
+  const float p = __fmul_rn(float(c), scale);
+  return fast ? div_rn(p, 127.0f, make_recip(127.0f)) : __fdiv_rn(p, 127.0f);
+}
+// Four int8 codes (one word, code 0 in the low byte) -> float(code) exactly,
+// without an int->float conversion: 0x4B400000 | (byte ^ 0x80) is the float
+// 1.5*2^23 + 128 + code.
+__device__ __forceinline__ void int8x4_to_f2(uint32_t w, f2& lo, f2& hi) {
+  const uint32_t b = w ^ 0x80808080u;
+  const f2 nbias = pk2(-12583040.0f, -12583040.0f);  // -(1.5*2^23 + 128)
+  lo = add2(pk2(__uint_as_float(__byte_perm(b, 0x4B400000u, 0x7640)),
+                __uint_as_float(__byte_perm(b, 0x4B400000u, 0x7641))), nbias);
+  hi = add2(pk2(__uint_as_float(__byte_perm(b, 0x4B400000u, 0x7642)),
+                __uint_as_float(__byte_perm(b, 0x4B400000u, 0x7643))), nbias);
+}
 
 // ---------------------------------------------------------------- TMA / mbarrier
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {

@@ -63,12 +63,12 @@ __device__ __forceinline__ float scaled127(float x, bool fp32_product) {
   else return __bfloat162float(__float2bfloat16_rn(p));
 }
 
-__device__ __forceinline__ int32_t quant_code(float s, float am) {
-  float q = __fdiv_rn(s, am);
-  float r = __fadd_rn(q, q > 0.0f ? 0.5f : -0.5f);
-  int32_t c;
-  asm("cvt.rzi.sat.s8.f32 %0, %1;" : "=r"(c) : "f"(r));  // NaN -> 0
-  return c;
+// s = x * 127 stays finite for every x of a row whose absmax is am: always for
+// an fp32 product and for bf16 rows in the fast divisor range; fp16 rows need
+// 127 * am below the fp16 maximum.
+template <bool FP16>
+__device__ __forceinline__ bool products_finite(float am, bool fp32_product) {
+  return !FP16 || fp32_product || am < 515.0f;
 }
 
 __device__ __forceinline__ uint8_t* scale_addr(uint8_t* base, int64_t r, int32_t sps, int64_t slot_stride) {
@@ -114,22 +114,28 @@ __global__ void __launch_bounds__(256) int8_encode_kernel(const Int8EncParams p)
 
   uint8_t* out = p.codes + r * p.codes_stride;
   const bool f32p = p.fp32_product != 0;
+  const Int8Div d = int8_div(am, products_finite<FP16>(am, f32p));
 #pragma unroll
   for (int c = 0; c < NCH; ++c) {
     const uint32_t w[4] = {chunk[c].x, chunk[c].y, chunk[c].z, chunk[c].w};
     uint32_t packed[2];
+    if (!FP16 && !f32p) {
+      packed[0] = int8_codes4_bf16(w[0], w[1], d);
+      packed[1] = int8_codes4_bf16(w[2], w[3], d);
+    } else {
 #pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      uint32_t b = 0;
+      for (int h = 0; h < 2; ++h) {
+        uint32_t b = 0;
 #pragma unroll
-      for (int k = 0; k < 2; ++k) {
-        const uint32_t word = w[h * 2 + k];
-        const int32_t c0 = quant_code(scaled127<FP16>(in_lo<FP16>(word), f32p), am);
-        const int32_t c1 = quant_code(scaled127<FP16>(in_hi<FP16>(word), f32p), am);
-        b |= (uint32_t(c0) & 0xFFu) << (16 * k);
-        b |= (uint32_t(c1) & 0xFFu) << (16 * k + 8);
+        for (int k = 0; k < 2; ++k) {
+          const uint32_t word = w[h * 2 + k];
+          const int32_t c0 = int8_code(scaled127<FP16>(in_lo<FP16>(word), f32p), d);
+          const int32_t c1 = int8_code(scaled127<FP16>(in_hi<FP16>(word), f32p), d);
+          b |= (uint32_t(c0) & 0xFFu) << (16 * k);
+          b |= (uint32_t(c1) & 0xFFu) << (16 * k + 8);
+        }
+        packed[h] = b;
       }
-      packed[h] = b;
     }
     *reinterpret_cast<uint2*>(out + (int64_t(c) * TEAM + lane_in_team) * 8) = make_uint2(packed[0], packed[1]);
   }
@@ -156,16 +162,13 @@ __global__ void __launch_bounds__(256) int8_encode_generic_kernel(const Int8EncP
     *reinterpret_cast<uint16_t*>(sp) = p.scale_fp16 ? f32_to_f16(am) : f32_to_bf16(am);
   }
   uint8_t* out = p.codes + r * p.codes_stride;
+  const Int8Div d = int8_div(am, products_finite<FP16>(am, p.fp32_product != 0));
   for (int i = lane; i < p.row_len; i += 32) {
     const uint32_t w = row[i];
-    out[i] = uint8_t(quant_code(scaled127<FP16>(in_lo<FP16>(w), p.fp32_product != 0), am) & 0xFF);
+    out[i] = uint8_t(int8_code(scaled127<FP16>(in_lo<FP16>(w), p.fp32_product != 0), d) & 0xFF);
   }
 }
 
-__device__ __forceinline__ float dequant(int32_t c, float scale) {
-  // c * scale is exact in fp32 (8-bit code times an 8/11-bit significand).
-  return __fdiv_rn(__fmul_rn(float(c), scale), 127.0f);
-}
 
 __device__ __forceinline__ uint16_t out_bits(float v, bool fp16) {
   // Triton casts to bf16 first, then the store converts to the pointer's type.
@@ -186,6 +189,9 @@ __global__ void __launch_bounds__(256) int8_decode_kernel(const Int8DecParams p)
   const int64_t dst_row = p.row_index ? p.row_index[r] : r;
   uint16_t* out = p.dst + dst_row * p.dst_stride;
   const bool f16 = p.dst_fp16 != 0;
+  const bool fast = int8_dec_fast(scale);
+  const Recip y = make_recip(127.0f);
+  const f2 S = pk2(scale, scale), YHI = pk2(y.hi, y.hi), YLO = pk2(y.lo, y.lo), N127 = pk2(-127.0f, -127.0f);
 #pragma unroll
   for (int c = 0; c < NCH; ++c) {
     const int64_t e0 = (int64_t(c) * TEAM + lane_in_team) * 8;
@@ -194,12 +200,20 @@ __global__ void __launch_bounds__(256) int8_decode_kernel(const Int8DecParams p)
     uint32_t o[4];
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
+      f2 F[2];  // float(code) of bytes 0,1 and 2,3 of ww[h]
+      int8x4_to_f2(ww[h], F[0], F[1]);
 #pragma unroll
       for (int k = 0; k < 2; ++k) {
-        const int32_t c0 = int32_t(int8_t((ww[h] >> (16 * k)) & 0xFF));
-        const int32_t c1 = int32_t(int8_t((ww[h] >> (16 * k + 8)) & 0xFF));
-        o[h * 2 + k] = uint32_t(out_bits(dequant(c0, scale), f16)) |
-                       (uint32_t(out_bits(dequant(c1, scale), f16)) << 16);
+        float a, b;
+        if (fast) {
+          upk2(div2_rn(mul2(F[k], S), YHI, YLO, N127), a, b);
+        } else {
+          upk2(F[k], a, b);
+          a = __fdiv_rn(__fmul_rn(a, scale), 127.0f);
+          b = __fdiv_rn(__fmul_rn(b, scale), 127.0f);
+        }
+        o[h * 2 + k] = f16 ? (uint32_t(out_bits(a, true)) | (uint32_t(out_bits(b, true)) << 16))
+                           : f32x2_to_bf16x2(a, b);
       }
     }
     *reinterpret_cast<uint4*>(out + e0) = make_uint4(o[0], o[1], o[2], o[3]);
@@ -216,8 +230,9 @@ __global__ void __launch_bounds__(256) int8_decode_generic_kernel(const Int8DecP
   const uint8_t* in = p.codes + r * p.codes_stride;
   const int64_t dst_row = p.row_index ? p.row_index[r] : r;
   uint16_t* out = p.dst + dst_row * p.dst_stride;
+  const bool fast = int8_dec_fast(scale);
   for (int i = lane; i < p.row_len; i += 32)
-    out[i] = out_bits(dequant(int32_t(int8_t(in[i])), scale), p.dst_fp16 != 0);
+    out[i] = out_bits(int8_dequant(int32_t(int8_t(in[i])), scale, fast), p.dst_fp16 != 0);
 }
 
 template <typename P, typename KFast>

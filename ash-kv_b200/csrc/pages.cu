@@ -75,36 +75,22 @@ __device__ __forceinline__ void encode_row(const uint16_t* src, int8_t* codes, u
   am = fmaxf(am, 1e-8f);
   if (lane == 0) *scale = f32_to_f16(am);
   if (!on) return;
+  // bf16 x * 127 overflows only when am > 2.6e36, outside the fast divisor range
+  const Int8Div d = int8_div(am, true);
 #pragma unroll
   for (int c = 0; c < NCH; ++c) {
     const uint32_t w[4] = {ch[c].x, ch[c].y, ch[c].z, ch[c].w};
-    uint32_t pk[2];
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      uint32_t b = 0;
-#pragma unroll
-      for (int k = 0; k < 2; ++k) {
-        const uint32_t word = w[2 * h + k];
-#pragma unroll
-        for (int e = 0; e < 2; ++e) {
-          const float x = e ? bf16hi(word) : bf16lo(word);
-          const float s = __bfloat162float(__float2bfloat16_rn(__fmul_rn(x, 127.0f)));
-          const float q = __fdiv_rn(s, am);
-          const float r = __fadd_rn(q, q > 0.0f ? 0.5f : -0.5f);
-          int32_t cv;
-          asm("cvt.rzi.sat.s8.f32 %0, %1;" : "=r"(cv) : "f"(r));
-          b |= (uint32_t(cv) & 0xFFu) << (16 * k + 8 * e);
-        }
-      }
-      pk[h] = b;
-    }
-    *reinterpret_cast<uint2*>(codes + (c * kTeam + lane) * 8) = make_uint2(pk[0], pk[1]);
+    *reinterpret_cast<uint2*>(codes + (c * kTeam + lane) * 8) =
+        make_uint2(int8_codes4_bf16(w[0], w[1], d), int8_codes4_bf16(w[2], w[3], d));
   }
 }
 
 template <int NCH, bool HALF>
 __device__ __forceinline__ void decode_row(const int8_t* codes, float scale, uint16_t* dst, int lane) {
   if (HALF && lane >= 16) return;
+  const bool fast = int8_dec_fast(scale);
+  const Recip y = make_recip(127.0f);
+  const f2 S = pk2(scale, scale), YHI = pk2(y.hi, y.hi), YLO = pk2(y.lo, y.lo), N127 = pk2(-127.0f, -127.0f);
 #pragma unroll
   for (int c = 0; c < NCH; ++c) {
     const int e0 = (c * kTeam + lane) * 8;
@@ -112,13 +98,20 @@ __device__ __forceinline__ void decode_row(const int8_t* codes, float scale, uin
     const uint32_t ww[2] = {w.x, w.y};
     uint32_t o[4];
 #pragma unroll
-    for (int h = 0; h < 2; ++h)
-#pragma unroll
-      for (int k = 0; k < 2; ++k) {
-        const float a = __fdiv_rn(__fmul_rn(float(int8_t((ww[h] >> (16 * k)) & 0xFF)), scale), 127.0f);
-        const float b = __fdiv_rn(__fmul_rn(float(int8_t((ww[h] >> (16 * k + 8)) & 0xFF)), scale), 127.0f);
-        o[2 * h + k] = f32x2_to_bf16x2(a, b);
+    for (int h = 0; h < 2; ++h) {
+      f2 F0, F1;  // float(code) of bytes 0,1 and 2,3 of ww[h]
+      int8x4_to_f2(ww[h], F0, F1);
+      if (fast) {
+        o[2 * h] = f32x2_to_bf16x2_pk(div2_rn(mul2(F0, S), YHI, YLO, N127));
+        o[2 * h + 1] = f32x2_to_bf16x2_pk(div2_rn(mul2(F1, S), YHI, YLO, N127));
+      } else {
+        float a, b;
+        upk2(F0, a, b);
+        o[2 * h] = f32x2_to_bf16x2(__fdiv_rn(__fmul_rn(a, scale), 127.0f), __fdiv_rn(__fmul_rn(b, scale), 127.0f));
+        upk2(F1, a, b);
+        o[2 * h + 1] = f32x2_to_bf16x2(__fdiv_rn(__fmul_rn(a, scale), 127.0f), __fdiv_rn(__fmul_rn(b, scale), 127.0f));
       }
+    }
     *reinterpret_cast<uint4*>(dst + e0) = make_uint4(o[0], o[1], o[2], o[3]);
   }
 }
