@@ -30,6 +30,8 @@ namespace {
 
 constexpr int kThreads = 256;
 constexpr int kTeam = 32;  // one warp per row
+constexpr int kRowsInFlight = 4;  // decode: rows whose codes a warp loads before converting
+
 
 struct PagesParams {
   const uint64_t* layer_k;
@@ -85,17 +87,32 @@ __device__ __forceinline__ void encode_row(const uint16_t* src, int8_t* codes, u
   }
 }
 
+// A row's codes as held by one lane (NCH chunks of 8 bytes) and its scale.
+template <int NCH>
+struct RowCodes {
+  uint2 w[NCH];
+  float scale;
+};
 template <int NCH, bool HALF>
-__device__ __forceinline__ void decode_row(const int8_t* codes, float scale, uint16_t* dst, int lane) {
+__device__ __forceinline__ void load_row_codes(const int8_t* codes, const uint16_t* scale, int lane,
+                                               RowCodes<NCH>& rc) {
+  rc.scale = f16_to_f32(*scale);
   if (HALF && lane >= 16) return;
+#pragma unroll
+  for (int c = 0; c < NCH; ++c) rc.w[c] = *reinterpret_cast<const uint2*>(codes + (c * kTeam + lane) * 8);
+}
+
+template <int NCH, bool HALF>
+__device__ __forceinline__ void decode_row(const RowCodes<NCH>& rc, uint16_t* dst, int lane) {
+  if (HALF && lane >= 16) return;
+  const float scale = rc.scale;
   const bool fast = int8_dec_fast(scale);
   const Recip y = make_recip(127.0f);
   const f2 S = pk2(scale, scale), YHI = pk2(y.hi, y.hi), YLO = pk2(y.lo, y.lo), N127 = pk2(-127.0f, -127.0f);
 #pragma unroll
   for (int c = 0; c < NCH; ++c) {
     const int e0 = (c * kTeam + lane) * 8;
-    const uint2 w = *reinterpret_cast<const uint2*>(codes + e0);
-    const uint32_t ww[2] = {w.x, w.y};
+    const uint32_t ww[2] = {rc.w[c].x, rc.w[c].y};
     uint32_t o[4];
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
@@ -170,12 +187,26 @@ __global__ void __launch_bounds__(kThreads) decode_pages_kernel(const PagesParam
     }
     const uint8_t* base = p.arena + int64_t(slot) * p.slot_bytes;
     const int64_t ts = p.token_start[page];
-    for (int r = warp; r < 2 * T; r += kThreads / 32) {
-      const bool is_v = r >= T;
-      const int j = is_v ? r - T : r;
-      uint16_t* dst = reinterpret_cast<uint16_t*>(is_v ? p.layer_v[l] : p.layer_k[l]) + (ts + j) * p.row_stride;
-      const float scale = f16_to_f32(reinterpret_cast<const uint16_t*>(base)[r]);
-      decode_row<NCH, HALF>(reinterpret_cast<const int8_t*>(base + c0 + int64_t(r) * p.row_len), scale, dst, lane);
+    // kRowsInFlight rows per warp: every row's codes are loaded before any is converted
+    constexpr int kWarps = kThreads / 32;
+    for (int r0 = warp; r0 < 2 * T; r0 += kRowsInFlight * kWarps) {
+      RowCodes<NCH> rc[kRowsInFlight];
+#pragma unroll
+      for (int u = 0; u < kRowsInFlight; ++u) {
+        const int r = r0 + u * kWarps;
+        if (r < 2 * T)
+          load_row_codes<NCH, HALF>(reinterpret_cast<const int8_t*>(base + c0 + int64_t(r) * p.row_len),
+                                    reinterpret_cast<const uint16_t*>(base) + r, lane, rc[u]);
+      }
+#pragma unroll
+      for (int u = 0; u < kRowsInFlight; ++u) {
+        const int r = r0 + u * kWarps;
+        if (r >= 2 * T) break;
+        const bool is_v = r >= T;
+        const int j = is_v ? r - T : r;
+        uint16_t* dst = reinterpret_cast<uint16_t*>(is_v ? p.layer_v[l] : p.layer_k[l]) + (ts + j) * p.row_stride;
+        decode_row<NCH, HALF>(rc[u], dst, lane);
+      }
     }
     __syncthreads();  // every warp is done reading the slot before it is released
     if (threadIdx.x == 0) {
