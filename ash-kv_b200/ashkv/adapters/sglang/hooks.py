@@ -20,8 +20,13 @@ last token, which the reference leaves uninitialised, are zero here).
 Differences in how the work is done:
   * demote: one gather+encode launch per layer and K/V writes the packed
     slots straight into a device staging buffer [tokens, layers, slot]; a
-    single device->host copy moves all layers (the reference runs two
-    synchronous .cpu() copies and a host scatter per layer);
+    single pitched device->host copy moves all layers (the reference runs two
+    synchronous .cpu() copies and a host scatter per layer).  With
+    ``compact_host_slots`` (the default) that copy carries only the used
+    2H + H*D bytes of each compressed slot, so the bytes saved are saved on
+    the link too; the zero tail [2H + H*D, 2*H*D), which nothing reads, is
+    then left as it was in the host pool.  ``compact_host_slots = False``
+    writes whole slots, zero tail included, byte for byte as the reference;
   * promote: a pitched host->device copy moves only the used 2H + H*D bytes
     of each slot, and the decode kernel scatters rows straight into the
     device pool at ``device_indices``;
@@ -64,6 +69,8 @@ class SGLangHooks:
         self.codec_name = codec_name
         self.circuit_breaker = CircuitBreakerRegistry()
         self.compressible_layers = None
+        self.compact_host_slots = True
+        self.transfer_stats = {"d2h_bytes": 0, "h2d_bytes": 0}  # bytes moved over the host link
         self.stats = {"tokens_compressed": 0, "tokens_decompressed": 0, "bytes_saved": 0,
                       "blocks_intercepted": 0, "last_flush_time": 0}
         os.makedirs("stats", exist_ok=True)
@@ -131,22 +138,41 @@ class SGLangHooks:
                                              scale_slot_stride=L * slot)
                 else:
                     staging[:, layer, :].view(torch.bfloat16).copy_(src[didx].view(n, row))
-            self._write_host_rows(getattr(host_pool, name), host_indices, staging, n, L, slot)
+            widths = [2 * H + row if (self.compact_host_slots and layer in compress) else slot for layer in range(L)]
+            self._write_host_rows(getattr(host_pool, name), host_indices, staging, n, L, slot, widths)
+            self.transfer_stats["d2h_bytes"] += n * sum(widths)
 
     @staticmethod
     def _write_host_rows(host_buf: torch.Tensor, host_indices, staging: torch.Tensor, n: int, L: int,
-                         slot: int) -> None:
-        """Copy staging [n, L, slot] into host rows host_buf[host_indices] (each row [L, H, D] bf16)."""
+                         slot: int, widths: list[int]) -> None:
+        """Copy the first widths[l] bytes of each staging slot [n, L, slot] into host rows
+        host_buf[host_indices] (each row [L, H, D] bf16, i.e. L slots of `slot` bytes)."""
         hview = host_buf.view(host_buf.shape[0], -1).view(torch.uint8)
         first = _contiguous_range(host_indices) if host_buf.is_contiguous() else None
         if first is not None:
-            hview[first:first + n].copy_(staging.view(n, L * slot), non_blocking=host_buf.is_pinned())
+            dst = hview[first:first + n]
+            if all(w == slot for w in widths):
+                dst.copy_(staging.view(n, L * slot), non_blocking=host_buf.is_pinned())
+            elif len(set(widths)) == 1:  # one pitched copy over all (token, layer) slots
+                _native.memcpy2d(dst.data_ptr(), slot, staging.data_ptr(), slot, widths[0], n * L, staging.device)
+            else:
+                for layer, w in enumerate(widths):
+                    _native.memcpy2d(dst.data_ptr() + layer * slot, L * slot, staging.data_ptr() + layer * slot,
+                                     L * slot, w, n, staging.device)
             if host_buf.is_pinned():
                 torch.cuda.current_stream(staging.device).synchronize()
         else:
-            bounce = staging.view(n, L * slot).to("cpu")
             hidx = host_indices.detach().to("cpu", torch.int64)
-            hview[hidx] = bounce
+            h3 = hview.view(hview.shape[0], L, slot)
+            if all(w == slot for w in widths):
+                hview[hidx] = staging.view(n, L * slot).to("cpu")
+            elif len(set(widths)) == 1:
+                w = widths[0]
+                h3[hidx, :, :w] = staging[:, :, :w].contiguous().to("cpu")
+            else:
+                bounce = staging.to("cpu")
+                for layer, w in enumerate(widths):
+                    h3[hidx, layer, :w] = bounce[:, layer, :w]
 
     # ------------------------------------------------------------------ promote
     def promote_hook(self, device_pool: Any, host_pool: Any, host_indices: torch.Tensor,
@@ -175,6 +201,7 @@ class SGLangHooks:
         dev = device_pool.k_buffer[0].device
         didx = device_indices.to(device=dev, dtype=torch.int64)
         used = slot if native_layer else 2 * H + row
+        self.transfer_stats["h2d_bytes"] += 2 * n * used
         for name in ("k_buffer", "v_buffer"):
             hbuf = getattr(host_pool, name)
             L = hbuf.shape[1]

@@ -2,7 +2,8 @@
 
 Byte formats are compared with the oracle: the host slot of (token t, layer
 l) must hold [fp16 scales of tokens t*H..t*H+H-1 | int8 codes of token t |
-zeros], as the reference's hooks write it.
+zeros], as the reference's hooks write it (with compact host slots, the
+zero tail is not transferred and keeps the host pool's previous bytes).
 """
 from __future__ import annotations
 
@@ -57,22 +58,32 @@ def expected_slots(k_layer: torch.Tensor, didx: torch.Tensor, H: int, D: int) ->
     return out
 
 
+@pytest.mark.parametrize("compact", [True, False])
 @pytest.mark.parametrize("contiguous,pin", [(True, True), (True, False), (False, False)])
-def test_demote_writes_reference_slot_bytes(cuda, tmp_path, monkeypatch, contiguous, pin):
+def test_demote_writes_reference_slot_bytes(cuda, tmp_path, monkeypatch, contiguous, pin, compact):
     monkeypatch.chdir(tmp_path)
     L, cap, H, D, n = 3, 300, 8, 128, 77
     dev = DevicePool(L, cap, H, D, cuda, seed=1)
     host = HostPool(L, cap, H, D, pin=pin)
+    before = host.k_buffer.view(cap, L, -1).view(torch.uint8).clone()
     didx = torch.randperm(cap, generator=torch.Generator().manual_seed(2))[:n].to(cuda)
     hidx = torch.arange(10, 10 + n) if contiguous else torch.randperm(cap, generator=torch.Generator().manual_seed(3))[:n]
     hooks = SGLangHooks()
+    hooks.compact_host_slots = compact
     assert hooks.demote_hook(dev, host, hidx, didx, "MHA") is True
+    used = 2 * H + H * D
     for name in ("k_buffer", "v_buffer"):
         hb = getattr(host, name).view(cap, L, -1).view(torch.uint8)
         for layer in range(L):
             got = hb[hidx.long(), layer].numpy()
             want = expected_slots(getattr(dev, name)[layer], didx, H, D)
-            assert np.array_equal(got, want), (name, layer)
+            if compact:
+                assert np.array_equal(got[:, :used], want[:, :used]), (name, layer)
+                assert np.array_equal(got[:, used:], before[hidx.long(), layer, used:].numpy())
+            else:
+                assert np.array_equal(got, want), (name, layer)
+    slot_bytes = used if compact else 2 * H * D
+    assert hooks.transfer_stats["d2h_bytes"] == 2 * n * L * slot_bytes
     # untouched host rows keep their contents
     others = np.setdiff1d(np.arange(cap), hidx.numpy())
     assert bool((host.k_buffer[torch.from_numpy(others)] == 7.0).all())
@@ -136,6 +147,16 @@ def test_hooks_decline_and_native_layers(cuda, tmp_path, monkeypatch):
     hooks.compressible_layers = [0]  # layer 1 travels as plain bf16
     hooks.demote_hook(dev, host, idx, idx.to(cuda), "MHA")
     assert torch.equal(host.k_buffer[:n, 1].view(torch.int16), dev.k_buffer[1][:n].cpu().view(torch.int16))
+    used = 2 * H + H * D  # layer 0 compact, layer 1 whole bf16 rows
+    got0 = host.k_buffer.view(cap, L, -1).view(torch.uint8)[:n, 0, :used].numpy()
+    assert np.array_equal(got0, expected_slots(dev.k_buffer[0], idx.to(cuda), H, D)[:, :used])
+    assert hooks.transfer_stats["d2h_bytes"] == 2 * n * (used + 2 * H * D)
+    # the same mixed layout through a non-contiguous host index list
+    perm = n + torch.randperm(cap - n, generator=torch.Generator().manual_seed(9))[:n]  # rows other than 0..n-1
+    hooks.demote_hook(dev, host, perm, idx.to(cuda), "MHA")
+    assert torch.equal(host.v_buffer[perm, 1].view(torch.int16), dev.v_buffer[1][:n].cpu().view(torch.int16))
+    got0 = host.v_buffer.view(cap, L, -1).view(torch.uint8)[perm, 0, :used].numpy()
+    assert np.array_equal(got0, expected_slots(dev.v_buffer[0], idx.to(cuda), H, D)[:, :used])
     saved = dev.k_buffer[1][:n].clone()
     dev.k_buffer[1].zero_()
     hooks.promote_hook(dev, host, idx, idx.to(cuda), 1, "MHA")
