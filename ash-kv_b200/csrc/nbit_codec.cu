@@ -451,55 +451,67 @@ __global__ void __launch_bounds__(kThreads, 4) nbit_encode_tma_kernel(const __gr
   }
 }
 
+// One group's packed codes (32 * BITS bits, MSB-first within each byte) and its delta.
 template <int BITS>
-__device__ __forceinline__ void unpack_codes(const uint8_t* codes, int64_t g, uint32_t (&code)[32]) {
+struct GroupCodes {
+  uint32_t w[BITS];
+  float delta;
+};
+template <int BITS>
+__device__ __forceinline__ void load_group(const uint16_t* scales, const uint8_t* codes, int64_t g,
+                                           GroupCodes<BITS>& gc) {
+  gc.delta = bf16_to_f32(scales[g]);
   if constexpr (BITS == 4) {
     const uint4 v = *reinterpret_cast<const uint4*>(codes + g * 16);
-    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-    for (int k = 0; k < 4; ++k)
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const uint32_t b = (w[k] >> (8 * j)) & 0xFFu;
-        code[8 * k + 2 * j] = b >> 4;
-        code[8 * k + 2 * j + 1] = b & 0xFu;
-      }
+    gc.w[0] = v.x; gc.w[1] = v.y; gc.w[2] = v.z; gc.w[3] = v.w;
   } else if constexpr (BITS == 2) {
     const uint2 v = *reinterpret_cast<const uint2*>(codes + g * 8);
-    const uint32_t w[2] = {v.x, v.y};
-#pragma unroll
-    for (int k = 0; k < 2; ++k)
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const uint32_t b = (w[k] >> (8 * j)) & 0xFFu;
-        const int i = 16 * k + 4 * j;
-        code[i] = b >> 6; code[i + 1] = (b >> 4) & 3u; code[i + 2] = (b >> 2) & 3u; code[i + 3] = b & 3u;
-      }
+    gc.w[0] = v.x; gc.w[1] = v.y;
   } else {
     const uint4 a = *reinterpret_cast<const uint4*>(codes + g * 32);
     const uint4 b = *reinterpret_cast<const uint4*>(codes + g * 32 + 16);
-    const uint32_t w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
-#pragma unroll
-    for (int k = 0; k < 8; ++k)
-#pragma unroll
-      for (int j = 0; j < 4; ++j) code[4 * k + j] = (w[k] >> (8 * j)) & 0xFFu;
+    gc.w[0] = a.x; gc.w[1] = a.y; gc.w[2] = a.z; gc.w[3] = a.w;
+    gc.w[4] = b.x; gc.w[5] = b.y; gc.w[6] = b.z; gc.w[7] = b.w;
   }
 }
 
+// Byte j of m (a code < 256) as the float 2^23 + code.
+__device__ __forceinline__ float code_plus_2p23(uint32_t m, int j) {
+  return __uint_as_float(__byte_perm(m, 0x4B000000u, 0x7540u + uint32_t(j)));
+}
+
+// out = bf16((code - half) * delta) for the 32 elements of a group:
+// float(code) = (2^23 + code) - 2^23 exactly, then the reference's two roundings.
 template <int BITS>
-__device__ __forceinline__ void dequant_group(const uint16_t* scales, const uint8_t* codes, int64_t g,
-                                              float half, uint16_t* dst) {
-  uint32_t code[32];
-  unpack_codes<BITS>(codes, g, code);
-  const float delta = bf16_to_f32(scales[g]);
+__device__ __forceinline__ void store_group(const GroupCodes<BITS>& gc, float half, uint16_t* out) {
+  const f2 DEL = pk2(gc.delta, gc.delta), NH = pk2(-half, -half), N23 = pk2(-8388608.0f, -8388608.0f);
   uint32_t o[16];
+  auto pair = [&](float a, float b) { return f32x2_to_bf16x2_pk(mul2(add2(add2(pk2(a, b), N23), NH), DEL)); };
+  if constexpr (BITS == 4) {
 #pragma unroll
-  for (int i = 0; i < 16; ++i) {
-    const float a = __fmul_rn(__fadd_rn(float(code[2 * i]), -half), delta);
-    const float b = __fmul_rn(__fadd_rn(float(code[2 * i + 1]), -half), delta);
-    o[i] = f32x2_to_bf16x2(a, b);
+    for (int k = 0; k < 4; ++k) {  // word k: elements 8k .. 8k+7, byte j = (elem 8k+2j) << 4 | elem 8k+2j+1
+      const uint32_t hi = (gc.w[k] >> 4) & 0x0F0F0F0Fu, lo = gc.w[k] & 0x0F0F0F0Fu;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) o[4 * k + j] = pair(code_plus_2p23(hi, j), code_plus_2p23(lo, j));
+    }
+  } else if constexpr (BITS == 2) {
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {  // word k: elements 16k .. 16k+15, four per byte
+      const uint32_t c0 = (gc.w[k] >> 6) & 0x03030303u, c1 = (gc.w[k] >> 4) & 0x03030303u;
+      const uint32_t c2 = (gc.w[k] >> 2) & 0x03030303u, c3 = gc.w[k] & 0x03030303u;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        o[8 * k + 2 * j] = pair(code_plus_2p23(c0, j), code_plus_2p23(c1, j));
+        o[8 * k + 2 * j + 1] = pair(code_plus_2p23(c2, j), code_plus_2p23(c3, j));
+      }
+    }
+  } else {
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {  // word k: elements 4k .. 4k+3, one per byte
+      o[2 * k] = pair(code_plus_2p23(gc.w[k], 0), code_plus_2p23(gc.w[k], 1));
+      o[2 * k + 1] = pair(code_plus_2p23(gc.w[k], 2), code_plus_2p23(gc.w[k], 3));
+    }
   }
-  uint16_t* out = dst + g * 32;
   U8 lo, hi;
 #pragma unroll
   for (int k = 0; k < 8; ++k) { lo.v[k] = o[k]; hi.v[k] = o[8 + k]; }
@@ -507,17 +519,16 @@ __device__ __forceinline__ void dequant_group(const uint16_t* scales, const uint
   st_cs_v8(out + 16, hi);
 }
 
-// One lane per group; each warp then overwrites its bucket's outliers.
 template <int BITS>
-__global__ void __launch_bounds__(kThreads) nbit_decode_kernel(const NbitDecParams p) {
-  const int64_t g = int64_t(blockIdx.x) * kThreads + threadIdx.x;
-  const int64_t g0 = g - (threadIdx.x & 31);
-  const int64_t bucket = g0 / 32;
-  // the bucket's count is fetched first so its latency overlaps the dequantisation
-  const uint32_t count = (p.bucket_counts && g0 < p.n_groups) ? p.bucket_counts[bucket] : 0u;
-  if (g < p.n_groups) dequant_group<BITS>(p.scales, p.codes, g, p.half_states, p.dst);
-  if (!p.bucket_counts || g0 >= p.n_groups) return;  // whole warp past the end
-  __syncwarp();  // the bucket's dense values are stored before its outliers overwrite them
+__device__ __forceinline__ void dequant_group(const uint16_t* scales, const uint8_t* codes, int64_t g,
+                                              float half, uint16_t* dst) {
+  GroupCodes<BITS> gc;
+  load_group<BITS>(scales, codes, g, gc);
+  store_group<BITS>(gc, half, dst + g * 32);
+}
+
+// Overwrite bucket b's outliers (after its dense values are stored); one warp.
+__device__ __forceinline__ void scatter_bucket(const NbitDecParams& p, int64_t bucket, uint32_t count) {
   const uint32_t n = min(count, uint32_t(p.bucket_cap));
   const uint32_t* ent = p.bucket_entries + bucket * p.bucket_cap;
   const int64_t base = bucket * ASHKV_NBIT_BUCKET_ELEMS;
@@ -528,6 +539,29 @@ __global__ void __launch_bounds__(kThreads) nbit_decode_kernel(const NbitDecPara
     if (idx < n_elems) p.dst[idx] = uint16_t(e & 0xFFFFu);
     else atomicOr(p.status, ASHKV_FLAG_INDEX_RANGE);
   }
+}
+
+// Two groups per lane (g and g + kThreads; both loads issued before either is
+// converted), so each warp covers buckets w and w + kWarps of its CTA's 16;
+// after a warp barrier it overwrites those buckets' outliers.
+template <int BITS>
+__global__ void __launch_bounds__(kThreads) nbit_decode_kernel(const NbitDecParams p) {
+  const int lane = threadIdx.x & 31;
+  const int64_t ga = int64_t(blockIdx.x) * (2 * kThreads) + threadIdx.x, gb = ga + kThreads;
+  const int64_t bucket_a = (ga - lane) / 32, bucket_b = (gb - lane) / 32;
+  const bool has_a = bucket_a * 32 < p.n_groups, has_b = bucket_b * 32 < p.n_groups;  // warp-uniform
+  // the buckets' counts are fetched first so their latency overlaps the dequantisation
+  const uint32_t count_a = (p.bucket_counts && has_a) ? p.bucket_counts[bucket_a] : 0u;
+  const uint32_t count_b = (p.bucket_counts && has_b) ? p.bucket_counts[bucket_b] : 0u;
+  GroupCodes<BITS> a, b;
+  if (ga < p.n_groups) load_group<BITS>(p.scales, p.codes, ga, a);
+  if (gb < p.n_groups) load_group<BITS>(p.scales, p.codes, gb, b);
+  if (ga < p.n_groups) store_group<BITS>(a, p.half_states, p.dst + ga * 32);
+  if (gb < p.n_groups) store_group<BITS>(b, p.half_states, p.dst + gb * 32);
+  if (!p.bucket_counts) return;
+  __syncwarp();  // the buckets' dense values are stored before their outliers overwrite them
+  if (has_a) scatter_bucket(p, bucket_a, count_a);
+  if (has_b) scatter_bucket(p, bucket_b, count_b);
 }
 
 template <int BITS>
@@ -764,7 +798,7 @@ extern "C" ashkv_status_t ashkv_nbit_decode(
   if (d_bucket_counts && (!d_status || (bucket_cap > 0 && !d_bucket_entries))) return ASHKV_BAD_ARGUMENT;
   if (!aligned(d_dst, 32) || !aligned(d_scales, 2) || !aligned(d_codes, bits == 2 ? 8 : 16))
     return ASHKV_BAD_ARGUMENT;
-  const int64_t n_ctas = (n_groups + kThreads - 1) / kThreads;  // 8 buckets per CTA
+  const int64_t n_ctas = (n_groups + 2 * kThreads - 1) / (2 * kThreads);  // 16 buckets per CTA
   if (n_ctas > 0x7FFFFFFF) return ASHKV_BAD_ARGUMENT;
 
   NbitDecParams p;

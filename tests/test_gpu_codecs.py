@@ -316,6 +316,46 @@ def test_nbit_pinned_api_matches_bytes_api(cuda, bits, hidden):
     assert DitheredNBitCodec().encode_pinned(torch.empty(0, dtype=torch.bfloat16)).numpy().tobytes() == bytes(8)
 
 
+def test_nbit_config3_full_size_int2_properties(cuda):
+    """INT2 workload at full size: 80 layers x K,V x [2048 pages, 16, 8 heads, 128],
+    N(0, s^2) with s ~ U[0.5, 2] per (layer, K/V, head), 5.37 G elements in 160
+    tensors, each encoded with the INT2 codec's dither seed and decoded back.
+    Per tensor: outliers restored bit-exactly, every other element within one
+    quantisation step of its group; a sample of buckets bit-exact against the oracle."""
+    pages, T, H, D = 2048, 16, 8, 128
+    n = pages * T * H * D
+    g = torch.Generator(device=cuda).manual_seed(0)
+    sd_gen = torch.Generator().manual_seed(1)
+    total_out = 0
+    for layer in range(80):
+        for kv in range(2):
+            sd = torch.empty(H).uniform_(0.5, 2.0, generator=sd_gen).to(cuda)
+            x = (torch.randn(pages, T, H, D, generator=g, device=cuda) * sd.view(1, 1, H, 1)).to(torch.bfloat16)
+            x = x.view(-1)
+            enc = nb.encode_groups(x, 2, 3.0, seed=42)
+            dec = nb.decode_groups(enc)
+            idx, val, total = nb.flatten_outliers(enc)
+            t = int(total.item())
+            total_out += t
+            ii = idx[:t].long()
+            assert torch.equal(dec[ii].view(torch.int16), x[ii].view(torch.int16))
+            delta = enc.scales.float().repeat_interleave(32)
+            err = (dec.float() - x.float()).abs()
+            err[ii] = 0.0
+            assert bool((err <= delta * 1.01).all()), (layer, kv)
+            assert int(enc.status.item()) == 0
+            if layer % 27 == 0:
+                xs, sc, codes = bits_of(x), bits_of(enc.scales), enc.codes.cpu().numpy()
+                for lo in range(0, n, n // 4):
+                    u = oracle.philox_dither(8192, 42, lo)
+                    osc, ocodes, _, _ = oracle.nbit_encode(xs[lo:lo + 8192], 2, u, 3.0)
+                    assert np.array_equal(sc[lo // 32:(lo + 8192) // 32], osc)
+                    assert np.array_equal(codes[lo // 4:(lo + 8192) // 4], ocodes)
+            del x, enc, dec, err, delta
+    # 3-sigma tails of Gaussian groups: a fraction of a percent of the elements
+    assert 0 < total_out < 80 * 2 * n // 100
+
+
 def test_nbit_codec_seeding_policy(cuda):
     x = bits_of(rand_bf16(4 * 128, 51)).tobytes()
     c = DitheredNBitCodec()
