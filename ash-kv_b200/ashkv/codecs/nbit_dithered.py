@@ -145,6 +145,17 @@ def _host_bytes(data: bytes, out: Optional[torch.Tensor]) -> torch.Tensor:
     return o[:len(data)]
 
 
+_SIDE_STREAMS: dict = {}
+
+
+def _side_streams(dev: torch.device):
+    """Per-device (host->device, device->host) copy streams of the host-buffer API."""
+    key = dev.index
+    if key not in _SIDE_STREAMS:
+        _SIDE_STREAMS[key] = (torch.cuda.Stream(dev), torch.cuda.Stream(dev))
+    return _SIDE_STREAMS[key]
+
+
 def _sha8(raw: bytes) -> int:
     return int.from_bytes(hashlib.sha256(raw).digest()[:8], "little", signed=False)
 
@@ -226,83 +237,163 @@ class DitheredNBitCodec:
 
         With pinned buffers the host<->device transfers are DMA copies straight
         from ``src`` and into ``out``; the call returns once ``out`` is complete."""
-        self._encode_calls += 1
-        flat = _host_flat(src, torch.bfloat16)
+        return self.encode_pinned_batch([src], [out], uniforms=[uniform])[0]
+
+    def encode_pinned_batch(self, srcs, outs=None, *, uniforms=None) -> list:
+        """``encode_pinned`` over several tensors, in order (one call each, so each
+        gets the seed that call would get).  Host->device copies run on one side
+        stream and device->host copies on another, so a tensor's blob travels
+        back while the next tensor's input is still arriving."""
+        outs = list(outs) if outs is not None else [None] * len(srcs)
+        uniforms = list(uniforms) if uniforms is not None else [None] * len(srcs)
+        if not (len(outs) == len(uniforms) == len(srcs)):
+            raise ValueError("srcs, outs and uniforms must have the same length")
         L = self._hidden_dim
-        num_tokens = flat.numel() // L
-        header = struct.pack("<II", num_tokens, 0)
-        if num_tokens == 0:
-            return _host_bytes(header, out)
-        if L % self._group_size:
-            raise RuntimeError(f"shape '[{num_tokens}, {L // self._group_size}, {self._group_size}]' is invalid "
-                               f"for input of size {num_tokens * L}")
-        dev = _staging.device()
-        n_elems = num_tokens * L
-        d_src = torch.empty(n_elems, dtype=torch.bfloat16, device=dev)
-        d_src.copy_(flat[:n_elems], non_blocking=True)
-        u = None
-        if uniform is not None:
-            u = torch.as_tensor(uniform, dtype=torch.float32).reshape(-1)
-            if u.numel() != n_elems:
-                raise ValueError(f"uniform has {u.numel()} values, expected {n_elems}")
-            u = u.to(dev, non_blocking=True).contiguous()
-        enc = encode_groups(d_src, self._bits, self._sigma, uniform=u, seed=self._seed())
-        idx, val, total = flatten_outliers(enc)
-        n_out = int(total.item())
-        n_groups = enc.n_groups
-        n_codes = n_groups * 32 * self._bits // 8
-        size = 8 + 2 * n_groups + 6 * n_out + n_codes
-        out = _host_out(out, size, torch.uint8)
-        out[:8].numpy()[:] = np.frombuffer(struct.pack("<II", num_tokens, n_out), dtype=np.uint8)
-        o = 8
-        out[o:o + 2 * n_groups].copy_(enc.scales.view(torch.uint8), non_blocking=True); o += 2 * n_groups
-        if n_out:
-            out[o:o + 4 * n_out].copy_(idx[:n_out].view(torch.uint8), non_blocking=True); o += 4 * n_out
-            out[o:o + 2 * n_out].copy_(val[:n_out].view(torch.uint8), non_blocking=True); o += 2 * n_out
-        out[o:o + n_codes].copy_(enc.codes[:n_codes], non_blocking=True)
-        torch.cuda.current_stream(dev).synchronize()
-        return out[:size]
+        dev = None
+        jobs = []
+        for src in srcs:
+            flat = _host_flat(src, torch.bfloat16)
+            num_tokens = flat.numel() // L
+            if num_tokens and L % self._group_size:
+                raise RuntimeError(f"shape '[{num_tokens}, {L // self._group_size}, {self._group_size}]' is invalid "
+                                   f"for input of size {num_tokens * L}")
+            jobs.append({"flat": flat, "num_tokens": num_tokens})
+        if any(j["num_tokens"] for j in jobs):
+            dev = _staging.device()
+            cur = torch.cuda.current_stream(dev)
+            h2d, d2h = _side_streams(dev)
+            h2d.wait_stream(cur)   # device buffers below may reuse memory the current stream still uses
+            for j, u in zip(jobs, uniforms):
+                if not j["num_tokens"]:
+                    continue
+                n_elems = j["num_tokens"] * L
+                j["d_src"] = torch.empty(n_elems, dtype=torch.bfloat16, device=dev)
+                if u is not None:
+                    u = torch.as_tensor(u, dtype=torch.float32).reshape(-1)
+                    if u.numel() != n_elems:
+                        raise ValueError(f"uniform has {u.numel()} values, expected {n_elems}")
+                with torch.cuda.stream(h2d):
+                    j["d_src"].copy_(j["flat"][:n_elems], non_blocking=True)
+                    j["u"] = None if u is None else u.to(dev, non_blocking=True).contiguous()
+                j["ready"] = h2d.record_event()
+            totals = torch.empty(len(jobs), dtype=torch.int32, pin_memory=True)
+        for i, j in enumerate(jobs):
+            self._encode_calls += 1
+            if not j["num_tokens"]:
+                continue
+            cur.wait_event(j["ready"])
+            enc = encode_groups(j["d_src"], self._bits, self._sigma, uniform=j["u"], seed=self._seed())
+            idx, val, total = flatten_outliers(enc)
+            totals[i:i + 1].copy_(total, non_blocking=True)
+            j.update(enc=enc, idx=idx, val=val, done=cur.record_event())
+        results = []
+        for i, (j, out) in enumerate(zip(jobs, outs)):
+            if not j["num_tokens"]:
+                results.append(_host_bytes(struct.pack("<II", 0, 0), out))
+                continue
+            j["done"].synchronize()
+            n_out = int(totals[i])
+            enc = j["enc"]
+            n_groups = enc.n_groups
+            n_codes = n_groups * 32 * self._bits // 8
+            size = 8 + 2 * n_groups + 6 * n_out + n_codes
+            out = _host_out(out, size, torch.uint8)
+            out[:8].numpy()[:] = np.frombuffer(struct.pack("<II", j["num_tokens"], n_out), dtype=np.uint8)
+            d2h.wait_event(j["done"])
+            with torch.cuda.stream(d2h):
+                o = 8
+                out[o:o + 2 * n_groups].copy_(enc.scales.view(torch.uint8), non_blocking=True); o += 2 * n_groups
+                if n_out:
+                    out[o:o + 4 * n_out].copy_(j["idx"][:n_out].view(torch.uint8), non_blocking=True); o += 4 * n_out
+                    out[o:o + 2 * n_out].copy_(j["val"][:n_out].view(torch.uint8), non_blocking=True); o += 2 * n_out
+                out[o:o + n_codes].copy_(enc.codes[:n_codes], non_blocking=True)
+            results.append(out[:size])
+        if dev is not None:
+            d2h.synchronize()
+        return results
 
     def decode_pinned(self, blob: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
         """Decode a blob held in a host uint8 tensor into the host bf16 tensor
         ``out`` (allocated pinned when None); returns ``out[:n]``, the values
         ``decode`` returns for the same bytes."""
-        self._decode_calls += 1
-        b = _host_flat(blob, torch.uint8)
-        if b.numel() < 8:
-            return _host_out(out, 0, torch.bfloat16)[:0]
-        num_tokens, n_out = struct.unpack("<II", b[:8].numpy().tobytes())
-        if num_tokens == 0:
-            return _host_out(out, 0, torch.bfloat16)[:0]
-        n_groups = num_tokens * (self._hidden_dim // self._group_size)
-        n_codes = n_groups * 32 * self._bits // 8
-        need = 8 + 2 * n_groups + 6 * n_out + n_codes
-        if b.numel() < need:
-            raise RuntimeError(f"N-bit blob too short: {b.numel()} bytes, layout needs {need}")
-        dev = _staging.device()
-        # one DMA per blob section, each into its own (aligned) device buffer
-        o = 8
-        d_sc = torch.empty(2 * n_groups, dtype=torch.uint8, device=dev)
-        d_sc.copy_(b[o:o + 2 * n_groups], non_blocking=True); o += 2 * n_groups
-        d_idx = torch.empty(max(4 * n_out, 4), dtype=torch.uint8, device=dev)
-        d_val = torch.empty(max(2 * n_out, 2), dtype=torch.uint8, device=dev)
-        if n_out:
-            d_idx[:4 * n_out].copy_(b[o:o + 4 * n_out], non_blocking=True); o += 4 * n_out
-            d_val[:2 * n_out].copy_(b[o:o + 2 * n_out], non_blocking=True); o += 2 * n_out
-        codes = torch.empty(max(n_codes, 16), dtype=torch.uint8, device=dev)
-        codes[:n_codes].copy_(b[o:o + n_codes], non_blocking=True)
-        dv = torch.empty(n_groups * 32, dtype=torch.bfloat16, device=dev)
-        status = torch.zeros(1, dtype=torch.int32, device=dev)
-        _native.nbit_decode_flat(d_sc.view(torch.bfloat16), codes, n_groups, self._bits,
-                                 d_idx.view(torch.int32) if n_out else None,
-                                 d_val.view(torch.int16) if n_out else None, n_out, dv, status)
-        out = _host_out(out, n_groups * 32, torch.bfloat16)
-        out[:n_groups * 32].copy_(dv, non_blocking=True)
-        st = status.to("cpu", non_blocking=True)
-        torch.cuda.current_stream(dev).synchronize()
-        if int(st.item()) & _native.FLAG_INDEX_RANGE:
-            raise IndexError(f"outlier index out of range for a decoded size of {n_groups * 32} elements")
-        return out[:n_groups * 32]
+        return self.decode_pinned_batch([blob], [out])[0]
+
+    def decode_pinned_batch(self, blobs, outs=None) -> list:
+        """``decode_pinned`` over several blobs; a blob's values travel back to the
+        host while the next blob is still being copied in and decoded."""
+        outs = list(outs) if outs is not None else [None] * len(blobs)
+        if len(outs) != len(blobs):
+            raise ValueError("blobs and outs must have the same length")
+        jobs = []
+        for blob in blobs:
+            self._decode_calls += 1
+            b = _host_flat(blob, torch.uint8)
+            num_tokens = n_out = 0
+            if b.numel() >= 8:
+                num_tokens, n_out = struct.unpack("<II", b[:8].numpy().tobytes())
+            j = {"b": b, "num_tokens": num_tokens, "n_out": n_out}
+            if num_tokens:
+                n_groups = num_tokens * (self._hidden_dim // self._group_size)
+                n_codes = n_groups * 32 * self._bits // 8
+                need = 8 + 2 * n_groups + 6 * n_out + n_codes
+                if b.numel() < need:
+                    raise RuntimeError(f"N-bit blob too short: {b.numel()} bytes, layout needs {need}")
+                j.update(n_groups=n_groups, n_codes=n_codes)
+            jobs.append(j)
+        dev = None
+        if any(j["num_tokens"] for j in jobs):
+            dev = _staging.device()
+            cur = torch.cuda.current_stream(dev)
+            h2d, d2h = _side_streams(dev)
+            h2d.wait_stream(cur)
+            for j in jobs:
+                if not j["num_tokens"]:
+                    continue
+                b, g, nc, n_out = j["b"], j["n_groups"], j["n_codes"], j["n_out"]
+                # one DMA per blob section, each into its own (aligned) device buffer
+                d_sc = torch.empty(2 * g, dtype=torch.uint8, device=dev)
+                d_idx = torch.empty(max(4 * n_out, 4), dtype=torch.uint8, device=dev)
+                d_val = torch.empty(max(2 * n_out, 2), dtype=torch.uint8, device=dev)
+                codes = torch.empty(max(nc, 16), dtype=torch.uint8, device=dev)
+                with torch.cuda.stream(h2d):
+                    o = 8
+                    d_sc.copy_(b[o:o + 2 * g], non_blocking=True); o += 2 * g
+                    if n_out:
+                        d_idx[:4 * n_out].copy_(b[o:o + 4 * n_out], non_blocking=True); o += 4 * n_out
+                        d_val[:2 * n_out].copy_(b[o:o + 2 * n_out], non_blocking=True); o += 2 * n_out
+                    codes[:nc].copy_(b[o:o + nc], non_blocking=True)
+                j.update(d_sc=d_sc, d_idx=d_idx, d_val=d_val, codes=codes, ready=h2d.record_event())
+            statuses = torch.zeros(len(jobs), dtype=torch.int32, device=dev)
+            h_status = torch.empty(len(jobs), dtype=torch.int32, pin_memory=True)
+        results = []
+        for i, (j, out) in enumerate(zip(jobs, outs)):
+            if not j["num_tokens"]:
+                results.append(_host_out(out, 0, torch.bfloat16)[:0])
+                continue
+            g, n_out = j["n_groups"], j["n_out"]
+            cur.wait_event(j["ready"])
+            dv = torch.empty(g * 32, dtype=torch.bfloat16, device=dev)
+            _native.nbit_decode_flat(j["d_sc"].view(torch.bfloat16), j["codes"], g, self._bits,
+                                     j["d_idx"].view(torch.int32) if n_out else None,
+                                     j["d_val"].view(torch.int16) if n_out else None, n_out, dv,
+                                     statuses[i:i + 1])
+            done = cur.record_event()
+            out = _host_out(out, g * 32, torch.bfloat16)
+            d2h.wait_event(done)
+            with torch.cuda.stream(d2h):
+                out[:g * 32].copy_(dv, non_blocking=True)
+            j["dv"] = dv
+            results.append(out[:g * 32])
+        if dev is not None:
+            d2h.wait_stream(cur)
+            with torch.cuda.stream(d2h):
+                h_status.copy_(statuses, non_blocking=True)
+            d2h.synchronize()
+            for i, j in enumerate(jobs):
+                if j["num_tokens"] and int(h_status[i]) & _native.FLAG_INDEX_RANGE:
+                    raise IndexError(f"outlier index out of range for a decoded size of {j['n_groups'] * 32} "
+                                     f"elements")
+        return results
 
     def decode(self, target_bytes: bytes) -> bytes:
         self._decode_calls += 1

@@ -11,7 +11,8 @@ both back to bf16.
              inputs resident in HBM (device-timed with CUDA events), summed
              over ranks (weak scaling: every rank owns its own K/V shard).
 ``e2e``    — the same metric through the codec's host-buffer API
-             (``DitheredNBitCodec.encode_pinned`` / ``.decode_pinned``): K and V
+             (``DitheredNBitCodec.encode_pinned_batch`` / ``.decode_pinned_batch``
+             over [K, V]; copies in each direction on their own streams): K and V
              start in pinned host memory, every step copies them to the device,
              encodes, writes the reference blob into pinned host memory, copies
              the blobs back, decodes, and reads the bf16 result back to the
@@ -374,7 +375,7 @@ def main() -> None:
     blobV = torch.empty(blob_cap, dtype=torch.uint8, pin_memory=True)
     decK = torch.empty(ELEMS, dtype=torch.bfloat16, pin_memory=True)
     decV = torch.empty(ELEMS, dtype=torch.bfloat16, pin_memory=True)
-    codec.decode_pinned(codec.encode_pinned(pinK, blobK), decK)  # warm
+    codec.decode_pinned_batch(codec.encode_pinned_batch([pinK, pinV], [blobK, blobV]), [decK, decV])  # warm
     h2d = d2h = 0
     t_e2e = 0.0
     torch.cuda.synchronize()
@@ -382,10 +383,8 @@ def main() -> None:
         dist.barrier()
     for _ in range(args.e2e_steps):
         t0 = time.perf_counter()
-        bk = codec.encode_pinned(pinK, blobK)
-        bv = codec.encode_pinned(pinV, blobV)
-        dk = codec.decode_pinned(bk, decK)
-        dv = codec.decode_pinned(bv, decV)
+        bk, bv = codec.encode_pinned_batch([pinK, pinV], [blobK, blobV])
+        dk, dv = codec.decode_pinned_batch([bk, bv], [decK, decV])
         t_e2e += time.perf_counter() - t0
         h2d = 2 * ELEMS * 2 + (bk.numel() - 8) + (bv.numel() - 8)
         d2h = bk.numel() + bv.numel() + 2 * (dk.numel() + dv.numel())
@@ -445,7 +444,7 @@ def main() -> None:
             "decode": {"kernel": "nbit_decode_kernel<4>", "avg_launch_ms": round(dec_ms, 4),
                        "achieved_gbs": round(dec_achieved, 1), "frac": round(dec_achieved / peak, 4)},
             "e2e": {"value": round(e2e_value, 3), "unit": "GB/s", "h2d_bytes_per_step": h2d,
-                    "d2h_bytes_per_step": d2h, "api": "DitheredNBitCodec.encode_pinned/decode_pinned",
+                    "d2h_bytes_per_step": d2h, "api": "DitheredNBitCodec.encode_pinned_batch/decode_pinned_batch",
                     "steps": args.e2e_steps},
             "e2e_bytes_api": None if e2e_bytes_value is None else
             {"value": round(e2e_bytes_value, 3), "unit": "GB/s", "api": "DitheredNBitCodec.encode/decode(bytes)",

@@ -310,6 +310,14 @@ def test_nbit_pinned_api_matches_bytes_api(cuda, bits, hidden):
         out = torch.empty(x.numel() + 8, dtype=torch.bfloat16, pin_memory=True)
         dec = b.decode_pinned(pblob, out)
         assert dec.view(torch.int16).numpy().tobytes() == a.decode(blob)
+    # batched calls: the same blobs and seeds as the same calls made one by one
+    y = rand_bf16(190 * hidden, 72, "wide")
+    seq, bat = DitheredNBitCodec(hidden_dim=hidden, bits=bits), DitheredNBitCodec(hidden_dim=hidden, bits=bits)
+    want = [seq.encode(bits_of(t).tobytes()) for t in (x, y, x)]
+    got = bat.encode_pinned_batch([x.pin_memory(), y.pin_memory(), x])
+    assert [g.numpy().tobytes() for g in got] == want
+    back = bat.decode_pinned_batch(got)
+    assert [t.view(torch.int16).numpy().tobytes() for t in back] == [seq.decode(w) for w in want]
     c = DitheredINT2Codec()
     u = torch.rand(x.numel() // 128 * 128)
     assert c.encode_pinned(x, uniform=u).numpy().tobytes() == c.encode(data, uniform=u)
