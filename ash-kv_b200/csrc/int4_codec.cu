@@ -66,61 +66,84 @@ __device__ __forceinline__ float group_max_finish(float m) {
 // ---------------------------------------------------------------- fast encode
 // TPG = G/8 threads per group, 8 values per thread (one 16-byte load) -> one
 // 32-bit store of 8 nibbles.  Values at index >= n are the zero padding.
+__device__ __forceinline__ uint4 load_chunk(const uint16_t* __restrict__ src, int64_t n, int64_t c, bool active) {
+  const int64_t e0 = c * 8;
+  if (!active) return make_uint4(0u, 0u, 0u, 0u);
+  if (e0 + 8 <= n) return ld_nc_v4(src + e0);
+  uint32_t w[4];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const uint32_t lo = e0 + 2 * k < n ? src[e0 + 2 * k] : 0u;
+    const uint32_t hi = e0 + 2 * k + 1 < n ? src[e0 + 2 * k + 1] : 0u;
+    w[k] = lo | (hi << 16);
+  }
+  return make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+// Called by every lane of the warp (the group maximum is a shuffle reduction).
+template <int TPG>
+__device__ __forceinline__ void encode_chunk(uint4 v, int64_t c, bool active, uint16_t* __restrict__ scales,
+                                             uint32_t* __restrict__ packed) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+  float x[8];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) { x[2 * k] = bf16lo(w[k]); x[2 * k + 1] = bf16hi(w[k]); }
+  float m = max3_abs_nan(x[0], x[1], x[2]);
+  m = max3_abs_nan(m, x[3], x[4]);
+  m = max3_abs_nan(m, x[5], x[6]);
+  m = max3_abs_nan(m, x[7], x[7]);
+#pragma unroll
+  for (int off = 1; off < TPG; off <<= 1) m = max_nan(m, __shfl_xor_sync(0xFFFFFFFFu, m, off));
+  const float am = group_max_finish(m);
+  if (!active) return;
+  if ((c % TPG) == 0) scales[c / TPG] = static_cast<uint16_t>(bf16_cpu(am));
+  uint32_t out = 0;
+  const GroupDiv d = group_div(am);
+  if (d.mode == 0) {
+    // am finite and in Markstein's range: every x is finite and |x| <= am, so
+    // v = RN(RN(7x)/am) lies in [-7, 7] and numpy's cast and clip are the
+    // identity; RN(v + 1.5*2^23 + 8) leaves rint(v) + 8 (ties to even, 8 being
+    // even) in the low 4 bits.
+    const f2 yhi = pk2(d.y.hi, d.y.hi), ylo = pk2(d.y.lo, d.y.lo), nb = pk2(-am, -am);
+    const f2 seven = pk2(7.0f, 7.0f), magic = pk2(12582920.0f, 12582920.0f);
+    uint32_t t[8];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      float v0, v1;
+      upk2(add2(div2_rn(mul2(pk2(x[2 * k], x[2 * k + 1]), seven), yhi, ylo, nb), magic), v0, v1);
+      t[2 * k] = __float_as_uint(v0);
+      t[2 * k + 1] = __float_as_uint(v1);
+    }
+    // bytes m0..m3 and m4..m7 (each t's low byte is its nibble value, < 16)
+    const uint32_t X = __byte_perm(__byte_perm(t[0], t[1], 0x0040), __byte_perm(t[2], t[3], 0x0040), 0x5410);
+    const uint32_t Y = __byte_perm(__byte_perm(t[4], t[5], 0x0040), __byte_perm(t[6], t[7], 0x0040), 0x5410);
+    // byte j of X*16 + (X >> 8) is (m_j << 4) + m_{j+1}: keep bytes 0 and 2 of each
+    out = __byte_perm(X * 16u + (X >> 8), Y * 16u + (Y >> 8), 0x6420);
+  } else {
+#pragma unroll
+    for (int k = 0; k < 4; ++k)
+      out |= ((nibble_of(x[2 * k], d) << 4) | nibble_of(x[2 * k + 1], d)) << (8 * k);
+  }
+  packed[c] = out;
+}
+
+// Two chunks per lane per iteration (c and c + stride), both loaded before
+// either is encoded.  The loop runs per warp (c0 = the warp's first chunk) so
+// that every lane takes part in the shuffles; n_chunks is a multiple of TPG,
+// so the lanes of one group are all active or all idle.
 template <int TPG>
 __global__ void __launch_bounds__(256) int4_encode_fast(const uint16_t* __restrict__ src, int64_t n,
                                                         int64_t n_chunks, uint16_t* __restrict__ scales,
                                                         uint32_t* __restrict__ packed) {
   const int64_t stride = int64_t(gridDim.x) * blockDim.x;
   const int lane = threadIdx.x & 31;
-  // The loop runs per warp (c0 = the warp's first chunk) so that every lane
-  // takes part in the shuffles; n_chunks is a multiple of TPG, so the lanes
-  // of one group are all active or all idle.
-  for (int64_t c0 = int64_t(blockIdx.x) * blockDim.x + (threadIdx.x & ~31); c0 < n_chunks; c0 += stride) {
-    const int64_t c = c0 + lane;
-    const bool active = c < n_chunks;
-    const int64_t e0 = c * 8;
-    uint32_t w[4] = {0u, 0u, 0u, 0u};
-    if (!active) {
-    } else if (e0 + 8 <= n) {
-      const uint4 v = ld_nc_v4(src + e0);
-      w[0] = v.x; w[1] = v.y; w[2] = v.z; w[3] = v.w;
-    } else {
-#pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        const uint32_t lo = e0 + 2 * k < n ? src[e0 + 2 * k] : 0u;
-        const uint32_t hi = e0 + 2 * k + 1 < n ? src[e0 + 2 * k + 1] : 0u;
-        w[k] = lo | (hi << 16);
-      }
-    }
-    float x[8];
-#pragma unroll
-    for (int k = 0; k < 4; ++k) { x[2 * k] = bf16lo(w[k]); x[2 * k + 1] = bf16hi(w[k]); }
-    float m = max3_abs_nan(x[0], x[1], x[2]);
-    m = max3_abs_nan(m, x[3], x[4]);
-    m = max3_abs_nan(m, x[5], x[6]);
-    m = max3_abs_nan(m, x[7], x[7]);
-#pragma unroll
-    for (int off = 1; off < TPG; off <<= 1) m = max_nan(m, __shfl_xor_sync(0xFFFFFFFFu, m, off));
-    const float am = group_max_finish(m);
-    if (!active) continue;
-    if ((c % TPG) == 0) scales[c / TPG] = static_cast<uint16_t>(bf16_cpu(am));
-    uint32_t out = 0;
-    const GroupDiv d = group_div(am);
-    if (d.mode == 0) {
-      const f2 yhi = pk2(d.y.hi, d.y.hi), ylo = pk2(d.y.lo, d.y.lo), nb = pk2(-am, -am);
-      const f2 seven = pk2(7.0f, 7.0f);
-#pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        float q0, q1;
-        upk2(div2_rn(mul2(pk2(x[2 * k], x[2 * k + 1]), seven), yhi, ylo, nb), q0, q1);
-        out |= ((nibble_np(q0) << 4) | nibble_np(q1)) << (8 * k);
-      }
-    } else {
-#pragma unroll
-      for (int k = 0; k < 4; ++k)
-        out |= ((nibble_of(x[2 * k], d) << 4) | nibble_of(x[2 * k + 1], d)) << (8 * k);
-    }
-    packed[c] = out;
+  for (int64_t c0 = int64_t(blockIdx.x) * blockDim.x + (threadIdx.x & ~31); c0 < n_chunks; c0 += 2 * stride) {
+    const int64_t ca = c0 + lane, cb = ca + stride;
+    const bool act_a = ca < n_chunks, act_b = cb < n_chunks;
+    const uint4 va = load_chunk(src, n, ca, act_a);
+    const uint4 vb = load_chunk(src, n, cb, act_b);
+    encode_chunk<TPG>(va, ca, act_a, scales, packed);
+    encode_chunk<TPG>(vb, cb, act_b, scales, packed);
   }
 }
 

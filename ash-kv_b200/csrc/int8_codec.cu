@@ -76,23 +76,37 @@ __device__ __forceinline__ uint8_t* scale_addr(uint8_t* base, int64_t r, int32_t
 }
 
 // Each thread owns NCH chunks of 8 consecutive elements of its row.
-template <bool FP16, int NCH, int TEAM>
-__global__ void __launch_bounds__(256) int8_encode_kernel(const Int8EncParams p) {
-  constexpr int ROWS_PER_CTA = 256 / TEAM;
-  const int lane_in_team = threadIdx.x % TEAM;
-  const int64_t r = int64_t(blockIdx.x) * ROWS_PER_CTA + threadIdx.x / TEAM;
-  const bool active = r < p.n_rows;
+// bf16 rows of up to 2 chunks per lane take two rows per team, both loaded
+// before either is encoded (more bytes in flight per thread).
+template <bool FP16, int NCH>
+__host__ __device__ constexpr int enc_rows_per_team() { return (!FP16 && NCH <= 2) ? 2 : 1; }
 
+template <int NCH>
+struct LoadedRow {
   uint4 chunk[NCH];
+  float am;
+};
+
+template <bool FP16, int NCH, int TEAM>
+__device__ __forceinline__ void load_row(const Int8EncParams& p, int64_t r, bool active, int lane_in_team,
+                                         LoadedRow<NCH>& L) {
+  L.am = 0.0f;
+  if (!active) return;
+  const int64_t src_row = p.row_index ? p.row_index[r] : r;
+  const uint16_t* row = p.src + src_row * p.src_stride;
+#pragma unroll
+  for (int c = 0; c < NCH; ++c) L.chunk[c] = ld_nc_v4(row + (int64_t(c) * TEAM + lane_in_team) * 8);
+}
+
+// Called by every lane of the warp (the row maximum is a shuffle reduction).
+template <bool FP16, int NCH, int TEAM>
+__device__ __forceinline__ void encode_loaded_row(const Int8EncParams& p, int64_t r, bool active, int lane_in_team,
+                                                  LoadedRow<NCH>& L) {
   float am = 0.0f;
-  const uint16_t* row = nullptr;
   if (active) {
-    const int64_t src_row = p.row_index ? p.row_index[r] : r;
-    row = p.src + src_row * p.src_stride;
 #pragma unroll
     for (int c = 0; c < NCH; ++c) {
-      chunk[c] = ld_nc_v4(row + (int64_t(c) * TEAM + lane_in_team) * 8);
-      const uint32_t w[4] = {chunk[c].x, chunk[c].y, chunk[c].z, chunk[c].w};
+      const uint32_t w[4] = {L.chunk[c].x, L.chunk[c].y, L.chunk[c].z, L.chunk[c].w};
 #pragma unroll
       for (int k = 0; k < 4; ++k) {
         am = fmaxf(am, fabsf(in_lo<FP16>(w[k])));  // fmaxf ignores NaN, like tl.maximum
@@ -117,7 +131,7 @@ __global__ void __launch_bounds__(256) int8_encode_kernel(const Int8EncParams p)
   const Int8Div d = int8_div(am, products_finite<FP16>(am, f32p));
 #pragma unroll
   for (int c = 0; c < NCH; ++c) {
-    const uint32_t w[4] = {chunk[c].x, chunk[c].y, chunk[c].z, chunk[c].w};
+    const uint32_t w[4] = {L.chunk[c].x, L.chunk[c].y, L.chunk[c].z, L.chunk[c].w};
     uint32_t packed[2];
     if (!FP16 && !f32p) {
       packed[0] = int8_codes4_bf16(w[0], w[1], d);
@@ -138,6 +152,26 @@ __global__ void __launch_bounds__(256) int8_encode_kernel(const Int8EncParams p)
       }
     }
     *reinterpret_cast<uint2*>(out + (int64_t(c) * TEAM + lane_in_team) * 8) = make_uint2(packed[0], packed[1]);
+  }
+}
+
+// Each thread owns NCH chunks of 8 consecutive elements of its row(s).
+template <bool FP16, int NCH, int TEAM>
+__global__ void __launch_bounds__(256) int8_encode_kernel(const Int8EncParams p) {
+  constexpr int ROWS_PER_PASS = 256 / TEAM;
+  constexpr int RPT = enc_rows_per_team<FP16, NCH>();
+  const int lane_in_team = threadIdx.x % TEAM;
+  const int64_t r0 = int64_t(blockIdx.x) * (ROWS_PER_PASS * RPT) + threadIdx.x / TEAM;
+  LoadedRow<NCH> L[RPT];
+#pragma unroll
+  for (int u = 0; u < RPT; ++u) {
+    const int64_t r = r0 + int64_t(u) * ROWS_PER_PASS;
+    load_row<FP16, NCH, TEAM>(p, r, r < p.n_rows, lane_in_team, L[u]);
+  }
+#pragma unroll
+  for (int u = 0; u < RPT; ++u) {
+    const int64_t r = r0 + int64_t(u) * ROWS_PER_PASS;
+    encode_loaded_row<FP16, NCH, TEAM>(p, r, r < p.n_rows, lane_in_team, L[u]);
   }
 }
 
@@ -250,7 +284,8 @@ bool pick_team(int32_t row_len, int& team, int& nch) {
 
 #define ASHKV_ENC_CASE(FP, NC, TM)                                                        \
   if (nch == NC && team == TM) {                                                          \
-    int8_encode_kernel<FP, NC, TM><<<unsigned((p.n_rows + 256 / TM - 1) / (256 / TM)), 256, 0, st>>>(p); \
+    int8_encode_kernel<FP, NC, TM><<<unsigned((p.n_rows + (256 / TM) * enc_rows_per_team<FP, NC>() - 1) /      \
+                                             ((256 / TM) * enc_rows_per_team<FP, NC>())), 256, 0, st>>>(p);           \
     return check_launch("int8_encode");                                                  \
   }
 

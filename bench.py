@@ -171,6 +171,69 @@ def cpu_port_rate(threads: int, budget_s: float) -> tuple[float, dict]:
                             f"encode+decode, Philox dither"}
 
 
+def codec_suite(K: torch.Tensor, V: torch.Tensor, peak: float, iters: int = 20) -> dict:
+    """Every registered codec's kernels on the K/V tensors (67M bf16 elements each,
+    alternated so the 128 MiB inputs do not stay in L2): average CUDA-event time per
+    launch, algorithmic bytes / time, and the fraction of the HBM peak."""
+    from ashkv.codecs import fp8 as fp8m, int4 as int4m, int8 as int8m
+    from ashkv.codecs import nbit_dithered as nb
+
+    E = K.numel()
+    st = torch.cuda.current_stream(K.device)
+
+    def timed(fn_a, fn_b) -> float:
+        for _ in range(3):
+            fn_a(); fn_b()
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(2 * iters + 1)]
+        torch.cuda.synchronize()
+        ev[0].record(st)
+        for i in range(iters):
+            (fn_a if i % 2 == 0 else fn_b)()
+            ev[i + 1].record(st)
+        torch.cuda.synchronize()
+        return statistics.mean(ev[i].elapsed_time(ev[i + 1]) for i in range(iters))
+
+    def entry(kernel: str, nbytes: int, ms: float) -> dict:
+        gbs = nbytes / (ms / 1e3) / 1e9
+        return {"kernel": kernel, "avg_launch_ms": round(ms, 4), "alg_bytes": nbytes, "achieved_gbs": round(gbs, 1),
+                "frac": round(gbs / peak, 4)}
+
+    out = {}
+    Kr, Vr = K.view(-1, 128), V.view(-1, 128)
+    cK, sK = int8m.encode_rows(Kr)
+    cV, sV = int8m.encode_rows(Vr)
+    oK, oV = torch.empty_like(Kr), torch.empty_like(Vr)
+    ms = timed(lambda: int8m.encode_rows(Kr, codes=cK, scales=sK), lambda: int8m.encode_rows(Vr, codes=cV, scales=sV))
+    out["int8_rows_L128_encode"] = entry("int8_encode_kernel<bf16,1,16>", 3 * E + 2 * (E // 128), ms)
+    ms = timed(lambda: int8m.decode_rows(cK, sK, out=oK), lambda: int8m.decode_rows(cV, sV, out=oV))
+    out["int8_rows_L128_decode"] = entry("int8_decode_kernel<1,16>", 3 * E + 2 * (E // 128), ms)
+    fK, fV = fp8m.encode_tensor(K), fp8m.encode_tensor(V)
+    bK, bV = torch.empty_like(K), torch.empty_like(V)
+    ms = timed(lambda: fp8m.encode_tensor(K, out=fK), lambda: fp8m.encode_tensor(V, out=fV))
+    out["fp8_encode"] = entry("fp8_encode_v16", 3 * E, ms)
+    ms = timed(lambda: fp8m.decode_tensor(fK, out=bK), lambda: fp8m.decode_tensor(fV, out=bV))
+    out["fp8_decode"] = entry("fp8_decode_v16", 3 * E, ms)
+    s4K, p4K, _ = int4m.encode_tensor(K, 64)
+    s4V, p4V, _ = int4m.encode_tensor(V, 64)
+    i4 = 2 * E + E // 2 + 2 * (E // 64)
+    ms = timed(lambda: int4m.encode_tensor(K, 64, scales=s4K, packed=p4K),
+               lambda: int4m.encode_tensor(V, 64, scales=s4V, packed=p4V))
+    out["int4_g64_encode"] = entry("int4_encode_fast<8>", i4, ms)
+    ms = timed(lambda: int4m.decode_tensor(s4K, p4K, 64, out=bK), lambda: int4m.decode_tensor(s4V, p4V, 64, out=bV))
+    out["int4_g64_decode"] = entry("int4_decode_fast<16>", i4, ms)
+    cap = nb._native.NBIT_BUCKET_GROUPS * nb.max_outliers_per_group(SIGMA)
+    e2K = nb.NBitEncoded.allocate(E // 32, 2, cap, K.device)
+    e2V = nb.NBitEncoded.allocate(E // 32, 2, cap, K.device)
+    ms = timed(lambda: nb.encode_groups(K, 2, SIGMA, seed=42, out=e2K), lambda: nb.encode_groups(V, 2, SIGMA, seed=42, out=e2V))
+    n_out = int(e2K.bucket_counts.sum().item())
+    nbk = nb._native.nbit_bucket_count(E // 32)
+    i2 = 2 * E + E // 4 + 2 * (E // 32) + 4 * n_out + 4 * nbk
+    out["int2_dithered_encode"] = entry("nbit_encode_tma_kernel<2,PHILOX,3>", i2, ms)
+    ms = timed(lambda: nb.decode_groups(e2K, out=bK), lambda: nb.decode_groups(e2V, out=bV))
+    out["int2_dithered_decode"] = entry("nbit_decode_kernel<2>", i2, ms)
+    return out
+
+
 def run_reference(args) -> None:
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
@@ -298,6 +361,7 @@ def main() -> None:
     ap.add_argument("--ref-seconds", type=float, default=5.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-demote", action="store_true")
+    ap.add_argument("--no-codec-suite", action="store_true")
     ap.add_argument("--demote-steps", type=int, default=10)
     ap.add_argument("--demote-layers", type=int, default=DEMOTE_LAYERS,
                     help="layers of the config-4 model (64; fewer only for small profiling cases)")
@@ -325,7 +389,7 @@ def main() -> None:
 
     K = make_kv(1000 + 2 * rank, dev)
     V = make_kv(1001 + 2 * rank, dev)
-    cap = 256 * nb.max_outliers_per_group(SIGMA)
+    cap = nb._native.NBIT_BUCKET_GROUPS * nb.max_outliers_per_group(SIGMA)  # never overflows
     encK = nb.NBitEncoded.allocate(ELEMS // 32, BITS, cap, dev)
     encV = nb.NBitEncoded.allocate(ELEMS // 32, BITS, cap, dev)
     outK = torch.empty_like(K)
@@ -403,6 +467,28 @@ def main() -> None:
         codec.decode(codec.encode(hostV))
         t_bytes += time.perf_counter() - t0
 
+    # quality, outside every timed region: the reference's cosine (flattened fp32
+    # tensors), outlier count, and bit-exactness of a 1M-element sample against the oracle
+    quality = None
+    suite = None
+    if rank == 0 and not args.no_codec_suite:
+        suite = codec_suite(K, V, measured_hbm_peak()[0])
+    if rank == 0:
+        import oracle
+        encQ = nb.encode_groups(K, BITS, SIGMA, seed=42)
+        decQ = nb.decode_groups(encQ)
+        cos = torch.nn.functional.cosine_similarity(K.float().view(-1), decQ.float().view(-1), dim=0).item()
+        m = 1 << 20
+        xs = K.view(-1)[:m].cpu().view(torch.int16).numpy().view(np.uint16)
+        osc, ocodes, oidx, ovals = oracle.nbit_encode(xs, BITS, oracle.philox_dither(m, 42, 0), SIGMA)
+        odec = oracle.nbit_decode(osc, ocodes, BITS, oidx, ovals)
+        mism = int((encQ.scales[: m // 32].cpu().view(torch.int16).numpy().view(np.uint16) != osc).sum()
+                   + (encQ.codes[: m * BITS // 8].cpu().numpy() != ocodes).sum()
+                   + (decQ[:m].cpu().view(torch.int16).numpy().view(np.uint16) != odec).sum())
+        quality = {"cosine_K": round(cos, 6), "outliers_K": int(encQ.bucket_counts.sum().item()),
+                   "outlier_fraction": round(int(encQ.bucket_counts.sum().item()) / ELEMS, 6),
+                   "oracle_sample_elements": m, "oracle_sample_mismatches": mism}
+
     # max over ranks
     t = torch.tensor([elapsed_ms, t_e2e, t_bytes], dtype=torch.float64, device=dev)
     if dist:
@@ -439,6 +525,7 @@ def main() -> None:
             "encode_gbs_bf16": round(world * ELEMS * 2 / (enc_ms / 1e3) / 1e9, 2),
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "traffic": traffic, "peak_kind": peak_kind,
+                         "frac_of_nominal_8000": round(achieved / 8000.0, 4),
                          "kernel": "nbit_encode_tma_kernel<4,PHILOX,3>",
                          "alg_bytes_per_launch": enc_alg_bytes, "avg_launch_ms": round(enc_ms, 4)},
             "decode": {"kernel": "nbit_decode_kernel<4>", "avg_launch_ms": round(dec_ms, 4),
@@ -449,6 +536,8 @@ def main() -> None:
             "e2e_bytes_api": None if e2e_bytes_value is None else
             {"value": round(e2e_bytes_value, 3), "unit": "GB/s", "api": "DitheredNBitCodec.encode/decode(bytes)",
              "steps": args.e2e_bytes_steps},
+            "quality": quality,
+            "codecs": suite,
             "gpu_launches": 4 * args.steps,
             "clocks": clocks.summary(),
             "cpu_baseline": cpu,
