@@ -60,6 +60,9 @@ SIGNATURES: dict[str, tuple] = {
     "ashkv_fp8_decode": (_I32, [_P, _I64, _P, _P]),
     "ashkv_int4_group_count": (_I64, [_I64, _I32]),
     "ashkv_nbit_flatten_scratch_ints": (_I64, [_I64]),
+    "ashkv_saliency_scratch_floats": (_I64, [_I32, _I64, _I64]),
+    "ashkv_attention_saliency": (_I32, [_P, _P, _I32, _I32, _I32, _I64, _I64, _I64, _F32, _P, _P, _P, _P]),
+    "ashkv_page_features": (_I32, [_P, _P, _I32, _I64, _I32, _P, _P, _P, _P]),
     "ashkv_int4_encode": (_I32, [_P, _I64, _I32, _P, _P, _P]),
     "ashkv_int4_decode": (_I32, [_P, _P, _I64, _I32, _P, _P]),
 }
@@ -309,6 +312,42 @@ def int4_decode(scales: torch.Tensor, packed: torch.Tensor, n_groups: int, group
         raise ValueError("int4_decode: buffer sizes do not match n_groups * group_size")
     check(lib().ashkv_int4_decode(scales.data_ptr(), packed.data_ptr(), n_groups, group_size, dst.data_ptr(),
                                   stream_handle(dst.device)), "int4_decode")
+
+
+# --------------------------------------------------------------------------- page features
+def saliency_scratch_floats(heads_q: int, n_q: int, n_k: int) -> int:
+    return int(lib().ashkv_saliency_scratch_floats(heads_q, n_q, n_k))
+
+
+def attention_saliency(q: torch.Tensor, k: torch.Tensor, q_pos0: int, scale: float, scratch: torch.Tensor,
+                       out: torch.Tensor, status: torch.Tensor) -> None:
+    """q [n_q, heads_q, head_dim], k [n_k, heads_kv, head_dim] bf16 -> out[n_k] fp32 attention mass per key."""
+    _require_cuda(q, k, scratch, out, status)
+    if q.dtype != torch.bfloat16 or k.dtype != torch.bfloat16 or q.dim() != 3 or k.dim() != 3:
+        raise TypeError("attention_saliency takes bf16 tensors [tokens, heads, head_dim]")
+    if not (q.is_contiguous() and k.is_contiguous()):
+        raise ValueError("attention_saliency: q and k must be contiguous")
+    n_q, hq, d = q.shape
+    n_k, hkv, dk = k.shape
+    if dk != d:
+        raise ValueError("q and k head_dim differ")
+    if scratch.numel() < saliency_scratch_floats(hq, n_q, n_k) or out.numel() < n_k:
+        raise ValueError("attention_saliency: scratch or out too small")
+    check(lib().ashkv_attention_saliency(q.data_ptr(), k.data_ptr(), hq, hkv, d, n_q, n_k, q_pos0, scale,
+                                         scratch.data_ptr(), out.data_ptr(), status.data_ptr(),
+                                         stream_handle(q.device)), "attention_saliency")
+
+
+def page_features(token_saliency: Optional[torch.Tensor], k: torch.Tensor, tokens_per_page: int,
+                  s_raw: Optional[torch.Tensor], S: Optional[torch.Tensor], N: torch.Tensor) -> None:
+    _require_cuda(token_saliency, k, s_raw, S, N)
+    n_k = k.shape[0]
+    row_len = k[0].numel() if n_k else 1
+    n_pages = -(-n_k // tokens_per_page)
+    if N.numel() < n_pages or (token_saliency is not None and (S.numel() < n_pages or s_raw.numel() < n_pages)):
+        raise ValueError("page_features: outputs too small")
+    check(lib().ashkv_page_features(_ptr(token_saliency), k.data_ptr(), row_len, n_k, tokens_per_page, _ptr(s_raw),
+                                    _ptr(S), N.data_ptr(), stream_handle(k.device)), "page_features")
 
 
 # --------------------------------------------------------------------------- policy

@@ -1,6 +1,7 @@
 // Library-level entry points: version, status text, last CUDA error.
 #include <cstdio>
 #include <cstring>
+#include <mutex>
 
 #include "common.cuh"
 
@@ -19,6 +20,21 @@ ashkv_status_t check_launch(const char* what) {
   if (err == cudaSuccess) return ASHKV_OK;
   set_error(what, err);
   return ASHKV_LAUNCH_ERROR;
+}
+
+void* tensor_map_encoder() {
+  static void* fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &ptr, 12000, cudaEnableDefault, &q) ==
+            cudaSuccess && q == cudaDriverEntryPointSuccess)
+      fn = ptr;
+    else
+      cudaGetLastError();
+  });
+  return fn;
 }
 
 int sm_count() {

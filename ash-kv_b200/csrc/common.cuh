@@ -24,6 +24,10 @@ inline bool aligned(const void* p, uintptr_t a) {
 
 int sm_count();
 
+// cuTensorMapEncodeTiled fetched once through the runtime's driver entry point
+// (no -lcuda); nullptr when unavailable.  Cast to PFN_cuTensorMapEncodeTiled_v12000.
+void* tensor_map_encoder();
+
 // ---------------------------------------------------------------- bf16/fp16
 __device__ __forceinline__ float bf16lo(uint32_t w) { return __uint_as_float(w << 16); }
 __device__ __forceinline__ float bf16hi(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }

@@ -1,0 +1,490 @@
+// Attention-derived page features on sm_100a: saliency (tcgen05 tensor cores,
+// TMEM accumulators, TMA-fed shared memory) and key novelty.
+//
+// Saliency restates the reference simulator's attention mass per key
+// (ashkv/tests/simulator.py:66-80):
+//   s[h,i,j]  = (q_i . k_j) * scale,  masked to -inf unless key position j <= query position
+//   P[h,i,:]  = softmax_j(s[h,i,:])
+//   sal[j]    = sum over heads h and queries i of P[h,i,j]
+// in two tensor-core passes over the score tiles (the softmax normaliser of
+// every query row first, then each key row's column mass), with fp32
+// accumulation in TMEM.  The reference keeps only this per-token quantity;
+// per page it is summed over the page's tokens and divided by the largest
+// page's mass (S in [0, 1]), and the novelty input is the mean over the page
+// of ||k_t - k_{t-1}||^2 / (||k_t||^2 + ||k_{t-1}||^2) / 2 (in [0, 1]).
+//
+// Tiles: 128 queries x 128 keys per MMA group (M = N = 128, K = head_dim in
+// steps of 16), bf16 operands in 128-byte-swizzled K-major shared memory
+// (one 16 KiB chunk per 64 elements of head_dim), one fp32 accumulator of 128
+// TMEM columns per tile, two accumulators so the next tile's MMA overlaps this
+// tile's epilogue.  One thread per TMEM lane (accumulator row) runs the
+// epilogue, so no cross-thread reduction is needed: pass 1 keeps the online
+// max/sum of its query row, pass 2 (keys x queries) sums its key row.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include "common.cuh"
+
+namespace ashkv {
+namespace {
+
+constexpr int kTile = 128;                   // rows of a query or key tile
+constexpr int kChunkBytes = kTile * 128;     // 128 rows x 64 bf16 (one swizzle atom column) = 16 KiB
+constexpr int kThreadsF = 128;               // 4 warps: one TMEM lane per thread
+constexpr uint32_t kPolls = 1u << 24;        // bounded mbarrier waits
+constexpr uint32_t kAccCols = 256;           // two 128-column fp32 accumulators
+
+// ---------------------------------------------------------------- tcgen05 / TMA wrappers
+__device__ __forceinline__ void tmem_alloc(uint32_t* smem_dst, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
+               :: "r"(smem_u32(smem_dst)), "r"(ncols) : "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" :: "r"(taddr), "r"(ncols) : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// D[tmem] (+)= A * B^T, A: M x K and B: N x K, both K-major bf16 in shared memory.
+__device__ __forceinline__ void umma_bf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                          uint32_t accumulate) {
+  asm volatile("{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+               "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}"
+               :: "r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate),
+                  "r"(0u), "r"(0u), "r"(0u), "r"(0u) : "memory");
+}
+// Arrive on `bar` once every MMA this thread issued so far has completed.
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
+               :: "r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+               : "r"(taddr));
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row atoms of
+// 128 bytes stacked every 1024 bytes (stride byte offset), sm_100 version 1.
+__device__ __forceinline__ uint64_t sw128_kmajor_desc(uint32_t smem_addr) {
+  uint64_t d = uint64_t((smem_addr >> 4) & 0x3FFFu);  // start address (16-byte units)
+  d |= uint64_t(1) << 16;                              // leading byte offset: unused for swizzled K-major
+  d |= uint64_t(1024 >> 4) << 32;                      // stride byte offset
+  d |= uint64_t(1) << 46;                              // descriptor version
+  d |= uint64_t(2) << 61;                              // SWIZZLE_128B
+  return d;
+}
+// Instruction descriptor: kind::f16, A = B = bf16, D = f32, both K-major, M = N = 128.
+constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t(kTile) >> 3) << 17) |
+                            ((uint32_t(kTile) >> 4) << 24);
+
+__device__ __forceinline__ void tma_load_3d(void* smem_dst, const void* tmap, uint64_t* bar, int32_t x, int32_t y,
+                                            int32_t z) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];"
+      :: "r"(smem_u32(smem_dst)), "l"(tmap), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+struct SalParams {
+  int32_t heads_q, group, nch;  // group = heads_q / heads_kv; nch = head_dim / 64
+  int64_t n_q, n_k, q_pos0;
+  float c;                      // scale * log2(e)
+  float* lse2;                  // [heads_q, n_q]: log2 of sum_j 2^(s_ij * c)
+  float* colsum;                // [heads_q, n_k]
+  uint32_t* status;
+};
+
+// Loads `rows` tile t (all head_dim chunks) of head `head` into dst, arriving on bar.
+__device__ __forceinline__ void load_tile(const CUtensorMap* map, uint8_t* dst, uint64_t* bar, int nch, int head,
+                                          int64_t t) {
+  mbar_arrive_expect_tx(bar, uint32_t(nch * kChunkBytes));
+  for (int c = 0; c < nch; ++c) tma_load_3d(dst + c * kChunkBytes, map, bar, c * 64, head, int32_t(t * kTile));
+}
+
+// One tile's MMA group: acc (+)= A_tile * B_tile^T over head_dim.
+__device__ __forceinline__ void mma_tile(uint32_t acc, const uint8_t* a, const uint8_t* b, int nch) {
+  const uint32_t sa = smem_u32(a), sb = smem_u32(b);
+  for (int c = 0; c < nch; ++c)
+#pragma unroll
+    for (int j = 0; j < 4; ++j)  // K = 16 per MMA: 32 bytes further along the swizzled row
+      umma_bf16(acc, sw128_kmajor_desc(sa + c * kChunkBytes + j * 32), sw128_kmajor_desc(sb + c * kChunkBytes + j * 32),
+                kIdesc, (c | j) != 0);
+}
+
+// Shared layout of both passes: [A tile][B tile 0][B tile 1], 1024-byte aligned.
+struct PassSmem {
+  uint8_t* a;
+  uint8_t* b[2];
+};
+__device__ __forceinline__ PassSmem carve(uint8_t* raw, int nch) {
+  uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(raw) + 1023) & ~uintptr_t(1023));
+  PassSmem s;
+  s.a = base;
+  s.b[0] = base + nch * kChunkBytes;
+  s.b[1] = base + 2 * nch * kChunkBytes;
+  return s;
+}
+
+// The pipelined loop shared by both passes.  A (the CTA's fixed tile) is
+// loaded once; B tiles t = t0 .. t0 + nt - 1 stream through two buffers; the
+// MMA of tile i + 1 is issued before the epilogue of tile i.  `epi(i, acc)`
+// is called by every thread with the TMEM address of its accumulator row.
+// Returns false (and sets ASHKV_FLAG_TIMEOUT) if a bounded wait gave up; all
+// issued MMAs have completed when it returns.
+template <class Epi>
+__device__ bool run_tiles(const CUtensorMap* amap, int a_head, int64_t a_tile, const CUtensorMap* bmap, int b_head,
+                          int64_t t0, int nt, int nch, const PassSmem& sm, uint64_t* bar_a, uint64_t* bar_b,
+                          uint64_t* bar_mma, uint32_t tmem, uint32_t* status, Epi epi) {
+  const int tid = threadIdx.x, warp = tid >> 5;
+  __shared__ int s_fail;
+  // thread 0's record of the B tile loads: issued up to b_loaded, awaited up to b_waited
+  int b_loaded = -1, b_waited = -1;
+  bool a_waited = false;
+  if (tid == 0) {
+    s_fail = 0;
+    load_tile(amap, sm.a, bar_a, nch, a_head, a_tile);
+    for (int i = 0; i < 2 && i < nt; ++i) {
+      load_tile(bmap, sm.b[i], &bar_b[i], nch, b_head, t0 + i);
+      b_loaded = i;
+    }
+    a_waited = mbar_wait_bounded(bar_a, 0, kPolls);
+    if (!a_waited || !mbar_wait_bounded(&bar_b[0], 0, kPolls)) {
+      s_fail = 1;
+    } else {
+      b_waited = 0;
+      tc_fence_after();
+      mma_tile(tmem, sm.a, sm.b[0], nch);
+      umma_commit(&bar_mma[0]);
+    }
+  }
+  __syncthreads();
+  int issued = s_fail ? -1 : 0;  // last tile whose MMA was issued (same value in every thread)
+  int done = -1;                 // last tile whose MMA completion every thread has seen
+  bool ok = !s_fail;
+  for (int i = 0; ok && i < nt; ++i) {
+    const int buf = i & 1;
+    if (tid == 0 && i + 1 < nt) {
+      if (!mbar_wait_bounded(&bar_b[buf ^ 1], ((i + 1) >> 1) & 1, kPolls)) {
+        s_fail = 1;
+      } else {
+        b_waited = i + 1;
+        tc_fence_after();
+        mma_tile(tmem + uint32_t(buf ^ 1) * 128u, sm.a, sm.b[buf ^ 1], nch);
+        umma_commit(&bar_mma[buf ^ 1]);
+      }
+    }
+    const bool waited = mbar_wait_bounded(&bar_mma[buf], (i >> 1) & 1, kPolls);
+    const bool fail_b = __syncthreads_or(!waited || s_fail);
+    if (i + 1 < nt && !s_fail) issued = i + 1;
+    if (waited) done = i;
+    if (fail_b) {
+      ok = false;
+      break;
+    }
+    tc_fence_after();
+    // B buffer `buf` is free (MMA i has read it): refill with tile i + 2
+    if (tid == 0 && i + 2 < nt) {
+      load_tile(bmap, sm.b[buf], &bar_b[buf], nch, b_head, t0 + i + 2);
+      b_loaded = i + 2;
+    }
+    epi(i, tmem + (uint32_t(warp * 32) << 16) + uint32_t(buf) * 128u);
+    tc_fence_before();
+    __syncthreads();  // accumulator `buf` is free for the MMA of tile i + 2
+    tc_fence_after();
+  }
+  if (!ok) {
+    if (tid == 0) atomicOr(status, ASHKV_FLAG_TIMEOUT);
+    // let an issued MMA that was not seen to complete finish before TMEM is freed
+    for (int t = done + 1; t <= issued; ++t) mbar_wait_bounded(&bar_mma[t & 1], (t >> 1) & 1, kPolls);
+    // and every TMA load in flight, so none lands after the CTA has exited
+    if (tid == 0) {
+      if (!a_waited) mbar_wait_bounded(bar_a, 0, kPolls);
+      for (int t = b_waited + 1; t <= b_loaded; ++t) mbar_wait_bounded(&bar_b[t & 1], (t >> 1) & 1, kPolls);
+    }
+    __syncthreads();
+  }
+  return ok;
+}
+
+// Pass 1: CTA (query tile qt, query head h): log2-sum-exp2 of every query row.
+__global__ void __launch_bounds__(kThreadsF, 1) saliency_rows_kernel(const __grid_constant__ CUtensorMap tq,
+                                                                     const __grid_constant__ CUtensorMap tk,
+                                                                     const SalParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ uint64_t bar_a, bar_b[2], bar_mma[2];
+  __shared__ uint32_t s_tmem;
+  const int tid = threadIdx.x, warp = tid >> 5;
+  const int qt = blockIdx.x, h = blockIdx.y, hk = h / p.group;
+  const int64_t qrow = int64_t(qt) * kTile + tid, qpos = p.q_pos0 + qrow;
+  const int64_t q_hi = min(int64_t(qt + 1) * kTile, p.n_q) - 1;
+  const int64_t k_hi = min(p.q_pos0 + q_hi, p.n_k - 1);  // the last key any row of the tile attends
+  const int nt = k_hi < 0 ? 0 : int(k_hi / kTile) + 1;
+  const PassSmem sm = carve(smem_raw, p.nch);
+  if (warp == 0) tmem_alloc(&s_tmem, kAccCols);
+  if (tid == 0) {
+    mbar_init(&bar_a, 1); mbar_init(&bar_b[0], 1); mbar_init(&bar_b[1], 1);
+    mbar_init(&bar_mma[0], 1); mbar_init(&bar_mma[1], 1);
+    mbar_init_fence();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = s_tmem;
+  float m = -INFINITY, l = 0.0f;
+  const float c = p.c;
+  if (nt > 0) {
+    run_tiles(&tq, h, qt, &tk, hk, 0, nt, p.nch, sm, &bar_a, bar_b, bar_mma, tmem, p.status,
+              [&](int i, uint32_t acc) {
+                for (int cc = 0; cc < 4; ++cc) {
+                  float v[32];
+                  tmem_ld32(acc + uint32_t(cc * 32), v);
+                  tmem_ld_wait();
+                  const int64_t k0 = int64_t(i) * kTile + cc * 32;
+                  float mx = -INFINITY;
+#pragma unroll
+                  for (int j = 0; j < 32; ++j) {
+                    const bool valid = k0 + j <= qpos && k0 + j < p.n_k;
+                    v[j] = valid ? v[j] * c : -INFINITY;
+                    mx = fmaxf(mx, v[j]);
+                  }
+                  if (mx == -INFINITY) continue;
+                  const float mn = fmaxf(m, mx);
+                  float sum = 0.0f;
+#pragma unroll
+                  for (int j = 0; j < 32; ++j) sum += ex2(v[j] - mn);
+                  l = (m == -INFINITY ? 0.0f : l * ex2(m - mn)) + sum;
+                  m = mn;
+                }
+              });
+  }
+  if (qrow < p.n_q) p.lse2[int64_t(h) * p.n_q + qrow] = l > 0.0f ? m + __log2f(l) : INFINITY;
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tmem_dealloc(tmem, kAccCols);
+    tmem_relinquish();
+  }
+}
+
+// Pass 2: CTA (key tile kt, query head h): sum over the query rows of
+// 2^(s * c - lse2[q]) for every key row of the tile (scores computed as K Q^T).
+__global__ void __launch_bounds__(kThreadsF, 1) saliency_cols_kernel(const __grid_constant__ CUtensorMap tq,
+                                                                     const __grid_constant__ CUtensorMap tk,
+                                                                     const SalParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ uint64_t bar_a, bar_b[2], bar_mma[2];
+  __shared__ uint32_t s_tmem;
+  __shared__ float s_lse[2][kTile];
+  const int tid = threadIdx.x, warp = tid >> 5;
+  const int kt = blockIdx.x, h = blockIdx.y, hk = h / p.group;
+  const int64_t krow = int64_t(kt) * kTile + tid;
+  // queries that can attend a key of this tile: query position >= kt * 128
+  int64_t q_lo = int64_t(kt) * kTile - p.q_pos0;
+  if (q_lo < 0) q_lo = 0;
+  const int64_t n_qt = (p.n_q + kTile - 1) / kTile;
+  const int64_t t0 = q_lo / kTile;
+  const int nt = t0 < n_qt ? int(n_qt - t0) : 0;
+  const PassSmem sm = carve(smem_raw, p.nch);
+  if (warp == 0) tmem_alloc(&s_tmem, kAccCols);
+  if (tid == 0) {
+    mbar_init(&bar_a, 1); mbar_init(&bar_b[0], 1); mbar_init(&bar_b[1], 1);
+    mbar_init(&bar_mma[0], 1); mbar_init(&bar_mma[1], 1);
+    mbar_init_fence();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = s_tmem;
+  const float c = p.c;
+  const float* lse = p.lse2 + int64_t(h) * p.n_q;
+  float acc_sum = 0.0f;
+  if (nt > 0) {
+    run_tiles(&tk, hk, kt, &tq, h, t0, nt, p.nch, sm, &bar_a, bar_b, bar_mma, tmem, p.status,
+              [&](int i, uint32_t acc) {
+                const int64_t q0 = (t0 + i) * kTile;
+                // this tile's row normalisers (rows past n_q contribute 0)
+                float* sl = s_lse[i & 1];
+                sl[tid] = q0 + tid < p.n_q ? lse[q0 + tid] : INFINITY;
+                __syncthreads();
+                const int64_t kpos = krow;
+                for (int cc = 0; cc < 4; ++cc) {
+                  float v[32];
+                  tmem_ld32(acc + uint32_t(cc * 32), v);
+                  tmem_ld_wait();
+#pragma unroll
+                  for (int j = 0; j < 32; ++j) {
+                    const int64_t q = q0 + cc * 32 + j;
+                    const bool valid = p.q_pos0 + q >= kpos && q < p.n_q;
+                    acc_sum += valid ? ex2(v[j] * c - sl[cc * 32 + j]) : 0.0f;
+                  }
+                }
+              });
+  }
+  if (krow < p.n_k) p.colsum[int64_t(h) * p.n_k + krow] = acc_sum;
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tmem_dealloc(tmem, kAccCols);
+    tmem_relinquish();
+  }
+}
+
+// sal[k] = sum over query heads of colsum[h, k].
+__global__ void head_sum_kernel(const float* __restrict__ colsum, int32_t heads, int64_t n_k, float* __restrict__ sal) {
+  for (int64_t k = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; k < n_k; k += int64_t(gridDim.x) * blockDim.x) {
+    float s = 0.0f;
+    for (int h = 0; h < heads; ++h) s += colsum[int64_t(h) * n_k + k];
+    sal[k] = s;
+  }
+}
+
+// One warp per page: raw saliency mass (sum of the page's token saliency) and
+// novelty (mean over its tokens of ||k_t - k_{t-1}||^2 / (||k_t||^2 + ||k_{t-1}||^2) / 2).
+__global__ void page_raw_kernel(const float* __restrict__ sal, const uint16_t* __restrict__ k, int32_t row_len,
+                                int64_t n_k, int32_t tokens_per_page, int64_t n_pages, float* __restrict__ s_raw,
+                                float* __restrict__ novelty) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = int64_t(gridDim.x) * (blockDim.x / 32);
+  for (int64_t pg = int64_t(blockIdx.x) * (blockDim.x / 32) + (threadIdx.x >> 5); pg < n_pages; pg += warps) {
+    const int64_t t0 = pg * tokens_per_page;
+    const int64_t t1 = min(t0 + tokens_per_page, n_k);
+    float mass = 0.0f, nov = 0.0f;
+    for (int64_t t = t0; t < t1; ++t) {
+      if (sal) mass += sal[t];
+      if (t == 0) continue;
+      const uint16_t* a = k + t * row_len;
+      const uint16_t* b = a - row_len;
+      float dd = 0.0f, nn = 0.0f;
+      for (int e = lane; e < row_len; e += 32) {
+        const float x = bf16_to_f32(a[e]), y = bf16_to_f32(b[e]);
+        dd = fmaf(x - y, x - y, dd);
+        nn = fmaf(x, x, fmaf(y, y, nn));
+      }
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) {
+        dd += __shfl_xor_sync(0xFFFFFFFFu, dd, off);
+        nn += __shfl_xor_sync(0xFFFFFFFFu, nn, off);
+      }
+      nov += nn > 0.0f ? 0.5f * dd / nn : 0.0f;
+    }
+    if (lane == 0) {
+      if (s_raw) s_raw[pg] = mass;
+      novelty[pg] = nov / float(t1 - t0);
+    }
+  }
+}
+
+// One CTA: S[p] = s_raw[p] / max_p s_raw[p] (0 when every page has zero mass).
+__global__ void __launch_bounds__(1024) page_normalise_kernel(const float* __restrict__ s_raw, int64_t n_pages,
+                                                              float* __restrict__ s_out) {
+  __shared__ float s_max[32];
+  float m = 0.0f;
+  for (int64_t i = threadIdx.x; i < n_pages; i += blockDim.x) m = fmaxf(m, s_raw[i]);
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, off));
+  if ((threadIdx.x & 31) == 0) s_max[threadIdx.x >> 5] = m;
+  __syncthreads();
+  m = 0.0f;
+  for (int w = 0; w < int(blockDim.x / 32); ++w) m = fmaxf(m, s_max[w]);
+  const float inv = m > 0.0f ? 1.0f / m : 0.0f;
+  for (int64_t i = threadIdx.x; i < n_pages; i += blockDim.x) s_out[i] = s_raw[i] * inv;
+}
+
+// [n, heads, head_dim] bf16 as a 3-D tensor map; box = 64 elements x 1 head x 128 tokens, 128-byte swizzle.
+bool make_qk_tmap(CUtensorMap* map, const void* ptr, int64_t n, int32_t heads, int32_t head_dim) {
+  auto fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(tensor_map_encoder());
+  if (!fn || !aligned(ptr, 16) || n <= 0 || n > 0x7FFFFFFFLL) return false;
+  cuuint64_t dims[3] = {cuuint64_t(head_dim), cuuint64_t(heads), cuuint64_t(n)};
+  cuuint64_t strides[2] = {cuuint64_t(head_dim) * 2, cuuint64_t(heads) * head_dim * 2};
+  cuuint32_t box[3] = {64, 1, uint32_t(kTile)};
+  cuuint32_t estr[3] = {1, 1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(ptr), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+unsigned grid_for(int64_t items, int threads) {
+  const int64_t need = (items + threads - 1) / threads;
+  const int64_t cap = int64_t(sm_count() > 0 ? sm_count() : 148) * 8;
+  return unsigned(need < cap ? (need > 0 ? need : 1) : cap);
+}
+
+}  // namespace
+}  // namespace ashkv
+
+using namespace ashkv;
+
+extern "C" int64_t ashkv_saliency_scratch_floats(int32_t heads_q, int64_t n_q, int64_t n_k) {
+  if (heads_q <= 0 || n_q < 0 || n_k < 0) return -1;
+  return int64_t(heads_q) * (n_q + n_k);
+}
+
+extern "C" ashkv_status_t ashkv_attention_saliency(const void* d_q, const void* d_k, int32_t heads_q, int32_t heads_kv,
+                                                   int32_t head_dim, int64_t n_q, int64_t n_k, int64_t q_pos0,
+                                                   float scale, float* d_scratch, float* d_token_saliency,
+                                                   uint32_t* d_status, void* stream) {
+  if (heads_q <= 0 || heads_kv <= 0 || heads_q % heads_kv || (head_dim != 64 && head_dim != 128)) {
+    set_message("ashkv_attention_saliency: heads_q must be a multiple of heads_kv and head_dim 64 or 128");
+    return ASHKV_BAD_ARGUMENT;
+  }
+  if (n_q < 0 || n_k < 0 || n_q > (int64_t(1) << 30) || n_k > (int64_t(1) << 30)) return ASHKV_BAD_ARGUMENT;
+  if (n_k == 0) return ASHKV_OK;
+  if (!d_q || !d_k || !d_scratch || !d_token_saliency || !d_status) return ASHKV_BAD_ARGUMENT;
+  cudaStream_t st = as_stream(stream);
+  SalParams p;
+  p.heads_q = heads_q; p.group = heads_q / heads_kv; p.nch = head_dim / 64;
+  p.n_q = n_q; p.n_k = n_k; p.q_pos0 = q_pos0;
+  p.c = scale * 1.4426950408889634f;
+  p.lse2 = d_scratch;
+  p.colsum = d_scratch + int64_t(heads_q) * n_q;
+  p.status = d_status;
+  if (n_q == 0) {
+    if (cudaMemsetAsync(d_token_saliency, 0, size_t(n_k) * sizeof(float), st) != cudaSuccess)
+      return check_launch("ashkv_attention_saliency");
+    return ASHKV_OK;
+  }
+  CUtensorMap tq, tk;
+  if (!make_qk_tmap(&tq, d_q, n_q, heads_q, head_dim) || !make_qk_tmap(&tk, d_k, n_k, heads_kv, head_dim)) {
+    set_message("ashkv_attention_saliency: cannot build the tensor maps (16-byte aligned buffers needed)");
+    return ASHKV_BAD_ARGUMENT;
+  }
+  // Always the head_dim 128 size: at most two CTAs per SM, so their 2 x 256 TMEM columns fit in 512.
+  const int smem = 3 * 2 * kChunkBytes + 1024;
+  if (cudaFuncSetAttribute(saliency_rows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess ||
+      cudaFuncSetAttribute(saliency_cols_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+    return check_launch("ashkv_attention_saliency smem attribute");
+  const dim3 grid_rows{unsigned((n_q + kTile - 1) / kTile), unsigned(heads_q)};
+  saliency_rows_kernel<<<grid_rows, kThreadsF, smem, st>>>(tq, tk, p);
+  const dim3 grid_cols{unsigned((n_k + kTile - 1) / kTile), unsigned(heads_q)};
+  saliency_cols_kernel<<<grid_cols, kThreadsF, smem, st>>>(tq, tk, p);
+  head_sum_kernel<<<grid_for(n_k, 256), 256, 0, st>>>(p.colsum, heads_q, n_k, d_token_saliency);
+  return check_launch("ashkv_attention_saliency");
+}
+
+extern "C" ashkv_status_t ashkv_page_features(const float* d_token_saliency, const void* d_k, int32_t row_len,
+                                              int64_t n_k, int32_t tokens_per_page, float* d_s_raw, float* d_S,
+                                              float* d_N, void* stream) {
+  if (n_k < 0 || row_len <= 0 || tokens_per_page <= 0) return ASHKV_BAD_ARGUMENT;
+  if (n_k == 0) return ASHKV_OK;
+  if (!d_k || !d_N || (d_token_saliency && (!d_s_raw || !d_S))) return ASHKV_BAD_ARGUMENT;
+  cudaStream_t st = as_stream(stream);
+  const int64_t n_pages = (n_k + tokens_per_page - 1) / tokens_per_page;
+  page_raw_kernel<<<grid_for(n_pages * 32, 256), 256, 0, st>>>(d_token_saliency, static_cast<const uint16_t*>(d_k),
+                                                                row_len, n_k, tokens_per_page, n_pages,
+                                                                d_token_saliency ? d_s_raw : nullptr, d_N);
+  if (d_token_saliency) page_normalise_kernel<<<1, 1024, 0, st>>>(d_s_raw, n_pages, d_S);
+  return check_launch("ashkv_page_features");
+}

@@ -311,6 +311,36 @@ ASHKV_API ashkv_status_t ashkv_int4_encode(const void* d_src_bf16, int64_t n, in
 ASHKV_API ashkv_status_t ashkv_int4_decode(const void* d_scales_bf16, const void* d_packed, int64_t n_groups,
                                            int32_t group_size, void* d_dst_bf16, void* stream);
 
+/* ========================================================================
+ * Attention-derived page features (the S and N inputs of ashkv_score).
+ * Saliency restates the attention mass per key of the reference simulator
+ * (ashkv/tests/simulator.py:66-80): for query rows q [n_q, heads_q, head_dim]
+ * and key rows k [n_k, heads_kv, head_dim] (bf16, contiguous, 16-byte
+ * aligned; query head h reads key head h / (heads_q / heads_kv)),
+ *   P[h,i,:] = softmax_j(scale * q_i . k_j), keys j <= q_pos0 + i only,
+ *   d_token_saliency[j] = sum over h and i of P[h,i,j]          (fp32).
+ * Scores run on the tensor cores (tcgen05, fp32 accumulation in TMEM),
+ * so results match an fp32 evaluation to fp32 accumulation-order accuracy.
+ * head_dim must be 64 or 128; d_scratch holds
+ * ashkv_saliency_scratch_floats(heads_q, n_q, n_k) floats.
+ * ashkv_page_features: per page of tokens_per_page consecutive keys,
+ *   d_S[p] = (sum of the page's token saliency) / (largest page sum),
+ *   d_N[p] = mean over the page's tokens t of
+ *            ||k_t - k_{t-1}||^2 / (||k_t||^2 + ||k_{t-1}||^2) / 2  (0 for t = 0),
+ * k rows of row_len = heads_kv * head_dim bf16; d_s_raw: n_pages floats of
+ * scratch.  With d_token_saliency NULL only d_N is written.  The reference
+ * defines no page-level saliency and no novelty producer; these are this
+ * library's definitions, both in [0, 1].
+ * ======================================================================== */
+ASHKV_API int64_t ashkv_saliency_scratch_floats(int32_t heads_q, int64_t n_q, int64_t n_k);
+ASHKV_API ashkv_status_t ashkv_attention_saliency(const void* d_q, const void* d_k, int32_t heads_q, int32_t heads_kv,
+                                                  int32_t head_dim, int64_t n_q, int64_t n_k, int64_t q_pos0,
+                                                  float scale, float* d_scratch, float* d_token_saliency,
+                                                  uint32_t* d_status, void* stream);
+ASHKV_API ashkv_status_t ashkv_page_features(const float* d_token_saliency, const void* d_k, int32_t row_len,
+                                             int64_t n_k, int32_t tokens_per_page, float* d_s_raw, float* d_S,
+                                             float* d_N, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

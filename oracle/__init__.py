@@ -305,3 +305,51 @@ def int4_decode(scales: np.ndarray, packed: np.ndarray, group_size: int = 64,
 def int4_blob(scales: np.ndarray, packed: np.ndarray, num_values: int) -> bytes:
     """INT4Codec blob (int4.py:74-75): <II num_groups, num_values> + bf16 scales + packed."""
     return struct.pack("<II", scales.size, num_values) + scales.astype(np.uint16).tobytes() + packed.tobytes()
+
+
+# --------------------------------------------------------------------- page features
+def attention_saliency(q, k, q_pos0=None, scale=None):
+    """Attention mass per key as the reference simulator computes it
+    (ashkv/tests/simulator.py:66-80): fp32 scores q.k / sqrt(head_dim), causal
+    mask (key position <= query position), softmax over keys, summed over heads
+    and queries.  q [n_q, heads_q, d], k [n_k, heads_kv, d] (torch, any float
+    dtype; evaluated in fp32 on the CPU); query head h reads key head h // group."""
+    import torch
+    q = q.float().cpu()
+    k = k.float().cpu()
+    n_q, hq, d = q.shape
+    n_k, hkv, _ = k.shape
+    if q_pos0 is None:
+        q_pos0 = n_k - n_q
+    if scale is None:
+        scale = 1.0 / (d ** 0.5)
+    group = hq // hkv
+    q_h = q.transpose(0, 1)                                  # [hq, n_q, d]
+    k_h = k.transpose(0, 1).repeat_interleave(group, dim=0)  # [hq, n_k, d]
+    scores = torch.matmul(q_h, k_h.transpose(-2, -1)) * scale
+    qpos = torch.arange(n_q).view(-1, 1) + q_pos0
+    kpos = torch.arange(n_k).view(1, -1)
+    scores = scores.masked_fill(kpos > qpos, float("-inf"))
+    attn = torch.softmax(scores, dim=-1)
+    attn = torch.nan_to_num(attn, nan=0.0)   # rows with no visible key
+    return attn.sum(dim=(0, 1))
+
+
+def page_features(k, tokens_per_page, token_saliency=None):
+    """(S, N) per page as the library defines them (numpy fp64 reference)."""
+    import torch
+    kf = k.float().cpu().reshape(k.shape[0], -1).double().numpy()
+    n_k = kf.shape[0]
+    n_pages = -(-n_k // tokens_per_page)
+    delta = np.zeros(n_k)
+    if n_k > 1:
+        d = ((kf[1:] - kf[:-1]) ** 2).sum(1)
+        nn = (kf[1:] ** 2).sum(1) + (kf[:-1] ** 2).sum(1)
+        delta[1:] = np.where(nn > 0, 0.5 * d / np.where(nn > 0, nn, 1), 0.0)
+    N = np.array([delta[p * tokens_per_page:(p + 1) * tokens_per_page].mean() for p in range(n_pages)])
+    S = None
+    if token_saliency is not None:
+        s = np.asarray(token_saliency, dtype=np.float64)
+        raw = np.array([s[p * tokens_per_page:(p + 1) * tokens_per_page].sum() for p in range(n_pages)])
+        S = raw / raw.max() if raw.max() > 0 else raw * 0
+    return S, N

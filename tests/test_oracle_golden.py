@@ -172,3 +172,24 @@ def test_int4_golden_covers_special_values():
                 if np.any((F84[f"int4_in_{ci}"] & 0x7F80) == 0x7F80)]
     assert specials, "no NaN/inf case in the INT4 fixture"
     assert F84["int4_empty_blob"].tobytes() == b"\0\0\0\0"
+
+
+def test_feature_oracle_properties():
+    """The saliency oracle conserves probability mass (every visible query row sums
+    to 1) and matches a float64 evaluation; novelty is 0 for repeated keys."""
+    import torch
+    g = torch.Generator().manual_seed(0)
+    q = torch.randn(40, 4, 16, generator=g)
+    k = torch.randn(50, 2, 16, generator=g)
+    s = oracle.attention_saliency(q, k)
+    assert abs(float(s.sum()) - 4 * 40) < 1e-3
+    # float64 restatement
+    qh = q.double().transpose(0, 1)
+    kh = k.double().transpose(0, 1).repeat_interleave(2, dim=0)
+    sc = qh @ kh.transpose(-2, -1) / 4.0
+    mask = torch.arange(50).view(1, -1) > (torch.arange(40).view(-1, 1) + 10)
+    p = torch.softmax(sc.masked_fill(mask, float("-inf")), dim=-1).sum(dim=(0, 1))
+    assert np.allclose(s.numpy(), p.numpy(), rtol=1e-5, atol=1e-6)
+    kk = torch.ones(32, 2, 16)
+    S, N = oracle.page_features(kk, 16, np.arange(32, dtype=np.float64))
+    assert np.all(N == 0) and S.max() == 1.0
