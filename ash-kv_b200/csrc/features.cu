@@ -17,9 +17,12 @@
 // steps of 16), bf16 operands in 128-byte-swizzled K-major shared memory
 // (one 16 KiB chunk per 64 elements of head_dim), one fp32 accumulator of 128
 // TMEM columns per tile, two accumulators so the next tile's MMA overlaps this
-// tile's epilogue.  One thread per TMEM lane (accumulator row) runs the
-// epilogue, so no cross-thread reduction is needed: pass 1 keeps the online
-// max/sum of its query row, pass 2 (keys x queries) sums its key row.
+// tile's epilogue.  Sixteen warps share a tile's epilogue: warp w reads TMEM
+// lanes 32 (w % 4) .. + 31 (accumulator rows) and columns 32 (w / 4) .. + 31,
+// so each thread handles 32 values per tile; pass 1 keeps an online max/sum
+// per (row, column group), pass 2 (keys x queries) a sum per (key row, column
+// group), merged through shared memory at the end.  The causal mask is
+// evaluated only for column groups that cross the diagonal.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -30,7 +33,8 @@ namespace {
 
 constexpr int kTile = 128;                   // rows of a query or key tile
 constexpr int kChunkBytes = kTile * 128;     // 128 rows x 64 bf16 (one swizzle atom column) = 16 KiB
-constexpr int kThreadsF = 128;               // 4 warps: one TMEM lane per thread
+constexpr int kThreadsF = 512;               // 16 warps: TMEM lane quadrant (warp % 4) x 32-column group (warp / 4)
+constexpr int kColGroups = 4;
 constexpr uint32_t kPolls = 1u << 24;        // bounded mbarrier waits
 constexpr uint32_t kAccCols = 256;           // two 128-column fp32 accumulators
 
@@ -200,7 +204,7 @@ __device__ bool run_tiles(const CUtensorMap* amap, int a_head, int64_t a_tile, c
       load_tile(bmap, sm.b[buf], &bar_b[buf], nch, b_head, t0 + i + 2);
       b_loaded = i + 2;
     }
-    epi(i, tmem + (uint32_t(warp * 32) << 16) + uint32_t(buf) * 128u);
+    epi(i, tmem + (uint32_t((warp & 3) * 32) << 16) + uint32_t(buf) * 128u + uint32_t(warp >> 2) * 32u);
     tc_fence_before();
     __syncthreads();  // accumulator `buf` is free for the MMA of tile i + 2
     tc_fence_after();
@@ -220,15 +224,18 @@ __device__ bool run_tiles(const CUtensorMap* amap, int a_head, int64_t a_tile, c
 }
 
 // Pass 1: CTA (query tile qt, query head h): log2-sum-exp2 of every query row.
-__global__ void __launch_bounds__(kThreadsF, 1) saliency_rows_kernel(const __grid_constant__ CUtensorMap tq,
+// Query tiles run in reverse order so the longest (most key tiles) start first.
+__global__ void __launch_bounds__(kThreadsF, 2) saliency_rows_kernel(const __grid_constant__ CUtensorMap tq,
                                                                      const __grid_constant__ CUtensorMap tk,
                                                                      const SalParams p) {
   extern __shared__ uint8_t smem_raw[];
   __shared__ uint64_t bar_a, bar_b[2], bar_mma[2];
   __shared__ uint32_t s_tmem;
+  __shared__ float s_m[kColGroups][kTile], s_l[kColGroups][kTile];
   const int tid = threadIdx.x, warp = tid >> 5;
-  const int qt = blockIdx.x, h = blockIdx.y, hk = h / p.group;
-  const int64_t qrow = int64_t(qt) * kTile + tid, qpos = p.q_pos0 + qrow;
+  const int row = (warp & 3) * 32 + (tid & 31), cg = warp >> 2;
+  const int qt = int(gridDim.x) - 1 - int(blockIdx.x), h = blockIdx.y, hk = h / p.group;
+  const int64_t qrow = int64_t(qt) * kTile + row, qpos = p.q_pos0 + qrow;
   const int64_t q_hi = min(int64_t(qt + 1) * kTile, p.n_q) - 1;
   const int64_t k_hi = min(p.q_pos0 + q_hi, p.n_k - 1);  // the last key any row of the tile attends
   const int nt = k_hi < 0 ? 0 : int(k_hi / kTile) + 1;
@@ -248,31 +255,49 @@ __global__ void __launch_bounds__(kThreadsF, 1) saliency_rows_kernel(const __gri
   if (nt > 0) {
     run_tiles(&tq, h, qt, &tk, hk, 0, nt, p.nch, sm, &bar_a, bar_b, bar_mma, tmem, p.status,
               [&](int i, uint32_t acc) {
-                for (int cc = 0; cc < 4; ++cc) {
-                  float v[32];
-                  tmem_ld32(acc + uint32_t(cc * 32), v);
-                  tmem_ld_wait();
-                  const int64_t k0 = int64_t(i) * kTile + cc * 32;
-                  float mx = -INFINITY;
+                float v[32];
+                tmem_ld32(acc, v);
+                tmem_ld_wait();
+                const int64_t k0 = int64_t(i) * kTile + cg * 32;
+                float mx = -INFINITY;
+                if (k0 + 31 <= qpos && k0 + 31 < p.n_k) {  // the whole column group is visible
 #pragma unroll
                   for (int j = 0; j < 32; ++j) {
-                    const bool valid = k0 + j <= qpos && k0 + j < p.n_k;
-                    v[j] = valid ? v[j] * c : -INFINITY;
+                    v[j] *= c;
                     mx = fmaxf(mx, v[j]);
                   }
-                  if (mx == -INFINITY) continue;
-                  const float mn = fmaxf(m, mx);
-                  float sum = 0.0f;
+                } else {
 #pragma unroll
-                  for (int j = 0; j < 32; ++j) sum += ex2(v[j] - mn);
-                  l = (m == -INFINITY ? 0.0f : l * ex2(m - mn)) + sum;
-                  m = mn;
+                  for (int j = 0; j < 32; ++j) {
+                    v[j] = (k0 + j <= qpos && k0 + j < p.n_k) ? v[j] * c : -INFINITY;
+                    mx = fmaxf(mx, v[j]);
+                  }
                 }
+                if (mx == -INFINITY) return;
+                const float mn = fmaxf(m, mx);
+                float sum = 0.0f;
+#pragma unroll
+                for (int j = 0; j < 32; ++j) sum += ex2(v[j] - mn);
+                l = (m == -INFINITY ? 0.0f : l * ex2(m - mn)) + sum;
+                m = mn;
               });
   }
-  if (qrow < p.n_q) p.lse2[int64_t(h) * p.n_q + qrow] = l > 0.0f ? m + __log2f(l) : INFINITY;
+  // merge the four column groups of each row
+  s_m[cg][row] = m;
+  s_l[cg][row] = l;
   tc_fence_before();
   __syncthreads();
+  if (cg == 0 && qrow < p.n_q) {
+    float M = -INFINITY;
+#pragma unroll
+    for (int g = 0; g < kColGroups; ++g) M = fmaxf(M, s_m[g][row]);
+    float L = 0.0f;
+    if (M != -INFINITY)
+#pragma unroll
+      for (int g = 0; g < kColGroups; ++g)
+        if (s_l[g][row] > 0.0f) L += s_l[g][row] * ex2(s_m[g][row] - M);
+    p.lse2[int64_t(h) * p.n_q + qrow] = L > 0.0f ? M + __log2f(L) : INFINITY;
+  }
   if (warp == 0) {
     tmem_dealloc(tmem, kAccCols);
     tmem_relinquish();
@@ -281,16 +306,18 @@ __global__ void __launch_bounds__(kThreadsF, 1) saliency_rows_kernel(const __gri
 
 // Pass 2: CTA (key tile kt, query head h): sum over the query rows of
 // 2^(s * c - lse2[q]) for every key row of the tile (scores computed as K Q^T).
-__global__ void __launch_bounds__(kThreadsF, 1) saliency_cols_kernel(const __grid_constant__ CUtensorMap tq,
+__global__ void __launch_bounds__(kThreadsF, 2) saliency_cols_kernel(const __grid_constant__ CUtensorMap tq,
                                                                      const __grid_constant__ CUtensorMap tk,
                                                                      const SalParams p) {
   extern __shared__ uint8_t smem_raw[];
   __shared__ uint64_t bar_a, bar_b[2], bar_mma[2];
   __shared__ uint32_t s_tmem;
   __shared__ float s_lse[2][kTile];
+  __shared__ float s_sum[kColGroups][kTile];
   const int tid = threadIdx.x, warp = tid >> 5;
+  const int row = (warp & 3) * 32 + (tid & 31), cg = warp >> 2;
   const int kt = blockIdx.x, h = blockIdx.y, hk = h / p.group;
-  const int64_t krow = int64_t(kt) * kTile + tid;
+  const int64_t kpos = int64_t(kt) * kTile + row;
   // queries that can attend a key of this tile: query position >= kt * 128
   int64_t q_lo = int64_t(kt) * kTile - p.q_pos0;
   if (q_lo < 0) q_lo = 0;
@@ -317,25 +344,30 @@ __global__ void __launch_bounds__(kThreadsF, 1) saliency_cols_kernel(const __gri
                 const int64_t q0 = (t0 + i) * kTile;
                 // this tile's row normalisers (rows past n_q contribute 0)
                 float* sl = s_lse[i & 1];
-                sl[tid] = q0 + tid < p.n_q ? lse[q0 + tid] : INFINITY;
+                if (tid < kTile) sl[tid] = q0 + tid < p.n_q ? lse[q0 + tid] : INFINITY;
                 __syncthreads();
-                const int64_t kpos = krow;
-                for (int cc = 0; cc < 4; ++cc) {
-                  float v[32];
-                  tmem_ld32(acc + uint32_t(cc * 32), v);
-                  tmem_ld_wait();
+                float v[32];
+                tmem_ld32(acc, v);
+                tmem_ld_wait();
+                const int64_t qc = q0 + cg * 32;
+                const float* slc = sl + cg * 32;
+                if (p.q_pos0 + qc >= kpos && qc + 31 < p.n_q) {  // every query of the group sees this key
+#pragma unroll
+                  for (int j = 0; j < 32; ++j) acc_sum += ex2(fmaf(v[j], c, -slc[j]));
+                } else {
 #pragma unroll
                   for (int j = 0; j < 32; ++j) {
-                    const int64_t q = q0 + cc * 32 + j;
-                    const bool valid = p.q_pos0 + q >= kpos && q < p.n_q;
-                    acc_sum += valid ? ex2(v[j] * c - sl[cc * 32 + j]) : 0.0f;
+                    const bool valid = p.q_pos0 + qc + j >= kpos && qc + j < p.n_q;
+                    acc_sum += valid ? ex2(fmaf(v[j], c, -slc[j])) : 0.0f;
                   }
                 }
               });
   }
-  if (krow < p.n_k) p.colsum[int64_t(h) * p.n_k + krow] = acc_sum;
+  s_sum[cg][row] = acc_sum;
   tc_fence_before();
   __syncthreads();
+  if (cg == 0 && kpos < p.n_k)
+    p.colsum[int64_t(h) * p.n_k + kpos] = (s_sum[0][row] + s_sum[1][row]) + (s_sum[2][row] + s_sum[3][row]);
   if (warp == 0) {
     tmem_dealloc(tmem, kAccCols);
     tmem_relinquish();

@@ -64,6 +64,54 @@ def measured_hbm_peak() -> tuple[float, str]:
         return 6650.0, "fallback"
 
 
+def measured_bf16_peak() -> tuple[float, str]:
+    """Dense bf16 tensor peak in TFLOP/s (burst figure; the kernel is timed alone)."""
+    p = REPO / "MEASURED_PEAKS.json"
+    try:
+        return float(json.loads(p.read_text())["bf16_tflops"]), "measured"
+    except Exception:
+        return 1590.0, "fallback"
+
+
+def features_bench(dev, iters: int = 10) -> dict:
+    """Page feature inputs of one layer of the demote model: one 8192-token sequence,
+    8 KV heads x 128, causal queries at every position, 16-token pages.  Saliency is
+    tensor-bound: 2 passes x causal (query, key) pairs x 2*head_dim FLOPs per head."""
+    from ashkv.runtime import features as F
+    n, H, D, T = 8192, HEADS, HEAD_DIM, TOKENS
+    g = torch.Generator(device=dev).manual_seed(77)
+    q = (torch.randn(n, H, D, generator=g, device=dev) * 0.5).to(torch.bfloat16)
+    k = (torch.randn(n, H, D, generator=g, device=dev) * 0.5).to(torch.bfloat16)
+    sal = torch.empty(n, dtype=torch.float32, device=dev)
+    for _ in range(3):
+        F.attention_saliency(q, k, out=sal)
+        F.page_features(k, T, token_saliency=sal)
+    st = torch.cuda.current_stream(dev)
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+    ts, tp = [], []
+    for _ in range(iters):
+        ev[0].record(st)
+        F.attention_saliency(q, k, out=sal)
+        ev[1].record(st)
+        F.page_features(k, T, token_saliency=sal)
+        ev[2].record(st)
+        torch.cuda.synchronize()
+        ts.append(ev[0].elapsed_time(ev[1]))
+        tp.append(ev[1].elapsed_time(ev[2]))
+    ms = statistics.median(ts)
+    pairs = n * (n + 1) // 2
+    flops = 2 * pairs * 2 * D * H
+    tflops = flops / (ms / 1e3) / 1e12
+    peak, kind = measured_bf16_peak()
+    pages = -(-n // T)
+    return {"workload": f"one sequence of {n} tokens, {H} heads x {D}, causal, {T}-token pages ({pages})",
+            "saliency_ms": round(ms, 4), "page_features_ms": round(statistics.median(tp), 4),
+            "roofline": {"bound": "tensor", "achieved": round(tflops, 1), "peak": peak, "unit": "TFLOP/s",
+                         "frac": round(tflops / peak, 4), "peak_kind": kind, "flops_per_call": flops,
+                         "kernels": "saliency_rows_kernel + saliency_cols_kernel (tcgen05)"},
+            "pages_per_s": round(pages / ((ms + statistics.median(tp)) / 1e3), 1)}
+
+
 def profile_traffic() -> float | None:
     """DRAM bytes per encode launch from the committed ncu summary, if present."""
     p = REPO / "profiles" / "nbit_encode_int4_config2.md"
@@ -471,8 +519,10 @@ def main() -> None:
     # tensors), outlier count, and bit-exactness of a 1M-element sample against the oracle
     quality = None
     suite = None
+    features = None
     if rank == 0 and not args.no_codec_suite:
         suite = codec_suite(K, V, measured_hbm_peak()[0])
+        features = features_bench(dev)
     if rank == 0:
         import oracle
         encQ = nb.encode_groups(K, BITS, SIGMA, seed=42)
@@ -538,6 +588,7 @@ def main() -> None:
              "steps": args.e2e_bytes_steps},
             "quality": quality,
             "codecs": suite,
+            "page_features": features,
             "gpu_launches": 4 * args.steps,
             "clocks": clocks.summary(),
             "cpu_baseline": cpu,
