@@ -410,6 +410,8 @@ def main() -> None:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-demote", action="store_true")
     ap.add_argument("--no-codec-suite", action="store_true")
+    ap.add_argument("--only-features", action="store_true",
+                    help="run only the page-features leg on one GPU and print its JSON (profiling cases)")
     ap.add_argument("--demote-steps", type=int, default=10)
     ap.add_argument("--demote-layers", type=int, default=DEMOTE_LAYERS,
                     help="layers of the config-4 model (64; fewer only for small profiling cases)")
@@ -429,6 +431,9 @@ def main() -> None:
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
+    if args.only_features:
+        print(json.dumps({"page_features": features_bench(dev, iters=3)}), flush=True)
+        return
     dist = None
     if world > 1:
         import torch.distributed as dist
