@@ -142,20 +142,30 @@ __device__ __forceinline__ PassSmem carve(uint8_t* raw, int nch) {
   return s;
 }
 
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" :: "r"(smem_u32(bar)) : "memory");
+}
+
 // The pipelined loop shared by both passes.  A (the CTA's fixed tile) is
-// loaded once; B tiles t = t0 .. t0 + nt - 1 stream through two buffers; the
-// MMA of tile i + 1 is issued before the epilogue of tile i.  `epi(i, acc)`
-// is called by every thread with the TMEM address of its accumulator row.
-// Returns false (and sets ASHKV_FLAG_TIMEOUT) if a bounded wait gave up; all
-// issued MMAs have completed when it returns.
+// loaded once; B tiles t = t0 .. t0 + nt - 1 stream through two shared-memory
+// buffers and two TMEM accumulators.  Thread 0 also produces: it issues the
+// MMA of tile i + 1 once its B tile has landed and every warp has released
+// that accumulator (bar_empty, one arrival per warp), and refills a B buffer
+// once the MMA that read it has completed.  Each warp copies its 32 values of
+// tile i out of TMEM, releases the accumulator and then runs epi(i, v), so the
+// arithmetic overlaps the next tile's MMA.  Returns false (and sets
+// ASHKV_FLAG_TIMEOUT) if a bounded wait gave up; all issued MMAs and TMA
+// loads have completed when it returns.
 template <class Epi>
 __device__ bool run_tiles(const CUtensorMap* amap, int a_head, int64_t a_tile, const CUtensorMap* bmap, int b_head,
                           int64_t t0, int nt, int nch, const PassSmem& sm, uint64_t* bar_a, uint64_t* bar_b,
-                          uint64_t* bar_mma, uint32_t tmem, uint32_t* status, Epi epi) {
-  const int tid = threadIdx.x, warp = tid >> 5;
-  __shared__ int s_fail;
-  // thread 0's record of the B tile loads: issued up to b_loaded, awaited up to b_waited
-  int b_loaded = -1, b_waited = -1;
+                          uint64_t* bar_full, uint64_t* bar_empty, uint32_t tmem, uint32_t* status, Epi epi) {
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  volatile __shared__ int s_fail;
+  const uint32_t my_lanes = (uint32_t((warp & 3) * 32) << 16) + uint32_t(warp >> 2) * 32u;
+  // thread 0's record: B loads issued up to b_loaded and awaited up to b_waited,
+  // MMAs issued up to mma_issued and seen complete up to mma_done
+  int b_loaded = -1, b_waited = -1, mma_issued = -1, mma_done = -1;
   bool a_waited = false;
   if (tid == 0) {
     s_fail = 0;
@@ -171,55 +181,61 @@ __device__ bool run_tiles(const CUtensorMap* amap, int a_head, int64_t a_tile, c
       b_waited = 0;
       tc_fence_after();
       mma_tile(tmem, sm.a, sm.b[0], nch);
-      umma_commit(&bar_mma[0]);
+      umma_commit(&bar_full[0]);
+      mma_issued = 0;
     }
   }
   __syncthreads();
-  int issued = s_fail ? -1 : 0;  // last tile whose MMA was issued (same value in every thread)
-  int done = -1;                 // last tile whose MMA completion every thread has seen
-  bool ok = !s_fail;
-  for (int i = 0; ok && i < nt; ++i) {
+  for (int i = 0; i < nt && !s_fail; ++i) {
     const int buf = i & 1;
-    if (tid == 0 && i + 1 < nt) {
-      if (!mbar_wait_bounded(&bar_b[buf ^ 1], ((i + 1) >> 1) & 1, kPolls)) {
+    if (tid == 0 && i + 1 < nt) {  // produce tile i + 1
+      const int nb = (i + 1) & 1;
+      bool ok = mbar_wait_bounded(&bar_b[nb], ((i + 1) >> 1) & 1, kPolls);
+      if (ok) b_waited = i + 1;
+      if (ok && i + 1 >= 2) ok = mbar_wait_bounded(&bar_empty[nb], ((i - 1) >> 1) & 1, kPolls);
+      if (!ok) {
         s_fail = 1;
       } else {
-        b_waited = i + 1;
         tc_fence_after();
-        mma_tile(tmem + uint32_t(buf ^ 1) * 128u, sm.a, sm.b[buf ^ 1], nch);
-        umma_commit(&bar_mma[buf ^ 1]);
+        mma_tile(tmem + uint32_t(nb) * 128u, sm.a, sm.b[nb], nch);
+        umma_commit(&bar_full[nb]);
+        mma_issued = i + 1;
       }
     }
-    const bool waited = mbar_wait_bounded(&bar_mma[buf], (i >> 1) & 1, kPolls);
-    const bool fail_b = __syncthreads_or(!waited || s_fail);
-    if (i + 1 < nt && !s_fail) issued = i + 1;
-    if (waited) done = i;
-    if (fail_b) {
-      ok = false;
+    __syncwarp();
+    if (!mbar_wait_bounded(&bar_full[buf], (i >> 1) & 1, kPolls)) {
+      s_fail = 1;
       break;
     }
-    tc_fence_after();
-    // B buffer `buf` is free (MMA i has read it): refill with tile i + 2
-    if (tid == 0 && i + 2 < nt) {
-      load_tile(bmap, sm.b[buf], &bar_b[buf], nch, b_head, t0 + i + 2);
-      b_loaded = i + 2;
-    }
-    epi(i, tmem + (uint32_t((warp & 3) * 32) << 16) + uint32_t(buf) * 128u + uint32_t(warp >> 2) * 32u);
-    tc_fence_before();
-    __syncthreads();  // accumulator `buf` is free for the MMA of tile i + 2
-    tc_fence_after();
-  }
-  if (!ok) {
-    if (tid == 0) atomicOr(status, ASHKV_FLAG_TIMEOUT);
-    // let an issued MMA that was not seen to complete finish before TMEM is freed
-    for (int t = done + 1; t <= issued; ++t) mbar_wait_bounded(&bar_mma[t & 1], (t >> 1) & 1, kPolls);
-    // and every TMA load in flight, so none lands after the CTA has exited
     if (tid == 0) {
-      if (!a_waited) mbar_wait_bounded(bar_a, 0, kPolls);
-      for (int t = b_waited + 1; t <= b_loaded; ++t) mbar_wait_bounded(&bar_b[t & 1], (t >> 1) & 1, kPolls);
+      mma_done = i;
+      // MMA i has read B buffer `buf`: refill it with tile i + 2
+      if (i + 2 < nt) {
+        load_tile(bmap, sm.b[buf], &bar_b[buf], nch, b_head, t0 + i + 2);
+        b_loaded = i + 2;
+      }
     }
-    __syncthreads();
+    __syncwarp();
+    tc_fence_after();
+    float v[32];
+    tmem_ld32(tmem + my_lanes + uint32_t(buf) * 128u, v);
+    tmem_ld_wait();
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&bar_empty[buf]);  // this warp is done with accumulator `buf`
+    epi(i, v);
   }
+  __syncthreads();
+  const bool ok = !s_fail;
+  if (!ok && tid == 0) {
+    atomicOr(status, ASHKV_FLAG_TIMEOUT);
+    // let every issued MMA and TMA load finish before TMEM and shared memory are released
+    for (int t = mma_done + 1; t <= mma_issued; ++t) mbar_wait_bounded(&bar_full[t & 1], (t >> 1) & 1, kPolls);
+    if (!a_waited) mbar_wait_bounded(bar_a, 0, kPolls);
+    for (int t = b_waited + 1; t <= b_loaded; ++t) mbar_wait_bounded(&bar_b[t & 1], (t >> 1) & 1, kPolls);
+  }
+  tc_fence_before();
+  __syncthreads();
   return ok;
 }
 
@@ -229,7 +245,7 @@ __global__ void __launch_bounds__(kThreadsF, 2) saliency_rows_kernel(const __gri
                                                                      const __grid_constant__ CUtensorMap tk,
                                                                      const SalParams p) {
   extern __shared__ uint8_t smem_raw[];
-  __shared__ uint64_t bar_a, bar_b[2], bar_mma[2];
+  __shared__ uint64_t bar_a, bar_b[2], bar_full[2], bar_empty[2];
   __shared__ uint32_t s_tmem;
   __shared__ float s_m[kColGroups][kTile], s_l[kColGroups][kTile];
   const int tid = threadIdx.x, warp = tid >> 5;
@@ -243,7 +259,8 @@ __global__ void __launch_bounds__(kThreadsF, 2) saliency_rows_kernel(const __gri
   if (warp == 0) tmem_alloc(&s_tmem, kAccCols);
   if (tid == 0) {
     mbar_init(&bar_a, 1); mbar_init(&bar_b[0], 1); mbar_init(&bar_b[1], 1);
-    mbar_init(&bar_mma[0], 1); mbar_init(&bar_mma[1], 1);
+    mbar_init(&bar_full[0], 1); mbar_init(&bar_full[1], 1);
+    mbar_init(&bar_empty[0], kThreadsF / 32); mbar_init(&bar_empty[1], kThreadsF / 32);
     mbar_init_fence();
   }
   tc_fence_before();
@@ -253,11 +270,8 @@ __global__ void __launch_bounds__(kThreadsF, 2) saliency_rows_kernel(const __gri
   float m = -INFINITY, l = 0.0f;
   const float c = p.c;
   if (nt > 0) {
-    run_tiles(&tq, h, qt, &tk, hk, 0, nt, p.nch, sm, &bar_a, bar_b, bar_mma, tmem, p.status,
-              [&](int i, uint32_t acc) {
-                float v[32];
-                tmem_ld32(acc, v);
-                tmem_ld_wait();
+    run_tiles(&tq, h, qt, &tk, hk, 0, nt, p.nch, sm, &bar_a, bar_b, bar_full, bar_empty, tmem, p.status,
+              [&](int i, float (&v)[32]) {
                 const int64_t k0 = int64_t(i) * kTile + cg * 32;
                 float mx = -INFINITY;
                 if (k0 + 31 <= qpos && k0 + 31 < p.n_k) {  // the whole column group is visible
@@ -285,7 +299,6 @@ __global__ void __launch_bounds__(kThreadsF, 2) saliency_rows_kernel(const __gri
   // merge the four column groups of each row
   s_m[cg][row] = m;
   s_l[cg][row] = l;
-  tc_fence_before();
   __syncthreads();
   if (cg == 0 && qrow < p.n_q) {
     float M = -INFINITY;
@@ -310,9 +323,8 @@ __global__ void __launch_bounds__(kThreadsF, 2) saliency_cols_kernel(const __gri
                                                                      const __grid_constant__ CUtensorMap tk,
                                                                      const SalParams p) {
   extern __shared__ uint8_t smem_raw[];
-  __shared__ uint64_t bar_a, bar_b[2], bar_mma[2];
+  __shared__ uint64_t bar_a, bar_b[2], bar_full[2], bar_empty[2];
   __shared__ uint32_t s_tmem;
-  __shared__ float s_lse[2][kTile];
   __shared__ float s_sum[kColGroups][kTile];
   const int tid = threadIdx.x, warp = tid >> 5;
   const int row = (warp & 3) * 32 + (tid & 31), cg = warp >> 2;
@@ -328,7 +340,8 @@ __global__ void __launch_bounds__(kThreadsF, 2) saliency_cols_kernel(const __gri
   if (warp == 0) tmem_alloc(&s_tmem, kAccCols);
   if (tid == 0) {
     mbar_init(&bar_a, 1); mbar_init(&bar_b[0], 1); mbar_init(&bar_b[1], 1);
-    mbar_init(&bar_mma[0], 1); mbar_init(&bar_mma[1], 1);
+    mbar_init(&bar_full[0], 1); mbar_init(&bar_full[1], 1);
+    mbar_init(&bar_empty[0], kThreadsF / 32); mbar_init(&bar_empty[1], kThreadsF / 32);
     mbar_init_fence();
   }
   tc_fence_before();
@@ -339,32 +352,33 @@ __global__ void __launch_bounds__(kThreadsF, 2) saliency_cols_kernel(const __gri
   const float* lse = p.lse2 + int64_t(h) * p.n_q;
   float acc_sum = 0.0f;
   if (nt > 0) {
-    run_tiles(&tk, hk, kt, &tq, h, t0, nt, p.nch, sm, &bar_a, bar_b, bar_mma, tmem, p.status,
-              [&](int i, uint32_t acc) {
-                const int64_t q0 = (t0 + i) * kTile;
-                // this tile's row normalisers (rows past n_q contribute 0)
-                float* sl = s_lse[i & 1];
-                if (tid < kTile) sl[tid] = q0 + tid < p.n_q ? lse[q0 + tid] : INFINITY;
-                __syncthreads();
-                float v[32];
-                tmem_ld32(acc, v);
-                tmem_ld_wait();
-                const int64_t qc = q0 + cg * 32;
-                const float* slc = sl + cg * 32;
-                if (p.q_pos0 + qc >= kpos && qc + 31 < p.n_q) {  // every query of the group sees this key
+    run_tiles(&tk, hk, kt, &tq, h, t0, nt, p.nch, sm, &bar_a, bar_b, bar_full, bar_empty, tmem, p.status,
+              [&](int i, float (&v)[32]) {
+                const int64_t qc = (t0 + i) * kTile + cg * 32;
+                const bool full = p.q_pos0 + qc >= kpos && qc + 31 < p.n_q;  // every query of the group sees this key
+                if (full && (reinterpret_cast<uintptr_t>(lse + qc) & 15u) == 0) {
+                  const float4* l4 = reinterpret_cast<const float4*>(lse + qc);  // the group's row normalisers
 #pragma unroll
-                  for (int j = 0; j < 32; ++j) acc_sum += ex2(fmaf(v[j], c, -slc[j]));
+                  for (int j4 = 0; j4 < 8; ++j4) {
+                    const float4 n4 = __ldg(l4 + j4);
+                    acc_sum += ex2(fmaf(v[4 * j4], c, -n4.x));
+                    acc_sum += ex2(fmaf(v[4 * j4 + 1], c, -n4.y));
+                    acc_sum += ex2(fmaf(v[4 * j4 + 2], c, -n4.z));
+                    acc_sum += ex2(fmaf(v[4 * j4 + 3], c, -n4.w));
+                  }
+                } else if (full) {
+#pragma unroll
+                  for (int j = 0; j < 32; ++j) acc_sum += ex2(fmaf(v[j], c, -__ldg(lse + qc + j)));
                 } else {
 #pragma unroll
                   for (int j = 0; j < 32; ++j) {
                     const bool valid = p.q_pos0 + qc + j >= kpos && qc + j < p.n_q;
-                    acc_sum += valid ? ex2(fmaf(v[j], c, -slc[j])) : 0.0f;
+                    acc_sum += valid ? ex2(fmaf(v[j], c, -lse[qc + j])) : 0.0f;
                   }
                 }
               });
   }
   s_sum[cg][row] = acc_sum;
-  tc_fence_before();
   __syncthreads();
   if (cg == 0 && kpos < p.n_k)
     p.colsum[int64_t(h) * p.n_k + kpos] = (s_sum[0][row] + s_sum[1][row]) + (s_sum[2][row] + s_sum[3][row]);
