@@ -145,6 +145,23 @@ def _host_bytes(data: bytes, out: Optional[torch.Tensor]) -> torch.Tensor:
     return o[:len(data)]
 
 
+class PendingResult:
+    """A queued host-buffer codec call; ``result()`` completes it (once) and returns its value.
+    The buffers it writes must not be reused before ``result()`` returns."""
+
+    __slots__ = ("_finish", "_value")
+
+    def __init__(self, finish) -> None:
+        self._finish = finish
+        self._value = None
+
+    def result(self):
+        if self._finish is not None:
+            self._value = self._finish()
+            self._finish = None
+        return self._value
+
+
 _SIDE_STREAMS: dict = {}
 
 
@@ -239,17 +256,23 @@ class DitheredNBitCodec:
         from ``src`` and into ``out``; the call returns once ``out`` is complete."""
         return self.encode_pinned_batch([src], [out], uniforms=[uniform])[0]
 
-    def encode_pinned_batch(self, srcs, outs=None, *, uniforms=None) -> list:
+    def encode_pinned_batch(self, srcs, outs=None, *, uniforms=None, wait: bool = True):
         """``encode_pinned`` over several tensors, in order (one call each, so each
         gets the seed that call would get).  Host->device copies run on one side
         stream and device->host copies on another, so a tensor's blob travels
-        back while the next tensor's input is still arriving."""
+        back while the next tensor's input is still arriving.
+
+        With ``wait=False`` the call returns a :class:`PendingResult` once the
+        copies in and the kernels are queued; ``.result()`` then reads the outlier
+        counts, queues the copies out and returns the list of blobs.  Work queued
+        in between (for example the decode of the previous blobs) overlaps it."""
         outs = list(outs) if outs is not None else [None] * len(srcs)
         uniforms = list(uniforms) if uniforms is not None else [None] * len(srcs)
         if not (len(outs) == len(uniforms) == len(srcs)):
             raise ValueError("srcs, outs and uniforms must have the same length")
         L = self._hidden_dim
         dev = None
+        totals = None
         jobs = []
         for src in srcs:
             flat = _host_flat(src, torch.bfloat16)
@@ -286,6 +309,13 @@ class DitheredNBitCodec:
             idx, val, total = flatten_outliers(enc)
             totals[i:i + 1].copy_(total, non_blocking=True)
             j.update(enc=enc, idx=idx, val=val, done=cur.record_event())
+
+        def finish():
+            return self._encode_finish(jobs, outs, totals, dev)
+        return finish() if wait else PendingResult(finish)
+
+    def _encode_finish(self, jobs, outs, totals, dev) -> list:
+        d2h = _side_streams(dev)[1] if dev is not None else None
         results = []
         for i, (j, out) in enumerate(zip(jobs, outs)):
             if not j["num_tokens"]:
@@ -309,7 +339,7 @@ class DitheredNBitCodec:
                 out[o:o + n_codes].copy_(enc.codes[:n_codes], non_blocking=True)
             results.append(out[:size])
         if dev is not None:
-            d2h.synchronize()
+            d2h.record_event().synchronize()
         return results
 
     def decode_pinned(self, blob: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
@@ -318,9 +348,10 @@ class DitheredNBitCodec:
         ``decode`` returns for the same bytes."""
         return self.decode_pinned_batch([blob], [out])[0]
 
-    def decode_pinned_batch(self, blobs, outs=None) -> list:
+    def decode_pinned_batch(self, blobs, outs=None, *, wait: bool = True):
         """``decode_pinned`` over several blobs; a blob's values travel back to the
-        host while the next blob is still being copied in and decoded."""
+        host while the next blob is still being copied in and decoded.  With
+        ``wait=False`` returns a :class:`PendingResult` once everything is queued."""
         outs = list(outs) if outs is not None else [None] * len(blobs)
         if len(outs) != len(blobs):
             raise ValueError("blobs and outs must have the same length")
@@ -384,16 +415,22 @@ class DitheredNBitCodec:
                 out[:g * 32].copy_(dv, non_blocking=True)
             j["dv"] = dv
             results.append(out[:g * 32])
+        done = None
         if dev is not None:
             d2h.wait_stream(cur)
             with torch.cuda.stream(d2h):
                 h_status.copy_(statuses, non_blocking=True)
-            d2h.synchronize()
-            for i, j in enumerate(jobs):
-                if j["num_tokens"] and int(h_status[i]) & _native.FLAG_INDEX_RANGE:
-                    raise IndexError(f"outlier index out of range for a decoded size of {j['n_groups'] * 32} "
-                                     f"elements")
-        return results
+            done = d2h.record_event()
+
+        def finish():
+            if done is not None:
+                done.synchronize()
+                for i, j in enumerate(jobs):
+                    if j["num_tokens"] and int(h_status[i]) & _native.FLAG_INDEX_RANGE:
+                        raise IndexError(f"outlier index out of range for a decoded size of "
+                                         f"{j['n_groups'] * 32} elements")
+            return results
+        return finish() if wait else PendingResult(finish)
 
     def decode(self, target_bytes: bytes) -> bytes:
         self._decode_calls += 1

@@ -16,7 +16,11 @@ both back to bf16.
              start in pinned host memory, every step copies them to the device,
              encodes, writes the reference blob into pinned host memory, copies
              the blobs back, decodes, and reads the bf16 result back to the
-             host -- all inside the timed region.
+             host -- all inside the timed region.  Steps stream with one in
+             flight (the decode of step s-1 is queued before the encode of step
+             s, so its results travel device->host while step s's inputs travel
+             host->device); ``e2e_sequential`` is the same with no overlap
+             between steps.
 ``e2e_bytes_api`` — the same through ``encode(bytes)`` / ``decode(bytes)``
              (Python ``bytes`` in and out: adds host copies into pinned staging
              and into freshly allocated result objects).
@@ -493,8 +497,9 @@ def main() -> None:
     decK = torch.empty(ELEMS, dtype=torch.bfloat16, pin_memory=True)
     decV = torch.empty(ELEMS, dtype=torch.bfloat16, pin_memory=True)
     codec.decode_pinned_batch(codec.encode_pinned_batch([pinK, pinV], [blobK, blobV]), [decK, decV])  # warm
+    blob2 = [[blobK, blobV], [torch.empty_like(blobK).pin_memory(), torch.empty_like(blobV).pin_memory()]]
     h2d = d2h = 0
-    t_e2e = 0.0
+    t_seq = 0.0
     torch.cuda.synchronize()
     if dist:
         dist.barrier()
@@ -502,9 +507,22 @@ def main() -> None:
         t0 = time.perf_counter()
         bk, bv = codec.encode_pinned_batch([pinK, pinV], [blobK, blobV])
         dk, dv = codec.decode_pinned_batch([bk, bv], [decK, decV])
-        t_e2e += time.perf_counter() - t0
+        t_seq += time.perf_counter() - t0
         h2d = 2 * ELEMS * 2 + (bk.numel() - 8) + (bv.numel() - 8)
         d2h = bk.numel() + bv.numel() + 2 * (dk.numel() + dv.numel())
+    # streamed: step s's encode overlaps step s-1's decode (double-buffered blobs)
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    t0 = time.perf_counter()
+    blobs = codec.encode_pinned_batch([pinK, pinV], blob2[0])
+    for s_ in range(1, args.e2e_steps):
+        pend_dec = codec.decode_pinned_batch(blobs, [decK, decV], wait=False)
+        pend_enc = codec.encode_pinned_batch([pinK, pinV], blob2[s_ % 2], wait=False)
+        pend_dec.result()
+        blobs = pend_enc.result()
+    codec.decode_pinned_batch(blobs, [decK, decV])
+    t_e2e = time.perf_counter() - t0
 
     # the same through the bytes API
     hostK = pinK.view(torch.int16).numpy().tobytes()
@@ -545,14 +563,15 @@ def main() -> None:
                    "oracle_sample_elements": m, "oracle_sample_mismatches": mism}
 
     # max over ranks
-    t = torch.tensor([elapsed_ms, t_e2e, t_bytes], dtype=torch.float64, device=dev)
+    t = torch.tensor([elapsed_ms, t_e2e, t_bytes, t_seq], dtype=torch.float64, device=dev)
     if dist:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    elapsed_ms, t_e2e, t_bytes = float(t[0]), float(t[1]), float(t[2])
+    elapsed_ms, t_e2e, t_bytes, t_seq = float(t[0]), float(t[1]), float(t[2]), float(t[3])
 
     bytes_per_step = 2 * ELEMS * 2  # bf16 K + V through encode and decode
     value = world * bytes_per_step * args.steps / (elapsed_ms / 1e3) / 1e9
     e2e_value = world * bytes_per_step * args.e2e_steps / t_e2e / 1e9
+    e2e_seq_value = world * bytes_per_step * args.e2e_steps / t_seq / 1e9
     e2e_bytes_value = world * bytes_per_step * args.e2e_bytes_steps / t_bytes / 1e9 if t_bytes > 0 else None
     enc_alg_bytes = ELEMS * 2 + ELEMS * BITS // 8 + (ELEMS // 32) * 2 + 4 * n_out + 4 * nb._native.nbit_bucket_count(ELEMS // 32)
     achieved = enc_alg_bytes / (enc_ms / 1e3) / 1e9
@@ -587,7 +606,8 @@ def main() -> None:
                        "achieved_gbs": round(dec_achieved, 1), "frac": round(dec_achieved / peak, 4)},
             "e2e": {"value": round(e2e_value, 3), "unit": "GB/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "api": "DitheredNBitCodec.encode_pinned_batch/decode_pinned_batch",
-                    "steps": args.e2e_steps},
+                    "steps": args.e2e_steps, "mode": "streamed, one step in flight"},
+            "e2e_sequential": {"value": round(e2e_seq_value, 3), "unit": "GB/s", "steps": args.e2e_steps},
             "e2e_bytes_api": None if e2e_bytes_value is None else
             {"value": round(e2e_bytes_value, 3), "unit": "GB/s", "api": "DitheredNBitCodec.encode/decode(bytes)",
              "steps": args.e2e_bytes_steps},

@@ -318,6 +318,13 @@ def test_nbit_pinned_api_matches_bytes_api(cuda, bits, hidden):
     assert [g.numpy().tobytes() for g in got] == want
     back = bat.decode_pinned_batch(got)
     assert [t.view(torch.int16).numpy().tobytes() for t in back] == [seq.decode(w) for w in want]
+    # non-blocking calls, a decode queued between an encode and its result
+    asy = DitheredNBitCodec(hidden_dim=hidden, bits=bits)
+    first = asy.encode_pinned_batch([x.pin_memory(), y.pin_memory()])
+    pend_dec = asy.decode_pinned_batch(first, wait=False)
+    pend_enc = asy.encode_pinned_batch([x], wait=False)
+    assert [t.view(torch.int16).numpy().tobytes() for t in pend_dec.result()] == [seq.decode(w) for w in want[:2]]
+    assert pend_enc.result()[0].numpy().tobytes() == want[2]
     c = DitheredINT2Codec()
     u = torch.rand(x.numel() // 128 * 128)
     assert c.encode_pinned(x, uniform=u).numpy().tobytes() == c.encode(data, uniform=u)
