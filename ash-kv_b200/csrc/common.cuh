@@ -283,10 +283,10 @@ __device__ __forceinline__ uint32_t int8_codes4_bf16(uint32_t w0, uint32_t w1, c
 #pragma unroll
     for (int k = 0; k < 4; ++k) q[k] = __fdiv_rn(q[k], d.am);
   }
-  uint32_t out = 0;
-#pragma unroll
-  for (int k = 0; k < 4; ++k) out |= (uint32_t(int8_round_sat(q[k])) & 0xFFu) << (8 * k);
-  return out;
+  // each code is an int32 in [-128, 127]: its low byte is the int8 two's complement
+  const uint32_t c0 = uint32_t(int8_round_sat(q[0])), c1 = uint32_t(int8_round_sat(q[1]));
+  const uint32_t c2 = uint32_t(int8_round_sat(q[2])), c3 = uint32_t(int8_round_sat(q[3]));
+  return __byte_perm(__byte_perm(c0, c1, 0x0040), __byte_perm(c2, c3, 0x0040), 0x5410);
 }
 // Decode: v = RN(RN(float(code) * scale) / 127).  `fast` when the scale is
 // finite and in [2^-90, 2^90] (products are 0 or inside Markstein's range;

@@ -22,6 +22,7 @@ struct Int8EncParams {
   int64_t codes_stride;     // bytes
   uint8_t* scales;          // byte-addressed
   int32_t scales_per_slot;
+  int32_t sps_shift;        // log2(scales_per_slot) when it is a power of two, else -1
   int64_t scale_slot_stride;
   int32_t scale_fp16;
   int32_t fp32_product;
@@ -32,6 +33,7 @@ struct Int8DecParams {
   int64_t codes_stride;
   const uint8_t* scales;
   int32_t scales_per_slot;
+  int32_t sps_shift;        // log2(scales_per_slot) when it is a power of two, else -1
   int64_t scale_slot_stride;
   int32_t scale_fp16;
   int64_t n_rows;
@@ -71,8 +73,11 @@ __device__ __forceinline__ bool products_finite(float am, bool fp32_product) {
   return !FP16 || fp32_product || am < 515.0f;
 }
 
-__device__ __forceinline__ uint8_t* scale_addr(uint8_t* base, int64_t r, int32_t sps, int64_t slot_stride) {
-  return base + (r / sps) * slot_stride + (r % sps) * 2;
+// Byte offset of row r's scale: (r / sps) * slot_stride + (r % sps) * 2, with
+// shifts when sps is a power of two (the plain array and the hooks' head counts).
+__device__ __forceinline__ int64_t scale_offset(int64_t r, int32_t sps, int32_t sps_shift, int64_t slot_stride) {
+  if (sps_shift >= 0) return (r >> sps_shift) * slot_stride + (r & ((int64_t(1) << sps_shift) - 1)) * 2;
+  return (r / sps) * slot_stride + (r % sps) * 2;
 }
 
 // Each thread owns NCH chunks of 8 consecutive elements of its row.
@@ -121,7 +126,7 @@ __device__ __forceinline__ void encode_loaded_row(const Int8EncParams& p, int64_
   am = fmaxf(am, 1e-8f);
 
   if (lane_in_team == 0) {
-    uint8_t* sp = scale_addr(p.scales, r, p.scales_per_slot, p.scale_slot_stride);
+    uint8_t* sp = p.scales + scale_offset(r, p.scales_per_slot, p.sps_shift, p.scale_slot_stride);
     uint16_t sv = p.scale_fp16 ? f32_to_f16(am) : f32_to_bf16(am);
     *reinterpret_cast<uint16_t*>(sp) = sv;
   }
@@ -192,7 +197,7 @@ __global__ void __launch_bounds__(256) int8_encode_generic_kernel(const Int8EncP
   for (int off = 16; off > 0; off >>= 1) am = fmaxf(am, __shfl_xor_sync(0xFFFFFFFFu, am, off));
   am = fmaxf(am, 1e-8f);
   if (lane == 0) {
-    uint8_t* sp = scale_addr(p.scales, r, p.scales_per_slot, p.scale_slot_stride);
+    uint8_t* sp = p.scales + scale_offset(r, p.scales_per_slot, p.sps_shift, p.scale_slot_stride);
     *reinterpret_cast<uint16_t*>(sp) = p.scale_fp16 ? f32_to_f16(am) : f32_to_bf16(am);
   }
   uint8_t* out = p.codes + r * p.codes_stride;
@@ -217,7 +222,7 @@ __global__ void __launch_bounds__(256) int8_decode_kernel(const Int8DecParams p)
   const int64_t r = int64_t(blockIdx.x) * ROWS_PER_CTA + threadIdx.x / TEAM;
   if (r >= p.n_rows) return;
   const uint16_t sbits = *reinterpret_cast<const uint16_t*>(
-      p.scales + (r / p.scales_per_slot) * p.scale_slot_stride + (r % p.scales_per_slot) * 2);
+      p.scales + scale_offset(r, p.scales_per_slot, p.sps_shift, p.scale_slot_stride));
   const float scale = p.scale_fp16 ? f16_to_f32(sbits) : bf16_to_f32(sbits);
   const uint8_t* in = p.codes + r * p.codes_stride;
   const int64_t dst_row = p.row_index ? p.row_index[r] : r;
@@ -259,7 +264,7 @@ __global__ void __launch_bounds__(256) int8_decode_generic_kernel(const Int8DecP
   const int lane = threadIdx.x % 32;
   if (r >= p.n_rows) return;
   const uint16_t sbits = *reinterpret_cast<const uint16_t*>(
-      p.scales + (r / p.scales_per_slot) * p.scale_slot_stride + (r % p.scales_per_slot) * 2);
+      p.scales + scale_offset(r, p.scales_per_slot, p.sps_shift, p.scale_slot_stride));
   const float scale = p.scale_fp16 ? f16_to_f32(sbits) : bf16_to_f32(sbits);
   const uint8_t* in = p.codes + r * p.codes_stride;
   const int64_t dst_row = p.row_index ? p.row_index[r] : r;
@@ -267,6 +272,13 @@ __global__ void __launch_bounds__(256) int8_decode_generic_kernel(const Int8DecP
   const bool fast = int8_dec_fast(scale);
   for (int i = lane; i < p.row_len; i += 32)
     out[i] = out_bits(int8_dequant(int32_t(int8_t(in[i])), scale, fast), p.dst_fp16 != 0);
+}
+
+int32_t pow2_shift(int32_t v) {
+  if (v <= 0 || (v & (v - 1))) return -1;
+  int32_t k = 0;
+  while ((1 << k) < v) ++k;
+  return k;
 }
 
 template <typename P, typename KFast>
@@ -325,6 +337,7 @@ extern "C" ashkv_status_t ashkv_int8_encode_rows(
   p.n_rows = n_rows; p.row_len = row_len; p.src_stride = src_row_stride; p.row_index = d_row_index;
   p.codes = static_cast<uint8_t*>(d_codes); p.codes_stride = codes_row_stride;
   p.scales = static_cast<uint8_t*>(d_scales); p.scales_per_slot = scales_per_slot;
+  p.sps_shift = pow2_shift(scales_per_slot);
   p.scale_slot_stride = scale_slot_stride; p.scale_fp16 = scale_dtype == ASHKV_DTYPE_FP16;
   p.fp32_product = (flags & ASHKV_INT8_FP32_PRODUCT) ? 1 : 0;
 
@@ -360,6 +373,7 @@ extern "C" ashkv_status_t ashkv_int8_decode_rows(
   Int8DecParams p;
   p.codes = static_cast<const uint8_t*>(d_codes); p.codes_stride = codes_row_stride;
   p.scales = static_cast<const uint8_t*>(d_scales); p.scales_per_slot = scales_per_slot;
+  p.sps_shift = pow2_shift(scales_per_slot);
   p.scale_slot_stride = scale_slot_stride; p.scale_fp16 = scale_dtype == ASHKV_DTYPE_FP16;
   p.n_rows = n_rows; p.row_len = row_len;
   p.dst = static_cast<uint16_t*>(d_dst); p.dst_fp16 = dst_dtype == ASHKV_DTYPE_FP16;
