@@ -89,6 +89,13 @@ struct SmemGroup {  // rows of a 64-byte-swizzled shared-memory tile (the warp's
   }
 };
 
+// Hardware square-root approximation (relative error below 2^-21).
+__device__ __forceinline__ float sqrt_approx(float x) {
+  float r;
+  asm("sqrt.approx.f32 %0, %1;" : "=f"(r) : "f"(x));
+  return r;
+}
+
 // Two signed 16-bit integers clamped to [0, hi]: max(min(v, hi), 0) per half.
 __device__ __forceinline__ uint32_t clamp_codes_s16x2(uint32_t v, uint32_t hi) {
   uint32_t r;
@@ -167,9 +174,13 @@ __device__ __forceinline__ uint32_t encode_group(const Src& src, const NbitEncPa
 
   // Bounds on the reference threshold.  m2 has relative error < 2^-19 w.r.t.
   // sum (x - mu32)^2, which exceeds the exact M2 by 32 (mu - mu32)^2 with
-  // |mu - mu32| <= 31 * 2^-24 * max|x|.  Margins of 2^-16 / 2^-14 cover the
-  // remaining roundings (fp32 bound arithmetic, the fp32 rounding of sd,
-  // + 1e-8 and * sigma in the reference).
+  // |mu - mu32| <= 31 * 2^-24 * max|x|.  The bounds only choose between the
+  // fast and the exact outlier path, so they are evaluated with approximate
+  // operations: the product by RN(1/31) and sqrt.approx each err by less than
+  // 2^-21 relative (a flushed subnormal only lowers a bound by far less than
+  // the 1e-8 term's margin), and margins of 2^-16 on m2 and 2^-12 on the
+  // threshold cover them together with the other roundings (fp32 bound
+  // arithmetic, the fp32 rounding of sd, + 1e-8 and * sigma in the reference).
   const float sigma = p.sigma;
   const bool bounds_ok = sigma > 0.0f && isfinite(m2) && isfinite(xmax);
   float thr_lo = 0.0f, thr_hi = 0.0f;
@@ -177,8 +188,9 @@ __device__ __forceinline__ uint32_t encode_group(const Src& src, const NbitEncPa
     const float emu = 31.0001f * 0x1p-24f * xmax;
     const float m2_hi = m2 * (1.0f + 0x1p-16f);
     const float m2_lo = fmaxf(m2 * (1.0f - 0x1p-16f) - 32.0f * emu * emu * (1.0f + 0x1p-16f), 0.0f);
-    thr_hi = sigma * (sqrtf(m2_hi / 31.0f) + 1e-8f) * (1.0f + 0x1p-14f);
-    thr_lo = sigma * (sqrtf(m2_lo / 31.0f) + 1e-8f) * (1.0f - 0x1p-14f);
+    constexpr float kInv31 = 1.0f / 31.0f;
+    thr_hi = sigma * (sqrt_approx(m2_hi * kInv31) + 1e-8f) * (1.0f + 0x1p-12f);
+    thr_lo = sigma * (sqrt_approx(m2_lo * kInv31) + 1e-8f) * (1.0f - 0x1p-12f);
   }
   // Groups whose max |x - mu| exceeds thr_lo are resolved by the whole warp,
   // one group at a time: lane e takes element e, masks come from ballots, and
