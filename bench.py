@@ -442,7 +442,18 @@ def main() -> None:
     if world > 1:
         import torch.distributed as dist
         from datetime import timedelta
-        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+        # NCCL may print a version banner on stdout while its communicator is set
+        # up; send fd 1 to stderr meanwhile so stdout carries only the JSON line.
+        sys.stdout.flush()
+        saved = os.dup(1)
+        os.dup2(2, 1)
+        try:
+            dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+            dist.barrier()
+        finally:
+            sys.stdout.flush()
+            os.dup2(saved, 1)
+            os.close(saved)
 
     K = make_kv(1000 + 2 * rank, dev)
     V = make_kv(1001 + 2 * rank, dev)
