@@ -29,7 +29,6 @@ namespace ashkv {
 namespace {
 
 constexpr int kThreads = 256;
-constexpr int kTeam = 32;  // one warp per row
 constexpr int kRowsInFlight = 4;  // decode: rows whose codes a warp loads before converting
 
 
@@ -58,31 +57,48 @@ struct PagesParams {
 
 __host__ __device__ __forceinline__ int64_t codes_offset(int T) { return (4 * int64_t(T) + 15) / 16 * 16; }
 
-// Encode one row of `row_len` bf16 (NCH chunks of 8 per lane) into int8 codes + fp16 scale.
-// HALF: 128-element rows, only lanes 0..15 hold data.
-template <int NCH, bool HALF>
-__device__ __forceinline__ void encode_row(const uint16_t* src, int8_t* codes, uint16_t* scale, int lane) {
-  const bool on = !HALF || lane < 16;
+// Rows of 128 elements (HALF) are handled two per warp, one per 16-lane half;
+// longer rows take the whole warp.  `lin` is the lane's index within its row's
+// team, `on` whether the lane's row exists.
+template <bool HALF>
+constexpr int row_team() { return HALF ? 16 : 32; }
+
+// One lane's share of a row of `row_len` bf16 (NCH chunks of 8).
+template <int NCH>
+struct RowIn {
   uint4 ch[NCH];
+};
+
+template <int NCH, bool HALF>
+__device__ __forceinline__ void load_row_in(const uint16_t* src, int lin, bool on, RowIn<NCH>& ri) {
+#pragma unroll
+  for (int c = 0; c < NCH; ++c)
+    ri.ch[c] = on ? ld_nc_v4(src + (c * row_team<HALF>() + lin) * 8) : make_uint4(0, 0, 0, 0);
+}
+
+// Encode one loaded row into int8 codes + fp16 scale.  Called by every lane of the
+// warp (the row maximum is a shuffle reduction within the team).
+template <int NCH, bool HALF>
+__device__ __forceinline__ void encode_row(const RowIn<NCH>& ri, int8_t* codes, uint16_t* scale, int lin, bool on) {
+  constexpr int TEAM = row_team<HALF>();
   float am = 0.0f;
 #pragma unroll
   for (int c = 0; c < NCH; ++c) {
-    ch[c] = on ? ld_nc_v4(src + (c * kTeam + lane) * 8) : make_uint4(0, 0, 0, 0);
-    const uint32_t w[4] = {ch[c].x, ch[c].y, ch[c].z, ch[c].w};
+    const uint32_t w[4] = {ri.ch[c].x, ri.ch[c].y, ri.ch[c].z, ri.ch[c].w};
 #pragma unroll
     for (int k = 0; k < 4; ++k) am = fmaxf(am, fmaxf(fabsf(bf16lo(w[k])), fabsf(bf16hi(w[k]))));
   }
 #pragma unroll
-  for (int off = 16; off > 0; off >>= 1) am = fmaxf(am, __shfl_xor_sync(0xFFFFFFFFu, am, off));
+  for (int off = TEAM / 2; off > 0; off >>= 1) am = fmaxf(am, __shfl_xor_sync(0xFFFFFFFFu, am, off));
   am = fmaxf(am, 1e-8f);
-  if (lane == 0) *scale = f32_to_f16(am);
   if (!on) return;
+  if (lin == 0) *scale = f32_to_f16(am);
   // bf16 x * 127 overflows only when am > 2.6e36, outside the fast divisor range
   const Int8Div d = int8_div(am, true);
 #pragma unroll
   for (int c = 0; c < NCH; ++c) {
-    const uint32_t w[4] = {ch[c].x, ch[c].y, ch[c].z, ch[c].w};
-    *reinterpret_cast<uint2*>(codes + (c * kTeam + lane) * 8) =
+    const uint32_t w[4] = {ri.ch[c].x, ri.ch[c].y, ri.ch[c].z, ri.ch[c].w};
+    *reinterpret_cast<uint2*>(codes + (c * TEAM + lin) * 8) =
         make_uint2(int8_codes4_bf16(w[0], w[1], d), int8_codes4_bf16(w[2], w[3], d));
   }
 }
@@ -94,24 +110,25 @@ struct RowCodes {
   float scale;
 };
 template <int NCH, bool HALF>
-__device__ __forceinline__ void load_row_codes(const int8_t* codes, const uint16_t* scale, int lane,
+__device__ __forceinline__ void load_row_codes(const int8_t* codes, const uint16_t* scale, int lin, bool on,
                                                RowCodes<NCH>& rc) {
+  if (!on) return;
   rc.scale = f16_to_f32(*scale);
-  if (HALF && lane >= 16) return;
 #pragma unroll
-  for (int c = 0; c < NCH; ++c) rc.w[c] = *reinterpret_cast<const uint2*>(codes + (c * kTeam + lane) * 8);
+  for (int c = 0; c < NCH; ++c)
+    rc.w[c] = *reinterpret_cast<const uint2*>(codes + (c * row_team<HALF>() + lin) * 8);
 }
 
 template <int NCH, bool HALF>
-__device__ __forceinline__ void decode_row(const RowCodes<NCH>& rc, uint16_t* dst, int lane) {
-  if (HALF && lane >= 16) return;
+__device__ __forceinline__ void decode_row(const RowCodes<NCH>& rc, uint16_t* dst, int lin, bool on) {
+  if (!on) return;
   const float scale = rc.scale;
   const bool fast = int8_dec_fast(scale);
   const Recip y = make_recip(127.0f);
   const f2 S = pk2(scale, scale), YHI = pk2(y.hi, y.hi), YLO = pk2(y.lo, y.lo), N127 = pk2(-127.0f, -127.0f);
 #pragma unroll
   for (int c = 0; c < NCH; ++c) {
-    const int e0 = (c * kTeam + lane) * 8;
+    const int e0 = (c * row_team<HALF>() + lin) * 8;
     const uint32_t ww[2] = {rc.w[c].x, rc.w[c].y};
     uint32_t o[4];
 #pragma unroll
@@ -133,90 +150,150 @@ __device__ __forceinline__ void decode_row(const RowCodes<NCH>& rc, uint16_t* ds
   }
 }
 
+// A CTA walks its list entries (blockIdx.x, + gridDim.x, ...) in batches of kBatch:
+// the first kBatch threads resolve one entry each (list -> page -> layer, slot ->
+// row pointers) into shared memory, so that the chain of dependent index loads is
+// paid once per batch instead of once per page, then all warps stream the rows.
+constexpr int kBatch = 32;
+
+struct PageRef {
+  const uint16_t* k;  // K row of the page's first token
+  const uint16_t* v;
+  uint8_t* base;      // arena slot
+  int32_t page;
+  int32_t slot;       // -1: entry skipped (status already written)
+};
+
+__device__ __forceinline__ int batch_len(int64_t b0, int32_t count) {
+  const int64_t left = (count - b0 + gridDim.x - 1) / gridDim.x;
+  return left < kBatch ? int(left) : kBatch;
+}
+
+__device__ __forceinline__ PageRef page_ref(const PagesParams& p, int32_t page, int32_t l, int32_t slot) {
+  const int64_t off = int64_t(p.token_start[page]) * p.row_stride;
+  return PageRef{reinterpret_cast<const uint16_t*>(p.layer_k[l]) + off,
+                 reinterpret_cast<const uint16_t*>(p.layer_v[l]) + off,
+                 p.arena + int64_t(slot) * p.slot_bytes, page, slot};
+}
+
 template <int NCH, bool HALF>
 __global__ void __launch_bounds__(kThreads) encode_pages_kernel(const PagesParams p) {
+  __shared__ PageRef s_ref[kBatch];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int32_t count = min(*p.count, p.max_entries);
   const int32_t top = *p.free_top;
   const int T = p.tokens_per_page;
   const int64_t c0 = codes_offset(T);
-  for (int32_t i = blockIdx.x; i < count; i += gridDim.x) {
-    const int32_t page = p.list[i];
-    const bool have_slot = i < top;
-    const int32_t l = p.layer_id[page];
-    if (!have_slot || l < 0 || l >= p.n_layers) {
-      if (threadIdx.x == 0) p.entry_status[i] = have_slot ? 2 : 1;
-      continue;
+  constexpr int kWarps = kThreads / 32;
+  constexpr int RPW = HALF ? 2 : 1;                  // rows per warp: one per 16-lane half
+  constexpr int U = (HALF || NCH <= 2) ? 2 : 1;      // row slots whose loads are in flight together
+  const int sub = HALF ? (lane >> 4) : 0, lin = HALF ? (lane & 15) : lane;
+  for (int64_t b0 = blockIdx.x; b0 < count; b0 += int64_t(kBatch) * gridDim.x) {
+    const int nb = batch_len(b0, count);
+    if (threadIdx.x < nb) {
+      const int64_t i = b0 + int64_t(threadIdx.x) * gridDim.x;
+      const int32_t page = p.list[i];
+      PageRef ref{nullptr, nullptr, nullptr, page, -1};
+      int32_t status = 1;  // no free slot
+      if (i < top) {
+        const int32_t l = p.layer_id[page];
+        const int32_t slot = p.free_stack[top - 1 - i];
+        status = 2;
+        if (l >= 0 && l < p.n_layers && slot >= 0 && slot < p.n_slots) {
+          ref = page_ref(p, page, l, slot);
+          p.page_slot[page] = slot;
+          status = 0;
+        }
+      }
+      p.entry_status[i] = status;
+      s_ref[threadIdx.x] = ref;
     }
-    const int32_t slot = p.free_stack[top - 1 - i];
-    if (slot < 0 || slot >= p.n_slots) {
-      if (threadIdx.x == 0) p.entry_status[i] = 2;
-      continue;
+    __syncthreads();
+    for (int e = 0; e < nb; ++e) {
+      const PageRef ref = s_ref[e];
+      if (ref.slot < 0) continue;
+      for (int r0 = warp * RPW; r0 < 2 * T; r0 += U * RPW * kWarps) {
+        RowIn<NCH> ri[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          const int r = r0 + u * RPW * kWarps + sub;
+          const bool on = r < 2 * T;
+          const int j = r >= T ? r - T : r;
+          load_row_in<NCH, HALF>((r >= T ? ref.v : ref.k) + j * p.row_stride, lin, on, ri[u]);
+        }
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          const int r = r0 + u * RPW * kWarps + sub;
+          const bool on = r < 2 * T;
+          encode_row<NCH, HALF>(ri[u], reinterpret_cast<int8_t*>(ref.base + c0 + int64_t(r) * p.row_len),
+                                reinterpret_cast<uint16_t*>(ref.base) + r, lin, on);
+        }
+      }
     }
-    uint8_t* base = p.arena + int64_t(slot) * p.slot_bytes;
-    const int64_t ts = p.token_start[page];
-    for (int r = warp; r < 2 * T; r += kThreads / 32) {
-      const bool is_v = r >= T;
-      const int j = is_v ? r - T : r;
-      const uint16_t* src = reinterpret_cast<const uint16_t*>(is_v ? p.layer_v[l] : p.layer_k[l]) +
-                            (ts + j) * p.row_stride;
-      int8_t* codes = reinterpret_cast<int8_t*>(base + c0 + int64_t(r) * p.row_len);
-      uint16_t* scale = reinterpret_cast<uint16_t*>(base) + r;
-      encode_row<NCH, HALF>(src, codes, scale, lane);
-    }
-    if (threadIdx.x == 0) {
-      p.page_slot[page] = slot;
-      p.entry_status[i] = 0;
-    }
+    __syncthreads();  // s_ref is rewritten by the next batch
   }
 }
 
 template <int NCH, bool HALF>
 __global__ void __launch_bounds__(kThreads) decode_pages_kernel(const PagesParams p) {
+  __shared__ PageRef s_ref[kBatch];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int32_t count = min(*p.count, p.max_entries);
   const int T = p.tokens_per_page;
   const int64_t c0 = codes_offset(T);
-  for (int32_t i = blockIdx.x; i < count; i += gridDim.x) {
-    const int32_t page = p.list[i];
-    const int32_t l = p.layer_id[page];
-    const int32_t slot = p.page_slot[page];
-    if (l < 0 || l >= p.n_layers || slot < 0 || slot >= p.n_slots) {
-      if (threadIdx.x == 0) p.entry_status[i] = 2;
-      continue;
-    }
-    const uint8_t* base = p.arena + int64_t(slot) * p.slot_bytes;
-    const int64_t ts = p.token_start[page];
-    // kRowsInFlight rows per warp: every row's codes are loaded before any is converted
-    constexpr int kWarps = kThreads / 32;
-    for (int r0 = warp; r0 < 2 * T; r0 += kRowsInFlight * kWarps) {
-      RowCodes<NCH> rc[kRowsInFlight];
-#pragma unroll
-      for (int u = 0; u < kRowsInFlight; ++u) {
-        const int r = r0 + u * kWarps;
-        if (r < 2 * T)
-          load_row_codes<NCH, HALF>(reinterpret_cast<const int8_t*>(base + c0 + int64_t(r) * p.row_len),
-                                    reinterpret_cast<const uint16_t*>(base) + r, lane, rc[u]);
+  constexpr int kWarps = kThreads / 32;
+  constexpr int RPW = HALF ? 2 : 1;
+  const int sub = HALF ? (lane >> 4) : 0, lin = HALF ? (lane & 15) : lane;
+  for (int64_t b0 = blockIdx.x; b0 < count; b0 += int64_t(kBatch) * gridDim.x) {
+    const int nb = batch_len(b0, count);
+    if (threadIdx.x < nb) {
+      const int64_t i = b0 + int64_t(threadIdx.x) * gridDim.x;
+      const int32_t page = p.list[i];
+      const int32_t l = p.layer_id[page];
+      const int32_t slot = p.page_slot[page];
+      PageRef ref{nullptr, nullptr, nullptr, page, -1};
+      int32_t status = 2;
+      if (l >= 0 && l < p.n_layers && slot >= 0 && slot < p.n_slots) {
+        ref = page_ref(p, page, l, slot);
+        status = 0;
       }
+      p.entry_status[i] = status;
+      s_ref[threadIdx.x] = ref;
+    }
+    __syncthreads();
+    for (int e = 0; e < nb; ++e) {
+      const PageRef ref = s_ref[e];
+      if (ref.slot < 0) continue;
+      // kRowsInFlight row slots per warp (a slot is two rows of 128, one per
+      // 16-lane half, or one longer row): all codes are loaded before any is converted
+      for (int r0 = warp * RPW; r0 < 2 * T; r0 += kRowsInFlight * kWarps * RPW) {
+        RowCodes<NCH> rc[kRowsInFlight];
 #pragma unroll
-      for (int u = 0; u < kRowsInFlight; ++u) {
-        const int r = r0 + u * kWarps;
-        if (r >= 2 * T) break;
-        const bool is_v = r >= T;
-        const int j = is_v ? r - T : r;
-        uint16_t* dst = reinterpret_cast<uint16_t*>(is_v ? p.layer_v[l] : p.layer_k[l]) + (ts + j) * p.row_stride;
-        decode_row<NCH, HALF>(rc[u], dst, lane);
+        for (int u = 0; u < kRowsInFlight; ++u) {
+          const int r = r0 + u * kWarps * RPW + sub;
+          load_row_codes<NCH, HALF>(reinterpret_cast<const int8_t*>(ref.base + c0 + int64_t(r) * p.row_len),
+                                    reinterpret_cast<const uint16_t*>(ref.base) + r, lin, r < 2 * T, rc[u]);
+        }
+#pragma unroll
+        for (int u = 0; u < kRowsInFlight; ++u) {
+          const int r = r0 + u * kWarps * RPW + sub;
+          if (r0 + u * kWarps * RPW >= 2 * T) break;
+          const int j = r >= T ? r - T : r;
+          decode_row<NCH, HALF>(rc[u], const_cast<uint16_t*>(r >= T ? ref.v : ref.k) + j * p.row_stride, lin,
+                                r < 2 * T);
+        }
       }
     }
-    __syncthreads();  // every warp is done reading the slot before it is released
-    if (threadIdx.x == 0) {
-      p.entry_status[i] = 0;
-      if (p.free_slots) {
-        p.page_slot[page] = -1;
+    __syncthreads();  // every warp is done reading the batch's slots before they are released
+    if (threadIdx.x < nb && p.free_slots) {
+      const PageRef ref = s_ref[threadIdx.x];
+      if (ref.slot >= 0) {
+        p.page_slot[ref.page] = -1;
         const int32_t pos = atomicAdd(p.free_top_rw, 1);
-        if (pos < p.n_slots) p.free_stack[pos] = slot;
+        if (pos < p.n_slots) p.free_stack[pos] = ref.slot;
       }
     }
+    __syncthreads();  // s_ref is rewritten by the next batch
   }
 }
 

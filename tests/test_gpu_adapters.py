@@ -184,7 +184,7 @@ def test_shadow_allocator_arena(cuda):
     a.free(12345)
 
 
-@pytest.mark.parametrize("heads", [8, 1])
+@pytest.mark.parametrize("heads", [8, 4, 2, 1])
 def test_batch_policy_demote_promote_pages(cuda, heads):
     """Config-4 style: score -> tier -> gather+INT8 encode of demoted pages into arena
     slots, then decode+scatter back; bytes compared with the oracle per token row."""
@@ -233,6 +233,69 @@ def test_batch_policy_demote_promote_pages(cuda, heads):
         assert bool((k[li][ts:ts + T] == 0).all())
     mig.commit_transitions()
     assert bool((tab.tier[rows] == 1).all())
+
+
+@pytest.mark.parametrize("heads,T", [(1, 16), (2, 12), (8, 16)])
+def test_batch_pages_many_entries_per_cta(cuda, heads, T):
+    """More list entries than 32 x the grid, so every CTA resolves several batches of
+    entries (the last one partial); T=12 leaves row passes partly empty; one entry names
+    a layer out of range.  Slot bytes (scales, then K and V codes) and the decoded K/V
+    rows are compared with the oracle."""
+    layers, ppl = 4, 10240
+    tokens, n = ppl * T, layers * ppl
+    g = torch.Generator(device=cuda).manual_seed(23 + heads)
+    k = [torch.randn(tokens, heads, 128, generator=g, device=cuda).to(torch.bfloat16) for _ in range(layers)]
+    v = [torch.randn(tokens, heads, 128, generator=g, device=cuda).to(torch.bfloat16) for _ in range(layers)]
+    kv = KVLayers(k, v)
+    L = kv.row_len
+    tab = DevicePageTable.empty(n, cuda)
+    idx = torch.arange(n, device=cuda)
+    tab.layer.copy_(idx // ppl)
+    tab.token_start.copy_((idx % ppl) * T)
+    bad = n // 3
+    tab.layer[bad] = layers
+    sb = int8_page_slot_bytes(T, L)
+    arena = SlotArena(n, sb, cuda)
+    mig = BatchMigrator(tab, kv, arena, ASHKVConfig(), [(0, 1), (1, 0)], tokens_per_page=T)
+    lst = torch.randperm(n, generator=g, device=cuda).to(torch.int32)
+    cnt = torch.tensor([n], dtype=torch.int32, device=cuda)
+    orig = [[t.clone() for t in k], [t.clone() for t in v]]
+    mig.encode(lst, cnt)
+    torch.cuda.synchronize()
+    pos_bad = int((lst == bad).nonzero()[0, 0])
+    st = mig.status_encode[:n].cpu().numpy()
+    assert st[pos_bad] == 2 and int(np.count_nonzero(st)) == 1
+    assert arena.free_count() == 0
+    slot = tab.slot.cpu().numpy()
+    assert slot[bad] == -1 and len(np.unique(np.delete(slot, bad))) == n - 1
+    c0 = (4 * T + 15) // 16 * 16
+    sample = np.unique(np.r_[np.arange(0, n, n // 97), n - 1])
+    sample = sample[sample != bad]
+    blobs = arena.data.view(n, sb)[torch.from_numpy(slot[sample]).long().to(cuda)].cpu().numpy()
+    for p, blob in zip(sample, blobs):
+        li, ts = int(p) // ppl, (int(p) % ppl) * T
+        sc = blob[:4 * T].view(np.uint16)
+        for h in range(2):
+            codes, scales = oracle.int8_encode(u16(orig[h][li][ts:ts + T]).reshape(T, L), L, scale_fp16=True)
+            assert np.array_equal(sc[h * T:(h + 1) * T], scales)
+            assert np.array_equal(blob[c0 + h * T * L:c0 + (h + 1) * T * L].view(np.int8).reshape(T, L), codes)
+    for t in k + v:
+        t.zero_()
+    mig.decode(lst, cnt, free_slots=True)
+    torch.cuda.synchronize()
+    sd = mig.status_decode[:n].cpu().numpy()
+    assert sd[pos_bad] == 2 and int(np.count_nonzero(sd)) == 1
+    assert arena.free_count() == n - 1
+    assert int(tab.slot.ne(-1).sum()) == 0
+    rows = tokens if heads <= 2 else 2048  # whole layers through the oracle for narrow rows
+    for h, cur in enumerate((k, v)):
+        for li in range(layers):
+            codes, scales = oracle.int8_encode(u16(orig[h][li][:rows]).reshape(rows, L), L, scale_fp16=True)
+            want = oracle.int8_decode(codes, scales, scale_fp16=True)
+            if li == bad // ppl:
+                b0 = (bad % ppl) * T
+                want[b0:b0 + T] = 0
+            assert np.array_equal(u16(cur[li][:rows]).reshape(rows, L), want), (h, li)
 
 
 def test_batch_encode_runs_out_of_slots(cuda):
