@@ -29,7 +29,10 @@ namespace ashkv {
 namespace {
 
 constexpr int kThreads = 256;
-constexpr int kRowsInFlight = 4;  // decode: rows whose codes a warp loads before converting
+// decode: row groups whose codes a warp loads before converting any (4 for
+// full-warp rows; 2 when a warp holds several rows, which is already 2 x RPW rows)
+template <int TEAM>
+constexpr int rows_in_flight() { return TEAM == 32 ? 4 : 2; }
 
 
 struct PagesParams {
@@ -57,30 +60,29 @@ struct PagesParams {
 
 __host__ __device__ __forceinline__ int64_t codes_offset(int T) { return (4 * int64_t(T) + 15) / 16 * 16; }
 
-// Rows of 128 elements (HALF) are handled two per warp, one per 16-lane half;
-// longer rows take the whole warp.  `lin` is the lane's index within its row's
-// team, `on` whether the lane's row exists.
-template <bool HALF>
-constexpr int row_team() { return HALF ? 16 : 32; }
+// Row mapping: TEAM consecutive lanes hold one row, NCH chunks of 8 elements per
+// lane (row_len = TEAM * NCH * 8), so a warp covers RPW = 32 / TEAM rows at a time.
+// Every supported row width uses NCH = 4 (8 for 2048), which keeps the per-lane
+// work per row -- the row maximum's shuffles, the divisor, the scale -- spread
+// over 32 elements whatever the number of local heads.  `lin` is the lane's index
+// within its team, `on` whether its row exists.
 
-// One lane's share of a row of `row_len` bf16 (NCH chunks of 8).
+// One lane's share of a row (NCH chunks of 8 bf16).
 template <int NCH>
 struct RowIn {
   uint4 ch[NCH];
 };
 
-template <int NCH, bool HALF>
+template <int TEAM, int NCH>
 __device__ __forceinline__ void load_row_in(const uint16_t* src, int lin, bool on, RowIn<NCH>& ri) {
 #pragma unroll
-  for (int c = 0; c < NCH; ++c)
-    ri.ch[c] = on ? ld_nc_v4(src + (c * row_team<HALF>() + lin) * 8) : make_uint4(0, 0, 0, 0);
+  for (int c = 0; c < NCH; ++c) ri.ch[c] = on ? ld_nc_v4(src + (c * TEAM + lin) * 8) : make_uint4(0, 0, 0, 0);
 }
 
 // Encode one loaded row into int8 codes + fp16 scale.  Called by every lane of the
 // warp (the row maximum is a shuffle reduction within the team).
-template <int NCH, bool HALF>
+template <int TEAM, int NCH>
 __device__ __forceinline__ void encode_row(const RowIn<NCH>& ri, int8_t* codes, uint16_t* scale, int lin, bool on) {
-  constexpr int TEAM = row_team<HALF>();
   float am = 0.0f;
 #pragma unroll
   for (int c = 0; c < NCH; ++c) {
@@ -109,17 +111,16 @@ struct RowCodes {
   uint2 w[NCH];
   float scale;
 };
-template <int NCH, bool HALF>
+template <int TEAM, int NCH>
 __device__ __forceinline__ void load_row_codes(const int8_t* codes, const uint16_t* scale, int lin, bool on,
                                                RowCodes<NCH>& rc) {
   if (!on) return;
   rc.scale = f16_to_f32(*scale);
 #pragma unroll
-  for (int c = 0; c < NCH; ++c)
-    rc.w[c] = *reinterpret_cast<const uint2*>(codes + (c * row_team<HALF>() + lin) * 8);
+  for (int c = 0; c < NCH; ++c) rc.w[c] = *reinterpret_cast<const uint2*>(codes + (c * TEAM + lin) * 8);
 }
 
-template <int NCH, bool HALF>
+template <int TEAM, int NCH>
 __device__ __forceinline__ void decode_row(const RowCodes<NCH>& rc, uint16_t* dst, int lin, bool on) {
   if (!on) return;
   const float scale = rc.scale;
@@ -128,7 +129,7 @@ __device__ __forceinline__ void decode_row(const RowCodes<NCH>& rc, uint16_t* ds
   const f2 S = pk2(scale, scale), YHI = pk2(y.hi, y.hi), YLO = pk2(y.lo, y.lo), N127 = pk2(-127.0f, -127.0f);
 #pragma unroll
   for (int c = 0; c < NCH; ++c) {
-    const int e0 = (c * row_team<HALF>() + lin) * 8;
+    const int e0 = (c * TEAM + lin) * 8;
     const uint32_t ww[2] = {rc.w[c].x, rc.w[c].y};
     uint32_t o[4];
 #pragma unroll
@@ -155,6 +156,7 @@ __device__ __forceinline__ void decode_row(const RowCodes<NCH>& rc, uint16_t* ds
 // row pointers) into shared memory, so that the chain of dependent index loads is
 // paid once per batch instead of once per page, then all warps stream the rows.
 constexpr int kBatch = 32;
+constexpr int kWarps = kThreads / 32;
 
 struct PageRef {
   const uint16_t* k;  // K row of the page's first token
@@ -176,18 +178,36 @@ __device__ __forceinline__ PageRef page_ref(const PagesParams& p, int32_t page, 
                  p.arena + int64_t(slot) * p.slot_bytes, page, slot};
 }
 
-template <int NCH, bool HALF>
-__global__ void __launch_bounds__(kThreads) encode_pages_kernel(const PagesParams p) {
+// Warps of a CTA in groups of `wpp` per page: a pass of one warp covers SPAN =
+// U * RPW consecutive rows of its page, so a page of 2T rows takes
+// ceil(2T / SPAN) warps (at most kWarps) and the CTA streams kWarps / wpp pages
+// of its batch at once.
+struct WarpPlan {
+  int wpp, ppp, slot, wi;  // warps per page, pages per pass, this warp's page slot and index in its group
+};
+template <int SPAN>
+__device__ __forceinline__ WarpPlan warp_plan(int T, int warp) {
+  WarpPlan w;
+  w.wpp = min((2 * T + SPAN - 1) / SPAN, kWarps);
+  w.ppp = kWarps / w.wpp;
+  w.slot = warp / w.wpp;
+  w.wi = warp - w.slot * w.wpp;
+  return w;
+}
+
+template <int TEAM, int NCH>
+__global__ void __launch_bounds__(kThreads, NCH <= 4 ? 3 : 1) encode_pages_kernel(const PagesParams p) {
   __shared__ PageRef s_ref[kBatch];
+  constexpr int RPW = 32 / TEAM;                     // rows per warp-wide load
+  constexpr int U = NCH <= 2 ? 2 : 1;                // row groups whose loads are in flight together
+  constexpr int SPAN = U * RPW;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int sub = lane / TEAM, lin = lane % TEAM;
   const int32_t count = min(*p.count, p.max_entries);
   const int32_t top = *p.free_top;
   const int T = p.tokens_per_page;
   const int64_t c0 = codes_offset(T);
-  constexpr int kWarps = kThreads / 32;
-  constexpr int RPW = HALF ? 2 : 1;                  // rows per warp: one per 16-lane half
-  constexpr int U = (HALF || NCH <= 2) ? 2 : 1;      // row slots whose loads are in flight together
-  const int sub = HALF ? (lane >> 4) : 0, lin = HALF ? (lane & 15) : lane;
+  const WarpPlan wp = warp_plan<SPAN>(T, warp);
   for (int64_t b0 = blockIdx.x; b0 < count; b0 += int64_t(kBatch) * gridDim.x) {
     const int nb = batch_len(b0, count);
     if (threadIdx.x < nb) {
@@ -209,24 +229,24 @@ __global__ void __launch_bounds__(kThreads) encode_pages_kernel(const PagesParam
       s_ref[threadIdx.x] = ref;
     }
     __syncthreads();
-    for (int e = 0; e < nb; ++e) {
-      const PageRef ref = s_ref[e];
-      if (ref.slot < 0) continue;
-      for (int r0 = warp * RPW; r0 < 2 * T; r0 += U * RPW * kWarps) {
-        RowIn<NCH> ri[U];
+    if (wp.slot < wp.ppp) {
+      for (int e = wp.slot; e < nb; e += wp.ppp) {
+        const PageRef ref = s_ref[e];
+        if (ref.slot < 0) continue;
+        for (int r0 = wp.wi * SPAN; r0 < 2 * T; r0 += wp.wpp * SPAN) {
+          RowIn<NCH> ri[U];
 #pragma unroll
-        for (int u = 0; u < U; ++u) {
-          const int r = r0 + u * RPW * kWarps + sub;
-          const bool on = r < 2 * T;
-          const int j = r >= T ? r - T : r;
-          load_row_in<NCH, HALF>((r >= T ? ref.v : ref.k) + j * p.row_stride, lin, on, ri[u]);
-        }
+          for (int u = 0; u < U; ++u) {
+            const int r = r0 + u * RPW + sub;
+            const int j = r >= T ? r - T : r;
+            load_row_in<TEAM, NCH>((r >= T ? ref.v : ref.k) + j * p.row_stride, lin, r < 2 * T, ri[u]);
+          }
 #pragma unroll
-        for (int u = 0; u < U; ++u) {
-          const int r = r0 + u * RPW * kWarps + sub;
-          const bool on = r < 2 * T;
-          encode_row<NCH, HALF>(ri[u], reinterpret_cast<int8_t*>(ref.base + c0 + int64_t(r) * p.row_len),
-                                reinterpret_cast<uint16_t*>(ref.base) + r, lin, on);
+          for (int u = 0; u < U; ++u) {
+            const int r = r0 + u * RPW + sub;
+            encode_row<TEAM, NCH>(ri[u], reinterpret_cast<int8_t*>(ref.base + c0 + int64_t(r) * p.row_len),
+                                  reinterpret_cast<uint16_t*>(ref.base) + r, lin, r < 2 * T);
+          }
         }
       }
     }
@@ -234,16 +254,18 @@ __global__ void __launch_bounds__(kThreads) encode_pages_kernel(const PagesParam
   }
 }
 
-template <int NCH, bool HALF>
-__global__ void __launch_bounds__(kThreads) decode_pages_kernel(const PagesParams p) {
+template <int TEAM, int NCH>
+__global__ void __launch_bounds__(kThreads, TEAM < 32 ? 3 : 1) decode_pages_kernel(const PagesParams p) {
   __shared__ PageRef s_ref[kBatch];
+  constexpr int RPW = 32 / TEAM;
+  constexpr int U = rows_in_flight<TEAM>();
+  constexpr int SPAN = U * RPW;  // all codes of a pass are loaded before any is converted
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int sub = lane / TEAM, lin = lane % TEAM;
   const int32_t count = min(*p.count, p.max_entries);
   const int T = p.tokens_per_page;
   const int64_t c0 = codes_offset(T);
-  constexpr int kWarps = kThreads / 32;
-  constexpr int RPW = HALF ? 2 : 1;
-  const int sub = HALF ? (lane >> 4) : 0, lin = HALF ? (lane & 15) : lane;
+  const WarpPlan wp = warp_plan<SPAN>(T, warp);
   for (int64_t b0 = blockIdx.x; b0 < count; b0 += int64_t(kBatch) * gridDim.x) {
     const int nb = batch_len(b0, count);
     if (threadIdx.x < nb) {
@@ -261,26 +283,25 @@ __global__ void __launch_bounds__(kThreads) decode_pages_kernel(const PagesParam
       s_ref[threadIdx.x] = ref;
     }
     __syncthreads();
-    for (int e = 0; e < nb; ++e) {
-      const PageRef ref = s_ref[e];
-      if (ref.slot < 0) continue;
-      // kRowsInFlight row slots per warp (a slot is two rows of 128, one per
-      // 16-lane half, or one longer row): all codes are loaded before any is converted
-      for (int r0 = warp * RPW; r0 < 2 * T; r0 += kRowsInFlight * kWarps * RPW) {
-        RowCodes<NCH> rc[kRowsInFlight];
+    if (wp.slot < wp.ppp) {
+      for (int e = wp.slot; e < nb; e += wp.ppp) {
+        const PageRef ref = s_ref[e];
+        if (ref.slot < 0) continue;
+        for (int r0 = wp.wi * SPAN; r0 < 2 * T; r0 += wp.wpp * SPAN) {
+          RowCodes<NCH> rc[U];
 #pragma unroll
-        for (int u = 0; u < kRowsInFlight; ++u) {
-          const int r = r0 + u * kWarps * RPW + sub;
-          load_row_codes<NCH, HALF>(reinterpret_cast<const int8_t*>(ref.base + c0 + int64_t(r) * p.row_len),
-                                    reinterpret_cast<const uint16_t*>(ref.base) + r, lin, r < 2 * T, rc[u]);
-        }
+          for (int u = 0; u < U; ++u) {
+            const int r = r0 + u * RPW + sub;
+            load_row_codes<TEAM, NCH>(reinterpret_cast<const int8_t*>(ref.base + c0 + int64_t(r) * p.row_len),
+                                      reinterpret_cast<const uint16_t*>(ref.base) + r, lin, r < 2 * T, rc[u]);
+          }
 #pragma unroll
-        for (int u = 0; u < kRowsInFlight; ++u) {
-          const int r = r0 + u * kWarps * RPW + sub;
-          if (r0 + u * kWarps * RPW >= 2 * T) break;
-          const int j = r >= T ? r - T : r;
-          decode_row<NCH, HALF>(rc[u], const_cast<uint16_t*>(r >= T ? ref.v : ref.k) + j * p.row_stride, lin,
-                                r < 2 * T);
+          for (int u = 0; u < U; ++u) {
+            const int r = r0 + u * RPW + sub;
+            const int j = r >= T ? r - T : r;
+            decode_row<TEAM, NCH>(rc[u], const_cast<uint16_t*>(r >= T ? ref.v : ref.k) + j * p.row_stride, lin,
+                                  r < 2 * T);
+          }
         }
       }
     }
@@ -305,10 +326,8 @@ __global__ void slots_commit_kernel(const int32_t* count, int32_t max_entries, i
 
 // Row lengths head_num_local * 128 for 1..16 local heads (powers of two).
 bool pick_nch(int32_t row_len, int& nch) {
-  if (row_len == 128) { nch = 0; return true; }  // half-warp rows
-  if (row_len % 256) return false;
-  nch = row_len / 256;
-  return nch == 1 || nch == 2 || nch == 4 || nch == 8;
+  nch = row_len;
+  return row_len == 128 || row_len == 256 || row_len == 512 || row_len == 1024 || row_len == 2048;
 }
 
 ashkv_status_t validate(const PagesParams& p) {
@@ -335,11 +354,11 @@ using namespace ashkv;
 
 #define ASHKV_PAGES_DISPATCH(KERNEL, NAME)                                                  \
   switch (nch) {                                                                           \
-    case 0: KERNEL<1, true><<<grid_for(p.max_entries), kThreads, 0, st>>>(p); break;       \
-    case 1: KERNEL<1, false><<<grid_for(p.max_entries), kThreads, 0, st>>>(p); break;      \
-    case 2: KERNEL<2, false><<<grid_for(p.max_entries), kThreads, 0, st>>>(p); break;      \
-    case 4: KERNEL<4, false><<<grid_for(p.max_entries), kThreads, 0, st>>>(p); break;      \
-    default: KERNEL<8, false><<<grid_for(p.max_entries), kThreads, 0, st>>>(p); break;     \
+    case 128: KERNEL<4, 4><<<grid_for(p.max_entries), kThreads, 0, st>>>(p); break;        \
+    case 256: KERNEL<8, 4><<<grid_for(p.max_entries), kThreads, 0, st>>>(p); break;        \
+    case 512: KERNEL<16, 4><<<grid_for(p.max_entries), kThreads, 0, st>>>(p); break;       \
+    case 1024: KERNEL<32, 4><<<grid_for(p.max_entries), kThreads, 0, st>>>(p); break;      \
+    default: KERNEL<32, 8><<<grid_for(p.max_entries), kThreads, 0, st>>>(p); break;        \
   }                                                                                        \
   return check_launch(NAME);
 

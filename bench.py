@@ -318,17 +318,19 @@ def run_reference(args) -> None:
 DEMOTE_LAYERS, DEMOTE_HEADS, DEMOTE_TOKENS, DEMOTE_T = 64, 8, 32 * 8192, 16
 
 
-def run_demote(dev, world: int, rank: int, dist, steps: int, warmup: int, layers: int = DEMOTE_LAYERS) -> dict:
+def run_demote(dev, world: int, rank: int, dist, steps: int, warmup: int, layers: int = DEMOTE_LAYERS,
+               head_split: int = 0) -> dict:
     """64-layer model, 8 KV heads x 128, 32 seq x 8192 tokens in 16-token
     pages, features U[0,1], default policy, pressure 0.9.  KV heads are sharded over the
     ranks (TP); the page table is replicated; the only collective is the MAX all-reduce of
-    the allocator pressure before each plan.  One step = policy kernel (score -> tier ->
+    the allocator pressure before each plan.  ``head_split`` > 0 runs one rank's share of
+    that split (8 / head_split heads) on this GPU alone.  One step = policy kernel (score -> tier ->
     lists) + gather/INT8-encode of every page on the demotion list into arena slots
     (demote) + decode of those pages back into the KV pool (promote)."""
     from ashkv.contracts import ASHKVConfig
     from ashkv.runtime.batch import BatchMigrator, DevicePageTable, KVLayers, SlotArena, int8_page_slot_bytes
 
-    heads = DEMOTE_HEADS // world
+    heads = DEMOTE_HEADS // (head_split or world)
     pages_per_layer = DEMOTE_TOKENS // DEMOTE_T
     n = layers * pages_per_layer
     g = torch.Generator(device=dev).manual_seed(4000 + rank)
@@ -365,13 +367,15 @@ def run_demote(dev, world: int, rank: int, dist, steps: int, warmup: int, layers
         if ev is not None:
             ev[1].record(stream)
         mig.decode(L.demote, L.counts[0:1], free_slots=True)
+        if ev is not None:
+            ev[2].record(stream)
 
     for _ in range(warmup):
         step()
     torch.cuda.synchronize()
     if dist:
         dist.barrier()
-    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(steps)]
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(steps)]
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     start.record(stream)
     for i in range(steps):
@@ -380,10 +384,11 @@ def run_demote(dev, world: int, rank: int, dist, steps: int, warmup: int, layers
     torch.cuda.synchronize()
     ms = start.elapsed_time(stop) / steps
     enc_ms = statistics.mean(e[0].elapsed_time(e[1]) for e in evs)
-    t = torch.tensor([ms, enc_ms], dtype=torch.float64, device=dev)
+    dec_ms = statistics.mean(e[1].elapsed_time(e[2]) for e in evs)
+    t = torch.tensor([ms, enc_ms, dec_ms], dtype=torch.float64, device=dev)
     if dist:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms, enc_ms = float(t[0]), float(t[1])
+    ms, enc_ms, dec_ms = float(t[0]), float(t[1]), float(t[2])
     page_bytes = DEMOTE_T * kv.row_len * 2 * 2  # K + V bf16 of one page on this rank
     enc_alg = n_demote * (page_bytes + page_bytes // 2 + 4 * DEMOTE_T)
     ok = int(mig.status_encode[:n_demote].ne(0).sum().item()) == 0
@@ -394,8 +399,9 @@ def run_demote(dev, world: int, rank: int, dist, steps: int, warmup: int, layers
             "pages": n, "demoted_pages": n_demote, "heads_per_rank": heads,
             "demote_pages_per_s": round(n_demote / (enc_ms / 1e3), 1),
             "step_pages_per_s": round(n_demote / (ms / 1e3), 1),
-            "ms_per_step": round(ms, 4), "encode_ms": round(enc_ms, 4),
+            "ms_per_step": round(ms, 4), "encode_ms": round(enc_ms, 4), "decode_ms": round(dec_ms, 4),
             "encode_hbm_gbs": round(enc_alg / (enc_ms / 1e3) / 1e9, 1),
+            "decode_hbm_gbs": round(enc_alg / (dec_ms / 1e3) / 1e9, 1),
             "scaling": "strong (fixed model, heads split over ranks)", "all_slots_ok": ok,
             "step": "pressure all-reduce (N>1) + policy kernel + gather/INT8 encode of demoted pages + decode back",
             "gpu_launches_per_step": 5}
@@ -419,6 +425,8 @@ def main() -> None:
     ap.add_argument("--demote-steps", type=int, default=10)
     ap.add_argument("--demote-layers", type=int, default=DEMOTE_LAYERS,
                     help="layers of the config-4 model (64; fewer only for small profiling cases)")
+    ap.add_argument("--demote-head-split", type=int, default=0,
+                    help="run one rank's share of an N-way KV-head split on this GPU (profiling cases)")
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)
@@ -593,7 +601,8 @@ def main() -> None:
 
     demote = None
     if not args.no_demote:
-        demote = run_demote(dev, world, rank, dist, args.demote_steps, 3, args.demote_layers)
+        demote = run_demote(dev, world, rank, dist, args.demote_steps, 3, args.demote_layers,
+                            args.demote_head_split)
 
     if rank == 0:
         cpu = None
