@@ -235,6 +235,19 @@ __device__ __forceinline__ f2 div2_rn(f2 a, f2 yhi, f2 ylo, f2 nb) {
   return fma2(r, yhi, q0);
 }
 
+// The first step alone is already RN(a/b) when b's significand has at most 11
+// bits and a's at most 19 (products of bf16/fp16 values and small integers).
+// Write a = S*2^s, b = A*2^t with S, A odd integers, S < 2^19, A < 2^11.  A
+// rounding boundary of the binade [2^E, 2^(E+1)) is (2m+1)*2^(E-24), and
+// S*2^(s-t) - A*(2m+1)*2^(E-24) is a nonzero multiple of 2^(E-24) (it could only
+// vanish with S >= 2^24), so a/b lies more than 2^-36*|a/b| from every
+// boundary, while a*y_hi + RN(a*y_lo) differs from a/b by less than 2^-46*|a/b|
+// (y_hi + y_lo errs by < 2^-47/|b|).  Holds while a*y_lo is a normal number,
+// i.e. for |a/b| >= 2^-100.
+__device__ __forceinline__ bool short_significand(float b) { return (__float_as_uint(b) & 0x1FFFu) == 0u; }
+__device__ __forceinline__ float div_short(float a, Recip y) { return __fmaf_rn(a, y.hi, __fmul_rn(a, y.lo)); }
+__device__ __forceinline__ f2 div2_short(f2 a, f2 yhi, f2 ylo) { return fma2(a, yhi, mul2(a, ylo)); }
+
 
 // ---------------------------------------------------------------- INT8 codec arithmetic
 // Shared by the row kernels (int8_codec.cu) and the page kernels (pages.cu);
@@ -243,17 +256,21 @@ __device__ __forceinline__ f2 div2_rn(f2 a, f2 yhi, f2 ylo, f2 nb) {
 // (the reference adds +0.5 when q > 0 and -0.5 otherwise; the two differ only
 // at q = +0, where both truncate to 0).  s / am uses the per-row reciprocal
 // pair and Markstein's correction when `fast` (am within [2^-100, 2^100] and
-// s finite for every element of the row), __fdiv_rn otherwise.
+// s finite for every element of the row), __fdiv_rn otherwise.  When am is an
+// input value (a bf16/fp16 absmax, not the 1e-8 floor) its significand has at
+// most 11 bits and s at most 18, so the correction step is skipped (`shortq`):
+// quotients below 2^-100 in magnitude give code 0 whatever their rounding.
 struct Int8Div {
   float am;
   Recip y;
-  bool fast;
+  bool fast, shortq;
 };
 __device__ __forceinline__ Int8Div int8_div(float am, bool s_finite) {
   Int8Div d;
   d.am = am;
   d.y = make_recip(am);
   d.fast = s_finite && recip_ok(am);
+  d.shortq = d.fast && short_significand(am);
   return d;
 }
 __device__ __forceinline__ int32_t int8_round_sat(float q) {
@@ -263,7 +280,7 @@ __device__ __forceinline__ int32_t int8_round_sat(float q) {
   return c;
 }
 __device__ __forceinline__ int32_t int8_code(float s, const Int8Div& d) {
-  return int8_round_sat(d.fast ? div_rn(s, d.am, d.y) : __fdiv_rn(s, d.am));
+  return int8_round_sat(d.shortq ? div_short(s, d.y) : d.fast ? div_rn(s, d.am, d.y) : __fdiv_rn(s, d.am));
 }
 // Four bf16 inputs (two words, element 0 in the low half of w0) -> four
 // codes packed little-endian: s = bf16(x * 127) (exact product, one rounding).
@@ -273,7 +290,11 @@ __device__ __forceinline__ uint32_t int8_codes4_bf16(uint32_t w0, uint32_t w1, c
   const uint32_t s23 = f32x2_to_bf16x2_pk(mul2(pk2(bf16lo(w1), bf16hi(w1)), k127));
   const f2 Q0 = pk2(bf16lo(s01), bf16hi(s01)), Q1 = pk2(bf16lo(s23), bf16hi(s23));
   float q[4];
-  if (d.fast) {
+  if (d.shortq) {
+    const f2 yhi = pk2(d.y.hi, d.y.hi), ylo = pk2(d.y.lo, d.y.lo);
+    upk2(div2_short(Q0, yhi, ylo), q[0], q[1]);
+    upk2(div2_short(Q1, yhi, ylo), q[2], q[3]);
+  } else if (d.fast) {
     const f2 yhi = pk2(d.y.hi, d.y.hi), ylo = pk2(d.y.lo, d.y.lo), nb = pk2(-d.am, -d.am);
     upk2(div2_rn(Q0, yhi, ylo, nb), q[0], q[1]);
     upk2(div2_rn(Q1, yhi, ylo, nb), q[2], q[3]);
@@ -289,12 +310,13 @@ __device__ __forceinline__ uint32_t int8_codes4_bf16(uint32_t w0, uint32_t w1, c
   return __byte_perm(__byte_perm(c0, c1, 0x0040), __byte_perm(c2, c3, 0x0040), 0x5410);
 }
 // Decode: v = RN(RN(float(code) * scale) / 127).  `fast` when the scale is
-// finite and in [2^-90, 2^90] (products are 0 or inside Markstein's range;
-// scale > 0 keeps the sign of zero products).
+// finite and in [2^-90, 2^90] (products are 0 or at least 2^-90, and code *
+// scale is exact with at most 8 + 11 significant bits, so div_short applies to
+// the division by 127; scale > 0 keeps the sign of zero products).
 __device__ __forceinline__ bool int8_dec_fast(float scale) { return scale >= 0x1p-90f && scale <= 0x1p+90f; }
 __device__ __forceinline__ float int8_dequant(int32_t c, float scale, bool fast) {
   const float p = __fmul_rn(float(c), scale);
-  return fast ? div_rn(p, 127.0f, make_recip(127.0f)) : __fdiv_rn(p, 127.0f);
+  return fast ? div_short(p, make_recip(127.0f)) : __fdiv_rn(p, 127.0f);
 }
 // Four int8 codes (one word, code 0 in the low byte) -> float(code) exactly,
 // without an int->float conversion: 0x4B400000 | (byte ^ 0x80) is the float

@@ -13,10 +13,12 @@
 // same CPU NaN encoding.
 //
 // Divisions are correctly rounded: the per-group reciprocal pair plus
-// Markstein's correction (common.cuh) where its range conditions hold,
-// __fdiv_rn elsewhere.  Groups whose G is a power of two in [8, 256] take the
-// fast kernels (G/8 threads per group, 16-byte loads); any other G takes a
-// warp-per-group kernel.
+// Markstein's correction (common.cuh) where its range conditions hold, the
+// reciprocal pair alone where dividend and divisor have short significands
+// (div2_short: 7x by a bf16 absmax, q*s by 7), __fdiv_rn elsewhere.
+// Groups whose G is a power of two in [8, 256] take the fast kernels (G/32
+// threads per group with 32 values each, or G/8 threads for G = 8, 16; 16-byte
+// loads); any other G takes a warp-per-group kernel.
 #include "common.cuh"
 
 namespace ashkv {
@@ -80,37 +82,38 @@ __device__ __forceinline__ uint4 load_chunk(const uint16_t* __restrict__ src, in
   return make_uint4(w[0], w[1], w[2], w[3]);
 }
 
-// Called by every lane of the warp (the group maximum is a shuffle reduction).
-template <int TPG>
-__device__ __forceinline__ void encode_chunk(uint4 v, int64_t c, bool active, uint16_t* __restrict__ scales,
-                                             uint32_t* __restrict__ packed) {
+__device__ __forceinline__ void unpack_chunk(uint4 v, float (&x)[8]) {
   const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-  float x[8];
 #pragma unroll
   for (int k = 0; k < 4; ++k) { x[2 * k] = bf16lo(w[k]); x[2 * k + 1] = bf16hi(w[k]); }
-  float m = max3_abs_nan(x[0], x[1], x[2]);
-  m = max3_abs_nan(m, x[3], x[4]);
-  m = max3_abs_nan(m, x[5], x[6]);
-  m = max3_abs_nan(m, x[7], x[7]);
-#pragma unroll
-  for (int off = 1; off < TPG; off <<= 1) m = max_nan(m, __shfl_xor_sync(0xFFFFFFFFu, m, off));
-  const float am = group_max_finish(m);
-  if (!active) return;
-  if ((c % TPG) == 0) scales[c / TPG] = static_cast<uint16_t>(bf16_cpu(am));
+}
+
+__device__ __forceinline__ float chunk_max(float m, const float (&x)[8]) {
+  m = max3_abs_nan(m, x[0], x[1]);
+  m = max3_abs_nan(m, x[2], x[3]);
+  m = max3_abs_nan(m, x[4], x[5]);
+  return max3_abs_nan(m, x[6], x[7]);
+}
+
+// Eight values of a group with divisor d -> eight nibbles (element 0 in the
+// high nibble of the low byte).
+__device__ __forceinline__ uint32_t pack_chunk(const float (&x)[8], const GroupDiv& d) {
   uint32_t out = 0;
-  const GroupDiv d = group_div(am);
   if (d.mode == 0) {
     // am finite and in Markstein's range: every x is finite and |x| <= am, so
     // v = RN(RN(7x)/am) lies in [-7, 7] and numpy's cast and clip are the
     // identity; RN(v + 1.5*2^23 + 8) leaves rint(v) + 8 (ties to even, 8 being
-    // even) in the low 4 bits.
-    const f2 yhi = pk2(d.y.hi, d.y.hi), ylo = pk2(d.y.lo, d.y.lo), nb = pk2(-am, -am);
+    // even) in the low 4 bits.  When am is a bf16 absmax (not the 1e-8 floor)
+    // the quotient of the 11-bit product 7x by it needs no correction step.
+    const f2 yhi = pk2(d.y.hi, d.y.hi), ylo = pk2(d.y.lo, d.y.lo), nb = pk2(-d.am, -d.am);
     const f2 seven = pk2(7.0f, 7.0f), magic = pk2(12582920.0f, 12582920.0f);
+    const bool shortq = short_significand(d.am);
     uint32_t t[8];
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
+      const f2 p = mul2(pk2(x[2 * k], x[2 * k + 1]), seven);
       float v0, v1;
-      upk2(add2(div2_rn(mul2(pk2(x[2 * k], x[2 * k + 1]), seven), yhi, ylo, nb), magic), v0, v1);
+      upk2(add2(shortq ? div2_short(p, yhi, ylo) : div2_rn(p, yhi, ylo, nb), magic), v0, v1);
       t[2 * k] = __float_as_uint(v0);
       t[2 * k + 1] = __float_as_uint(v1);
     }
@@ -124,13 +127,28 @@ __device__ __forceinline__ void encode_chunk(uint4 v, int64_t c, bool active, ui
     for (int k = 0; k < 4; ++k)
       out |= ((nibble_of(x[2 * k], d) << 4) | nibble_of(x[2 * k + 1], d)) << (8 * k);
   }
-  packed[c] = out;
+  return out;
+}
+
+// Called by every lane of the warp (the group maximum is a shuffle reduction).
+template <int TPG>
+__device__ __forceinline__ void encode_chunk(uint4 v, int64_t c, bool active, uint16_t* __restrict__ scales,
+                                             uint32_t* __restrict__ packed) {
+  float x[8];
+  unpack_chunk(v, x);
+  float m = chunk_max(0.0f, x);
+#pragma unroll
+  for (int off = 1; off < TPG; off <<= 1) m = max_nan(m, __shfl_xor_sync(0xFFFFFFFFu, m, off));
+  const float am = group_max_finish(m);
+  if (!active) return;
+  if ((c % TPG) == 0) scales[c / TPG] = static_cast<uint16_t>(bf16_cpu(am));
+  packed[c] = pack_chunk(x, group_div(am));
 }
 
 // Two chunks per lane per iteration (c and c + stride), both loaded before
 // either is encoded.  The loop runs per warp (c0 = the warp's first chunk) so
 // that every lane takes part in the shuffles; n_chunks is a multiple of TPG,
-// so the lanes of one group are all active or all idle.
+// so the lanes of one group are all active or all idle.  Used for G = 8, 16.
 template <int TPG>
 __global__ void __launch_bounds__(256) int4_encode_fast(const uint16_t* __restrict__ src, int64_t n,
                                                         int64_t n_chunks, uint16_t* __restrict__ scales,
@@ -144,6 +162,43 @@ __global__ void __launch_bounds__(256) int4_encode_fast(const uint16_t* __restri
     const uint4 vb = load_chunk(src, n, cb, act_b);
     encode_chunk<TPG>(va, ca, act_a, scales, packed);
     encode_chunk<TPG>(vb, cb, act_b, scales, packed);
+  }
+}
+
+// G = 32 * TEAM (32..256): TEAM lanes per group, 4 chunks of 8 values per lane
+// (chunk k * TEAM + lane-in-team of the group, so each load and store of a warp
+// is contiguous), so the group's shuffles, divisor and scale are spread over 32
+// values per lane.  Warps walk tiles of 32 / TEAM groups.
+template <int TEAM>
+__global__ void __launch_bounds__(256) int4_encode_team(const uint16_t* __restrict__ src, int64_t n,
+                                                        int64_t n_groups, uint16_t* __restrict__ scales,
+                                                        uint32_t* __restrict__ packed) {
+  constexpr int GPW = 32 / TEAM;
+  const int lane = threadIdx.x & 31, lin = lane % TEAM;
+  const int64_t warps = int64_t(gridDim.x) * (blockDim.x / 32);
+  for (int64_t g0 = (int64_t(blockIdx.x) * (blockDim.x / 32) + (threadIdx.x >> 5)) * GPW; g0 < n_groups;
+       g0 += warps * GPW) {
+    const int64_t g = g0 + lane / TEAM;
+    const bool active = g < n_groups;
+    const int64_t c0 = g * (4 * TEAM) + lin;
+    uint4 v[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) v[k] = load_chunk(src, n, c0 + k * TEAM, active);
+    float x[4][8];
+    float m = 0.0f;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      unpack_chunk(v[k], x[k]);
+      m = chunk_max(m, x[k]);
+    }
+#pragma unroll
+    for (int off = 1; off < TEAM; off <<= 1) m = max_nan(m, __shfl_xor_sync(0xFFFFFFFFu, m, off));
+    const float am = group_max_finish(m);
+    if (!active) continue;
+    if (lin == 0) scales[g] = static_cast<uint16_t>(bf16_cpu(am));
+    const GroupDiv d = group_div(am);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) packed[c0 + k * TEAM] = pack_chunk(x[k], d);
   }
 }
 
@@ -188,7 +243,8 @@ __global__ void int4_encode_generic(const uint16_t* __restrict__ src, int64_t n,
 
 // ---------------------------------------------------------------- decode
 // out = bf16(RN(q * s) / 7).  Fast when s is finite and in [2^-90, 2^90]
-// (then q*s is 0 or within Markstein's range; s > 0 keeps the sign of 0).
+// (then q*s is 0 or at least 2^-90, and exact with at most 12 significant bits,
+// so the division by 7 takes div2_short; s > 0 keeps the sign of 0).
 
 template <int EPT>
 __global__ void __launch_bounds__(256) int4_decode_fast(const uint16_t* __restrict__ scales,
@@ -196,7 +252,7 @@ __global__ void __launch_bounds__(256) int4_decode_fast(const uint16_t* __restri
                                                         int32_t chunks_per_group, uint16_t* __restrict__ dst) {
   const int64_t stride = int64_t(gridDim.x) * blockDim.x;
   const Recip y7 = make_recip(7.0f);
-  const f2 yhi = pk2(y7.hi, y7.hi), ylo = pk2(y7.lo, y7.lo), nb = pk2(-7.0f, -7.0f);
+  const f2 yhi = pk2(y7.hi, y7.hi), ylo = pk2(y7.lo, y7.lo), bias = pk2(-8388616.0f, -8388616.0f);
   for (int64_t c = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; c < n_chunks; c += stride) {
     const float s = bf16_to_f32(scales[c / chunks_per_group]);
     const bool fast = s >= 0x1p-90f && s <= 0x1p+90f;
@@ -213,9 +269,12 @@ __global__ void __launch_bounds__(256) int4_decode_fast(const uint16_t* __restri
 #pragma unroll
       for (int b = 0; b < EPT / 2; ++b) {
         const uint32_t byte = (code[b / 4] >> (8 * (b % 4))) & 0xFFu;
-        const float qh = float(int(byte >> 4) - 8), ql = float(int(byte & 15u) - 8);
+        // q - 8 = (2^23 + q) - (2^23 + 8) exactly; q * s has at most 4 + 8 bits,
+        // so the division by 7 needs no correction step (div2_short)
+        const f2 q = add2(pk2(__uint_as_float(0x4B000000u | (byte >> 4)), __uint_as_float(0x4B000000u | (byte & 15u))),
+                          bias);
         float v0, v1;
-        upk2(div2_rn(mul2(pk2(qh, ql), ss), yhi, ylo, nb), v0, v1);
+        upk2(div2_short(mul2(q, ss), yhi, ylo), v0, v1);
         o[b] = f32x2_to_bf16x2(v0, v1);
       }
     } else {
@@ -283,15 +342,15 @@ extern "C" ashkv_status_t ashkv_int4_encode(const void* src_bf16, int64_t n, int
   auto* sc = static_cast<uint16_t*>(scales_bf16);
   if (fast_group(group_size) && aligned(src, 16) && aligned(packed, 4) && n_groups * group_size < (int64_t(1) << 40)) {
     const int64_t n_chunks = n_groups * (group_size / 8);
-    const unsigned grid = grid_for(n_chunks, 256);
     auto* pk = static_cast<uint32_t*>(packed);
+    const unsigned grid = grid_for(group_size >= 32 ? n_groups * (group_size / 32) : n_chunks, 256);
     switch (group_size / 8) {
       case 1: int4_encode_fast<1><<<grid, 256, 0, s>>>(src, n, n_chunks, sc, pk); break;
       case 2: int4_encode_fast<2><<<grid, 256, 0, s>>>(src, n, n_chunks, sc, pk); break;
-      case 4: int4_encode_fast<4><<<grid, 256, 0, s>>>(src, n, n_chunks, sc, pk); break;
-      case 8: int4_encode_fast<8><<<grid, 256, 0, s>>>(src, n, n_chunks, sc, pk); break;
-      case 16: int4_encode_fast<16><<<grid, 256, 0, s>>>(src, n, n_chunks, sc, pk); break;
-      default: int4_encode_fast<32><<<grid, 256, 0, s>>>(src, n, n_chunks, sc, pk); break;
+      case 4: int4_encode_team<1><<<grid, 256, 0, s>>>(src, n, n_groups, sc, pk); break;
+      case 8: int4_encode_team<2><<<grid, 256, 0, s>>>(src, n, n_groups, sc, pk); break;
+      case 16: int4_encode_team<4><<<grid, 256, 0, s>>>(src, n, n_groups, sc, pk); break;
+      default: int4_encode_team<8><<<grid, 256, 0, s>>>(src, n, n_groups, sc, pk); break;
     }
   } else {
     int4_encode_generic<<<grid_for(n_groups * 32, 256), 256, 0, s>>>(src, n, group_size, n_groups, sc,

@@ -4,8 +4,8 @@
 // (ashkv/codecs/int8.py:50-81 encode, :98-116 decode) as a single-pass CUDA
 // kernel: a "team" of threads owns one row, keeps the row in registers
 // between the absmax reduction and the quantisation, and issues 16-byte
-// loads/stores.  The team size is min(32, row_len / 8) so short rows
-// (INT8Codec, 128 elements) pack several rows per warp and long rows (the
+// loads/stores.  Short rows (INT8Codec, 128 elements) take row_len / 32
+// threads with 32 elements each, packing several rows per warp; long rows (the
 // SGLang hooks, head_num * head_dim elements) spread over a full warp.
 #include "common.cuh"
 
@@ -230,7 +230,7 @@ __global__ void __launch_bounds__(256) int8_decode_kernel(const Int8DecParams p)
   const bool f16 = p.dst_fp16 != 0;
   const bool fast = int8_dec_fast(scale);
   const Recip y = make_recip(127.0f);
-  const f2 S = pk2(scale, scale), YHI = pk2(y.hi, y.hi), YLO = pk2(y.lo, y.lo), N127 = pk2(-127.0f, -127.0f);
+  const f2 S = pk2(scale, scale), YHI = pk2(y.hi, y.hi), YLO = pk2(y.lo, y.lo);
 #pragma unroll
   for (int c = 0; c < NCH; ++c) {
     const int64_t e0 = (int64_t(c) * TEAM + lane_in_team) * 8;
@@ -245,7 +245,7 @@ __global__ void __launch_bounds__(256) int8_decode_kernel(const Int8DecParams p)
       for (int k = 0; k < 2; ++k) {
         float a, b;
         if (fast) {
-          upk2(div2_rn(mul2(F[k], S), YHI, YLO, N127), a, b);
+          upk2(div2_short(mul2(F[k], S), YHI, YLO), a, b);
         } else {
           upk2(F[k], a, b);
           a = __fdiv_rn(__fmul_rn(a, scale), 127.0f);
@@ -281,10 +281,19 @@ int32_t pow2_shift(int32_t v) {
   return k;
 }
 
+// Threads per row and 8-element chunks per thread.  Rows of 32..1016 elements
+// whose chunk count is 4 x a power of two take 4 chunks per thread (team =
+// chunks / 4), so the per-row work -- the shuffle reduction, the divisor, the
+// scale -- is spread over 32 elements per thread; longer rows take a full warp.
 template <typename P, typename KFast>
 bool pick_team(int32_t row_len, int& team, int& nch) {
   if (row_len % 8 != 0) return false;
   const int chunks = row_len / 8;
+  if (chunks >= 4 && chunks < 128 && chunks % 4 == 0 && !((chunks / 4) & (chunks / 4 - 1))) {
+    team = chunks / 4;
+    nch = 4;
+    return true;
+  }
   team = chunks >= 32 ? 32 : chunks;
   if (team & (team - 1)) return false;  // team must be a power of two
   if (chunks % team) return false;
@@ -306,7 +315,9 @@ static ashkv_status_t launch_encode(const Int8EncParams& p, int team, int nch, b
   if (fast) {
     ASHKV_ENC_CASE(FP16, 1, 1) ASHKV_ENC_CASE(FP16, 1, 2) ASHKV_ENC_CASE(FP16, 1, 4)
     ASHKV_ENC_CASE(FP16, 1, 8) ASHKV_ENC_CASE(FP16, 1, 16) ASHKV_ENC_CASE(FP16, 1, 32)
-    ASHKV_ENC_CASE(FP16, 2, 32) ASHKV_ENC_CASE(FP16, 4, 32) ASHKV_ENC_CASE(FP16, 8, 32)
+    ASHKV_ENC_CASE(FP16, 2, 1) ASHKV_ENC_CASE(FP16, 2, 32) ASHKV_ENC_CASE(FP16, 4, 1)
+    ASHKV_ENC_CASE(FP16, 4, 2) ASHKV_ENC_CASE(FP16, 4, 4) ASHKV_ENC_CASE(FP16, 4, 8)
+    ASHKV_ENC_CASE(FP16, 4, 16) ASHKV_ENC_CASE(FP16, 4, 32) ASHKV_ENC_CASE(FP16, 8, 32)
     ASHKV_ENC_CASE(FP16, 16, 32)
   }
   int8_encode_generic_kernel<FP16><<<unsigned((p.n_rows + 7) / 8), 256, 0, st>>>(p);
@@ -386,8 +397,9 @@ extern "C" ashkv_status_t ashkv_int8_decode_rows(
   cudaStream_t st = as_stream(stream);
   if (fast) {
     ASHKV_DEC_CASE(1, 1) ASHKV_DEC_CASE(1, 2) ASHKV_DEC_CASE(1, 4) ASHKV_DEC_CASE(1, 8)
-    ASHKV_DEC_CASE(1, 16) ASHKV_DEC_CASE(1, 32) ASHKV_DEC_CASE(2, 32) ASHKV_DEC_CASE(4, 32)
-    ASHKV_DEC_CASE(8, 32) ASHKV_DEC_CASE(16, 32)
+    ASHKV_DEC_CASE(1, 16) ASHKV_DEC_CASE(1, 32) ASHKV_DEC_CASE(2, 1) ASHKV_DEC_CASE(2, 32)
+    ASHKV_DEC_CASE(4, 1) ASHKV_DEC_CASE(4, 2) ASHKV_DEC_CASE(4, 4) ASHKV_DEC_CASE(4, 8) ASHKV_DEC_CASE(4, 16)
+    ASHKV_DEC_CASE(4, 32) ASHKV_DEC_CASE(8, 32) ASHKV_DEC_CASE(16, 32)
   }
   int8_decode_generic_kernel<<<unsigned((n_rows + 7) / 8), 256, 0, st>>>(p);
   return check_launch("int8_decode_generic");

@@ -126,7 +126,7 @@ __device__ __forceinline__ void decode_row(const RowCodes<NCH>& rc, uint16_t* ds
   const float scale = rc.scale;
   const bool fast = int8_dec_fast(scale);
   const Recip y = make_recip(127.0f);
-  const f2 S = pk2(scale, scale), YHI = pk2(y.hi, y.hi), YLO = pk2(y.lo, y.lo), N127 = pk2(-127.0f, -127.0f);
+  const f2 S = pk2(scale, scale), YHI = pk2(y.hi, y.hi), YLO = pk2(y.lo, y.lo);
 #pragma unroll
   for (int c = 0; c < NCH; ++c) {
     const int e0 = (c * TEAM + lin) * 8;
@@ -137,8 +137,8 @@ __device__ __forceinline__ void decode_row(const RowCodes<NCH>& rc, uint16_t* ds
       f2 F0, F1;  // float(code) of bytes 0,1 and 2,3 of ww[h]
       int8x4_to_f2(ww[h], F0, F1);
       if (fast) {
-        o[2 * h] = f32x2_to_bf16x2_pk(div2_rn(mul2(F0, S), YHI, YLO, N127));
-        o[2 * h + 1] = f32x2_to_bf16x2_pk(div2_rn(mul2(F1, S), YHI, YLO, N127));
+        o[2 * h] = f32x2_to_bf16x2_pk(div2_short(mul2(F0, S), YHI, YLO));
+        o[2 * h + 1] = f32x2_to_bf16x2_pk(div2_short(mul2(F1, S), YHI, YLO));
       } else {
         float a, b;
         upk2(F0, a, b);

@@ -238,6 +238,9 @@ def codec_suite(K: torch.Tensor, V: torch.Tensor, peak: float, iters: int = 20) 
             fn_a(); fn_b()
         ev = [torch.cuda.Event(enable_timing=True) for _ in range(2 * iters + 1)]
         torch.cuda.synchronize()
+        # hold the stream while the launches are queued, so the events see back-to-back
+        # kernels rather than the host's call overhead between them
+        torch.cuda._sleep(40_000_000)
         ev[0].record(st)
         for i in range(iters):
             (fn_a if i % 2 == 0 else fn_b)()
@@ -256,9 +259,9 @@ def codec_suite(K: torch.Tensor, V: torch.Tensor, peak: float, iters: int = 20) 
     cV, sV = int8m.encode_rows(Vr)
     oK, oV = torch.empty_like(Kr), torch.empty_like(Vr)
     ms = timed(lambda: int8m.encode_rows(Kr, codes=cK, scales=sK), lambda: int8m.encode_rows(Vr, codes=cV, scales=sV))
-    out["int8_rows_L128_encode"] = entry("int8_encode_kernel<bf16,1,16>", 3 * E + 2 * (E // 128), ms)
+    out["int8_rows_L128_encode"] = entry("int8_encode_kernel<bf16,4,4>", 3 * E + 2 * (E // 128), ms)
     ms = timed(lambda: int8m.decode_rows(cK, sK, out=oK), lambda: int8m.decode_rows(cV, sV, out=oV))
-    out["int8_rows_L128_decode"] = entry("int8_decode_kernel<1,16>", 3 * E + 2 * (E // 128), ms)
+    out["int8_rows_L128_decode"] = entry("int8_decode_kernel<4,4>", 3 * E + 2 * (E // 128), ms)
     fK, fV = fp8m.encode_tensor(K), fp8m.encode_tensor(V)
     bK, bV = torch.empty_like(K), torch.empty_like(V)
     ms = timed(lambda: fp8m.encode_tensor(K, out=fK), lambda: fp8m.encode_tensor(V, out=fV))

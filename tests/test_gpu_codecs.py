@@ -41,7 +41,7 @@ def rand_bf16(n: int, seed: int, kind: str = "normal") -> torch.Tensor:
 
 # ------------------------------------------------------------------- INT8
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
-@pytest.mark.parametrize("row_len", [128, 1024, 4096, 8, 24, 136])
+@pytest.mark.parametrize("row_len", [128, 1024, 4096, 8, 16, 24, 32, 64, 136, 256, 512, 2048])
 @pytest.mark.parametrize("fp32_product", [False, True])
 def test_int8_rows_bitexact(cuda, dtype, row_len, fp32_product):
     n_rows = 300
@@ -58,6 +58,51 @@ def test_int8_rows_bitexact(cuda, dtype, row_len, fp32_product):
         _native.int8_decode_rows(codes, scales, dec)
         want = oracle.int8_decode(oc, osc, scale_fp16=dtype == torch.float16, dst_fp16=out_dtype == torch.float16)
         assert np.array_equal(bits_of(dec), want.reshape(-1))
+
+
+def rows_under_absmax(L: int, am_bits, fill_tiny: bool = False) -> np.ndarray:
+    """bf16 rows of length L: for each absmax pattern a, rows that start with a and
+    then walk every bf16 pattern of magnitude <= a, both signs, so every quotient
+    s / am an encoder can form for that absmax occurs."""
+    rows = []
+    for a in am_bits:
+        mags = np.arange(0, int(a) + 1, dtype=np.uint32)
+        vals = np.concatenate([mags, mags | 0x8000]).astype(np.uint16)
+        pad = (-len(vals)) % (L - 1)
+        vals = np.concatenate([vals, np.zeros(pad, np.uint16)]).reshape(-1, L - 1)
+        rows.append(np.concatenate([np.full((len(vals), 1), a, np.uint16), vals], axis=1))
+    return np.concatenate(rows)
+
+
+@pytest.mark.parametrize("L", [128, 1024])
+def test_int8_rows_every_quotient_of_a_binade(cuda, L):
+    """Every bf16 absmax in [1, 2) (the quotient's rounding is invariant under
+    power-of-two scaling of both operands) against every bf16 value below it, plus
+    zero rows, rows under the 1e-8 floor and rows at the extremes of the range."""
+    am = list(range(0x3F80, 0x4000)) + [0x0001, 0x0080, 0x2000, 0x3300, 0x7F7F]
+    bits = rows_under_absmax(L, am)
+    extra = np.zeros((4, L), np.uint16)
+    extra[1, :] = 0x3100        # 1.86e-9: every row value under the 1e-8 floor
+    extra[2, ::3] = 0x8001      # negative subnormals
+    extra[3, :] = 0x7F80        # +inf
+    bits = np.concatenate([bits, extra])
+    x = torch.from_numpy(bits.view(np.int16)).view(torch.bfloat16).to(cuda)
+    for sdt in (torch.bfloat16, torch.float16):
+        codes, scales = int8_mod.encode_rows(x, scale_dtype=sdt)
+        oc, osc = oracle.int8_encode(bits, L, scale_fp16=sdt == torch.float16)
+        assert np.array_equal(codes.cpu().numpy(), oc)
+        assert np.array_equal(bits_of(scales), osc)
+
+
+@pytest.mark.parametrize("sdt", [torch.bfloat16, torch.float16])
+def test_int8_decode_every_code_and_scale(cuda, sdt):
+    """All 256 codes under every 16-bit scale pattern (subnormal, huge, inf, NaN, negative)."""
+    codes = np.tile(np.arange(-128, 128, dtype=np.int8), (65536, 1))
+    sc = np.arange(65536, dtype=np.uint16)
+    out = int8_mod.decode_rows(torch.from_numpy(codes).to(cuda),
+                               torch.from_numpy(sc.view(np.int16)).view(sdt).to(cuda))
+    want = oracle.int8_decode(codes, sc, scale_fp16=sdt == torch.float16)
+    assert np.array_equal(bits_of(out), want.reshape(-1))
 
 
 @pytest.mark.parametrize("ci", range(int(INT8["int8_n_cases"])))

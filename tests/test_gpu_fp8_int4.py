@@ -143,6 +143,33 @@ def test_int4_group_sizes_vs_oracle(cuda, gs):
     np.testing.assert_array_equal(bits_of(out), oracle.int4_decode(sc_o, pk_o, gs))
 
 
+@pytest.mark.parametrize("gs", [16, 32, 64, 256])
+def test_int4_every_quotient_of_a_binade(cuda, gs):
+    """Groups that start with each bf16 absmax in [1, 2) and walk every bf16 value of
+    magnitude <= it (both signs): every quotient 7x / am the encoder can form."""
+    groups = []
+    for a in range(0x3F80, 0x4000):
+        mags = np.arange(0, a + 1, dtype=np.uint32)
+        vals = np.concatenate([mags, mags | 0x8000]).astype(np.uint16)
+        vals = np.concatenate([vals, np.zeros((-len(vals)) % (gs - 1), np.uint16)]).reshape(-1, gs - 1)
+        groups.append(np.concatenate([np.full((len(vals), 1), a, np.uint16), vals], axis=1))
+    bits = np.concatenate(groups).reshape(-1)
+    if (bits.size // gs) % 2:
+        bits = np.concatenate([bits, np.zeros(gs, np.uint16)])
+    sc_o, pk_o, _ = oracle.int4_encode(bits, gs)
+    scales, packed, _ = int4_mod.encode_tensor(dev_bits(bits, cuda), gs)
+    np.testing.assert_array_equal(bits_of(scales), sc_o)
+    np.testing.assert_array_equal(packed.cpu().numpy(), pk_o)
+
+
+def test_int4_decode_every_nibble_and_scale(cuda):
+    """All 16 nibbles under every bf16 scale pattern."""
+    sc = np.arange(65536, dtype=np.uint16)
+    pk = np.tile(np.array([0x01, 0x23, 0x45, 0x67, 0x89, 0xAB, 0xCD, 0xEF], np.uint8), 65536)
+    out = int4_mod.decode_tensor(dev_bits(sc, cuda), torch.from_numpy(pk).to(cuda), 16)
+    np.testing.assert_array_equal(bits_of(out), oracle.int4_decode(sc, pk, 16))
+
+
 @pytest.mark.parametrize("gs", [64, 16])
 def test_int4_unaligned_buffers(cuda, gs):
     n = gs * 97
