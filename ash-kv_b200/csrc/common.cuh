@@ -31,6 +31,44 @@ void* tensor_map_encoder();
 // ---------------------------------------------------------------- bf16/fp16
 __device__ __forceinline__ float bf16lo(uint32_t w) { return __uint_as_float(w << 16); }
 __device__ __forceinline__ float bf16hi(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
+// Two bf16 products in one instruction, each the exact product rounded once to
+// bf16 (round to nearest even).
+__device__ __forceinline__ uint32_t bf16x2_mul(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+// Per-half unsigned maximum of two 16-bit pairs.
+__device__ __forceinline__ uint32_t max_u16x2(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("max.u16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+// Running max of |x| over bf16 pairs as 16-bit patterns: for non-NaN values the
+// order of |x| is the order of its bit pattern (sign cleared); NaN patterns lie
+// above 0x7F80 (infinity).
+__device__ __forceinline__ uint32_t absmax_bits_bf16x2(uint32_t m, uint32_t w) { return max_u16x2(m, w & 0x7FFF7FFFu); }
+
+// max |x| over the N words (2N bf16 values) a lane holds of a row, reduced over
+// the team of TEAM consecutive lanes, ignoring NaN (fmaxf semantics).  Called by
+// every lane of the warp; inactive lanes pass zeros.  A row holding a NaN (bit
+// maximum above 0x7F80) is redone with fmaxf.
+template <int TEAM, int N>
+__device__ __forceinline__ float team_absmax_bf16(const uint32_t (&w)[N]) {
+  uint32_t mb = 0;
+#pragma unroll
+  for (int k = 0; k < N; ++k) mb = absmax_bits_bf16x2(mb, w[k]);
+  uint32_t m = max(mb & 0xFFFFu, mb >> 16);
+#pragma unroll
+  for (int off = TEAM / 2; off > 0; off >>= 1) m = max(m, __shfl_xor_sync(0xFFFFFFFFu, m, off));
+  if (!__any_sync(0xFFFFFFFFu, m > 0x7F80u)) return __uint_as_float(m << 16);
+  float am = 0.0f;
+#pragma unroll
+  for (int k = 0; k < N; ++k) am = fmaxf(am, fmaxf(fabsf(bf16lo(w[k])), fabsf(bf16hi(w[k]))));
+#pragma unroll
+  for (int off = TEAM / 2; off > 0; off >>= 1) am = fmaxf(am, __shfl_xor_sync(0xFFFFFFFFu, am, off));
+  return am;
+}
 __device__ __forceinline__ float bf16_to_f32(uint16_t h) { return __uint_as_float(uint32_t(h) << 16); }
 
 // fp32 -> bf16, round to nearest even; NaN becomes 0x7FFF.
@@ -285,9 +323,8 @@ __device__ __forceinline__ int32_t int8_code(float s, const Int8Div& d) {
 // Four bf16 inputs (two words, element 0 in the low half of w0) -> four
 // codes packed little-endian: s = bf16(x * 127) (exact product, one rounding).
 __device__ __forceinline__ uint32_t int8_codes4_bf16(uint32_t w0, uint32_t w1, const Int8Div& d) {
-  const f2 k127 = pk2(127.0f, 127.0f);
-  const uint32_t s01 = f32x2_to_bf16x2_pk(mul2(pk2(bf16lo(w0), bf16hi(w0)), k127));
-  const uint32_t s23 = f32x2_to_bf16x2_pk(mul2(pk2(bf16lo(w1), bf16hi(w1)), k127));
+  const uint32_t s01 = bf16x2_mul(w0, 0x42FE42FEu);  // bf16 127.0 in both halves
+  const uint32_t s23 = bf16x2_mul(w1, 0x42FE42FEu);
   const f2 Q0 = pk2(bf16lo(s01), bf16hi(s01)), Q1 = pk2(bf16lo(s23), bf16hi(s23));
   float q[4];
   if (d.shortq) {

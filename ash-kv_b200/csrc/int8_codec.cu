@@ -108,20 +108,31 @@ template <bool FP16, int NCH, int TEAM>
 __device__ __forceinline__ void encode_loaded_row(const Int8EncParams& p, int64_t r, bool active, int lane_in_team,
                                                   LoadedRow<NCH>& L) {
   float am = 0.0f;
-  if (active) {
+  if constexpr (!FP16) {
+    uint32_t words[4 * NCH];
 #pragma unroll
     for (int c = 0; c < NCH; ++c) {
-      const uint32_t w[4] = {L.chunk[c].x, L.chunk[c].y, L.chunk[c].z, L.chunk[c].w};
+      const bool a = active;
+      words[4 * c] = a ? L.chunk[c].x : 0u; words[4 * c + 1] = a ? L.chunk[c].y : 0u;
+      words[4 * c + 2] = a ? L.chunk[c].z : 0u; words[4 * c + 3] = a ? L.chunk[c].w : 0u;
+    }
+    am = team_absmax_bf16<TEAM>(words);  // NaN ignored, like tl.maximum
+  } else {
+    if (active) {
 #pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        am = fmaxf(am, fabsf(in_lo<FP16>(w[k])));  // fmaxf ignores NaN, like tl.maximum
-        am = fmaxf(am, fabsf(in_hi<FP16>(w[k])));
+      for (int c = 0; c < NCH; ++c) {
+        const uint32_t w[4] = {L.chunk[c].x, L.chunk[c].y, L.chunk[c].z, L.chunk[c].w};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          am = fmaxf(am, fabsf(in_lo<FP16>(w[k])));  // fmaxf ignores NaN, like tl.maximum
+          am = fmaxf(am, fabsf(in_hi<FP16>(w[k])));
+        }
       }
     }
-  }
 #pragma unroll
-  for (int off = TEAM / 2; off > 0; off >>= 1)
-    am = fmaxf(am, __shfl_xor_sync(0xFFFFFFFFu, am, off, TEAM));
+    for (int off = TEAM / 2; off > 0; off >>= 1)
+      am = fmaxf(am, __shfl_xor_sync(0xFFFFFFFFu, am, off, TEAM));
+  }
   if (!active) return;
   am = fmaxf(am, 1e-8f);
 

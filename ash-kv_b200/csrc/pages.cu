@@ -83,16 +83,13 @@ __device__ __forceinline__ void load_row_in(const uint16_t* src, int lin, bool o
 // warp (the row maximum is a shuffle reduction within the team).
 template <int TEAM, int NCH>
 __device__ __forceinline__ void encode_row(const RowIn<NCH>& ri, int8_t* codes, uint16_t* scale, int lin, bool on) {
-  float am = 0.0f;
+  uint32_t words[4 * NCH];
 #pragma unroll
   for (int c = 0; c < NCH; ++c) {
-    const uint32_t w[4] = {ri.ch[c].x, ri.ch[c].y, ri.ch[c].z, ri.ch[c].w};
-#pragma unroll
-    for (int k = 0; k < 4; ++k) am = fmaxf(am, fmaxf(fabsf(bf16lo(w[k])), fabsf(bf16hi(w[k]))));
+    words[4 * c] = ri.ch[c].x; words[4 * c + 1] = ri.ch[c].y;
+    words[4 * c + 2] = ri.ch[c].z; words[4 * c + 3] = ri.ch[c].w;
   }
-#pragma unroll
-  for (int off = TEAM / 2; off > 0; off >>= 1) am = fmaxf(am, __shfl_xor_sync(0xFFFFFFFFu, am, off));
-  am = fmaxf(am, 1e-8f);
+  const float am = fmaxf(team_absmax_bf16<TEAM>(words), 1e-8f);
   if (!on) return;
   if (lin == 0) *scale = f32_to_f16(am);
   // bf16 x * 127 overflows only when am > 2.6e36, outside the fast divisor range

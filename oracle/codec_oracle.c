@@ -92,7 +92,12 @@ void oracle_int8_encode(const uint16_t* src, int src_fp16, int64_t n_rows, int32
   for (int64_t r = 0; r < n_rows; ++r) {
     const uint16_t* row = src + r * row_len;
     float am = 0.0f;
-    for (int32_t i = 0; i < row_len; ++i) am = fmaxf(am, fabsf(in_val(row, i, src_fp16)));
+    for (int32_t i = 0; i < row_len; ++i) {
+      /* every NaN is skipped, signalling ones too (the GPU max instruction's
+         rule; C library fmaxf may return a NaN for a signalling operand) */
+      const float a = fabsf(in_val(row, i, src_fp16));
+      if (a > am) am = a;
+    }
     am = fmaxf(am, 1e-8f);
     scales[r] = scale_fp16 ? oracle_f32_to_f16(am) : oracle_f32_to_bf16(am);
     for (int32_t i = 0; i < row_len; ++i) {

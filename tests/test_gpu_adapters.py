@@ -298,6 +298,43 @@ def test_batch_pages_many_entries_per_cta(cuda, heads, T):
             assert np.array_equal(u16(cur[li][:rows]).reshape(rows, L), want), (h, li)
 
 
+@pytest.mark.parametrize("heads", [1, 8])
+def test_batch_pages_nan_inf_rows_match_oracle(cuda, heads):
+    """Token rows holding NaN, +-inf, all-NaN and all-zero values: slot bytes equal the oracle's."""
+    T, ppl = 16, 8
+    tokens = T * ppl
+    g = torch.Generator(device=cuda).manual_seed(41)
+    k = torch.randn(tokens, heads, 128, generator=g, device=cuda).to(torch.bfloat16)
+    v = torch.randn(tokens, heads, 128, generator=g, device=cuda).to(torch.bfloat16)
+    kb, vb = k.view(torch.int16).view(tokens, -1), v.view(torch.int16).view(tokens, -1)
+    kb[0, 0] = 0x7FC0
+    kb[1, 5] = 0xFF80 - 0x10000     # -inf (0xFF80) as int16
+    kb[2, :] = 0x7FC0
+    kb[3, :] = 0
+    vb[4, 7] = 0x7FA0
+    vb[5, 1], vb[5, 2] = 0x7F80, 0x7FC0
+    kv = KVLayers([k], [v])
+    L = kv.row_len
+    tab = DevicePageTable.empty(ppl, cuda)
+    tab.token_start.copy_(torch.arange(ppl, device=cuda, dtype=torch.int32) * T)
+    sb = int8_page_slot_bytes(T, L)
+    arena = SlotArena(ppl, sb, cuda)
+    mig = BatchMigrator(tab, kv, arena, ASHKVConfig(), [(0, 1), (1, 0)])
+    lst = torch.arange(ppl, dtype=torch.int32, device=cuda)
+    mig.encode(lst, torch.tensor([ppl], dtype=torch.int32, device=cuda))
+    torch.cuda.synchronize()
+    assert int(mig.status_encode[:ppl].abs().sum()) == 0
+    slot = tab.slot.cpu().numpy()
+    data = arena.data.view(ppl, sb).cpu().numpy()
+    c0 = (4 * T + 15) // 16 * 16
+    for p in range(ppl):
+        blob = data[slot[p]]
+        for h, t in enumerate((k, v)):
+            codes, scales = oracle.int8_encode(u16(t[p * T:(p + 1) * T]).reshape(T, L), L, scale_fp16=True)
+            assert np.array_equal(blob[:4 * T].view(np.uint16)[h * T:(h + 1) * T], scales), (p, h)
+            assert np.array_equal(blob[c0 + h * T * L:c0 + (h + 1) * T * L].view(np.int8).reshape(T, L), codes), (p, h)
+
+
 def test_batch_encode_runs_out_of_slots(cuda):
     layers, tokens, T = 1, 1024, 16
     kv = KVLayers([torch.randn(tokens, 8, 128, device=cuda).to(torch.bfloat16)],

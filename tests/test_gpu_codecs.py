@@ -181,6 +181,28 @@ def test_int8_nan_inf_do_not_crash(cuda):
     assert c[0, 1].item() == 0  # NaN -> 0
 
 
+@pytest.mark.parametrize("L", [128, 1024, 32])
+def test_int8_rows_with_nan_and_inf_match_oracle(cuda, L):
+    """NaN is ignored by the row maximum (and codes 0); +-inf rows take the exact
+    division path; an all-NaN row falls to the 1e-8 floor."""
+    g = torch.Generator().manual_seed(5)
+    x = torch.randn(64, L, generator=g).to(torch.bfloat16)
+    b = x.view(torch.int16).numpy().view(np.uint16).copy()
+    b[0, 0] = 0x7FC0                # NaN in the first lane's first chunk
+    b[1, L - 1] = 0xFFC1            # negative NaN with a payload, last element
+    b[2, 3], b[2, 5] = 0x7F80, 0x7FC0
+    b[3, :] = 0x7FC0                # every element NaN
+    b[4, L // 2] = 0xFF80           # -inf
+    b[5, ::2] = 0x7FA0              # signalling-NaN pattern on every other element
+    b[6, :] = 0
+    xb = torch.from_numpy(b.view(np.int16)).view(torch.bfloat16).to(cuda)
+    for sdt in (torch.bfloat16, torch.float16):
+        codes, scales = int8_mod.encode_rows(xb, scale_dtype=sdt)
+        oc, osc = oracle.int8_encode(b, L, scale_fp16=sdt == torch.float16)
+        assert np.array_equal(codes.cpu().numpy(), oc)
+        assert np.array_equal(bits_of(scales), osc)
+
+
 # ------------------------------------------------------------------- N-bit
 @pytest.mark.parametrize("ci", range(int(NBIT["nbit_n_cases"])))
 def test_nbit_bytes_api_reproduces_reference_blob(cuda, ci):
