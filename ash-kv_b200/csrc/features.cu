@@ -397,39 +397,79 @@ __global__ void head_sum_kernel(const float* __restrict__ colsum, int32_t heads,
   }
 }
 
-// One warp per page: raw saliency mass (sum of the page's token saliency) and
+// One CTA per page: raw saliency mass (sum of the page's token saliency) and
 // novelty (mean over its tokens of ||k_t - k_{t-1}||^2 / (||k_t||^2 + ||k_{t-1}||^2) / 2).
-__global__ void page_raw_kernel(const float* __restrict__ sal, const uint16_t* __restrict__ k, int32_t row_len,
-                                int64_t n_k, int32_t tokens_per_page, int64_t n_pages, float* __restrict__ s_raw,
-                                float* __restrict__ novelty) {
-  const int lane = threadIdx.x & 31;
-  const int64_t warps = int64_t(gridDim.x) * (blockDim.x / 32);
-  for (int64_t pg = int64_t(blockIdx.x) * (blockDim.x / 32) + (threadIdx.x >> 5); pg < n_pages; pg += warps) {
+// Warp w takes tokens t0 + w, t0 + w + 8, ...; the warps' partial sums are added
+// in warp order, so the result is the same on every run.  Rows are read as
+// 16-byte chunks when row_len is a multiple of 8 and k is 16-byte aligned (VEC),
+// else element by element.
+template <bool VEC>
+__device__ __forceinline__ void token_sums(const uint16_t* a, const uint16_t* b, int32_t row_len, int lane, float& dd,
+                                           float& nn) {
+  dd = 0.0f;
+  nn = 0.0f;
+  if constexpr (VEC) {
+#pragma unroll 4
+    for (int e = lane * 8; e < row_len; e += 256) {
+      const uint4 va = ld_nc_v4(a + e), vb = ld_nc_v4(b + e);
+      const uint32_t wa[4] = {va.x, va.y, va.z, va.w}, wb[4] = {vb.x, vb.y, vb.z, vb.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float x0 = bf16lo(wa[j]), x1 = bf16hi(wa[j]), y0 = bf16lo(wb[j]), y1 = bf16hi(wb[j]);
+        dd = fmaf(x0 - y0, x0 - y0, fmaf(x1 - y1, x1 - y1, dd));
+        nn = fmaf(x0, x0, fmaf(y0, y0, fmaf(x1, x1, fmaf(y1, y1, nn))));
+      }
+    }
+  } else {
+    for (int e = lane; e < row_len; e += 32) {
+      const float x = bf16_to_f32(a[e]), y = bf16_to_f32(b[e]);
+      dd = fmaf(x - y, x - y, dd);
+      nn = fmaf(x, x, fmaf(y, y, nn));
+    }
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) {
+    dd += __shfl_xor_sync(0xFFFFFFFFu, dd, off);
+    nn += __shfl_xor_sync(0xFFFFFFFFu, nn, off);
+  }
+}
+
+constexpr int kRawWarps = 8;
+
+template <bool VEC>
+__global__ void __launch_bounds__(kRawWarps * 32) page_raw_kernel(const float* __restrict__ sal,
+                                                                  const uint16_t* __restrict__ k, int32_t row_len,
+                                                                  int64_t n_k, int32_t tokens_per_page,
+                                                                  int64_t n_pages, float* __restrict__ s_raw,
+                                                                  float* __restrict__ novelty) {
+  __shared__ float s_nov[kRawWarps], s_mass[kRawWarps];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  for (int64_t pg = blockIdx.x; pg < n_pages; pg += gridDim.x) {
     const int64_t t0 = pg * tokens_per_page;
     const int64_t t1 = min(t0 + tokens_per_page, n_k);
-    float mass = 0.0f, nov = 0.0f;
-    for (int64_t t = t0; t < t1; ++t) {
+    float nov = 0.0f, mass = 0.0f;
+    for (int64_t t = t0 + warp; t < t1; t += kRawWarps) {
       if (sal) mass += sal[t];
       if (t == 0) continue;
-      const uint16_t* a = k + t * row_len;
-      const uint16_t* b = a - row_len;
-      float dd = 0.0f, nn = 0.0f;
-      for (int e = lane; e < row_len; e += 32) {
-        const float x = bf16_to_f32(a[e]), y = bf16_to_f32(b[e]);
-        dd = fmaf(x - y, x - y, dd);
-        nn = fmaf(x, x, fmaf(y, y, nn));
-      }
-#pragma unroll
-      for (int off = 16; off > 0; off >>= 1) {
-        dd += __shfl_xor_sync(0xFFFFFFFFu, dd, off);
-        nn += __shfl_xor_sync(0xFFFFFFFFu, nn, off);
-      }
+      float dd, nn;
+      token_sums<VEC>(k + t * row_len, k + (t - 1) * row_len, row_len, lane, dd, nn);
       nov += nn > 0.0f ? 0.5f * dd / nn : 0.0f;
     }
     if (lane == 0) {
-      if (s_raw) s_raw[pg] = mass;
-      novelty[pg] = nov / float(t1 - t0);
+      s_nov[warp] = nov;
+      s_mass[warp] = mass;
     }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      float n_sum = 0.0f, m_sum = 0.0f;
+      for (int w = 0; w < kRawWarps; ++w) {
+        n_sum += s_nov[w];
+        m_sum += s_mass[w];
+      }
+      if (s_raw) s_raw[pg] = m_sum;
+      novelty[pg] = n_sum / float(t1 - t0);
+    }
+    __syncthreads();  // s_nov / s_mass are rewritten for the next page
   }
 }
 
@@ -528,9 +568,15 @@ extern "C" ashkv_status_t ashkv_page_features(const float* d_token_saliency, con
   if (!d_k || !d_N || (d_token_saliency && (!d_s_raw || !d_S))) return ASHKV_BAD_ARGUMENT;
   cudaStream_t st = as_stream(stream);
   const int64_t n_pages = (n_k + tokens_per_page - 1) / tokens_per_page;
-  page_raw_kernel<<<grid_for(n_pages * 32, 256), 256, 0, st>>>(d_token_saliency, static_cast<const uint16_t*>(d_k),
-                                                                row_len, n_k, tokens_per_page, n_pages,
-                                                                d_token_saliency ? d_s_raw : nullptr, d_N);
+  const auto* kb = static_cast<const uint16_t*>(d_k);
+  float* s_raw = d_token_saliency ? d_s_raw : nullptr;
+  const unsigned grid = grid_for(n_pages * 256, 256);  // one CTA per page, at most 8 per SM
+  if (row_len % 8 == 0 && aligned(d_k, 16))
+    page_raw_kernel<true><<<grid, kRawWarps * 32, 0, st>>>(d_token_saliency, kb, row_len, n_k, tokens_per_page,
+                                                           n_pages, s_raw, d_N);
+  else
+    page_raw_kernel<false><<<grid, kRawWarps * 32, 0, st>>>(d_token_saliency, kb, row_len, n_k, tokens_per_page,
+                                                            n_pages, s_raw, d_N);
   if (d_token_saliency) page_normalise_kernel<<<1, 1024, 0, st>>>(d_s_raw, n_pages, d_S);
   return check_launch("ashkv_page_features");
 }

@@ -76,6 +76,19 @@ def test_page_features_vs_oracle(cuda):
     assert none is None and torch.equal(N3, N)
 
 
+def test_page_novelty_odd_rows_and_unaligned_pool(cuda):
+    """Rows whose length is not a multiple of 8, and a pool starting 2 bytes past a
+    16-byte boundary, take the element-wise path; both match the oracle."""
+    g = torch.Generator().manual_seed(17)
+    k = torch.randn(301, 1, 100, generator=g).to(torch.bfloat16)
+    _, N = F.page_features(k.to(cuda), 16)
+    close(N, oracle.page_features(k, 16, None)[1])
+    base = torch.randn(1 + 257 * 8 * 128, generator=g).to(torch.bfloat16).to(cuda)
+    kk = base[1:].view(257, 8, 128)
+    _, N2 = F.page_features(kk, 16)
+    close(N2, oracle.page_features(kk.cpu(), 16, None)[1])
+
+
 def test_saliency_repeatable_and_feeds_policy(cuda):
     """Bitwise repeatable; the page inputs run through the GPU score kernel."""
     from ashkv.runtime.score import score_vectorized
