@@ -56,6 +56,8 @@ SIGNATURES: dict[str, tuple] = {
                                        _I32, _P, _P, _P, _P]),
     "ashkv_policy_step": (_I32, [_P, _P, _P, _P, _P, _I64, _F32, _F32, _F32, _F32, _F64, _F64, _F64, _F64,
                                  _F64, _P, _P, _P, _P, _P, _P, _P, _P, _P]),
+    "ashkv_policy_step_device_pressure": (_I32, [_P, _P, _P, _P, _P, _I64, _F32, _F32, _F32, _F32, _P, _F64, _F64,
+                                                 _F64, _F64, _P, _P, _P, _P, _P, _P, _P, _P, _P]),
     "ashkv_fp8_encode": (_I32, [_P, _I64, _P, _P]),
     "ashkv_fp8_decode": (_I32, [_P, _I64, _P, _P]),
     "ashkv_int4_group_count": (_I64, [_I64, _I32]),
@@ -389,16 +391,28 @@ def policy_scratch_ints(n: int) -> int:
     return int(lib().ashkv_policy_scratch_ints(n))
 
 
-def policy_step(T, S, N, P, cur, weights, pressure: float, theta_high: float, theta_low: float, delta: float,
+def policy_step(T, S, N, P, cur, weights, pressure, theta_high: float, theta_low: float, delta: float,
                 p_emergency: float, next_colder, next_hotter, R: Optional[torch.Tensor], target: torch.Tensor,
                 demote_list: torch.Tensor, promote_list: torch.Tensor, counts: torch.Tensor,
                 scratch: torch.Tensor) -> None:
+    """``pressure`` is a Python float, or a one-element float32 CUDA tensor that the
+    kernel reads on the device (no host read-back between a pressure all-reduce and
+    the plan)."""
     _require_cuda(T, S, N, P, cur, R, target, demote_list, promote_list, counts, scratch)
     n = T.numel()
     if scratch.numel() < policy_scratch_ints(n) or demote_list.numel() < n or promote_list.numel() < n:
         raise ValueError("policy_step: list/scratch buffers too small")
     w_T, w_S, w_N, w_P = (float(w) for w in weights)
     nc, nh = _table(next_colder), _table(next_hotter)
+    if isinstance(pressure, torch.Tensor):
+        if not pressure.is_cuda or pressure.dtype != torch.float32 or pressure.numel() != 1:
+            raise ValueError("policy_step: a device pressure must be a one-element float32 CUDA tensor")
+        check(lib().ashkv_policy_step_device_pressure(
+            T.data_ptr(), S.data_ptr(), N.data_ptr(), P.data_ptr(), cur.data_ptr(), n, w_T, w_S, w_N, w_P,
+            pressure.data_ptr(), theta_high, theta_low, delta, p_emergency, _addr(nc), _addr(nh),
+            _ptr(R), target.data_ptr(), demote_list.data_ptr(), promote_list.data_ptr(), counts.data_ptr(),
+            scratch.data_ptr(), stream_handle(T.device)), "policy_step_device_pressure")
+        return
     check(lib().ashkv_policy_step(
         T.data_ptr(), S.data_ptr(), N.data_ptr(), P.data_ptr(), cur.data_ptr(), n, w_T, w_S, w_N, w_P,
         pressure, theta_high, theta_low, delta, p_emergency, _addr(nc), _addr(nh),

@@ -146,10 +146,14 @@ class BatchMigrator:
         self.status_encode = torch.zeros(n, dtype=torch.int32, device=dev)
         self.status_decode = torch.zeros(n, dtype=torch.int32, device=dev)
 
-    def plan(self, pressure: float) -> StepLists:
-        """Score every page, pick desired tiers and build the transition lists (device-resident)."""
+    def plan(self, pressure) -> StepLists:
+        """Score every page, pick desired tiers and build the transition lists (device-resident).
+        ``pressure`` is a float, or a one-element float32 CUDA tensor read on the device (e.g.
+        the MAX all-reduce of the ranks' pressures), which keeps the step free of host syncs."""
         t, c, L = self.table, self.cfg, self.lists
-        _native.policy_step(t.T, t.S, t.N, t.P, t.tier, (c.w_T, c.w_S, c.w_N, c.w_P), float(pressure), c.theta_high,
+        if not isinstance(pressure, torch.Tensor):
+            pressure = float(pressure)
+        _native.policy_step(t.T, t.S, t.N, t.P, t.tier, (c.w_T, c.w_S, c.w_N, c.w_P), pressure, c.theta_high,
                             c.theta_low, c.delta, c.p_emergency, self.next_colder, self.next_hotter, L.R, L.target,
                             L.demote, L.promote, L.counts, self._scratch)
         return L

@@ -29,6 +29,8 @@ struct PolicyParams {
   int64_t n;
   float wT, wS, wN, wP;
   float up, down;             // promote / demote thresholds (fp32)
+  const float* pressure_dev;  // when set, up/down come from this device value and th_*
+  double th_high, th_low, th_delta, th_emergency;
   int8_t next_colder[kTiers];
   int8_t next_hotter[kTiers];
   int do_score, do_tiers;
@@ -48,12 +50,25 @@ __device__ __forceinline__ float score1(const PolicyParams& p, int64_t i) {
   return r;
 }
 
-__device__ __forceinline__ int8_t tier1(const PolicyParams& p, float r, int8_t c) {
+__device__ __forceinline__ int8_t tier1(const PolicyParams& p, float up, float down, float r, int8_t c) {
   int8_t t = c;
   if (c < 0 || c >= kTiers) return t;  // out-of-table tiers never move
-  if (r >= p.up && c > 0) t = p.next_hotter[c];
-  if (r <= p.down && c < 2) t = p.next_colder[c];  // demotion applied second: it wins
+  if (r >= up && c > 0) t = p.next_hotter[c];
+  if (r <= down && c < 2) t = p.next_colder[c];  // demotion applied second: it wins
   return t;
+}
+
+// The thresholds from a pressure held in device memory: the host's double
+// arithmetic (fill_params) with every operation rounded on its own.
+__device__ __forceinline__ void device_thresholds(const PolicyParams& p, float& up, float& down) {
+  const double pr = double(*p.pressure_dev);
+  double boost = 0.0;
+  if (pr >= p.th_emergency) {
+    boost = __dmul_rn(__dadd_rn(pr, -p.th_emergency), 2.0);
+    boost = boost < 0.15 ? boost : 0.15;
+  }
+  up = __double2float_rn(__dadd_rn(p.th_high, p.th_delta));
+  down = __double2float_rn(__dadd_rn(__dadd_rn(p.th_low, boost), -p.th_delta));
 }
 
 __global__ void __launch_bounds__(kThreads) policy_kernel(const PolicyParams p) {
@@ -61,6 +76,8 @@ __global__ void __launch_bounds__(kThreads) policy_kernel(const PolicyParams p) 
   if (threadIdx.x < 2) s_cnt[threadIdx.x] = 0;
   __syncthreads();
   int32_t nd = 0, np = 0;
+  float up = p.up, down = p.down;
+  if (p.do_tiers && p.pressure_dev) device_thresholds(p, up, down);
   const int64_t base = int64_t(blockIdx.x) * kPagesPerBlock + threadIdx.x;
 #pragma unroll
   for (int k = 0; k < kItems; ++k) {
@@ -70,7 +87,7 @@ __global__ void __launch_bounds__(kThreads) policy_kernel(const PolicyParams p) 
     if (p.R_out) p.R_out[i] = r;
     if (p.do_tiers) {
       const int8_t c = p.cur[i];
-      const int8_t t = tier1(p, r, c);
+      const int8_t t = tier1(p, up, down, r, c);
       if (p.target_out) p.target_out[i] = t;
       nd += t > c;
       np += t < c;
@@ -210,10 +227,14 @@ extern "C" int64_t ashkv_policy_scratch_ints(int64_t n) {
   return 2 * ((n + kPagesPerBlock - 1) / kPagesPerBlock) + 2;
 }
 
-extern "C" ashkv_status_t ashkv_policy_step(
+namespace ashkv {
+namespace {
+
+// Shared by the host-pressure and device-pressure entry points.
+ashkv_status_t policy_step_impl(
     const float* d_T, const float* d_S, const float* d_N, const float* d_P, const int8_t* d_cur, int64_t n,
-    float w_T, float w_S, float w_N, float w_P, double pressure, double theta_high, double theta_low,
-    double delta, double p_emergency, const int8_t* next_colder, const int8_t* next_hotter,
+    float w_T, float w_S, float w_N, float w_P, double pressure, const float* d_pressure, double theta_high,
+    double theta_low, double delta, double p_emergency, const int8_t* next_colder, const int8_t* next_hotter,
     float* d_R, int8_t* d_target, int32_t* d_demote_list, int32_t* d_promote_list, int32_t* d_counts,
     int32_t* d_scratch, void* stream) {
   if (n < 0 || !next_colder || !next_hotter) return ASHKV_BAD_ARGUMENT;
@@ -233,12 +254,28 @@ extern "C" ashkv_status_t ashkv_policy_step(
   p.wT = w_T; p.wS = w_S; p.wN = w_N; p.wP = w_P;
   p.do_score = 1; p.do_tiers = 1; p.R_out = d_R; p.target_out = d_target; p.block_counts = d_scratch;
   fill_params(p, pressure, theta_high, theta_low, delta, p_emergency, next_colder, next_hotter);
+  p.pressure_dev = d_pressure;
+  p.th_high = theta_high; p.th_low = theta_low; p.th_delta = delta; p.th_emergency = p_emergency;
   policy_kernel<<<unsigned(blocks), kThreads, 0, st>>>(p);
   ashkv_status_t s = check_launch("policy_step");
   if (s != ASHKV_OK) return s;
   compact_kernel<<<unsigned(blocks), kThreads, 0, st>>>(d_cur, d_target, n, d_scratch, d_demote_list,
                                                         d_promote_list, d_counts);
   return check_launch("policy_compact");
+}
+
+}  // namespace
+}  // namespace ashkv
+
+extern "C" ashkv_status_t ashkv_policy_step(
+    const float* d_T, const float* d_S, const float* d_N, const float* d_P, const int8_t* d_cur, int64_t n,
+    float w_T, float w_S, float w_N, float w_P, double pressure, double theta_high, double theta_low,
+    double delta, double p_emergency, const int8_t* next_colder, const int8_t* next_hotter,
+    float* d_R, int8_t* d_target, int32_t* d_demote_list, int32_t* d_promote_list, int32_t* d_counts,
+    int32_t* d_scratch, void* stream) {
+  return policy_step_impl(d_T, d_S, d_N, d_P, d_cur, n, w_T, w_S, w_N, w_P, pressure, nullptr, theta_high,
+                          theta_low, delta, p_emergency, next_colder, next_hotter, d_R, d_target, d_demote_list,
+                          d_promote_list, d_counts, d_scratch, stream);
 }
 
 // ---------------------------------------------------------------------------
@@ -316,4 +353,26 @@ extern "C" ashkv_status_t ashkv_policy_step_noalloc(
   return ashkv_policy_step(d_T, d_S, d_N, d_P, d_cur, n, w_T, w_S, w_N, w_P, pressure, theta_high, theta_low,
                            delta, p_emergency, next_colder, next_hotter, d_R, d_target, d_demote_list,
                            d_promote_list, d_counts, scratch, stream);
+}
+
+extern "C" ashkv_status_t ashkv_policy_step_device_pressure(
+    const float* d_T, const float* d_S, const float* d_N, const float* d_P, const int8_t* d_cur, int64_t n,
+    float w_T, float w_S, float w_N, float w_P, const float* d_pressure, double theta_high, double theta_low,
+    double delta, double p_emergency, const int8_t* next_colder, const int8_t* next_hotter,
+    float* d_R, int8_t* d_target, int32_t* d_demote_list, int32_t* d_promote_list, int32_t* d_counts,
+    int32_t* d_scratch, void* stream) {
+  if (!d_pressure) return ASHKV_BAD_ARGUMENT;
+  int32_t* scratch = d_scratch;
+  if (!scratch) {
+    if (n > ASHKV_POLICY_NOALLOC_MAX_PAGES) {
+      set_message("policy_step_device_pressure: without caller scratch the page table is limited to "
+                  "ASHKV_POLICY_NOALLOC_MAX_PAGES = 4194304 entries");
+      return ASHKV_BAD_ARGUMENT;
+    }
+    const ashkv_status_t s = scratch_for_current_device(&scratch);
+    if (s != ASHKV_OK) return s;
+  }
+  return policy_step_impl(d_T, d_S, d_N, d_P, d_cur, n, w_T, w_S, w_N, w_P, 0.0, d_pressure, theta_high,
+                          theta_low, delta, p_emergency, next_colder, next_hotter, d_R, d_target, d_demote_list,
+                          d_promote_list, d_counts, scratch, stream);
 }

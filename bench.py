@@ -363,7 +363,7 @@ def run_demote(dev, world: int, rank: int, dist, steps: int, warmup: int, layers
         pr = local_p.clone()
         if dist:
             dist.all_reduce(pr, op=dist.ReduceOp.MAX)
-        L = mig.plan(float(pr.item()))
+        L = mig.plan(pr)  # read on the device: no host sync inside the step
         if ev is not None:
             ev[0].record(stream)
         mig.demote()

@@ -281,6 +281,24 @@ ASHKV_API ashkv_status_t ashkv_policy_step_noalloc(
     void* stream);
 
 /* ========================================================================
+ * ashkv_policy_step with the allocator pressure read from device memory
+ * (one fp32 value, e.g. the result of the ranks' MAX all-reduce), so a
+ * step needs no host read-back between the pressure exchange and the
+ * plan.  The thresholds are computed in the kernel with the same double
+ * operations as ashkv_policy_step applies to (double)*d_pressure, so both
+ * give identical lists.  d_scratch may be NULL: the static scratch of
+ * ashkv_policy_step_noalloc is used then (same limits and sharing rule).
+ * No counterpart in the reference, whose pressure is a host float
+ * (ashkv/runtime/controller.py:32-106).
+ * ======================================================================== */
+ASHKV_API ashkv_status_t ashkv_policy_step_device_pressure(
+    const float* d_T, const float* d_S, const float* d_N, const float* d_P, const int8_t* d_cur, int64_t n,
+    float w_T, float w_S, float w_N, float w_P, const float* d_pressure, double theta_high, double theta_low,
+    double delta, double p_emergency, const int8_t* next_colder, const int8_t* next_hotter,
+    float* d_R, int8_t* d_target, int32_t* d_demote_list, int32_t* d_promote_list, int32_t* d_counts,
+    int32_t* d_scratch, void* stream);
+
+/* ========================================================================
  * FP8 codec: bf16 <-> float8_e4m3fn, one byte per element.
  * Replaces FP8Codec (ashkv/codecs/fp8.py:32-79), i.e. torch's casts
  * tensor.to(torch.float8_e4m3fn) and view(float8_e4m3fn).to(bfloat16):

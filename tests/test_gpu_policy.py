@@ -95,6 +95,49 @@ def test_policy_step_lists_config5(cuda, pressure):
     assert np.array_equal(pl[:npro].cpu().numpy(), np.nonzero(tn < cn)[0])
 
 
+@pytest.mark.parametrize("pressure", [0.5, 0.9, 0.95, 0.96, 0.97, 0.999, float("nan")])
+def test_policy_step_device_pressure_matches_host(cuda, pressure):
+    """The pressure read on the device (fp32, as after the ranks' all-reduce) gives the
+    lists the host path gives for the same fp32 value, with caller scratch or the
+    library's static scratch."""
+    n = 300_000
+    g = torch.Generator(device=cuda).manual_seed(7)
+    T, S, N, P = (torch.rand(n, generator=g, device=cuda) for _ in range(4))
+    cur = torch.randint(0, 4, (n,), generator=g, device=cuda, dtype=torch.int8)
+    nc, nh = controller_tables([(0, 1), (1, 0), (1, 2), (2, 1), (0, 2), (2, 0), (2, 3), (3, 2)])
+    p32 = torch.tensor([pressure], dtype=torch.float32, device=cuda)
+    outs = []
+    for mode in ("host", "device", "device_static"):
+        R = torch.empty(n, device=cuda)
+        target = torch.empty(n, dtype=torch.int8, device=cuda)
+        dl = torch.full((n,), -1, dtype=torch.int32, device=cuda)
+        pl = torch.full((n,), -1, dtype=torch.int32, device=cuda)
+        counts = torch.empty(2, dtype=torch.int32, device=cuda)
+        scratch = torch.empty(_native.policy_scratch_ints(n), dtype=torch.int32, device=cuda)
+        if mode == "host":
+            _native.policy_step(T, S, N, P, cur, (0.7, 0.1, 0.1, 0.1), float(p32.item()), 0.72, 0.33, 0.04, 0.95,
+                                nc, nh, R, target, dl, pl, counts, scratch)
+        elif mode == "device":
+            _native.policy_step(T, S, N, P, cur, (0.7, 0.1, 0.1, 0.1), p32, 0.72, 0.33, 0.04, 0.95,
+                                nc, nh, R, target, dl, pl, counts, scratch)
+        else:
+            ncb = np.ascontiguousarray(nc, dtype=np.int8)
+            nhb = np.ascontiguousarray(nh, dtype=np.int8)
+            _native.check(_native.lib().ashkv_policy_step_device_pressure(
+                T.data_ptr(), S.data_ptr(), N.data_ptr(), P.data_ptr(), cur.data_ptr(), n, 0.7, 0.1, 0.1, 0.1,
+                p32.data_ptr(), 0.72, 0.33, 0.04, 0.95, ncb.ctypes.data, nhb.ctypes.data, R.data_ptr(),
+                target.data_ptr(), dl.data_ptr(), pl.data_ptr(), counts.data_ptr(), None,
+                _native.stream_handle(cuda)), "policy_step_device_pressure")
+        torch.cuda.synchronize()
+        outs.append([t.cpu().numpy() for t in (R, target, dl, pl, counts)])
+    Rn = oracle.score(*(a.cpu().numpy() for a in (T, S, N, P)), 0.7, 0.1, 0.1, 0.1)
+    tn = oracle.desired_tiers(Rn, cur.cpu().numpy(), float(np.float32(pressure)), 0.72, 0.33, 0.04, 0.95, nc, nh)
+    for o in outs:
+        assert np.array_equal(o[1], tn)
+        for a, b in zip(o, outs[0]):
+            assert np.array_equal(a, b)
+
+
 @pytest.mark.parametrize("item_bytes,stride", [(32768, 32768), (32768, 33024), (1, 8), (31, 40), (100, 100),
                                                (77, 77), (4096 + 24, 4096 + 24)])
 def test_xxh64_items_match_xxhash(cuda, item_bytes, stride):
