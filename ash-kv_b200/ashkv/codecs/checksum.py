@@ -11,6 +11,7 @@ pages in one sm_100a kernel launch (libashkv_cuda ``ashkv_xxh64_items``).
 from __future__ import annotations
 
 import hashlib
+from typing import Optional
 
 import torch
 
@@ -37,7 +38,7 @@ def checksum_pair(raw_bytes: bytes) -> tuple[int, int]:
     return a, b
 
 
-def checksum_pages(pages: torch.Tensor, seed: int = 0) -> torch.Tensor:
+def checksum_pages(pages: torch.Tensor, seed: int = 0, out: Optional[torch.Tensor] = None) -> torch.Tensor:
     """XXH64 of each row of a CUDA tensor [n_pages, ...] (row = one page's bytes).
 
     Returns an int64 CUDA tensor holding the digests' bit patterns
@@ -50,6 +51,9 @@ def checksum_pages(pages: torch.Tensor, seed: int = 0) -> torch.Tensor:
     if flat.stride(-1) != 1:
         raise ValueError("checksum_pages: pages must be row-contiguous")
     item_bytes = flat.shape[1] * flat.element_size()
-    out = torch.empty(n, dtype=torch.int64, device=pages.device)
+    if out is None:
+        out = torch.empty(n, dtype=torch.int64, device=pages.device)
+    elif out.dtype != torch.int64 or out.numel() < n or not out.is_cuda:
+        raise ValueError("checksum_pages: out must be an int64 CUDA tensor of at least n_pages entries")
     _native.xxh64_items(flat, n, item_bytes, flat.stride(0) * flat.element_size(), out, seed)
     return out

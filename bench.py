@@ -286,6 +286,13 @@ def codec_suite(K: torch.Tensor, V: torch.Tensor, peak: float, iters: int = 20) 
     out["int2_dithered_encode"] = entry("nbit_encode_tma_kernel<2,PHILOX,3>", i2, ms)
     ms = timed(lambda: nb.decode_groups(e2K, out=bK), lambda: nb.decode_groups(e2V, out=bV))
     out["int2_dithered_decode"] = entry("nbit_decode_kernel<2>", i2, ms)
+    # per-page XXH64 (the migrate path's checksums): 4096 pages of 16 tokens x 8 heads x 128 bf16
+    from ashkv.codecs.checksum import checksum_pages
+    pK, pV = K.view(-1, TOKENS * HEADS * HEAD_DIM), V.view(-1, TOKENS * HEADS * HEAD_DIM)
+    dK = torch.empty(pK.shape[0], dtype=torch.int64, device=K.device)
+    dV = torch.empty_like(dK)
+    ms = timed(lambda: checksum_pages(pK, out=dK), lambda: checksum_pages(pV, out=dV))
+    out["xxh64_pages"] = entry("xxh64_items_kernel", 2 * E + 8 * pK.shape[0], ms)
     return out
 
 

@@ -139,7 +139,8 @@ def test_policy_step_device_pressure_matches_host(cuda, pressure):
 
 
 @pytest.mark.parametrize("item_bytes,stride", [(32768, 32768), (32768, 33024), (1, 8), (31, 40), (100, 100),
-                                               (77, 77), (4096 + 24, 4096 + 24)])
+                                               (77, 77), (4096 + 24, 4096 + 24), (4096 + 24, 4096 + 32),
+                                               (1024, 1024), (1040, 1040), (5000, 5008), (65536 + 7, 65536 + 16)])
 def test_xxh64_items_match_xxhash(cuda, item_bytes, stride):
     n = 64
     rng = np.random.default_rng(item_bytes)
@@ -156,6 +157,22 @@ def test_xxh64_items_match_xxhash(cuda, item_bytes, stride):
     _native.xxh64_items(d[3:], n - 1, item_bytes, stride, out, 0)
     want = [xxhash.xxh64(buf[3 + i * stride:3 + i * stride + item_bytes].tobytes()).intdigest() for i in range(n - 1)]
     assert out[: n - 1].cpu().numpy().view(np.uint64).tolist() == want
+
+
+def test_xxh64_many_items_and_one_long_item(cuda):
+    """More item groups than SMs (the staged kernel's CTAs stride over groups; the
+    last group is partial), and a single 1 MiB item (a long chunk sequence)."""
+    rng = np.random.default_rng(99)
+    n, L = 148 * 32 + 37, 1024
+    buf = rng.integers(0, 256, n * L, dtype=np.uint8)
+    out = torch.empty(n, dtype=torch.int64, device=cuda)
+    _native.xxh64_items(torch.from_numpy(buf).to(cuda), n, L, L, out, 7)
+    want = [xxhash.xxh64(buf[i * L:(i + 1) * L].tobytes(), seed=7).intdigest() for i in range(n)]
+    assert out.cpu().numpy().view(np.uint64).tolist() == want
+    big = rng.integers(0, 256, (1 << 20) + 3, dtype=np.uint8)
+    one = torch.empty(1, dtype=torch.int64, device=cuda)
+    _native.xxh64_items(torch.from_numpy(big).to(cuda), 1, big.size, big.size, one, 0)
+    assert int(one.cpu().numpy().view(np.uint64)[0]) == xxhash.xxh64(big.tobytes()).intdigest()
 
 
 def test_checksum_pages_of_kv_pages(cuda):
