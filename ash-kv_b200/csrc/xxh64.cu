@@ -210,8 +210,13 @@ __global__ void __launch_bounds__(kItemsPerCta * 4, 1) xxh64_items_staged_kernel
     const int64_t cb = sbytes - cc * kChunk;
     const int rows = int((cb < kChunk ? cb : kChunk) / 32);
     const uint8_t* row = sm + cstage * (kItemsPerCta * kRow) + slot * kRow + 8 * lane;
+    if (rows == kChunk / 32) {  // full chunk: a fixed trip count, loads hoisted ahead of the chain
+#pragma unroll 16
+      for (int r = 0; r < kChunk / 32; ++r) v = xxround(v, lds64(row + r * 32));
+    } else {
 #pragma unroll 8
-    for (int r = 0; r < rows; ++r) v = xxround(v, lds64(row + r * 32));
+      for (int r = 0; r < rows; ++r) v = xxround(v, lds64(row + r * 32));
+    }
     if (cc == n_chunks - 1) {  // the group's items are complete: merge, tail, avalanche
       const unsigned qbase = (tid & 31u) & ~3u;
       const uint64_t v1 = __shfl_sync(0xFFFFFFFFu, v, int(qbase + 0));
