@@ -165,12 +165,30 @@ class PendingResult:
 _SIDE_STREAMS: dict = {}
 
 
-def _side_streams(dev: torch.device):
-    """Per-device (host->device, device->host) copy streams of the host-buffer API."""
-    key = dev.index
+def _side_streams(dev: torch.device, kind: str = "encode"):
+    """Per-device (host->device, device->host) copy streams of the host-buffer API;
+    encodes and decodes have their own pair, so the copies of one never queue
+    behind the other's (the copy engines run both directions and both pairs at once)."""
+    key = (dev.index, kind)
     if key not in _SIDE_STREAMS:
         _SIDE_STREAMS[key] = (torch.cuda.Stream(dev), torch.cuda.Stream(dev))
     return _SIDE_STREAMS[key]
+
+
+# Host blob buffers whose device->host copies were queued without a host wait
+# (encode_pinned_batch(host_sync=False)): data pointer -> CUDA event that
+# completes with the copies.  decode_pinned_batch orders its reads of such a
+# buffer after the event on the GPU; sync_host_blobs() waits on the host.
+_BLOB_WRITES: dict = {}
+
+
+def sync_host_blobs(blobs) -> None:
+    """Wait until the blobs returned by ``encode_pinned_batch(host_sync=False)`` are
+    complete in host memory (only needed before reading their bytes on the host)."""
+    for b in blobs:
+        ev = _BLOB_WRITES.pop(b.data_ptr(), None)
+        if ev is not None:
+            ev.synchronize()
 
 
 def _sha8(raw: bytes) -> int:
@@ -256,7 +274,8 @@ class DitheredNBitCodec:
         from ``src`` and into ``out``; the call returns once ``out`` is complete."""
         return self.encode_pinned_batch([src], [out], uniforms=[uniform])[0]
 
-    def encode_pinned_batch(self, srcs, outs=None, *, uniforms=None, wait: bool = True):
+    def encode_pinned_batch(self, srcs, outs=None, *, uniforms=None, wait: bool = True,
+                            host_sync: bool = True):
         """``encode_pinned`` over several tensors, in order (one call each, so each
         gets the seed that call would get).  Host->device copies run on one side
         stream and device->host copies on another, so a tensor's blob travels
@@ -265,7 +284,14 @@ class DitheredNBitCodec:
         With ``wait=False`` the call returns a :class:`PendingResult` once the
         copies in and the kernels are queued; ``.result()`` then reads the outlier
         counts, queues the copies out and returns the list of blobs.  Work queued
-        in between (for example the decode of the previous blobs) overlaps it."""
+        in between (for example the decode of the previous blobs) overlaps it.
+
+        With ``host_sync=False`` the blobs are returned as soon as their copies out
+        are queued: their 8-byte headers are final, the rest lands when the copies
+        complete.  ``decode_pinned_batch`` may be given such blobs directly (it
+        orders its reads after the copies on the GPU); ``sync_host_blobs(blobs)``
+        waits for them before the host reads their bytes.  The output buffers must
+        not be handed to another encode until the blobs' decode has completed."""
         outs = list(outs) if outs is not None else [None] * len(srcs)
         uniforms = list(uniforms) if uniforms is not None else [None] * len(srcs)
         if not (len(outs) == len(uniforms) == len(srcs)):
@@ -298,6 +324,11 @@ class DitheredNBitCodec:
                 with torch.cuda.stream(h2d):
                     j["d_src"].copy_(j["flat"][:n_elems], non_blocking=True)
                     j["u"] = None if u is None else u.to(dev, non_blocking=True).contiguous()
+                # the buffers come from the current stream's pool but are written on h2d:
+                # tell the caching allocator, so a free cannot hand them out while h2d is busy
+                j["d_src"].record_stream(h2d)
+                if j["u"] is not None:
+                    j["u"].record_stream(h2d)
                 j["ready"] = h2d.record_event()
             totals = torch.empty(len(jobs), dtype=torch.int32, pin_memory=True)
         for i, j in enumerate(jobs):
@@ -311,10 +342,10 @@ class DitheredNBitCodec:
             j.update(enc=enc, idx=idx, val=val, done=cur.record_event())
 
         def finish():
-            return self._encode_finish(jobs, outs, totals, dev)
+            return self._encode_finish(jobs, outs, totals, dev, host_sync)
         return finish() if wait else PendingResult(finish)
 
-    def _encode_finish(self, jobs, outs, totals, dev) -> list:
+    def _encode_finish(self, jobs, outs, totals, dev, host_sync: bool = True) -> list:
         d2h = _side_streams(dev)[1] if dev is not None else None
         results = []
         for i, (j, out) in enumerate(zip(jobs, outs)):
@@ -337,9 +368,18 @@ class DitheredNBitCodec:
                     out[o:o + 4 * n_out].copy_(j["idx"][:n_out].view(torch.uint8), non_blocking=True); o += 4 * n_out
                     out[o:o + 2 * n_out].copy_(j["val"][:n_out].view(torch.uint8), non_blocking=True); o += 2 * n_out
                 out[o:o + n_codes].copy_(enc.codes[:n_codes], non_blocking=True)
+            # read on d2h, possibly after this call returns (host_sync=False)
+            for t in (enc.scales, enc.codes, j["idx"], j["val"]):
+                t.record_stream(d2h)
             results.append(out[:size])
         if dev is not None:
-            d2h.record_event().synchronize()
+            copied = d2h.record_event()
+            if host_sync:
+                copied.synchronize()
+            else:
+                for r in results:
+                    if r.numel() > 8:
+                        _BLOB_WRITES[r.data_ptr()] = copied
         return results
 
     def decode_pinned(self, blob: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
@@ -375,12 +415,15 @@ class DitheredNBitCodec:
         if any(j["num_tokens"] for j in jobs):
             dev = _staging.device()
             cur = torch.cuda.current_stream(dev)
-            h2d, d2h = _side_streams(dev)
+            h2d, d2h = _side_streams(dev, "decode")
             h2d.wait_stream(cur)
             for j in jobs:
                 if not j["num_tokens"]:
                     continue
                 b, g, nc, n_out = j["b"], j["n_groups"], j["n_codes"], j["n_out"]
+                written = _BLOB_WRITES.pop(b.data_ptr(), None)
+                if written is not None:  # blob bytes still arriving from an encode
+                    h2d.wait_event(written)
                 # one DMA per blob section, each into its own (aligned) device buffer
                 d_sc = torch.empty(2 * g, dtype=torch.uint8, device=dev)
                 d_idx = torch.empty(max(4 * n_out, 4), dtype=torch.uint8, device=dev)
@@ -393,6 +436,8 @@ class DitheredNBitCodec:
                         d_idx[:4 * n_out].copy_(b[o:o + 4 * n_out], non_blocking=True); o += 4 * n_out
                         d_val[:2 * n_out].copy_(b[o:o + 2 * n_out], non_blocking=True); o += 2 * n_out
                     codes[:nc].copy_(b[o:o + nc], non_blocking=True)
+                for t in (d_sc, d_idx, d_val, codes):  # written on h2d (see encode_pinned_batch)
+                    t.record_stream(h2d)
                 j.update(d_sc=d_sc, d_idx=d_idx, d_val=d_val, codes=codes, ready=h2d.record_event())
             statuses = torch.zeros(len(jobs), dtype=torch.int32, device=dev)
             h_status = torch.empty(len(jobs), dtype=torch.int32, pin_memory=True)
@@ -413,6 +458,7 @@ class DitheredNBitCodec:
             d2h.wait_event(done)
             with torch.cuda.stream(d2h):
                 out[:g * 32].copy_(dv, non_blocking=True)
+            dv.record_stream(d2h)
             j["dv"] = dv
             results.append(out[:g * 32])
         done = None
@@ -420,6 +466,7 @@ class DitheredNBitCodec:
             d2h.wait_stream(cur)
             with torch.cuda.stream(d2h):
                 h_status.copy_(statuses, non_blocking=True)
+            statuses.record_stream(d2h)  # read on d2h after this call returns (wait=False)
             done = d2h.record_event()
 
         def finish():

@@ -392,10 +392,61 @@ def test_nbit_pinned_api_matches_bytes_api(cuda, bits, hidden):
     pend_enc = asy.encode_pinned_batch([x], wait=False)
     assert [t.view(torch.int16).numpy().tobytes() for t in pend_dec.result()] == [seq.decode(w) for w in want[:2]]
     assert pend_enc.result()[0].numpy().tobytes() == want[2]
+    # blobs handed from an encode to a decode on another stream without a host wait
+    # (the decode's reads ordered after the encode's copies on the GPU), over a
+    # three-deep rotation of blob buffers as a streaming caller uses them
+    nw = DitheredNBitCodec(hidden_dim=hidden, bits=bits)
+    bufs = [[torch.empty(len(w) + 64, dtype=torch.uint8, pin_memory=True) for w in want[:2]] for _ in range(3)]
+    outs = [[torch.empty(t.numel(), dtype=torch.bfloat16, pin_memory=True) for t in (x, y)] for _ in range(2)]
+    side = torch.cuda.Stream(cuda)
+    ref = DitheredNBitCodec(hidden_dim=hidden, bits=bits)  # same call sequence, same seeds
+    wants = [ref.encode(bits_of(t).tobytes()) for _ in range(3) for t in (x, y)]
+    blobs = nw.encode_pinned_batch([x.pin_memory(), y.pin_memory()], bufs[0], host_sync=False)
+    got_blobs, pend = [], []
+    for s_ in range(1, 4):
+        pe = nw.encode_pinned_batch([x.pin_memory(), y.pin_memory()], bufs[s_ % 3], wait=False, host_sync=False) \
+            if s_ < 3 else None
+        with torch.cuda.stream(side):
+            pend.append((blobs, nw.decode_pinned_batch(blobs, outs[s_ % 2], wait=False)))
+        if pe is not None:
+            blobs = pe.result()
+        prev_blobs, pd = pend.pop(0)
+        decoded = [t.view(torch.int16).numpy().tobytes() for t in pd.result()]
+        got_blobs.append([bb.numpy().tobytes() for bb in prev_blobs])
+        assert decoded == [seq.decode(w) for w in got_blobs[-1]]
+    assert [b_ for pair in got_blobs for b_ in pair] == wants
+    from ashkv.codecs.nbit_dithered import sync_host_blobs
+    last = nw.encode_pinned_batch([x.pin_memory()], [bufs[0][0]], host_sync=False)
+    sync_host_blobs(last)
+    assert last[0].numpy().tobytes() == ref.encode(bits_of(x).tobytes())
     c = DitheredINT2Codec()
     u = torch.rand(x.numel() // 128 * 128)
     assert c.encode_pinned(x, uniform=u).numpy().tobytes() == c.encode(data, uniform=u)
     assert DitheredNBitCodec().encode_pinned(torch.empty(0, dtype=torch.bfloat16)).numpy().tobytes() == bytes(8)
+
+
+def test_nbit_pinned_streaming_loop_keeps_buffers_alive(cuda):
+    """A decode queued with wait=False and then an encode queued with wait=False,
+    repeated: the decode's device status word (read back on a side stream after the
+    call returns) and every other side-stream buffer stay reserved until their
+    copies finish, so the encode's allocations cannot land on them (a use-after-free
+    here showed up as spurious index-range/overflow flags)."""
+    n = 1 << 22
+    x = rand_bf16(n, 81, "outliers").pin_memory()
+    y = rand_bf16(n, 82, "wide").pin_memory()
+    ref = DitheredNBitCodec(hidden_dim=128, bits=4)
+    want = [[ref.encode(bits_of(t).tobytes()) for t in (x, y)] for _ in range(7)]
+    c = DitheredNBitCodec(hidden_dim=128, bits=4)
+    bufs = [[torch.empty(len(w) + 64, dtype=torch.uint8, pin_memory=True) for w in want[0]] for _ in range(2)]
+    outs = [torch.empty(n, dtype=torch.bfloat16, pin_memory=True) for _ in range(2)]
+    blobs = c.encode_pinned_batch([x, y], bufs[0])
+    for s_ in range(1, 7):
+        pd = c.decode_pinned_batch(blobs, outs, wait=False)
+        pe = c.encode_pinned_batch([x, y], bufs[s_ % 2], wait=False)
+        got = [t.view(torch.int16).numpy().tobytes() for t in pd.result()]
+        assert got == [ref.decode(w) for w in want[s_ - 1]]
+        blobs = pe.result()
+        assert [b.numpy().tobytes() for b in blobs] == want[s_]
 
 
 def test_nbit_config3_full_size_int2_properties(cuda):
