@@ -102,6 +102,18 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+// Two 2^x on an fp32 pair.
+__device__ __forceinline__ f2 ex2_2(f2 x) {
+  float a, b;
+  upk2(x, a, b);
+  return pk2(ex2(a), ex2(b));
+}
+
 struct SalParams {
   int32_t heads_q, group, nch;  // group = heads_q / heads_kv; nch = head_dim / 64
   int64_t n_q, n_k, q_pos0;
@@ -274,12 +286,26 @@ __global__ void __launch_bounds__(kThreadsF, 2) saliency_rows_kernel(const __gri
               [&](int i, float (&v)[32]) {
                 const int64_t k0 = int64_t(i) * kTile + cg * 32;
                 float mx = -INFINITY;
-                if (k0 + 31 <= qpos && k0 + 31 < p.n_k) {  // the whole column group is visible
+                if (k0 + 31 <= qpos && k0 + 31 < p.n_k) {  // the whole column group is visible: fp32 pairs
+                  const f2 C2 = pk2(c, c);
+                  f2 V[16];
 #pragma unroll
-                  for (int j = 0; j < 32; ++j) {
-                    v[j] *= c;
-                    mx = fmaxf(mx, v[j]);
+                  for (int j = 0; j < 16; ++j) {
+                    V[j] = mul2(pk2(v[2 * j], v[2 * j + 1]), C2);
+                    float a, b;
+                    upk2(V[j], a, b);
+                    mx = max3f(mx, a, b);
                   }
+                  const float mn = fmaxf(m, mx);
+                  const f2 NMN = pk2(-mn, -mn);
+                  f2 S = pk2(0.0f, 0.0f);
+#pragma unroll
+                  for (int j = 0; j < 16; ++j) S = add2(S, ex2_2(add2(V[j], NMN)));
+                  float s0, s1;
+                  upk2(S, s0, s1);
+                  l = (m == -INFINITY ? 0.0f : l * ex2(m - mn)) + (s0 + s1);
+                  m = mn;
+                  return;
                 } else {
 #pragma unroll
                   for (int j = 0; j < 32; ++j) {
@@ -358,14 +384,17 @@ __global__ void __launch_bounds__(kThreadsF, 2) saliency_cols_kernel(const __gri
                 const bool full = p.q_pos0 + qc >= kpos && qc + 31 < p.n_q;  // every query of the group sees this key
                 if (full && (reinterpret_cast<uintptr_t>(lse + qc) & 15u) == 0) {
                   const float4* l4 = reinterpret_cast<const float4*>(lse + qc);  // the group's row normalisers
+                  const f2 C2 = pk2(c, c);
+                  f2 S = pk2(0.0f, 0.0f);
 #pragma unroll
                   for (int j4 = 0; j4 < 8; ++j4) {
                     const float4 n4 = __ldg(l4 + j4);
-                    acc_sum += ex2(fmaf(v[4 * j4], c, -n4.x));
-                    acc_sum += ex2(fmaf(v[4 * j4 + 1], c, -n4.y));
-                    acc_sum += ex2(fmaf(v[4 * j4 + 2], c, -n4.z));
-                    acc_sum += ex2(fmaf(v[4 * j4 + 3], c, -n4.w));
+                    S = add2(S, ex2_2(fma2(pk2(v[4 * j4], v[4 * j4 + 1]), C2, pk2(-n4.x, -n4.y))));
+                    S = add2(S, ex2_2(fma2(pk2(v[4 * j4 + 2], v[4 * j4 + 3]), C2, pk2(-n4.z, -n4.w))));
                   }
+                  float s0, s1;
+                  upk2(S, s0, s1);
+                  acc_sum += s0 + s1;
                 } else if (full) {
 #pragma unroll
                   for (int j = 0; j < 32; ++j) acc_sum += ex2(fmaf(v[j], c, -__ldg(lse + qc + j)));
