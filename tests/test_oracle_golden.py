@@ -72,6 +72,28 @@ def test_int8_decode_formula():
     assert np.all(np.abs(got - want) <= np.abs(want) * 2.0 ** -8)
 
 
+def test_int8_oracle_row_maximum_skips_every_nan():
+    """The row maximum ignores quiet and signalling NaNs alike (the GPU max
+    instruction's rule, which Triton's tl.maximum lowers to), NaN codes are 0,
+    and an all-NaN row falls to the 1e-8 floor."""
+    L = 128
+    rng = np.random.default_rng(3)
+    x = rng.standard_normal((4, L)).astype(np.float32)
+    bits = (x.view(np.uint32) >> 16).astype(np.uint16)  # truncated to bf16 bits
+    bits[0, ::2] = 0x7FA0           # signalling-NaN pattern on every other element
+    bits[1, 5] = 0xFFC1             # negative quiet NaN with a payload
+    bits[2, :] = 0x7FC0             # every element NaN
+    codes, scales = oracle.int8_encode(bits, L)
+    vals = (bits.astype(np.uint32) << 16).view(np.float32)
+    for r in (0, 1):
+        finite = vals[r][~np.isnan(vals[r])]
+        want = oracle.lib().oracle_f32_to_bf16(float(np.abs(finite).max()))
+        assert scales[r] == want
+        assert np.all(codes[r][np.isnan(vals[r])] == 0)
+    assert scales[2] == oracle.lib().oracle_f32_to_bf16(1e-8)
+    assert np.all(codes[2] == 0)
+
+
 def test_policy_oracle_matches_reference():
     z = POLICY
     R = oracle.score(z["policy_T"], z["policy_S"], z["policy_N"], z["policy_P"], 0.7, 0.1, 0.1, 0.1)
