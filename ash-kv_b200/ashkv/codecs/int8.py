@@ -15,7 +15,6 @@ from __future__ import annotations
 import struct
 from typing import Optional
 
-import numpy as np
 import torch
 
 from .. import _native, _staging

@@ -1,7 +1,6 @@
 """Shared pytest setup: import paths, the ``gpu`` marker, library build."""
 from __future__ import annotations
 
-import os
 import sys
 from pathlib import Path
 

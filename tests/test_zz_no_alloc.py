@@ -10,7 +10,6 @@ sorts last so a run that stops at the first failure has run all other tests.
 """
 from __future__ import annotations
 
-import numpy as np
 import pytest
 import torch
 
