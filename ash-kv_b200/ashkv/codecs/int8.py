@@ -43,6 +43,68 @@ def decode_rows(codes: torch.Tensor, scales: torch.Tensor, *, out_dtype: torch.d
     return out
 
 
+class _RowKernel:
+    """A launcher with the call shape of the reference's Triton INT8 kernels.
+
+    ``kernel[grid](a, b, c, num_tokens, hidden_dim)`` runs one row per program
+    of ``grid`` (as the Triton kernel does: it never reads ``num_tokens``) over
+    contiguous buffers addressed as ``row * hidden_dim + i``.  Triton meta
+    arguments (``BLOCK_SIZE``, ``num_warps``) are accepted and ignored.
+    """
+
+    def __init__(self, launch):
+        self._launch = launch
+
+    def __getitem__(self, grid):
+        rows = int(grid[0] if isinstance(grid, (tuple, list)) else grid)
+
+        def run(a, b, c, num_tokens, hidden_dim, **_meta):
+            self._launch(rows, int(hidden_dim), a, b, c)
+        return run
+
+
+def _flat_rows(t: torch.Tensor, rows: int, L: int, what: str) -> torch.Tensor:
+    if not t.is_contiguous():
+        raise ValueError(f"{what} must be contiguous (the kernel addresses it as row * hidden_dim + i)")
+    flat = t.view(-1)
+    if flat.numel() < rows * L:
+        raise ValueError(f"{what} holds {flat.numel()} elements, fewer than {rows} rows of {L}")
+    return flat[: rows * L].view(rows, L)
+
+
+def _flat_scales(t: torch.Tensor, rows: int) -> torch.Tensor:
+    if not t.is_contiguous() or t.numel() < rows:
+        raise ValueError(f"scale buffer must be contiguous with at least {rows} entries")
+    return t.view(-1)
+
+
+def _launch_encode(rows: int, L: int, src: torch.Tensor, codes: torch.Tensor, scales: torch.Tensor) -> None:
+    if rows == 0:
+        return
+    _native.int8_encode_rows(_flat_rows(src, rows, L, "input"), _flat_rows(codes, rows, L, "code buffer"),
+                             _flat_scales(scales, rows))
+
+
+def _launch_decode(rows: int, L: int, codes: torch.Tensor, scales: torch.Tensor, dst: torch.Tensor) -> None:
+    if rows == 0:
+        return
+    _native.int8_decode_rows(_flat_rows(codes, rows, L, "code buffer"), _flat_scales(scales, rows),
+                             _flat_rows(dst, rows, L, "output"))
+
+
+_KERNELS = (_RowKernel(_launch_encode), _RowKernel(_launch_decode))
+
+
+def _get_kernels():
+    """(encode, decode) launchers in the call shape of ``_get_kernels()`` of the
+    reference (ashkv/codecs/int8.py:27-120), so code written against the Triton
+    kernels — ``encode[grid](src, int8_out, scale_out, num_tokens, hidden_dim)``
+    and ``decode[grid](int8_in, scale_in, out, num_tokens, hidden_dim)`` — runs
+    on ``ashkv_int8_encode_rows`` / ``ashkv_int8_decode_rows``.  Inputs are bf16
+    or fp16 rows; scale buffers bf16 or fp16 (one per row, flat index = row)."""
+    return _KERNELS
+
+
 class INT8Codec:
     """INT8 codec with one bf16 absmax scale per ``hidden_dim``-element row."""
 

@@ -289,61 +289,70 @@ __device__ __forceinline__ f2 div2_short(f2 a, f2 yhi, f2 ylo) { return fma2(a, 
 
 // ---------------------------------------------------------------- INT8 codec arithmetic
 // Shared by the row kernels (int8_codec.cu) and the page kernels (pages.cu);
-// restates ashkv/codecs/int8.py:70-80 (encode) and :110-115 (decode).
-//   code = sat_int8(trunc(q + copysign(0.5, q))),  q = RN(s / am)   (NaN -> 0)
-// (the reference adds +0.5 when q > 0 and -0.5 otherwise; the two differ only
-// at q = +0, where both truncate to 0).  s / am uses the per-row reciprocal
-// pair and Markstein's correction when `fast` (am within [2^-100, 2^100] and
-// s finite for every element of the row), __fdiv_rn otherwise.  When am is an
-// input value (a bf16/fp16 absmax, not the 1e-8 floor) its significand has at
-// most 11 bits and s at most 18, so the correction step is skipped (`shortq`):
-// quotients below 2^-100 in magnitude give code 0 whatever their rounding.
+// restates ashkv/codecs/int8.py:70-80 (encode) and :110-115 (decode) as the
+// reference's Triton kernel executes them on the GPU:
+//   q    = s / am, s = x * 127 rounded to the input dtype.  Triton lowers an
+//          fp32 division to PTX div.full.f32 (an approximation within 2 ulp,
+//          not IEEE division); for divisors below 2^126 that instruction equals
+//          RN(s * rcp.approx(am)) bit for bit (checked on a B200 over every bf16
+//          and every fp16 dividend/divisor pair), so rows with am < 2^126 take
+//          one reciprocal per row and one multiply per element, and larger
+//          divisors take div.full.f32 itself.
+//   code = low byte of int32(trunc(RN(q + (q > 0 ? 0.5 : -0.5))))
+//          (Triton's fp32 -> int8 cast: convert to int32, saturating, NaN -> 0,
+//          then keep the low byte; only an infinite product leaves [-128, 127]:
+//          +inf gives -1 and -inf gives 0, as the reference does).
+__device__ __forceinline__ float rcp_approx(float b) {
+  float r;
+  asm("rcp.approx.f32 %0, %1;" : "=f"(r) : "f"(b));
+  return r;
+}
+__device__ __forceinline__ float div_full(float a, float b) {
+  float r;
+  asm("div.full.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+  return r;
+}
 struct Int8Div {
   float am;
-  Recip y;
-  bool fast, shortq;
+  float r;    // rcp.approx(am)
+  bool full;  // am >= 2^126 (or not finite): div.full.f32 per element
 };
-__device__ __forceinline__ Int8Div int8_div(float am, bool s_finite) {
+__device__ __forceinline__ Int8Div int8_div(float am) {
   Int8Div d;
   d.am = am;
-  d.y = make_recip(am);
-  d.fast = s_finite && recip_ok(am);
-  d.shortq = d.fast && short_significand(am);
+  d.full = !(am < 0x1p126f);
+  d.r = rcp_approx(am);
   return d;
 }
-__device__ __forceinline__ int32_t int8_round_sat(float q) {
-  const float r = __fadd_rn(q, copysignf(0.5f, q));
+__device__ __forceinline__ float int8_quot(float s, const Int8Div& d) {
+  return d.full ? div_full(s, d.am) : __fmul_rn(s, d.r);
+}
+// int32 whose low byte is the code.
+__device__ __forceinline__ int32_t int8_round(float q) {
+  const float r = __fadd_rn(q, q > 0.0f ? 0.5f : -0.5f);
   int32_t c;
-  asm("cvt.rzi.sat.s8.f32 %0, %1;" : "=r"(c) : "f"(r));  // NaN -> 0
+  asm("cvt.rzi.s32.f32 %0, %1;" : "=r"(c) : "f"(r));  // saturating; NaN -> 0
   return c;
 }
-__device__ __forceinline__ int32_t int8_code(float s, const Int8Div& d) {
-  return int8_round_sat(d.shortq ? div_short(s, d.y) : d.fast ? div_rn(s, d.am, d.y) : __fdiv_rn(s, d.am));
-}
+__device__ __forceinline__ int32_t int8_code(float s, const Int8Div& d) { return int8_round(int8_quot(s, d)); }
 // Four bf16 inputs (two words, element 0 in the low half of w0) -> four
 // codes packed little-endian: s = bf16(x * 127) (exact product, one rounding).
 __device__ __forceinline__ uint32_t int8_codes4_bf16(uint32_t w0, uint32_t w1, const Int8Div& d) {
   const uint32_t s01 = bf16x2_mul(w0, 0x42FE42FEu);  // bf16 127.0 in both halves
   const uint32_t s23 = bf16x2_mul(w1, 0x42FE42FEu);
-  const f2 Q0 = pk2(bf16lo(s01), bf16hi(s01)), Q1 = pk2(bf16lo(s23), bf16hi(s23));
   float q[4];
-  if (d.shortq) {
-    const f2 yhi = pk2(d.y.hi, d.y.hi), ylo = pk2(d.y.lo, d.y.lo);
-    upk2(div2_short(Q0, yhi, ylo), q[0], q[1]);
-    upk2(div2_short(Q1, yhi, ylo), q[2], q[3]);
-  } else if (d.fast) {
-    const f2 yhi = pk2(d.y.hi, d.y.hi), ylo = pk2(d.y.lo, d.y.lo), nb = pk2(-d.am, -d.am);
-    upk2(div2_rn(Q0, yhi, ylo, nb), q[0], q[1]);
-    upk2(div2_rn(Q1, yhi, ylo, nb), q[2], q[3]);
+  if (!d.full) {
+    const f2 R = pk2(d.r, d.r);
+    upk2(mul2(pk2(bf16lo(s01), bf16hi(s01)), R), q[0], q[1]);
+    upk2(mul2(pk2(bf16lo(s23), bf16hi(s23)), R), q[2], q[3]);
   } else {
-    upk2(Q0, q[0], q[1]);
-    upk2(Q1, q[2], q[3]);
-#pragma unroll
-    for (int k = 0; k < 4; ++k) q[k] = __fdiv_rn(q[k], d.am);
+    q[0] = div_full(bf16lo(s01), d.am);
+    q[1] = div_full(bf16hi(s01), d.am);
+    q[2] = div_full(bf16lo(s23), d.am);
+    q[3] = div_full(bf16hi(s23), d.am);
   }
-  // each code is an int32 in [-128, 127]: its low byte is the int8 two's complement
-  const uint32_t c0 = uint32_t(int8_round_sat(q[0])), c1 = uint32_t(int8_round_sat(q[1]));
-  const uint32_t c2 = uint32_t(int8_round_sat(q[2])), c3 = uint32_t(int8_round_sat(q[3]));
+  const uint32_t c0 = uint32_t(int8_round(q[0])), c1 = uint32_t(int8_round(q[1]));
+  const uint32_t c2 = uint32_t(int8_round(q[2])), c3 = uint32_t(int8_round(q[3]));
   return __byte_perm(__byte_perm(c0, c1, 0x0040), __byte_perm(c2, c3, 0x0040), 0x5410);
 }
 // Decode: v = RN(RN(float(code) * scale) / 127).  `fast` when the scale is

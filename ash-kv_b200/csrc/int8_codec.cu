@@ -65,14 +65,6 @@ __device__ __forceinline__ float scaled127(float x, bool fp32_product) {
   else return __bfloat162float(__float2bfloat16_rn(p));
 }
 
-// s = x * 127 stays finite for every x of a row whose absmax is am: always for
-// an fp32 product and for bf16 rows in the fast divisor range; fp16 rows need
-// 127 * am below the fp16 maximum.
-template <bool FP16>
-__device__ __forceinline__ bool products_finite(float am, bool fp32_product) {
-  return !FP16 || fp32_product || am < 515.0f;
-}
-
 // Byte offset of row r's scale: (r / sps) * slot_stride + (r % sps) * 2, with
 // shifts when sps is a power of two (the plain array and the hooks' head counts).
 __device__ __forceinline__ int64_t scale_offset(int64_t r, int32_t sps, int32_t sps_shift, int64_t slot_stride) {
@@ -144,7 +136,7 @@ __device__ __forceinline__ void encode_loaded_row(const Int8EncParams& p, int64_
 
   uint8_t* out = p.codes + r * p.codes_stride;
   const bool f32p = p.fp32_product != 0;
-  const Int8Div d = int8_div(am, products_finite<FP16>(am, f32p));
+  const Int8Div d = int8_div(am);
 #pragma unroll
   for (int c = 0; c < NCH; ++c) {
     const uint32_t w[4] = {L.chunk[c].x, L.chunk[c].y, L.chunk[c].z, L.chunk[c].w};
@@ -212,7 +204,7 @@ __global__ void __launch_bounds__(256) int8_encode_generic_kernel(const Int8EncP
     *reinterpret_cast<uint16_t*>(sp) = p.scale_fp16 ? f32_to_f16(am) : f32_to_bf16(am);
   }
   uint8_t* out = p.codes + r * p.codes_stride;
-  const Int8Div d = int8_div(am, products_finite<FP16>(am, p.fp32_product != 0));
+  const Int8Div d = int8_div(am);
   for (int i = lane; i < p.row_len; i += 32) {
     const uint32_t w = row[i];
     out[i] = uint8_t(int8_code(scaled127<FP16>(in_lo<FP16>(w), p.fp32_product != 0), d) & 0xFF);

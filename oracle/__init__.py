@@ -9,7 +9,13 @@ only ``tests/``, ``__graft_entry__.smoke()`` and ``bench.py``'s
 Parity status: pinned.  ``tests/golden/`` holds fixtures produced by running
 the reference's own Python code (N-bit/INT2 codecs with an injected dither,
 score/controller, checksum) and its Triton INT8 kernel under the Triton
-interpreter; ``tests/test_oracle_golden.py`` checks this oracle against them.
+interpreter, and fixtures produced on a B200 by the reference's Triton INT8
+kernels, its SGLang hooks, its simulator's attention mass and its N-bit codecs
+run natively on CUDA (``tests/golden/make_golden_gpu.py``);
+``tests/test_oracle_golden.py`` checks this oracle against all of them.  One
+operation is restated up to ties: the Triton INT8 kernel divides with the
+GPU's approximate ``div.full.f32``, the oracle exactly, and its tie mask marks
+the elements where that can move a code by one.
 
 Restated reference functions (paths relative to the ASH-KV source tree):
 
@@ -45,7 +51,7 @@ def lib() -> ctypes.CDLL:
         L = ctypes.CDLL(str(path))
         P = ctypes.c_void_p
         i64, i32, f32, u64 = ctypes.c_int64, ctypes.c_int32, ctypes.c_float, ctypes.c_uint64
-        L.oracle_int8_encode.argtypes = [P, i32, i64, i32, i32, P, P, i32]
+        L.oracle_int8_encode.argtypes = [P, i32, i64, i32, i32, P, P, i32, P]
         L.oracle_int8_decode.argtypes = [P, P, i32, i64, i32, P, i32]
         L.oracle_nbit_encode.argtypes = [P, i64, i32, f32, P, P, P, P]
         L.oracle_nbit_decode.argtypes = [P, P, i64, i32, P, P, i64, P]
@@ -71,16 +77,33 @@ def _p(a: np.ndarray):
 
 # --------------------------------------------------------------------- INT8
 def int8_encode(x_bits: np.ndarray, row_len: int, src_fp16: bool = False, scale_fp16: bool = False,
-                fp32_product: bool = False) -> tuple[np.ndarray, np.ndarray]:
-    """Rows of ``row_len`` bf16/fp16 values (uint16 bits) -> (int8 codes, uint16 scale bits)."""
+                fp32_product: bool = False, with_ties: bool = False):
+    """Rows of ``row_len`` bf16/fp16 values (uint16 bits) -> (int8 codes, uint16 scale bits)
+    [, tie mask].  The oracle divides exactly; the reference's Triton kernel uses
+    the GPU's approximate ``div.full.f32``.  The tie mask marks the elements whose
+    exact quotient lies so close to a half-integer that the two can give codes
+    one apart (see :func:`int8_codes_agree`)."""
     x = np.ascontiguousarray(x_bits, dtype=np.uint16).reshape(-1)
     n_rows = x.size // row_len
     codes = np.empty(n_rows * row_len, dtype=np.int8)
     scales = np.empty(n_rows, dtype=np.uint16)
+    tie = np.zeros(n_rows * row_len, dtype=np.uint8)
     if n_rows:
         lib().oracle_int8_encode(_p(x), int(src_fp16), n_rows, row_len, int(fp32_product), _p(codes),
-                                 _p(scales), int(scale_fp16))
+                                 _p(scales), int(scale_fp16), _p(tie))
+    if with_ties:
+        return codes.reshape(n_rows, row_len), scales, tie.reshape(n_rows, row_len).astype(bool)
     return codes.reshape(n_rows, row_len), scales
+
+
+def int8_codes_agree(got: np.ndarray, want: np.ndarray, tie: np.ndarray) -> tuple[bool, int]:
+    """(every code equals the oracle's, or differs by one at a tie-zone element; number of such ties)."""
+    g = np.asarray(got).view(np.int8).astype(np.int16).reshape(-1)
+    w = np.asarray(want).view(np.int8).astype(np.int16).reshape(-1)
+    t = np.asarray(tie, dtype=bool).reshape(-1)
+    diff = g != w
+    ok = not np.any(diff & ~(t & (np.abs(g - w) == 1)))
+    return ok, int(np.count_nonzero(diff))
 
 
 def int8_decode(codes: np.ndarray, scales: np.ndarray, scale_fp16: bool = False,

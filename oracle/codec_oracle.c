@@ -78,17 +78,28 @@ static float in_val(const uint16_t* src, int64_t i, int fp16) {
   return fp16 ? oracle_f16_to_f32(src[i]) : bf16_to_f32(src[i]);
 }
 
-static int32_t sat_trunc_s8(float r) {
-  if (isnan(r)) return 0;
-  if (r >= 127.0f) return 127;
-  if (r <= -128.0f) return -128;
-  return (int32_t)r; /* C cast truncates toward zero */
+/* Triton's fp32 -> int8 cast on the GPU: truncate to int32 (saturating, NaN
+ * -> 0), keep the low byte.  Only an infinite product leaves [-128, 127]:
+ * +inf gives -1 and -inf gives 0 (pinned by the B200 reference fixtures). */
+static int8_t triton_cast_s8(float r) {
+  int32_t v;
+  if (isnan(r)) v = 0;
+  else if (r >= 2147483648.0f) v = INT32_MAX;
+  else if (r <= -2147483648.0f) v = INT32_MIN;
+  else v = (int32_t)r; /* C cast truncates toward zero */
+  return (int8_t)(uint8_t)((uint32_t)v & 0xFFu);
 }
 
 /* Per row: am = max(max|x| (NaN ignored), 1e-8); s = x*127 rounded to the
- * input dtype (fp32 if fp32_product); code = sat(trunc(s/am +- 0.5)). */
+ * input dtype (fp32 if fp32_product); code = cast(trunc(s/am +- 0.5)).
+ *
+ * The reference's Triton kernel divides with PTX div.full.f32, an
+ * approximation within 2 ulp whose exact results this CPU restatement cannot
+ * reproduce; it divides exactly and, when `tie` is given, sets tie[i] = 1 for
+ * every element whose exact quotient lies within 2^-20 * max(|q|, 1) of a
+ * half-integer.  Only there can the two divisions give codes one apart. */
 void oracle_int8_encode(const uint16_t* src, int src_fp16, int64_t n_rows, int32_t row_len,
-                        int fp32_product, int8_t* codes, uint16_t* scales, int scale_fp16) {
+                        int fp32_product, int8_t* codes, uint16_t* scales, int scale_fp16, uint8_t* tie) {
   for (int64_t r = 0; r < n_rows; ++r) {
     const uint16_t* row = src + r * row_len;
     float am = 0.0f;
@@ -108,7 +119,12 @@ void oracle_int8_encode(const uint16_t* src, int src_fp16, int64_t n_rows, int32
       else s = bf16_to_f32(oracle_f32_to_bf16(p));
       float q = s / am;
       float rr = q + (q > 0.0f ? 0.5f : -0.5f);
-      codes[r * row_len + i] = (int8_t)sat_trunc_s8(rr);
+      codes[r * row_len + i] = triton_cast_s8(rr);
+      if (tie) {
+        const double aq = fabs((double)s / (double)am);
+        const double f = aq - floor(aq);
+        tie[r * row_len + i] = (uint8_t)(isfinite(aq) && fabs(f - 0.5) <= ldexp(1.0, -20) * fmax(aq, 1.0));
+      }
     }
   }
 }

@@ -1,8 +1,13 @@
 """GPU parity: the sm_100a codec kernels (through the C ABI) against the oracle.
 
 Integer/byte outputs (codes, scales, outlier lists, packed blobs, decoded
-bf16 bits) must be bit-exact.  The oracle itself is pinned to the
-reference's outputs by tests/test_oracle_golden.py.
+bf16 bits) must be bit-exact, with one exception: INT8 codes may be one apart
+from the oracle's at tie-zone elements (the reference divides with the GPU's
+approximate div.full.f32, which this library reproduces and the CPU oracle
+cannot; see ``conftest.assert_int8_codes``).  The oracle itself is pinned to
+the reference's outputs by tests/test_oracle_golden.py, and the kernels are
+compared with the reference's own B200 outputs, exactly, by
+tests/test_gpu_reference_fixtures.py.
 """
 from __future__ import annotations
 
@@ -11,7 +16,7 @@ import pytest
 import torch
 
 import oracle
-from conftest import GOLDEN
+from conftest import GOLDEN, assert_int8_codes
 
 from ashkv import _native
 from ashkv.codecs import DitheredINT2Codec, DitheredNBitCodec, INT8Codec
@@ -49,14 +54,15 @@ def test_int8_rows_bitexact(cuda, dtype, row_len, fp32_product):
     codes = torch.empty(n_rows, row_len, dtype=torch.int8, device=cuda)
     scales = torch.empty(n_rows, dtype=dtype, device=cuda)
     _native.int8_encode_rows(x.to(cuda), codes, scales, fp32_product=fp32_product)
-    oc, osc = oracle.int8_encode(bits_of(x), row_len, src_fp16=dtype == torch.float16,
-                                 scale_fp16=dtype == torch.float16, fp32_product=fp32_product)
-    assert np.array_equal(codes.cpu().numpy(), oc)
+    oc, osc, tie = oracle.int8_encode(bits_of(x), row_len, src_fp16=dtype == torch.float16,
+                                      scale_fp16=dtype == torch.float16, fp32_product=fp32_product, with_ties=True)
+    got = codes.cpu().numpy()
+    assert_int8_codes(got, oc, tie)
     assert np.array_equal(bits_of(scales), osc)
     for out_dtype in (torch.bfloat16, torch.float16):
         dec = torch.empty(n_rows, row_len, dtype=out_dtype, device=cuda)
         _native.int8_decode_rows(codes, scales, dec)
-        want = oracle.int8_decode(oc, osc, scale_fp16=dtype == torch.float16, dst_fp16=out_dtype == torch.float16)
+        want = oracle.int8_decode(got, osc, scale_fp16=dtype == torch.float16, dst_fp16=out_dtype == torch.float16)
         assert np.array_equal(bits_of(dec), want.reshape(-1))
 
 
@@ -89,8 +95,9 @@ def test_int8_rows_every_quotient_of_a_binade(cuda, L):
     x = torch.from_numpy(bits.view(np.int16)).view(torch.bfloat16).to(cuda)
     for sdt in (torch.bfloat16, torch.float16):
         codes, scales = int8_mod.encode_rows(x, scale_dtype=sdt)
-        oc, osc = oracle.int8_encode(bits, L, scale_fp16=sdt == torch.float16)
-        assert np.array_equal(codes.cpu().numpy(), oc)
+        oc, osc, tie = oracle.int8_encode(bits, L, scale_fp16=sdt == torch.float16, with_ties=True)
+        n_ties = assert_int8_codes(codes.cpu().numpy(), oc, tie)
+        assert n_ties <= 0.001 * oc.size, n_ties
         assert np.array_equal(bits_of(scales), osc)
 
 
@@ -115,8 +122,11 @@ def test_int8_kernel_matches_reference_golden(cuda, ci):
     _native.int8_encode_rows(src.to(cuda), codes, scales)
     got = codes.cpu().numpy()
     x = src.float().numpy()
-    overflow = np.abs(x) * 127.0 > 65504.0  # fp16 product is inf: the reference cast is undefined there
-    assert np.array_equal(got[~overflow], INT8[pre + "codes"][~overflow])
+    # fp16 product is inf: the interpreter's cast of that differs from the GPU's
+    overflow = np.abs(x) * 127.0 > 65504.0
+    # the interpreter divides exactly, the GPU kernel as Triton does on the device
+    _, _, tie = oracle.int8_encode(INT8[pre + "src"], L, src_fp16=True, scale_fp16=True, with_ties=True)
+    assert_int8_codes(got[~overflow], INT8[pre + "codes"][~overflow], tie[~overflow])
     assert np.array_equal(bits_of(scales), INT8[pre + "scales"])
 
 
@@ -133,15 +143,16 @@ def test_int8_gather_and_flat_scale_slots(cuda):
     scales_base = staging.view(-1)[:].view(torch.float16)  # scale t at byte (t//H)*slot + 2*(t%H)
     _native.int8_encode_rows(pool, codes_view, scales_base, row_index=idx, scales_per_slot=H,
                              scale_slot_stride=slot)
-    oc, osc = oracle.int8_encode(bits_of(pool[idx.cpu()]), L, scale_fp16=True)
+    oc, osc, tie = oracle.int8_encode(bits_of(pool[idx.cpu()]), L, scale_fp16=True, with_ties=True)
     st = staging.cpu().numpy()
-    assert np.array_equal(st[:, 2 * H:2 * H + L].view(np.int8), oc)
+    got = st[:, 2 * H:2 * H + L].view(np.int8)
+    assert_int8_codes(got, oc, tie)
     flat = st[:, :2 * H].copy().view(np.uint16).reshape(-1)  # concatenated per-slot scale regions
     assert np.array_equal(flat[:n], osc)
     # decode straight back into a scattered destination
     out = torch.zeros(cap, L, dtype=torch.bfloat16, device=cuda)
     _native.int8_decode_rows(codes_view, scales_base, out, row_index=idx, scales_per_slot=H, scale_slot_stride=slot)
-    want = oracle.int8_decode(oc, osc, scale_fp16=True)
+    want = oracle.int8_decode(got, osc, scale_fp16=True)
     assert np.array_equal(bits_of(out[idx]).reshape(n, L), want)
 
 
@@ -149,10 +160,12 @@ def test_int8_codec_bytes_api_matches_oracle(cuda):
     x = rand_bf16(123 * 128 + 5, 9)  # ragged tail: trailing values are dropped
     codec = INT8Codec()
     blob = codec.encode(bits_of(x).tobytes())
-    oc, osc = oracle.int8_encode(bits_of(x)[:123 * 128], 128)
-    assert blob == oracle.int8_blob(oc, osc)
+    oc, osc, tie = oracle.int8_encode(bits_of(x)[:123 * 128], 128, with_ties=True)
+    assert blob[:4 + 2 * 123] == oracle.int8_blob(oc, osc)[:4 + 2 * 123] and len(blob) == 4 + 123 * 130
+    got = np.frombuffer(blob, np.int8, 123 * 128, 4 + 2 * 123).reshape(123, 128)
+    assert_int8_codes(got, oc, tie)
     dec = codec.decode(blob)
-    assert dec == oracle.int8_decode(oc, osc).tobytes()
+    assert dec == oracle.int8_decode(got, osc).tobytes()
     assert codec.encode(b"") == b"\x00\x00\x00\x00"
     assert codec.encode(b"\x00\x01" * 10) == b"\x00\x00\x00\x00"
     assert codec.decode(b"\x00\x00\x00\x00") == b"" and codec.decode(b"\x01") == b""
@@ -183,8 +196,9 @@ def test_int8_nan_inf_do_not_crash(cuda):
 
 @pytest.mark.parametrize("L", [128, 1024, 32])
 def test_int8_rows_with_nan_and_inf_match_oracle(cuda, L):
-    """NaN is ignored by the row maximum (and codes 0); +-inf rows take the exact
-    division path; an all-NaN row falls to the 1e-8 floor."""
+    """NaN is ignored by the row maximum (and codes 0); a row whose absmax is
+    infinite divides with div.full.f32 (every finite value gives 0); an all-NaN
+    row falls to the 1e-8 floor."""
     g = torch.Generator().manual_seed(5)
     x = torch.randn(64, L, generator=g).to(torch.bfloat16)
     b = x.view(torch.int16).numpy().view(np.uint16).copy()
@@ -198,8 +212,8 @@ def test_int8_rows_with_nan_and_inf_match_oracle(cuda, L):
     xb = torch.from_numpy(b.view(np.int16)).view(torch.bfloat16).to(cuda)
     for sdt in (torch.bfloat16, torch.float16):
         codes, scales = int8_mod.encode_rows(xb, scale_dtype=sdt)
-        oc, osc = oracle.int8_encode(b, L, scale_fp16=sdt == torch.float16)
-        assert np.array_equal(codes.cpu().numpy(), oc)
+        oc, osc, tie = oracle.int8_encode(b, L, scale_fp16=sdt == torch.float16, with_ties=True)
+        assert_int8_codes(codes.cpu().numpy(), oc, tie)
         assert np.array_equal(bits_of(scales), osc)
 
 
