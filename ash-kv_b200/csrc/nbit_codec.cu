@@ -22,6 +22,7 @@
 #include <mutex>
 
 #include "common.cuh"
+#include "nbit_group.cuh"
 
 namespace ashkv {
 namespace {
@@ -30,22 +31,6 @@ constexpr int kThreads = 256;                     // 8 warps per CTA
 constexpr int kWarps = kThreads / 32;
 static_assert(ASHKV_NBIT_BUCKET_GROUPS == 32, "one bucket per warp, one group per lane");
 
-struct NbitEncParams {
-  const uint16_t* src;
-  int64_t n_groups;
-  const float* dither;
-  uint32_t round_keys[20];  // Philox key schedule: (k0 + r*W0, k1 + r*W1) for r = 0..9
-  uint64_t seed;
-  uint64_t dither_offset;
-  float sigma;
-  float half_states;
-  uint16_t* scales;
-  uint8_t* codes;
-  uint32_t* bucket_counts;
-  uint32_t* bucket_entries;
-  int32_t bucket_cap;
-  uint32_t* status;
-};
 
 struct NbitDecParams {
   const uint16_t* scales;
@@ -59,278 +44,6 @@ struct NbitDecParams {
   uint32_t* status;
 };
 
-// One thread per 32-element group, one warp (32 groups) per outlier bucket.
-//
-// Outlier decisions are made against the reference threshold without
-// computing its fp64 variance in the common case: an fp32 variance with a
-// rigorous error bound gives thr_lo <= thr <= thr_hi.  If every |x - mu| of
-// the group is <= thr_lo the group has no outliers (the usual case).
-// Otherwise per-element masks against thr_lo and thr_hi are built; if they
-// agree, that is the exact mask, and only if some |x - mu| falls between the
-// two bounds is the exact fp64 threshold computed.
-// A group's 32 bf16 values as 4 chunks of 8 (16 bytes each), plus access to
-// element e of the group owned by another lane of the warp.
-struct RegGroup {  // held in registers; other groups read back from global memory
-  const uint32_t* w;
-  const uint16_t* src;  // the kernel's source (group g at src + 32 g)
-  int64_t g0;           // group of lane 0 of the warp
-  __device__ __forceinline__ uint4 chunk(int c) const { return make_uint4(w[4 * c], w[4 * c + 1], w[4 * c + 2], w[4 * c + 3]); }
-  __device__ __forceinline__ uint32_t elem(int owner_lane, int e) const { return src[(g0 + owner_lane) * 32 + e]; }
-};
-struct SmemGroup {  // rows of a 64-byte-swizzled shared-memory tile (the warp's bucket), one per lane
-  uint32_t tile, row, sw;
-  __device__ __forceinline__ uint4 chunk(int c) const { return lds128(row + 16u * (uint32_t(c) ^ sw)); }
-  __device__ __forceinline__ uint32_t elem(int owner_lane, int e) const {
-    const uint32_t osw = uint32_t(owner_lane >> 1) & 3u;
-    const uint32_t a = tile + uint32_t(owner_lane) * 64u + 16u * ((uint32_t(e) >> 3) ^ osw) + 2u * (uint32_t(e) & 7u);
-    uint16_t v;
-    asm volatile("ld.shared.u16 %0, [%1];" : "=h"(v) : "r"(a));
-    return v;
-  }
-};
-
-// Hardware square-root approximation (relative error below 2^-21).
-__device__ __forceinline__ float sqrt_approx(float x) {
-  float r;
-  asm("sqrt.approx.f32 %0, %1;" : "=f"(r) : "f"(x));
-  return r;
-}
-
-// Two signed 16-bit integers clamped to [0, hi]: max(min(v, hi), 0) per half.
-__device__ __forceinline__ uint32_t clamp_codes_s16x2(uint32_t v, uint32_t hi) {
-  uint32_t r;
-  asm("min.relu.s16x2 %0, %1, %2;" : "=r"(r) : "r"(v), "r"(hi | (hi << 16)));
-  return r;
-}
-
-__device__ __forceinline__ double warp_sum_f64(double v) {  // pairwise (butterfly) order, same in every lane
-#pragma unroll
-  for (int off = 1; off < 32; off <<= 1) v = __dadd_rn(v, __shfl_xor_sync(0xFFFFFFFFu, v, off));
-  return v;
-}
-__device__ __forceinline__ float warp_max_abs_nan(float v) {
-  v = fabsf(v);
-#pragma unroll
-  for (int off = 16; off > 0; off >>= 1) v = max_nan(v, __shfl_xor_sync(0xFFFFFFFFu, v, off));
-  return v;
-}
-
-template <typename Src>
-__device__ __forceinline__ void chunk_pairs(const Src& src, int c, f2 (&P)[4]) {
-  const uint4 q = src.chunk(c);
-  P[0] = pk2(bf16lo(q.x), bf16hi(q.x));
-  P[1] = pk2(bf16lo(q.y), bf16hi(q.y));
-  P[2] = pk2(bf16lo(q.z), bf16hi(q.z));
-  P[3] = pk2(bf16lo(q.w), bf16hi(q.w));
-}
-
-// Encodes one group (writes its packed codes and bf16 delta) and returns the
-// outlier bit mask.  The group is re-read from `src` for each pass so only
-// one 8-element chunk is live in registers at a time.
-template <int BITS, int DMODE, typename Src>
-__device__ __forceinline__ uint32_t encode_group(const Src& src, const NbitEncParams& p, int64_t g, bool active) {
-  constexpr uint32_t kMaxCode = (1u << BITS) - 1u;
-  // ---- mean: acc[i] = ((x_i + x_{8+i}) + x_{16+i}) + x_{24+i}, then acc[0] + ... + acc[7]
-  //      in order (PyTorch's CPU reduction order for a 32-wide inner dimension).
-  f2 A[4];
-  chunk_pairs(src, 0, A);
-#pragma unroll
-  for (int c = 1; c < 4; ++c) {
-    f2 P[4];
-    chunk_pairs(src, c, P);
-#pragma unroll
-    for (int i = 0; i < 4; ++i) A[i] = add2(A[i], P[i]);
-  }
-  float acc[8];
-#pragma unroll
-  for (int i = 0; i < 4; ++i) upk2(A[i], acc[2 * i], acc[2 * i + 1]);
-  float s = acc[0];
-#pragma unroll
-  for (int i = 1; i < 8; ++i) s = __fadd_rn(s, acc[i]);
-  const float mu = __fmul_rn(s, 0.03125f);
-
-  // ---- fp32 variance estimate, max|x - mu|, max|x| (NaN-propagating)
-  const f2 NMU = pk2(-mu, -mu);
-  f2 M2 = pk2(0.0f, 0.0f);
-  float dmax = 0.0f, xmax = 0.0f;
-#pragma unroll
-  for (int c = 0; c < 4; ++c) {
-    f2 P[4];
-    chunk_pairs(src, c, P);
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const f2 D = add2(P[i], NMU);
-      M2 = fma2(D, D, M2);
-      float d0, d1, x0, x1;
-      upk2(D, d0, d1);
-      upk2(P[i], x0, x1);
-      dmax = max3_abs_nan(dmax, d0, d1);
-      xmax = max3_abs_nan(xmax, x0, x1);
-    }
-  }
-  float m2a, m2b;
-  upk2(M2, m2a, m2b);
-  const float m2 = __fadd_rn(m2a, m2b);
-
-  // Bounds on the reference threshold.  m2 has relative error < 2^-19 w.r.t.
-  // sum (x - mu32)^2, which exceeds the exact M2 by 32 (mu - mu32)^2 with
-  // |mu - mu32| <= 31 * 2^-24 * max|x|.  The bounds only choose between the
-  // fast and the exact outlier path, so they are evaluated with approximate
-  // operations: the product by RN(1/31) and sqrt.approx each err by less than
-  // 2^-21 relative (a flushed subnormal only lowers a bound by far less than
-  // the 1e-8 term's margin), and margins of 2^-16 on m2 and 2^-12 on the
-  // threshold cover them together with the other roundings (fp32 bound
-  // arithmetic, the fp32 rounding of sd, + 1e-8 and * sigma in the reference).
-  const float sigma = p.sigma;
-  const bool bounds_ok = sigma > 0.0f && isfinite(m2) && isfinite(xmax);
-  float thr_lo = 0.0f, thr_hi = 0.0f;
-  if (bounds_ok) {
-    const float emu = 31.0001f * 0x1p-24f * xmax;
-    const float m2_hi = m2 * (1.0f + 0x1p-16f);
-    const float m2_lo = fmaxf(m2 * (1.0f - 0x1p-16f) - 32.0f * emu * emu * (1.0f + 0x1p-16f), 0.0f);
-    constexpr float kInv31 = 1.0f / 31.0f;
-    thr_hi = sigma * (sqrt_approx(m2_hi * kInv31) + 1e-8f) * (1.0f + 0x1p-12f);
-    thr_lo = sigma * (sqrt_approx(m2_lo * kInv31) + 1e-8f) * (1.0f - 0x1p-12f);
-  }
-  // Groups whose max |x - mu| exceeds thr_lo are resolved by the whole warp,
-  // one group at a time: lane e takes element e, masks come from ballots, and
-  // if an |x - mu| lies between the bounds the exact threshold is computed
-  // (fp64, pairwise order over the 32 elements).
-  uint32_t omask = 0;
-  float am = xmax;
-  const int lane = threadIdx.x & 31;
-  uint32_t todo = __ballot_sync(0xFFFFFFFFu, active && !(bounds_ok && dmax <= thr_lo));
-  while (todo) {
-    const int owner = __ffs(todo) - 1;
-    todo &= todo - 1;
-    const float mu_o = __shfl_sync(0xFFFFFFFFu, mu, owner);
-    const float lo_o = __shfl_sync(0xFFFFFFFFu, thr_lo, owner);
-    const float hi_o = __shfl_sync(0xFFFFFFFFu, thr_hi, owner);
-    const bool ok_o = __shfl_sync(0xFFFFFFFFu, int(bounds_ok), owner) != 0;
-    const float x = bf16_to_f32(uint16_t(src.elem(owner, lane)));
-    const float d = fabsf(__fadd_rn(x, -mu_o));
-    const uint32_t mlo = __ballot_sync(0xFFFFFFFFu, d > lo_o);
-    uint32_t m = __ballot_sync(0xFFFFFFFFu, d > hi_o);
-    if (!ok_o || mlo != m) {
-      const double s64 = warp_sum_f64(double(x));
-      const double e = __dadd_rn(double(x), -__dmul_rn(s64, 0.03125));
-      const double m2e = warp_sum_f64(__dmul_rn(e, e));
-      const float sd = __double2float_rn(__dsqrt_rn(__ddiv_rn(m2e, 31.0)));
-      const float thr = __fmul_rn(sigma, __fadd_rn(sd, 1e-8f));
-      m = __ballot_sync(0xFFFFFFFFu, d > thr);
-    }
-    const float amv = warp_max_abs_nan((m >> lane) & 1u ? mu_o : x);
-    if (lane == owner) {
-      omask = m;
-      am = amv;
-    }
-  }
-  if (!active) omask = 0;
-  if (!(am >= 1e-8f) && am == am) am = 1e-8f;  // clamp(min=1e-8); NaN propagates
-  const float delta = __fdiv_rn(am, p.half_states);
-
-  // ---- dither, quantise (x' + (U-0.5)*delta) / delta + half, pack
-  const Recip y = make_recip(delta);
-  const bool fast_div = recip_ok(delta);
-  const f2 DELTA = pk2(delta, delta), YHI = pk2(y.hi, y.hi), YLO = pk2(y.lo, y.lo), NDELTA = pk2(-delta, -delta);
-  const float half = p.half_states;
-  const f2 HALF = pk2(half, half), MAGIC = pk2(12582912.0f, 12582912.0f);
-  uint32_t o[BITS];  // packed codes: 32 * BITS bits, MSB-first within each byte
-#pragma unroll
-  for (int k = 0; k < BITS; ++k) o[k] = 0u;
-#pragma unroll
-  for (int c = 0; c < 4; ++c) {  // 8 elements per chunk / Philox draw
-    f2 P[4];
-    chunk_pairs(src, c, P);
-    if (omask & (0xFFu << (8 * c))) {
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        float x0, x1;
-        upk2(P[i], x0, x1);
-        const int e = 8 * c + 2 * i;
-        P[i] = pk2((omask >> e) & 1u ? mu : x0, (omask >> (e + 1)) & 1u ? mu : x1);
-      }
-    }
-    f2 DZ[4];
-    if constexpr (DMODE == ASHKV_DITHER_TENSOR) {
-      U8 u;
-      if (active) u = ld_nc_v8(p.dither + g * 32 + 8 * c);
-      else {
-#pragma unroll
-        for (int k = 0; k < 8; ++k) u.v[k] = 0x3F000000u;  // 0.5 -> zero dither
-      }
-#pragma unroll
-      for (int h = 0; h < 4; ++h)
-        DZ[h] = add2(pk2(__uint_as_float(u.v[2 * h]), __uint_as_float(u.v[2 * h + 1])), pk2(-0.5f, -0.5f));
-    } else {
-      const uint64_t ctr = ((p.dither_offset + uint64_t(g) * 32) >> 3) + c;
-      const Philox4 r = philox4x32_10_rk(uint32_t(ctr), uint32_t(ctr >> 32), 0u, 0u, p.round_keys);
-#pragma unroll
-      for (int h = 0; h < 4; ++h) {
-        // f = 1 + h16 * 2^-23, so U - 0.5 = 128 f - 128.5 exactly
-        const float flo = __uint_as_float(__byte_perm(r.v[h], 0x3F800000u, 0x7610));
-        const float fhi = __uint_as_float(__byte_perm(r.v[h], 0x3F800000u, 0x7632));
-        DZ[h] = fma2(pk2(flo, fhi), pk2(128.0f, 128.0f), pk2(-128.5f, -128.5f));
-      }
-    }
-    // v = RN(RN(a / delta) + half), a = x' + noise; code = clamp(rint(v), 0, 2^bits - 1).
-    // rint: RN(v + 1.5 * 2^23) leaves rint(v) in the low mantissa bits (|v| < 2^22).
-    // With delta in Markstein's range every a is finite and |a / delta| <= half + 1,
-    // so the clamp runs on the integers (two codes per s16x2 word); otherwise the
-    // float clamp comes first (NaN -> 0), as in the reference.
-    f2 Q[4];
-#pragma unroll
-    for (int h = 0; h < 4; ++h) Q[h] = add2(P[h], mul2(DZ[h], DELTA));  // a = x' + noise
-    if (fast_div) {
-#pragma unroll
-      for (int h = 0; h < 4; ++h) Q[h] = add2(add2(div2_rn(Q[h], YHI, YLO, NDELTA), HALF), MAGIC);
-    } else {
-#pragma unroll
-      for (int h = 0; h < 4; ++h) {
-        float a0, a1;
-        upk2(Q[h], a0, a1);
-        const float v0 = fminf(fmaxf(__fadd_rn(__fdiv_rn(a0, delta), half), 0.0f), float(kMaxCode));
-        const float v1 = fminf(fmaxf(__fadd_rn(__fdiv_rn(a1, delta), half), 0.0f), float(kMaxCode));
-        Q[h] = add2(pk2(v0, v1), MAGIC);
-      }
-    }
-    uint32_t W[4];  // codes of elements 2h (low half) and 2h + 1 (high half)
-#pragma unroll
-    for (int h = 0; h < 4; ++h) {
-      float t0, t1;
-      upk2(Q[h], t0, t1);
-      W[h] = clamp_codes_s16x2(__byte_perm(__float_as_uint(t0), __float_as_uint(t1), 0x5410), kMaxCode);
-    }
-    // bytes c0..c3 of elements 8c..8c+3, and c4..c7
-    const uint32_t X = __byte_perm(W[0], W[1], 0x6420), Y = __byte_perm(W[2], W[3], 0x6420);
-    if constexpr (BITS == 8) {
-      o[2 * c] = X;
-      o[2 * c + 1] = Y;
-    } else if constexpr (BITS == 4) {
-      // byte j of X*16 + (X >> 8) is (c_j << 4) + c_{j+1}: keep bytes 0 and 2 of each half.
-      o[c] = __byte_perm(X * 16u + (X >> 8), Y * 16u + (Y >> 8), 0x6420);
-    } else {
-      const uint32_t tx = X * 4u + (X >> 8), ty = Y * 4u + (Y >> 8);   // bytes 0, 2: c0c1, c2c3
-      const uint32_t ux = tx * 16u + (tx >> 16), uy = ty * 16u + (ty >> 16);  // byte 0: c0c1c2c3
-      o[c >> 1] |= (__byte_perm(ux, uy, 0x0040) & 0xFFFFu) << (16 * (c & 1));
-    }
-  }
-
-  if (active) {
-    p.scales[g] = f32_to_bf16(delta);
-    if constexpr (BITS == 4) {
-      st_cs_v4(p.codes + g * 16, make_uint4(o[0], o[1], o[2], o[3]));
-    } else if constexpr (BITS == 2) {
-      *reinterpret_cast<uint2*>(p.codes + g * 8) = make_uint2(o[0], o[1]);
-    } else {
-      U8 ov;
-#pragma unroll
-      for (int k = 0; k < 8; ++k) ov.v[k] = o[k];
-      st_cs_v8(p.codes + g * 32, ov);
-    }
-  }
-  return omask;
-}
 
 // Append this lane's outliers (bits of omask) to the warp's bucket; the
 // ranks come from a warp scan, so the list is in ascending element order.
@@ -463,73 +176,6 @@ __global__ void __launch_bounds__(kThreads, 4) nbit_encode_tma_kernel(const __gr
   }
 }
 
-// One group's packed codes (32 * BITS bits, MSB-first within each byte) and its delta.
-template <int BITS>
-struct GroupCodes {
-  uint32_t w[BITS];
-  float delta;
-};
-template <int BITS>
-__device__ __forceinline__ void load_group(const uint16_t* scales, const uint8_t* codes, int64_t g,
-                                           GroupCodes<BITS>& gc) {
-  gc.delta = bf16_to_f32(scales[g]);
-  if constexpr (BITS == 4) {
-    const uint4 v = *reinterpret_cast<const uint4*>(codes + g * 16);
-    gc.w[0] = v.x; gc.w[1] = v.y; gc.w[2] = v.z; gc.w[3] = v.w;
-  } else if constexpr (BITS == 2) {
-    const uint2 v = *reinterpret_cast<const uint2*>(codes + g * 8);
-    gc.w[0] = v.x; gc.w[1] = v.y;
-  } else {
-    const uint4 a = *reinterpret_cast<const uint4*>(codes + g * 32);
-    const uint4 b = *reinterpret_cast<const uint4*>(codes + g * 32 + 16);
-    gc.w[0] = a.x; gc.w[1] = a.y; gc.w[2] = a.z; gc.w[3] = a.w;
-    gc.w[4] = b.x; gc.w[5] = b.y; gc.w[6] = b.z; gc.w[7] = b.w;
-  }
-}
-
-// Byte j of m (a code < 256) as the float 2^23 + code.
-__device__ __forceinline__ float code_plus_2p23(uint32_t m, int j) {
-  return __uint_as_float(__byte_perm(m, 0x4B000000u, 0x7540u + uint32_t(j)));
-}
-
-// out = bf16((code - half) * delta) for the 32 elements of a group:
-// float(code) = (2^23 + code) - 2^23 exactly, then the reference's two roundings.
-template <int BITS>
-__device__ __forceinline__ void store_group(const GroupCodes<BITS>& gc, float half, uint16_t* out) {
-  const f2 DEL = pk2(gc.delta, gc.delta), NH = pk2(-half, -half), N23 = pk2(-8388608.0f, -8388608.0f);
-  uint32_t o[16];
-  auto pair = [&](float a, float b) { return f32x2_to_bf16x2_pk(mul2(add2(add2(pk2(a, b), N23), NH), DEL)); };
-  if constexpr (BITS == 4) {
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {  // word k: elements 8k .. 8k+7, byte j = (elem 8k+2j) << 4 | elem 8k+2j+1
-      const uint32_t hi = (gc.w[k] >> 4) & 0x0F0F0F0Fu, lo = gc.w[k] & 0x0F0F0F0Fu;
-#pragma unroll
-      for (int j = 0; j < 4; ++j) o[4 * k + j] = pair(code_plus_2p23(hi, j), code_plus_2p23(lo, j));
-    }
-  } else if constexpr (BITS == 2) {
-#pragma unroll
-    for (int k = 0; k < 2; ++k) {  // word k: elements 16k .. 16k+15, four per byte
-      const uint32_t c0 = (gc.w[k] >> 6) & 0x03030303u, c1 = (gc.w[k] >> 4) & 0x03030303u;
-      const uint32_t c2 = (gc.w[k] >> 2) & 0x03030303u, c3 = gc.w[k] & 0x03030303u;
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        o[8 * k + 2 * j] = pair(code_plus_2p23(c0, j), code_plus_2p23(c1, j));
-        o[8 * k + 2 * j + 1] = pair(code_plus_2p23(c2, j), code_plus_2p23(c3, j));
-      }
-    }
-  } else {
-#pragma unroll
-    for (int k = 0; k < 8; ++k) {  // word k: elements 4k .. 4k+3, one per byte
-      o[2 * k] = pair(code_plus_2p23(gc.w[k], 0), code_plus_2p23(gc.w[k], 1));
-      o[2 * k + 1] = pair(code_plus_2p23(gc.w[k], 2), code_plus_2p23(gc.w[k], 3));
-    }
-  }
-  U8 lo, hi;
-#pragma unroll
-  for (int k = 0; k < 8; ++k) { lo.v[k] = o[k]; hi.v[k] = o[8 + k]; }
-  st_cs_v8(out, lo);
-  st_cs_v8(out + 16, hi);
-}
 
 template <int BITS>
 __device__ __forceinline__ void dequant_group(const uint16_t* scales, const uint8_t* codes, int64_t g,
