@@ -67,6 +67,10 @@ SIGNATURES: dict[str, tuple] = {
     "ashkv_page_features": (_I32, [_P, _P, _I32, _I64, _I32, _P, _P, _P, _P]),
     "ashkv_int4_encode": (_I32, [_P, _I64, _I32, _P, _P, _P]),
     "ashkv_int4_decode": (_I32, [_P, _P, _I64, _I32, _P, _P]),
+    "ashkv_page_slot_bytes": (_I64, [_I32, _I32, _I32, _I32]),
+    "ashkv_migrate_pages": (_I32, [_P, _P, _P, _P, _P, _I64, _P, _P, _P, _I32, _P, _P, _I32, _I32, _I32, _I64, _P,
+                                   _F32, _U64, _I32, _P, _P, _P]),
+    "ashkv_release_slots": (_I32, [_P, _P, _I32, _P, _P, _P]),
 }
 
 
@@ -449,3 +453,38 @@ def policy_step_noalloc(T, S, N, P, cur, weights, pressure: float, theta_high: f
         pressure, theta_high, theta_low, delta, p_emergency, _addr(nc), _addr(nh), _ptr(R), target.data_ptr(),
         demote_list.data_ptr(), promote_list.data_ptr(), counts.data_ptr(), stream_handle(T.device)),
         "policy_step_noalloc")
+
+
+# --------------------------------------------------------------------------- tiered pages
+PAGE_NONE, PAGE_BF16, PAGE_INT8, PAGE_FP8, PAGE_INT4, PAGE_NBIT4, PAGE_NBIT2 = -1, 0, 1, 2, 3, 4, 5
+MIGRATE_OK, MIGRATE_NO_SLOT, MIGRATE_BAD_PAGE, MIGRATE_PINNED, MIGRATE_SAME_TIER, MIGRATE_NO_CODEC, \
+    MIGRATE_OVERFLOW = range(7)
+
+
+class TierStoreDesc(ctypes.Structure):
+    """ashkv_tier_store_t."""
+    _fields_ = [("d_data", ctypes.c_void_p), ("slot_bytes", ctypes.c_int64), ("n_slots", ctypes.c_int32),
+                ("format", ctypes.c_int32), ("d_free_stack", ctypes.c_void_p), ("d_free_top", ctypes.c_void_p)]
+
+
+def page_slot_bytes(fmt: int, tokens_per_page: int, row_len: int, outlier_cap: int = 0) -> int:
+    return int(lib().ashkv_page_slot_bytes(fmt, tokens_per_page, row_len, outlier_cap))
+
+
+def migrate_pages(tier, pin, layer_id, token_start, page_slot, target, lst, count, layer_k_ptrs, layer_v_ptrs,
+                  n_layers: int, tokens_per_page: int, row_len: int, row_stride: int, stores, sigma: float,
+                  seed: int, outlier_cap: int, entry_status, released) -> None:
+    """ashkv_migrate_pages; ``stores`` is a ctypes array of six TierStoreDesc (kept alive by the caller)."""
+    _require_cuda(tier, pin, layer_id, token_start, page_slot, target, lst, count, entry_status, released)
+    check(lib().ashkv_migrate_pages(
+        tier.data_ptr(), _ptr(pin), layer_id.data_ptr(), token_start.data_ptr(), page_slot.data_ptr(), tier.numel(),
+        target.data_ptr(), lst.data_ptr(), count.data_ptr(), lst.numel(), layer_k_ptrs.data_ptr(),
+        layer_v_ptrs.data_ptr(), n_layers, tokens_per_page, row_len, row_stride, ctypes.addressof(stores),
+        float(sigma), int(seed) & 0xFFFFFFFFFFFFFFFF, outlier_cap, entry_status.data_ptr(), released.data_ptr(),
+        stream_handle(tier.device)), "migrate_pages")
+
+
+def release_slots(released, count, max_entries: int, stores, status=None) -> None:
+    _require_cuda(released, count, status)
+    check(lib().ashkv_release_slots(released.data_ptr(), count.data_ptr(), max_entries, ctypes.addressof(stores),
+                                    _ptr(status), stream_handle(released.device)), "release_slots")

@@ -3,26 +3,38 @@
 The reference applies ``score_vectorized`` -> ``desired_tiers`` to a host
 snapshot of the page table and would call ``migrate`` once per page
 (ashkv/runtime/migrate.py:35-191), moving bytes through the host for every
-page.  Here one decode step is four kernel launches with no host round trip:
+page.  Here one decode step is a handful of kernel launches with no host round
+trip:
 
-1. ``ashkv_policy_step``      score -> desired tier -> stable demote / promote lists
-2. ``ashkv_int8_encode_pages`` gather each listed BF16 page (K and V rows of one
-                               layer) and INT8-encode it into a shadow-arena slot
-3. ``ashkv_slots_commit``      pop the used slots off the device free stack
-4. ``ashkv_int8_decode_pages`` decode listed pages back into the KV pool and
-                               push their slots back on the free stack
+1. ``ashkv_policy_step``    score -> desired tier -> stable demote / promote lists
+2. ``ashkv_migrate_pages``  every listed page, whatever its (current, target)
+                            tier edge, is decoded from its current tier's store
+                            and encoded into a slot of the target tier's store
+                            (or back into its KV-pool rows); tier and slot are
+                            committed in the device page table
+3. ``ashkv_release_slots``  the slots pages gave up go back on their stores'
+                            free stacks
 
-List lengths stay on the device; every kernel reads them there.
+List lengths stay on the device; every kernel reads them there.  Each tier
+has its own :class:`TierStore` whose page format follows the codec the
+resolver puts on the edge into that tier (``ashkv.compiler.tier_formats``):
+BF16 pages live in the KV pool, the FP8 tier holds INT8 (the hooks' per-token
+layout) or FP8 pages, the INT4 tier INT4Codec or dithered 4-bit pages, the
+archive tier dithered INT2 pages.
 
-Tier commits are explicit (``commit_transitions``): with a lossy codec the
-reference's verify step (checksum of decode(encode(x)) against the BF16
-checksum) always reports CORRUPT, so the batched path leaves the choice of
-when a page changes tier to the caller instead of re-running that check.
+As in ``migrate()``, pinned pages, pages already at their target and tiers
+without a codec are skipped and reported per entry; a slot is taken only for
+a page that moves, and the slot a page leaves is released in the same step.
+
+``Int8PageCodec`` keeps the raw BF16 <-> INT8 page kernels
+(``ashkv_int8_encode_pages`` / ``_decode_pages``) for callers that manage
+tiers themselves.
 """
 from __future__ import annotations
 
+import ctypes
 from dataclasses import dataclass
-from typing import Optional, Sequence
+from typing import Mapping, Optional, Sequence
 
 import numpy as np
 import torch
@@ -32,6 +44,8 @@ from ..compiler.runtime_builder import controller_tables
 from ..contracts.config import ASHKVConfig
 from ..contracts.page import PageTable
 from ..contracts.tiers import Tier
+
+NUM_TIERS = 6
 
 
 @dataclass
@@ -45,7 +59,7 @@ class DevicePageTable:
     pin: torch.Tensor          # int32
     layer: torch.Tensor        # int32
     token_start: torch.Tensor  # int32
-    slot: torch.Tensor         # int32, arena slot of the encoded copy or -1
+    slot: torch.Tensor         # int32, slot of the page in its tier's store, or -1
 
     @property
     def n(self) -> int:
@@ -78,8 +92,10 @@ class SlotArena:
     """Fixed-size slots in one device buffer with a device-side free stack."""
 
     def __init__(self, n_slots: int, slot_bytes: int, device: torch.device):
+        if slot_bytes % 16:
+            raise ValueError("slot_bytes must be a multiple of 16")
         self.n_slots, self.slot_bytes = n_slots, slot_bytes
-        self.data = torch.empty(n_slots * slot_bytes, dtype=torch.uint8, device=device)
+        self.data = torch.empty(max(n_slots, 1) * slot_bytes, dtype=torch.uint8, device=device)
         # slot 0 on top of the stack first
         self.free_stack = torch.arange(n_slots - 1, -1, -1, dtype=torch.int32, device=device)
         self.free_top = torch.full((1,), n_slots, dtype=torch.int32, device=device)
@@ -89,6 +105,30 @@ class SlotArena:
 
     def pressure(self) -> float:
         return 1.0 - self.free_count() / max(self.n_slots, 1)
+
+    def pressure_tensor(self) -> torch.Tensor:
+        """Occupied fraction as a one-element float32 device tensor (no host sync)."""
+        return 1.0 - self.free_top.float() / float(max(self.n_slots, 1))
+
+    def slot_view(self) -> torch.Tensor:
+        return self.data[: self.n_slots * self.slot_bytes].view(self.n_slots, self.slot_bytes)
+
+
+class TierStore(SlotArena):
+    """The slots of one tier: ``n_slots`` pages in ``fmt`` (an ``_native.PAGE_*`` format)."""
+
+    def __init__(self, fmt: int, n_slots: int, device: torch.device, tokens_per_page: int, row_len: int,
+                 outlier_cap: int = 0):
+        need = _native.page_slot_bytes(fmt, tokens_per_page, row_len, outlier_cap)
+        if need <= 0:
+            raise ValueError(f"page format {fmt} cannot store pages of {tokens_per_page} x {row_len}")
+        super().__init__(n_slots, need, device)
+        self.format = fmt
+        self.outlier_cap = outlier_cap
+
+    def desc(self) -> "_native.TierStoreDesc":
+        return _native.TierStoreDesc(self.data.data_ptr(), self.slot_bytes, self.n_slots, self.format,
+                                     self.free_stack.data_ptr(), self.free_top.data_ptr())
 
 
 class KVLayers:
@@ -124,27 +164,39 @@ class StepLists:
 
 
 class BatchMigrator:
-    """Policy + BF16<->INT8 page migration over a DevicePageTable (see module docstring).
+    """Policy plan + mixed-tier migration over a DevicePageTable (see the module docstring).
 
-    ``status_encode[i]`` / ``status_decode[i]`` report list entry i of the last
-    encode / decode: 0 ok, 1 no free slot, 2 bad page or slot.
+    ``stores`` maps each compressed tier (``Tier.FP8``, ``Tier.INT4``,
+    ``Tier.ARCHIVE``) to its :class:`TierStore`; a tier without a store has no
+    codec and pages never move there.  ``status[i]`` / ``released[i]`` report
+    entry i of the last :meth:`migrate` call (``_native.MIGRATE_*``).
     """
 
-    def __init__(self, table: DevicePageTable, kv: KVLayers, arena: SlotArena, config: ASHKVConfig,
-                 codec_keys: Sequence[tuple[int, int]], tokens_per_page: int = 16, keep_scores: bool = False):
-        self.table, self.kv, self.arena, self.cfg = table, kv, arena, config
-        self.tokens_per_page = tokens_per_page
+    def __init__(self, table: DevicePageTable, kv: KVLayers, stores: Mapping[int, TierStore],
+                 config: ASHKVConfig, codec_keys: Sequence[tuple[int, int]], *, tokens_per_page: int = 16,
+                 seed: int = 42, sigma: float = 3.0, keep_scores: bool = False):
+        self.table, self.kv, self.cfg = table, kv, config
+        self.tokens_per_page, self.seed, self.sigma = tokens_per_page, int(seed), float(sigma)
+        self.stores = {int(t): s for t, s in stores.items()}
         self.next_colder, self.next_hotter = controller_tables(codec_keys)
-        need = int(_native.lib().ashkv_int8_page_slot_bytes(tokens_per_page, kv.row_len))
-        if arena.slot_bytes < need:
-            raise ValueError(f"arena slots of {arena.slot_bytes} bytes cannot hold a page ({need} bytes)")
+        caps = {s.outlier_cap for s in self.stores.values() if s.format in (_native.PAGE_NBIT4, _native.PAGE_NBIT2)}
+        if len(caps) > 1:
+            raise ValueError("dithered stores must share one outlier capacity")
+        self.outlier_cap = caps.pop() if caps else 0
+        descs = (_native.TierStoreDesc * NUM_TIERS)()
+        descs[0] = _native.TierStoreDesc(None, 0, 0, _native.PAGE_BF16, None, None)
+        for t in range(1, NUM_TIERS):
+            s = self.stores.get(t)
+            descs[t] = s.desc() if s is not None else _native.TierStoreDesc(None, 0, 0, _native.PAGE_NONE, None, None)
+        self._descs = descs
         n, dev = table.n, table.T.device
         self.lists = StepLists(torch.empty(n, dtype=torch.int32, device=dev), torch.empty(n, dtype=torch.int32, device=dev),
                                torch.zeros(2, dtype=torch.int32, device=dev), torch.empty(n, dtype=torch.int8, device=dev),
                                torch.empty(n, dtype=torch.float32, device=dev) if keep_scores else None)
         self._scratch = torch.empty(_native.policy_scratch_ints(n), dtype=torch.int32, device=dev)
-        self.status_encode = torch.zeros(n, dtype=torch.int32, device=dev)
-        self.status_decode = torch.zeros(n, dtype=torch.int32, device=dev)
+        self.status = torch.zeros(n, dtype=torch.int32, device=dev)
+        self.released = torch.full((n,), -1, dtype=torch.int32, device=dev)
+        self.device_status = torch.zeros(1, dtype=torch.int32, device=dev)
 
     def plan(self, pressure) -> StepLists:
         """Score every page, pick desired tiers and build the transition lists (device-resident).
@@ -157,6 +209,64 @@ class BatchMigrator:
                             c.theta_low, c.delta, c.p_emergency, self.next_colder, self.next_hotter, L.R, L.target,
                             L.demote, L.promote, L.counts, self._scratch)
         return L
+
+    def migrate(self, lst: torch.Tensor, count: torch.Tensor, target: Optional[torch.Tensor] = None) -> None:
+        """Move the first ``*count`` pages of ``lst`` to ``target[page]`` (default: the last plan's
+        targets), then release the slots they gave up."""
+        t, kv = self.table, self.kv
+        tgt = self.lists.target if target is None else target
+        _native.migrate_pages(t.tier, t.pin, t.layer, t.token_start, t.slot, tgt, lst, count, kv.k_ptrs, kv.v_ptrs,
+                              kv.n_layers, self.tokens_per_page, kv.row_len, kv.row_len, self._descs, self.sigma,
+                              self.seed, self.outlier_cap, self.status, self.released)
+        _native.release_slots(self.released, count, lst.numel(), self._descs, self.device_status)
+
+    def demote(self) -> None:
+        self.migrate(self.lists.demote, self.lists.counts[0:1])
+
+    def promote(self) -> None:
+        self.migrate(self.lists.promote, self.lists.counts[1:2])
+
+    def step(self, pressure) -> StepLists:
+        """plan -> demote -> promote, all on the device."""
+        L = self.plan(pressure)
+        self.demote()
+        self.promote()
+        return L
+
+    def pressure(self) -> torch.Tensor:
+        """Occupied fraction of the most occupied store, as a one-element device tensor."""
+        ps = [s.pressure_tensor() for s in self.stores.values()]
+        return torch.stack(ps).max().reshape(1) if ps else torch.zeros(1, device=self.table.T.device)
+
+    def live_slots(self, tier: int) -> int:
+        return int(((self.table.tier == tier) & (self.table.slot >= 0)).sum())
+
+    def sync_tiers_to_host(self, page_table: PageTable) -> None:
+        """Copy the device tiers back into the host PageTable (row order of ``from_host``)."""
+        tiers = self.table.tier.cpu().numpy()
+        page_table.columns()["tier"][:] = tiers
+
+
+class Int8PageCodec:
+    """Raw BF16 <-> INT8 page kernels over one SlotArena (``ashkv_int8_encode_pages`` /
+    ``ashkv_int8_decode_pages``).
+
+    The caller owns the tiers: listed pages must be BF16 pages of valid layers
+    without a slot (encode) or pages holding a slot (decode).  ``status_encode[i]``
+    / ``status_decode[i]`` report list entry i: 0 ok, 1 no free slot, 2 bad page
+    or slot (an encode entry with status 2 leaves its stack slot popped; the
+    mixed-tier :class:`BatchMigrator` takes slots only for pages that move).
+    """
+
+    def __init__(self, table: DevicePageTable, kv: KVLayers, arena: SlotArena, *, tokens_per_page: int = 16):
+        self.table, self.kv, self.arena = table, kv, arena
+        self.tokens_per_page = tokens_per_page
+        need = int(_native.lib().ashkv_int8_page_slot_bytes(tokens_per_page, kv.row_len))
+        if arena.slot_bytes < need:
+            raise ValueError(f"arena slots of {arena.slot_bytes} bytes cannot hold a page ({need} bytes)")
+        n, dev = table.n, table.T.device
+        self.status_encode = torch.zeros(n, dtype=torch.int32, device=dev)
+        self.status_decode = torch.zeros(n, dtype=torch.int32, device=dev)
 
     def _pages_args(self, lst: torch.Tensor, count: torch.Tensor):
         t, kv, a = self.table, self.kv, self.arena
@@ -182,26 +292,23 @@ class BatchMigrator:
             a.free_top.data_ptr(), self.status_decode.data_ptr(), _native.stream_handle(lst.device)),
             "int8_decode_pages")
 
-    def demote(self) -> None:
-        self.encode(self.lists.demote, self.lists.counts[0:1])
-
-    def promote(self) -> None:
-        self.decode(self.lists.promote, self.lists.counts[1:2])
-
-    def commit_transitions(self) -> None:
-        """Make the planned target tiers current for pages whose transition succeeded."""
-        t, L = self.table, self.lists
-        n_d, n_p = (int(v) for v in L.counts.tolist())
-        for lst, cnt, status in ((L.demote, n_d, self.status_encode), (L.promote, n_p, self.status_decode)):
-            if cnt:
-                rows = lst[:cnt].long()
-                ok = status[:cnt] == 0
-                ok &= t.pin[rows] <= 0
-                t.tier[rows[ok]] = L.target[rows[ok]]
-
 
 def int8_page_slot_bytes(tokens_per_page: int, row_len: int) -> int:
     return int(_native.lib().ashkv_int8_page_slot_bytes(tokens_per_page, row_len))
 
 
-__all__ = ["DevicePageTable", "SlotArena", "KVLayers", "BatchMigrator", "StepLists", "int8_page_slot_bytes", "Tier"]
+def stores_for(table: Mapping[tuple[int, int], object], n_slots: Mapping[int, int], device: torch.device,
+               tokens_per_page: int, row_len: int, outlier_cap: int = 512) -> dict[int, TierStore]:
+    """One TierStore per compressed tier of a resolved codec table (``resolve_codecs``)."""
+    from ..compiler.codec_resolver import tier_formats
+    out = {}
+    for tier, fmt in tier_formats(dict(table)).items():
+        if tier == int(Tier.BF16) or fmt < 0 or tier not in n_slots:
+            continue
+        cap = outlier_cap if fmt in (_native.PAGE_NBIT4, _native.PAGE_NBIT2) else 0
+        out[tier] = TierStore(fmt, n_slots[tier], device, tokens_per_page, row_len, cap)
+    return out
+
+
+__all__ = ["DevicePageTable", "SlotArena", "TierStore", "KVLayers", "BatchMigrator", "Int8PageCodec", "StepLists",
+           "int8_page_slot_bytes", "stores_for", "Tier"]

@@ -1,0 +1,631 @@
+// Mixed-tier page migration: one launch moves every page of a transition list
+// from its current tier's representation to its target tier's (sm_100a).
+//
+// Replaces the per-page migrate() ladder (ashkv/runtime/migrate.py:35-191)
+// for the transitions the controller plans (ashkv/runtime/controller.py:88-104:
+// one step hotter on promotion, one step colder on demotion), with the codec
+// of each tier edge as the resolver assigns it
+// (ashkv/compiler/codec_resolver.py:56-95): BF16 <-> FP8 slot (INT8 or FP8
+// codec), FP8 slot <-> INT4 (INT4Codec or the dithered 4-bit codec), INT4 <->
+// ARCHIVE (the dithered INT2 codec).  The reference's migrate applies the
+// edge's codec to the page's stored bytes; here a page is decoded from its
+// current format to bf16 and encoded into the target format, so every tier
+// holds a compressed image of the page's bf16 values.
+//
+// A page is 2*T token rows of row_len bf16 (its K rows, then its V rows) of one
+// layer: E = 2 * T * row_len elements.  Per list entry one CTA
+//   1. checks the entry the way migrate() does (pinned -> skipped, already at
+//      target -> skipped, a tier without a codec -> skipped) and takes a slot
+//      of the target tier's store (free stack, popped with an atomic);
+//   2. decodes the page into a bf16 staging tile in shared memory (64-byte
+//      rows of 32 elements, 16-byte chunks XOR-swizzled so thread-per-group
+//      and thread-per-chunk access are both free of bank conflicts);
+//   3. encodes the tile into the target slot (or the page's KV-pool rows);
+//   4. commits tier and slot in the device page table and records the slot it
+//      gave up.  ashkv_release_slots pushes recorded slots back afterwards, so
+//      stacks are only popped in this kernel and only pushed in that one.
+// Entries are resolved 32 at a time by one warp (list -> page -> table
+// columns -> slot) so that chain of dependent loads is paid once per batch.
+#include <algorithm>
+
+#include "common.cuh"
+#include "fp8_conv.cuh"
+#include "int4_group.cuh"
+#include "nbit_group.cuh"
+
+namespace ashkv {
+namespace {
+
+constexpr int kThreads = 256;
+constexpr int kWarps = kThreads / 32;
+constexpr int kTiers = 6;
+constexpr int kBatch = 32;
+constexpr int kMaxElems = 65536;  // 128 KiB of staging; outlier indices fit in 16 bits
+
+struct Store {
+  uint8_t* data;
+  int64_t slot_bytes;
+  int32_t n_slots;
+  int32_t format;
+  int32_t* free_stack;
+  int32_t* free_top;
+};
+
+struct MigParams {
+  int8_t* tier;
+  const int32_t* pin;
+  const int32_t* layer_id;
+  const int32_t* token_start;
+  int32_t* page_slot;
+  int64_t n_pages;
+  const int8_t* target;
+  const int32_t* list;
+  const int32_t* count;
+  int32_t max_entries;
+  const uint64_t* layer_k;
+  const uint64_t* layer_v;
+  int32_t n_layers;
+  int32_t T;
+  int32_t row_len;
+  int64_t row_stride;
+  Store store[kTiers];
+  float sigma;
+  int32_t outlier_cap;
+  uint32_t round_keys[20];
+  int32_t* entry_status;
+  int32_t* released;
+};
+
+struct Entry {
+  int32_t page, cur, tgt, layer, ts, old_slot, new_slot, status;
+};
+
+__host__ __device__ __forceinline__ int64_t int8_codes_offset(int T) { return (4 * int64_t(T) + 15) / 16 * 16; }
+
+// Slot layouts (E elements, offsets in bytes):
+//   INT8   [2T fp16 scales | pad to 16 | E int8 codes]           (the hooks' per-token layout)
+//   FP8    [E e4m3fn bytes]
+//   INT4   [E/64 bf16 scales | E/2 nibble bytes]                 (INT4Codec, group 64)
+//   NBIT*  [u32 n_out, 3 x u32 0 | E/32 bf16 delta | E*bits/8 codes | cap x u32 outliers]
+//          outlier entry = (element index in the page << 16) | bf16 bits, ascending
+__host__ __device__ __forceinline__ int64_t nbit_delta_off() { return 16; }
+__host__ __device__ __forceinline__ int64_t nbit_codes_off(int64_t E) { return 16 + E / 16; }
+__host__ __device__ __forceinline__ int64_t nbit_entries_off(int64_t E, int bits) {
+  return nbit_codes_off(E) + E * bits / 8;
+}
+
+int64_t slot_bytes_for(int32_t format, int64_t E, int32_t cap) {
+  int64_t b = -1;
+  switch (format) {
+    case ASHKV_PAGE_INT8: b = -1; break;  // needs T; computed by the caller
+    case ASHKV_PAGE_FP8: b = E; break;
+    case ASHKV_PAGE_INT4: b = E / 32 + E / 2; break;
+    case ASHKV_PAGE_NBIT4: b = nbit_entries_off(E, 4) + 4 * int64_t(cap); break;
+    case ASHKV_PAGE_NBIT2: b = nbit_entries_off(E, 2) + 4 * int64_t(cap); break;
+    default: break;
+  }
+  return b;
+}
+
+// Byte offset of element e in the staging tile: group g = e / 32 is a 64-byte
+// row; 16-byte chunk k of it sits at position k ^ ((g >> 1) & 3).
+__device__ __forceinline__ uint32_t stage_off(uint32_t e) {
+  const uint32_t g = e >> 5;
+  return (g << 6) + ((((e >> 3) & 3u) ^ ((g >> 1) & 3u)) << 4) + ((e & 7u) << 1);
+}
+__device__ __forceinline__ uint4 lds_chunk(const uint8_t* stage, uint32_t e) {
+  return *reinterpret_cast<const uint4*>(stage + stage_off(e));
+}
+__device__ __forceinline__ void sts_chunk(uint8_t* stage, uint32_t e, uint4 v) {
+  *reinterpret_cast<uint4*>(stage + stage_off(e)) = v;
+}
+
+__device__ __forceinline__ uint16_t* pool_row(const MigParams& p, const Entry& en, int r) {
+  const int T = p.T;
+  const uint64_t base = (r < T ? p.layer_k : p.layer_v)[en.layer];
+  return reinterpret_cast<uint16_t*>(base) + (int64_t(en.ts) + (r < T ? r : r - T)) * p.row_stride;
+}
+
+// ---------------------------------------------------------------- decoders (slot -> staging)
+template <int ROW>
+__device__ void stage_from_pool(const MigParams& p, const Entry& en, uint8_t* stage, int n8) {
+  constexpr int CPR = ROW / 8;  // chunks per row
+  for (int k0 = threadIdx.x; k0 < n8; k0 += 4 * kThreads) {
+    uint4 v[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int k = k0 + u * kThreads;
+      if (k < n8) v[u] = ld_nc_v4(pool_row(p, en, k / CPR) + (k % CPR) * 8);
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int k = k0 + u * kThreads;
+      if (k < n8) sts_chunk(stage, uint32_t(k) * 8u, v[u]);
+    }
+  }
+}
+
+template <int ROW>
+__device__ void stage_from_int8(const uint8_t* slot, int T, uint8_t* stage, int n8) {
+  constexpr int CPR = ROW / 8;
+  const uint8_t* codes = slot + int8_codes_offset(T);
+  const Recip y = make_recip(127.0f);
+  const f2 YHI = pk2(y.hi, y.hi), YLO = pk2(y.lo, y.lo);
+  for (int k = threadIdx.x; k < n8; k += kThreads) {
+    const float s = f16_to_f32(reinterpret_cast<const uint16_t*>(slot)[k / CPR]);
+    const uint2 cw = *reinterpret_cast<const uint2*>(codes + int64_t(k) * 8);
+    const uint32_t ww[2] = {cw.x, cw.y};
+    uint32_t o[4];
+    const bool fast = int8_dec_fast(s);
+    const f2 S = pk2(s, s);
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      f2 F0, F1;
+      int8x4_to_f2(ww[h], F0, F1);
+      if (fast) {
+        o[2 * h] = f32x2_to_bf16x2_pk(div2_short(mul2(F0, S), YHI, YLO));
+        o[2 * h + 1] = f32x2_to_bf16x2_pk(div2_short(mul2(F1, S), YHI, YLO));
+      } else {
+        float a, b;
+        upk2(F0, a, b);
+        o[2 * h] = f32x2_to_bf16x2(__fdiv_rn(__fmul_rn(a, s), 127.0f), __fdiv_rn(__fmul_rn(b, s), 127.0f));
+        upk2(F1, a, b);
+        o[2 * h + 1] = f32x2_to_bf16x2(__fdiv_rn(__fmul_rn(a, s), 127.0f), __fdiv_rn(__fmul_rn(b, s), 127.0f));
+      }
+    }
+    sts_chunk(stage, uint32_t(k) * 8u, make_uint4(o[0], o[1], o[2], o[3]));
+  }
+}
+
+__device__ void stage_from_fp8(const uint8_t* slot, uint8_t* stage, int n8) {
+  for (int k = threadIdx.x; k < n8; k += kThreads) {
+    const uint2 c = *reinterpret_cast<const uint2*>(slot + int64_t(k) * 8);
+    sts_chunk(stage, uint32_t(k) * 8u,
+              make_uint4(bf16x2_from_fp8x2(c.x & 0xFFFFu), bf16x2_from_fp8x2(c.x >> 16),
+                         bf16x2_from_fp8x2(c.y & 0xFFFFu), bf16x2_from_fp8x2(c.y >> 16)));
+  }
+}
+
+__device__ void stage_from_int4(const uint8_t* slot, int64_t E, uint8_t* stage, int n8) {
+  const uint16_t* scales = reinterpret_cast<const uint16_t*>(slot);
+  const uint32_t* nib = reinterpret_cast<const uint32_t*>(slot + E / 32);
+  for (int k = threadIdx.x; k < n8; k += kThreads) {
+    uint32_t o[4];
+    unpack_nibbles8(nib[k], bf16_to_f32(scales[k >> 3]), o);
+    sts_chunk(stage, uint32_t(k) * 8u, make_uint4(o[0], o[1], o[2], o[3]));
+  }
+}
+
+template <int BITS>
+__device__ void stage_from_nbit(const uint8_t* slot, int64_t E, int32_t cap, uint8_t* stage) {
+  const uint16_t* delta = reinterpret_cast<const uint16_t*>(slot + nbit_delta_off());
+  const uint8_t* codes = slot + nbit_codes_off(E);
+  const int n_groups = int(E / 32);
+  constexpr float half = float((1 << BITS) - 1) * 0.5f;
+  for (int g = threadIdx.x; g < n_groups; g += kThreads) {
+    GroupCodes<BITS> gc;
+    load_group<BITS>(delta, codes, g, gc);
+    uint32_t o[16];
+    group_bf16<BITS>(gc, half, o);
+#pragma unroll
+    for (int c = 0; c < 4; ++c)
+      sts_chunk(stage, uint32_t(g) * 32u + 8u * c, make_uint4(o[4 * c], o[4 * c + 1], o[4 * c + 2], o[4 * c + 3]));
+  }
+  __syncthreads();  // dense values first, then the outliers overwrite theirs
+  const uint32_t n_out = min(*reinterpret_cast<const uint32_t*>(slot), uint32_t(cap));
+  const uint32_t* ent = reinterpret_cast<const uint32_t*>(slot + nbit_entries_off(E, BITS));
+  for (uint32_t j = threadIdx.x; j < n_out; j += kThreads) {
+    const uint32_t e = ent[j];
+    const uint32_t idx = e >> 16;
+    if (idx < uint32_t(E)) *reinterpret_cast<uint16_t*>(stage + stage_off(idx)) = uint16_t(e & 0xFFFFu);
+  }
+}
+
+// ---------------------------------------------------------------- encoders (staging -> slot)
+template <int ROW>
+__device__ void pool_from_stage(const MigParams& p, const Entry& en, const uint8_t* stage, int n8) {
+  constexpr int CPR = ROW / 8;
+  for (int k = threadIdx.x; k < n8; k += kThreads)
+    *reinterpret_cast<uint4*>(pool_row(p, en, k / CPR) + (k % CPR) * 8) = lds_chunk(stage, uint32_t(k) * 8u);
+}
+
+// TEAM lanes per row, NCH chunks of 8 per lane (the row kernels' mapping).
+template <int ROW>
+__device__ void int8_from_stage(const uint8_t* stage, int T, uint8_t* slot) {
+  constexpr int TEAM = ROW >= 1024 ? 32 : ROW / 32;
+  constexpr int NCH = ROW / (8 * TEAM);
+  constexpr int RPW = 32 / TEAM;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int sub = lane / TEAM, lin = lane % TEAM;
+  uint8_t* codes = slot + int8_codes_offset(T);
+  for (int r0 = warp * RPW; r0 < 2 * T; r0 += kWarps * RPW) {  // warp-uniform loop
+    const int r = r0 + sub;
+    const bool on = r < 2 * T;
+    uint32_t w[4 * NCH];
+#pragma unroll
+    for (int c = 0; c < NCH; ++c) {
+      const uint4 v = on ? lds_chunk(stage, uint32_t(r) * ROW + uint32_t(c * TEAM + lin) * 8u) : make_uint4(0, 0, 0, 0);
+      w[4 * c] = v.x; w[4 * c + 1] = v.y; w[4 * c + 2] = v.z; w[4 * c + 3] = v.w;
+    }
+    const float am = fmaxf(team_absmax_bf16<TEAM>(w), 1e-8f);
+    if (!on) continue;
+    if (lin == 0) reinterpret_cast<uint16_t*>(slot)[r] = f32_to_f16(am);
+    const Int8Div d = int8_div(am);
+#pragma unroll
+    for (int c = 0; c < NCH; ++c)
+      *reinterpret_cast<uint2*>(codes + int64_t(r) * ROW + (c * TEAM + lin) * 8) =
+          make_uint2(int8_codes4_bf16(w[4 * c], w[4 * c + 1], d), int8_codes4_bf16(w[4 * c + 2], w[4 * c + 3], d));
+  }
+}
+
+__device__ void fp8_from_stage(const uint8_t* stage, uint8_t* slot, int n8) {
+  for (int k = threadIdx.x; k < n8; k += kThreads) {
+    const uint4 v = lds_chunk(stage, uint32_t(k) * 8u);
+    *reinterpret_cast<uint2*>(slot + int64_t(k) * 8) =
+        make_uint2(fp8x2_from_bf16x2(v.x) | (fp8x2_from_bf16x2(v.y) << 16),
+                   fp8x2_from_bf16x2(v.z) | (fp8x2_from_bf16x2(v.w) << 16));
+  }
+}
+
+// INT4Codec, group 64: two lanes per group, each with one 32-element staging row.
+__device__ void int4_from_stage(const uint8_t* stage, int64_t E, uint8_t* slot) {
+  uint16_t* scales = reinterpret_cast<uint16_t*>(slot);
+  uint8_t* nib = slot + E / 32;
+  const int n_rows = int(E / 32), lane = threadIdx.x & 31;
+  for (int base = threadIdx.x & ~31; base < n_rows; base += kThreads) {  // warp-uniform
+    const int g = base + lane;
+    const bool on = g < n_rows;
+    float x[4][8];
+    float m = 0.0f;
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      unpack_chunk(on ? lds_chunk(stage, uint32_t(g) * 32u + 8u * c) : make_uint4(0, 0, 0, 0), x[c]);
+      m = chunk_max(m, x[c]);
+    }
+    m = max_nan(m, __shfl_xor_sync(0xFFFFFFFFu, m, 1));
+    if (!on) continue;
+    const float am = group_max_finish(m);
+    if ((g & 1) == 0) scales[g >> 1] = static_cast<uint16_t>(bf16_cpu(am));
+    const GroupDiv d = group_div(am);
+    uint32_t o[4];
+#pragma unroll
+    for (int c = 0; c < 4; ++c) o[c] = pack_chunk(x[c], d);
+    *reinterpret_cast<uint4*>(nib + int64_t(g) * 16) = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+}
+
+__device__ __forceinline__ uint32_t block_exclusive_scan(uint32_t v, uint32_t* s_warp, uint32_t& total) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  uint32_t inc = v;
+#pragma unroll
+  for (int off = 1; off < 32; off <<= 1) {
+    const uint32_t t = __shfl_up_sync(0xFFFFFFFFu, inc, off);
+    if (lane >= off) inc += t;
+  }
+  if (lane == 31) s_warp[warp] = inc;
+  __syncthreads();
+  uint32_t before = 0;
+  total = 0;
+#pragma unroll
+  for (int w = 0; w < kWarps; ++w) {
+    const uint32_t t = s_warp[w];
+    before += w < warp ? t : 0u;
+    total += t;
+  }
+  return before + inc - v;
+}
+
+// Dithered N-bit: one thread per 32-element group (encode_group), then the
+// page's outliers ranked by a block scan.  Returns false on outlier overflow.
+template <int BITS>
+__device__ bool nbit_from_stage(const MigParams& p, const Entry& en, const uint8_t* stage, int64_t E, uint8_t* slot,
+                                uint32_t* s_omask, uint32_t* s_warp) {
+  NbitEncParams np{};
+  np.sigma = p.sigma;
+  np.half_states = float((1 << BITS) - 1) * 0.5f;
+#pragma unroll
+  for (int k = 0; k < 20; ++k) np.round_keys[k] = p.round_keys[k];
+  np.dither_offset = uint64_t(en.page) * uint64_t(E);
+  np.scales = reinterpret_cast<uint16_t*>(slot + nbit_delta_off());
+  np.codes = slot + nbit_codes_off(E);
+  const int n_groups = int(E / 32), lane = threadIdx.x & 31;
+  const uint32_t stage_base = smem_u32(stage);
+  for (int base = threadIdx.x & ~31; base < n_groups; base += kThreads) {  // warp-uniform
+    const int g = base + lane;
+    const bool on = g < n_groups;
+    const uint32_t tile = stage_base + uint32_t(base) * 64u;
+    const SmemGroup src{tile, tile + uint32_t(lane) * 64u, uint32_t(lane >> 1) & 3u};
+    const uint32_t om = encode_group<BITS, ASHKV_DITHER_PHILOX>(src, np, g, on);
+    if (on) s_omask[g] = om;
+  }
+  __syncthreads();
+  // groups [g0, g0 + per) of this thread, in order
+  const int per = (n_groups + kThreads - 1) / kThreads;
+  const int g0 = threadIdx.x * per;
+  uint32_t cnt = 0;
+  for (int j = 0; j < per; ++j)
+    if (g0 + j < n_groups) cnt += uint32_t(__popc(s_omask[g0 + j]));
+  uint32_t total;
+  uint32_t pos = block_exclusive_scan(cnt, s_warp, total);
+  const uint32_t cap = uint32_t(p.outlier_cap);
+  uint32_t* ent = reinterpret_cast<uint32_t*>(slot + nbit_entries_off(E, BITS));
+  if (total <= cap) {
+    for (int j = 0; j < per; ++j) {
+      const int g = g0 + j;
+      if (g >= n_groups) break;
+      uint32_t m = s_omask[g];
+      while (m) {
+        const uint32_t b = uint32_t(__ffs(m) - 1);
+        m &= m - 1;
+        const uint32_t idx = uint32_t(g) * 32u + b;
+        ent[pos++] = (idx << 16) | *reinterpret_cast<const uint16_t*>(stage + stage_off(idx));
+      }
+    }
+  }
+  if (threadIdx.x == 0) {
+    uint4 hdr = make_uint4(total <= cap ? total : 0u, 0u, 0u, 0u);
+    *reinterpret_cast<uint4*>(slot) = hdr;
+  }
+  return total <= cap;
+}
+
+__device__ __forceinline__ int fmt_of(const MigParams& p, int t) {
+  return (t >= 0 && t < kTiers) ? p.store[t].format : ASHKV_PAGE_NONE;
+}
+
+// Resolve entry i (one lane): the migrate() ladder's checks, then the slot.
+__device__ Entry resolve(const MigParams& p, int64_t i) {
+  Entry e{};
+  e.status = ASHKV_MIGRATE_BAD_PAGE;
+  e.old_slot = e.new_slot = -1;
+  const int32_t page = p.list[i];
+  e.page = page;
+  if (page < 0 || page >= p.n_pages) return e;
+  e.cur = p.tier[page];
+  e.tgt = p.target[page];
+  e.layer = p.layer_id[page];
+  e.ts = p.token_start[page];
+  e.old_slot = p.page_slot[page];
+  const int32_t pin = p.pin ? p.pin[page] : 0;
+  if (pin > 0) { e.status = ASHKV_MIGRATE_PINNED; return e; }
+  if (e.cur == e.tgt) { e.status = ASHKV_MIGRATE_SAME_TIER; return e; }
+  const int fs = fmt_of(p, e.cur), ft = fmt_of(p, e.tgt);
+  if (fs == ASHKV_PAGE_NONE || ft == ASHKV_PAGE_NONE) { e.status = ASHKV_MIGRATE_NO_CODEC; return e; }
+  if (e.layer < 0 || e.layer >= p.n_layers || e.ts < 0) return e;
+  if (fs != ASHKV_PAGE_BF16 && (e.old_slot < 0 || e.old_slot >= p.store[e.cur].n_slots)) return e;
+  if (ft != ASHKV_PAGE_BF16) {
+    const Store& s = p.store[e.tgt];
+    const int32_t pos = atomicSub(s.free_top, 1) - 1;
+    if (pos < 0 || pos >= s.n_slots) {
+      atomicAdd(s.free_top, 1);
+      e.status = ASHKV_MIGRATE_NO_SLOT;
+      return e;
+    }
+    e.new_slot = s.free_stack[pos];
+    if (e.new_slot < 0 || e.new_slot >= s.n_slots) {  // corrupt stack entry: leave it popped, report it
+      e.status = ASHKV_MIGRATE_BAD_PAGE;
+      e.new_slot = -1;
+      return e;
+    }
+  }
+  e.status = ASHKV_MIGRATE_OK;
+  return e;
+}
+
+template <int ROW>
+__global__ void __launch_bounds__(kThreads, 2) migrate_pages_kernel(const MigParams p) {
+  extern __shared__ __align__(16) uint8_t smem[];
+  __shared__ Entry s_ent[kBatch];
+  __shared__ uint32_t s_warp[kWarps];
+  __shared__ int32_t s_ok;
+  const int T = p.T;
+  const int64_t E = 2 * int64_t(T) * ROW;
+  const int n8 = int(E / 8);
+  uint8_t* stage = smem;
+  uint32_t* s_omask = reinterpret_cast<uint32_t*>(smem + E * 2);
+  const int32_t count = min(*p.count, p.max_entries);
+  for (int64_t b0 = blockIdx.x; b0 < count; b0 += int64_t(kBatch) * gridDim.x) {
+    const int64_t left = (count - b0 + gridDim.x - 1) / gridDim.x;
+    const int nb = left < kBatch ? int(left) : kBatch;
+    if (threadIdx.x < nb) s_ent[threadIdx.x] = resolve(p, b0 + int64_t(threadIdx.x) * gridDim.x);
+    __syncthreads();
+    for (int k = 0; k < nb; ++k) {
+      const Entry en = s_ent[k];
+      const int64_t i = b0 + int64_t(k) * gridDim.x;
+      bool ok = en.status == ASHKV_MIGRATE_OK;
+      if (ok) {
+        const int fs = p.store[en.cur].format, ft = p.store[en.tgt].format;
+        const uint8_t* src = fs == ASHKV_PAGE_BF16 ? nullptr
+                                                   : p.store[en.cur].data + int64_t(en.old_slot) * p.store[en.cur].slot_bytes;
+        uint8_t* dst = ft == ASHKV_PAGE_BF16 ? nullptr
+                                             : p.store[en.tgt].data + int64_t(en.new_slot) * p.store[en.tgt].slot_bytes;
+        switch (fs) {
+          case ASHKV_PAGE_BF16: stage_from_pool<ROW>(p, en, stage, n8); break;
+          case ASHKV_PAGE_INT8: stage_from_int8<ROW>(src, T, stage, n8); break;
+          case ASHKV_PAGE_FP8: stage_from_fp8(src, stage, n8); break;
+          case ASHKV_PAGE_INT4: stage_from_int4(src, E, stage, n8); break;
+          case ASHKV_PAGE_NBIT4: stage_from_nbit<4>(src, E, p.outlier_cap, stage); break;
+          default: stage_from_nbit<2>(src, E, p.outlier_cap, stage); break;
+        }
+        __syncthreads();
+        switch (ft) {
+          case ASHKV_PAGE_BF16: pool_from_stage<ROW>(p, en, stage, n8); break;
+          case ASHKV_PAGE_INT8: int8_from_stage<ROW>(stage, T, dst); break;
+          case ASHKV_PAGE_FP8: fp8_from_stage(stage, dst, n8); break;
+          case ASHKV_PAGE_INT4: int4_from_stage(stage, E, dst); break;
+          case ASHKV_PAGE_NBIT4: ok = nbit_from_stage<4>(p, en, stage, E, dst, s_omask, s_warp); break;
+          default: ok = nbit_from_stage<2>(p, en, stage, E, dst, s_omask, s_warp); break;
+        }
+        if (threadIdx.x == 0) s_ok = ok;
+        __syncthreads();  // staging, s_omask and s_warp are free again; s_ok visible
+        ok = s_ok != 0;
+      }
+      if (threadIdx.x == 0) {
+        int32_t status = en.status, rel = -1;
+        if (en.status == ASHKV_MIGRATE_OK && ok) {
+          p.tier[en.page] = int8_t(en.tgt);
+          p.page_slot[en.page] = en.new_slot;  // -1 when the page returns to its BF16 rows
+          if (en.old_slot >= 0 && p.store[en.cur].format != ASHKV_PAGE_BF16) rel = (en.cur << 24) | en.old_slot;
+        } else if (en.status == ASHKV_MIGRATE_OK) {
+          status = ASHKV_MIGRATE_OVERFLOW;
+          rel = (en.tgt << 24) | en.new_slot;
+        } else if (en.status == ASHKV_MIGRATE_NO_SLOT || en.new_slot < 0) {
+          rel = -1;
+        }
+        p.entry_status[i] = status;
+        p.released[i] = rel;
+      }
+    }
+    __syncthreads();  // s_ent is rewritten by the next batch
+  }
+}
+
+struct ReleaseParams {
+  const int32_t* released;
+  const int32_t* count;
+  int32_t max_entries;
+  Store store[kTiers];
+  uint32_t* status;
+};
+
+__global__ void __launch_bounds__(256) release_slots_kernel(const ReleaseParams p) {
+  const int32_t count = min(*p.count, p.max_entries);
+  for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < count; i += int64_t(gridDim.x) * blockDim.x) {
+    const int32_t v = p.released[i];
+    if (v < 0) continue;
+    const int t = v >> 24, slot = v & 0xFFFFFF;
+    if (t <= 0 || t >= kTiers || !p.store[t].free_stack || slot >= p.store[t].n_slots) {
+      if (p.status) atomicOr(p.status, ASHKV_FLAG_INDEX_RANGE);
+      continue;
+    }
+    const int32_t pos = atomicAdd(p.store[t].free_top, 1);
+    if (pos >= 0 && pos < p.store[t].n_slots) p.store[t].free_stack[pos] = slot;
+    else if (p.status) atomicOr(p.status, ASHKV_FLAG_INDEX_RANGE);
+  }
+}
+
+bool row_ok(int32_t row) { return row == 128 || row == 256 || row == 512 || row == 1024 || row == 2048; }
+
+template <int ROW>
+ashkv_status_t launch_migrate(const MigParams& p, size_t smem, cudaStream_t st) {
+  const cudaError_t e = cudaFuncSetAttribute(migrate_pages_kernel<ROW>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             int(smem));
+  if (e != cudaSuccess) {
+    set_error("migrate_pages (shared memory attribute)", e);
+    return ASHKV_LAUNCH_ERROR;
+  }
+  const int sms = sm_count() > 0 ? sm_count() : 148;
+  const int64_t g = std::min<int64_t>(p.max_entries, int64_t(sms) * 2);
+  migrate_pages_kernel<ROW><<<unsigned(g > 0 ? g : 1), kThreads, smem, st>>>(p);
+  return check_launch("migrate_pages");
+}
+
+bool copy_stores(const ashkv_tier_store_t* stores, Store (&out)[kTiers], bool need_data) {
+  if (!stores) return false;
+  for (int t = 0; t < kTiers; ++t) {
+    const ashkv_tier_store_t& s = stores[t];
+    out[t] = Store{static_cast<uint8_t*>(s.d_data), s.slot_bytes, s.n_slots, s.format, s.d_free_stack, s.d_free_top};
+    if (t == 0) {
+      if (s.format != ASHKV_PAGE_BF16) return false;
+      continue;
+    }
+    if (s.format == ASHKV_PAGE_NONE) continue;
+    if (s.format < ASHKV_PAGE_INT8 || s.format > ASHKV_PAGE_NBIT2) return false;
+    if (s.n_slots < 0 || s.n_slots > 0xFFFFFF || !s.d_free_stack || !s.d_free_top) return false;
+    if (need_data && (!s.d_data || !aligned(s.d_data, 16) || s.slot_bytes % 16)) return false;
+  }
+  return true;
+}
+
+}  // namespace
+}  // namespace ashkv
+
+using namespace ashkv;
+
+extern "C" int64_t ashkv_page_slot_bytes(int32_t format, int32_t tokens_per_page, int32_t row_len,
+                                         int32_t outlier_cap) {
+  if (tokens_per_page <= 0 || row_len <= 0 || outlier_cap < 0) return -1;
+  const int64_t E = 2 * int64_t(tokens_per_page) * row_len;
+  int64_t b = format == ASHKV_PAGE_INT8 ? int8_codes_offset(tokens_per_page) + E : slot_bytes_for(format, E, outlier_cap);
+  if (b < 0) return -1;
+  return (b + 255) / 256 * 256;
+}
+
+extern "C" ashkv_status_t ashkv_migrate_pages(
+    int8_t* d_tier, const int32_t* d_pin, const int32_t* d_layer_id, const int32_t* d_token_start,
+    int32_t* d_page_slot, int64_t n_pages, const int8_t* d_target, const int32_t* d_list, const int32_t* d_count,
+    int32_t max_entries, const uint64_t* d_layer_k, const uint64_t* d_layer_v, int32_t n_layers,
+    int32_t tokens_per_page, int32_t row_len, int64_t row_stride, const ashkv_tier_store_t* stores, float sigma,
+    uint64_t seed, int32_t outlier_cap, int32_t* d_entry_status, int32_t* d_released, void* stream) {
+  MigParams p{};
+  p.tier = d_tier; p.pin = d_pin; p.layer_id = d_layer_id; p.token_start = d_token_start; p.page_slot = d_page_slot;
+  p.n_pages = n_pages; p.target = d_target; p.list = d_list; p.count = d_count; p.max_entries = max_entries;
+  p.layer_k = d_layer_k; p.layer_v = d_layer_v; p.n_layers = n_layers; p.T = tokens_per_page; p.row_len = row_len;
+  p.row_stride = row_stride; p.sigma = sigma; p.outlier_cap = outlier_cap;
+  p.entry_status = d_entry_status; p.released = d_released;
+  if (max_entries < 0 || n_pages < 0 || n_layers <= 0 || tokens_per_page <= 0 || outlier_cap < 0) {
+    set_message("ashkv_migrate_pages: negative size or no layers");
+    return ASHKV_BAD_ARGUMENT;
+  }
+  if (max_entries == 0) return ASHKV_OK;
+  if (!d_tier || !d_layer_id || !d_token_start || !d_page_slot || !d_target || !d_list || !d_count || !d_layer_k ||
+      !d_layer_v || !d_entry_status || !d_released) {
+    set_message("ashkv_migrate_pages: null device pointer");
+    return ASHKV_BAD_ARGUMENT;
+  }
+  if (!row_ok(row_len) || (row_stride * 2) % 16 || row_stride < row_len) {
+    set_message("ashkv_migrate_pages: row_len must be 128, 256, 512, 1024 or 2048 with a 16-byte row stride");
+    return ASHKV_BAD_ARGUMENT;
+  }
+  const int64_t E = 2 * int64_t(tokens_per_page) * row_len;
+  if (E > kMaxElems || E % 1024) {
+    set_message("ashkv_migrate_pages: a page (2 * tokens_per_page * row_len) must be a multiple of 1024 and at most "
+                "65536 elements");
+    return ASHKV_BAD_ARGUMENT;
+  }
+  if (!copy_stores(stores, p.store, true)) {
+    set_message("ashkv_migrate_pages: bad tier store table (store 0 must be the BF16 pool)");
+    return ASHKV_BAD_ARGUMENT;
+  }
+  for (int t = 1; t < kTiers; ++t) {
+    const Store& s = p.store[t];
+    if (s.format == ASHKV_PAGE_NONE) continue;
+    const int64_t need = ashkv_page_slot_bytes(s.format, tokens_per_page, row_len, outlier_cap);
+    if (s.slot_bytes < need) {
+      set_message("ashkv_migrate_pages: a tier store's slots are smaller than its format needs");
+      return ASHKV_BAD_ARGUMENT;
+    }
+  }
+  if ((p.store[1].format == ASHKV_PAGE_NBIT4 || p.store[2].format == ASHKV_PAGE_NBIT4 ||
+       p.store[3].format == ASHKV_PAGE_NBIT4 || p.store[1].format == ASHKV_PAGE_NBIT2 ||
+       p.store[2].format == ASHKV_PAGE_NBIT2 || p.store[3].format == ASHKV_PAGE_NBIT2) && !(sigma > 0.0f)) {
+    set_message("ashkv_migrate_pages: sigma must be positive for the dithered formats");
+    return ASHKV_BAD_ARGUMENT;
+  }
+  philox_round_keys(seed, p.round_keys);
+  const size_t smem = size_t(E) * 2 + size_t(E / 32) * 4;
+  cudaStream_t st = as_stream(stream);
+  switch (row_len) {
+    case 128: return launch_migrate<128>(p, smem, st);
+    case 256: return launch_migrate<256>(p, smem, st);
+    case 512: return launch_migrate<512>(p, smem, st);
+    case 1024: return launch_migrate<1024>(p, smem, st);
+    default: return launch_migrate<2048>(p, smem, st);
+  }
+}
+
+extern "C" ashkv_status_t ashkv_release_slots(const int32_t* d_released, const int32_t* d_count, int32_t max_entries,
+                                              const ashkv_tier_store_t* stores, uint32_t* d_status, void* stream) {
+  ReleaseParams p{};
+  p.released = d_released; p.count = d_count; p.max_entries = max_entries; p.status = d_status;
+  if (max_entries < 0) return ASHKV_BAD_ARGUMENT;
+  if (max_entries == 0) return ASHKV_OK;
+  if (!d_released || !d_count || !copy_stores(stores, p.store, false)) {
+    set_message("ashkv_release_slots: null pointer or bad tier store table");
+    return ASHKV_BAD_ARGUMENT;
+  }
+  const int sms = sm_count() > 0 ? sm_count() : 148;
+  const int64_t g = std::min<int64_t>((int64_t(max_entries) + 255) / 256, int64_t(sms) * 4);
+  release_slots_kernel<<<unsigned(g > 0 ? g : 1), 256, 0, as_stream(stream)>>>(p);
+  return check_launch("release_slots");
+}

@@ -259,6 +259,82 @@ ASHKV_API ashkv_status_t ashkv_int8_decode_pages(
     int32_t* d_entry_status, void* stream);
 
 /* ========================================================================
+ * Mixed-tier page migration over device-resident transition lists.
+ * Replaces the per-page migrate() ladder (ashkv/runtime/migrate.py:35-191)
+ * for every (current, target) tier edge the controller plans
+ * (ashkv/runtime/controller.py:88-104), each running the codec the resolver
+ * puts on that tier (ashkv/compiler/codec_resolver.py:56-95).
+ *
+ * A page p is 2 * tokens_per_page rows of row_len bf16: its K rows, then its
+ * V rows, at token d_token_start[p] of layer d_layer_id[p] of the KV pool
+ * (K rows at d_layer_k[l] + token * row_stride elements, V likewise).  Each
+ * tier t holds its pages in stores[t] (a host array of six entries indexed by
+ * tier: BF16, FP8, INT4, ARCHIVE, CPU, DISK): store 0 must have format
+ * ASHKV_PAGE_BF16 (the pool rows themselves); a tier whose format is
+ * ASHKV_PAGE_NONE has no codec.  Other stores are arrays of n_slots slots of
+ * slot_bytes (>= ashkv_page_slot_bytes) with a device free stack
+ * (d_free_stack[0 .. *d_free_top)).
+ *
+ * ashkv_migrate_pages, for each entry i < min(*d_count, max_entries) of
+ * d_list (page p, current tier d_tier[p], target d_target[p]):
+ *   pinned (d_pin[p] > 0) -> ASHKV_MIGRATE_PINNED, already at target ->
+ *   ASHKV_MIGRATE_SAME_TIER, a tier without a codec -> ASHKV_MIGRATE_NO_CODEC,
+ *   bad layer / slot -> ASHKV_MIGRATE_BAD_PAGE, empty target stack ->
+ *   ASHKV_MIGRATE_NO_SLOT; otherwise the page is decoded from its current
+ *   slot (or pool rows) and encoded into a slot popped from the target store
+ *   (or its pool rows), and d_tier[p], d_page_slot[p] are updated (-1 for
+ *   BF16).  A dithered page with more outliers than outlier_cap is not moved
+ *   (ASHKV_MIGRATE_OVERFLOW).  d_entry_status[i] gets the status and
+ *   d_released[i] the slot given up, as (tier << 24) | slot, or -1.
+ *   Dithered formats draw Philox4x32-10(seed) at counter (p * E + e) / 8 for
+ *   element e of page p (E = 2 * tokens_per_page * row_len), sigma as in
+ *   DitheredNBitCodec.  row_len is 128, 256, 512, 1024 or 2048; E is a
+ *   multiple of 1024 and at most 65536.  A page must appear at most once per
+ *   call.
+ * ashkv_release_slots then pushes every recorded slot back on its store's
+ * free stack.  Run it after ashkv_migrate_pages and before the next one
+ * (pops and pushes never share a launch).
+ * ======================================================================== */
+#define ASHKV_PAGE_NONE  (-1)  /* the tier has no codec */
+#define ASHKV_PAGE_BF16  0     /* the page's rows in the KV pool */
+#define ASHKV_PAGE_INT8  1     /* [2T fp16 row scales | pad to 16 | int8 codes] (the hooks' layout) */
+#define ASHKV_PAGE_FP8   2     /* FP8Codec: e4m3fn bytes */
+#define ASHKV_PAGE_INT4  3     /* INT4Codec, group 64: [E/64 bf16 scales | E/2 nibble bytes] */
+#define ASHKV_PAGE_NBIT4 4     /* DitheredNBitCodec(bits=4): [u32 n_out, 12 B | E/32 bf16 delta | codes | outliers] */
+#define ASHKV_PAGE_NBIT2 5     /* DitheredINT2Codec: the same layout with 2-bit codes */
+
+#define ASHKV_MIGRATE_OK        0
+#define ASHKV_MIGRATE_NO_SLOT   1
+#define ASHKV_MIGRATE_BAD_PAGE  2
+#define ASHKV_MIGRATE_PINNED    3
+#define ASHKV_MIGRATE_SAME_TIER 4
+#define ASHKV_MIGRATE_NO_CODEC  5
+#define ASHKV_MIGRATE_OVERFLOW  6
+
+typedef struct {
+  void* d_data;          /* n_slots * slot_bytes bytes, 16-byte aligned */
+  int64_t slot_bytes;    /* multiple of 16 */
+  int32_t n_slots;       /* at most 2^24 - 1 */
+  int32_t format;        /* ASHKV_PAGE_* */
+  int32_t* d_free_stack; /* [n_slots] */
+  int32_t* d_free_top;   /* [1] */
+} ashkv_tier_store_t;
+
+/* Bytes of one slot of `format` (rounded up to 256); -1 for a bad argument. */
+ASHKV_API int64_t ashkv_page_slot_bytes(int32_t format, int32_t tokens_per_page, int32_t row_len,
+                                        int32_t outlier_cap);
+
+ASHKV_API ashkv_status_t ashkv_migrate_pages(
+    int8_t* d_tier, const int32_t* d_pin, const int32_t* d_layer_id, const int32_t* d_token_start,
+    int32_t* d_page_slot, int64_t n_pages, const int8_t* d_target, const int32_t* d_list, const int32_t* d_count,
+    int32_t max_entries, const uint64_t* d_layer_k, const uint64_t* d_layer_v, int32_t n_layers,
+    int32_t tokens_per_page, int32_t row_len, int64_t row_stride, const ashkv_tier_store_t* stores, float sigma,
+    uint64_t seed, int32_t outlier_cap, int32_t* d_entry_status, int32_t* d_released, void* stream);
+
+ASHKV_API ashkv_status_t ashkv_release_slots(const int32_t* d_released, const int32_t* d_count, int32_t max_entries,
+                                             const ashkv_tier_store_t* stores, uint32_t* d_status, void* stream);
+
+/* ========================================================================
  * ashkv_policy_step without a scratch argument.  No counterpart in the
  * reference: it exists for callers that cannot allocate device memory while
  * they plan a step (an engine that has reserved nearly all HBM for its KV

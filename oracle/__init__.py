@@ -376,3 +376,79 @@ def page_features(k, tokens_per_page, token_saliency=None):
         raw = np.array([s[p * tokens_per_page:(p + 1) * tokens_per_page].sum() for p in range(n_pages)])
         S = raw / raw.max() if raw.max() > 0 else raw * 0
     return S, N
+
+
+# --------------------------------------------------------------------- tiered pages
+# Page formats of the batched migration (ashkv_migrate_pages): a page is the
+# bf16 values of its K rows then its V rows (E = 2 * T * row_len elements).
+PAGE_BF16, PAGE_INT8, PAGE_FP8, PAGE_INT4, PAGE_NBIT4, PAGE_NBIT2 = 0, 1, 2, 3, 4, 5
+
+
+def _int8_codes_offset(T: int) -> int:
+    return (4 * T + 15) // 16 * 16
+
+
+def page_encode(fmt: int, page_bits: np.ndarray, T: int, row_len: int, *, page_id: int = 0, seed: int = 0,
+                sigma: float = 3.0, outlier_cap: int = 0):
+    """bf16 page -> (slot bytes it defines, tie mask over those bytes, n_outliers).
+
+    INT8: rows of ``row_len`` with fp16 scales (the hooks' row codec,
+    ashkv/codecs/int8.py:50-81); FP8: FP8Codec (ashkv/codecs/fp8.py:32-79);
+    INT4: INT4Codec, group 64 (ashkv/codecs/int4.py:38-75); NBIT4/NBIT2:
+    DitheredNBitCodec / DitheredINT2Codec group arithmetic
+    (ashkv/codecs/nbit_dithered.py:57-104) with U from Philox4x32-10(seed) at
+    element offset page_id * E.  The tie mask marks INT8 code bytes that may be
+    one apart (see int8_encode)."""
+    x = np.ascontiguousarray(page_bits, dtype=np.uint16).reshape(-1)
+    E = 2 * T * row_len
+    assert x.size == E
+    if fmt == PAGE_INT8:
+        codes, scales, tie = int8_encode(x, row_len, scale_fp16=True, with_ties=True)
+        c0 = _int8_codes_offset(T)
+        out = np.zeros(c0 + E, np.uint8)
+        out[:4 * T] = scales.view(np.uint8)
+        out[c0:] = codes.view(np.uint8).reshape(-1)
+        ties = np.zeros(out.size, bool)
+        ties[c0:] = tie.reshape(-1)
+        return out, ties, 0
+    if fmt == PAGE_FP8:
+        out = fp8_encode(x)
+        return out, np.zeros(out.size, bool), 0
+    if fmt == PAGE_INT4:
+        scales, packed, _ = int4_encode(x, 64)
+        out = np.concatenate([scales.view(np.uint8), packed])
+        return out, np.zeros(out.size, bool), 0
+    bits = 4 if fmt == PAGE_NBIT4 else 2
+    U = philox_dither(E, seed, page_id * E)
+    sc, codes, idx, vals = nbit_encode(x, bits, U, sigma)
+    n_out = idx.size
+    hdr = np.zeros(16, np.uint8)
+    hdr[:4] = np.array([n_out if n_out <= outlier_cap else 0], np.uint32).view(np.uint8)
+    ent = ((idx.astype(np.uint32) << 16) | vals.astype(np.uint32)).astype(np.uint32)
+    body = [hdr, sc.view(np.uint8), codes]
+    if n_out <= outlier_cap:
+        body.append(ent.view(np.uint8))
+    out = np.concatenate(body)
+    return out, np.zeros(out.size, bool), n_out
+
+
+def page_decode(fmt: int, slot: np.ndarray, T: int, row_len: int, *, outlier_cap: int = 0) -> np.ndarray:
+    """Slot bytes -> bf16 page (the inverse codecs; INT8 decode as int8.py:98-116)."""
+    s = np.ascontiguousarray(slot, dtype=np.uint8).reshape(-1)
+    E = 2 * T * row_len
+    if fmt == PAGE_INT8:
+        c0 = _int8_codes_offset(T)
+        scales = s[:4 * T].copy().view(np.uint16)
+        codes = s[c0:c0 + E].copy().view(np.int8).reshape(2 * T, row_len)
+        return int8_decode(codes, scales, scale_fp16=True).reshape(-1)
+    if fmt == PAGE_FP8:
+        return fp8_decode(s[:E])
+    if fmt == PAGE_INT4:
+        return int4_decode(s[:E // 32].copy().view(np.uint16), s[E // 32:E // 32 + E // 2], 64)
+    bits = 4 if fmt == PAGE_NBIT4 else 2
+    n_out = min(int(s[:4].copy().view(np.uint32)[0]), outlier_cap)
+    d0, c0 = 16, 16 + E // 16
+    e0 = c0 + E * bits // 8
+    ent = s[e0:e0 + 4 * n_out].copy().view(np.uint32)
+    return nbit_decode(s[d0:c0].copy().view(np.uint16), s[c0:e0], bits, (ent >> 16).astype(np.int32),
+                       (ent & 0xFFFF).astype(np.uint16))

@@ -17,7 +17,9 @@ from conftest import assert_int8_codes, assert_int8_roundtrip
 from ashkv.adapters.sglang.allocator import SGLangShadowAllocator
 from ashkv.adapters.sglang.hooks import SGLangHooks
 from ashkv.contracts import ASHKVConfig, Tier
-from ashkv.runtime.batch import BatchMigrator, DevicePageTable, KVLayers, SlotArena, int8_page_slot_bytes
+from ashkv import _native
+from ashkv.runtime.batch import (BatchMigrator, DevicePageTable, Int8PageCodec, KVLayers, SlotArena, TierStore,
+                                int8_page_slot_bytes)
 
 pytestmark = pytest.mark.gpu
 
@@ -206,8 +208,8 @@ def test_shadow_allocator_arena(cuda):
 
 @pytest.mark.parametrize("heads", [8, 4, 2, 1])
 def test_batch_policy_demote_promote_pages(cuda, heads):
-    """Config-4 style: score -> tier -> gather+INT8 encode of demoted pages into arena
-    slots, then decode+scatter back; bytes compared with the oracle per token row."""
+    """Config-4 style: score -> tier -> gather+INT8 encode of the demoted pages into the FP8
+    tier's store, then decode+scatter back; bytes compared with the oracle per token row."""
     layers, tokens, T = 4, 4096, 16
     pages_per_layer = tokens // T
     g = torch.Generator(device=cuda).manual_seed(11)
@@ -220,38 +222,38 @@ def test_batch_policy_demote_promote_pages(cuda, heads):
         getattr(tab, name).copy_(torch.rand(n, generator=g, device=cuda))
     tab.layer.copy_(torch.arange(n, device=cuda) // pages_per_layer)
     tab.token_start.copy_((torch.arange(n, device=cuda) % pages_per_layer) * T)
-    slot = int8_page_slot_bytes(T, kv.row_len)
-    arena = SlotArena(n, slot, cuda)
+    store = TierStore(_native.PAGE_INT8, n, cuda, T, kv.row_len)
     keys = [(0, 1), (1, 0), (1, 2), (2, 1)]
-    mig = BatchMigrator(tab, kv, arena, ASHKVConfig(), keys, keep_scores=True)
+    mig = BatchMigrator(tab, kv, {int(Tier.FP8): store}, ASHKVConfig(), keys, keep_scores=True)
     L = mig.plan(0.9)
     nd, npro = L.counts.tolist()
     assert npro == 0 and nd > n // 10
     orig_k = [t.clone() for t in k]
     mig.demote()
     torch.cuda.synchronize()
-    assert arena.free_count() == n - nd
-    assert int(mig.status_encode[:nd].abs().sum()) == 0
+    assert store.free_count() == n - nd
+    assert int(mig.status[:nd].abs().sum()) == 0 and bool((mig.released[:nd] == -1).all())
     rows = L.demote[:nd].long()
-    assert bool((tab.slot[rows] >= 0).all())
-    # wipe the demoted pages' K/V, then decode them back from their slots
+    assert bool((tab.slot[rows] >= 0).all()) and bool((tab.tier[rows] == int(Tier.FP8)).all())
+    # wipe the pool, then promote the demoted pages back from their slots
     for li in range(layers):
         k[li].zero_(); v[li].zero_()
-    mig.decode(L.demote, L.counts[0:1], free_slots=True)
+    back = torch.zeros(n, dtype=torch.int8, device=cuda)
+    mig.migrate(L.demote, L.counts[0:1], target=back)
     torch.cuda.synchronize()
-    assert arena.free_count() == n
+    assert store.free_count() == n
+    assert int(mig.status[:nd].abs().sum()) == 0 and bool((tab.tier[rows] == 0).all())
+    assert int(tab.slot.ne(-1).sum()) == 0
     sample = rows[:: max(1, nd // 50)].cpu().numpy()
     for p in sample:
         li, ts = int(p) // pages_per_layer, (int(p) % pages_per_layer) * T
         src = u16(orig_k[li][ts:ts + T]).reshape(T, -1)
         assert_int8_roundtrip(u16(k[li][ts:ts + T]), src, kv.row_len)
-    # pages that were not demoted stay wiped (decode touched only listed pages)
+    # pages that were not demoted stay wiped (the promotion touched only listed pages)
     keep = np.setdiff1d(np.arange(n), rows.cpu().numpy())[:5]
     for p in keep:
         li, ts = int(p) // pages_per_layer, (int(p) % pages_per_layer) * T
         assert bool((k[li][ts:ts + T] == 0).all())
-    mig.commit_transitions()
-    assert bool((tab.tier[rows] == 1).all())
 
 
 @pytest.mark.parametrize("heads,T", [(1, 16), (2, 12), (8, 16)])
@@ -275,7 +277,7 @@ def test_batch_pages_many_entries_per_cta(cuda, heads, T):
     tab.layer[bad] = layers
     sb = int8_page_slot_bytes(T, L)
     arena = SlotArena(n, sb, cuda)
-    mig = BatchMigrator(tab, kv, arena, ASHKVConfig(), [(0, 1), (1, 0)], tokens_per_page=T)
+    mig = Int8PageCodec(tab, kv, arena, tokens_per_page=T)
     lst = torch.randperm(n, generator=g, device=cuda).to(torch.int32)
     cnt = torch.tensor([n], dtype=torch.int32, device=cuda)
     orig = [[t.clone() for t in k], [t.clone() for t in v]]
@@ -340,7 +342,7 @@ def test_batch_pages_nan_inf_rows_match_oracle(cuda, heads):
     tab.token_start.copy_(torch.arange(ppl, device=cuda, dtype=torch.int32) * T)
     sb = int8_page_slot_bytes(T, L)
     arena = SlotArena(ppl, sb, cuda)
-    mig = BatchMigrator(tab, kv, arena, ASHKVConfig(), [(0, 1), (1, 0)])
+    mig = Int8PageCodec(tab, kv, arena)
     lst = torch.arange(ppl, dtype=torch.int32, device=cuda)
     mig.encode(lst, torch.tensor([ppl], dtype=torch.int32, device=cuda))
     torch.cuda.synchronize()
@@ -365,7 +367,7 @@ def test_batch_encode_runs_out_of_slots(cuda):
     tab = DevicePageTable.empty(n, cuda)
     tab.token_start.copy_(torch.arange(n, device=cuda, dtype=torch.int32) * T)
     arena = SlotArena(10, int8_page_slot_bytes(T, kv.row_len), cuda)
-    mig = BatchMigrator(tab, kv, arena, ASHKVConfig(), [(0, 1), (1, 0)])
+    mig = Int8PageCodec(tab, kv, arena)
     lst = torch.arange(n, dtype=torch.int32, device=cuda)
     cnt = torch.tensor([n], dtype=torch.int32, device=cuda)
     mig.encode(lst, cnt)
