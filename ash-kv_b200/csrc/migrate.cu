@@ -26,6 +26,11 @@
 //      stacks are only popped in this kernel and only pushed in that one.
 // Entries are resolved 32 at a time by one warp (list -> page -> table
 // columns -> slot) so that chain of dependent loads is paid once per batch.
+// Two launches share a list.  The direct pass moves the edges that need no
+// staging tile (BF16 -> INT8 row by row, BF16 -> FP8 chunk by chunk, and every
+// decode into BF16, which first copies the compressed slot into shared memory
+// with cp.async) and reports the entries that do not move; the staged pass
+// (the tile above, and the dithered encoder's registers) takes the rest.
 #include <algorithm>
 
 #include "common.cuh"
@@ -41,6 +46,8 @@ constexpr int kWarps = kThreads / 32;
 constexpr int kTiers = 6;
 constexpr int kBatch = 32;
 constexpr int kMaxElems = 65536;  // 128 KiB of staging; outlier indices fit in 16 bits
+constexpr int kDirectBlocks = 3;  // CTAs per SM of the direct pass (registers <= 85)
+constexpr int kStagedBlocks = 3;  // CTAs per SM of the staged pass (registers <= 85, 3 x 68 KiB)
 
 struct Store {
   uint8_t* data;
@@ -77,6 +84,7 @@ struct MigParams {
 };
 
 struct Entry {
+  uint64_t kbase, vbase;  // K / V row of the page's first token in the pool
   int32_t page, cur, tgt, layer, ts, old_slot, new_slot, status;
 };
 
@@ -107,6 +115,20 @@ int64_t slot_bytes_for(int32_t format, int64_t E, int32_t cap) {
   return b;
 }
 
+// Bytes of a slot that hold data (rounded up to 16; slots are rounded to 256).
+__host__ __device__ __forceinline__ int64_t used_bytes(int32_t format, int64_t E, int T, int32_t cap) {
+  int64_t b = 0;
+  switch (format) {
+    case ASHKV_PAGE_INT8: b = int8_codes_offset(T) + E; break;
+    case ASHKV_PAGE_FP8: b = E; break;
+    case ASHKV_PAGE_INT4: b = E / 32 + E / 2; break;
+    case ASHKV_PAGE_NBIT4: b = nbit_entries_off(E, 4) + 4 * int64_t(cap); break;
+    case ASHKV_PAGE_NBIT2: b = nbit_entries_off(E, 2) + 4 * int64_t(cap); break;
+    default: break;
+  }
+  return (b + 15) / 16 * 16;
+}
+
 // Byte offset of element e in the staging tile: group g = e / 32 is a 64-byte
 // row; 16-byte chunk k of it sits at position k ^ ((g >> 1) & 3).
 __device__ __forceinline__ uint32_t stage_off(uint32_t e) {
@@ -122,27 +144,68 @@ __device__ __forceinline__ void sts_chunk(uint8_t* stage, uint32_t e, uint4 v) {
 
 __device__ __forceinline__ uint16_t* pool_row(const MigParams& p, const Entry& en, int r) {
   const int T = p.T;
-  const uint64_t base = (r < T ? p.layer_k : p.layer_v)[en.layer];
-  return reinterpret_cast<uint16_t*>(base) + (int64_t(en.ts) + (r < T ? r : r - T)) * p.row_stride;
+  return reinterpret_cast<uint16_t*>(r < T ? en.kbase : en.vbase) + int64_t(r < T ? r : r - T) * p.row_stride;
+}
+// Chunk k (8 elements) of the page -> its address in the pool.
+template <int ROW>
+__device__ __forceinline__ uint16_t* pool_chunk(const MigParams& p, const Entry& en, int k) {
+  constexpr int CPR = ROW / 8;
+  return pool_row(p, en, k / CPR) + (k % CPR) * 8;
+}
+
+// 16-byte asynchronous global -> shared copy: no register staging, so every
+// chunk of a page can be in flight at once; cp.async.wait_all completes them.
+__device__ __forceinline__ void cp_async16(uint32_t smem_addr, const void* gptr) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" :: "r"(smem_addr), "l"(gptr) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+__device__ __forceinline__ uint2 ld_nc_v2(const void* p) {
+  uint2 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v2.u32 {%0,%1}, [%2];" : "=r"(r.x), "=r"(r.y) : "l"(p));
+  return r;
+}
+
+// ---------------------------------------------------------------- 8-element decoders
+// Eight INT8 codes with scale s -> eight bf16 (the reference decode).
+__device__ __forceinline__ uint4 int8_dec8(uint2 cw, float s) {
+  const Recip y = make_recip(127.0f);
+  const f2 YHI = pk2(y.hi, y.hi), YLO = pk2(y.lo, y.lo), S = pk2(s, s);
+  const bool fast = int8_dec_fast(s);
+  const uint32_t ww[2] = {cw.x, cw.y};
+  uint32_t o[4];
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    f2 F0, F1;
+    int8x4_to_f2(ww[h], F0, F1);
+    if (fast) {
+      o[2 * h] = f32x2_to_bf16x2_pk(div2_short(mul2(F0, S), YHI, YLO));
+      o[2 * h + 1] = f32x2_to_bf16x2_pk(div2_short(mul2(F1, S), YHI, YLO));
+    } else {
+      float a, b;
+      upk2(F0, a, b);
+      o[2 * h] = f32x2_to_bf16x2(__fdiv_rn(__fmul_rn(a, s), 127.0f), __fdiv_rn(__fmul_rn(b, s), 127.0f));
+      upk2(F1, a, b);
+      o[2 * h + 1] = f32x2_to_bf16x2(__fdiv_rn(__fmul_rn(a, s), 127.0f), __fdiv_rn(__fmul_rn(b, s), 127.0f));
+    }
+  }
+  return make_uint4(o[0], o[1], o[2], o[3]);
+}
+__device__ __forceinline__ uint4 fp8_dec8(uint2 c) {
+  return make_uint4(bf16x2_from_fp8x2(c.x & 0xFFFFu), bf16x2_from_fp8x2(c.x >> 16),
+                    bf16x2_from_fp8x2(c.y & 0xFFFFu), bf16x2_from_fp8x2(c.y >> 16));
+}
+__device__ __forceinline__ uint4 int4_dec8(uint32_t c, uint16_t scale) {
+  uint32_t o[4];
+  unpack_nibbles8(c, bf16_to_f32(scale), o);
+  return make_uint4(o[0], o[1], o[2], o[3]);
 }
 
 // ---------------------------------------------------------------- decoders (slot -> staging)
 template <int ROW>
 __device__ void stage_from_pool(const MigParams& p, const Entry& en, uint8_t* stage, int n8) {
-  constexpr int CPR = ROW / 8;  // chunks per row
-  for (int k0 = threadIdx.x; k0 < n8; k0 += 4 * kThreads) {
-    uint4 v[4];
-#pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      const int k = k0 + u * kThreads;
-      if (k < n8) v[u] = ld_nc_v4(pool_row(p, en, k / CPR) + (k % CPR) * 8);
-    }
-#pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      const int k = k0 + u * kThreads;
-      if (k < n8) sts_chunk(stage, uint32_t(k) * 8u, v[u]);
-    }
-  }
+  const uint32_t base = smem_u32(stage);
+  for (int k = threadIdx.x; k < n8; k += kThreads) cp_async16(base + stage_off(uint32_t(k) * 8u), pool_chunk<ROW>(p, en, k));
+  cp_async_wait_all();
 }
 
 template <int ROW>
@@ -151,48 +214,55 @@ __device__ void stage_from_int8(const uint8_t* slot, int T, uint8_t* stage, int 
   const uint8_t* codes = slot + int8_codes_offset(T);
   const Recip y = make_recip(127.0f);
   const f2 YHI = pk2(y.hi, y.hi), YLO = pk2(y.lo, y.lo);
-  for (int k = threadIdx.x; k < n8; k += kThreads) {
-    const float s = f16_to_f32(reinterpret_cast<const uint16_t*>(slot)[k / CPR]);
-    const uint2 cw = *reinterpret_cast<const uint2*>(codes + int64_t(k) * 8);
-    const uint32_t ww[2] = {cw.x, cw.y};
-    uint32_t o[4];
-    const bool fast = int8_dec_fast(s);
-    const f2 S = pk2(s, s);
+  constexpr int U = 4;
+  (void)YHI; (void)YLO;
+  for (int k0 = threadIdx.x; k0 < n8; k0 += U * kThreads) {
+    uint2 cw[U];
+    uint16_t sc[U];
 #pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      f2 F0, F1;
-      int8x4_to_f2(ww[h], F0, F1);
-      if (fast) {
-        o[2 * h] = f32x2_to_bf16x2_pk(div2_short(mul2(F0, S), YHI, YLO));
-        o[2 * h + 1] = f32x2_to_bf16x2_pk(div2_short(mul2(F1, S), YHI, YLO));
-      } else {
-        float a, b;
-        upk2(F0, a, b);
-        o[2 * h] = f32x2_to_bf16x2(__fdiv_rn(__fmul_rn(a, s), 127.0f), __fdiv_rn(__fmul_rn(b, s), 127.0f));
-        upk2(F1, a, b);
-        o[2 * h + 1] = f32x2_to_bf16x2(__fdiv_rn(__fmul_rn(a, s), 127.0f), __fdiv_rn(__fmul_rn(b, s), 127.0f));
+    for (int u = 0; u < U; ++u) {
+      const int k = k0 + u * kThreads;
+      if (k < n8) {
+        cw[u] = ld_nc_v2(codes + int64_t(k) * 8);
+        sc[u] = reinterpret_cast<const uint16_t*>(slot)[k / CPR];
       }
     }
-    sts_chunk(stage, uint32_t(k) * 8u, make_uint4(o[0], o[1], o[2], o[3]));
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int k = k0 + u * kThreads;
+      if (k < n8) sts_chunk(stage, uint32_t(k) * 8u, int8_dec8(cw[u], f16_to_f32(sc[u])));
+    }
   }
 }
 
 __device__ void stage_from_fp8(const uint8_t* slot, uint8_t* stage, int n8) {
-  for (int k = threadIdx.x; k < n8; k += kThreads) {
-    const uint2 c = *reinterpret_cast<const uint2*>(slot + int64_t(k) * 8);
-    sts_chunk(stage, uint32_t(k) * 8u,
-              make_uint4(bf16x2_from_fp8x2(c.x & 0xFFFFu), bf16x2_from_fp8x2(c.x >> 16),
-                         bf16x2_from_fp8x2(c.y & 0xFFFFu), bf16x2_from_fp8x2(c.y >> 16)));
+  constexpr int U = 4;
+  for (int k0 = threadIdx.x; k0 < n8; k0 += U * kThreads) {
+    uint2 c[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u)
+      if (k0 + u * kThreads < n8) c[u] = ld_nc_v2(slot + int64_t(k0 + u * kThreads) * 8);
+#pragma unroll
+    for (int u = 0; u < U; ++u)
+      if (k0 + u * kThreads < n8) sts_chunk(stage, uint32_t(k0 + u * kThreads) * 8u, fp8_dec8(c[u]));
   }
 }
 
 __device__ void stage_from_int4(const uint8_t* slot, int64_t E, uint8_t* stage, int n8) {
   const uint16_t* scales = reinterpret_cast<const uint16_t*>(slot);
   const uint32_t* nib = reinterpret_cast<const uint32_t*>(slot + E / 32);
-  for (int k = threadIdx.x; k < n8; k += kThreads) {
-    uint32_t o[4];
-    unpack_nibbles8(nib[k], bf16_to_f32(scales[k >> 3]), o);
-    sts_chunk(stage, uint32_t(k) * 8u, make_uint4(o[0], o[1], o[2], o[3]));
+  constexpr int U = 4;
+  for (int k0 = threadIdx.x; k0 < n8; k0 += U * kThreads) {
+    uint32_t c[U];
+    uint16_t sc[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int k = k0 + u * kThreads;
+      if (k < n8) { c[u] = nib[k]; sc[u] = scales[k >> 3]; }
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u)
+      if (k0 + u * kThreads < n8) sts_chunk(stage, uint32_t(k0 + u * kThreads) * 8u, int4_dec8(c[u], sc[u]));
   }
 }
 
@@ -294,6 +364,125 @@ __device__ void int4_from_stage(const uint8_t* stage, int64_t E, uint8_t* slot) 
   }
 }
 
+// ---------------------------------------------------------------- direct paths (no staging tile)
+// BF16 -> INT8 walks the page row by row, BF16 -> FP8 chunk by chunk, and a
+// decode into BF16 needs no tile either: warps stream the page with several
+// rows in flight.  A compressed source is first copied whole into shared
+// memory with cp.async (all of its bytes in flight), then decoded from there
+// into the pool rows.
+
+// BF16 pool rows -> INT8 slot: TEAM lanes per row, NCH chunks per lane, U row
+// groups loaded before any is encoded.
+template <int ROW>
+__device__ void int8_from_pool(const MigParams& p, const Entry& en, uint8_t* slot) {
+  constexpr int TEAM = ROW >= 1024 ? 32 : ROW / 32;
+  constexpr int NCH = ROW / (8 * TEAM);
+  constexpr int RPW = 32 / TEAM;
+  constexpr int U = NCH <= 4 ? 2 : 1;
+  const int T = p.T;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int sub = lane / TEAM, lin = lane % TEAM;
+  uint8_t* codes = slot + int8_codes_offset(T);
+  for (int r0 = warp * RPW * U; r0 < 2 * T; r0 += kWarps * RPW * U) {  // warp-uniform
+    uint32_t w[U][4 * NCH];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int r = r0 + u * RPW + sub;
+      const uint16_t* row = r < 2 * T ? pool_row(p, en, r) : nullptr;
+#pragma unroll
+      for (int c = 0; c < NCH; ++c) {
+        const uint4 v = row ? ld_nc_v4(row + (c * TEAM + lin) * 8) : make_uint4(0, 0, 0, 0);
+        w[u][4 * c] = v.x; w[u][4 * c + 1] = v.y; w[u][4 * c + 2] = v.z; w[u][4 * c + 3] = v.w;
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int r = r0 + u * RPW + sub;
+      const float am = fmaxf(team_absmax_bf16<TEAM>(w[u]), 1e-8f);
+      if (r >= 2 * T) continue;
+      if (lin == 0) reinterpret_cast<uint16_t*>(slot)[r] = f32_to_f16(am);
+      const Int8Div d = int8_div(am);
+#pragma unroll
+      for (int c = 0; c < NCH; ++c)
+        *reinterpret_cast<uint2*>(codes + int64_t(r) * ROW + (c * TEAM + lin) * 8) = make_uint2(
+            int8_codes4_bf16(w[u][4 * c], w[u][4 * c + 1], d), int8_codes4_bf16(w[u][4 * c + 2], w[u][4 * c + 3], d));
+    }
+  }
+}
+
+// BF16 pool rows -> FP8 slot, U chunks in flight per thread.
+template <int ROW>
+__device__ void fp8_from_pool(const MigParams& p, const Entry& en, uint8_t* slot, int n8) {
+  constexpr int U = 4;
+  for (int k0 = threadIdx.x; k0 < n8; k0 += U * kThreads) {
+    uint4 v[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u)
+      if (k0 + u * kThreads < n8) v[u] = ld_nc_v4(pool_chunk<ROW>(p, en, k0 + u * kThreads));
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int k = k0 + u * kThreads;
+      if (k >= n8) continue;
+      *reinterpret_cast<uint2*>(slot + int64_t(k) * 8) =
+          make_uint2(fp8x2_from_bf16x2(v[u].x) | (fp8x2_from_bf16x2(v[u].y) << 16),
+                     fp8x2_from_bf16x2(v[u].z) | (fp8x2_from_bf16x2(v[u].w) << 16));
+    }
+  }
+}
+
+// Copy `bytes` (a multiple of 16) of a slot into shared memory.
+__device__ __forceinline__ void raw_copy(const uint8_t* slot, int64_t bytes, uint8_t* raw) {
+  const uint32_t base = smem_u32(raw);
+  for (int64_t o = int64_t(threadIdx.x) * 16; o < bytes; o += kThreads * 16) cp_async16(base + uint32_t(o), slot + o);
+  cp_async_wait_all();
+  __syncthreads();
+}
+
+// INT8 / FP8 / INT4 bytes in shared memory -> BF16 pool rows.
+template <int ROW, int FMT>
+__device__ void pool_from_raw(const MigParams& p, const Entry& en, const uint8_t* raw, int64_t E, int n8) {
+  constexpr int CPR = ROW / 8;
+  for (int k = threadIdx.x; k < n8; k += kThreads) {
+    uint4 o;
+    if constexpr (FMT == ASHKV_PAGE_INT8) {
+      const uint2 cw = *reinterpret_cast<const uint2*>(raw + int8_codes_offset(p.T) + int64_t(k) * 8);
+      o = int8_dec8(cw, f16_to_f32(reinterpret_cast<const uint16_t*>(raw)[k / CPR]));
+    } else if constexpr (FMT == ASHKV_PAGE_FP8) {
+      o = fp8_dec8(*reinterpret_cast<const uint2*>(raw + int64_t(k) * 8));
+    } else {
+      o = int4_dec8(reinterpret_cast<const uint32_t*>(raw + E / 32)[k], reinterpret_cast<const uint16_t*>(raw)[k >> 3]);
+    }
+    *reinterpret_cast<uint4*>(pool_chunk<ROW>(p, en, k)) = o;
+  }
+}
+
+// Dithered N-bit bytes in shared memory -> BF16 pool rows; a group never crosses a row.
+template <int ROW, int BITS>
+__device__ void pool_from_nbit(const MigParams& p, const Entry& en, const uint8_t* raw, int64_t E) {
+  const uint16_t* delta = reinterpret_cast<const uint16_t*>(raw + nbit_delta_off());
+  const uint8_t* codes = raw + nbit_codes_off(E);
+  const int n_groups = int(E / 32);
+  constexpr float half = float((1 << BITS) - 1) * 0.5f;
+  for (int g = threadIdx.x; g < n_groups; g += kThreads) {
+    GroupCodes<BITS> gc;
+    load_group<BITS>(delta, codes, g, gc);
+    uint32_t o[16];
+    group_bf16<BITS>(gc, half, o);
+    uint16_t* dst = pool_chunk<ROW>(p, en, 4 * g);
+#pragma unroll
+    for (int c = 0; c < 4; ++c)
+      *reinterpret_cast<uint4*>(dst + 8 * c) = make_uint4(o[4 * c], o[4 * c + 1], o[4 * c + 2], o[4 * c + 3]);
+  }
+  __syncthreads();  // dense values first, then the outliers overwrite theirs
+  const uint32_t n_out = min(*reinterpret_cast<const uint32_t*>(raw), uint32_t(p.outlier_cap));
+  const uint32_t* ent = reinterpret_cast<const uint32_t*>(raw + nbit_entries_off(E, BITS));
+  for (uint32_t j = threadIdx.x; j < n_out; j += kThreads) {
+    const uint32_t e = ent[j];
+    const uint32_t idx = e >> 16;
+    if (idx < uint32_t(E)) pool_row(p, en, int(idx / ROW))[idx % ROW] = uint16_t(e & 0xFFFFu);
+  }
+}
+
 __device__ __forceinline__ uint32_t block_exclusive_scan(uint32_t v, uint32_t* s_warp, uint32_t& total) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   uint32_t inc = v;
@@ -373,11 +562,29 @@ __device__ __forceinline__ int fmt_of(const MigParams& p, int t) {
   return (t >= 0 && t < kTiers) ? p.store[t].format : ASHKV_PAGE_NONE;
 }
 
+// Entries are processed by two launches over the same list.  The direct pass
+// moves the pages whose edge needs no staging tile (BF16 -> INT8 / FP8, and
+// every edge into BF16) and reports every entry that does not move; it marks
+// the other moving entries kDeferred without taking a slot, and the staged
+// pass (staging tile, the dithered encoder) moves only those.
+constexpr int kDirect = 0, kStaged = 1;
+constexpr int32_t kDeferred = 100;
+constexpr int32_t kNotMine = 101;
+
+__device__ __forceinline__ bool direct_edge(int fs, int ft) {
+  return ft == ASHKV_PAGE_BF16 || (fs == ASHKV_PAGE_BF16 && (ft == ASHKV_PAGE_INT8 || ft == ASHKV_PAGE_FP8));
+}
+
 // Resolve entry i (one lane): the migrate() ladder's checks, then the slot.
+template <int MODE>
 __device__ Entry resolve(const MigParams& p, int64_t i) {
   Entry e{};
   e.status = ASHKV_MIGRATE_BAD_PAGE;
   e.old_slot = e.new_slot = -1;
+  if (MODE == kStaged && p.entry_status[i] != kDeferred) {
+    e.status = kNotMine;
+    return e;
+  }
   const int32_t page = p.list[i];
   e.page = page;
   if (page < 0 || page >= p.n_pages) return e;
@@ -393,6 +600,12 @@ __device__ Entry resolve(const MigParams& p, int64_t i) {
   if (fs == ASHKV_PAGE_NONE || ft == ASHKV_PAGE_NONE) { e.status = ASHKV_MIGRATE_NO_CODEC; return e; }
   if (e.layer < 0 || e.layer >= p.n_layers || e.ts < 0) return e;
   if (fs != ASHKV_PAGE_BF16 && (e.old_slot < 0 || e.old_slot >= p.store[e.cur].n_slots)) return e;
+  e.kbase = p.layer_k[e.layer] + uint64_t(e.ts) * uint64_t(p.row_stride) * 2u;
+  e.vbase = p.layer_v[e.layer] + uint64_t(e.ts) * uint64_t(p.row_stride) * 2u;
+  if (MODE == kDirect && !direct_edge(fs, ft)) {
+    e.status = kDeferred;
+    return e;
+  }
   if (ft != ASHKV_PAGE_BF16) {
     const Store& s = p.store[e.tgt];
     const int32_t pos = atomicSub(s.free_top, 1) - 1;
@@ -412,8 +625,9 @@ __device__ Entry resolve(const MigParams& p, int64_t i) {
   return e;
 }
 
-template <int ROW>
-__global__ void __launch_bounds__(kThreads, 2) migrate_pages_kernel(const MigParams p) {
+template <int ROW, int MODE>
+__global__ void __launch_bounds__(kThreads, MODE == kDirect ? kDirectBlocks : kStagedBlocks)
+    migrate_pages_kernel(const MigParams p) {
   extern __shared__ __align__(16) uint8_t smem[];
   __shared__ Entry s_ent[kBatch];
   __shared__ uint32_t s_warp[kWarps];
@@ -421,17 +635,18 @@ __global__ void __launch_bounds__(kThreads, 2) migrate_pages_kernel(const MigPar
   const int T = p.T;
   const int64_t E = 2 * int64_t(T) * ROW;
   const int n8 = int(E / 8);
-  uint8_t* stage = smem;
+  uint8_t* stage = smem;  // direct pass: the raw copy of a compressed source
   uint32_t* s_omask = reinterpret_cast<uint32_t*>(smem + E * 2);
   const int32_t count = min(*p.count, p.max_entries);
   for (int64_t b0 = blockIdx.x; b0 < count; b0 += int64_t(kBatch) * gridDim.x) {
     const int64_t left = (count - b0 + gridDim.x - 1) / gridDim.x;
     const int nb = left < kBatch ? int(left) : kBatch;
-    if (threadIdx.x < nb) s_ent[threadIdx.x] = resolve(p, b0 + int64_t(threadIdx.x) * gridDim.x);
+    if (threadIdx.x < nb) s_ent[threadIdx.x] = resolve<MODE>(p, b0 + int64_t(threadIdx.x) * gridDim.x);
     __syncthreads();
     for (int k = 0; k < nb; ++k) {
       const Entry en = s_ent[k];
       const int64_t i = b0 + int64_t(k) * gridDim.x;
+      if (en.status == kNotMine) continue;
       bool ok = en.status == ASHKV_MIGRATE_OK;
       if (ok) {
         const int fs = p.store[en.cur].format, ft = p.store[en.tgt].format;
@@ -439,38 +654,56 @@ __global__ void __launch_bounds__(kThreads, 2) migrate_pages_kernel(const MigPar
                                                    : p.store[en.cur].data + int64_t(en.old_slot) * p.store[en.cur].slot_bytes;
         uint8_t* dst = ft == ASHKV_PAGE_BF16 ? nullptr
                                              : p.store[en.tgt].data + int64_t(en.new_slot) * p.store[en.tgt].slot_bytes;
-        switch (fs) {
-          case ASHKV_PAGE_BF16: stage_from_pool<ROW>(p, en, stage, n8); break;
-          case ASHKV_PAGE_INT8: stage_from_int8<ROW>(src, T, stage, n8); break;
-          case ASHKV_PAGE_FP8: stage_from_fp8(src, stage, n8); break;
-          case ASHKV_PAGE_INT4: stage_from_int4(src, E, stage, n8); break;
-          case ASHKV_PAGE_NBIT4: stage_from_nbit<4>(src, E, p.outlier_cap, stage); break;
-          default: stage_from_nbit<2>(src, E, p.outlier_cap, stage); break;
+        if constexpr (MODE == kDirect) {
+          if (fs == ASHKV_PAGE_BF16 && ft == ASHKV_PAGE_INT8) {
+            int8_from_pool<ROW>(p, en, dst);
+          } else if (fs == ASHKV_PAGE_BF16) {
+            fp8_from_pool<ROW>(p, en, dst, n8);
+          } else {  // into BF16
+            raw_copy(src, used_bytes(fs, E, T, p.outlier_cap), stage);
+            switch (fs) {
+              case ASHKV_PAGE_INT8: pool_from_raw<ROW, ASHKV_PAGE_INT8>(p, en, stage, E, n8); break;
+              case ASHKV_PAGE_FP8: pool_from_raw<ROW, ASHKV_PAGE_FP8>(p, en, stage, E, n8); break;
+              case ASHKV_PAGE_INT4: pool_from_raw<ROW, ASHKV_PAGE_INT4>(p, en, stage, E, n8); break;
+              case ASHKV_PAGE_NBIT4: pool_from_nbit<ROW, 4>(p, en, stage, E); break;
+              default: pool_from_nbit<ROW, 2>(p, en, stage, E); break;
+            }
+            __syncthreads();  // the raw copy is free again
+          }
+        } else {
+          switch (fs) {
+            case ASHKV_PAGE_BF16: stage_from_pool<ROW>(p, en, stage, n8); break;
+            case ASHKV_PAGE_INT8: stage_from_int8<ROW>(src, T, stage, n8); break;
+            case ASHKV_PAGE_FP8: stage_from_fp8(src, stage, n8); break;
+            case ASHKV_PAGE_INT4: stage_from_int4(src, E, stage, n8); break;
+            case ASHKV_PAGE_NBIT4: stage_from_nbit<4>(src, E, p.outlier_cap, stage); break;
+            default: stage_from_nbit<2>(src, E, p.outlier_cap, stage); break;
+          }
+          __syncthreads();
+          switch (ft) {
+            case ASHKV_PAGE_BF16: pool_from_stage<ROW>(p, en, stage, n8); break;
+            case ASHKV_PAGE_INT8: int8_from_stage<ROW>(stage, T, dst); break;
+            case ASHKV_PAGE_FP8: fp8_from_stage(stage, dst, n8); break;
+            case ASHKV_PAGE_INT4: int4_from_stage(stage, E, dst); break;
+            case ASHKV_PAGE_NBIT4: ok = nbit_from_stage<4>(p, en, stage, E, dst, s_omask, s_warp); break;
+            default: ok = nbit_from_stage<2>(p, en, stage, E, dst, s_omask, s_warp); break;
+          }
+          if (threadIdx.x == 0) s_ok = ok;
+          __syncthreads();  // staging, s_omask and s_warp are free again; s_ok visible
+          ok = s_ok != 0;
         }
-        __syncthreads();
-        switch (ft) {
-          case ASHKV_PAGE_BF16: pool_from_stage<ROW>(p, en, stage, n8); break;
-          case ASHKV_PAGE_INT8: int8_from_stage<ROW>(stage, T, dst); break;
-          case ASHKV_PAGE_FP8: fp8_from_stage(stage, dst, n8); break;
-          case ASHKV_PAGE_INT4: int4_from_stage(stage, E, dst); break;
-          case ASHKV_PAGE_NBIT4: ok = nbit_from_stage<4>(p, en, stage, E, dst, s_omask, s_warp); break;
-          default: ok = nbit_from_stage<2>(p, en, stage, E, dst, s_omask, s_warp); break;
-        }
-        if (threadIdx.x == 0) s_ok = ok;
-        __syncthreads();  // staging, s_omask and s_warp are free again; s_ok visible
-        ok = s_ok != 0;
       }
       if (threadIdx.x == 0) {
         int32_t status = en.status, rel = -1;
-        if (en.status == ASHKV_MIGRATE_OK && ok) {
+        if (en.status == kDeferred) {
+          // moved by the staged pass
+        } else if (en.status == ASHKV_MIGRATE_OK && ok) {
           p.tier[en.page] = int8_t(en.tgt);
           p.page_slot[en.page] = en.new_slot;  // -1 when the page returns to its BF16 rows
           if (en.old_slot >= 0 && p.store[en.cur].format != ASHKV_PAGE_BF16) rel = (en.cur << 24) | en.old_slot;
         } else if (en.status == ASHKV_MIGRATE_OK) {
           status = ASHKV_MIGRATE_OVERFLOW;
           rel = (en.tgt << 24) | en.new_slot;
-        } else if (en.status == ASHKV_MIGRATE_NO_SLOT || en.new_slot < 0) {
-          rel = -1;
         }
         p.entry_status[i] = status;
         p.released[i] = rel;
@@ -507,17 +740,24 @@ __global__ void __launch_bounds__(256) release_slots_kernel(const ReleaseParams 
 bool row_ok(int32_t row) { return row == 128 || row == 256 || row == 512 || row == 1024 || row == 2048; }
 
 template <int ROW>
-ashkv_status_t launch_migrate(const MigParams& p, size_t smem, cudaStream_t st) {
-  const cudaError_t e = cudaFuncSetAttribute(migrate_pages_kernel<ROW>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             int(smem));
+ashkv_status_t launch_migrate(const MigParams& p, size_t raw_smem, size_t stage_smem, cudaStream_t st) {
+  const int sms = sm_count() > 0 ? sm_count() : 148;
+  cudaError_t e = cudaFuncSetAttribute(migrate_pages_kernel<ROW, kDirect>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, int(raw_smem));
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(migrate_pages_kernel<ROW, kStaged>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             int(stage_smem));
   if (e != cudaSuccess) {
     set_error("migrate_pages (shared memory attribute)", e);
     return ASHKV_LAUNCH_ERROR;
   }
-  const int sms = sm_count() > 0 ? sm_count() : 148;
-  const int64_t g = std::min<int64_t>(p.max_entries, int64_t(sms) * 2);
-  migrate_pages_kernel<ROW><<<unsigned(g > 0 ? g : 1), kThreads, smem, st>>>(p);
-  return check_launch("migrate_pages");
+  const int64_t gd = std::min<int64_t>(p.max_entries, int64_t(sms) * kDirectBlocks);
+  migrate_pages_kernel<ROW, kDirect><<<unsigned(gd > 0 ? gd : 1), kThreads, raw_smem, st>>>(p);
+  const ashkv_status_t rc = check_launch("migrate_pages (direct pass)");
+  if (rc != ASHKV_OK) return rc;
+  const int64_t gs = std::min<int64_t>(p.max_entries, int64_t(sms) * kStagedBlocks);
+  migrate_pages_kernel<ROW, kStaged><<<unsigned(gs > 0 ? gs : 1), kThreads, stage_smem, st>>>(p);
+  return check_launch("migrate_pages (staged pass)");
 }
 
 bool copy_stores(const ashkv_tier_store_t* stores, Store (&out)[kTiers], bool need_data) {
@@ -604,13 +844,21 @@ extern "C" ashkv_status_t ashkv_migrate_pages(
   }
   philox_round_keys(seed, p.round_keys);
   const size_t smem = size_t(E) * 2 + size_t(E / 32) * 4;
+  size_t raw = 16;
+  for (int t = 1; t < kTiers; ++t)
+    if (p.store[t].format != ASHKV_PAGE_NONE)
+      raw = std::max<size_t>(raw, size_t(used_bytes(p.store[t].format, E, tokens_per_page, outlier_cap)));
+  if (raw > size_t(200) * 1024) {
+    set_message("ashkv_migrate_pages: outlier_cap too large for one page in shared memory");
+    return ASHKV_BAD_ARGUMENT;
+  }
   cudaStream_t st = as_stream(stream);
   switch (row_len) {
-    case 128: return launch_migrate<128>(p, smem, st);
-    case 256: return launch_migrate<256>(p, smem, st);
-    case 512: return launch_migrate<512>(p, smem, st);
-    case 1024: return launch_migrate<1024>(p, smem, st);
-    default: return launch_migrate<2048>(p, smem, st);
+    case 128: return launch_migrate<128>(p, raw, smem, st);
+    case 256: return launch_migrate<256>(p, raw, smem, st);
+    case 512: return launch_migrate<512>(p, raw, smem, st);
+    case 1024: return launch_migrate<1024>(p, raw, smem, st);
+    default: return launch_migrate<2048>(p, raw, smem, st);
   }
 }
 

@@ -324,97 +324,228 @@ def run_reference(args) -> None:
 
 
 
-# ------------------------------------------------------------------ demote leg (config 4)
+# ------------------------------------------------------------------ migration legs (configs 4 and 5)
 DEMOTE_LAYERS, DEMOTE_HEADS, DEMOTE_TOKENS, DEMOTE_T = 64, 8, 32 * 8192, 16
+C5_PRESSURES = (0.5, 0.7, 0.9, 0.95, 0.96, 0.97)
+
+
+def page_format_bytes(fmt: int, E: int, T: int, n_out: float = 0.0) -> float:
+    """Algorithmic bytes of one page held in `fmt` (E elements of K then V rows)."""
+    from ashkv import _native as N
+    return {N.PAGE_BF16: 2 * E, N.PAGE_INT8: E + 4 * T, N.PAGE_FP8: E, N.PAGE_INT4: E // 2 + E // 32,
+            N.PAGE_NBIT4: 16 + E // 16 + E // 2 + 4 * n_out, N.PAGE_NBIT2: 16 + E // 16 + E // 4 + 4 * n_out}[fmt]
+
+
+class MigrationModel:
+    """The paged KV pool of the demote model on one rank: `layers` x K,V [tokens, heads, 128]
+    bf16 in 16-token pages, a replicated page table with U[0,1] features (same on every
+    rank), and one TierStore per compressed tier (slots for a fraction of the pages)."""
+
+    def __init__(self, dev, rank: int, layers: int, heads: int, formats: dict, slots: dict, seed: int):
+        from ashkv.contracts import ASHKVConfig
+        from ashkv.runtime.batch import BatchMigrator, DevicePageTable, KVLayers, TierStore
+        self.dev, self.T = dev, DEMOTE_T
+        ppl = DEMOTE_TOKENS // DEMOTE_T
+        self.n = layers * ppl
+        g = torch.Generator(device=dev).manual_seed(seed + rank)
+        k, v = [], []
+        for _ in range(layers):
+            k.append(torch.randn(DEMOTE_TOKENS, heads, 128, generator=g, device=dev).to(torch.bfloat16))
+            v.append(torch.randn(DEMOTE_TOKENS, heads, 128, generator=g, device=dev).to(torch.bfloat16))
+        self.k, self.v = k, v
+        self.kv = KVLayers(k, v)
+        self.E = 2 * DEMOTE_T * self.kv.row_len
+        self.tab = DevicePageTable.empty(self.n, dev)
+        idx = torch.arange(self.n, device=dev, dtype=torch.int64)
+        self.tab.layer.copy_(idx // ppl)
+        self.tab.token_start.copy_((idx % ppl) * DEMOTE_T)
+        self.stores = {t: TierStore(f, int(slots[t] * self.n), dev, DEMOTE_T, self.kv.row_len,
+                                    512 if f in (4, 5) else 0) for t, f in formats.items()}
+        keys = [(0, 1), (1, 0), (1, 2), (2, 1), (2, 3), (3, 2)]
+        self.mig = BatchMigrator(self.tab, self.kv, self.stores, ASHKVConfig(), keys, seed=4242)
+        self.formats = {0: 0, **formats}
+
+    def features(self, seed: int) -> None:
+        gf = torch.Generator(device=self.dev).manual_seed(seed)  # same features on every rank
+        for name in ("T", "S", "N", "P"):
+            getattr(self.tab, name).copy_(torch.rand(self.n, generator=gf, device=self.dev))
+
+    def place(self, tiers0: torch.Tensor) -> None:
+        """Encode every page from its BF16 rows straight into its starting tier (setup, untimed)."""
+        pages = (tiers0 != self.tab.tier).nonzero().flatten().to(torch.int32)
+        if pages.numel():
+            self.mig.migrate(pages, torch.tensor([pages.numel()], dtype=torch.int32, device=self.dev), target=tiers0)
+        torch.cuda.synchronize()
+        assert torch.equal(self.tab.tier, tiers0), "setup placement failed"
+
+    def restore(self, tiers0: torch.Tensor) -> None:
+        moved = (self.tab.tier != tiers0).nonzero().flatten().to(torch.int32)
+        if moved.numel():
+            self.mig.migrate(moved, torch.tensor([moved.numel()], dtype=torch.int32, device=self.dev), target=tiers0)
+
+    def free(self) -> None:
+        del self.k, self.v, self.kv, self.stores, self.mig, self.tab
+        torch.cuda.empty_cache()
+
+
+def edge_histogram(m: MigrationModel, tiers_before: torch.Tensor) -> dict:
+    after = m.tab.tier
+    moved = after != tiers_before
+    src, dst = tiers_before[moved].long(), after[moved].long()
+    h = torch.bincount(src * 8 + dst, minlength=64).cpu().tolist()
+    return {(i // 8, i % 8): c for i, c in enumerate(h) if c}
 
 
 def run_demote(dev, world: int, rank: int, dist, steps: int, warmup: int, layers: int = DEMOTE_LAYERS,
                head_split: int = 0) -> dict:
     """64-layer model, 8 KV heads x 128, 32 seq x 8192 tokens in 16-token
-    pages, features U[0,1], default policy, pressure 0.9.  KV heads are sharded over the
-    ranks (TP); the page table is replicated; the only collective is the MAX all-reduce of
-    the allocator pressure before each plan.  ``head_split`` > 0 runs one rank's share of
-    that split (8 / head_split heads) on this GPU alone.  One step = policy kernel (score -> tier ->
-    lists) + gather/INT8-encode of every page on the demotion list into arena slots
-    (demote) + decode of those pages back into the KV pool (promote)."""
-    from ashkv.contracts import ASHKVConfig
-    from ashkv.runtime.batch import BatchMigrator, DevicePageTable, KVLayers, SlotArena, int8_page_slot_bytes
-
+    pages, features U[0,1], default policy.  KV heads are sharded over the ranks (TP); the
+    page table is replicated; the only collective is the MAX all-reduce of the ranks'
+    allocator pressure (the FP8 tier store's occupancy) before each plan.  The pages the
+    policy would promote (R >= theta_high + delta, ~10%) start in the FP8 tier as INT8
+    slots, so one step runs the policy's own two lists: pressure all-reduce ->
+    ashkv_policy_step -> migrate the demotion list (BF16 -> INT8 slot) -> migrate the
+    promotion list (INT8 slot -> BF16), each followed by its slot release.  Steps are timed
+    with CUDA events; the pages are put back in their starting tiers between steps, outside
+    the timed events.  ``head_split`` > 0 runs one rank's share of that split on this GPU."""
     heads = DEMOTE_HEADS // (head_split or world)
-    pages_per_layer = DEMOTE_TOKENS // DEMOTE_T
-    n = layers * pages_per_layer
-    g = torch.Generator(device=dev).manual_seed(4000 + rank)
-    k, v = [], []
-    for _ in range(layers):
-        k.append(torch.randn(DEMOTE_TOKENS, heads, 128, generator=g, device=dev).to(torch.bfloat16))
-        v.append(torch.randn(DEMOTE_TOKENS, heads, 128, generator=g, device=dev).to(torch.bfloat16))
-    kv = KVLayers(k, v)
-    tab = DevicePageTable.empty(n, dev)
-    gf = torch.Generator(device=dev).manual_seed(4242)  # same features on every rank (replicated table)
-    for name in ("T", "S", "N", "P"):
-        getattr(tab, name).copy_(torch.rand(n, generator=gf, device=dev))
-    idx = torch.arange(n, device=dev, dtype=torch.int64)
-    tab.layer.copy_(idx // pages_per_layer)
-    tab.token_start.copy_((idx % pages_per_layer) * DEMOTE_T)
-    keys = [(0, 1), (1, 0), (1, 2), (2, 1), (0, 2), (2, 0), (2, 3), (3, 2)]
-    slot = int8_page_slot_bytes(DEMOTE_T, kv.row_len)
-    mig0 = BatchMigrator(tab, kv, SlotArena(1, slot, dev), ASHKVConfig(), keys)
-    n_demote = int(mig0.plan(0.9).counts[0].item())
-    arena = SlotArena(n_demote + 1024, slot, dev)
-    mig = BatchMigrator(tab, kv, arena, ASHKVConfig(), keys)
-    del mig0
-    local_p = torch.tensor([0.9], dtype=torch.float32, device=dev)
+    m = MigrationModel(dev, rank, layers, heads, {1: 1}, {1: 0.45}, seed=4000)
+    m.features(4242)
+    cfg = m.mig.cfg
+    R = torch.empty(m.n, dtype=torch.float32, device=dev)
+    from ashkv import _native
+    _native.score(m.tab.T, m.tab.S, m.tab.N, m.tab.P, cfg.w_T, cfg.w_S, cfg.w_N, cfg.w_P, R)
+    up = float(np.float32(cfg.theta_high + cfg.delta))
+    tiers0 = (R >= up).to(torch.int8)
+    m.place(tiers0)
     stream = torch.cuda.current_stream(dev)
 
     def step(ev=None):
-        pr = local_p.clone()
-        if dist:
-            dist.all_reduce(pr, op=dist.ReduceOp.MAX)
-        L = mig.plan(pr)  # read on the device: no host sync inside the step
         if ev is not None:
             ev[0].record(stream)
-        mig.demote()
+        pr = m.mig.pressure()  # the ranks' FP8-store occupancy, read on the device
+        if dist:
+            dist.all_reduce(pr, op=dist.ReduceOp.MAX)
+        m.mig.plan(pr)
         if ev is not None:
             ev[1].record(stream)
-        mig.decode(L.demote, L.counts[0:1], free_slots=True)
+        m.mig.demote()
         if ev is not None:
             ev[2].record(stream)
+        m.mig.promote()
+        if ev is not None:
+            ev[3].record(stream)
 
     for _ in range(warmup):
         step()
+        m.restore(tiers0)
     torch.cuda.synchronize()
     if dist:
         dist.barrier()
-    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(steps)]
-    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    start.record(stream)
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(steps)]
     for i in range(steps):
         step(evs[i])
-    stop.record(stream)
+        if i == 0:
+            torch.cuda.synchronize()
+            hist = edge_histogram(m, tiers0)
+            counts = m.mig.lists.counts.tolist()
+            st_p = m.mig.status[: counts[1]].clone()  # statuses of the last migrate (promotions)
+        m.restore(tiers0)
     torch.cuda.synchronize()
-    ms = start.elapsed_time(stop) / steps
-    enc_ms = statistics.mean(e[0].elapsed_time(e[1]) for e in evs)
-    dec_ms = statistics.mean(e[1].elapsed_time(e[2]) for e in evs)
-    t = torch.tensor([ms, enc_ms, dec_ms], dtype=torch.float64, device=dev)
+    plan_ms = statistics.mean(e[0].elapsed_time(e[1]) for e in evs)
+    dem_ms = statistics.mean(e[1].elapsed_time(e[2]) for e in evs)
+    pro_ms = statistics.mean(e[2].elapsed_time(e[3]) for e in evs)
+    t = torch.tensor([plan_ms, dem_ms, pro_ms], dtype=torch.float64, device=dev)
     if dist:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms, enc_ms, dec_ms = float(t[0]), float(t[1]), float(t[2])
-    page_bytes = DEMOTE_T * kv.row_len * 2 * 2  # K + V bf16 of one page on this rank
-    enc_alg = n_demote * (page_bytes + page_bytes // 2 + 4 * DEMOTE_T)
-    ok = int(mig.status_encode[:n_demote].ne(0).sum().item()) == 0
-    del k, v, kv, arena, mig
-    torch.cuda.empty_cache()
-    return {"workload": f"{layers} layers x K,V [262144 tokens, 8 KV heads, 128] bf16 sharded over KV heads; "
-                        f"{n} (layer, 16-token page) entries; U[0,1] features; pressure 0.9",
-            "pages": n, "demoted_pages": n_demote, "heads_per_rank": heads,
-            "demote_pages_per_s": round(n_demote / (enc_ms / 1e3), 1),
-            "step_pages_per_s": round(n_demote / (ms / 1e3), 1),
-            "ms_per_step": round(ms, 4), "encode_ms": round(enc_ms, 4), "decode_ms": round(dec_ms, 4),
-            "encode_hbm_gbs": round(enc_alg / (enc_ms / 1e3) / 1e9, 1),
-            "decode_hbm_gbs": round(enc_alg / (dec_ms / 1e3) / 1e9, 1),
-            "scaling": "strong (fixed model, heads split over ranks)", "all_slots_ok": ok,
-            "step": "pressure all-reduce (N>1) + policy kernel + gather/INT8 encode of demoted pages + decode back",
-            "gpu_launches_per_step": 5}
+    plan_ms, dem_ms, pro_ms = float(t[0]), float(t[1]), float(t[2])
+    ms = plan_ms + dem_ms + pro_ms
+    n_dem, n_pro = counts
+    E, T = m.E, DEMOTE_T
+    b16, b8 = page_format_bytes(0, E, T), page_format_bytes(1, E, T)
+    ok = hist.get((0, 1), 0) == n_dem and hist.get((1, 0), 0) == n_pro and bool((st_p == 0).all())
+    out = {"workload": f"{layers} layers x K,V [262144 tokens, 8 KV heads, 128] bf16 sharded over KV heads; "
+                       f"{m.n} (layer, 16-token page) entries; U[0,1] features; the ~10% of pages the policy "
+                       f"promotes start in the FP8 tier (INT8 slots)",
+           "pages": m.n, "demoted_pages": n_dem, "promoted_pages": n_pro, "heads_per_rank": heads,
+           "pressure_source": "FP8 tier store occupancy, MAX over ranks (below p_emergency: same plan as 0.9)",
+           "demote_pages_per_s": round(n_dem / (dem_ms / 1e3), 1),
+           "promote_pages_per_s": round(n_pro / (pro_ms / 1e3), 1),
+           "step_pages_per_s": round((n_dem + n_pro) / (ms / 1e3), 1),
+           "ms_per_step": round(ms, 4), "plan_ms": round(plan_ms, 4), "demote_ms": round(dem_ms, 4),
+           "promote_ms": round(pro_ms, 4), "plan_includes": "pressure read + MAX all-reduce (N>1) + policy kernels",
+           "demote_hbm_gbs": round(n_dem * (b16 + b8) / (dem_ms / 1e3) / 1e9, 1),
+           "promote_hbm_gbs": round(n_pro * (b16 + b8) / (pro_ms / 1e3) / 1e9, 1),
+           "scaling": "strong (fixed model, heads split over ranks)", "all_transitions_ok": ok,
+           "step": "pressure all-reduce (N>1) + policy kernels + migrate(demote list: direct + staged pass) "
+                   "+ release + migrate(promote list) + release",
+           "gpu_launches_per_step": 8}
+    m.free()
+    return out
+
+
+def run_config5(dev, world: int, rank: int, dist, layers: int = DEMOTE_LAYERS) -> dict:
+    """a page table of 1,048,576 pages (64 layers x 16384 pages of
+    [16 tokens, 8 heads, 128] bf16 K and V, heads sharded over ranks) with U[0,1]
+    features and current tiers uniform over {BF16, INT8 (FP8 tier), INT4, INT2 (archive)};
+    for each pressure of the sweep one step (plan -> migrate demotions -> migrate
+    promotions) runs every tier edge the controller picks with its codec: BF16 <-> INT8
+    (int8_default), INT8 <-> INT4 (int4_default), INT2 -> INT4 (int2_dithered).  The pages
+    are put back in their starting tiers after each step, outside the timed events."""
+    from ashkv import _native as N
+    heads = DEMOTE_HEADS // world
+    m = MigrationModel(dev, rank, layers, heads, {1: N.PAGE_INT8, 2: N.PAGE_INT4, 3: N.PAGE_NBIT2},
+                       {1: 0.42, 2: 0.40, 3: 0.28}, seed=5000)
+    m.features(5151)
+    g = torch.Generator(device=dev).manual_seed(5252)
+    tiers0 = torch.randint(0, 4, (m.n,), generator=g, device=dev).to(torch.int8)
+    m.place(tiers0)
+    stream = torch.cuda.current_stream(dev)
+    n_out = float(m.stores[3].slot_view()[:4096, :4].contiguous().view(torch.int32).float().mean())
+    rows = []
+    for p in C5_PRESSURES:
+        pr = torch.tensor([p], dtype=torch.float32, device=dev)
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+        for rep in range(2):  # the first repetition warms up
+            ev[0].record(stream)
+            if dist:
+                dist.all_reduce(pr, op=dist.ReduceOp.MAX)
+            m.mig.plan(pr)
+            ev[1].record(stream)
+            m.mig.demote()
+            ev[2].record(stream)
+            m.mig.promote()
+            ev[3].record(stream)
+            torch.cuda.synchronize()
+            if rep == 1:
+                hist = edge_histogram(m, tiers0)
+                nd, npro = m.mig.lists.counts.tolist()
+            m.restore(tiers0)
+            torch.cuda.synchronize()
+        t = torch.tensor([ev[0].elapsed_time(ev[1]), ev[1].elapsed_time(ev[2]), ev[2].elapsed_time(ev[3])],
+                         dtype=torch.float64, device=dev)
+        if dist:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        plan_ms, dem_ms, pro_ms = (float(x) for x in t)
+        moved = sum(hist.values())
+        alg = sum(c * (page_format_bytes(m.formats[a], m.E, m.T, n_out) + page_format_bytes(m.formats[b], m.E, m.T, n_out))
+                  for (a, b), c in hist.items())
+        ms = plan_ms + dem_ms + pro_ms
+        rows.append({"pressure": p, "demote_list": nd, "promote_list": npro, "moved": moved,
+                     "edges": {f"{a}->{b}": c for (a, b), c in sorted(hist.items())},
+                     "plan_ms": round(plan_ms, 4), "demote_ms": round(dem_ms, 4), "promote_ms": round(pro_ms, 4),
+                     "pages_per_s": round(moved / (ms / 1e3), 1),
+                     "migrate_hbm_gbs": round(alg / ((dem_ms + pro_ms) / 1e3) / 1e9, 1)})
+    tot_moved = sum(r["moved"] for r in rows)
+    tot_ms = sum(r["plan_ms"] + r["demote_ms"] + r["promote_ms"] for r in rows)
+    out = {"workload": f"{m.n} pages ({layers} layers x 16384) of [16, {heads} local heads, 128] bf16 K+V, "
+                       f"tiers uniform over BF16/INT8/INT4/INT2, U[0,1] features, pressure swept {list(C5_PRESSURES)}",
+           "pages": m.n, "heads_per_rank": heads, "per_pressure": rows,
+           "pages_per_s": round(tot_moved / (tot_ms / 1e3), 1), "ms_per_sweep": round(tot_ms, 4),
+           "scaling": "strong (fixed table, heads split over ranks)",
+           "archive_outliers_per_page": round(n_out, 2)}
+    m.free()
+    return out
 
 # ------------------------------------------------------------------ GPU leg
 def main() -> None:
@@ -429,6 +560,7 @@ def main() -> None:
     ap.add_argument("--ref-seconds", type=float, default=5.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-demote", action="store_true")
+    ap.add_argument("--no-config5", action="store_true")
     ap.add_argument("--no-codec-suite", action="store_true")
     ap.add_argument("--only-features", action="store_true",
                     help="run only the page-features leg on one GPU and print its JSON (profiling cases)")
@@ -632,6 +764,9 @@ def main() -> None:
     if not args.no_demote:
         demote = run_demote(dev, world, rank, dist, args.demote_steps, 3, args.demote_layers,
                             args.demote_head_split)
+    config5 = None
+    if not args.no_config5:
+        config5 = run_config5(dev, world, rank, dist, args.demote_layers)
 
     if rank == 0:
         cpu = None
@@ -668,6 +803,7 @@ def main() -> None:
             "clocks": clocks.summary(),
             "cpu_baseline": cpu,
             "demote": demote,
+            "config5": config5,
         }
         print(json.dumps(line), flush=True)
     if dist:
