@@ -37,6 +37,8 @@ SIGNATURES: dict[str, tuple] = {
     "ashkv_device_sm_count": (_I32, []),
     "ashkv_int8_encode_rows": (_I32, [_P, _I32, _I64, _I32, _I64, _P, _P, _I64, _P, _I32, _I32, _I64, _U32, _P]),
     "ashkv_int8_decode_rows": (_I32, [_P, _I64, _P, _I32, _I32, _I64, _I64, _I32, _P, _I32, _I64, _P, _P]),
+    "ashkv_int8_encode_rows_layers": (_I32, [_P, _I32, _I32, _I64, _I32, _I64, _P, _P, _I64, _I64, _P, _I32, _I32,
+                                             _I64, _I64, _U32, _P]),
     "ashkv_nbit_encode": (_I32, [_P, _I64, _I32, _F32, _I32, _P, _U64, _U64, _P, _P, _P, _P, _I32, _P, _P]),
     "ashkv_nbit_decode": (_I32, [_P, _P, _I64, _I32, _P, _P, _I32, _P, _P, _P]),
     "ashkv_nbit_outliers_flatten": (_I32, [_P, _P, _I32, _I64, _P, _P, _P, _P, _P]),
@@ -46,6 +48,8 @@ SIGNATURES: dict[str, tuple] = {
     "ashkv_desired_tiers": (_I32, [_P, _P, _I64, _F64, _F64, _F64, _F64, _F64, _P, _P, _P, _P]),
     "ashkv_policy_scratch_ints": (_I64, [_I64]),
     "ashkv_memcpy2d": (_I32, [_P, _I64, _P, _I64, _I64, _I64, _P]),
+    "ashkv_copy_rows_indexed": (_I32, [_P, _I64, _I64, _P, _I64, _P, _I64, _I64, _P, _I64, _I64, _I64, _I64, _P,
+                                       _P]),
     "ashkv_policy_step_noalloc": (_I32, [_P, _P, _P, _P, _P, _I64, _F32, _F32, _F32, _F32, _F64, _F64, _F64, _F64,
                                          _F64, _P, _P, _P, _P, _P, _P, _P, _P]),
     "ashkv_int8_page_slot_bytes": (_I64, [_I32, _I32]),
@@ -163,6 +167,26 @@ def int8_encode_rows(src: torch.Tensor, codes: torch.Tensor, scales: torch.Tenso
         codes.data_ptr(), codes.stride(0) * codes.element_size(),
         scales.data_ptr(), _dtype_tag(scales.dtype), scales_per_slot, scale_slot_stride, flags,
         stream_handle(src.device)), "int8_encode_rows")
+
+
+def int8_encode_rows_layers(layer_ptrs: torch.Tensor, n_layers: int, src_dtype: torch.dtype, row_len: int,
+                            src_row_stride: int, row_index: torch.Tensor, n_rows: int, codes_ptr: int,
+                            codes_row_stride: int, layer_codes_offset: int, scales_ptr: int,
+                            scales_per_slot: int, scale_slot_stride: int, layer_scales_offset: int,
+                            device: torch.device) -> None:
+    """``int8_encode_rows`` over ``n_layers`` layers in one launch (fp16 scales).  ``layer_ptrs``
+    is an int64 CUDA tensor of 16-byte aligned layer base addresses; codes and scales are
+    raw device addresses with per-layer byte offsets."""
+    _require_cuda(layer_ptrs, row_index)
+    if layer_ptrs.dtype != torch.int64 or layer_ptrs.numel() < n_layers:
+        raise ValueError("int8_encode_rows_layers: layer_ptrs must hold n_layers int64 addresses")
+    if row_index is None or row_index.dtype != torch.int64 or row_index.numel() != n_rows:
+        raise ValueError("int8_encode_rows_layers: row_index must be int64 with one entry per row")
+    check(lib().ashkv_int8_encode_rows_layers(
+        layer_ptrs.data_ptr(), n_layers, _dtype_tag(src_dtype), n_rows, row_len, src_row_stride,
+        row_index.data_ptr(), codes_ptr, codes_row_stride, layer_codes_offset, scales_ptr, DTYPE_FP16,
+        scales_per_slot, scale_slot_stride, layer_scales_offset, 0, stream_handle(device)),
+        "int8_encode_rows_layers")
 
 
 def int8_decode_rows(codes: torch.Tensor, scales: torch.Tensor, dst: torch.Tensor, *,
@@ -430,6 +454,18 @@ def memcpy2d(dst_ptr: int, dst_pitch: int, src_ptr: int, src_pitch: int, width: 
     """Pitched async copy on the current stream (host pointers should be pinned for async)."""
     check(lib().ashkv_memcpy2d(dst_ptr, dst_pitch, src_ptr, src_pitch, width, height, stream_handle(device)),
           "memcpy2d")
+
+
+def copy_rows_indexed(dst_ptr: int, dst_row_stride: int, dst_sub_stride: int, dst_index: Optional[torch.Tensor],
+                      dst_rows: int, src_ptr: int, src_row_stride: int, src_sub_stride: int,
+                      src_index: Optional[torch.Tensor], src_rows: int, width: int, n_sub: int, n_rows: int,
+                      device: torch.device, status: Optional[torch.Tensor] = None) -> None:
+    """Indexed row gather/scatter between device memory and mapped page-locked host memory."""
+    _require_cuda(dst_index, src_index, status)
+    check(lib().ashkv_copy_rows_indexed(dst_ptr, dst_row_stride, dst_sub_stride, _ptr(dst_index), dst_rows,
+                                        src_ptr, src_row_stride, src_sub_stride, _ptr(src_index), src_rows,
+                                        width, n_sub, n_rows, _ptr(status), stream_handle(device)),
+          "copy_rows_indexed")
 
 
 POLICY_NOALLOC_MAX_PAGES = 4194304

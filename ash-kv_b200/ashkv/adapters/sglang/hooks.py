@@ -18,10 +18,11 @@ same way.  This module keeps that placement byte for byte (entries past the
 last token, which the reference leaves uninitialised, are zero here).
 
 Differences in how the work is done:
-  * demote: one gather+encode launch per layer and K/V writes the packed
-    slots straight into a device staging buffer [tokens, layers, slot]; a
-    single pitched device->host copy moves all layers (the reference runs two
-    synchronous .cpu() copies and a host scatter per layer).  With
+  * demote: one gather+encode launch over all layers for K and one for V
+    writes the packed slots straight into a reused device staging buffer
+    [tokens, layers, slot]; a single pitched device->host copy each moves all
+    layers, and the hook waits once for both (the reference runs one Triton
+    launch, two synchronous .cpu() copies and a host scatter per layer).  With
     ``compact_host_slots`` (the default) that copy carries only the used
     2H + H*D bytes of each compressed slot, so the bytes saved are saved on
     the link too; the zero tail [2H + H*D, 2*H*D), which nothing reads, is
@@ -62,6 +63,10 @@ def _contiguous_range(idx: torch.Tensor) -> int | None:
     return None
 
 
+def _ceil16(n: int) -> int:
+    return (n + 15) // 16 * 16
+
+
 class SGLangHooks:
     """Demote (GPU -> CPU, compress) and promote (CPU -> GPU, decompress) hooks."""
 
@@ -71,6 +76,8 @@ class SGLangHooks:
         self.compressible_layers = None
         self.compact_host_slots = True
         self.transfer_stats = {"d2h_bytes": 0, "h2d_bytes": 0}  # bytes moved over the host link
+        self._stage_bufs: dict = {}  # device -> reusable staging buffer
+        self._ptr_cache: dict = {}   # (device, layer addresses) -> device table of them
         self.stats = {"tokens_compressed": 0, "tokens_decompressed": 0, "bytes_saved": 0,
                       "blocks_intercepted": 0, "last_flush_time": 0}
         os.makedirs("stats", exist_ok=True)
@@ -120,27 +127,67 @@ class SGLangHooks:
         with torch.cuda.device(dev):
             self._demote_cuda(device_pool, host_pool, host_indices, device_indices, n, H, D, L, compress)
 
+    def _staging(self, dev: torch.device, nbytes: int) -> torch.Tensor:
+        """A device byte buffer reused across calls (grown when a call needs more)."""
+        buf = self._stage_bufs.get(dev)
+        if buf is None or buf.numel() < nbytes:
+            buf = torch.empty(max(nbytes, 1 << 20), dtype=torch.uint8, device=dev)
+            self._stage_bufs[dev] = buf
+        return buf[:nbytes]
+
+    def _layer_ptrs(self, layers, dev: torch.device) -> torch.Tensor:
+        key = (dev, tuple(t.data_ptr() for t in layers))
+        t = self._ptr_cache.get(key)
+        if t is None:
+            if len(self._ptr_cache) > 16:
+                self._ptr_cache.clear()
+            t = torch.tensor(list(key[1]), dtype=torch.int64, device=dev)
+            self._ptr_cache[key] = t
+        return t
+
     def _demote_cuda(self, device_pool, host_pool, host_indices, device_indices, n, H, D, L, compress) -> None:
         row, slot = H * D, 2 * H * D
         dev = device_pool.k_buffer[0].device
         didx = device_indices.to(device=dev, dtype=torch.int64)
-        for name in ("k_buffer", "v_buffer"):
+        # staging [K/V, token, layer, slot]: the host pools' row order, so each of K and V
+        # leaves in one pitched copy
+        staging = self._staging(dev, 2 * n * L * slot).view(2, n, L, slot)
+        # scale entries past the last token stay zero; with whole slots the zero tail travels too
+        staging[:, :, :, :2 * H].zero_()
+        if not self.compact_host_slots:
+            staging[:, :, :, 2 * H + row:].zero_()
+        elif (2 * H + row) % 16:  # an indexed host scatter moves whole 16-byte chunks: pad with zeros
+            staging[:, :, :, 2 * H + row:_ceil16(2 * H + row)].zero_()
+        all_layers = len(compress) == L
+        pinned = False
+        for kv, name in enumerate(("k_buffer", "v_buffer")):
             dbuf = getattr(device_pool, name)
-            staging = torch.zeros((n, L, slot), dtype=torch.uint8, device=dev)
-            flat = staging.view(-1)
-            for layer in range(L):
-                src = dbuf[layer].view(-1, row)
-                if layer in compress:
-                    codes = staging[:, layer, 2 * H:2 * H + row].view(torch.int8)
-                    # scale of token t -> staging[t // H, layer, 2 * (t % H)]
-                    scales = flat[layer * slot:].view(torch.float16)
-                    _native.int8_encode_rows(src, codes, scales, row_index=didx, scales_per_slot=H,
-                                             scale_slot_stride=L * slot)
-                else:
-                    staging[:, layer, :].view(torch.bfloat16).copy_(src[didx].view(n, row))
+            st = staging[kv]
+            layers = [dbuf[layer] for layer in range(L)]
+            if all_layers and all(t.is_contiguous() and t.data_ptr() % 16 == 0 for t in layers):
+                # one launch over every layer: layer l's codes at slot l of each token row
+                _native.int8_encode_rows_layers(
+                    self._layer_ptrs(layers, dev), L, layers[0].dtype, row, row, didx, n,
+                    st.data_ptr() + 2 * H, L * slot, slot, st.data_ptr(), H, L * slot, slot, dev)
+            else:
+                flat = st.reshape(-1)
+                for layer in range(L):
+                    src = layers[layer].view(-1, row)
+                    if layer in compress:
+                        codes = st[:, layer, 2 * H:2 * H + row].view(torch.int8)
+                        # scale of token t -> st[t // H, layer, 2 * (t % H)]
+                        scales = flat[layer * slot:].view(torch.float16)
+                        _native.int8_encode_rows(src, codes, scales, row_index=didx, scales_per_slot=H,
+                                                 scale_slot_stride=L * slot)
+                    else:
+                        st[:, layer, :].view(torch.bfloat16).copy_(src[didx].view(n, row))
             widths = [2 * H + row if (self.compact_host_slots and layer in compress) else slot for layer in range(L)]
-            self._write_host_rows(getattr(host_pool, name), host_indices, staging, n, L, slot, widths)
+            hbuf = getattr(host_pool, name)
+            self._write_host_rows(hbuf, host_indices, st, n, L, slot, widths)
+            pinned |= hbuf.is_pinned()
             self.transfer_stats["d2h_bytes"] += n * sum(widths)
+        if pinned:  # the host pool is complete when the hook returns, as after the reference's .cpu() copies
+            torch.cuda.current_stream(dev).synchronize()
 
     @staticmethod
     def _write_host_rows(host_buf: torch.Tensor, host_indices, staging: torch.Tensor, n: int, L: int,
@@ -159,8 +206,14 @@ class SGLangHooks:
                 for layer, w in enumerate(widths):
                     _native.memcpy2d(dst.data_ptr() + layer * slot, L * slot, staging.data_ptr() + layer * slot,
                                      L * slot, w, n, staging.device)
-            if host_buf.is_pinned():
-                torch.cuda.current_stream(staging.device).synchronize()
+        elif host_buf.is_pinned() and host_buf.is_contiguous():
+            # scattered rows: one kernel writes the slots into the pinned pool through its device mapping
+            hidx = host_indices.detach().to(staging.device, torch.int64)
+            groups = [(0, L, widths[0])] if len(set(widths)) == 1 else [(layer, 1, w) for layer, w in enumerate(widths)]
+            for first_layer, n_sub, w in groups:
+                _native.copy_rows_indexed(host_buf.data_ptr() + first_layer * slot, L * slot, slot, hidx,
+                                          host_buf.shape[0], staging.data_ptr() + first_layer * slot, L * slot,
+                                          slot, None, n, _ceil16(w), n_sub, n, staging.device)
         else:
             hidx = host_indices.detach().to("cpu", torch.int64)
             h3 = hview.view(hview.shape[0], L, slot)
@@ -205,27 +258,34 @@ class SGLangHooks:
         for name in ("k_buffer", "v_buffer"):
             hbuf = getattr(host_pool, name)
             L = hbuf.shape[1]
-            staged = torch.empty((n, used), dtype=torch.uint8, device=dev)
+            upad = _ceil16(used)  # staged rows padded to 16 bytes for the indexed gather
+            staged = torch.empty((n, upad), dtype=torch.uint8, device=dev)
             self._read_host_slots(hbuf, host_indices, layer_id, staged, n, L, slot, used)
             dst = getattr(device_pool, name)[layer_id].view(-1, row)
             if native_layer:
                 dst[didx] = staged.view(torch.bfloat16).view(n, row)
                 continue
-            codes = staged[:, 2 * H:].view(torch.int8)
+            codes = staged[:, 2 * H:2 * H + row].view(torch.int8)
             scales = staged.view(-1).view(torch.float16)
             _native.int8_decode_rows(codes, scales, dst, row_index=didx, scales_per_slot=H,
-                                     scale_slot_stride=used)
+                                     scale_slot_stride=upad)
 
     @staticmethod
     def _read_host_slots(hbuf: torch.Tensor, host_indices, layer_id: int, staged: torch.Tensor, n: int, L: int,
                          slot: int, used: int) -> None:
         first = _contiguous_range(host_indices) if hbuf.is_contiguous() else None
+        upad = staged.shape[1]
         if first is not None:
             base = hbuf.data_ptr() + (first * L + layer_id) * slot
-            _native.memcpy2d(staged.data_ptr(), used, base, L * slot, used, n, staged.device)
+            _native.memcpy2d(staged.data_ptr(), upad, base, L * slot, used, n, staged.device)
             if not hbuf.is_pinned():
                 torch.cuda.current_stream(staged.device).synchronize()
+        elif hbuf.is_pinned() and hbuf.is_contiguous():
+            # scattered rows: one kernel reads the slots from the pinned pool through its device mapping
+            hidx = host_indices.detach().to(staged.device, torch.int64)
+            _native.copy_rows_indexed(staged.data_ptr(), upad, 0, None, n, hbuf.data_ptr() + layer_id * slot,
+                                      L * slot, 0, hidx, hbuf.shape[0], upad, 1, n, staged.device)
         else:
             hidx = host_indices.detach().to("cpu", torch.int64)
-            rows = hbuf[hidx, layer_id].contiguous().view(n, -1).view(torch.uint8)[:, :used].contiguous()
-            staged.copy_(rows)
+            rows = hbuf[hidx, layer_id].contiguous().view(n, -1).view(torch.uint8)[:, :used]
+            staged[:, :used].copy_(rows)

@@ -182,9 +182,21 @@ def _side_streams(dev: torch.device, kind: str = "encode"):
 _BLOB_WRITES: dict = {}
 
 
+def _record_blob_write(ptr: int, event) -> None:
+    """Remember that the blob at host address ``ptr`` is complete once ``event`` is.
+    Entries whose copies have already finished are dropped first, so blobs that are
+    never decoded or synced do not accumulate (and a later buffer at a reused
+    address never waits on a stale event)."""
+    for k in [k for k, ev in _BLOB_WRITES.items() if ev.query()]:
+        del _BLOB_WRITES[k]
+    _BLOB_WRITES[ptr] = event
+
+
 def sync_host_blobs(blobs) -> None:
     """Wait until the blobs returned by ``encode_pinned_batch(host_sync=False)`` are
-    complete in host memory (only needed before reading their bytes on the host)."""
+    complete in host memory.  Needed before reading their bytes on the host (a
+    blob passed to ``decode_pinned_batch`` is ordered on the GPU instead); a blob
+    that is neither synced nor decoded is forgotten once its copies finish."""
     for b in blobs:
         ev = _BLOB_WRITES.pop(b.data_ptr(), None)
         if ev is not None:
@@ -379,7 +391,7 @@ class DitheredNBitCodec:
             else:
                 for r in results:
                     if r.numel() > 8:
-                        _BLOB_WRITES[r.data_ptr()] = copied
+                        _record_blob_write(r.data_ptr(), copied)
         return results
 
     def decode_pinned(self, blob: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:

@@ -26,7 +26,24 @@ struct Int8EncParams {
   int64_t scale_slot_stride;
   int32_t scale_fp16;
   int32_t fp32_product;
+  // several layers in one launch (blockIdx.y = layer): source rows from
+  // layer_src[layer], codes and scales shifted by layer * layer_*_offset bytes
+  const uint64_t* layer_src;
+  int32_t n_layers;
+  int64_t layer_codes_offset;
+  int64_t layer_scales_offset;
 };
+
+__device__ __forceinline__ Int8EncParams for_layer(const Int8EncParams& p0) {
+  Int8EncParams p = p0;
+  if (p0.layer_src) {
+    const int64_t l = blockIdx.y;
+    p.src = reinterpret_cast<const uint16_t*>(p0.layer_src[l]);
+    p.codes += l * p0.layer_codes_offset;
+    p.scales += l * p0.layer_scales_offset;
+  }
+  return p;
+}
 
 struct Int8DecParams {
   const uint8_t* codes;
@@ -165,7 +182,8 @@ __device__ __forceinline__ void encode_loaded_row(const Int8EncParams& p, int64_
 
 // Each thread owns NCH chunks of 8 consecutive elements of its row(s).
 template <bool FP16, int NCH, int TEAM>
-__global__ void __launch_bounds__(256) int8_encode_kernel(const Int8EncParams p) {
+__global__ void __launch_bounds__(256) int8_encode_kernel(const Int8EncParams p0) {
+  const Int8EncParams p = for_layer(p0);
   constexpr int ROWS_PER_PASS = 256 / TEAM;
   constexpr int RPT = enc_rows_per_team<FP16, NCH>();
   const int lane_in_team = threadIdx.x % TEAM;
@@ -185,7 +203,8 @@ __global__ void __launch_bounds__(256) int8_encode_kernel(const Int8EncParams p)
 
 // Generic path: any row length / alignment, one element per thread step.
 template <bool FP16>
-__global__ void __launch_bounds__(256) int8_encode_generic_kernel(const Int8EncParams p) {
+__global__ void __launch_bounds__(256) int8_encode_generic_kernel(const Int8EncParams p0) {
+  const Int8EncParams p = for_layer(p0);
   const int64_t r = int64_t(blockIdx.x) * 8 + threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
   if (r >= p.n_rows) return;
@@ -308,8 +327,9 @@ bool pick_team(int32_t row_len, int& team, int& nch) {
 
 #define ASHKV_ENC_CASE(FP, NC, TM)                                                        \
   if (nch == NC && team == TM) {                                                          \
-    int8_encode_kernel<FP, NC, TM><<<unsigned((p.n_rows + (256 / TM) * enc_rows_per_team<FP, NC>() - 1) /      \
-                                             ((256 / TM) * enc_rows_per_team<FP, NC>())), 256, 0, st>>>(p);           \
+    int8_encode_kernel<FP, NC, TM><<<dim3(unsigned((p.n_rows + (256 / TM) * enc_rows_per_team<FP, NC>() - 1) / \
+                                             ((256 / TM) * enc_rows_per_team<FP, NC>())), unsigned(p.n_layers)), \
+                                      256, 0, st>>>(p);                                   \
     return check_launch("int8_encode");                                                  \
   }
 
@@ -323,7 +343,7 @@ static ashkv_status_t launch_encode(const Int8EncParams& p, int team, int nch, b
     ASHKV_ENC_CASE(FP16, 4, 16) ASHKV_ENC_CASE(FP16, 4, 32) ASHKV_ENC_CASE(FP16, 8, 32)
     ASHKV_ENC_CASE(FP16, 16, 32)
   }
-  int8_encode_generic_kernel<FP16><<<unsigned((p.n_rows + 7) / 8), 256, 0, st>>>(p);
+  int8_encode_generic_kernel<FP16><<<dim3(unsigned((p.n_rows + 7) / 8), unsigned(p.n_layers)), 256, 0, st>>>(p);
   return check_launch("int8_encode_generic");
 }
 #undef ASHKV_ENC_CASE
@@ -346,7 +366,8 @@ extern "C" ashkv_status_t ashkv_int8_encode_rows(
   if (n_rows > (int64_t(1) << 40)) return ASHKV_BAD_ARGUMENT;
   if (!aligned(d_scales, 2) || (scale_slot_stride % 2)) return ASHKV_BAD_ARGUMENT;
 
-  Int8EncParams p;
+  Int8EncParams p{};
+  p.n_layers = 1;
   p.src = static_cast<const uint16_t*>(d_src);
   p.n_rows = n_rows; p.row_len = row_len; p.src_stride = src_row_stride; p.row_index = d_row_index;
   p.codes = static_cast<uint8_t*>(d_codes); p.codes_stride = codes_row_stride;
@@ -360,6 +381,45 @@ extern "C" ashkv_status_t ashkv_int8_encode_rows(
   // 16-byte loads need 16-byte aligned rows; 8-byte stores need 8-byte aligned code rows.
   fast = fast && aligned(d_src, 16) && ((src_row_stride * 2) % 16 == 0) &&
          aligned(d_codes, 8) && (codes_row_stride % 8 == 0);
+  cudaStream_t st = as_stream(stream);
+  return src_dtype == ASHKV_DTYPE_FP16 ? launch_encode<true>(p, team, nch, fast, st)
+                                       : launch_encode<false>(p, team, nch, fast, st);
+}
+
+extern "C" ashkv_status_t ashkv_int8_encode_rows_layers(
+    const uint64_t* d_layer_src, int32_t n_layers, int32_t src_dtype, int64_t n_rows, int32_t row_len,
+    int64_t src_row_stride, const int64_t* d_row_index,
+    void* d_codes, int64_t codes_row_stride, int64_t layer_codes_offset,
+    void* d_scales, int32_t scale_dtype, int32_t scales_per_slot, int64_t scale_slot_stride,
+    int64_t layer_scales_offset, uint32_t flags, void* stream) {
+  if (n_rows < 0 || row_len <= 0 || scales_per_slot <= 0 || n_layers < 0 || n_layers > 65535)
+    return ASHKV_BAD_ARGUMENT;
+  if (src_dtype != ASHKV_DTYPE_BF16 && src_dtype != ASHKV_DTYPE_FP16) return ASHKV_BAD_ARGUMENT;
+  if (scale_dtype != ASHKV_DTYPE_BF16 && scale_dtype != ASHKV_DTYPE_FP16) return ASHKV_BAD_ARGUMENT;
+  if (n_rows == 0 || n_layers == 0) return ASHKV_OK;
+  if (!d_layer_src || !d_codes || !d_scales) return ASHKV_BAD_ARGUMENT;
+  if (n_rows > (int64_t(1) << 40)) return ASHKV_BAD_ARGUMENT;
+  if (!aligned(d_scales, 2) || (scale_slot_stride % 2) || (layer_scales_offset % 2)) return ASHKV_BAD_ARGUMENT;
+
+  Int8EncParams p{};
+  p.n_layers = n_layers;
+  p.layer_src = d_layer_src;
+  p.src = nullptr;
+  p.n_rows = n_rows; p.row_len = row_len; p.src_stride = src_row_stride; p.row_index = d_row_index;
+  p.codes = static_cast<uint8_t*>(d_codes); p.codes_stride = codes_row_stride;
+  p.layer_codes_offset = layer_codes_offset;
+  p.scales = static_cast<uint8_t*>(d_scales); p.scales_per_slot = scales_per_slot;
+  p.sps_shift = pow2_shift(scales_per_slot);
+  p.scale_slot_stride = scale_slot_stride; p.scale_fp16 = scale_dtype == ASHKV_DTYPE_FP16;
+  p.layer_scales_offset = layer_scales_offset;
+  p.fp32_product = (flags & ASHKV_INT8_FP32_PRODUCT) ? 1 : 0;
+
+  int team = 0, nch = 0;
+  bool fast = pick_team<void, void>(row_len, team, nch);
+  // every layer's rows must meet the fast kernel's alignment: the caller guarantees
+  // 16-byte aligned layer bases (checked on the host side of the binding)
+  fast = fast && ((src_row_stride * 2) % 16 == 0) && aligned(d_codes, 8) && (codes_row_stride % 8 == 0) &&
+         (layer_codes_offset % 8 == 0);
   cudaStream_t st = as_stream(stream);
   return src_dtype == ASHKV_DTYPE_FP16 ? launch_encode<true>(p, team, nch, fast, st)
                                        : launch_encode<false>(p, team, nch, fast, st);

@@ -547,6 +547,104 @@ def run_config5(dev, world: int, rank: int, dist, layers: int = DEMOTE_LAYERS) -
     m.free()
     return out
 
+# ------------------------------------------------------------------ SGLang hooks leg
+class _HookDevPool:
+    def __init__(self, L, cap, H, D, dev):
+        g = torch.Generator(device=dev).manual_seed(77)
+        self.head_num, self.head_dim, self.layer_num = H, D, L
+        self.k_buffer = [torch.randn(cap, H, D, generator=g, device=dev).to(torch.bfloat16) for _ in range(L)]
+        self.v_buffer = [torch.randn(cap, H, D, generator=g, device=dev).to(torch.bfloat16) for _ in range(L)]
+
+
+class _HookHostPool:
+    def __init__(self, L, cap, H, D):
+        self.k_buffer = torch.empty((cap, L, H, D), dtype=torch.bfloat16).pin_memory()
+        self.v_buffer = torch.empty((cap, L, H, D), dtype=torch.bfloat16).pin_memory()
+
+
+def run_hooks(dev, reps: int = 5) -> dict:
+    """SGLangHooks.demote_hook / promote_hook (the reference's production path) on
+    config-4 shapes: 64 layers x 8 KV heads x 128, a 16384-token device pool and a
+    pinned host pool; demote batches of 4096 tokens at scattered device slots into
+    contiguous (and scattered) host slots; promote of the same batch, one call per
+    layer as SGLang loads.  Wall-clock per call (the hooks return with the host pool
+    complete); link GB/s = bytes moved / time, against a plain pinned copy of the same
+    byte count in each direction."""
+    import tempfile
+    from ashkv.adapters.sglang.hooks import SGLangHooks
+    L, cap, H, D, n = 64, 16384, 8, 128, 4096
+    dp, hp = _HookDevPool(L, cap, H, D, dev), _HookHostPool(L, cap, H, D)
+    g = torch.Generator().manual_seed(5)
+    didx = torch.randperm(cap, generator=g)[:n].sort().values.to(dev)
+    h_contig = torch.arange(1000, 1000 + n)
+    h_scatter = torch.randperm(cap, generator=g)[:n]
+    cwd = os.getcwd()
+    tmp = tempfile.mkdtemp()
+    os.chdir(tmp)  # the hooks write their stats file under ./stats
+    try:
+        hooks = SGLangHooks()
+        out = {}
+        for label, hidx in (("contiguous_host_slots", h_contig), ("scattered_host_slots", h_scatter)):
+            for _ in range(2):
+                hooks.demote_hook(dp, hp, hidx, didx, "MHA")
+            d0 = hooks.transfer_stats["d2h_bytes"]
+            t = []
+            for _ in range(reps):
+                torch.cuda.synchronize()
+                t0 = time.perf_counter()
+                hooks.demote_hook(dp, hp, hidx, didx, "MHA")
+                t.append(time.perf_counter() - t0)
+            sec = statistics.median(t)
+            moved = (hooks.transfer_stats["d2h_bytes"] - d0) / reps
+            out[f"demote_{label}"] = {"ms": round(sec * 1e3, 3), "tokens_per_s": round(n / sec, 1),
+                                      "token_layers_per_s": round(n * L / sec, 1),
+                                      "d2h_gbs": round(moved / sec / 1e9, 2), "d2h_bytes": int(moved)}
+        # promote the batch back, one call per layer
+        for _ in range(2):
+            for layer in range(L):
+                hooks.promote_hook(dp, hp, h_contig, didx, layer, "MHA")
+        torch.cuda.synchronize()
+        t = []
+        h0 = hooks.transfer_stats["h2d_bytes"]
+        for _ in range(reps):
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            for layer in range(L):
+                hooks.promote_hook(dp, hp, h_contig, didx, layer, "MHA")
+            torch.cuda.synchronize()
+            t.append(time.perf_counter() - t0)
+        sec = statistics.median(t)
+        moved = (hooks.transfer_stats["h2d_bytes"] - h0) / reps
+        out["promote_contiguous_host_slots"] = {"ms": round(sec * 1e3, 3), "tokens_per_s": round(n / sec, 1),
+                                                "token_layers_per_s": round(n * L / sec, 1),
+                                                "h2d_gbs": round(moved / sec / 1e9, 2), "h2d_bytes": int(moved),
+                                                "calls": L}
+        # the link: plain pinned copies of the same byte counts
+        nb = int(out["demote_contiguous_host_slots"]["d2h_bytes"])
+        dbuf = torch.empty(nb, dtype=torch.uint8, device=dev)
+        hbuf = torch.empty(nb, dtype=torch.uint8).pin_memory()
+        for _ in range(2):
+            hbuf.copy_(dbuf, non_blocking=True); dbuf.copy_(hbuf, non_blocking=True)
+        torch.cuda.synchronize()
+        t0 = time.perf_counter(); hbuf.copy_(dbuf, non_blocking=True); torch.cuda.synchronize()
+        d2h = nb / (time.perf_counter() - t0) / 1e9
+        t0 = time.perf_counter(); dbuf.copy_(hbuf, non_blocking=True); torch.cuda.synchronize()
+        h2d = nb / (time.perf_counter() - t0) / 1e9
+        out["link"] = {"d2h_gbs": round(d2h, 2), "h2d_gbs": round(h2d, 2), "bytes": nb,
+                       "how": "one pinned torch copy of the demote's byte count"}
+        for k in ("demote_contiguous_host_slots", "demote_scattered_host_slots"):
+            out[k]["frac_of_link"] = round(out[k]["d2h_gbs"] / d2h, 3)
+        out["promote_contiguous_host_slots"]["frac_of_link"] = round(
+            out["promote_contiguous_host_slots"]["h2d_gbs"] / h2d, 3)
+        out["workload"] = (f"{L} layers x [{cap} tokens, {H} heads, {D}] bf16 K and V on the device, pinned host "
+                           f"pool of the same shape; {n}-token batches")
+    finally:
+        os.chdir(cwd)
+    del dp, hp
+    torch.cuda.empty_cache()
+    return out
+
+
 # ------------------------------------------------------------------ GPU leg
 def main() -> None:
     ap = argparse.ArgumentParser()
@@ -561,6 +659,7 @@ def main() -> None:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-demote", action="store_true")
     ap.add_argument("--no-config5", action="store_true")
+    ap.add_argument("--no-hooks", action="store_true")
     ap.add_argument("--no-codec-suite", action="store_true")
     ap.add_argument("--only-features", action="store_true",
                     help="run only the page-features leg on one GPU and print its JSON (profiling cases)")
@@ -767,6 +866,7 @@ def main() -> None:
     config5 = None
     if not args.no_config5:
         config5 = run_config5(dev, world, rank, dist, args.demote_layers)
+    hooks = run_hooks(dev) if (rank == 0 and not args.no_hooks) else None
 
     if rank == 0:
         cpu = None
@@ -804,6 +904,7 @@ def main() -> None:
             "cpu_baseline": cpu,
             "demote": demote,
             "config5": config5,
+            "hooks": hooks,
         }
         print(json.dumps(line), flush=True)
     if dist:

@@ -80,8 +80,10 @@ ASHKV_API int32_t ashkv_device_sm_count(void);
  * encode, per row r of `row_len` elements:
  *   am      = max(max_i |x_i|, 1e-8)              (fp32, NaN ignored)
  *   s_i     = round_to_input_dtype(x_i * 127)      (fp32 product if ASHKV_INT8_FP32_PRODUCT)
- *   q       = s_i / am                              (fp32, correctly rounded)
- *   code_i  = sat_int8(trunc(q + (q > 0 ? 0.5 : -0.5)))   (NaN -> 0)
+ *   q       = s_i / am                              (PTX div.full.f32, as the Triton
+ *                                                    kernel divides on the GPU)
+ *   code_i  = low byte of int32(trunc(q + (q > 0 ? 0.5 : -0.5)))  (saturating, NaN -> 0;
+ *                                                    Triton's fp32 -> int8 cast)
  *   scale_r = am rounded to scale_dtype
  * Row r is read from d_src + (d_row_index ? d_row_index[r] : r) * src_row_stride
  * (elements), written to d_codes + r * codes_row_stride (bytes).  Its scale
@@ -95,6 +97,20 @@ ASHKV_API ashkv_status_t ashkv_int8_encode_rows(
     void* d_codes, int64_t codes_row_stride,
     void* d_scales, int32_t scale_dtype, int32_t scales_per_slot, int64_t scale_slot_stride,
     uint32_t flags, void* stream);
+
+/* The same encode over n_layers layers in one launch, for the SGLang demote
+ * hook, which encodes the same token rows of every layer
+ * (ashkv/adapters/sglang/hooks.py:93-137 loops over layers with one Triton
+ * launch each): layer l reads its rows from d_layer_src[l] (16-byte aligned),
+ * writes codes at d_codes + l * layer_codes_offset and scales at d_scales +
+ * l * layer_scales_offset (bytes), with the per-layer addressing above.
+ * n_layers is at most 65535. */
+ASHKV_API ashkv_status_t ashkv_int8_encode_rows_layers(
+    const uint64_t* d_layer_src, int32_t n_layers, int32_t src_dtype, int64_t n_rows, int32_t row_len,
+    int64_t src_row_stride, const int64_t* d_row_index,
+    void* d_codes, int64_t codes_row_stride, int64_t layer_codes_offset,
+    void* d_scales, int32_t scale_dtype, int32_t scales_per_slot, int64_t scale_slot_stride,
+    int64_t layer_scales_offset, uint32_t flags, void* stream);
 
 /* decode, per element: out = round_to_out_dtype(bf16((float)code * (float)scale / 127)).
  * Row r is written to d_dst + (d_row_index ? d_row_index[r] : r) * dst_row_stride.
@@ -219,6 +235,26 @@ ASHKV_API ashkv_status_t ashkv_policy_step(
  * ======================================================================== */
 ASHKV_API ashkv_status_t ashkv_memcpy2d(void* dst, int64_t dst_pitch, const void* src, int64_t src_pitch,
                                         int64_t width, int64_t height, void* stream);
+
+/* ========================================================================
+ * Indexed row copies: for r < n_rows and s < n_sub, `width` bytes from
+ *   src + (d_src_index ? d_src_index[r] : r) * src_row_stride + s * src_sub_stride
+ * to
+ *   dst + (d_dst_index ? d_dst_index[r] : r) * dst_row_stride + s * dst_sub_stride,
+ * in one kernel.  Used by the SGLang hooks for host pool rows that are not one
+ * contiguous run (ashkv/adapters/sglang/hooks.py:118-137 scatters them with a
+ * host-side index assignment per layer, :198-216 gathers them likewise).
+ * dst and src are device memory or page-locked host memory mapped for the
+ * current device (read and written through that mapping); anything else is
+ * refused with ASHKV_BAD_ARGUMENT before any launch.  Index lists are device
+ * memory; an index outside [0, dst_rows) / [0, src_rows) skips that row and
+ * sets ASHKV_FLAG_INDEX_RANGE in *d_status (if given).  Addresses, strides
+ * and width are multiples of 16 bytes.
+ * ======================================================================== */
+ASHKV_API ashkv_status_t ashkv_copy_rows_indexed(
+    void* dst, int64_t dst_row_stride, int64_t dst_sub_stride, const int64_t* d_dst_index, int64_t dst_rows,
+    const void* src, int64_t src_row_stride, int64_t src_sub_stride, const int64_t* d_src_index, int64_t src_rows,
+    int64_t width, int64_t n_sub, int64_t n_rows, uint32_t* d_status, void* stream);
 
 /* ========================================================================
  * Batched BF16 <-> INT8 page migration over device-resident lists.

@@ -2,7 +2,9 @@
 
 Run in a container that has the reference source tree (read-only is fine):
 
-    python tests/golden/make_golden.py --reference /root/reference
+    python tests/golden/make_golden.py --reference <reference tree>
+
+(or set ASHKV_REFERENCE to that tree instead of passing --reference)
 
 The reference is imported as the ``ashkv`` package from that tree, so this
 script must not import this repository's own ``ashkv``.  It produces:
@@ -318,9 +320,12 @@ def make_fp8_int4(out: dict) -> None:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("ASHKV_REFERENCE"),
+                    help="the reference source tree (default: $ASHKV_REFERENCE)")
     ap.add_argument("--out", default=str(HERE))
     args = ap.parse_args()
+    if not args.reference:
+        ap.error("give --reference or set ASHKV_REFERENCE")
     sys.dont_write_bytecode = True
     sys.path.insert(0, args.reference)
     import ashkv  # noqa: F401  (the reference package)

@@ -78,7 +78,7 @@ def decoded_rows(slots: np.ndarray, n: int, H: int, D: int) -> np.ndarray:
 
 
 @pytest.mark.parametrize("compact", [True, False])
-@pytest.mark.parametrize("contiguous,pin", [(True, True), (True, False), (False, False)])
+@pytest.mark.parametrize("contiguous,pin", [(True, True), (True, False), (False, False), (False, True)])
 def test_demote_writes_reference_slot_bytes(cuda, tmp_path, monkeypatch, contiguous, pin, compact):
     monkeypatch.chdir(tmp_path)
     L, cap, H, D, n = 3, 300, 8, 128, 77
@@ -134,12 +134,14 @@ def test_demote_promote_roundtrip_matches_oracle(cuda, tmp_path, monkeypatch):
     assert hooks.stats["tokens_decompressed"] == n
 
 
-def test_promote_subset_in_reference_order(cuda, tmp_path, monkeypatch):
-    """Promote into different device rows with a non-contiguous host index list."""
+@pytest.mark.parametrize("pin,heads", [(False, 8), (True, 8), (True, 1)])
+def test_promote_subset_in_reference_order(cuda, tmp_path, monkeypatch, pin, heads):
+    """Promote into different device rows with a non-contiguous host index list (a pinned
+    host pool takes the indexed gather kernel; 1 head leaves 130-byte slots, padded to 16)."""
     monkeypatch.chdir(tmp_path)
-    L, cap, H, D, n = 2, 200, 8, 128, 40
+    L, cap, H, D, n = 2, 200, heads, 128, 40
     dev = DevicePool(L, cap, H, D, cuda, seed=5)
-    host = HostPool(L, cap, H, D)
+    host = HostPool(L, cap, H, D, pin=pin)
     didx = torch.arange(n, device=cuda)
     hidx = torch.randperm(cap, generator=torch.Generator().manual_seed(6))[:n]
     hooks = SGLangHooks()
