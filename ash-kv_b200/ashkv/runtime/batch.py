@@ -247,6 +247,40 @@ class BatchMigrator:
         page_table.columns()["tier"][:] = tiers
 
 
+class StepGraph:
+    """A migration step captured once in a CUDA graph and replayed.
+
+    ``body`` issues the step's device work on the current stream (for a
+    tensor-parallel step: the pressure exchange, then ``plan`` with the
+    exchanged device pressure, ``demote``, ``promote``).  Replaying the graph
+    launches every kernel of the step at once, so the small policy kernels do
+    not wait on the host between launches.  Every tensor the body reads must
+    keep its address between replays (update pressure inputs in place).
+    Construction runs ``body`` once on a side stream first (any one-time
+    set-up), which performs a real step: bring the page table back to the
+    wanted state before the first replay.
+    """
+
+    def __init__(self, body, device: torch.device):
+        self.body, self.device = body, device
+        side = torch.cuda.Stream(device)
+        side.wait_stream(torch.cuda.current_stream(device))
+        with torch.cuda.stream(side):
+            body()
+        torch.cuda.current_stream(device).wait_stream(side)
+        torch.cuda.synchronize(device)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            body()
+
+    def replay(self) -> None:
+        self.graph.replay()
+
+    def release(self) -> None:
+        """Drop the graph (before the process group that its collectives use is destroyed)."""
+        self.graph = None
+
+
 class Int8PageCodec:
     """Raw BF16 <-> INT8 page kernels over one SlotArena (``ashkv_int8_encode_pages`` /
     ``ashkv_int8_decode_pages``).
@@ -310,5 +344,6 @@ def stores_for(table: Mapping[tuple[int, int], object], n_slots: Mapping[int, in
     return out
 
 
-__all__ = ["DevicePageTable", "SlotArena", "TierStore", "KVLayers", "BatchMigrator", "Int8PageCodec", "StepLists",
+__all__ = ["DevicePageTable", "SlotArena", "TierStore", "KVLayers", "BatchMigrator", "StepGraph", "Int8PageCodec",
+           "StepLists",
            "int8_page_slot_bytes", "stores_for", "Tier"]

@@ -41,8 +41,13 @@
 namespace ashkv {
 namespace {
 
-constexpr int kThreads = 256;
+constexpr int kThreads = 256;  // largest CTA; smaller pages take smaller CTAs (block_threads)
 constexpr int kWarps = kThreads / 32;
+// Threads / warps of the running CTA: one page per CTA, and the CTA is sized to
+// the page (a 128-wide row's page gets one warp) so that no warp idles.
+#define kNT int(blockDim.x)
+#define kNW int(blockDim.x >> 5)
+__host__ __device__ constexpr int block_threads(int row) { return row >= 1024 ? 256 : row / 4; }
 constexpr int kTiers = 6;
 constexpr int kBatch = 32;
 constexpr int kMaxElems = 65536;  // 128 KiB of staging; outlier indices fit in 16 bits
@@ -204,7 +209,7 @@ __device__ __forceinline__ uint4 int4_dec8(uint32_t c, uint16_t scale) {
 template <int ROW>
 __device__ void stage_from_pool(const MigParams& p, const Entry& en, uint8_t* stage, int n8) {
   const uint32_t base = smem_u32(stage);
-  for (int k = threadIdx.x; k < n8; k += kThreads) cp_async16(base + stage_off(uint32_t(k) * 8u), pool_chunk<ROW>(p, en, k));
+  for (int k = threadIdx.x; k < n8; k += kNT) cp_async16(base + stage_off(uint32_t(k) * 8u), pool_chunk<ROW>(p, en, k));
   cp_async_wait_all();
 }
 
@@ -216,12 +221,12 @@ __device__ void stage_from_int8(const uint8_t* slot, int T, uint8_t* stage, int 
   const f2 YHI = pk2(y.hi, y.hi), YLO = pk2(y.lo, y.lo);
   constexpr int U = 4;
   (void)YHI; (void)YLO;
-  for (int k0 = threadIdx.x; k0 < n8; k0 += U * kThreads) {
+  for (int k0 = threadIdx.x; k0 < n8; k0 += U * kNT) {
     uint2 cw[U];
     uint16_t sc[U];
 #pragma unroll
     for (int u = 0; u < U; ++u) {
-      const int k = k0 + u * kThreads;
+      const int k = k0 + u * kNT;
       if (k < n8) {
         cw[u] = ld_nc_v2(codes + int64_t(k) * 8);
         sc[u] = reinterpret_cast<const uint16_t*>(slot)[k / CPR];
@@ -229,7 +234,7 @@ __device__ void stage_from_int8(const uint8_t* slot, int T, uint8_t* stage, int 
     }
 #pragma unroll
     for (int u = 0; u < U; ++u) {
-      const int k = k0 + u * kThreads;
+      const int k = k0 + u * kNT;
       if (k < n8) sts_chunk(stage, uint32_t(k) * 8u, int8_dec8(cw[u], f16_to_f32(sc[u])));
     }
   }
@@ -237,14 +242,14 @@ __device__ void stage_from_int8(const uint8_t* slot, int T, uint8_t* stage, int 
 
 __device__ void stage_from_fp8(const uint8_t* slot, uint8_t* stage, int n8) {
   constexpr int U = 4;
-  for (int k0 = threadIdx.x; k0 < n8; k0 += U * kThreads) {
+  for (int k0 = threadIdx.x; k0 < n8; k0 += U * kNT) {
     uint2 c[U];
 #pragma unroll
     for (int u = 0; u < U; ++u)
-      if (k0 + u * kThreads < n8) c[u] = ld_nc_v2(slot + int64_t(k0 + u * kThreads) * 8);
+      if (k0 + u * kNT < n8) c[u] = ld_nc_v2(slot + int64_t(k0 + u * kNT) * 8);
 #pragma unroll
     for (int u = 0; u < U; ++u)
-      if (k0 + u * kThreads < n8) sts_chunk(stage, uint32_t(k0 + u * kThreads) * 8u, fp8_dec8(c[u]));
+      if (k0 + u * kNT < n8) sts_chunk(stage, uint32_t(k0 + u * kNT) * 8u, fp8_dec8(c[u]));
   }
 }
 
@@ -252,17 +257,17 @@ __device__ void stage_from_int4(const uint8_t* slot, int64_t E, uint8_t* stage, 
   const uint16_t* scales = reinterpret_cast<const uint16_t*>(slot);
   const uint32_t* nib = reinterpret_cast<const uint32_t*>(slot + E / 32);
   constexpr int U = 4;
-  for (int k0 = threadIdx.x; k0 < n8; k0 += U * kThreads) {
+  for (int k0 = threadIdx.x; k0 < n8; k0 += U * kNT) {
     uint32_t c[U];
     uint16_t sc[U];
 #pragma unroll
     for (int u = 0; u < U; ++u) {
-      const int k = k0 + u * kThreads;
+      const int k = k0 + u * kNT;
       if (k < n8) { c[u] = nib[k]; sc[u] = scales[k >> 3]; }
     }
 #pragma unroll
     for (int u = 0; u < U; ++u)
-      if (k0 + u * kThreads < n8) sts_chunk(stage, uint32_t(k0 + u * kThreads) * 8u, int4_dec8(c[u], sc[u]));
+      if (k0 + u * kNT < n8) sts_chunk(stage, uint32_t(k0 + u * kNT) * 8u, int4_dec8(c[u], sc[u]));
   }
 }
 
@@ -272,7 +277,7 @@ __device__ void stage_from_nbit(const uint8_t* slot, int64_t E, int32_t cap, uin
   const uint8_t* codes = slot + nbit_codes_off(E);
   const int n_groups = int(E / 32);
   constexpr float half = float((1 << BITS) - 1) * 0.5f;
-  for (int g = threadIdx.x; g < n_groups; g += kThreads) {
+  for (int g = threadIdx.x; g < n_groups; g += kNT) {
     GroupCodes<BITS> gc;
     load_group<BITS>(delta, codes, g, gc);
     uint32_t o[16];
@@ -284,7 +289,7 @@ __device__ void stage_from_nbit(const uint8_t* slot, int64_t E, int32_t cap, uin
   __syncthreads();  // dense values first, then the outliers overwrite theirs
   const uint32_t n_out = min(*reinterpret_cast<const uint32_t*>(slot), uint32_t(cap));
   const uint32_t* ent = reinterpret_cast<const uint32_t*>(slot + nbit_entries_off(E, BITS));
-  for (uint32_t j = threadIdx.x; j < n_out; j += kThreads) {
+  for (uint32_t j = threadIdx.x; j < n_out; j += kNT) {
     const uint32_t e = ent[j];
     const uint32_t idx = e >> 16;
     if (idx < uint32_t(E)) *reinterpret_cast<uint16_t*>(stage + stage_off(idx)) = uint16_t(e & 0xFFFFu);
@@ -295,7 +300,7 @@ __device__ void stage_from_nbit(const uint8_t* slot, int64_t E, int32_t cap, uin
 template <int ROW>
 __device__ void pool_from_stage(const MigParams& p, const Entry& en, const uint8_t* stage, int n8) {
   constexpr int CPR = ROW / 8;
-  for (int k = threadIdx.x; k < n8; k += kThreads)
+  for (int k = threadIdx.x; k < n8; k += kNT)
     *reinterpret_cast<uint4*>(pool_row(p, en, k / CPR) + (k % CPR) * 8) = lds_chunk(stage, uint32_t(k) * 8u);
 }
 
@@ -308,7 +313,7 @@ __device__ void int8_from_stage(const uint8_t* stage, int T, uint8_t* slot) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int sub = lane / TEAM, lin = lane % TEAM;
   uint8_t* codes = slot + int8_codes_offset(T);
-  for (int r0 = warp * RPW; r0 < 2 * T; r0 += kWarps * RPW) {  // warp-uniform loop
+  for (int r0 = warp * RPW; r0 < 2 * T; r0 += kNW * RPW) {  // warp-uniform loop
     const int r = r0 + sub;
     const bool on = r < 2 * T;
     uint32_t w[4 * NCH];
@@ -329,7 +334,7 @@ __device__ void int8_from_stage(const uint8_t* stage, int T, uint8_t* slot) {
 }
 
 __device__ void fp8_from_stage(const uint8_t* stage, uint8_t* slot, int n8) {
-  for (int k = threadIdx.x; k < n8; k += kThreads) {
+  for (int k = threadIdx.x; k < n8; k += kNT) {
     const uint4 v = lds_chunk(stage, uint32_t(k) * 8u);
     *reinterpret_cast<uint2*>(slot + int64_t(k) * 8) =
         make_uint2(fp8x2_from_bf16x2(v.x) | (fp8x2_from_bf16x2(v.y) << 16),
@@ -342,7 +347,7 @@ __device__ void int4_from_stage(const uint8_t* stage, int64_t E, uint8_t* slot) 
   uint16_t* scales = reinterpret_cast<uint16_t*>(slot);
   uint8_t* nib = slot + E / 32;
   const int n_rows = int(E / 32), lane = threadIdx.x & 31;
-  for (int base = threadIdx.x & ~31; base < n_rows; base += kThreads) {  // warp-uniform
+  for (int base = threadIdx.x & ~31; base < n_rows; base += kNT) {  // warp-uniform
     const int g = base + lane;
     const bool on = g < n_rows;
     float x[4][8];
@@ -383,7 +388,7 @@ __device__ void int8_from_pool(const MigParams& p, const Entry& en, uint8_t* slo
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int sub = lane / TEAM, lin = lane % TEAM;
   uint8_t* codes = slot + int8_codes_offset(T);
-  for (int r0 = warp * RPW * U; r0 < 2 * T; r0 += kWarps * RPW * U) {  // warp-uniform
+  for (int r0 = warp * RPW * U; r0 < 2 * T; r0 += kNW * RPW * U) {  // warp-uniform
     uint32_t w[U][4 * NCH];
 #pragma unroll
     for (int u = 0; u < U; ++u) {
@@ -414,14 +419,14 @@ __device__ void int8_from_pool(const MigParams& p, const Entry& en, uint8_t* slo
 template <int ROW>
 __device__ void fp8_from_pool(const MigParams& p, const Entry& en, uint8_t* slot, int n8) {
   constexpr int U = 4;
-  for (int k0 = threadIdx.x; k0 < n8; k0 += U * kThreads) {
+  for (int k0 = threadIdx.x; k0 < n8; k0 += U * kNT) {
     uint4 v[U];
 #pragma unroll
     for (int u = 0; u < U; ++u)
-      if (k0 + u * kThreads < n8) v[u] = ld_nc_v4(pool_chunk<ROW>(p, en, k0 + u * kThreads));
+      if (k0 + u * kNT < n8) v[u] = ld_nc_v4(pool_chunk<ROW>(p, en, k0 + u * kNT));
 #pragma unroll
     for (int u = 0; u < U; ++u) {
-      const int k = k0 + u * kThreads;
+      const int k = k0 + u * kNT;
       if (k >= n8) continue;
       *reinterpret_cast<uint2*>(slot + int64_t(k) * 8) =
           make_uint2(fp8x2_from_bf16x2(v[u].x) | (fp8x2_from_bf16x2(v[u].y) << 16),
@@ -433,7 +438,7 @@ __device__ void fp8_from_pool(const MigParams& p, const Entry& en, uint8_t* slot
 // Copy `bytes` (a multiple of 16) of a slot into shared memory.
 __device__ __forceinline__ void raw_copy(const uint8_t* slot, int64_t bytes, uint8_t* raw) {
   const uint32_t base = smem_u32(raw);
-  for (int64_t o = int64_t(threadIdx.x) * 16; o < bytes; o += kThreads * 16) cp_async16(base + uint32_t(o), slot + o);
+  for (int64_t o = int64_t(threadIdx.x) * 16; o < bytes; o += kNT * 16) cp_async16(base + uint32_t(o), slot + o);
   cp_async_wait_all();
   __syncthreads();
 }
@@ -442,7 +447,7 @@ __device__ __forceinline__ void raw_copy(const uint8_t* slot, int64_t bytes, uin
 template <int ROW, int FMT>
 __device__ void pool_from_raw(const MigParams& p, const Entry& en, const uint8_t* raw, int64_t E, int n8) {
   constexpr int CPR = ROW / 8;
-  for (int k = threadIdx.x; k < n8; k += kThreads) {
+  for (int k = threadIdx.x; k < n8; k += kNT) {
     uint4 o;
     if constexpr (FMT == ASHKV_PAGE_INT8) {
       const uint2 cw = *reinterpret_cast<const uint2*>(raw + int8_codes_offset(p.T) + int64_t(k) * 8);
@@ -463,7 +468,7 @@ __device__ void pool_from_nbit(const MigParams& p, const Entry& en, const uint8_
   const uint8_t* codes = raw + nbit_codes_off(E);
   const int n_groups = int(E / 32);
   constexpr float half = float((1 << BITS) - 1) * 0.5f;
-  for (int g = threadIdx.x; g < n_groups; g += kThreads) {
+  for (int g = threadIdx.x; g < n_groups; g += kNT) {
     GroupCodes<BITS> gc;
     load_group<BITS>(delta, codes, g, gc);
     uint32_t o[16];
@@ -476,7 +481,7 @@ __device__ void pool_from_nbit(const MigParams& p, const Entry& en, const uint8_
   __syncthreads();  // dense values first, then the outliers overwrite theirs
   const uint32_t n_out = min(*reinterpret_cast<const uint32_t*>(raw), uint32_t(p.outlier_cap));
   const uint32_t* ent = reinterpret_cast<const uint32_t*>(raw + nbit_entries_off(E, BITS));
-  for (uint32_t j = threadIdx.x; j < n_out; j += kThreads) {
+  for (uint32_t j = threadIdx.x; j < n_out; j += kNT) {
     const uint32_t e = ent[j];
     const uint32_t idx = e >> 16;
     if (idx < uint32_t(E)) pool_row(p, en, int(idx / ROW))[idx % ROW] = uint16_t(e & 0xFFFFu);
@@ -496,7 +501,7 @@ __device__ __forceinline__ uint32_t block_exclusive_scan(uint32_t v, uint32_t* s
   uint32_t before = 0;
   total = 0;
 #pragma unroll
-  for (int w = 0; w < kWarps; ++w) {
+  for (int w = 0; w < kNW; ++w) {
     const uint32_t t = s_warp[w];
     before += w < warp ? t : 0u;
     total += t;
@@ -519,7 +524,7 @@ __device__ bool nbit_from_stage(const MigParams& p, const Entry& en, const uint8
   np.codes = slot + nbit_codes_off(E);
   const int n_groups = int(E / 32), lane = threadIdx.x & 31;
   const uint32_t stage_base = smem_u32(stage);
-  for (int base = threadIdx.x & ~31; base < n_groups; base += kThreads) {  // warp-uniform
+  for (int base = threadIdx.x & ~31; base < n_groups; base += kNT) {  // warp-uniform
     const int g = base + lane;
     const bool on = g < n_groups;
     const uint32_t tile = stage_base + uint32_t(base) * 64u;
@@ -529,7 +534,7 @@ __device__ bool nbit_from_stage(const MigParams& p, const Entry& en, const uint8
   }
   __syncthreads();
   // groups [g0, g0 + per) of this thread, in order
-  const int per = (n_groups + kThreads - 1) / kThreads;
+  const int per = (n_groups + kNT - 1) / kNT;
   const int g0 = threadIdx.x * per;
   uint32_t cnt = 0;
   for (int j = 0; j < per; ++j)
@@ -575,53 +580,67 @@ __device__ __forceinline__ bool direct_edge(int fs, int ft) {
   return ft == ASHKV_PAGE_BF16 || (fs == ASHKV_PAGE_BF16 && (ft == ASHKV_PAGE_INT8 || ft == ASHKV_PAGE_FP8));
 }
 
-// Resolve entry i (one lane): the migrate() ladder's checks, then the slot.
+// Resolve entry i: the migrate() ladder's checks, then the slot.  Called by all
+// 32 lanes of a warp (lanes with !valid take part in the collectives only); the
+// slots are popped with one atomic per target tier and warp, lanes ranked by
+// their position in the ballot.
 template <int MODE>
-__device__ Entry resolve(const MigParams& p, int64_t i) {
+__device__ Entry resolve(const MigParams& p, int64_t i, bool valid) {
+  const int lane = threadIdx.x & 31;
   Entry e{};
   e.status = ASHKV_MIGRATE_BAD_PAGE;
   e.old_slot = e.new_slot = -1;
-  if (MODE == kStaged && p.entry_status[i] != kDeferred) {
-    e.status = kNotMine;
-    return e;
-  }
-  const int32_t page = p.list[i];
-  e.page = page;
-  if (page < 0 || page >= p.n_pages) return e;
-  e.cur = p.tier[page];
-  e.tgt = p.target[page];
-  e.layer = p.layer_id[page];
-  e.ts = p.token_start[page];
-  e.old_slot = p.page_slot[page];
-  const int32_t pin = p.pin ? p.pin[page] : 0;
-  if (pin > 0) { e.status = ASHKV_MIGRATE_PINNED; return e; }
-  if (e.cur == e.tgt) { e.status = ASHKV_MIGRATE_SAME_TIER; return e; }
-  const int fs = fmt_of(p, e.cur), ft = fmt_of(p, e.tgt);
-  if (fs == ASHKV_PAGE_NONE || ft == ASHKV_PAGE_NONE) { e.status = ASHKV_MIGRATE_NO_CODEC; return e; }
-  if (e.layer < 0 || e.layer >= p.n_layers || e.ts < 0) return e;
-  if (fs != ASHKV_PAGE_BF16 && (e.old_slot < 0 || e.old_slot >= p.store[e.cur].n_slots)) return e;
-  e.kbase = p.layer_k[e.layer] + uint64_t(e.ts) * uint64_t(p.row_stride) * 2u;
-  e.vbase = p.layer_v[e.layer] + uint64_t(e.ts) * uint64_t(p.row_stride) * 2u;
-  if (MODE == kDirect && !direct_edge(fs, ft)) {
-    e.status = kDeferred;
-    return e;
-  }
-  if (ft != ASHKV_PAGE_BF16) {
-    const Store& s = p.store[e.tgt];
-    const int32_t pos = atomicSub(s.free_top, 1) - 1;
-    if (pos < 0 || pos >= s.n_slots) {
-      atomicAdd(s.free_top, 1);
-      e.status = ASHKV_MIGRATE_NO_SLOT;
-      return e;
+  e.tgt = -1;
+  bool pop = false;
+  do {
+    if (!valid || (MODE == kStaged && p.entry_status[i] != kDeferred)) {
+      e.status = kNotMine;
+      break;
     }
-    e.new_slot = s.free_stack[pos];
-    if (e.new_slot < 0 || e.new_slot >= s.n_slots) {  // corrupt stack entry: leave it popped, report it
-      e.status = ASHKV_MIGRATE_BAD_PAGE;
-      e.new_slot = -1;
-      return e;
+    const int32_t page = p.list[i];
+    e.page = page;
+    if (page < 0 || page >= p.n_pages) break;
+    e.cur = p.tier[page];
+    e.tgt = p.target[page];
+    e.layer = p.layer_id[page];
+    e.ts = p.token_start[page];
+    e.old_slot = p.page_slot[page];
+    const int32_t pin = p.pin ? p.pin[page] : 0;
+    if (pin > 0) { e.status = ASHKV_MIGRATE_PINNED; break; }
+    if (e.cur == e.tgt) { e.status = ASHKV_MIGRATE_SAME_TIER; break; }
+    const int fs = fmt_of(p, e.cur), ft = fmt_of(p, e.tgt);
+    if (fs == ASHKV_PAGE_NONE || ft == ASHKV_PAGE_NONE) { e.status = ASHKV_MIGRATE_NO_CODEC; break; }
+    if (e.layer < 0 || e.layer >= p.n_layers || e.ts < 0) break;
+    if (fs != ASHKV_PAGE_BF16 && (e.old_slot < 0 || e.old_slot >= p.store[e.cur].n_slots)) break;
+    e.kbase = p.layer_k[e.layer] + uint64_t(e.ts) * uint64_t(p.row_stride) * 2u;
+    e.vbase = p.layer_v[e.layer] + uint64_t(e.ts) * uint64_t(p.row_stride) * 2u;
+    if (MODE == kDirect && !direct_edge(fs, ft)) { e.status = kDeferred; break; }
+    e.status = ASHKV_MIGRATE_OK;
+    pop = ft != ASHKV_PAGE_BF16;
+  } while (false);
+#pragma unroll 1
+  for (int t = 1; t < kTiers; ++t) {
+    const bool mine = pop && e.tgt == t;
+    const unsigned m = __ballot_sync(0xFFFFFFFFu, mine);
+    if (!m) continue;
+    const int leader = __ffs(m) - 1, want = __popc(m);
+    int32_t old = 0;
+    if (lane == leader) old = atomicSub(p.store[t].free_top, want);
+    old = __shfl_sync(0xFFFFFFFFu, old, leader);
+    const int taken = old <= 0 ? 0 : (old < want ? old : want);
+    if (lane == leader && taken < want) atomicAdd(p.store[t].free_top, want - taken);
+    if (mine) {
+      const int rank = __popc(m & ((1u << lane) - 1u));
+      const int32_t pos = old - 1 - rank;
+      if (rank >= taken) {
+        e.status = ASHKV_MIGRATE_NO_SLOT;
+      } else if (pos >= p.store[t].n_slots || (e.new_slot = p.store[t].free_stack[pos]) < 0 ||
+                 e.new_slot >= p.store[t].n_slots) {  // corrupt stack: leave it popped, report it
+        e.status = ASHKV_MIGRATE_BAD_PAGE;
+        e.new_slot = -1;
+      }
     }
   }
-  e.status = ASHKV_MIGRATE_OK;
   return e;
 }
 
@@ -641,7 +660,10 @@ __global__ void __launch_bounds__(kThreads, MODE == kDirect ? kDirectBlocks : kS
   for (int64_t b0 = blockIdx.x; b0 < count; b0 += int64_t(kBatch) * gridDim.x) {
     const int64_t left = (count - b0 + gridDim.x - 1) / gridDim.x;
     const int nb = left < kBatch ? int(left) : kBatch;
-    if (threadIdx.x < nb) s_ent[threadIdx.x] = resolve<MODE>(p, b0 + int64_t(threadIdx.x) * gridDim.x);
+    if (threadIdx.x < 32) {
+      const Entry e = resolve<MODE>(p, b0 + int64_t(threadIdx.x) * gridDim.x, int(threadIdx.x) < nb);
+      if (int(threadIdx.x) < nb) s_ent[threadIdx.x] = e;
+    }
     __syncthreads();
     for (int k = 0; k < nb; ++k) {
       const Entry en = s_ent[k];
@@ -721,19 +743,34 @@ struct ReleaseParams {
   uint32_t* status;
 };
 
+// Pushes with one atomic per tier and warp (lanes ranked in the ballot).
 __global__ void __launch_bounds__(256) release_slots_kernel(const ReleaseParams p) {
   const int32_t count = min(*p.count, p.max_entries);
-  for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < count; i += int64_t(gridDim.x) * blockDim.x) {
-    const int32_t v = p.released[i];
-    if (v < 0) continue;
-    const int t = v >> 24, slot = v & 0xFFFFFF;
-    if (t <= 0 || t >= kTiers || !p.store[t].free_stack || slot >= p.store[t].n_slots) {
+  const int lane = threadIdx.x & 31;
+  const int64_t stride = int64_t(gridDim.x) * blockDim.x;
+  for (int64_t i0 = int64_t(blockIdx.x) * blockDim.x + (threadIdx.x & ~31); i0 < count; i0 += stride) {
+    const int64_t i = i0 + lane;
+    const int32_t v = i < count ? p.released[i] : -1;
+    int t = v < 0 ? 0 : (v >> 24);
+    const int32_t slot = v & 0xFFFFFF;
+    if (v >= 0 && (t <= 0 || t >= kTiers || !p.store[t].free_stack || slot >= p.store[t].n_slots)) {
       if (p.status) atomicOr(p.status, ASHKV_FLAG_INDEX_RANGE);
-      continue;
+      t = 0;
     }
-    const int32_t pos = atomicAdd(p.store[t].free_top, 1);
-    if (pos >= 0 && pos < p.store[t].n_slots) p.store[t].free_stack[pos] = slot;
-    else if (p.status) atomicOr(p.status, ASHKV_FLAG_INDEX_RANGE);
+#pragma unroll 1
+    for (int tt = 1; tt < kTiers; ++tt) {
+      const unsigned m = __ballot_sync(0xFFFFFFFFu, t == tt);
+      if (!m) continue;
+      const int leader = __ffs(m) - 1;
+      int32_t base = 0;
+      if (lane == leader) base = atomicAdd(p.store[tt].free_top, __popc(m));
+      base = __shfl_sync(0xFFFFFFFFu, base, leader);
+      if (t == tt) {
+        const int32_t pos = base + __popc(m & ((1u << lane) - 1u));
+        if (pos >= 0 && pos < p.store[tt].n_slots) p.store[tt].free_stack[pos] = slot;
+        else if (p.status) atomicOr(p.status, ASHKV_FLAG_INDEX_RANGE);
+      }
+    }
   }
 }
 
@@ -742,6 +779,8 @@ bool row_ok(int32_t row) { return row == 128 || row == 256 || row == 512 || row 
 template <int ROW>
 ashkv_status_t launch_migrate(const MigParams& p, size_t raw_smem, size_t stage_smem, cudaStream_t st) {
   const int sms = sm_count() > 0 ? sm_count() : 148;
+  constexpr int NT = block_threads(ROW);
+  constexpr int CTA_SCALE = kThreads / NT;  // CTAs per SM grow as CTAs shrink
   cudaError_t e = cudaFuncSetAttribute(migrate_pages_kernel<ROW, kDirect>,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, int(raw_smem));
   if (e == cudaSuccess)
@@ -751,12 +790,12 @@ ashkv_status_t launch_migrate(const MigParams& p, size_t raw_smem, size_t stage_
     set_error("migrate_pages (shared memory attribute)", e);
     return ASHKV_LAUNCH_ERROR;
   }
-  const int64_t gd = std::min<int64_t>(p.max_entries, int64_t(sms) * kDirectBlocks);
-  migrate_pages_kernel<ROW, kDirect><<<unsigned(gd > 0 ? gd : 1), kThreads, raw_smem, st>>>(p);
+  const int64_t gd = std::min<int64_t>(p.max_entries, int64_t(sms) * kDirectBlocks * CTA_SCALE);
+  migrate_pages_kernel<ROW, kDirect><<<unsigned(gd > 0 ? gd : 1), NT, raw_smem, st>>>(p);
   const ashkv_status_t rc = check_launch("migrate_pages (direct pass)");
   if (rc != ASHKV_OK) return rc;
-  const int64_t gs = std::min<int64_t>(p.max_entries, int64_t(sms) * kStagedBlocks);
-  migrate_pages_kernel<ROW, kStaged><<<unsigned(gs > 0 ? gs : 1), kThreads, stage_smem, st>>>(p);
+  const int64_t gs = std::min<int64_t>(p.max_entries, int64_t(sms) * kStagedBlocks * CTA_SCALE);
+  migrate_pages_kernel<ROW, kStaged><<<unsigned(gs > 0 ? gs : 1), NT, stage_smem, st>>>(p);
   return check_launch("migrate_pages (staged pass)");
 }
 

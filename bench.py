@@ -388,6 +388,43 @@ class MigrationModel:
         torch.cuda.empty_cache()
 
 
+def graph_times(m: MigrationModel, body, tiers0: torch.Tensor, steps: int, dist, dev, before=None):
+    """Capture `body` (one step) in a CUDA graph and time `steps` replays with CUDA events, the
+    page table restored between them; (max-over-ranks ms per step, error text or None).  Every
+    rank learns whether all ranks captured before any rank replays a collective."""
+    from ashkv.runtime.batch import StepGraph
+    stream = torch.cuda.current_stream(dev)
+    sg, err = None, None
+    try:
+        sg = StepGraph(body, dev)  # runs one step on a side stream first
+    except Exception as e:  # noqa: BLE001 -- reported in the JSON line
+        err = f"{type(e).__name__}: {e}"[:200]
+    torch.cuda.synchronize()
+    m.restore(tiers0)
+    ok = torch.tensor([0.0 if sg is None else 1.0], device=dev)
+    if dist:
+        dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+    if float(ok) < 1.0:
+        return None, err or "capture failed on another rank"
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(steps)]
+    if dist:
+        dist.barrier()
+    for i in range(steps):
+        if before is not None:
+            before()
+        ev[i][0].record(stream)
+        sg.replay()
+        ev[i][1].record(stream)
+        m.restore(tiers0)
+    torch.cuda.synchronize()
+    ms = statistics.mean(e[0].elapsed_time(e[1]) for e in ev)
+    t = torch.tensor([ms], dtype=torch.float64, device=dev)
+    if dist:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    sg.release()
+    return float(t[0]), None
+
+
 def edge_histogram(m: MigrationModel, tiers_before: torch.Tensor) -> dict:
     after = m.tab.tier
     moved = after != tiers_before
@@ -459,7 +496,19 @@ def run_demote(dev, world: int, rank: int, dist, steps: int, warmup: int, layers
     if dist:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     plan_ms, dem_ms, pro_ms = float(t[0]), float(t[1]), float(t[2])
-    ms = plan_ms + dem_ms + pro_ms
+    eager_ms = plan_ms + dem_ms + pro_ms
+    pr_buf = torch.zeros(1, dtype=torch.float32, device=dev)
+
+    def body():
+        pr_buf.copy_(m.mig.pressure())
+        if dist:
+            dist.all_reduce(pr_buf, op=dist.ReduceOp.MAX)
+        m.mig.plan(pr_buf)
+        m.mig.demote()
+        m.mig.promote()
+
+    graph_ms, graph_err = graph_times(m, body, tiers0, steps, dist, dev)
+    ms = graph_ms if graph_ms is not None else eager_ms
     n_dem, n_pro = counts
     E, T = m.E, DEMOTE_T
     b16, b8 = page_format_bytes(0, E, T), page_format_bytes(1, E, T)
@@ -472,7 +521,9 @@ def run_demote(dev, world: int, rank: int, dist, steps: int, warmup: int, layers
            "demote_pages_per_s": round(n_dem / (dem_ms / 1e3), 1),
            "promote_pages_per_s": round(n_pro / (pro_ms / 1e3), 1),
            "step_pages_per_s": round((n_dem + n_pro) / (ms / 1e3), 1),
-           "ms_per_step": round(ms, 4), "plan_ms": round(plan_ms, 4), "demote_ms": round(dem_ms, 4),
+           "ms_per_step": round(ms, 4), "timing": "CUDA graph replay of the whole step" if graph_ms is not None
+           else "eager launches", "ms_per_step_eager": round(eager_ms, 4), "graph_error": graph_err,
+           "plan_ms": round(plan_ms, 4), "demote_ms": round(dem_ms, 4),
            "promote_ms": round(pro_ms, 4), "plan_includes": "pressure read + MAX all-reduce (N>1) + policy kernels",
            "demote_hbm_gbs": round(n_dem * (b16 + b8) / (dem_ms / 1e3) / 1e9, 1),
            "promote_hbm_gbs": round(n_pro * (b16 + b8) / (pro_ms / 1e3) / 1e9, 1),
@@ -527,17 +578,28 @@ def run_config5(dev, world: int, rank: int, dist, layers: int = DEMOTE_LAYERS) -
         if dist:
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
         plan_ms, dem_ms, pro_ms = (float(x) for x in t)
+        pr_buf = torch.tensor([p], dtype=torch.float32, device=dev)
+
+        def body():
+            if dist:
+                dist.all_reduce(pr_buf, op=dist.ReduceOp.MAX)
+            m.mig.plan(pr_buf)
+            m.mig.demote()
+            m.mig.promote()
+
+        graph_ms, graph_err = graph_times(m, body, tiers0, 3, dist, dev, before=lambda: pr_buf.fill_(p))
         moved = sum(hist.values())
         alg = sum(c * (page_format_bytes(m.formats[a], m.E, m.T, n_out) + page_format_bytes(m.formats[b], m.E, m.T, n_out))
                   for (a, b), c in hist.items())
-        ms = plan_ms + dem_ms + pro_ms
+        ms = graph_ms if graph_ms is not None else plan_ms + dem_ms + pro_ms
         rows.append({"pressure": p, "demote_list": nd, "promote_list": npro, "moved": moved,
+                     "step_ms": round(ms, 4), "graph_error": graph_err,
                      "edges": {f"{a}->{b}": c for (a, b), c in sorted(hist.items())},
                      "plan_ms": round(plan_ms, 4), "demote_ms": round(dem_ms, 4), "promote_ms": round(pro_ms, 4),
                      "pages_per_s": round(moved / (ms / 1e3), 1),
                      "migrate_hbm_gbs": round(alg / ((dem_ms + pro_ms) / 1e3) / 1e9, 1)})
     tot_moved = sum(r["moved"] for r in rows)
-    tot_ms = sum(r["plan_ms"] + r["demote_ms"] + r["promote_ms"] for r in rows)
+    tot_ms = sum(r["step_ms"] for r in rows)
     out = {"workload": f"{m.n} pages ({layers} layers x 16384) of [16, {heads} local heads, 128] bf16 K+V, "
                        f"tiers uniform over BF16/INT8/INT4/INT2, U[0,1] features, pressure swept {list(C5_PRESSURES)}",
            "pages": m.n, "heads_per_rank": heads, "per_pressure": rows,

@@ -118,11 +118,11 @@ EDGES = [(BF16, INT8), (BF16, FP8), (BF16, INT4), (BF16, NBIT4), (INT8, BF16), (
 FMT_NAME = {BF16: "bf16", INT8: "int8", FP8: "fp8", INT4: "int4", NBIT4: "nbit4", NBIT2: "nbit2"}
 
 
-@pytest.mark.parametrize("heads", [8, 1])
+@pytest.mark.parametrize("heads", [8, 4, 1])
 @pytest.mark.parametrize("edge", EDGES, ids=[f"{FMT_NAME[a]}-{FMT_NAME[b]}" for a, b in EDGES])
 def test_edge_matches_oracle(cuda, edge, heads):
     src_fmt, dst_fmt = edge
-    n = 96 if heads == 8 else 256
+    n = {8: 96, 4: 128, 1: 256}[heads]
     env = Env(cuda, n, 16, heads, seed=7 + src_fmt * 7 + dst_fmt)
     src_tier = 0 if src_fmt == BF16 else 1
     dst_tier = 0 if dst_fmt == BF16 else (2 if src_fmt != BF16 else 1)
