@@ -21,6 +21,10 @@ both back to bf16.
              s, so its results travel device->host while step s's inputs travel
              host->device); ``e2e_sequential`` is the same with no overlap
              between steps.
+             ``e2e.link_bound`` is the same metric at the PCIe bound: one step's
+             host->device and device->host bytes as two concurrent plain pinned
+             copies, all ranks at once.  Each rank first restricts itself to the
+             CPUs local to its GPU, so its pinned buffers live on that socket.
 ``e2e_bytes_api`` — the same through ``encode(bytes)`` / ``decode(bytes)``
              (Python ``bytes`` in and out: adds host copies into pinned staging
              and into freshly allocated result objects).
@@ -471,6 +475,80 @@ def edge_histogram(m: MigrationModel, tiers_before: torch.Tensor) -> dict:
     return {(i // 8, i % 8): c for i, c in enumerate(h) if c}
 
 
+def link_time(dev, h2d_bytes: int, d2h_bytes: int, dist, reps: int = 5) -> float:
+    """Seconds for one host->device copy of h2d_bytes and one device->host copy of
+    d2h_bytes, issued at once on two streams between pinned host memory and the
+    device (the PCIe bound of one e2e step); all ranks copy at the same time."""
+    hs = torch.empty(h2d_bytes, dtype=torch.uint8, pin_memory=True)
+    dd = torch.empty(h2d_bytes, dtype=torch.uint8, device=dev)
+    ds = torch.zeros(d2h_bytes, dtype=torch.uint8, device=dev)
+    hd = torch.empty(d2h_bytes, dtype=torch.uint8, pin_memory=True)
+    s1, s2 = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+
+    def once():
+        with torch.cuda.stream(s1):
+            dd.copy_(hs, non_blocking=True)
+        with torch.cuda.stream(s2):
+            hd.copy_(ds, non_blocking=True)
+
+    once()
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        once()
+    torch.cuda.synchronize()
+    dt = (time.perf_counter() - t0) / reps
+    del hs, dd, ds, hd
+    return dt
+
+
+def config4_model(dev, rank: int, layers: int, heads: int):
+    """The config-4 model placed in its starting tiers: the pages the policy would promote
+    (R >= theta_high + delta) in the FP8 tier as INT8 slots, the rest BF16."""
+    m = MigrationModel(dev, rank, layers, heads, {1: 1}, {1: 0.45}, seed=4000)
+    m.features(4242)
+    cfg = m.mig.cfg
+    R = torch.empty(m.n, dtype=torch.float32, device=dev)
+    from ashkv import _native
+    _native.score(m.tab.T, m.tab.S, m.tab.N, m.tab.P, cfg.w_T, cfg.w_S, cfg.w_N, cfg.w_P, R)
+    up = float(np.float32(cfg.theta_high + cfg.delta))
+    tiers0 = (R >= up).to(torch.int8)
+    m.place(tiers0)
+    return m, tiers0
+
+
+def config5_model(dev, rank: int, layers: int, heads: int):
+    """The config-5 table placed in its starting tiers, uniform over BF16/INT8/INT4/INT2."""
+    from ashkv import _native as N
+    m = MigrationModel(dev, rank, layers, heads, {1: N.PAGE_INT8, 2: N.PAGE_INT4, 3: N.PAGE_NBIT2},
+                       {1: 0.42, 2: 0.40, 3: 0.28}, seed=5000)
+    m.features(5151)
+    g = torch.Generator(device=dev).manual_seed(5252)
+    tiers0 = torch.randint(0, 4, (m.n,), generator=g, device=dev).to(torch.int8)
+    m.place(tiers0)
+    return m, tiers0
+
+
+def profile_migrate(dev, which: str, layers: int, heads: int) -> dict:
+    """One eager migration step of config 4 or 5 (pressure 0.9) for profiling: after the
+    placement launches (one direct and one staged migrate pass) come exactly four migrate
+    launches — demote list direct, staged; promote list direct, staged."""
+    m, tiers0 = (config4_model if which == "config4" else config5_model)(dev, 0, layers, heads)
+    torch.cuda.synchronize()
+    m.mig.plan(torch.tensor([0.9], dtype=torch.float32, device=dev))
+    m.mig.demote()
+    m.mig.promote()
+    torch.cuda.synchronize()
+    hist = edge_histogram(m, tiers0)
+    out = {"profile_migrate": which, "layers": layers, "heads": heads, "pages": m.n,
+           "lists": m.mig.lists.counts.tolist(), "edges": {f"{a}->{b}": c for (a, b), c in sorted(hist.items())},
+           "page_elems": m.E}
+    m.free()
+    return out
+
+
 def run_demote(dev, world: int, rank: int, dist, steps: int, warmup: int, layers: int = DEMOTE_LAYERS,
                head_split: int = 0) -> dict:
     """64-layer model, 8 KV heads x 128, 32 seq x 8192 tokens in 16-token
@@ -484,15 +562,7 @@ def run_demote(dev, world: int, rank: int, dist, steps: int, warmup: int, layers
     with CUDA events; the pages are put back in their starting tiers between steps, outside
     the timed events.  ``head_split`` > 0 runs one rank's share of that split on this GPU."""
     heads = DEMOTE_HEADS // (head_split or world)
-    m = MigrationModel(dev, rank, layers, heads, {1: 1}, {1: 0.45}, seed=4000)
-    m.features(4242)
-    cfg = m.mig.cfg
-    R = torch.empty(m.n, dtype=torch.float32, device=dev)
-    from ashkv import _native
-    _native.score(m.tab.T, m.tab.S, m.tab.N, m.tab.P, cfg.w_T, cfg.w_S, cfg.w_N, cfg.w_P, R)
-    up = float(np.float32(cfg.theta_high + cfg.delta))
-    tiers0 = (R >= up).to(torch.int8)
-    m.place(tiers0)
+    m, tiers0 = config4_model(dev, rank, layers, heads)
     stream = torch.cuda.current_stream(dev)
 
     def step(ev=None):
@@ -581,14 +651,8 @@ def run_config5(dev, world: int, rank: int, dist, layers: int = DEMOTE_LAYERS) -
     promotions) runs every tier edge the controller picks with its codec: BF16 <-> INT8
     (int8_default), INT8 <-> INT4 (int4_default), INT2 -> INT4 (int2_dithered).  The pages
     are put back in their starting tiers after each step, outside the timed events."""
-    from ashkv import _native as N
     heads = DEMOTE_HEADS // world
-    m = MigrationModel(dev, rank, layers, heads, {1: N.PAGE_INT8, 2: N.PAGE_INT4, 3: N.PAGE_NBIT2},
-                       {1: 0.42, 2: 0.40, 3: 0.28}, seed=5000)
-    m.features(5151)
-    g = torch.Generator(device=dev).manual_seed(5252)
-    tiers0 = torch.randint(0, 4, (m.n,), generator=g, device=dev).to(torch.int8)
-    m.place(tiers0)
+    m, tiers0 = config5_model(dev, rank, layers, heads)
     stream = torch.cuda.current_stream(dev)
     n_out = float(m.stores[3].slot_view()[:4096, :4].contiguous().view(torch.int32).float().mean())
     rows = []
@@ -763,6 +827,8 @@ def main() -> None:
     ap.add_argument("--no-codec-suite", action="store_true")
     ap.add_argument("--only-features", action="store_true",
                     help="run only the page-features leg on one GPU and print its JSON (profiling cases)")
+    ap.add_argument("--profile-migrate", choices=["config4", "config5"], default=None,
+                    help="run one eager migration step of config 4 or 5 on one GPU (profiling cases)")
     ap.add_argument("--demote-steps", type=int, default=10)
     ap.add_argument("--demote-layers", type=int, default=DEMOTE_LAYERS,
                     help="layers of the config-4 model (64; fewer only for small profiling cases)")
@@ -784,8 +850,15 @@ def main() -> None:
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
+    # host threads and pinned buffers on the GPU's own CPU socket (before any pinned allocation)
+    from ashkv.runtime.host import bind_to_device
+    affinity = bind_to_device(dev)
     if args.only_features:
         print(json.dumps({"page_features": features_bench(dev, iters=3)}), flush=True)
+        return
+    if args.profile_migrate:
+        heads = DEMOTE_HEADS // (args.demote_head_split or 1)
+        print(json.dumps(profile_migrate(dev, args.profile_migrate, args.demote_layers, heads)), flush=True)
         return
     dist = None
     if world > 1:
@@ -903,6 +976,10 @@ def main() -> None:
     streamed(steps_e2e)
     t_e2e = time.perf_counter() - t0
 
+    # the link bound of that step: one step's host->device and device->host byte counts as
+    # two plain pinned copies at once, on every rank at the same time
+    t_link = link_time(dev, h2d, d2h, dist)
+
     # the same through the bytes API
     hostK = pinK.view(torch.int16).numpy().tobytes()
     hostV = pinV.view(torch.int16).numpy().tobytes()
@@ -942,15 +1019,16 @@ def main() -> None:
                    "oracle_sample_elements": m, "oracle_sample_mismatches": mism}
 
     # max over ranks
-    t = torch.tensor([elapsed_ms, t_e2e, t_bytes, t_seq], dtype=torch.float64, device=dev)
+    t = torch.tensor([elapsed_ms, t_e2e, t_bytes, t_seq, t_link], dtype=torch.float64, device=dev)
     if dist:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    elapsed_ms, t_e2e, t_bytes, t_seq = float(t[0]), float(t[1]), float(t[2]), float(t[3])
+    elapsed_ms, t_e2e, t_bytes, t_seq, t_link = (float(x) for x in t)
 
     bytes_per_step = 2 * ELEMS * 2  # bf16 K + V through encode and decode
     value = world * bytes_per_step * args.steps / (elapsed_ms / 1e3) / 1e9
     e2e_value = world * bytes_per_step * steps_e2e / t_e2e / 1e9
     e2e_seq_value = world * bytes_per_step * args.e2e_steps / t_seq / 1e9
+    link_value = world * bytes_per_step / t_link / 1e9  # e2e units: bf16 bytes per second at the link bound
     e2e_bytes_value = world * bytes_per_step * args.e2e_bytes_steps / t_bytes / 1e9 if t_bytes > 0 else None
     enc_alg_bytes = ELEMS * 2 + ELEMS * BITS // 8 + (ELEMS // 32) * 2 + 4 * n_out + 4 * nb._native.nbit_bucket_count(ELEMS // 32)
     achieved = enc_alg_bytes / (enc_ms / 1e3) / 1e9
@@ -991,7 +1069,11 @@ def main() -> None:
             "e2e": {"value": round(e2e_value, 3), "unit": "GB/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "api": "DitheredNBitCodec.encode_pinned_batch/decode_pinned_batch",
                     "steps": steps_e2e,
-                    "mode": "streamed: decode of step s-1 beside encode of step s, blob copies ordered on the GPU"},
+                    "mode": "streamed: decode of step s-1 beside encode of step s, blob copies ordered on the GPU",
+                    "link_bound": round(link_value, 3), "frac_of_link": round(e2e_value / link_value, 4),
+                    "link": f"one step's h2d and d2h bytes as two concurrent pinned copies on all {world} "
+                            f"rank(s) at once: {round(t_link * 1e3, 2)} ms (max over ranks)",
+                    "host_affinity": affinity},
             "e2e_sequential": {"value": round(e2e_seq_value, 3), "unit": "GB/s", "steps": args.e2e_steps},
             "e2e_bytes_api": None if e2e_bytes_value is None else
             {"value": round(e2e_bytes_value, 3), "unit": "GB/s", "api": "DitheredNBitCodec.encode/decode(bytes)",
