@@ -16,8 +16,11 @@
 // Tiles: 128 queries x 128 keys per MMA group (M = N = 128, K = head_dim in
 // steps of 16), bf16 operands in 128-byte-swizzled K-major shared memory
 // (one 16 KiB chunk per 64 elements of head_dim), one fp32 accumulator of 128
-// TMEM columns per tile, two accumulators so the next tile's MMA overlaps this
-// tile's epilogue.  Sixteen warps share a tile's epilogue: warp w reads TMEM
+// TMEM columns per tile.  One CTA per SM: a producer warp issues the TMA loads
+// (4 B-tile stages, 160 KiB with the A tile) and the MMAs into 4 accumulators
+// (all 512 TMEM columns), so up to three tiles' MMAs run ahead of the
+// epilogue and the loads run further ahead still; no epilogue thread issues
+// anything.  Sixteen warps share a tile's epilogue: warp w reads TMEM
 // lanes 32 (w % 4) .. + 31 (accumulator rows) and columns 32 (w / 4) .. + 31,
 // so each thread handles 32 values per tile; pass 1 keeps an online max/sum
 // per (row, column group), pass 2 (keys x queries) a sum per (key row, column
@@ -33,10 +36,13 @@ namespace {
 
 constexpr int kTile = 128;                   // rows of a query or key tile
 constexpr int kChunkBytes = kTile * 128;     // 128 rows x 64 bf16 (one swizzle atom column) = 16 KiB
-constexpr int kThreadsF = 512;               // 16 warps: TMEM lane quadrant (warp % 4) x 32-column group (warp / 4)
+constexpr int kEpiWarps = 16;                // TMEM lane quadrant (warp % 4) x 32-column group (warp / 4)
+constexpr int kThreadsF = (kEpiWarps + 1) * 32;  // + one producer warp (TMA loads and MMA issue)
 constexpr int kColGroups = 4;
 constexpr uint32_t kPolls = 1u << 24;        // bounded mbarrier waits
-constexpr uint32_t kAccCols = 256;           // two 128-column fp32 accumulators
+constexpr int kSB = 4;                       // B tile stages
+constexpr int kAcc = 4;                      // 128-column fp32 accumulators
+constexpr uint32_t kAccCols = 128 * kAcc;    // the whole TMEM of the SM: one CTA per SM
 
 // ---------------------------------------------------------------- tcgen05 / TMA wrappers
 __device__ __forceinline__ void tmem_alloc(uint32_t* smem_dst, uint32_t ncols) {
@@ -140,18 +146,29 @@ __device__ __forceinline__ void mma_tile(uint32_t acc, const uint8_t* a, const u
                 kIdesc, (c | j) != 0);
 }
 
-// Shared layout of both passes: [A tile][B tile 0][B tile 1], 1024-byte aligned.
+// Shared layout of both passes: [A tile][B stage 0] .. [B stage kSB-1], 1024-byte aligned.
 struct PassSmem {
   uint8_t* a;
-  uint8_t* b[2];
+  uint32_t stage_bytes;  // one tile: nch chunks
+  __device__ __forceinline__ uint8_t* b(int i) const { return a + uint32_t(i + 1) * stage_bytes; }
 };
 __device__ __forceinline__ PassSmem carve(uint8_t* raw, int nch) {
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(raw) + 1023) & ~uintptr_t(1023));
   PassSmem s;
   s.a = base;
-  s.b[0] = base + nch * kChunkBytes;
-  s.b[1] = base + 2 * nch * kChunkBytes;
+  s.stage_bytes = uint32_t(nch) * kChunkBytes;
   return s;
+}
+struct PassBars {
+  uint64_t a, b[kSB], bfree[kSB], full[kAcc], empty[kAcc];
+};
+__device__ __forceinline__ void init_bars(PassBars& br) {
+  mbar_init(&br.a, 1);
+#pragma unroll
+  for (int i = 0; i < kSB; ++i) { mbar_init(&br.b[i], 1); mbar_init(&br.bfree[i], 1); }
+#pragma unroll
+  for (int i = 0; i < kAcc; ++i) { mbar_init(&br.full[i], 1); mbar_init(&br.empty[i], kEpiWarps); }
+  mbar_init_fence();
 }
 
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
@@ -159,92 +176,83 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
 }
 
 // The pipelined loop shared by both passes.  A (the CTA's fixed tile) is
-// loaded once; B tiles t = t0 .. t0 + nt - 1 stream through two shared-memory
-// buffers and two TMEM accumulators.  Thread 0 also produces: it issues the
-// MMA of tile i + 1 once its B tile has landed and every warp has released
-// that accumulator (bar_empty, one arrival per warp), and refills a B buffer
-// once the MMA that read it has completed.  Each warp copies its 32 values of
-// tile i out of TMEM, releases the accumulator and then runs epi(i, v), so the
-// arithmetic overlaps the next tile's MMA.  Returns false (and sets
-// ASHKV_FLAG_TIMEOUT) if a bounded wait gave up; all issued MMAs and TMA
-// loads have completed when it returns.
+// loaded once; B tiles t = t0 .. t0 + nt - 1 stream through kSB shared-memory
+// stages into kAcc TMEM accumulators.  One producer warp (its lane 0) issues
+// the TMA loads and the MMAs: tile i's MMA once its B stage has landed and the
+// epilogue warps have drained accumulator i % kAcc, and the refill of tile
+// i - 1's stage once that MMA has completed.  The epilogue warps copy their 32
+// values of tile i out of TMEM, release the accumulator and run epi(i, v).
+// Returns false (and sets ASHKV_FLAG_TIMEOUT) if a bounded wait gave up; all
+// issued MMAs and TMA loads have completed when it returns.
 template <class Epi>
 __device__ bool run_tiles(const CUtensorMap* amap, int a_head, int64_t a_tile, const CUtensorMap* bmap, int b_head,
-                          int64_t t0, int nt, int nch, const PassSmem& sm, uint64_t* bar_a, uint64_t* bar_b,
-                          uint64_t* bar_full, uint64_t* bar_empty, uint32_t tmem, uint32_t* status, Epi epi) {
+                          int64_t t0, int nt, int nch, const PassSmem& sm, PassBars& br, uint32_t tmem,
+                          uint32_t* status, Epi epi) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   volatile __shared__ int s_fail;
-  const uint32_t my_lanes = (uint32_t((warp & 3) * 32) << 16) + uint32_t(warp >> 2) * 32u;
-  // thread 0's record: B loads issued up to b_loaded and awaited up to b_waited,
-  // MMAs issued up to mma_issued and seen complete up to mma_done
-  int b_loaded = -1, b_waited = -1, mma_issued = -1, mma_done = -1;
-  bool a_waited = false;
-  if (tid == 0) {
-    s_fail = 0;
-    load_tile(amap, sm.a, bar_a, nch, a_head, a_tile);
-    for (int i = 0; i < 2 && i < nt; ++i) {
-      load_tile(bmap, sm.b[i], &bar_b[i], nch, b_head, t0 + i);
-      b_loaded = i;
-    }
-    a_waited = mbar_wait_bounded(bar_a, 0, kPolls);
-    if (!a_waited || !mbar_wait_bounded(&bar_b[0], 0, kPolls)) {
-      s_fail = 1;
-    } else {
-      b_waited = 0;
-      tc_fence_after();
-      mma_tile(tmem, sm.a, sm.b[0], nch);
-      umma_commit(&bar_full[0]);
-      mma_issued = 0;
-    }
-  }
+  if (tid == 0) s_fail = 0;
   __syncthreads();
-  for (int i = 0; i < nt && !s_fail; ++i) {
-    const int buf = i & 1;
-    if (tid == 0 && i + 1 < nt) {  // produce tile i + 1
-      const int nb = (i + 1) & 1;
-      bool ok = mbar_wait_bounded(&bar_b[nb], ((i + 1) >> 1) & 1, kPolls);
-      if (ok) b_waited = i + 1;
-      if (ok && i + 1 >= 2) ok = mbar_wait_bounded(&bar_empty[nb], ((i - 1) >> 1) & 1, kPolls);
-      if (!ok) {
-        s_fail = 1;
-      } else {
+  // producer's record, for the clean-up: B loads issued up to `loaded` and awaited up
+  // to `waited`, MMAs issued up to `issued` and seen complete up to `done`
+  int loaded = -1, waited = -1, issued = -1, done = -1;
+  bool a_ok = true;
+  if (warp == kEpiWarps) {
+    if (lane == 0) {
+      load_tile(amap, sm.a, &br.a, nch, a_head, a_tile);
+      for (int t = 0; t < kSB && t < nt; ++t) {
+        load_tile(bmap, sm.b(t), &br.b[t], nch, b_head, t0 + t);
+        loaded = t;
+      }
+      a_ok = mbar_wait_bounded(&br.a, 0, kPolls);
+      bool ok = a_ok;
+      for (int i = 0; ok && i < nt; ++i) {
+        const int st = i % kSB, ac = i % kAcc;
+        ok = mbar_wait_bounded(&br.b[st], (i / kSB) & 1, kPolls);
+        if (!ok) break;
+        waited = i;
+        if (i >= kAcc && !(ok = mbar_wait_bounded(&br.empty[ac], ((i / kAcc) - 1) & 1, kPolls))) break;
         tc_fence_after();
-        mma_tile(tmem + uint32_t(nb) * 128u, sm.a, sm.b[nb], nch);
-        umma_commit(&bar_full[nb]);
-        mma_issued = i + 1;
+        mma_tile(tmem + uint32_t(ac) * 128u, sm.a, sm.b(st), nch);
+        umma_commit(&br.full[ac]);
+        umma_commit(&br.bfree[st]);
+        issued = i;
+        const int j = i - 1;  // tile j's MMA is the one before: refill its stage once it has completed
+        if (j >= 0 && j + kSB < nt) {
+          if (!(ok = mbar_wait_bounded(&br.bfree[j % kSB], (j / kSB) & 1, kPolls))) break;
+          done = j;
+          load_tile(bmap, sm.b(j % kSB), &br.b[j % kSB], nch, b_head, t0 + j + kSB);
+          loaded = j + kSB;
+        }
       }
+      if (!ok) s_fail = 1;
     }
     __syncwarp();
-    if (!mbar_wait_bounded(&bar_full[buf], (i >> 1) & 1, kPolls)) {
-      s_fail = 1;
-      break;
-    }
-    if (tid == 0) {
-      mma_done = i;
-      // MMA i has read B buffer `buf`: refill it with tile i + 2
-      if (i + 2 < nt) {
-        load_tile(bmap, sm.b[buf], &bar_b[buf], nch, b_head, t0 + i + 2);
-        b_loaded = i + 2;
+  } else {
+    const uint32_t my_lanes = (uint32_t((warp & 3) * 32) << 16) + uint32_t(warp >> 2) * 32u;
+    for (int i = 0; i < nt; ++i) {
+      const int ac = i % kAcc;
+      if (!mbar_wait_bounded(&br.full[ac], (i / kAcc) & 1, kPolls)) {
+        s_fail = 1;
+        break;
       }
+      tc_fence_after();
+      float v[32];
+      tmem_ld32(tmem + my_lanes + uint32_t(ac) * 128u, v);
+      tmem_ld_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&br.empty[ac]);  // this warp is done with the accumulator
+      epi(i, v);
     }
-    __syncwarp();
-    tc_fence_after();
-    float v[32];
-    tmem_ld32(tmem + my_lanes + uint32_t(buf) * 128u, v);
-    tmem_ld_wait();
-    tc_fence_before();
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&bar_empty[buf]);  // this warp is done with accumulator `buf`
-    epi(i, v);
   }
   __syncthreads();
   const bool ok = !s_fail;
-  if (!ok && tid == 0) {
-    atomicOr(status, ASHKV_FLAG_TIMEOUT);
-    // let every issued MMA and TMA load finish before TMEM and shared memory are released
-    for (int t = mma_done + 1; t <= mma_issued; ++t) mbar_wait_bounded(&bar_full[t & 1], (t >> 1) & 1, kPolls);
-    if (!a_waited) mbar_wait_bounded(bar_a, 0, kPolls);
-    for (int t = b_waited + 1; t <= b_loaded; ++t) mbar_wait_bounded(&bar_b[t & 1], (t >> 1) & 1, kPolls);
+  if (warp == kEpiWarps && lane == 0) {
+    if (!ok) atomicOr(status, ASHKV_FLAG_TIMEOUT);
+    // every issued MMA and TMA load completes before TMEM and shared memory are released
+    for (int t = done + 1; t <= issued; ++t) mbar_wait_bounded(&br.bfree[t % kSB], (t / kSB) & 1, kPolls);
+    if (!a_ok) mbar_wait_bounded(&br.a, 0, kPolls);
+    for (int t = waited + 1; t <= loaded; ++t) mbar_wait_bounded(&br.b[t % kSB], (t / kSB) & 1, kPolls);
   }
   tc_fence_before();
   __syncthreads();
@@ -253,11 +261,11 @@ __device__ bool run_tiles(const CUtensorMap* amap, int a_head, int64_t a_tile, c
 
 // Pass 1: CTA (query tile qt, query head h): log2-sum-exp2 of every query row.
 // Query tiles run in reverse order so the longest (most key tiles) start first.
-__global__ void __launch_bounds__(kThreadsF, 2) saliency_rows_kernel(const __grid_constant__ CUtensorMap tq,
+__global__ void __launch_bounds__(kThreadsF, 1) saliency_rows_kernel(const __grid_constant__ CUtensorMap tq,
                                                                      const __grid_constant__ CUtensorMap tk,
                                                                      const SalParams p) {
   extern __shared__ uint8_t smem_raw[];
-  __shared__ uint64_t bar_a, bar_b[2], bar_full[2], bar_empty[2];
+  __shared__ PassBars br;
   __shared__ uint32_t s_tmem;
   __shared__ float s_m[kColGroups][kTile], s_l[kColGroups][kTile];
   const int tid = threadIdx.x, warp = tid >> 5;
@@ -269,12 +277,7 @@ __global__ void __launch_bounds__(kThreadsF, 2) saliency_rows_kernel(const __gri
   const int nt = k_hi < 0 ? 0 : int(k_hi / kTile) + 1;
   const PassSmem sm = carve(smem_raw, p.nch);
   if (warp == 0) tmem_alloc(&s_tmem, kAccCols);
-  if (tid == 0) {
-    mbar_init(&bar_a, 1); mbar_init(&bar_b[0], 1); mbar_init(&bar_b[1], 1);
-    mbar_init(&bar_full[0], 1); mbar_init(&bar_full[1], 1);
-    mbar_init(&bar_empty[0], kThreadsF / 32); mbar_init(&bar_empty[1], kThreadsF / 32);
-    mbar_init_fence();
-  }
+  if (tid == 0) init_bars(br);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -282,7 +285,7 @@ __global__ void __launch_bounds__(kThreadsF, 2) saliency_rows_kernel(const __gri
   float m = -INFINITY, l = 0.0f;
   const float c = p.c;
   if (nt > 0) {
-    run_tiles(&tq, h, qt, &tk, hk, 0, nt, p.nch, sm, &bar_a, bar_b, bar_full, bar_empty, tmem, p.status,
+    run_tiles(&tq, h, qt, &tk, hk, 0, nt, p.nch, sm, br, tmem, p.status,
               [&](int i, float (&v)[32]) {
                 const int64_t k0 = int64_t(i) * kTile + cg * 32;
                 float mx = -INFINITY;
@@ -323,8 +326,10 @@ __global__ void __launch_bounds__(kThreadsF, 2) saliency_rows_kernel(const __gri
               });
   }
   // merge the four column groups of each row
-  s_m[cg][row] = m;
-  s_l[cg][row] = l;
+  if (warp < kEpiWarps) {
+    s_m[cg][row] = m;
+    s_l[cg][row] = l;
+  }
   __syncthreads();
   if (cg == 0 && qrow < p.n_q) {
     float M = -INFINITY;
@@ -345,11 +350,11 @@ __global__ void __launch_bounds__(kThreadsF, 2) saliency_rows_kernel(const __gri
 
 // Pass 2: CTA (key tile kt, query head h): sum over the query rows of
 // 2^(s * c - lse2[q]) for every key row of the tile (scores computed as K Q^T).
-__global__ void __launch_bounds__(kThreadsF, 2) saliency_cols_kernel(const __grid_constant__ CUtensorMap tq,
+__global__ void __launch_bounds__(kThreadsF, 1) saliency_cols_kernel(const __grid_constant__ CUtensorMap tq,
                                                                      const __grid_constant__ CUtensorMap tk,
                                                                      const SalParams p) {
   extern __shared__ uint8_t smem_raw[];
-  __shared__ uint64_t bar_a, bar_b[2], bar_full[2], bar_empty[2];
+  __shared__ PassBars br;
   __shared__ uint32_t s_tmem;
   __shared__ float s_sum[kColGroups][kTile];
   const int tid = threadIdx.x, warp = tid >> 5;
@@ -364,12 +369,7 @@ __global__ void __launch_bounds__(kThreadsF, 2) saliency_cols_kernel(const __gri
   const int nt = t0 < n_qt ? int(n_qt - t0) : 0;
   const PassSmem sm = carve(smem_raw, p.nch);
   if (warp == 0) tmem_alloc(&s_tmem, kAccCols);
-  if (tid == 0) {
-    mbar_init(&bar_a, 1); mbar_init(&bar_b[0], 1); mbar_init(&bar_b[1], 1);
-    mbar_init(&bar_full[0], 1); mbar_init(&bar_full[1], 1);
-    mbar_init(&bar_empty[0], kThreadsF / 32); mbar_init(&bar_empty[1], kThreadsF / 32);
-    mbar_init_fence();
-  }
+  if (tid == 0) init_bars(br);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -378,7 +378,7 @@ __global__ void __launch_bounds__(kThreadsF, 2) saliency_cols_kernel(const __gri
   const float* lse = p.lse2 + int64_t(h) * p.n_q;
   float acc_sum = 0.0f;
   if (nt > 0) {
-    run_tiles(&tk, hk, kt, &tq, h, t0, nt, p.nch, sm, &bar_a, bar_b, bar_full, bar_empty, tmem, p.status,
+    run_tiles(&tk, hk, kt, &tq, h, t0, nt, p.nch, sm, br, tmem, p.status,
               [&](int i, float (&v)[32]) {
                 const int64_t qc = (t0 + i) * kTile + cg * 32;
                 const bool full = p.q_pos0 + qc >= kpos && qc + 31 < p.n_q;  // every query of the group sees this key
@@ -407,7 +407,7 @@ __global__ void __launch_bounds__(kThreadsF, 2) saliency_cols_kernel(const __gri
                 }
               });
   }
-  s_sum[cg][row] = acc_sum;
+  if (warp < kEpiWarps) s_sum[cg][row] = acc_sum;
   __syncthreads();
   if (cg == 0 && kpos < p.n_k)
     p.colsum[int64_t(h) * p.n_k + kpos] = (s_sum[0][row] + s_sum[1][row]) + (s_sum[2][row] + s_sum[3][row]);
@@ -576,8 +576,8 @@ extern "C" ashkv_status_t ashkv_attention_saliency(const void* d_q, const void* 
     set_message("ashkv_attention_saliency: cannot build the tensor maps (16-byte aligned buffers needed)");
     return ASHKV_BAD_ARGUMENT;
   }
-  // Always the head_dim 128 size: at most two CTAs per SM, so their 2 x 256 TMEM columns fit in 512.
-  const int smem = 3 * 2 * kChunkBytes + 1024;
+  // Always the head_dim 128 size: one CTA per SM, which holds all 512 TMEM columns.
+  const int smem = (1 + kSB) * 2 * kChunkBytes + 1024;
   if (cudaFuncSetAttribute(saliency_rows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess ||
       cudaFuncSetAttribute(saliency_cols_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
     return check_launch("ashkv_attention_saliency smem attribute");

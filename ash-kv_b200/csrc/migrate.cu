@@ -17,10 +17,11 @@
 //   1. checks the entry the way migrate() does (pinned -> skipped, already at
 //      target -> skipped, a tier without a codec -> skipped) and takes a slot
 //      of the target tier's store (free stack, popped with an atomic);
-//   2. decodes the page into a bf16 staging tile in shared memory (64-byte
-//      rows of 32 elements, 16-byte chunks XOR-swizzled so thread-per-group
-//      and thread-per-chunk access are both free of bank conflicts);
-//   3. encodes the tile into the target slot (or the page's KV-pool rows);
+//   2. decodes the page (into a bf16 staging tile in shared memory for the
+//      staged edges: 64-byte rows of 32 elements, 16-byte chunks XOR-swizzled
+//      so thread-per-group and thread-per-chunk access are both free of bank
+//      conflicts);
+//   3. encodes it into the target slot (or the page's KV-pool rows);
 //   4. commits tier and slot in the device page table and records the slot it
 //      gave up.  ashkv_release_slots pushes recorded slots back afterwards, so
 //      stacks are only popped in this kernel and only pushed in that one.
@@ -29,8 +30,14 @@
 // Two launches share a list.  The direct pass moves the edges that need no
 // staging tile (BF16 -> INT8 row by row, BF16 -> FP8 chunk by chunk, and every
 // decode into BF16, which first copies the compressed slot into shared memory
-// with cp.async) and reports the entries that do not move; the staged pass
-// (the tile above, and the dithered encoder's registers) takes the rest.
+// with cp.async) and reports the entries that do not move.  With two or more
+// compressed tiers it also moves compressed -> INT8 / FP8 / INT4 pages: the
+// raw slot copy is decoded chunk by chunk straight into the target's encoder
+// (dithered sources overlay their outliers from a per-group index of the
+// sorted outlier list), so that compute-heavy work runs beside the
+// memory-bound BF16 edges of the same list.  The staged pass (the bf16 tile,
+// and the dithered encoder's per-page outlier ranking) takes the edges into
+// the dithered formats and BF16 -> INT4.
 #include <algorithm>
 
 #include "common.cuh"
@@ -86,6 +93,7 @@ struct MigParams {
   uint32_t round_keys[20];
   int32_t* entry_status;
   int32_t* released;
+  int32_t first_offset;  // direct pass: byte offset of the outlier index after the raw slot copy
 };
 
 struct Entry {
@@ -488,6 +496,206 @@ __device__ void pool_from_nbit(const MigParams& p, const Entry& en, const uint8_
   }
 }
 
+// ---------------------------------------------------------------- compressed -> compressed, direct
+// A compressed source slot, copied whole into shared memory (`raw`), read chunk
+// by chunk (8 elements) as the bf16 values its decoder gives, so that an edge
+// between two compressed tiers needs no bf16 staging tile: the target encoder
+// pulls its chunks straight from the raw bytes.  Dithered sources keep their
+// outliers in a sorted list; `first[g]` is the first list entry of group g or
+// later (built once per page), so a chunk finds its outliers in a few steps.
+
+// Eight codes of a dithered group (chunk c of group g) -> eight bf16, as group_bf16 decodes them.
+template <int BITS>
+__device__ __forceinline__ uint4 nbit_chunk(const uint8_t* raw, int64_t E, int k) {
+  constexpr float half = float((1 << BITS) - 1) * 0.5f;
+  const int g = k >> 2, c = k & 3;
+  const float delta = bf16_to_f32(reinterpret_cast<const uint16_t*>(raw + nbit_delta_off())[g]);
+  const f2 DEL = pk2(delta, delta), NH = pk2(-half, -half), N23 = pk2(-8388608.0f, -8388608.0f);
+  auto pair = [&](float a, float b) { return f32x2_to_bf16x2_pk(mul2(add2(add2(pk2(a, b), N23), NH), DEL)); };
+  const uint8_t* codes = raw + nbit_codes_off(E) + int64_t(g) * (4 * BITS);
+  uint32_t o[4];
+  if constexpr (BITS == 4) {  // word c: elements 8c .. 8c+7, byte j = (elem 2j) << 4 | elem 2j+1
+    const uint32_t w = reinterpret_cast<const uint32_t*>(codes)[c];
+    const uint32_t hi = (w >> 4) & 0x0F0F0F0Fu, lo = w & 0x0F0F0F0Fu;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) o[j] = pair(code_plus_2p23(hi, j), code_plus_2p23(lo, j));
+  } else {  // bytes 2c, 2c+1 of the group: four codes each, the first in the top bits
+    const uint32_t w = reinterpret_cast<const uint16_t*>(codes)[c];
+    const uint32_t c0 = (w >> 6) & 0x0303u, c1 = (w >> 4) & 0x0303u, c2 = (w >> 2) & 0x0303u, c3 = w & 0x0303u;
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      o[2 * j] = pair(code_plus_2p23(c0, j), code_plus_2p23(c1, j));
+      o[2 * j + 1] = pair(code_plus_2p23(c2, j), code_plus_2p23(c3, j));
+    }
+  }
+  return make_uint4(o[0], o[1], o[2], o[3]);
+}
+
+// first[g] = index of the first outlier entry whose element lies in group g or
+// later, for every group of the page (n_out where none does).  Entries are
+// ascending by element index, as the encoder writes them.
+template <int BITS>
+__device__ void build_outlier_index(const uint8_t* raw, int64_t E, int32_t cap, uint16_t* first) {
+  const uint32_t n_out = min(*reinterpret_cast<const uint32_t*>(raw), uint32_t(cap));
+  const uint32_t* ent = reinterpret_cast<const uint32_t*>(raw + nbit_entries_off(E, BITS));
+  const int n_groups = int(E / 32);
+  for (uint32_t j = threadIdx.x; j < n_out; j += kNT) {
+    const int gj = min(int(ent[j] >> 21), n_groups - 1);  // element index >> 5
+    const int gp = j == 0 ? -1 : min(int(ent[j - 1] >> 21), n_groups - 1);
+    for (int g = gp + 1; g <= gj; ++g) first[g] = uint16_t(j);
+  }
+  const int g_last = n_out == 0 ? -1 : min(int(ent[n_out - 1] >> 21), n_groups - 1);
+  for (int g = g_last + 1 + int(threadIdx.x); g < n_groups; g += kNT) first[g] = uint16_t(n_out);
+}
+
+// Overwrite chunk k's outliers (elements 8k .. 8k+7) in v.
+template <int BITS>
+__device__ __forceinline__ uint4 overlay_outliers(uint4 v, const uint8_t* raw, int64_t E, int32_t cap,
+                                                  const uint16_t* first, int k) {
+  const uint32_t n_out = min(*reinterpret_cast<const uint32_t*>(raw), uint32_t(cap));
+  const uint32_t* ent = reinterpret_cast<const uint32_t*>(raw + nbit_entries_off(E, BITS));
+  const uint32_t lo = uint32_t(k) * 8u, hi = lo + 8u;
+  for (uint32_t j = first[k >> 2]; j < n_out; ++j) {
+    const uint32_t e = ent[j], idx = e >> 16;
+    if (idx >= hi) break;
+    if (idx < lo) continue;
+    const uint32_t i = idx - lo, bits = e & 0xFFFFu;
+    const uint32_t keep = (i & 1u) ? 0x0000FFFFu : 0xFFFF0000u, put = (i & 1u) ? (bits << 16) : bits;
+    switch (i >> 1) {
+      case 0: v.x = (v.x & keep) | put; break;
+      case 1: v.y = (v.y & keep) | put; break;
+      case 2: v.z = (v.z & keep) | put; break;
+      default: v.w = (v.w & keep) | put; break;
+    }
+  }
+  return v;
+}
+
+// Chunk k of a compressed page in shared memory, decoded to bf16.
+template <int ROW, int FS>
+__device__ __forceinline__ uint4 raw_chunk(const uint8_t* raw, int T, int64_t E, int32_t cap, const uint16_t* first,
+                                           int k) {
+  if constexpr (FS == ASHKV_PAGE_INT8) {
+    const uint2 cw = *reinterpret_cast<const uint2*>(raw + int8_codes_offset(T) + int64_t(k) * 8);
+    return int8_dec8(cw, f16_to_f32(reinterpret_cast<const uint16_t*>(raw)[k / (ROW / 8)]));
+  } else if constexpr (FS == ASHKV_PAGE_FP8) {
+    return fp8_dec8(*reinterpret_cast<const uint2*>(raw + int64_t(k) * 8));
+  } else if constexpr (FS == ASHKV_PAGE_INT4) {
+    return int4_dec8(reinterpret_cast<const uint32_t*>(raw + E / 32)[k], reinterpret_cast<const uint16_t*>(raw)[k >> 3]);
+  } else {
+    constexpr int BITS = FS == ASHKV_PAGE_NBIT4 ? 4 : 2;
+    return overlay_outliers<BITS>(nbit_chunk<BITS>(raw, E, k), raw, E, cap, first, k);
+  }
+}
+
+// -> INT8 slot: TEAM lanes per row, NCH chunks per lane (int8_from_stage's mapping).
+template <int ROW, int FS>
+__device__ void int8_from_raw(const uint8_t* raw, int T, int64_t E, int32_t cap, const uint16_t* first,
+                              uint8_t* slot) {
+  constexpr int TEAM = ROW >= 1024 ? 32 : ROW / 32;
+  constexpr int NCH = ROW / (8 * TEAM);
+  constexpr int RPW = 32 / TEAM;
+  constexpr int CPR = ROW / 8;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int sub = lane / TEAM, lin = lane % TEAM;
+  uint8_t* codes = slot + int8_codes_offset(T);
+  for (int r0 = warp * RPW; r0 < 2 * T; r0 += kNW * RPW) {  // warp-uniform
+    const int r = r0 + sub;
+    const bool on = r < 2 * T;
+    uint32_t w[4 * NCH];
+#pragma unroll
+    for (int c = 0; c < NCH; ++c) {
+      const uint4 v = on ? raw_chunk<ROW, FS>(raw, T, E, cap, first, r * CPR + c * TEAM + lin) : make_uint4(0, 0, 0, 0);
+      w[4 * c] = v.x; w[4 * c + 1] = v.y; w[4 * c + 2] = v.z; w[4 * c + 3] = v.w;
+    }
+    const float am = fmaxf(team_absmax_bf16<TEAM>(w), 1e-8f);
+    if (!on) continue;
+    if (lin == 0) reinterpret_cast<uint16_t*>(slot)[r] = f32_to_f16(am);
+    const Int8Div d = int8_div(am);
+#pragma unroll
+    for (int c = 0; c < NCH; ++c)
+      *reinterpret_cast<uint2*>(codes + int64_t(r) * ROW + (c * TEAM + lin) * 8) =
+          make_uint2(int8_codes4_bf16(w[4 * c], w[4 * c + 1], d), int8_codes4_bf16(w[4 * c + 2], w[4 * c + 3], d));
+  }
+}
+
+// -> FP8 slot, chunk by chunk.
+template <int ROW, int FS>
+__device__ void fp8_from_raw(const uint8_t* raw, int T, int64_t E, int32_t cap, const uint16_t* first, uint8_t* slot,
+                             int n8) {
+  for (int k = threadIdx.x; k < n8; k += kNT) {
+    const uint4 v = raw_chunk<ROW, FS>(raw, T, E, cap, first, k);
+    *reinterpret_cast<uint2*>(slot + int64_t(k) * 8) =
+        make_uint2(fp8x2_from_bf16x2(v.x) | (fp8x2_from_bf16x2(v.y) << 16),
+                   fp8x2_from_bf16x2(v.z) | (fp8x2_from_bf16x2(v.w) << 16));
+  }
+}
+
+// -> INT4 slot (group 64): two lanes per group, four chunks (32 elements) per lane.
+template <int ROW, int FS>
+__device__ void int4_from_raw(const uint8_t* raw, int T, int64_t E, int32_t cap, const uint16_t* first,
+                              uint8_t* slot) {
+  uint16_t* scales = reinterpret_cast<uint16_t*>(slot);
+  uint8_t* nib = slot + E / 32;
+  const int n_rows = int(E / 32), lane = threadIdx.x & 31;
+  for (int base = threadIdx.x & ~31; base < n_rows; base += kNT) {  // warp-uniform
+    const int g = base + lane;
+    const bool on = g < n_rows;
+    float x[4][8];
+    float m = 0.0f;
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      unpack_chunk(on ? raw_chunk<ROW, FS>(raw, T, E, cap, first, 4 * g + c) : make_uint4(0, 0, 0, 0), x[c]);
+      m = chunk_max(m, x[c]);
+    }
+    m = max_nan(m, __shfl_xor_sync(0xFFFFFFFFu, m, 1));
+    if (!on) continue;
+    const float am = group_max_finish(m);
+    if ((g & 1) == 0) scales[g >> 1] = static_cast<uint16_t>(bf16_cpu(am));
+    const GroupDiv d = group_div(am);
+    uint32_t o[4];
+#pragma unroll
+    for (int c = 0; c < 4; ++c) o[c] = pack_chunk(x[c], d);
+    *reinterpret_cast<uint4*>(nib + int64_t(g) * 16) = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+}
+
+// One compressed -> compressed edge from the raw source bytes (FT: INT8, FP8 or INT4).
+template <int ROW, int FS>
+__device__ void xcode_from_raw(const MigParams& p, int ft, const uint8_t* raw, const uint16_t* first, int64_t E,
+                               uint8_t* dst) {
+  const int T = p.T;
+  if (ft == ASHKV_PAGE_INT8) int8_from_raw<ROW, FS>(raw, T, E, p.outlier_cap, first, dst);
+  else if (ft == ASHKV_PAGE_FP8) fp8_from_raw<ROW, FS>(raw, T, E, p.outlier_cap, first, dst, int(E / 8));
+  else int4_from_raw<ROW, FS>(raw, T, E, p.outlier_cap, first, dst);
+}
+
+// A compressed -> INT8 / FP8 / INT4 page: the source slot copied whole into
+// shared memory, then transcoded chunk by chunk (a dithered source first
+// indexes its outliers).  Called by every thread of the CTA.
+template <int ROW>
+__device__ __forceinline__ void xcode_page(const MigParams& p, int fs, int ft, const uint8_t* src, uint8_t* raw,
+                                           uint8_t* smem, int64_t E, uint8_t* dst) {
+  raw_copy(src, used_bytes(fs, E, p.T, p.outlier_cap), raw);
+  uint16_t* first = reinterpret_cast<uint16_t*>(smem + p.first_offset);
+  switch (fs) {
+    case ASHKV_PAGE_INT8: xcode_from_raw<ROW, ASHKV_PAGE_INT8>(p, ft, raw, first, E, dst); break;
+    case ASHKV_PAGE_FP8: xcode_from_raw<ROW, ASHKV_PAGE_FP8>(p, ft, raw, first, E, dst); break;
+    case ASHKV_PAGE_INT4: xcode_from_raw<ROW, ASHKV_PAGE_INT4>(p, ft, raw, first, E, dst); break;
+    case ASHKV_PAGE_NBIT4:
+      build_outlier_index<4>(raw, E, p.outlier_cap, first);
+      __syncthreads();
+      xcode_from_raw<ROW, ASHKV_PAGE_NBIT4>(p, ft, raw, first, E, dst);
+      break;
+    default:
+      build_outlier_index<2>(raw, E, p.outlier_cap, first);
+      __syncthreads();
+      xcode_from_raw<ROW, ASHKV_PAGE_NBIT2>(p, ft, raw, first, E, dst);
+      break;
+  }
+  __syncthreads();  // the raw copy and the outlier index are free again
+}
+
 __device__ __forceinline__ uint32_t block_exclusive_scan(uint32_t v, uint32_t* s_warp, uint32_t& total) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   uint32_t inc = v;
@@ -572,12 +780,19 @@ __device__ __forceinline__ int fmt_of(const MigParams& p, int t) {
 // every edge into BF16) and reports every entry that does not move; it marks
 // the other moving entries kDeferred without taking a slot, and the staged
 // pass (staging tile, the dithered encoder) moves only those.
-constexpr int kDirect = 0, kStaged = 1;
+// kDirectX is the direct pass of a tier set with two or more compressed tiers: it
+// also moves compressed -> INT8 / FP8 / INT4 pages (from the raw source copy), so
+// that work overlaps the memory-bound BF16 edges of the same list; a tier set
+// with one compressed tier launches the plain kDirect code.
+constexpr int kDirect = 0, kStaged = 1, kDirectX = 2;
 constexpr int32_t kDeferred = 100;
 constexpr int32_t kNotMine = 101;
 
+template <int MODE>
 __device__ __forceinline__ bool direct_edge(int fs, int ft) {
-  return ft == ASHKV_PAGE_BF16 || (fs == ASHKV_PAGE_BF16 && (ft == ASHKV_PAGE_INT8 || ft == ASHKV_PAGE_FP8));
+  if (ft == ASHKV_PAGE_BF16) return true;
+  if (fs == ASHKV_PAGE_BF16) return ft == ASHKV_PAGE_INT8 || ft == ASHKV_PAGE_FP8;
+  return MODE == kDirectX && (ft == ASHKV_PAGE_INT8 || ft == ASHKV_PAGE_FP8 || ft == ASHKV_PAGE_INT4);
 }
 
 // Resolve entry i: the migrate() ladder's checks, then the slot.  Called by all
@@ -614,7 +829,7 @@ __device__ Entry resolve(const MigParams& p, int64_t i, bool valid) {
     if (fs != ASHKV_PAGE_BF16 && (e.old_slot < 0 || e.old_slot >= p.store[e.cur].n_slots)) break;
     e.kbase = p.layer_k[e.layer] + uint64_t(e.ts) * uint64_t(p.row_stride) * 2u;
     e.vbase = p.layer_v[e.layer] + uint64_t(e.ts) * uint64_t(p.row_stride) * 2u;
-    if (MODE == kDirect && !direct_edge(fs, ft)) { e.status = kDeferred; break; }
+    if (MODE != kStaged && !direct_edge<MODE>(fs, ft)) { e.status = kDeferred; break; }
     e.status = ASHKV_MIGRATE_OK;
     pop = ft != ASHKV_PAGE_BF16;
   } while (false);
@@ -645,7 +860,7 @@ __device__ Entry resolve(const MigParams& p, int64_t i, bool valid) {
 }
 
 template <int ROW, int MODE>
-__global__ void __launch_bounds__(kThreads, MODE == kDirect ? kDirectBlocks : kStagedBlocks)
+__global__ void __launch_bounds__(kThreads, MODE == kStaged ? kStagedBlocks : kDirectBlocks)
     migrate_pages_kernel(const MigParams p) {
   extern __shared__ __align__(16) uint8_t smem[];
   __shared__ Entry s_ent[kBatch];
@@ -654,7 +869,7 @@ __global__ void __launch_bounds__(kThreads, MODE == kDirect ? kDirectBlocks : kS
   const int T = p.T;
   const int64_t E = 2 * int64_t(T) * ROW;
   const int n8 = int(E / 8);
-  uint8_t* stage = smem;  // direct pass: the raw copy of a compressed source
+  uint8_t* stage = smem;  // direct pass: the raw copy of a compressed source; staged pass: the bf16 tile
   uint32_t* s_omask = reinterpret_cast<uint32_t*>(smem + E * 2);
   const int32_t count = min(*p.count, p.max_entries);
   for (int64_t b0 = blockIdx.x; b0 < count; b0 += int64_t(kBatch) * gridDim.x) {
@@ -676,12 +891,12 @@ __global__ void __launch_bounds__(kThreads, MODE == kDirect ? kDirectBlocks : kS
                                                    : p.store[en.cur].data + int64_t(en.old_slot) * p.store[en.cur].slot_bytes;
         uint8_t* dst = ft == ASHKV_PAGE_BF16 ? nullptr
                                              : p.store[en.tgt].data + int64_t(en.new_slot) * p.store[en.tgt].slot_bytes;
-        if constexpr (MODE == kDirect) {
+        if constexpr (MODE != kStaged) {
           if (fs == ASHKV_PAGE_BF16 && ft == ASHKV_PAGE_INT8) {
             int8_from_pool<ROW>(p, en, dst);
           } else if (fs == ASHKV_PAGE_BF16) {
             fp8_from_pool<ROW>(p, en, dst, n8);
-          } else {  // into BF16
+          } else if (MODE == kDirect || ft == ASHKV_PAGE_BF16) {  // into BF16
             raw_copy(src, used_bytes(fs, E, T, p.outlier_cap), stage);
             switch (fs) {
               case ASHKV_PAGE_INT8: pool_from_raw<ROW, ASHKV_PAGE_INT8>(p, en, stage, E, n8); break;
@@ -691,6 +906,8 @@ __global__ void __launch_bounds__(kThreads, MODE == kDirect ? kDirectBlocks : kS
               default: pool_from_nbit<ROW, 2>(p, en, stage, E); break;
             }
             __syncthreads();  // the raw copy is free again
+          } else {
+            xcode_page<ROW>(p, fs, ft, src, stage, smem, E, dst);
           }
         } else {
           switch (fs) {
@@ -777,12 +994,13 @@ __global__ void __launch_bounds__(256) release_slots_kernel(const ReleaseParams 
 bool row_ok(int32_t row) { return row == 128 || row == 256 || row == 512 || row == 1024 || row == 2048; }
 
 template <int ROW>
-ashkv_status_t launch_migrate(const MigParams& p, size_t raw_smem, size_t stage_smem, cudaStream_t st) {
+ashkv_status_t launch_migrate(const MigParams& p, bool xcode_direct, size_t raw_smem, size_t stage_smem,
+                              cudaStream_t st) {
   const int sms = sm_count() > 0 ? sm_count() : 148;
   constexpr int NT = block_threads(ROW);
   constexpr int CTA_SCALE = kThreads / NT;  // CTAs per SM grow as CTAs shrink
-  cudaError_t e = cudaFuncSetAttribute(migrate_pages_kernel<ROW, kDirect>,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize, int(raw_smem));
+  auto direct = xcode_direct ? migrate_pages_kernel<ROW, kDirectX> : migrate_pages_kernel<ROW, kDirect>;
+  cudaError_t e = cudaFuncSetAttribute(direct, cudaFuncAttributeMaxDynamicSharedMemorySize, int(raw_smem));
   if (e == cudaSuccess)
     e = cudaFuncSetAttribute(migrate_pages_kernel<ROW, kStaged>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              int(stage_smem));
@@ -791,7 +1009,7 @@ ashkv_status_t launch_migrate(const MigParams& p, size_t raw_smem, size_t stage_
     return ASHKV_LAUNCH_ERROR;
   }
   const int64_t gd = std::min<int64_t>(p.max_entries, int64_t(sms) * kDirectBlocks * CTA_SCALE);
-  migrate_pages_kernel<ROW, kDirect><<<unsigned(gd > 0 ? gd : 1), NT, raw_smem, st>>>(p);
+  direct<<<unsigned(gd > 0 ? gd : 1), NT, raw_smem, st>>>(p);
   const ashkv_status_t rc = check_launch("migrate_pages (direct pass)");
   if (rc != ASHKV_OK) return rc;
   const int64_t gs = std::min<int64_t>(p.max_entries, int64_t(sms) * kStagedBlocks * CTA_SCALE);
@@ -887,17 +1105,26 @@ extern "C" ashkv_status_t ashkv_migrate_pages(
   for (int t = 1; t < kTiers; ++t)
     if (p.store[t].format != ASHKV_PAGE_NONE)
       raw = std::max<size_t>(raw, size_t(used_bytes(p.store[t].format, E, tokens_per_page, outlier_cap)));
-  if (raw > size_t(200) * 1024) {
+  // Two or more compressed tiers: compressed -> INT8 / FP8 / INT4 edges can occur,
+  // and the direct pass takes them (the raw source copy, then the per-group
+  // outlier index of a dithered source).  With one, every edge has a BF16 end.
+  int compressed_tiers = 0;
+  for (int t = 1; t < kTiers; ++t) compressed_tiers += p.store[t].format != ASHKV_PAGE_NONE;
+  const bool xcode_direct = compressed_tiers >= 2;
+  p.first_offset = int32_t(raw);  // used_bytes is a multiple of 16
+  const size_t raw_smem = xcode_direct ? raw + size_t(E / 32) * 2 : raw;
+  const size_t stage_smem = smem;
+  if (raw_smem > size_t(200) * 1024) {
     set_message("ashkv_migrate_pages: outlier_cap too large for one page in shared memory");
     return ASHKV_BAD_ARGUMENT;
   }
   cudaStream_t st = as_stream(stream);
   switch (row_len) {
-    case 128: return launch_migrate<128>(p, raw, smem, st);
-    case 256: return launch_migrate<256>(p, raw, smem, st);
-    case 512: return launch_migrate<512>(p, raw, smem, st);
-    case 1024: return launch_migrate<1024>(p, raw, smem, st);
-    default: return launch_migrate<2048>(p, raw, smem, st);
+    case 128: return launch_migrate<128>(p, xcode_direct, raw_smem, stage_smem, st);
+    case 256: return launch_migrate<256>(p, xcode_direct, raw_smem, stage_smem, st);
+    case 512: return launch_migrate<512>(p, xcode_direct, raw_smem, stage_smem, st);
+    case 1024: return launch_migrate<1024>(p, xcode_direct, raw_smem, stage_smem, st);
+    default: return launch_migrate<2048>(p, xcode_direct, raw_smem, stage_smem, st);
   }
 }
 

@@ -25,6 +25,18 @@ __device__ __forceinline__ uint64_t xxround(uint64_t acc, uint64_t in) {
   acc = rotl64(acc, 31);
   return acc * P1;
 }
+// One lane step written around the chain's critical path.  With the lane state
+// kept as a = acc + in * P2 (the sum before the rotation), the next state is
+// rotl(a, 31) * P1 + in' * P2: the 64-bit addend rides in the wide multiply-add
+// of the low product, and the two cross products go to the high word, so the
+// 64-bit add no longer follows the multiply (in' * P2 is off the chain).
+__device__ __forceinline__ uint64_t rot_mul_add(uint64_t a, uint64_t m) {
+  const uint32_t al = uint32_t(a), ah = uint32_t(a >> 32);
+  const uint32_t rl = __funnelshift_l(ah, al, 31), rh = __funnelshift_l(al, ah, 31);  // rotl(a, 31)
+  const uint64_t w = uint64_t(rl) * uint32_t(P1) + m;
+  const uint32_t t = rl * uint32_t(P1 >> 32) + rh * uint32_t(P1);
+  return w + (uint64_t(t) << 32);
+}
 __device__ __forceinline__ uint64_t xxmerge(uint64_t h, uint64_t v) {
   h ^= xxround(0, v);
   return h * P1 + P4;
@@ -211,8 +223,10 @@ __global__ void __launch_bounds__(kItemsPerCta * 4, 1) xxh64_items_staged_kernel
     const int rows = int((cb < kChunk ? cb : kChunk) / 32);
     const uint8_t* row = sm + cstage * (kItemsPerCta * kRow) + slot * kRow + 8 * lane;
     if (rows == kChunk / 32) {  // full chunk: a fixed trip count, loads hoisted ahead of the chain
+      uint64_t a = v + lds64(row) * P2;
 #pragma unroll 16
-      for (int r = 0; r < kChunk / 32; ++r) v = xxround(v, lds64(row + r * 32));
+      for (int r = 1; r < kChunk / 32; ++r) a = rot_mul_add(a, lds64(row + r * 32) * P2);
+      v = rot_mul_add(a, 0);  // = xxround applied to all kChunk / 32 words
     } else {
 #pragma unroll 8
       for (int r = 0; r < rows; ++r) v = xxround(v, lds64(row + r * 32));

@@ -114,7 +114,8 @@ def assert_bytes(got: np.ndarray, want: np.ndarray, ties: np.ndarray, what) -> N
 
 EDGES = [(BF16, INT8), (BF16, FP8), (BF16, INT4), (BF16, NBIT4), (INT8, BF16), (FP8, BF16), (INT8, INT4),
          (INT8, NBIT4), (FP8, INT4), (INT4, INT8), (NBIT4, INT8), (INT4, NBIT2), (NBIT2, INT4), (NBIT2, NBIT4),
-         (NBIT4, NBIT2), (NBIT2, BF16), (INT4, FP8)]
+         (NBIT4, NBIT2), (NBIT2, BF16), (INT4, FP8), (NBIT4, FP8), (FP8, INT8), (NBIT2, INT8), (INT8, FP8),
+         (NBIT4, INT4)]
 FMT_NAME = {BF16: "bf16", INT8: "int8", FP8: "fp8", INT4: "int4", NBIT4: "nbit4", NBIT2: "nbit2"}
 
 
