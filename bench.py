@@ -300,6 +300,10 @@ def codec_suite(K: torch.Tensor, V: torch.Tensor, peak: float, iters: int = 20) 
     dV = torch.empty_like(dK)
     ms = timed(lambda: checksum_pages(pK, out=dK), lambda: checksum_pages(pV, out=dV))
     out["xxh64_pages"] = entry("xxh64_items_kernel", 2 * E + 8 * pK.shape[0], ms)
+    # write-only stream of the same size as a decoder's output (torch's fill kernel): the
+    # context for the write-dominated decoders, whose bytes are mostly the bf16 they write
+    ms = timed(lambda: bK.fill_(0.0), lambda: bV.fill_(0.0))
+    out["write_stream_fill"] = entry("torch fill_ (write only)", 2 * E, ms)
     return out
 
 
@@ -1014,7 +1018,14 @@ def main() -> None:
         mism = int((encQ.scales[: m // 32].cpu().view(torch.int16).numpy().view(np.uint16) != osc).sum()
                    + (encQ.codes[: m * BITS // 8].cpu().numpy() != ocodes).sum()
                    + (decQ[:m].cpu().view(torch.int16).numpy().view(np.uint16) != odec).sum())
-        quality = {"cosine_K": round(cos, 6), "outliers_K": int(encQ.bucket_counts.sum().item()),
+        # the same encode with fp32 torch.rand uniforms (the reference's kind of dither)
+        # in place of the in-kernel 16-bit Philox uniforms
+        u32 = torch.rand(ELEMS, generator=torch.Generator(device=dev).manual_seed(42), device=dev)
+        decU = nb.decode_groups(nb.encode_groups(K, BITS, SIGMA, uniform=u32))
+        cos_u = torch.nn.functional.cosine_similarity(K.float().view(-1), decU.float().view(-1), dim=0).item()
+        del u32, decU
+        quality = {"cosine_K": round(cos, 6), "cosine_K_fp32_uniform_dither": round(cos_u, 6),
+                   "outliers_K": int(encQ.bucket_counts.sum().item()),
                    "outlier_fraction": round(int(encQ.bucket_counts.sum().item()) / ELEMS, 6),
                    "oracle_sample_elements": m, "oracle_sample_mismatches": mism}
 
