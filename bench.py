@@ -949,26 +949,30 @@ def main() -> None:
         t_seq += time.perf_counter() - t0
         h2d = 2 * ELEMS * 2 + (bk.numel() - 8) + (bv.numel() - 8)
         d2h = bk.numel() + bv.numel() + 2 * (dk.numel() + dv.numel())
-    # streamed: the decode of step s-1 (queued first, on its own stream) runs beside the
-    # encode of step s, so the decoded values travel device->host while step s's inputs
-    # travel host->device; the blobs return without a host wait (the decode's reads are
+    # streamed: the decode of step s-1 (on its own stream) runs beside the encode of
+    # step s, so the decoded values travel device->host while step s's inputs travel
+    # host->device; the blobs return without a host wait (the decode's reads are
     # ordered after the encode's copies on the GPU); the host waits only for each
-    # encode's outlier counts (the blob layout) and, a step later, for each decode
-    # (three blob buffers, two output buffers)
+    # encode's outlier counts (the blob layout), with the next step's encode already
+    # queued, and, a step later, for each decode (three blob buffers, two output buffers)
     dec_stream = torch.cuda.Stream(dev)
     steps_e2e = args.e2e_steps
 
     def streamed(n_steps: int) -> None:
-        blobs = codec.encode_pinned_batch([pinK, pinV], blob3[0], host_sync=False)
+        # two encodes in flight: step s's inputs are queued host->device before the host
+        # waits for step s-1's outlier counts, so the host->device link does not idle
+        # while that encode runs and its blobs are queued device->host
+        pe = codec.encode_pinned_batch([pinK, pinV], blob3[0], wait=False, host_sync=False)
         pend = []
-        for s_ in range(1, n_steps):
+        for s_ in range(1, n_steps + 1):
+            nxt = (codec.encode_pinned_batch([pinK, pinV], blob3[s_ % 3], wait=False, host_sync=False)
+                   if s_ < n_steps else None)
+            blobs = pe.result()
             with torch.cuda.stream(dec_stream):
                 pend.append(codec.decode_pinned_batch(blobs, dec2[s_ % 2], wait=False))
-            blobs = codec.encode_pinned_batch([pinK, pinV], blob3[s_ % 3], wait=False, host_sync=False).result()
             if len(pend) > 1:
                 pend.pop(0).result()
-        with torch.cuda.stream(dec_stream):
-            pend.append(codec.decode_pinned_batch(blobs, dec2[n_steps % 2], wait=False))
+            pe = nxt
         for p_ in pend:
             p_.result()
 
@@ -1080,7 +1084,7 @@ def main() -> None:
             "e2e": {"value": round(e2e_value, 3), "unit": "GB/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "api": "DitheredNBitCodec.encode_pinned_batch/decode_pinned_batch",
                     "steps": steps_e2e,
-                    "mode": "streamed: decode of step s-1 beside encode of step s, blob copies ordered on the GPU",
+                    "mode": "streamed: decode of step s-1 beside encode of step s (the encode of step s+1 queued), blob copies ordered on the GPU",
                     "link_bound": round(link_value, 3), "frac_of_link": round(e2e_value / link_value, 4),
                     "link": f"one step's h2d and d2h bytes as two concurrent pinned copies on all {world} "
                             f"rank(s) at once: {round(t_link * 1e3, 2)} ms (max over ranks)",
