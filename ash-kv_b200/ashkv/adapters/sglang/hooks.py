@@ -43,6 +43,7 @@ import os
 import time
 from typing import Any
 
+import numpy as np
 import torch
 
 from ... import _native
@@ -56,9 +57,9 @@ def _contiguous_range(idx: torch.Tensor) -> int | None:
     n = idx.numel()
     if n == 0:
         return None
-    i = idx.detach().to("cpu", torch.int64)
-    first = int(i[0])
-    if n == 1 or (int(i[-1]) - first == n - 1 and bool((i[1:] - i[:-1] == 1).all())):
+    a = idx.detach().to("cpu", torch.int64).reshape(-1).numpy()  # host indices: no copy
+    first = int(a[0])
+    if n == 1 or (int(a[-1]) - first == n - 1 and bool((np.diff(a) == 1).all())):
         return first
     return None
 
@@ -255,12 +256,14 @@ class SGLangHooks:
         didx = device_indices.to(device=dev, dtype=torch.int64)
         used = slot if native_layer else 2 * H + row
         self.transfer_stats["h2d_bytes"] += 2 * n * used
+        first = _contiguous_range(host_indices)  # once for K and V (SGLang calls this hook per layer)
+        hidx = {}
         for name in ("k_buffer", "v_buffer"):
             hbuf = getattr(host_pool, name)
             L = hbuf.shape[1]
             upad = _ceil16(used)  # staged rows padded to 16 bytes for the indexed gather
             staged = torch.empty((n, upad), dtype=torch.uint8, device=dev)
-            self._read_host_slots(hbuf, host_indices, layer_id, staged, n, L, slot, used)
+            self._read_host_slots(hbuf, host_indices, layer_id, staged, n, L, slot, used, first, hidx)
             dst = getattr(device_pool, name)[layer_id].view(-1, row)
             if native_layer:
                 dst[didx] = staged.view(torch.bfloat16).view(n, row)
@@ -272,8 +275,10 @@ class SGLangHooks:
 
     @staticmethod
     def _read_host_slots(hbuf: torch.Tensor, host_indices, layer_id: int, staged: torch.Tensor, n: int, L: int,
-                         slot: int, used: int) -> None:
-        first = _contiguous_range(host_indices) if hbuf.is_contiguous() else None
+                         slot: int, used: int, first: int | None, hidx: dict) -> None:
+        """``first``: the contiguity of ``host_indices`` (from _contiguous_range); ``hidx`` caches
+        the indices' device copy between the K and V calls."""
+        first = first if hbuf.is_contiguous() else None
         upad = staged.shape[1]
         if first is not None:
             base = hbuf.data_ptr() + (first * L + layer_id) * slot
@@ -282,9 +287,10 @@ class SGLangHooks:
                 torch.cuda.current_stream(staged.device).synchronize()
         elif hbuf.is_pinned() and hbuf.is_contiguous():
             # scattered rows: one kernel reads the slots from the pinned pool through its device mapping
-            hidx = host_indices.detach().to(staged.device, torch.int64)
+            if "dev" not in hidx:
+                hidx["dev"] = host_indices.detach().to(staged.device, torch.int64)
             _native.copy_rows_indexed(staged.data_ptr(), upad, 0, None, n, hbuf.data_ptr() + layer_id * slot,
-                                      L * slot, 0, hidx, hbuf.shape[0], upad, 1, n, staged.device)
+                                      L * slot, 0, hidx["dev"], hbuf.shape[0], upad, 1, n, staged.device)
         else:
             hidx = host_indices.detach().to("cpu", torch.int64)
             rows = hbuf[hidx, layer_id].contiguous().view(n, -1).view(torch.uint8)[:, :used]

@@ -196,7 +196,10 @@ class BatchMigrator:
         self._scratch = torch.empty(_native.policy_scratch_ints(n), dtype=torch.int32, device=dev)
         self.status = torch.zeros(n, dtype=torch.int32, device=dev)
         self.released = torch.full((n,), -1, dtype=torch.int32, device=dev)
+        self.demote_status = torch.zeros(n, dtype=torch.int32, device=dev)
+        self.demote_released = torch.full((n,), -1, dtype=torch.int32, device=dev)
         self.device_status = torch.zeros(1, dtype=torch.int32, device=dev)
+        self._side: Optional[torch.cuda.Stream] = None
 
     def plan(self, pressure) -> StepLists:
         """Score every page, pick desired tiers and build the transition lists (device-resident).
@@ -210,14 +213,17 @@ class BatchMigrator:
                             L.demote, L.promote, L.counts, self._scratch)
         return L
 
-    def migrate(self, lst: torch.Tensor, count: torch.Tensor, target: Optional[torch.Tensor] = None) -> None:
-        """Move the first ``*count`` pages of ``lst`` to ``target[page]`` (default: the last plan's
-        targets), then release the slots they gave up."""
+    def _move(self, lst, count, target, status, released) -> None:
         t, kv = self.table, self.kv
         tgt = self.lists.target if target is None else target
         _native.migrate_pages(t.tier, t.pin, t.layer, t.token_start, t.slot, tgt, lst, count, kv.k_ptrs, kv.v_ptrs,
                               kv.n_layers, self.tokens_per_page, kv.row_len, kv.row_len, self._descs, self.sigma,
-                              self.seed, self.outlier_cap, self.status, self.released)
+                              self.seed, self.outlier_cap, status, released)
+
+    def migrate(self, lst: torch.Tensor, count: torch.Tensor, target: Optional[torch.Tensor] = None) -> None:
+        """Move the first ``*count`` pages of ``lst`` to ``target[page]`` (default: the last plan's
+        targets), then release the slots they gave up.  ``status`` / ``released`` report the entries."""
+        self._move(lst, count, target, self.status, self.released)
         _native.release_slots(self.released, count, lst.numel(), self._descs, self.device_status)
 
     def demote(self) -> None:
@@ -226,11 +232,36 @@ class BatchMigrator:
     def promote(self) -> None:
         self.migrate(self.lists.promote, self.lists.counts[1:2])
 
+    def demote_and_promote(self) -> None:
+        """Both lists of the last plan.  With one compressed tier every edge has a BF16 end:
+        demotions only take that tier's slots and promotions only give slots back, which are
+        released after both lists either way, so the two lists are moved concurrently on two
+        streams.  With more tiers they run in order (a promotion may take a slot a demotion
+        released).  ``demote_status`` / ``demote_released`` report the demotion list,
+        ``status`` / ``released`` the promotion list."""
+        L = self.lists
+        if len(self.stores) != 1:
+            self._move(L.demote, L.counts[0:1], None, self.demote_status, self.demote_released)
+            _native.release_slots(self.demote_released, L.counts[0:1], L.demote.numel(), self._descs,
+                                  self.device_status)
+            self.promote()
+            return
+        dev = self.table.T.device
+        cur = torch.cuda.current_stream(dev)
+        if self._side is None:
+            self._side = torch.cuda.Stream(dev)
+        self._side.wait_stream(cur)
+        with torch.cuda.stream(self._side):
+            self._move(L.promote, L.counts[1:2], None, self.status, self.released)
+        self._move(L.demote, L.counts[0:1], None, self.demote_status, self.demote_released)
+        cur.wait_stream(self._side)
+        _native.release_slots(self.demote_released, L.counts[0:1], L.demote.numel(), self._descs, self.device_status)
+        _native.release_slots(self.released, L.counts[1:2], L.promote.numel(), self._descs, self.device_status)
+
     def step(self, pressure) -> StepLists:
         """plan -> demote -> promote, all on the device."""
         L = self.plan(pressure)
-        self.demote()
-        self.promote()
+        self.demote_and_promote()
         return L
 
     def pressure(self) -> torch.Tensor:

@@ -555,7 +555,7 @@ def profile_migrate(dev, which: str, layers: int, heads: int) -> dict:
 
 def run_demote(dev, world: int, rank: int, dist, steps: int, warmup: int, layers: int = DEMOTE_LAYERS,
                head_split: int = 0) -> dict:
-    """64-layer model, 8 KV heads x 128, 32 seq x 8192 tokens in 16-token
+    """The demote/promote workload: 64-layer model, 8 KV heads x 128, 32 seq x 8192 tokens in 16-token
     pages, features U[0,1], default policy.  KV heads are sharded over the ranks (TP); the
     page table is replicated; the only collective is the MAX all-reduce of the ranks'
     allocator pressure (the FP8 tier store's occupancy) before each plan.  The pages the
@@ -616,8 +616,7 @@ def run_demote(dev, world: int, rank: int, dist, steps: int, warmup: int, layers
         if dist:
             dist.all_reduce(pr_buf, op=dist.ReduceOp.MAX)
         m.mig.plan(pr_buf)
-        m.mig.demote()
-        m.mig.promote()
+        m.mig.demote_and_promote()  # one compressed tier: the two lists move concurrently
 
     graph_ms, graph_err = graph_times(m, body, tiers0, steps, dist, dev)
     ms = graph_ms if graph_ms is not None else eager_ms
@@ -640,15 +639,15 @@ def run_demote(dev, world: int, rank: int, dist, steps: int, warmup: int, layers
            "demote_hbm_gbs": round(n_dem * (b16 + b8) / (dem_ms / 1e3) / 1e9, 1),
            "promote_hbm_gbs": round(n_pro * (b16 + b8) / (pro_ms / 1e3) / 1e9, 1),
            "scaling": "strong (fixed model, heads split over ranks)", "all_transitions_ok": ok,
-           "step": "pressure all-reduce (N>1) + policy kernels + migrate(demote list: direct + staged pass) "
-                   "+ release + migrate(promote list) + release",
+           "step": "pressure all-reduce (N>1) + policy kernels + migrate(demote list) beside migrate(promote "
+                   "list) on two streams (one compressed tier) + release of both",
            "gpu_launches_per_step": 8}
     m.free()
     return out
 
 
 def run_config5(dev, world: int, rank: int, dist, layers: int = DEMOTE_LAYERS) -> dict:
-    """a page table of 1,048,576 pages (64 layers x 16384 pages of
+    """The mixed-tier workload: a page table of 1,048,576 pages (64 layers x 16384 pages of
     [16 tokens, 8 heads, 128] bf16 K and V, heads sharded over ranks) with U[0,1]
     features and current tiers uniform over {BF16, INT8 (FP8 tier), INT4, INT2 (archive)};
     for each pressure of the sweep one step (plan -> migrate demotions -> migrate
@@ -690,8 +689,7 @@ def run_config5(dev, world: int, rank: int, dist, layers: int = DEMOTE_LAYERS) -
             if dist:
                 dist.all_reduce(pr_buf, op=dist.ReduceOp.MAX)
             m.mig.plan(pr_buf)
-            m.mig.demote()
-            m.mig.promote()
+            m.mig.demote_and_promote()  # three compressed tiers: in order
 
         graph_ms, graph_err = graph_times(m, body, tiers0, 3, dist, dev, before=lambda: pr_buf.fill_(p))
         moved = sum(hist.values())

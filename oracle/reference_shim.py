@@ -1,4 +1,4 @@
-"""Run the reference's own dithered N-bit codec on the host cores — TEST/BASELINE INFRASTRUCTURE ONLY.
+"""Run the reference's own dithered N-bit codec on the host cores — TEST AND CPU-BASELINE INFRASTRUCTURE ONLY.
 
 The reference's ``DitheredNBitCodec`` (ashkv/codecs/nbit_dithered.py:43-167)
 is PyTorch code that moves every tensor to CUDA (``.cuda()``,

@@ -96,11 +96,11 @@ def make_nbit(out: dict) -> None:
     def data(kind: str, n: int, g: torch.Generator) -> torch.Tensor:
         if kind == "normal":
             x = torch.randn(n, generator=g)
-        elif kind == "outliers":  # 0.1% of entries x50 at seeded positions (BASELINE config 2 style)
+        elif kind == "outliers":  # 0.1% of entries x50 at seeded positions (the INT4 codec workload's distribution)
             x = torch.randn(n, generator=g)
             pos = torch.randperm(n, generator=g)[: max(1, n // 1000)]
             x[pos] *= 50.0
-        elif kind == "headstd":  # per-row std ~U[0.5, 2] (BASELINE config 3 style)
+        elif kind == "headstd":  # per-row std ~U[0.5, 2] (the INT2 KV workload's distribution)
             x = torch.randn(n // 128, 128, generator=g) * (0.5 + 1.5 * torch.rand(n // 128, 1, generator=g))
             x = x.reshape(-1)
         elif kind == "wide":  # wide dynamic range: exercises the mean order and fp64 std

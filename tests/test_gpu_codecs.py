@@ -347,7 +347,7 @@ def test_nbit_decode_paths_agree(cuda):
 
 
 def test_nbit_config2_full_size_properties(cuda):
-    """BASELINE config 2 (INT4, K: [4096, 16, 8, 128], 0.1% x50 outliers) at full size:
+    """The INT4 codec workload (K: [4096, 16, 8, 128], 0.1% x50 outliers) at full size:
     outliers restored bit-exactly, inlier error bounded by one quantisation step,
     and a 1/64 sample of buckets bit-exact against the oracle."""
     n = 4096 * 16 * 8 * 128

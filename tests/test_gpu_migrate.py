@@ -237,17 +237,22 @@ def _check_accounting(env: Env, mig: BatchMigrator) -> None:
         assert len(np.intersect1d(free, live)) == 0 and len(np.unique(free)) == free.size
 
 
-def test_repeated_steps_account_every_slot(cuda):
+@pytest.mark.parametrize("tiers", [3, 1])
+def test_repeated_steps_account_every_slot(cuda, tiers):
     """Plan -> demote -> promote repeated with changing features, changing pressure and
     pinned pages: no slot is lost or shared, pinned pages never move, and every page that
-    moved holds the oracle's transcode of what it held before the step."""
+    moved holds the oracle's transcode of what it held before the step.  With one
+    compressed tier the step moves its two lists concurrently."""
     n = 2048
     env = Env(cuda, n, 16, 1, seed=5)
-    stores = {1: TierStore(INT8, n, cuda, env.T, env.row), 2: TierStore(INT4, n, cuda, env.T, env.row),
-              3: TierStore(NBIT2, n, cuda, env.T, env.row, outlier_cap=CAP)}
-    mig = BatchMigrator(env.tab, env.kv, stores, ASHKVConfig(), KEYS_ALL, seed=SEED)
+    stores = {1: TierStore(INT8, n, cuda, env.T, env.row)}
+    if tiers == 3:
+        stores.update({2: TierStore(INT4, n, cuda, env.T, env.row),
+                       3: TierStore(NBIT2, n, cuda, env.T, env.row, outlier_cap=CAP)})
+    keys = KEYS_ALL if tiers == 3 else [(0, 1), (1, 0)]
+    mig = BatchMigrator(env.tab, env.kv, stores, ASHKVConfig(), keys, seed=SEED)
     rng = np.random.default_rng(0)
-    _place_mixed(env, mig, rng.integers(0, 4, n))
+    _place_mixed(env, mig, rng.integers(0, tiers + 1, n))
     pinned = rng.choice(n, 100, replace=False)
     env.tab.pin[torch.from_numpy(pinned).to(cuda)] = 1
     sample = rng.choice(n, 48, replace=False)

@@ -71,7 +71,7 @@ def test_device_tensors_stay_on_device(cuda):
 
 @pytest.mark.parametrize("pressure", [0.5, 0.7, 0.9, 0.95, 0.96, 0.97])
 def test_policy_step_lists_config5(cuda, pressure):
-    """1,048,576 pages, tiers uniform in {0..3}, pressure sweep."""
+    """The mixed-tier plan at scale: 1,048,576 pages, tiers uniform in {0..3}, pressure sweep."""
     n = 1 << 20
     g = torch.Generator(device=cuda).manual_seed(int(pressure * 100))
     T, S, N, P = (torch.rand(n, generator=g, device=cuda) for _ in range(4))
