@@ -16,11 +16,13 @@ both back to bf16.
              start in pinned host memory, every step copies them to the device,
              encodes, writes the reference blob into pinned host memory, copies
              the blobs back, decodes, and reads the bf16 result back to the
-             host -- all inside the timed region.  Steps stream with one in
-             flight (the decode of step s-1 is queued before the encode of step
-             s, so its results travel device->host while step s's inputs travel
-             host->device); ``e2e_sequential`` is the same with no overlap
-             between steps.
+             host -- all inside the timed region.  Two ways to drive those calls
+             are timed: ``e2e_streamed`` (the decode of step s-1 beside the
+             encode of step s, step s+1's encode queued before the host waits
+             for step s's outlier counts) and ``e2e_sequential`` (each step's
+             calls in order); ``e2e`` is the faster, named in ``e2e.mode``
+             (streaming wins on a link of its own, in-order copies measured
+             faster where ranks share the host link).
              ``e2e.link_bound`` is the same metric at the PCIe bound: one step's
              host->device and device->host bytes as two concurrent plain pinned
              copies, all ranks at once.  Each rank first restricts itself to the
@@ -1039,8 +1041,13 @@ def main() -> None:
 
     bytes_per_step = 2 * ELEMS * 2  # bf16 K + V through encode and decode
     value = world * bytes_per_step * args.steps / (elapsed_ms / 1e3) / 1e9
-    e2e_value = world * bytes_per_step * steps_e2e / t_e2e / 1e9
+    e2e_stream_value = world * bytes_per_step * steps_e2e / t_e2e / 1e9
     e2e_seq_value = world * bytes_per_step * args.e2e_steps / t_seq / 1e9
+    # the end-to-end figure is the faster of the two ways to drive the same API calls:
+    # one process per GPU streams best on its own link, while ranks that share one host
+    # link measured faster issuing each step's copies in order (both are reported)
+    e2e_streamed_wins = e2e_stream_value >= e2e_seq_value
+    e2e_value = max(e2e_stream_value, e2e_seq_value)
     link_value = world * bytes_per_step / t_link / 1e9  # e2e units: bf16 bytes per second at the link bound
     e2e_bytes_value = world * bytes_per_step * args.e2e_bytes_steps / t_bytes / 1e9 if t_bytes > 0 else None
     enc_alg_bytes = ELEMS * 2 + ELEMS * BITS // 8 + (ELEMS // 32) * 2 + 4 * n_out + 4 * nb._native.nbit_bucket_count(ELEMS // 32)
@@ -1081,13 +1088,17 @@ def main() -> None:
                        "achieved_gbs": round(dec_achieved, 1), "frac": round(dec_achieved / peak, 4)},
             "e2e": {"value": round(e2e_value, 3), "unit": "GB/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "api": "DitheredNBitCodec.encode_pinned_batch/decode_pinned_batch",
-                    "steps": steps_e2e,
-                    "mode": "streamed: decode of step s-1 beside encode of step s (the encode of step s+1 queued), blob copies ordered on the GPU",
+                    "steps": steps_e2e if e2e_streamed_wins else args.e2e_steps,
+                    "mode": "streamed" if e2e_streamed_wins else "sequential",
                     "link_bound": round(link_value, 3), "frac_of_link": round(e2e_value / link_value, 4),
                     "link": f"one step's h2d and d2h bytes as two concurrent pinned copies on all {world} "
                             f"rank(s) at once: {round(t_link * 1e3, 2)} ms (max over ranks)",
                     "host_affinity": affinity},
-            "e2e_sequential": {"value": round(e2e_seq_value, 3), "unit": "GB/s", "steps": args.e2e_steps},
+            "e2e_streamed": {"value": round(e2e_stream_value, 3), "unit": "GB/s", "steps": steps_e2e,
+                             "mode": "decode of step s-1 beside encode of step s (the encode of step s+1 queued), "
+                                     "blob copies ordered on the GPU"},
+            "e2e_sequential": {"value": round(e2e_seq_value, 3), "unit": "GB/s", "steps": args.e2e_steps,
+                               "mode": "encode_pinned_batch then decode_pinned_batch per step, each waited for"},
             "e2e_bytes_api": None if e2e_bytes_value is None else
             {"value": round(e2e_bytes_value, 3), "unit": "GB/s", "api": "DitheredNBitCodec.encode/decode(bytes)",
              "steps": args.e2e_bytes_steps},
