@@ -327,9 +327,13 @@ __device__ __forceinline__ Int8Div int8_div(float am) {
 __device__ __forceinline__ float int8_quot(float s, const Int8Div& d) {
   return d.full ? div_full(s, d.am) : __fmul_rn(s, d.r);
 }
-// int32 whose low byte is the code.
+// int32 whose low byte is the code.  The half is copysign(0.5, q), one logic op
+// instead of a compare and a select: it equals q > 0 ? 0.5 : -0.5 for every q
+// but the zeros (+0 takes +0.5 here), where both sums truncate to 0, and a NaN
+// q gives NaN either way.
 __device__ __forceinline__ int32_t int8_round(float q) {
-  const float r = __fadd_rn(q, q > 0.0f ? 0.5f : -0.5f);
+  const float h = __uint_as_float((__float_as_uint(q) & 0x80000000u) | 0x3F000000u);
+  const float r = __fadd_rn(q, h);
   int32_t c;
   asm("cvt.rzi.s32.f32 %0, %1;" : "=r"(c) : "f"(r));  // saturating; NaN -> 0
   return c;
