@@ -8,8 +8,9 @@ same empty-input behaviour and the same SHA-256-based ``checksum``.
 
 Dither.  The reference draws ``U = torch.rand(...)`` from a CUDA generator
 seeded ``42 + encode_calls``.  Here ``encode`` generates the dither in-kernel
-from Philox4x32-10 keyed by that same seed (a different random stream, same
-distribution and seeding policy).  Passing ``uniform=`` (the U tensor the
+from Philox4x32-10 keyed by that same seed (a different random stream with
+the same seeding policy: centred 8-bit uniforms U = (b + 0.5) / 256, 16 per
+Philox draw, a dither resolution of 1/256 of the quantisation step).  Passing ``uniform=`` (the U tensor the
 reference would draw) reproduces the reference's output bit for bit.
 
 Device-resident entry points (no host copies): :func:`encode_groups`,

@@ -203,7 +203,10 @@ __device__ __forceinline__ void st_cs_v8(void* p, const U8& r) {
 }
 
 // Packed fp32 pairs (lo, hi) in a 64-bit register; f32x2 arithmetic rounds
-// each lane exactly like the scalar .rn instruction.
+// each lane exactly like the scalar .rn instruction.  One exception was
+// measured: mul.rn.f32x2 feeding add.rn.f32x2 came out as one fused
+// multiply-add (single rounding), so a product that must be rounded before a
+// sum is added with scalar add.rn, which is never contracted.
 typedef unsigned long long f2;
 __device__ __forceinline__ f2 pk2(float lo, float hi) {
   f2 r;

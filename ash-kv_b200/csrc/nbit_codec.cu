@@ -4,9 +4,10 @@
 // DitheredINT2Codec (ashkv/codecs/int2_dithered.py:36-147).  The reference
 // runs ~10 op-by-op tensor passes plus a nonzero()/host sync per call; here a
 // single pass does everything per 32-element group in one thread:
-//   load (16-byte streaming loads) -> mean -> fp64 variance -> outlier mask
-//   -> inlier absmax -> delta -> dithered quantise -> MSB-first pack ->
-//   one vector store of the codes + one bf16 delta store.
+//   load -> mean, sum of squares, min/max (one read) -> outlier mask (fp64
+//   variance only near the threshold) -> inlier absmax -> delta -> dithered
+//   quantise (second read) -> MSB-first pack -> one vector store of the codes
+//   + one bf16 delta store.
 // Outliers are ranked with a warp scan of per-group popcounts: each warp's
 // 32 groups form one "bucket" of 1024 elements whose ascending outlier list
 // the warp writes with no CTA or global synchronisation.
@@ -398,7 +399,7 @@ extern "C" ashkv_status_t ashkv_nbit_encode(
   if (!d_src || !d_scales || !d_codes || !d_bucket_counts || !d_status) return ASHKV_BAD_ARGUMENT;
   if (bucket_cap > 0 && !d_bucket_entries) return ASHKV_BAD_ARGUMENT;
   if (dither_mode == ASHKV_DITHER_TENSOR && !d_dither) return ASHKV_BAD_ARGUMENT;
-  if (dither_mode == ASHKV_DITHER_PHILOX && (dither_elem_offset % 8)) return ASHKV_BAD_ARGUMENT;
+  if (dither_mode == ASHKV_DITHER_PHILOX && (dither_elem_offset % 16)) return ASHKV_BAD_ARGUMENT;
   // 16-byte vector accesses; the 2-bit codes use 8-byte stores.
   // 32-byte vector loads of the source and dither; 8/16/32-byte code stores.
   if (!aligned(d_src, 32) || !aligned(d_scales, 2) || !aligned(d_codes, bits == 2 ? 8 : bits == 4 ? 16 : 32))

@@ -73,6 +73,22 @@ __device__ __forceinline__ uint32_t clamp_codes_s16x2(uint32_t v, uint32_t hi) {
   return r;
 }
 
+__device__ __forceinline__ float max3_nan(float a, float b, float c) {
+  float r;
+  asm("max.NaN.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+__device__ __forceinline__ float min3_nan(float a, float b, float c) {
+  float r;
+  asm("min.NaN.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+__device__ __forceinline__ float min_nan(float a, float b) {
+  float r;
+  asm("min.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+  return r;
+}
+
 __device__ __forceinline__ double warp_sum_f64(double v) {  // pairwise (butterfly) order, same in every lane
 #pragma unroll
   for (int off = 1; off < 32; off <<= 1) v = __dadd_rn(v, __shfl_xor_sync(0xFFFFFFFFu, v, off));
@@ -95,21 +111,41 @@ __device__ __forceinline__ void chunk_pairs(const Src& src, int c, f2 (&P)[4]) {
 }
 
 // Encodes one group (writes its packed codes and bf16 delta) and returns the
-// outlier bit mask.  The group is re-read from `src` for each pass so only
-// one 8-element chunk is live in registers at a time.
+// outlier bit mask.  The group is read from `src` twice (statistics, then
+// quantisation) so only one 8-element chunk is live in registers at a time.
 template <int BITS, int DMODE, typename Src>
 __device__ __forceinline__ uint32_t encode_group(const Src& src, const NbitEncParams& p, int64_t g, bool active) {
   constexpr uint32_t kMaxCode = (1u << BITS) - 1u;
-  // ---- mean: acc[i] = ((x_i + x_{8+i}) + x_{16+i}) + x_{24+i}, then acc[0] + ... + acc[7]
-  //      in order (PyTorch's CPU reduction order for a 32-wide inner dimension).
+  // ---- one pass over the group: the sum in the reference's order, acc[i] =
+  //      ((x_i + x_{8+i}) + x_{16+i}) + x_{24+i}, then acc[0] + ... + acc[7] in
+  //      order (PyTorch's CPU reduction order for a 32-wide inner dimension);
+  //      the sum of squares; the signed maximum and minimum (NaN-propagating).
   f2 A[4];
   chunk_pairs(src, 0, A);
+  f2 SQ0 = mul2(A[0], A[0]), SQ1 = mul2(A[1], A[1]);
+  SQ0 = fma2(A[2], A[2], SQ0);
+  SQ1 = fma2(A[3], A[3], SQ1);
+  float mx, mn;
+  {
+    float a0, a1, b0, b1, c0, c1, d0, d1;
+    upk2(A[0], a0, a1); upk2(A[1], b0, b1); upk2(A[2], c0, c1); upk2(A[3], d0, d1);
+    mx = max3_nan(max3_nan(a0, a1, b0), max3_nan(b1, c0, c1), max_nan(d0, d1));
+    mn = min3_nan(min3_nan(a0, a1, b0), min3_nan(b1, c0, c1), min_nan(d0, d1));
+  }
 #pragma unroll
   for (int c = 1; c < 4; ++c) {
     f2 P[4];
     chunk_pairs(src, c, P);
 #pragma unroll
-    for (int i = 0; i < 4; ++i) A[i] = add2(A[i], P[i]);
+    for (int i = 0; i < 4; ++i) {
+      A[i] = add2(A[i], P[i]);
+      if (i & 1) SQ1 = fma2(P[i], P[i], SQ1);
+      else SQ0 = fma2(P[i], P[i], SQ0);
+      float x0, x1;
+      upk2(P[i], x0, x1);
+      mx = max3_nan(mx, x0, x1);
+      mn = min3_nan(mn, x0, x1);
+    }
   }
   float acc[8];
 #pragma unroll
@@ -118,46 +154,33 @@ __device__ __forceinline__ uint32_t encode_group(const Src& src, const NbitEncPa
 #pragma unroll
   for (int i = 1; i < 8; ++i) s = __fadd_rn(s, acc[i]);
   const float mu = __fmul_rn(s, 0.03125f);
+  // max |x - mu| = max(RN(max x - mu), RN(mu - min x)) (rounding is monotone and odd).
+  const float dmax = max_nan(__fadd_rn(mx, -mu), __fadd_rn(mu, -mn));
+  const float xmax = max_nan(fabsf(mx), fabsf(mn));
+  float q2a, q2b;
+  upk2(add2(SQ0, SQ1), q2a, q2b);
+  const float q2 = __fadd_rn(q2a, q2b);
 
-  // ---- fp32 variance estimate, max|x - mu|, max|x| (NaN-propagating)
-  const f2 NMU = pk2(-mu, -mu);
-  f2 M2 = pk2(0.0f, 0.0f);
-  float dmax = 0.0f, xmax = 0.0f;
-#pragma unroll
-  for (int c = 0; c < 4; ++c) {
-    f2 P[4];
-    chunk_pairs(src, c, P);
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const f2 D = add2(P[i], NMU);
-      M2 = fma2(D, D, M2);
-      float d0, d1, x0, x1;
-      upk2(D, d0, d1);
-      upk2(P[i], x0, x1);
-      dmax = max3_abs_nan(dmax, d0, d1);
-      xmax = max3_abs_nan(xmax, x0, x1);
-    }
-  }
-  float m2a, m2b;
-  upk2(M2, m2a, m2b);
-  const float m2 = __fadd_rn(m2a, m2b);
-
-  // Bounds on the reference threshold.  m2 has relative error < 2^-19 w.r.t.
-  // sum (x - mu32)^2, which exceeds the exact M2 by 32 (mu - mu32)^2 with
-  // |mu - mu32| <= 31 * 2^-24 * max|x|.  The bounds only choose between the
-  // fast and the exact outlier path, so they are evaluated with approximate
-  // operations: the product by RN(1/31) and sqrt.approx each err by less than
-  // 2^-21 relative (a flushed subnormal only lowers a bound by far less than
-  // the 1e-8 term's margin), and margins of 2^-16 on m2 and 2^-12 on the
-  // threshold cover them together with the other roundings (fp32 bound
-  // arithmetic, the fp32 rounding of sd, + 1e-8 and * sigma in the reference).
+  // Bounds on the reference threshold from M2 = sum (x - m)^2 = q2_exact - 32 m^2
+  // (m the exact mean).  q2 is within 10u of q2_exact (u = 2^-24: at most ten
+  // roundings deep), and |m - mu| <= 31 u max|x| =: emu, so with mlo = max(|mu| - emu, 0)
+  // and mhi = |mu| + emu,
+  //   RN(RN(q2 (1 - 2^-17)) - RN(RN(32 mhi^2) (1 + 2^-17))) <= M2
+  //   RN(RN(q2 (1 + 2^-17)) - RN(RN(32 mlo^2) (1 - 2^-17))) >= M2,
+  // the 2^-17 = 128u margins covering every rounding on the way.  The bounds
+  // only choose between the fast and the exact outlier path; the threshold
+  // arithmetic below (sqrt.approx and the product by RN(1/31), each within
+  // 2^-21 relative, the fp32 rounding of sd, + 1e-8 and * sigma in the
+  // reference) is covered by the 2^-12 margin on the threshold.
   const float sigma = p.sigma;
-  const bool bounds_ok = sigma > 0.0f && isfinite(m2) && isfinite(xmax);
+  const bool bounds_ok = sigma > 0.0f && isfinite(q2) && isfinite(xmax);
   float thr_lo = 0.0f, thr_hi = 0.0f;
   if (bounds_ok) {
     const float emu = 31.0001f * 0x1p-24f * xmax;
-    const float m2_hi = m2 * (1.0f + 0x1p-16f);
-    const float m2_lo = fmaxf(m2 * (1.0f - 0x1p-16f) - 32.0f * emu * emu * (1.0f + 0x1p-16f), 0.0f);
+    const float amu = fabsf(mu);
+    const float mlo = fmaxf(amu - emu, 0.0f), mhi = amu + emu;
+    const float m2_hi = q2 * (1.0f + 0x1p-17f) - (32.0f * (mlo * mlo)) * (1.0f - 0x1p-17f);
+    const float m2_lo = fmaxf(q2 * (1.0f - 0x1p-17f) - (32.0f * (mhi * mhi)) * (1.0f + 0x1p-17f), 0.0f);
     constexpr float kInv31 = 1.0f / 31.0f;
     thr_hi = sigma * (sqrt_approx(m2_hi * kInv31) + 1e-8f) * (1.0f + 0x1p-12f);
     thr_lo = sigma * (sqrt_approx(m2_lo * kInv31) + 1e-8f) * (1.0f - 0x1p-12f);
@@ -208,8 +231,9 @@ __device__ __forceinline__ uint32_t encode_group(const Src& src, const NbitEncPa
   uint32_t o[BITS];  // packed codes: 32 * BITS bits, MSB-first within each byte
 #pragma unroll
   for (int k = 0; k < BITS; ++k) o[k] = 0u;
+  Philox4 rr;
 #pragma unroll
-  for (int c = 0; c < 4; ++c) {  // 8 elements per chunk / Philox draw
+  for (int c = 0; c < 4; ++c) {  // 8 elements per chunk, 16 per Philox draw
     f2 P[4];
     chunk_pairs(src, c, P);
     if (omask & (0xFFu << (8 * c))) {
@@ -233,13 +257,17 @@ __device__ __forceinline__ uint32_t encode_group(const Src& src, const NbitEncPa
       for (int h = 0; h < 4; ++h)
         DZ[h] = add2(pk2(__uint_as_float(u.v[2 * h]), __uint_as_float(u.v[2 * h + 1])), pk2(-0.5f, -0.5f));
     } else {
-      const uint64_t ctr = ((p.dither_offset + uint64_t(g) * 32) >> 3) + c;
-      const Philox4 r = philox4x32_10_rk(uint32_t(ctr), uint32_t(ctr >> 32), 0u, 0u, p.round_keys);
+      if ((c & 1) == 0) {
+        const uint64_t ctr = ((p.dither_offset + uint64_t(g) * 32) >> 4) + (c >> 1);
+        rr = philox4x32_10_rk(uint32_t(ctr), uint32_t(ctr >> 32), 0u, 0u, p.round_keys);
+      }
 #pragma unroll
       for (int h = 0; h < 4; ++h) {
-        // f = 1 + h16 * 2^-23, so U - 0.5 = 128 f - 128.5 exactly
-        const float flo = __uint_as_float(__byte_perm(r.v[h], 0x3F800000u, 0x7610));
-        const float fhi = __uint_as_float(__byte_perm(r.v[h], 0x3F800000u, 0x7632));
+        // U = (b + 0.5) / 256 from byte b = e & 15 of the draw for counter e >> 4:
+        // f = 1 + (2b + 1) * 2^-16, so U - 0.5 = 128 f - 128.5 exactly
+        const uint32_t wv = rr.v[2 * (c & 1) + (h >> 1)];
+        const float flo = __uint_as_float(__byte_perm(wv, 0x3F808080u, (h & 1) ? 0x7624 : 0x7604));
+        const float fhi = __uint_as_float(__byte_perm(wv, 0x3F808080u, (h & 1) ? 0x7634 : 0x7614));
         DZ[h] = fma2(pk2(flo, fhi), pk2(128.0f, 128.0f), pk2(-128.5f, -128.5f));
       }
     }
@@ -250,7 +278,15 @@ __device__ __forceinline__ uint32_t encode_group(const Src& src, const NbitEncPa
     // float clamp comes first (NaN -> 0), as in the reference.
     f2 Q[4];
 #pragma unroll
-    for (int h = 0; h < 4; ++h) Q[h] = add2(P[h], mul2(DZ[h], DELTA));  // a = x' + noise
+    for (int h = 0; h < 4; ++h) {
+      // a = RN(x' + RN((U - 0.5) * delta)).  The sum is taken with scalar add.rn: a packed
+      // add.rn.f32x2 fed by a packed multiply was measured to come out single-rounded (a fused
+      // multiply-add), which flips codes one ulp from a rounding tie.
+      float x0, x1, n0, n1;
+      upk2(P[h], x0, x1);
+      upk2(mul2(DZ[h], DELTA), n0, n1);
+      Q[h] = pk2(__fadd_rn(x0, n0), __fadd_rn(x1, n1));
+    }
     if (fast_div) {
 #pragma unroll
       for (int h = 0; h < 4; ++h) Q[h] = add2(add2(div2_rn(Q[h], YHI, YLO, NDELTA), HALF), MAGIC);
@@ -263,6 +299,36 @@ __device__ __forceinline__ uint32_t encode_group(const Src& src, const NbitEncPa
         const float v1 = fminf(fmaxf(__fadd_rn(__fdiv_rn(a1, delta), half), 0.0f), float(kMaxCode));
         Q[h] = add2(pk2(v0, v1), MAGIC);
       }
+    }
+    if constexpr (DMODE == ASHKV_DITHER_PHILOX) {
+      // No clamp is needed: |U - 0.5| <= 127.5/256 and |x'| <= am = delta * half (1 + 2^-23),
+      // so |a / delta| < half + 0.4982, and v = RN(RN(a / delta) + half) lies in
+      // (-0.5, 2 half + 0.5) = (-0.5, 2^BITS - 0.5): its rint is already a code, and
+      // byte 0 of each float above (1.5 * 2^23 + code) holds it.  The slow path
+      // clamps in float first.
+      uint32_t u[8];
+#pragma unroll
+      for (int h = 0; h < 4; ++h) {
+        float t0, t1;
+        upk2(Q[h], t0, t1);
+        u[2 * h] = __float_as_uint(t0);
+        u[2 * h + 1] = __float_as_uint(t1);
+      }
+      if constexpr (BITS == 8) {
+        o[2 * c] = __byte_perm(__byte_perm(u[0], u[1], 0x0040), __byte_perm(u[2], u[3], 0x0040), 0x5410);
+        o[2 * c + 1] = __byte_perm(__byte_perm(u[4], u[5], 0x0040), __byte_perm(u[6], u[7], 0x0040), 0x5410);
+      } else if constexpr (BITS == 4) {
+        // byte 0 of u0 * 16 + u1 is (c0 << 4) | c1; the bits above byte 0 never carry into it.
+        const uint32_t b0 = u[0] * 16u + u[1], b1 = u[2] * 16u + u[3], b2 = u[4] * 16u + u[5], b3 = u[6] * 16u + u[7];
+        o[c] = __byte_perm(__byte_perm(b0, b1, 0x0040), __byte_perm(b2, b3, 0x0040), 0x5410);
+      } else {
+        const uint32_t b0 = (u[0] * 4u + u[1]) * 16u + (u[2] * 4u + u[3]);
+        const uint32_t b1 = (u[4] * 4u + u[5]) * 16u + (u[6] * 4u + u[7]);
+        const uint32_t half16 = __byte_perm(b0, b1, 0x0040);
+        if ((c & 1) == 0) o[c >> 1] = half16;
+        else o[c >> 1] = __byte_perm(o[c >> 1], half16, 0x5410);
+      }
+      continue;
     }
     uint32_t W[4];  // codes of elements 2h (low half) and 2h + 1 (high half)
 #pragma unroll

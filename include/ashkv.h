@@ -141,8 +141,9 @@ ASHKV_API ashkv_status_t ashkv_int8_decode_rows(
  * (element index within the bucket << 16) | bf16 bits, ascending.
  * dither_mode ASHKV_DITHER_TENSOR reads U = d_dither[e] (fp32 in [0, 1), one
  * per element, what torch.rand returns in the reference); ASHKV_DITHER_PHILOX
- * derives U - 0.5 = h * 2^-16 - 0.5 from the (e & 7)-th 16-bit field of
- * Philox4x32-10(key = seed, counter = (dither_elem_offset + e) / 8).
+ * derives U = (b + 0.5) / 256 from byte b = (e & 15) of the four output words
+ * (little-endian) of Philox4x32-10(key = seed, counter = (dither_elem_offset
+ * + e) / 16); dither_elem_offset must be a multiple of 16.
  * ======================================================================== */
 ASHKV_API ashkv_status_t ashkv_nbit_encode(
     const void* d_src, int64_t n_groups, int32_t bits, float sigma,

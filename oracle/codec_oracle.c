@@ -298,24 +298,24 @@ void oracle_philox4x32_10(const uint32_t ctr[4], const uint32_t key[2], uint32_t
   out[0] = c0; out[1] = c1; out[2] = c2; out[3] = c3;
 }
 
-/* Uniforms U = h16 * 2^-16 that the PHILOX mode of the kernel uses for
- * elements [offset, offset + n), h16 being the (e & 7)-th 16-bit field
- * (little-endian order) of Philox4x32-10(counter = e >> 3, key = seed). */
+/* Uniforms U = (b + 0.5) / 256 that the PHILOX mode of the kernel uses for
+ * elements [offset, offset + n), b being byte (e & 15) (little-endian order
+ * over the four output words) of Philox4x32-10(counter = e >> 4, key = seed). */
 void oracle_philox_dither(int64_t n, uint64_t seed, uint64_t offset, float* out) {
   const uint32_t key[2] = {(uint32_t)seed, (uint32_t)(seed >> 32)};
   uint64_t cached = ~0ull;
   uint32_t r[4] = {0, 0, 0, 0};
   for (int64_t i = 0; i < n; ++i) {
     const uint64_t e = offset + (uint64_t)i;
-    const uint64_t c = e >> 3;
+    const uint64_t c = e >> 4;
     if (c != cached) {
       const uint32_t ctr[4] = {(uint32_t)c, (uint32_t)(c >> 32), 0u, 0u};
       oracle_philox4x32_10(ctr, key, r);
       cached = c;
     }
-    const int f = (int)(e & 7u);
-    const uint32_t h = (r[f >> 1] >> (16 * (f & 1))) & 0xFFFFu;
-    out[i] = (float)h * (1.0f / 65536.0f);
+    const int f = (int)(e & 15u);
+    const uint32_t b = (r[f >> 2] >> (8 * (f & 3))) & 0xFFu;
+    out[i] = ((float)b + 0.5f) * (1.0f / 256.0f);
   }
 }
 

@@ -297,6 +297,58 @@ def test_nbit_philox_dither_matches_oracle(cuda, bits):
     assert np.array_equal(enc.codes[: ocodes.size].cpu().numpy(), ocodes)
 
 
+# A group of INT4-grid values (multiples of 2.8027344 / 7 rounded to bf16, largest 2.0) and
+# 8-bit-grid uniforms: element 5 lands one ulp above a rounding tie, v = RN(RN(a / delta) + 1.5)
+# = 0.5 + 2^-24, and only a separately rounded noise term a = RN(x + RN((U - 0.5) * delta))
+# gives code 1 there (a fused x + (U - 0.5) * delta gives 0).
+NEAR_TIE_X = [0.80078125, 0.0, 0.80078125, -1.1953125, 1.6015625, -1.6015625, -1.1953125, 2.0,
+              -0.80078125, 0.80078125, -0.400390625, 0.400390625, 0.400390625, 1.1953125, 0.400390625,
+              -1.1953125, 2.0, 1.6015625, -0.80078125, -0.400390625, -0.80078125, 1.6015625, -0.80078125,
+              0.80078125, 0.400390625, -0.400390625, 0.0, 0.80078125, -0.400390625, 1.6015625, 0.0, 0.0]
+NEAR_TIE_B = [242, 149, 154, 8, 145, 179, 65, 14, 215, 95, 213, 12, 145, 82, 73, 105,
+              224, 194, 174, 12, 116, 164, 7, 17, 218, 86, 20, 168, 152, 51, 7, 183]
+
+
+@pytest.mark.parametrize("bits", [2, 4, 8])
+def test_nbit_noise_rounded_separately(cuda, bits):
+    x = torch.tensor(NEAR_TIE_X * 32, dtype=torch.float32).to(torch.bfloat16)
+    u = ((torch.tensor(NEAR_TIE_B * 32, dtype=torch.float32) + 0.5) / 256.0)
+    enc = nb.encode_groups(x.to(cuda), bits, 3.0, uniform=u.to(cuda))
+    osc, ocodes, _, _ = oracle.nbit_encode(bits_of(x), bits, u.numpy(), 3.0)
+    assert np.array_equal(bits_of(enc.scales), osc)
+    assert np.array_equal(enc.codes[: ocodes.size].cpu().numpy(), ocodes)
+    if bits == 2:
+        assert (int(ocodes[1]) >> 4) & 3 == 1  # the near-tie element
+
+
+@pytest.mark.parametrize("bits", [2, 4, 8])
+@pytest.mark.parametrize("mode", ["tensor", "philox"])
+def test_nbit_structured_values_match_oracle(cuda, bits, mode):
+    """INT4-decoded values (a small grid per 64 elements) with uniforms on the 8-bit
+    grid hit exact and one-ulp rounding ties of the quantiser far more often than
+    Gaussian data does; every code, delta and outlier must still equal the oracle's."""
+    n = 32 * 32768
+    x = rand_bf16(n, 91, "outliers")
+    sc, pk, _ = oracle.int4_encode(bits_of(x), 64)
+    xs = oracle.int4_decode(sc, pk, 64)[:n]
+    xt = torch.from_numpy(xs.view(np.int16).copy()).view(torch.bfloat16)
+    if mode == "tensor":
+        g = torch.Generator().manual_seed(bits)
+        u = (torch.randint(0, 256, (n,), generator=g).float() + 0.5) / 256.0
+        enc = nb.encode_groups(xt.to(cuda), bits, 3.0, uniform=u.to(cuda))
+        un = u.numpy()
+    else:
+        enc = nb.encode_groups(xt.to(cuda), bits, 3.0, seed=1234, dither_offset=32768)
+        un = oracle.philox_dither(n, 1234, 32768)
+    osc, ocodes, oidx, ovals = oracle.nbit_encode(xs, bits, un, 3.0)
+    assert np.array_equal(bits_of(enc.scales), osc)
+    assert np.array_equal(enc.codes[: ocodes.size].cpu().numpy(), ocodes)
+    idx, val, total = nb.flatten_outliers(enc)
+    t = int(total.item())
+    assert t == oidx.size and np.array_equal(idx[:t].cpu().numpy(), oidx)
+    assert np.array_equal(val[:t].cpu().numpy().view(np.uint16), ovals)
+
+
 def test_nbit_flatten_spans_scan_tiles(cuda):
     """More buckets than one scan tile (4096): flat list and offsets against the oracle."""
     n = 5 * 4096 * 1024 + 32 * 77

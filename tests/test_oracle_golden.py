@@ -134,9 +134,14 @@ def test_philox_known_answers():
 
 def test_philox_dither_range_and_offset():
     u = oracle.philox_dither(4096, seed=7)
-    assert u.min() >= 0.0 and u.max() < 1.0
+    assert u.min() > 0.0 and u.max() < 1.0
     assert np.array_equal(oracle.philox_dither(64, seed=7, offset=1024), u[1024:1088])
     assert abs(float(u.mean()) - 0.5) < 0.02
+    # centred 8-bit uniforms: U = (b + 0.5) / 256, b = byte e & 15 of Philox4x32-10(counter e >> 4)
+    b = u * 256.0 - 0.5
+    assert np.array_equal(b, np.round(b)) and b.min() >= 0 and b.max() <= 255
+    words = oracle.philox4x32_10([3, 0, 0, 0], [7, 0])
+    assert np.array_equal(b[48:64].astype(np.uint8), words.view(np.uint8))
 
 
 def test_outlier_bound_holds_on_adversarial_groups():
