@@ -179,11 +179,6 @@ inline void philox_round_keys(uint64_t seed, uint32_t (&rk)[20]) {
   }
 }
 
-// 16-bit field -> dither value h * 2^-16 - 0.5 in [-0.5, 0.5), exact.
-__device__ __forceinline__ float dither16(uint32_t h16) {
-  return __fadd_rn(__uint_as_float(0x3F800000u | (h16 << 7)), -1.5f);
-}
-
 
 // ---------------------------------------------------------------- sm_100 vector ops
 // 256-bit streaming load / store (one full 32-byte sector per thread).

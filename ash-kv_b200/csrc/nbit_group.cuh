@@ -32,8 +32,8 @@ struct NbitEncParams {
 // One thread per 32-element group, one warp (32 groups) per outlier bucket.
 //
 // Outlier decisions are made against the reference threshold without
-// computing its fp64 variance in the common case: an fp32 variance with a
-// rigorous error bound gives thr_lo <= thr <= thr_hi.  If every |x - mu| of
+// computing its fp64 variance in the common case: fp32 sums of the values and
+// of their squares, with rigorous error bounds, give thr_lo <= thr <= thr_hi.  If every |x - mu| of
 // the group is <= thr_lo the group has no outliers (the usual case).
 // Otherwise per-element masks against thr_lo and thr_hi are built; if they
 // agree, that is the exact mask, and only if some |x - mu| falls between the
@@ -87,6 +87,14 @@ __device__ __forceinline__ float min_nan(float a, float b) {
   float r;
   asm("min.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
   return r;
+}
+
+// (RN(bf16lo(w) + a), RN(bf16hi(w) + b)): sm_100 mixed-precision adds, one rounding each.
+__device__ __forceinline__ f2 add_bf16x2_f32(uint32_t w, float a, float b) {
+  float lo, hi;
+  asm("{ .reg .b16 l, h; mov.b32 {l, h}, %2; add.rn.f32.bf16 %0, l, %3; add.rn.f32.bf16 %1, h, %4; }"
+      : "=f"(lo), "=f"(hi) : "r"(w), "f"(a), "f"(b));
+  return pk2(lo, hi);
 }
 
 __device__ __forceinline__ double warp_sum_f64(double v) {  // pairwise (butterfly) order, same in every lane
@@ -220,7 +228,14 @@ __device__ __forceinline__ uint32_t encode_group(const Src& src, const NbitEncPa
   }
   if (!active) omask = 0;
   if (!(am >= 1e-8f) && am == am) am = 1e-8f;  // clamp(min=1e-8); NaN propagates
-  const float delta = __fdiv_rn(am, p.half_states);
+  // delta = RN(am / half) by Markstein's correction with the compile-time reciprocal pair of
+  // half: exact for every finite am >= 1e-8 (checked exhaustively for the three halves; no
+  // step can underflow or overflow there), NaN stays NaN, and +inf is passed through.
+  constexpr float kHalf = float(kMaxCode) * 0.5f;
+  constexpr float kHy = 1.0f / kHalf;
+  constexpr float kHlo = float(double(float(1.0 - double(kHalf) * double(kHy))) * double(kHy));
+  const float dq = div_rn(am, kHalf, Recip{kHy, kHlo});
+  const float delta = am == INFINITY ? am : dq;
 
   // ---- dither, quantise (x' + (U-0.5)*delta) / delta + half, pack
   const Recip y = make_recip(delta);
@@ -234,17 +249,8 @@ __device__ __forceinline__ uint32_t encode_group(const Src& src, const NbitEncPa
   Philox4 rr;
 #pragma unroll
   for (int c = 0; c < 4; ++c) {  // 8 elements per chunk, 16 per Philox draw
-    f2 P[4];
-    chunk_pairs(src, c, P);
-    if (omask & (0xFFu << (8 * c))) {
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        float x0, x1;
-        upk2(P[i], x0, x1);
-        const int e = 8 * c + 2 * i;
-        P[i] = pk2((omask >> e) & 1u ? mu : x0, (omask >> (e + 1)) & 1u ? mu : x1);
-      }
-    }
+    const uint4 raw = src.chunk(c);
+    const uint32_t rw[4] = {raw.x, raw.y, raw.z, raw.w};
     f2 DZ[4];
     if constexpr (DMODE == ASHKV_DITHER_TENSOR) {
       U8 u;
@@ -278,14 +284,27 @@ __device__ __forceinline__ uint32_t encode_group(const Src& src, const NbitEncPa
     // float clamp comes first (NaN -> 0), as in the reference.
     f2 Q[4];
 #pragma unroll
-    for (int h = 0; h < 4; ++h) {
-      // a = RN(x' + RN((U - 0.5) * delta)).  The sum is taken with scalar add.rn: a packed
-      // add.rn.f32x2 fed by a packed multiply was measured to come out single-rounded (a fused
-      // multiply-add), which flips codes one ulp from a rounding tie.
-      float x0, x1, n0, n1;
-      upk2(P[h], x0, x1);
-      upk2(mul2(DZ[h], DELTA), n0, n1);
-      Q[h] = pk2(__fadd_rn(x0, n0), __fadd_rn(x1, n1));
+    // a = RN(x' + RN((U - 0.5) * delta)), x' = mu at outliers.  The sum is a scalar add.rn (a
+    // packed add.rn.f32x2 fed by a packed multiply was measured to come out single-rounded, a
+    // fused multiply-add, which flips codes one ulp from a rounding tie); without outliers in
+    // the chunk it takes the bf16 operand directly (add.rn.f32.bf16: exact widening, one rounding).
+    if (omask & (0xFFu << (8 * c))) {
+#pragma unroll
+      for (int h = 0; h < 4; ++h) {
+        const int e = 8 * c + 2 * h;
+        const float x0 = (omask >> e) & 1u ? mu : bf16lo(rw[h]);
+        const float x1 = (omask >> (e + 1)) & 1u ? mu : bf16hi(rw[h]);
+        float n0, n1;
+        upk2(mul2(DZ[h], DELTA), n0, n1);
+        Q[h] = pk2(__fadd_rn(x0, n0), __fadd_rn(x1, n1));
+      }
+    } else {
+#pragma unroll
+      for (int h = 0; h < 4; ++h) {
+        float n0, n1;
+        upk2(mul2(DZ[h], DELTA), n0, n1);
+        Q[h] = add_bf16x2_f32(rw[h], n0, n1);
+      }
     }
     if (fast_div) {
 #pragma unroll

@@ -1023,7 +1023,7 @@ def main() -> None:
                    + (encQ.codes[: m * BITS // 8].cpu().numpy() != ocodes).sum()
                    + (decQ[:m].cpu().view(torch.int16).numpy().view(np.uint16) != odec).sum())
         # the same encode with fp32 torch.rand uniforms (the reference's kind of dither)
-        # in place of the in-kernel 16-bit Philox uniforms
+        # in place of the in-kernel 8-bit Philox uniforms
         u32 = torch.rand(ELEMS, generator=torch.Generator(device=dev).manual_seed(42), device=dev)
         decU = nb.decode_groups(nb.encode_groups(K, BITS, SIGMA, uniform=u32))
         cos_u = torch.nn.functional.cosine_similarity(K.float().view(-1), decU.float().view(-1), dim=0).item()

@@ -1,8 +1,8 @@
 """Quality of the production dither against the reference's kind of dither.
 
 The reference dithers with ``torch.rand`` (fp32 uniforms, 24 random bits);
-this library's production path draws 16-bit uniforms from an in-kernel
-Philox4x32-10 stream.  The reference's adversarial stress test
+this library's production path draws centred 8-bit uniforms, U = (b + 0.5) / 256,
+from an in-kernel Philox4x32-10 stream.  The reference's adversarial stress test
 (ashkv/tests/stress_test_nbit.py:50-89: 1024 tokens x 8 heads x 64, K and V
 N(0, 0.02^2) with 1 % of the entries shifted by 50 standard deviations, the
 attention output of decoded K/V against the original, thresholds INT2 > 0.98,
@@ -60,5 +60,5 @@ def test_production_dither_matches_fp32_uniform_quality(cuda, bits):
                            roundtrip(DitheredNBitCodec(hidden_dim=D, bits=bits), v, uv))
     assert cos_philox > THRESHOLDS[bits], (bits, cos_philox)
     assert cos_fp32 > THRESHOLDS[bits], (bits, cos_fp32)
-    # the 16-bit uniforms cost at most a sliver of the fp32 uniforms' fidelity
+    # the 8-bit uniforms cost at most a sliver of the fp32 uniforms' fidelity
     assert (1.0 - cos_philox) <= 1.5 * (1.0 - cos_fp32) + 1e-6, (bits, cos_philox, cos_fp32)
