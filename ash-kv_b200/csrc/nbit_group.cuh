@@ -128,6 +128,14 @@ __device__ __forceinline__ uint32_t encode_group(const Src& src, const NbitEncPa
   //      ((x_i + x_{8+i}) + x_{16+i}) + x_{24+i}, then acc[0] + ... + acc[7] in
   //      order (PyTorch's CPU reduction order for a 32-wide inner dimension);
   //      the sum of squares; the signed maximum and minimum (NaN-propagating).
+  // the group's two Philox draws do not depend on its values: computing them first gives
+  // the scheduler independent work beside the statistics' dependency chains
+  Philox4 rd[2];
+  if constexpr (DMODE == ASHKV_DITHER_PHILOX) {
+    const uint64_t ctr = (p.dither_offset + uint64_t(g) * 32) >> 4;
+    rd[0] = philox4x32_10_rk(uint32_t(ctr), uint32_t(ctr >> 32), 0u, 0u, p.round_keys);
+    rd[1] = philox4x32_10_rk(uint32_t(ctr + 1), uint32_t((ctr + 1) >> 32), 0u, 0u, p.round_keys);
+  }
   f2 A[4];
   chunk_pairs(src, 0, A);
   f2 SQ0 = mul2(A[0], A[0]), SQ1 = mul2(A[1], A[1]);
@@ -246,7 +254,6 @@ __device__ __forceinline__ uint32_t encode_group(const Src& src, const NbitEncPa
   uint32_t o[BITS];  // packed codes: 32 * BITS bits, MSB-first within each byte
 #pragma unroll
   for (int k = 0; k < BITS; ++k) o[k] = 0u;
-  Philox4 rr;
 #pragma unroll
   for (int c = 0; c < 4; ++c) {  // 8 elements per chunk, 16 per Philox draw
     const uint4 raw = src.chunk(c);
@@ -263,10 +270,7 @@ __device__ __forceinline__ uint32_t encode_group(const Src& src, const NbitEncPa
       for (int h = 0; h < 4; ++h)
         DZ[h] = add2(pk2(__uint_as_float(u.v[2 * h]), __uint_as_float(u.v[2 * h + 1])), pk2(-0.5f, -0.5f));
     } else {
-      if ((c & 1) == 0) {
-        const uint64_t ctr = ((p.dither_offset + uint64_t(g) * 32) >> 4) + (c >> 1);
-        rr = philox4x32_10_rk(uint32_t(ctr), uint32_t(ctr >> 32), 0u, 0u, p.round_keys);
-      }
+      const Philox4& rr = rd[c >> 1];
 #pragma unroll
       for (int h = 0; h < 4; ++h) {
         // U = (b + 0.5) / 256 from byte b = e & 15 of the draw for counter e >> 4:
