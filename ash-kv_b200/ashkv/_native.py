@@ -48,6 +48,7 @@ SIGNATURES: dict[str, tuple] = {
     "ashkv_desired_tiers": (_I32, [_P, _P, _I64, _F64, _F64, _F64, _F64, _F64, _P, _P, _P, _P]),
     "ashkv_policy_scratch_ints": (_I64, [_I64]),
     "ashkv_memcpy2d": (_I32, [_P, _I64, _P, _I64, _I64, _I64, _P]),
+    "ashkv_fill32": (_I32, [_P, _I64, _U32, _P]),
     "ashkv_copy_rows_indexed": (_I32, [_P, _I64, _I64, _P, _I64, _P, _I64, _I64, _P, _I64, _I64, _I64, _I64, _P,
                                        _P]),
     "ashkv_policy_step_noalloc": (_I32, [_P, _P, _P, _P, _P, _I64, _F32, _F32, _F32, _F32, _F64, _F64, _F64, _F64,
@@ -454,6 +455,15 @@ def memcpy2d(dst_ptr: int, dst_pitch: int, src_ptr: int, src_pitch: int, width: 
     """Pitched async copy on the current stream (host pointers should be pinned for async)."""
     check(lib().ashkv_memcpy2d(dst_ptr, dst_pitch, src_ptr, src_pitch, width, height, stream_handle(device)),
           "memcpy2d")
+
+
+def fill32(t: torch.Tensor, value: int = 0) -> None:
+    """Fill a contiguous CUDA tensor's bytes with a repeated 32-bit pattern on the current stream."""
+    _require_cuda(t)
+    if not t.is_contiguous():
+        raise ValueError("fill32 needs a contiguous tensor")
+    nbytes = t.numel() * t.element_size()
+    check(lib().ashkv_fill32(t.data_ptr(), nbytes, value & 0xFFFFFFFF, stream_handle(t.device)), "fill32")
 
 
 def copy_rows_indexed(dst_ptr: int, dst_row_stride: int, dst_sub_stride: int, dst_index: Optional[torch.Tensor],

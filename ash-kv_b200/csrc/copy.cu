@@ -119,3 +119,39 @@ extern "C" ashkv_status_t ashkv_copy_rows_indexed(
   copy_rows_kernel<<<unsigned(g > 0 ? g : 1), 256, 0, as_stream(stream)>>>(p);
   return check_launch("copy_rows_indexed");
 }
+
+// ---------------------------------------------------------------- fill
+// A 32-bit pattern over `bytes` of device memory: 32-byte streaming stores for
+// the 32-byte-aligned body, 4-byte stores for the head and tail, grid-stride
+// over 16 CTAs of 128 threads per SM.  Clears staging buffers and slot tails,
+// and is the plain write stream the write-dominated decoders are compared with.
+namespace ashkv {
+namespace {
+__global__ void __launch_bounds__(128) fill32_kernel(uint32_t* head, int64_t n_head, uint32_t* body, int64_t n_body,
+                                                     uint32_t* tail, int64_t n_tail, uint32_t v) {
+  const int64_t i0 = int64_t(blockIdx.x) * blockDim.x + threadIdx.x, step = int64_t(gridDim.x) * blockDim.x;
+  for (int64_t i = i0; i < n_body; i += step)
+    asm volatile("st.global.cs.v8.u32 [%0], {%1,%1,%1,%1,%1,%1,%1,%1};" :: "l"(body + 8 * i), "r"(v) : "memory");
+  if (i0 < n_head) head[i0] = v;
+  if (i0 < n_tail) tail[i0] = v;
+}
+}  // namespace
+}  // namespace ashkv
+
+extern "C" ashkv_status_t ashkv_fill32(void* d_dst, int64_t bytes, uint32_t value, void* stream) {
+  using namespace ashkv;
+  if (bytes < 0 || (bytes & 3)) return ASHKV_BAD_ARGUMENT;
+  if (bytes == 0) return ASHKV_OK;
+  if (!d_dst || !aligned(d_dst, 4)) return ASHKV_BAD_ARGUMENT;
+  const uintptr_t a = reinterpret_cast<uintptr_t>(d_dst), end = a + uintptr_t(bytes);
+  uintptr_t b0 = (a + 31) & ~uintptr_t(31), b1 = end & ~uintptr_t(31);
+  if (b1 < b0) b0 = b1 = end;  // shorter than one aligned 32-byte block: all head
+  const int64_t n_head = int64_t(b0 - a) / 4, n_body = int64_t(b1 - b0) / 32, n_tail = int64_t(end - b1) / 4;
+  const int64_t need = (std::max<int64_t>(n_body, 8) + 127) / 128;
+  const int64_t cap = int64_t(sm_count() > 0 ? sm_count() : 148) * 16;
+  const unsigned grid = unsigned(std::max<int64_t>(1, std::min(need, cap)));
+  fill32_kernel<<<grid, 128, 0, as_stream(stream)>>>(reinterpret_cast<uint32_t*>(a), n_head,
+                                                     reinterpret_cast<uint32_t*>(b0), n_body,
+                                                     reinterpret_cast<uint32_t*>(b1), n_tail, value);
+  return check_launch("fill32");
+}

@@ -302,9 +302,11 @@ def codec_suite(K: torch.Tensor, V: torch.Tensor, peak: float, iters: int = 20) 
     dV = torch.empty_like(dK)
     ms = timed(lambda: checksum_pages(pK, out=dK), lambda: checksum_pages(pV, out=dV))
     out["xxh64_pages"] = entry("xxh64_items_kernel", 2 * E + 8 * pK.shape[0], ms)
-    # write-only stream of the same size as a decoder's output (torch's fill kernel): context
-    # for the write-dominated decoders, whose bytes are mostly the bf16 they write (a plain
-    # write stream, not the part's write ceiling)
+    # write-only streams of the same size as a decoder's output: context for the
+    # write-dominated decoders, whose bytes are mostly the bf16 they write; the library's
+    # fill (32-byte streaming stores) and torch's fill kernel
+    ms = timed(lambda: nb._native.fill32(bK), lambda: nb._native.fill32(bV))
+    out["write_stream"] = entry("ashkv_fill32 (write only)", 2 * E, ms)
     ms = timed(lambda: bK.fill_(0.0), lambda: bV.fill_(0.0))
     out["write_stream_fill"] = entry("torch fill_ (write only)", 2 * E, ms)
     return out

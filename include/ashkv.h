@@ -238,6 +238,14 @@ ASHKV_API ashkv_status_t ashkv_memcpy2d(void* dst, int64_t dst_pitch, const void
                                         int64_t width, int64_t height, void* stream);
 
 /* ========================================================================
+ * Fill: the 32-bit pattern `value` repeated over `bytes` bytes of device
+ * memory at d_dst (4-byte aligned, bytes a multiple of 4), with 32-byte
+ * streaming stores.  Clears staging buffers and host-slot tails, and is the
+ * plain write stream the write-dominated decoders are measured against.
+ * ======================================================================== */
+ASHKV_API ashkv_status_t ashkv_fill32(void* d_dst, int64_t bytes, uint32_t value, void* stream);
+
+/* ========================================================================
  * Indexed row copies: for r < n_rows and s < n_sub, `width` bytes from
  *   src + (d_src_index ? d_src_index[r] : r) * src_row_stride + s * src_sub_stride
  * to

@@ -563,3 +563,14 @@ def test_nbit_codec_seeding_policy(cuda):
     c2 = DitheredINT2Codec()
     assert c2.encode(x) == c2.encode(x)  # fixed seed 42
     assert DitheredNBitCodec().encode(b"") == b"\x00" * 8
+
+
+@pytest.mark.parametrize("offset_words,n_words", [(0, 1), (1, 7), (3, 9), (7, 8), (5, 1000), (0, 1 << 20), (2, (1 << 20) + 3)])
+def test_fill32_head_body_tail(cuda, offset_words, n_words):
+    """Every word of [offset, offset + n) gets the pattern; the words around it do not."""
+    buf = torch.zeros(offset_words + n_words + 16, dtype=torch.int32, device=cuda)
+    view = buf[offset_words:offset_words + n_words]
+    _native.fill32(view, 0xA5A5_5A5A)
+    got = buf.cpu().numpy().view(np.uint32)
+    assert (got[offset_words:offset_words + n_words] == 0xA5A55A5A).all()
+    assert (got[:offset_words] == 0).all() and (got[offset_words + n_words:] == 0).all()
