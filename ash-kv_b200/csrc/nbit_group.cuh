@@ -287,7 +287,6 @@ __device__ __forceinline__ uint32_t encode_group(const Src& src, const NbitEncPa
     // so the clamp runs on the integers (two codes per s16x2 word); otherwise the
     // float clamp comes first (NaN -> 0), as in the reference.
     f2 Q[4];
-#pragma unroll
     // a = RN(x' + RN((U - 0.5) * delta)), x' = mu at outliers.  The sum is a scalar add.rn (a
     // packed add.rn.f32x2 fed by a packed multiply was measured to come out single-rounded, a
     // fused multiply-add, which flips codes one ulp from a rounding tie); without outliers in
@@ -351,27 +350,27 @@ __device__ __forceinline__ uint32_t encode_group(const Src& src, const NbitEncPa
         if ((c & 1) == 0) o[c >> 1] = half16;
         else o[c >> 1] = __byte_perm(o[c >> 1], half16, 0x5410);
       }
-      continue;
-    }
-    uint32_t W[4];  // codes of elements 2h (low half) and 2h + 1 (high half)
-#pragma unroll
-    for (int h = 0; h < 4; ++h) {
-      float t0, t1;
-      upk2(Q[h], t0, t1);
-      W[h] = clamp_codes_s16x2(__byte_perm(__float_as_uint(t0), __float_as_uint(t1), 0x5410), kMaxCode);
-    }
-    // bytes c0..c3 of elements 8c..8c+3, and c4..c7
-    const uint32_t X = __byte_perm(W[0], W[1], 0x6420), Y = __byte_perm(W[2], W[3], 0x6420);
-    if constexpr (BITS == 8) {
-      o[2 * c] = X;
-      o[2 * c + 1] = Y;
-    } else if constexpr (BITS == 4) {
-      // byte j of X*16 + (X >> 8) is (c_j << 4) + c_{j+1}: keep bytes 0 and 2 of each half.
-      o[c] = __byte_perm(X * 16u + (X >> 8), Y * 16u + (Y >> 8), 0x6420);
     } else {
-      const uint32_t tx = X * 4u + (X >> 8), ty = Y * 4u + (Y >> 8);   // bytes 0, 2: c0c1, c2c3
-      const uint32_t ux = tx * 16u + (tx >> 16), uy = ty * 16u + (ty >> 16);  // byte 0: c0c1c2c3
-      o[c >> 1] |= (__byte_perm(ux, uy, 0x0040) & 0xFFFFu) << (16 * (c & 1));
+      uint32_t W[4];  // codes of elements 2h (low half) and 2h + 1 (high half)
+#pragma unroll
+      for (int h = 0; h < 4; ++h) {
+        float t0, t1;
+        upk2(Q[h], t0, t1);
+        W[h] = clamp_codes_s16x2(__byte_perm(__float_as_uint(t0), __float_as_uint(t1), 0x5410), kMaxCode);
+      }
+      // bytes c0..c3 of elements 8c..8c+3, and c4..c7
+      const uint32_t X = __byte_perm(W[0], W[1], 0x6420), Y = __byte_perm(W[2], W[3], 0x6420);
+      if constexpr (BITS == 8) {
+        o[2 * c] = X;
+        o[2 * c + 1] = Y;
+      } else if constexpr (BITS == 4) {
+        // byte j of X*16 + (X >> 8) is (c_j << 4) + c_{j+1}: keep bytes 0 and 2 of each half.
+        o[c] = __byte_perm(X * 16u + (X >> 8), Y * 16u + (Y >> 8), 0x6420);
+      } else {
+        const uint32_t tx = X * 4u + (X >> 8), ty = Y * 4u + (Y >> 8);   // bytes 0, 2: c0c1, c2c3
+        const uint32_t ux = tx * 16u + (tx >> 16), uy = ty * 16u + (ty >> 16);  // byte 0: c0c1c2c3
+        o[c >> 1] |= (__byte_perm(ux, uy, 0x0040) & 0xFFFFu) << (16 * (c & 1));
+      }
     }
   }
 
