@@ -287,26 +287,26 @@ __device__ __forceinline__ uint32_t encode_group(const Src& src, const NbitEncPa
     // so the clamp runs on the integers (two codes per s16x2 word); otherwise the
     // float clamp comes first (NaN -> 0), as in the reference.
     f2 Q[4];
-    // a = RN(x' + RN((U - 0.5) * delta)), x' = mu at outliers.  The sum is a scalar add.rn (a
+    // a = RN(x' + RN((U - 0.5) * delta)), x' = mu at outliers.  The sum is a scalar add (a
     // packed add.rn.f32x2 fed by a packed multiply was measured to come out single-rounded, a
-    // fused multiply-add, which flips codes one ulp from a rounding tie); without outliers in
-    // the chunk it takes the bf16 operand directly (add.rn.f32.bf16: exact widening, one rounding).
-    if (omask & (0xFFu << (8 * c))) {
+    // fused multiply-add, which flips codes one ulp from a rounding tie): every element takes
+    // the bf16 operand directly (add.rn.f32.bf16: exact widening, one rounding), and only the
+    // chunks holding outliers then redo those elements with mu (one divergent path, not two).
+    float NZ[8];
+#pragma unroll
+    for (int h = 0; h < 4; ++h) {
+      upk2(mul2(DZ[h], DELTA), NZ[2 * h], NZ[2 * h + 1]);
+      Q[h] = add_bf16x2_f32(rw[h], NZ[2 * h], NZ[2 * h + 1]);
+    }
+    if (omask & (0xFFu << (8 * c))) {  // outliers of this chunk take x' = mu
 #pragma unroll
       for (int h = 0; h < 4; ++h) {
         const int e = 8 * c + 2 * h;
-        const float x0 = (omask >> e) & 1u ? mu : bf16lo(rw[h]);
-        const float x1 = (omask >> (e + 1)) & 1u ? mu : bf16hi(rw[h]);
-        float n0, n1;
-        upk2(mul2(DZ[h], DELTA), n0, n1);
-        Q[h] = pk2(__fadd_rn(x0, n0), __fadd_rn(x1, n1));
-      }
-    } else {
-#pragma unroll
-      for (int h = 0; h < 4; ++h) {
-        float n0, n1;
-        upk2(mul2(DZ[h], DELTA), n0, n1);
-        Q[h] = add_bf16x2_f32(rw[h], n0, n1);
+        float q0, q1;
+        upk2(Q[h], q0, q1);
+        if ((omask >> e) & 1u) q0 = __fadd_rn(mu, NZ[2 * h]);
+        if ((omask >> (e + 1)) & 1u) q1 = __fadd_rn(mu, NZ[2 * h + 1]);
+        Q[h] = pk2(q0, q1);
       }
     }
     if (fast_div) {
