@@ -102,11 +102,10 @@ __device__ __forceinline__ double warp_sum_f64(double v) {  // pairwise (butterf
   for (int off = 1; off < 32; off <<= 1) v = __dadd_rn(v, __shfl_xor_sync(0xFFFFFFFFu, v, off));
   return v;
 }
+// max |v| over the warp, NaN if any lane holds NaN: the bit patterns of non-negative floats
+// order like unsigned integers (NaNs above +inf), so one redux.sync max does it.
 __device__ __forceinline__ float warp_max_abs_nan(float v) {
-  v = fabsf(v);
-#pragma unroll
-  for (int off = 16; off > 0; off >>= 1) v = max_nan(v, __shfl_xor_sync(0xFFFFFFFFu, v, off));
-  return v;
+  return __uint_as_float(__reduce_max_sync(0xFFFFFFFFu, __float_as_uint(v) & 0x7FFFFFFFu));
 }
 
 template <typename Src>

@@ -574,3 +574,48 @@ def test_fill32_head_body_tail(cuda, offset_words, n_words):
     got = buf.cpu().numpy().view(np.uint32)
     assert (got[offset_words:offset_words + n_words] == 0xA5A55A5A).all()
     assert (got[:offset_words] == 0).all() and (got[offset_words + n_words:] == 0).all()
+
+
+def _bits_equal_or_both_nan(a: np.ndarray, b: np.ndarray) -> bool:
+    """bf16 bit arrays equal, NaN against NaN whatever the payload (CUDA writes 0x7FFF)."""
+    nan_a = (a & 0x7F80) == 0x7F80
+    nan_a &= (a & 0x007F) != 0
+    nan_b = ((b & 0x7F80) == 0x7F80) & ((b & 0x007F) != 0)
+    return bool(np.all((a == b) | (nan_a & nan_b)))
+
+
+@pytest.mark.parametrize("bits", [2, 4, 8])
+@pytest.mark.parametrize("mode", ["tensor", "philox"])
+def test_nbit_nan_inf_groups_match_oracle(cuda, bits, mode):
+    """Groups holding NaN (quiet, signalling pattern, negative with payload), +-inf, both,
+    or only NaN, among ordinary groups: codes and outlier lists exact, scales equal or
+    both NaN."""
+    n_groups = 64 * 32
+    x = rand_bf16(n_groups * 32, 41 + bits, "outliers")
+    b = bits_of(x).reshape(n_groups, 32).copy()
+    b[1, 0] = 0x7FC0               # quiet NaN
+    b[3, 31] = 0xFFC1              # negative NaN with a payload
+    b[5, 7] = 0x7FA0               # signalling-NaN pattern
+    b[7, 3] = 0x7F80               # +inf
+    b[9, 12] = 0xFF80              # -inf
+    b[11, 2], b[11, 9] = 0x7F80, 0xFF80
+    b[13, 4], b[13, 5] = 0x7FC0, 0x7F80
+    b[15, :] = 0x7FC0              # every element NaN
+    b[17, :] = 0x7F80              # every element +inf
+    b[100::97, 6] = 0x7FC0         # NaN sprinkled over later buckets
+    b = b.reshape(-1)
+    xt = torch.from_numpy(b.view(np.int16).copy()).view(torch.bfloat16).to(cuda)
+    if mode == "tensor":
+        u = torch.rand(b.size, generator=torch.Generator().manual_seed(bits))
+        enc = nb.encode_groups(xt, bits, 3.0, uniform=u.to(cuda))
+        un = u.numpy()
+    else:
+        enc = nb.encode_groups(xt, bits, 3.0, seed=99, dither_offset=0)
+        un = oracle.philox_dither(b.size, 99, 0)
+    osc, ocodes, oidx, ovals = oracle.nbit_encode(b, bits, un, 3.0)
+    assert _bits_equal_or_both_nan(bits_of(enc.scales), osc)
+    assert np.array_equal(enc.codes[: ocodes.size].cpu().numpy(), ocodes)
+    idx, val, total = nb.flatten_outliers(enc)
+    t = int(total.item())
+    assert t == oidx.size and np.array_equal(idx[:t].cpu().numpy(), oidx)
+    assert np.array_equal(val[:t].cpu().numpy().view(np.uint16), ovals)
